@@ -1,0 +1,388 @@
+"""Benchmark: CCPE+WCA reuse-prefill tok/s (and decode tok/s) on B200.
+
+Workload (kernel microbenchmark config): per GPU 8 requests, 32 query / 8 KV
+heads x 128, 4096 tokens in 8 chunks of 512 (chunk 3 recomputed, the rest
+reused), CoPE npos 64, paged KV blocks of 16 with shuffled physical ids, WCA
+15 % with profile K = K + N(0, 0.05).  Synthetic seeded data.
+
+One step = one reuse-prefill layer of every request: SLIDE baseline write,
+WCA calibration scoring + top-k, fused WCA blend+scatter of the active rows,
+WCA commit (cosine gate + promotion), CCPE attention of the active rows over
+all 4096 keys through the paged slots.  ``value`` = prompt tokens / s with
+inputs resident in HBM; ``e2e`` repeats the step with the per-layer snapshot
+and the fresh rows copied from pinned host memory and the outputs copied back.
+
+``--impl reference`` times the reference algorithm on the host cores (the
+numpy restatement of the reference's CPU path) on a bounded sample.
+Multi-GPU (torchrun): requests are sharded by rank, no data-path collective.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "CCPE+WCA reuse-prefill tok/s"
+WORKLOAD = "c2-kernel-microbench: B=8/GPU, Hq=32, Hkv=8, D=128, S=4096 (8x512), npos=64, block=16, WCA=15%"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--requests", type=int, default=8)
+    ap.add_argument("--seq", type=int, default=4096)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample-rows", type=int, default=128)
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text()), "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+# ----------------------------------------------------------- accounting
+def attention_flops(work) -> float:
+    """Algorithmic FLOPs of the attention launches of one step.
+
+    QK over every causal cell (the gates count all causal keys), PV over every
+    visible cell (association policy), plus the q.E table.
+    """
+    c = work.cfg
+    total = 0.0
+    for r in work.requests:
+        qpos = r.active.cpu().numpy()
+        causal = (qpos + 1).astype(np.float64)
+        sel = r.q_sel.cpu().numpy().astype(bool)
+        fixed = r.reused.cpu().numpy()
+        dyn_prefix = np.cumsum(~fixed)  # dynamic keys with position <= p
+        visible = np.where(sel, dyn_prefix[qpos] + 1, causal)
+        total += 2 * c.head_dim * c.q_heads * (causal.sum() + visible.sum())
+        total += 2 * len(qpos) * c.q_heads * c.npos * c.head_dim
+    return total
+
+
+def hot_bytes(work) -> dict:
+    c = work.cfg
+    rec = c.kv_heads * c.head_dim * 2  # bytes of K (or V) of one token
+    out = {}
+    n = c.seq
+    a = sum(r.a for r in work.requests) / len(work.requests)
+    out["slide_scatter"] = 2 * 2 * n * rec  # read dense K,V + write paged K,V
+    out["wca_initialize"] = 2 * n * rec  # read cached K + calib K
+    out["wca_update"] = 3 * 2 * a * rec  # old + fresh + fused (K and V)
+    out["decode_attention"] = (n + 1) * 2 * rec + c.q_heads * c.head_dim * 2 + (n + 1) * 8
+    return out
+
+
+# --------------------------------------------------------------- clocks
+class Clocks:
+    def __init__(self, index: int):
+        self.path = Path(tempfile.mkstemp(prefix="clk", suffix=".csv")[1])
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        self.path.unlink(missing_ok=True)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------- CPU legs
+def cpu_layer_sample(work, b: int, rows: int, threads: int):
+    """Reference algorithm for one request on the host (numpy restatement of
+    the reference CPU path): SLIDE baseline write, WCA initialize + select +
+    update, fused rows written back, logical gather, CCPE attention on `rows`
+    of the active query rows.  Returns (seconds for the full request, with the
+    attention extrapolated by causal cells, description, sample wall time)."""
+    from oracle import cope as ocope
+    from oracle import slide as oslide
+    from oracle import wca as owca
+
+    r = work.requests[b]
+    c = work.cfg
+    f32 = lambda t: t.float().cpu().numpy()  # noqa: E731
+    cached_k, cached_v = f32(r.cached_k), f32(r.cached_v)
+    calib_k = f32(r.calib_k)
+    q_all, fresh_k, fresh_v = f32(r.q_all), f32(r.fresh_k), f32(r.fresh_v)
+    cache = np.zeros((work.cache.shape[0], c.kv_heads, c.block, 2 * c.head_dim), np.float32)
+    slots = r.slots.cpu().numpy()
+    E = work.E.float().cpu().numpy()
+    key_chunk = r.key_chunk.cpu().numpy()
+    offsets = r.offsets.cpu().numpy()
+    fixed = r.fixed.cpu().numpy()
+    reused, mandatory = r.reused.cpu().numpy(), r.mandatory.cpu().numpy()
+
+    t0 = time.perf_counter()
+    oslide.scatter(cache, None, None, slots, cached_k, cached_v)
+    st = owca.OracleWCA(correction_fraction=c.fraction).initialize(
+        cached_k, calib_k, reused, mandatory)
+    active = st.active
+    sel_prev = np.nonzero(st.selected & ~mandatory)[0]
+    q = q_all[active]
+    upd = st.update(2, cached_k, cached_v, fresh_k[active], fresh_v[active])
+    oslide.scatter(cache, None, None, slots[active], upd["fused_k"].astype(np.float32),
+                   upd["fused_v"].astype(np.float32))
+    k, v = oslide.gather(cache, None, None, slots)
+    t_wca = time.perf_counter() - t0
+    pick = np.linspace(0, len(active) - 1, min(rows, len(active))).astype(np.int64)
+
+    def part(idx):
+        return ocope.cope_attention(
+            q[idx], k, v, E, active[idx],
+            visibility_fn=lambda a_, b_: ocope.association_mask(a_, b_, fixed, sel_prev),
+            chunk_reset=(key_chunk, offsets[:, active[idx]]), chunk=16)
+
+    t1 = time.perf_counter()
+    groups = np.array_split(pick, max(1, threads))
+    with ThreadPoolExecutor(max_workers=threads) as pool:
+        list(pool.map(part, [g for g in groups if len(g)]))
+    t_att = time.perf_counter() - t1
+    cells_all = float((active + 1).sum())
+    cells_s = float((active[pick] + 1).sum())
+    seconds = t_wca + t_att * cells_all / cells_s
+    desc = (f"request {b}: full SLIDE write + WCA init/update + gather; attention on "
+            f"{len(pick)} of {len(active)} active rows, extrapolated by causal cells; "
+            f"{threads} threads")
+    return seconds, desc, t_wca + t_att
+
+
+def run_reference(args):
+    """--impl reference: the reference algorithm on host cores (numpy port)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+
+    from cacheslide_b200.reuse import SyntheticWorkload, WorkloadConfig
+
+    threads = os.cpu_count() or 1
+    cfg = WorkloadConfig(requests=1, seq=args.seq)
+    # inputs are built on the host; nothing of this package runs on this arm
+    work = SyntheticWorkload(cfg, torch.device("cpu"))
+    times = []
+    for i in range(args.warmup + args.steps):
+        sec, desc, _ = cpu_layer_sample(work, 0, max(16, args.cpu_sample_rows // 4), threads)
+        if i >= args.warmup:
+            times.append(sec)
+    per_req = statistics.median(times)
+    value = cfg.seq / per_req
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": per_req * 8 * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "sample": desc},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------ our arm
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import torch
+    import torch.distributed as dist
+
+    from cacheslide_b200 import _native as N
+    from cacheslide_b200.reuse import ReuseStep, SyntheticWorkload, WorkloadConfig
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    cfg = WorkloadConfig(requests=args.requests, seq=args.seq, seed=1000 + rank)
+    work = SyntheticWorkload(cfg, dev)
+    step = ReuseStep(work)
+    stream = torch.cuda.current_stream(dev)
+    s = stream.cuda_stream
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > 126 MB L2
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(max(3, args.warmup)):
+        step.run(s)
+        step.decode(s)
+    barrier()
+    step.check_status()
+
+    # ---- device-timed reuse-prefill steps (L2 flushed between steps)
+    clocks = Clocks(torch.cuda.current_device()) if rank == 0 else None
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    barrier()
+    for i in range(args.steps):
+        flush.fill_(i & 0xFF)
+        ev[i][0].record(stream)
+        step.run(s)
+        ev[i][1].record(stream)
+    barrier()
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    total_ms = sum(step_ms)
+
+    # ---- attention launches alone (roofline of the dominant kernel)
+    att = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.fill_(i & 0xFF)
+        att[i][0].record(stream)
+        for r in work.requests:
+            step.attention(r, s)
+        att[i][1].record(stream)
+    # ---- decode steps
+    dec = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.fill_(i & 0xFF)
+        dec[i][0].record(stream)
+        step.decode(s)
+        dec[i][1].record(stream)
+    barrier()
+    clk = clocks.stop() if clocks else None
+    step.check_status()
+    att_ms = statistics.mean(a.elapsed_time(b) for a, b in att)
+    dec_ms = statistics.mean(a.elapsed_time(b) for a, b in dec)
+
+    # ---- e2e: snapshot + fresh rows from pinned host memory, outputs back
+    host = []
+    h2d = d2h = 0
+    for r in work.requests:
+        item = {}
+        for name in ("cached_k", "cached_v", "q", "fk", "fv"):
+            t = getattr(r, name)
+            item[name] = t.cpu().pin_memory()
+            h2d += t.numel() * t.element_size()
+        item["out"] = torch.empty(r.out.shape, dtype=r.out.dtype).pin_memory()
+        d2h += r.out.numel() * r.out.element_size()
+        host.append(item)
+    e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+    barrier()
+    for i in range(args.steps):
+        flush.fill_(i & 0xFF)
+        e2e_ev[i][0].record(stream)
+        for r, item in zip(work.requests, host):
+            for name in ("cached_k", "cached_v", "q", "fk", "fv"):
+                getattr(r, name).copy_(item[name], non_blocking=True)
+        step.run(s)
+        for r, item in zip(work.requests, host):
+            item["out"].copy_(r.out, non_blocking=True)
+        e2e_ev[i][1].record(stream)
+    barrier()
+    e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_ev)
+
+    # ---- max over ranks
+    vals = torch.tensor([total_ms, att_ms, dec_ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    total_ms, att_ms, dec_ms, e2e_ms = vals.tolist()
+    tokens = args.requests * cfg.seq * world
+    value = tokens * args.steps / (total_ms / 1e3)
+    e2e_value = tokens * args.steps / (e2e_ms / 1e3)
+    decode_value = args.requests * world / (dec_ms / 1e3)
+
+    if rank == 0:
+        pk, pk_kind = peaks()
+        flops = attention_flops(work)  # per attention pass over this rank's requests
+        achieved = flops / (att_ms / 1e3) / 1e12
+        peak = float(pk.get("bf16_tflops", 1590.0))
+        cpu = None
+        if not args.no_cpu_baseline:
+            threads = os.cpu_count() or 1
+            sec, desc, wall = cpu_layer_sample(work, 0, args.cpu_sample_rows, threads)
+            cpu = {"value": cfg.seq / sec, "unit": "tok/s", "cores": threads, "kind": "port",
+                   "sample": desc + f"; sample wall {wall:.1f}s"}
+        launches_per_step = len(work.requests) * 6
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random-init inputs of the C2 shapes)",
+            "config": {"workload": WORKLOAD, "requests_per_gpu": args.requests,
+                       "l2": "flushed (256 MB write) between timed steps",
+                       "parallelism": f"request-sharded x{world}"},
+            "decode": {"value": decode_value, "unit": "tok/s",
+                       "ms_per_step": dec_ms, "note": "one token per request over 4097 keys"},
+            "roofline": {"bound": "tensor", "kernel": "CCPE attention (all requests)",
+                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "peak_kind": pk_kind,
+                         "flops_per_launch_set": flops, "ms_per_launch_set": att_ms,
+                         "traffic": None},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": h2d * world,
+                    "d2h_bytes_per_step": d2h * world},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk,
+            "hot_bytes": hot_bytes(work),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,198 @@
+// SLIDE paged KV data movement: gather, scatter and paged-to-paged relocate.
+//
+// Each (slot, kv_head) record is 2*D elements (K then V).  With the native
+// layout [block, kv_head, offset, 2*D] and a contiguous innermost dimension a
+// record is 2*D*esize contiguous bytes, so one warp moves 512 bytes per D=128
+// bf16 record as 32 aligned 16-byte vectors: fully coalesced, bit-exact.
+// Views whose innermost stride is not 1 (or whose rows are not 16-byte
+// aligned) take an element-wise path with the same semantics.
+#include "common.cuh"
+
+namespace cs {
+namespace {
+
+// 16-byte vector count per K or V half of a record
+struct Geometry {
+  int64_t n, heads, head_dim;
+  int esize;
+};
+
+template <typename V>
+__device__ __forceinline__ void move(char* dst, const char* src) {
+  *reinterpret_cast<V*>(dst) = *reinterpret_cast<const V*>(src);
+}
+
+// gather: out[r] = record(slots[r]); unit = bytes moved per thread step
+template <typename V>
+__global__ void gather_kernel(PagedView pv, const int64_t* __restrict__ slots, int64_t n,
+                              char* __restrict__ out_k, char* __restrict__ out_v,
+                              int64_t o_row, int64_t o_head, int32_t* status) {
+  const int64_t per_half = pv.head_dim * pv.esize / (int64_t)sizeof(V);
+  const int64_t per_rec = 2 * per_half;
+  const int64_t total = n * pv.kv_heads * per_rec;
+  const int64_t elems_per_unit = (int64_t)sizeof(V) / pv.esize;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    int64_t rec = t / per_rec, u = t - rec * per_rec;
+    int64_t r = rec / pv.kv_heads, h = rec - r * pv.kv_heads;
+    int64_t s = slots[r];
+    if (!pv.valid(s)) {
+      if (u == 0) report(status, CS_ST_SLOT_RANGE);
+      continue;
+    }
+    int half = u >= per_half;
+    int64_t within = (u - half * per_half) * elems_per_unit;
+    const char* src = pv.addr(s, h, half * pv.head_dim + within);
+    char* dst = (half ? out_v : out_k) + r * o_row + h * o_head + within * pv.esize;
+    move<V>(dst, src);
+  }
+}
+
+template <typename V>
+__global__ void scatter_kernel(PagedView pv, const int64_t* __restrict__ slots,
+                               const int64_t* __restrict__ rows, int64_t n,
+                               const char* __restrict__ in_k, const char* __restrict__ in_v,
+                               int64_t i_row, int64_t i_head, int32_t* status) {
+  const int64_t per_half = pv.head_dim * pv.esize / (int64_t)sizeof(V);
+  const int64_t per_rec = 2 * per_half;
+  const int64_t total = n * pv.kv_heads * per_rec;
+  const int64_t elems_per_unit = (int64_t)sizeof(V) / pv.esize;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    int64_t rec = t / per_rec, u = t - rec * per_rec;
+    int64_t r = rec / pv.kv_heads, h = rec - r * pv.kv_heads;
+    int64_t s = slots[r];
+    if (!pv.valid(s)) {
+      if (u == 0) report(status, CS_ST_SLOT_RANGE);
+      continue;
+    }
+    int64_t src_row = rows ? rows[r] : r;
+    int half = u >= per_half;
+    int64_t within = (u - half * per_half) * elems_per_unit;
+    const char* src = (half ? in_v : in_k) + src_row * i_row + h * i_head + within * pv.esize;
+    move<V>(pv.addr(s, h, half * pv.head_dim + within), src);
+  }
+}
+
+template <typename V>
+__global__ void relocate_kernel(PagedView pv, const int64_t* __restrict__ src_slots,
+                                const int64_t* __restrict__ dst_slots, int64_t n,
+                                int32_t* status) {
+  const int64_t per_half = pv.head_dim * pv.esize / (int64_t)sizeof(V);
+  const int64_t per_rec = 2 * per_half;
+  const int64_t total = n * pv.kv_heads * per_rec;
+  const int64_t elems_per_unit = (int64_t)sizeof(V) / pv.esize;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    int64_t rec = t / per_rec, u = t - rec * per_rec;
+    int64_t r = rec / pv.kv_heads, h = rec - r * pv.kv_heads;
+    int64_t s = src_slots[r], d = dst_slots[r];
+    if (!pv.valid(s) || !pv.valid(d)) {
+      if (u == 0) report(status, CS_ST_SLOT_RANGE);
+      continue;
+    }
+    int64_t e = u * elems_per_unit;  // 0 .. 2D, never straddles the K|V split
+    move<V>(pv.addr(d, h, e), pv.addr(s, h, e));
+  }
+}
+
+int grid_for(int64_t units, int threads) {
+  int64_t blocks = (units + threads - 1) / threads;
+  int64_t cap = (int64_t)num_sms() * 16;
+  if (blocks > cap) blocks = cap;
+  return blocks < 1 ? 1 : (int)blocks;
+}
+
+bool aligned16(const void* p, int64_t a, int64_t b) {
+  return (reinterpret_cast<uintptr_t>(p) % 16 == 0) && (a % 16 == 0) && (b % 16 == 0);
+}
+
+bool check_view(const cs_paged_kv* kv) {
+  return kv && kv->cache && kv->num_blocks > 0 && kv->kv_heads > 0 && kv->block_size > 0 &&
+         kv->head_dim > 0 && dtype_size(kv->dtype) > 0;
+}
+
+}  // namespace
+}  // namespace cs
+
+using namespace cs;
+
+extern "C" int cs_slide_gather(const cs_paged_kv* kv, const int64_t* slots, int64_t n,
+                               void* out_k, void* out_v, int64_t out_stride_row,
+                               int64_t out_stride_head, int32_t* status, void* stream) {
+  CS_HOST_CHECK(check_view(kv) && n >= 0);
+  if (n == 0) return CS_OK;
+  CS_HOST_CHECK(slots && out_k && out_v);
+  PagedView pv = PagedView::make(*kv);
+  const int64_t orow = out_stride_row * pv.esize, ohead = out_stride_head * pv.esize;
+  const int threads = 256;
+  if (pv.vec16() && aligned16(out_k, orow, ohead) && aligned16(out_v, orow, ohead)) {
+    int64_t units = n * pv.kv_heads * 2 * (pv.head_dim * pv.esize / 16);
+    gather_kernel<uint4><<<grid_for(units, threads), threads, 0, as_stream(stream)>>>(
+        pv, slots, n, (char*)out_k, (char*)out_v, orow, ohead, status);
+  } else {
+    int64_t units = n * pv.kv_heads * 2 * pv.head_dim;
+    int g = grid_for(units, threads);
+    auto s = as_stream(stream);
+    switch (pv.esize) {
+      case 2: gather_kernel<uint16_t><<<g, threads, 0, s>>>(pv, slots, n, (char*)out_k, (char*)out_v, orow, ohead, status); break;
+      case 4: gather_kernel<uint32_t><<<g, threads, 0, s>>>(pv, slots, n, (char*)out_k, (char*)out_v, orow, ohead, status); break;
+      default: gather_kernel<uint64_t><<<g, threads, 0, s>>>(pv, slots, n, (char*)out_k, (char*)out_v, orow, ohead, status); break;
+    }
+  }
+  CS_LAUNCH_CHECK();
+  return CS_OK;
+}
+
+extern "C" int cs_slide_scatter(const cs_paged_kv* kv, const int64_t* slots, const int64_t* rows,
+                                int64_t n, const void* k, const void* v, int64_t in_stride_row,
+                                int64_t in_stride_head, int32_t* status, void* stream) {
+  CS_HOST_CHECK(check_view(kv) && n >= 0);
+  if (n == 0) return CS_OK;
+  CS_HOST_CHECK(slots && k && v);
+  PagedView pv = PagedView::make(*kv);
+  const int64_t irow = in_stride_row * pv.esize, ihead = in_stride_head * pv.esize;
+  const int threads = 256;
+  auto s = as_stream(stream);
+  if (pv.vec16() && aligned16(k, irow, ihead) && aligned16(v, irow, ihead)) {
+    int64_t units = n * pv.kv_heads * 2 * (pv.head_dim * pv.esize / 16);
+    scatter_kernel<uint4><<<grid_for(units, threads), threads, 0, s>>>(
+        pv, slots, rows, n, (const char*)k, (const char*)v, irow, ihead, status);
+  } else {
+    int64_t units = n * pv.kv_heads * 2 * pv.head_dim;
+    int g = grid_for(units, threads);
+    switch (pv.esize) {
+      case 2: scatter_kernel<uint16_t><<<g, threads, 0, s>>>(pv, slots, rows, n, (const char*)k, (const char*)v, irow, ihead, status); break;
+      case 4: scatter_kernel<uint32_t><<<g, threads, 0, s>>>(pv, slots, rows, n, (const char*)k, (const char*)v, irow, ihead, status); break;
+      default: scatter_kernel<uint64_t><<<g, threads, 0, s>>>(pv, slots, rows, n, (const char*)k, (const char*)v, irow, ihead, status); break;
+    }
+  }
+  CS_LAUNCH_CHECK();
+  return CS_OK;
+}
+
+extern "C" int cs_slide_relocate(const cs_paged_kv* kv, const int64_t* src_slots,
+                                 const int64_t* dst_slots, int64_t n, int32_t* status,
+                                 void* stream) {
+  CS_HOST_CHECK(check_view(kv) && n >= 0);
+  if (n == 0) return CS_OK;
+  CS_HOST_CHECK(src_slots && dst_slots);
+  PagedView pv = PagedView::make(*kv);
+  const int threads = 256;
+  auto s = as_stream(stream);
+  if (pv.vec16()) {
+    int64_t units = n * pv.kv_heads * 2 * (pv.head_dim * pv.esize / 16);
+    relocate_kernel<uint4><<<grid_for(units, threads), threads, 0, s>>>(pv, src_slots, dst_slots, n,
+                                                                         status);
+  } else {
+    int64_t units = n * pv.kv_heads * 2 * pv.head_dim;
+    int g = grid_for(units, threads);
+    switch (pv.esize) {
+      case 2: relocate_kernel<uint16_t><<<g, threads, 0, s>>>(pv, src_slots, dst_slots, n, status); break;
+      case 4: relocate_kernel<uint32_t><<<g, threads, 0, s>>>(pv, src_slots, dst_slots, n, status); break;
+      default: relocate_kernel<uint64_t><<<g, threads, 0, s>>>(pv, src_slots, dst_slots, n, status); break;
+    }
+  }
+  CS_LAUNCH_CHECK();
+  return CS_OK;
+}

@@ -1,0 +1,591 @@
+// Weighted Correction Attention kernels: float64 deviation/weight reductions,
+// mean-head cosine, block radix top-k with stable tie-break, the fused
+// blend (+ paged scatter) update and the selection commit.
+//
+// All reductions accumulate in float64 like the reference (wca.py:55-112).
+// Each token row is owned by one warp; rows are [heads, dim] with arbitrary
+// row/head strides and a contiguous innermost dimension.
+#include "common.cuh"
+
+namespace cs {
+namespace {
+
+constexpr int kSelectThreads = 1024;
+constexpr int kSelectMaxChosen = 16384;  // ordered picks staged in shared memory
+
+// --------------------------------------------------------------- row access
+template <typename T>
+struct Rows {
+  const char* base;
+  int64_t srow, shead;  // byte strides
+  __device__ __forceinline__ const T* ptr(int64_t r, int64_t h) const {
+    return reinterpret_cast<const T*>(base + r * srow + h * shead);
+  }
+};
+
+// Order-preserving map from float64 to uint64 (larger key -> larger code).
+__device__ __forceinline__ uint64_t order_code(double x) {
+  uint64_t b = __double_as_longlong(x);
+  return (b >> 63) ? ~b : (b | 0x8000000000000000ull);
+}
+
+// inclusive block scan of an int over blockDim.x threads (multiple of 32)
+__device__ int block_inclusive_scan(int v, int* warp_tot) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int o = 1; o < 32; o <<= 1) {
+    int t = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += t;
+  }
+  if (lane == 31) warp_tot[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    int nw = blockDim.x >> 5;
+    int w = lane < nw ? warp_tot[lane] : 0;
+    for (int o = 1; o < 32; o <<= 1) {
+      int t = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += t;
+    }
+    if (lane < nw) warp_tot[lane] = w;
+  }
+  __syncthreads();
+  int add = warp > 0 ? warp_tot[warp - 1] : 0;
+  __syncthreads();
+  return v + add;
+}
+
+__device__ int block_sum(int v, int* warp_tot) {
+  int inc = block_inclusive_scan(v, warp_tot);
+  __shared__ int total;
+  if (threadIdx.x == blockDim.x - 1) total = inc;
+  __syncthreads();
+  int t = total;
+  __syncthreads();
+  return t;
+}
+
+// Shared-memory workspace of the block selection.
+struct SelectSmem {
+  int hist[256];
+  int warp_tot[32];
+  uint64_t prefix, mask;
+  int remaining;
+  int chosen_count;
+  int eq_taken;
+};
+
+// Select the `slots` largest keys among available tokens, ties to the lower
+// index (the order of a stable descending argsort, wca.py:282-285).  Must be
+// called by every thread of one block of kSelectThreads threads.  `avail`
+// is a functor (int64 i) -> bool evaluated against the current state.
+template <typename Avail>
+__device__ int64_t block_select_topk(const double* __restrict__ keys, Avail avail, int64_t n,
+                                     int64_t slots, uint8_t* __restrict__ selected,
+                                     int64_t* __restrict__ chosen_out, SelectSmem& sm,
+                                     double* stage_key, int* stage_idx, int32_t* status) {
+  const int tid = threadIdx.x;
+  // how many are available at all
+  int local = 0;
+  for (int64_t i = tid; i < n; i += blockDim.x) local += avail(i) ? 1 : 0;
+  int64_t total = block_sum(local, sm.warp_tot);
+  int64_t want = slots < total ? slots : total;
+  if (want <= 0) return 0;
+  if (tid == 0) {
+    sm.prefix = 0;
+    sm.mask = 0;
+    sm.remaining = (int)want;
+  }
+  __syncthreads();
+  // MSB-first radix select over 8-bit digits of the order code
+  for (int shift = 56; shift >= 0; shift -= 8) {
+    for (int b = tid; b < 256; b += blockDim.x) sm.hist[b] = 0;
+    __syncthreads();
+    const uint64_t prefix = sm.prefix, mask = sm.mask;
+    for (int64_t i = tid; i < n; i += blockDim.x) {
+      if (!avail(i)) continue;
+      uint64_t c = order_code(keys[i]);
+      if ((c & mask) == prefix) atomicAdd(&sm.hist[(c >> shift) & 255], 1);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int need = sm.remaining, above = 0, bin = 0;
+      for (int b = 255; b >= 0; --b) {
+        if (above + sm.hist[b] >= need) {
+          bin = b;
+          break;
+        }
+        above += sm.hist[b];
+      }
+      sm.remaining = need - above;  // how many equal-to-threshold keys to take
+      sm.prefix = prefix | ((uint64_t)bin << shift);
+      sm.mask = mask | (255ull << shift);
+    }
+    __syncthreads();
+  }
+  const uint64_t thr = sm.prefix;
+  const int take_eq = sm.remaining;
+  // mark picks: code > thr, or code == thr among the first take_eq by index
+  if (tid == 0) {
+    sm.chosen_count = 0;
+    sm.eq_taken = 0;
+  }
+  __syncthreads();
+  const bool stage = chosen_out != nullptr && want <= kSelectMaxChosen;
+  for (int64_t base = 0; base < n; base += blockDim.x) {
+    int64_t i = base + tid;
+    bool av = i < n && avail(i);
+    uint64_t c = av ? order_code(keys[i]) : 0;
+    int eq = (av && c == thr) ? 1 : 0;
+    int eq_rank = block_inclusive_scan(eq, sm.warp_tot) - eq + sm.eq_taken;
+    bool pick = av && (c > thr || (eq && eq_rank < take_eq));
+    int pk = pick ? 1 : 0;
+    int slot = block_inclusive_scan(pk, sm.warp_tot) - pk + sm.chosen_count;
+    if (pick) {
+      selected[i] = 1;
+      if (stage) {
+        stage_key[slot] = keys[i];
+        stage_idx[slot] = (int)i;
+      }
+    }
+    __syncthreads();
+    if (tid == blockDim.x - 1) {
+      sm.eq_taken = eq_rank + eq;
+      sm.chosen_count = slot + pk;
+    }
+    __syncthreads();
+  }
+  const int k = sm.chosen_count;
+  if (chosen_out != nullptr) {
+    if (!stage) {
+      if (tid == 0) report(status, CS_ST_SLOT_RANGE);
+      return k;
+    }
+    // rank each pick by (key desc, index asc) and place it
+    for (int a = tid; a < k; a += blockDim.x) {
+      double ka = stage_key[a];
+      int ia = stage_idx[a], rank = 0;
+      for (int b = 0; b < k; ++b) {
+        double kb = stage_key[b];
+        rank += (kb > ka || (kb == ka && stage_idx[b] < ia)) ? 1 : 0;
+      }
+      chosen_out[rank] = ia;
+    }
+  }
+  __syncthreads();
+  return k;
+}
+
+// ------------------------------------------------------------ row reductions
+// one warp per row: dev = sum (f - c)^2, nrm = sum c^2 (float64)
+// returns true (in every lane) when all inputs of the row pair are finite
+template <typename T>
+__device__ __forceinline__ bool row_dev_nrm(Rows<T> c, int64_t crow, Rows<T> f, int64_t frow,
+                                            int64_t heads, int64_t dim, double& dev,
+                                            double& nrm) {
+  const int lane = threadIdx.x & 31;
+  double d_acc = 0.0, n_acc = 0.0;
+  bool ok = true;
+  for (int64_t h = 0; h < heads; ++h) {
+    const T* cp = c.ptr(crow, h);
+    const T* fp = f.ptr(frow, h);
+    for (int64_t e = lane; e < dim; e += 32) {
+      double cv = Elem<T>::to_d(cp[e]);
+      double fv = Elem<T>::to_d(fp[e]);
+      ok &= isfinite(cv) && isfinite(fv);
+      double df = __dsub_rn(fv, cv);
+      d_acc = __dadd_rn(d_acc, __dmul_rn(df, df));
+      n_acc = __dadd_rn(n_acc, __dmul_rn(cv, cv));
+    }
+  }
+  dev = warp_sum(d_acc);
+  nrm = warp_sum(n_acc);
+  return __all_sync(0xffffffffu, ok);
+}
+
+__device__ __forceinline__ bool finite(double x) { return isfinite(x); }
+
+template <typename T>
+__global__ void deviation_kernel(Rows<T> c, const int64_t* __restrict__ crows, Rows<T> f,
+                                 int64_t n, int64_t heads, int64_t dim, double eps, int clamp,
+                                 double* dev_out, double* alpha_out,
+                                 const uint8_t* __restrict__ reused, uint8_t* candidate,
+                                 unsigned long long* counts, int32_t* status) {
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < n;
+       r += warps) {
+    double dev, nrm;
+    bool in_ok = row_dev_nrm(c, crows ? crows[r] : r, f, r, heads, dim, dev, nrm);
+    if ((threadIdx.x & 31) == 0) {
+      double den = nrm + eps;
+      double a = dev / den;
+      if (!in_ok) report(status, CS_ST_INPUT_NONFINITE);
+      if (!finite(dev) || !finite(den) || !finite(a)) report(status, CS_ST_NONFINITE);
+      if (clamp) a = fmin(fmax(a, 0.0), 1.0);
+      if (dev_out) dev_out[r] = dev;
+      if (alpha_out) alpha_out[r] = a;
+      if (candidate) {
+        bool ru = reused[r] != 0;
+        bool cand = ru && dev > 0.0;
+        candidate[r] = cand ? 1 : 0;
+        if (ru) atomicAdd(&counts[0], 1ull);
+        if (cand) atomicAdd(&counts[1], 1ull);
+      }
+    }
+  }
+}
+
+// mean-head cosine of one row pair, result valid in every lane
+template <typename T>
+__device__ double row_cosine(Rows<T> a, int64_t arow, Rows<T> b, int64_t brow, int64_t heads,
+                             int64_t dim, double eps) {
+  const int lane = threadIdx.x & 31;
+  const double tiny = 2.2250738585072014e-308;
+  double acc = 0.0;
+  for (int64_t h = 0; h < heads; ++h) {
+    const T* ap = a.ptr(arow, h);
+    const T* bp = b.ptr(brow, h);
+    double amax = 0.0, bmax = 0.0;
+    for (int64_t e = lane; e < dim; e += 32) {
+      amax = fmax(amax, fabs(Elem<T>::to_d(ap[e])));
+      bmax = fmax(bmax, fabs(Elem<T>::to_d(bp[e])));
+    }
+    amax = fmax(warp_max(amax), eps);
+    bmax = fmax(warp_max(bmax), eps);
+    double na = 0.0, nb = 0.0;
+    for (int64_t e = lane; e < dim; e += 32) {
+      double x = Elem<T>::to_d(ap[e]) / amax, y = Elem<T>::to_d(bp[e]) / bmax;
+      na = __dadd_rn(na, __dmul_rn(x, x));
+      nb = __dadd_rn(nb, __dmul_rn(y, y));
+    }
+    na = fmax(sqrt(warp_sum(na)), tiny);
+    nb = fmax(sqrt(warp_sum(nb)), tiny);
+    double dot = 0.0;
+    for (int64_t e = lane; e < dim; e += 32) {
+      double x = (Elem<T>::to_d(ap[e]) / amax) / na, y = (Elem<T>::to_d(bp[e]) / bmax) / nb;
+      dot = __dadd_rn(dot, __dmul_rn(x, y));
+    }
+    dot = warp_sum(dot);
+    acc += fmin(fmax(dot, -1.0), 1.0);
+  }
+  return acc / (double)heads;
+}
+
+template <typename T>
+__global__ void cosine_kernel(Rows<T> a, Rows<T> b, const int64_t* __restrict__ brows, int64_t n,
+                              int64_t heads, int64_t dim, double eps, double* out) {
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < n;
+       r += warps) {
+    double c = row_cosine(a, r, b, brows ? brows[r] : r, heads, dim, eps);
+    if ((threadIdx.x & 31) == 0) out[r] = c;
+  }
+}
+
+// fused update: weight, blend (float64, no contraction), cast, write dense
+// and/or paged records, optional cosine
+template <typename T>
+__global__ void update_kernel(Rows<T> ck, Rows<T> cv, Rows<T> fk, Rows<T> fv,
+                              const int64_t* __restrict__ indices, int64_t a, int64_t heads,
+                              int64_t dim, const double* __restrict__ alpha,
+                              const uint8_t* __restrict__ mandatory, int same_layer, double eps,
+                              int clamp, T* fused_k, T* fused_v, double* next_alpha_out,
+                              double* used_out, double* cos_out, PagedView pv, int use_paged,
+                              const int64_t* __restrict__ slots, int32_t* status) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < a;
+       r += warps) {
+    const int64_t idx = indices[r];
+    double dev, nrm;
+    bool bad = !row_dev_nrm(ck, idx, fk, r, heads, dim, dev, nrm);
+    double den = nrm + eps;
+    double nxt = dev / den;
+    bad |= !finite(dev) || !finite(den) || !finite(nxt);
+    if (clamp) nxt = fmin(fmax(nxt, 0.0), 1.0);
+    double w = mandatory[idx] ? 1.0 : (same_layer ? nxt : alpha[idx]);
+    double wo = __dsub_rn(1.0, w);
+    int64_t slot = use_paged ? slots[r] : 0;
+    bool slot_ok = !use_paged || pv.valid(slot);
+    if (use_paged && !slot_ok && lane == 0) report(status, CS_ST_SLOT_RANGE);
+    for (int half = 0; half < 2; ++half) {
+      Rows<T> o = half ? cv : ck;
+      Rows<T> f = half ? fv : fk;
+      T* dst = half ? fused_v : fused_k;
+      for (int64_t h = 0; h < heads; ++h) {
+        const T* op = o.ptr(idx, h);
+        const T* fp = f.ptr(r, h);
+        for (int64_t e = lane; e < dim; e += 32) {
+          double x = __dadd_rn(__dmul_rn(w, Elem<T>::to_d(fp[e])),
+                               __dmul_rn(wo, Elem<T>::to_d(op[e])));
+          T y = Elem<T>::from_d(x);
+          bad |= !isfinite(Elem<T>::to_d(y));
+          if (dst) dst[(r * heads + h) * dim + e] = y;
+          if (use_paged && slot_ok)
+            *reinterpret_cast<T*>(pv.addr(slot, h, half * dim + e)) = y;
+        }
+      }
+    }
+    bad = __any_sync(0xffffffffu, bad);
+    double cs = 0.0;
+    if (cos_out) cs = row_cosine(fk, r, ck, idx, heads, dim, eps);
+    if (lane == 0) {
+      if (bad) report(status, CS_ST_NONFINITE);
+      if (next_alpha_out) next_alpha_out[r] = nxt;
+      if (used_out) used_out[r] = w;
+      if (cos_out) cos_out[r] = cs;
+    }
+  }
+}
+
+// ------------------------------------------------------------- select kernels
+__global__ void __launch_bounds__(kSelectThreads)
+    select_kernel(const double* __restrict__ keys, const uint8_t* __restrict__ available, int64_t n,
+                  int64_t slots, uint8_t* selected, int64_t* chosen_out, int64_t* count_out,
+                  int32_t* status) {
+  extern __shared__ __align__(16) unsigned char dyn[];
+  __shared__ SelectSmem sm;
+  double* stage_key = reinterpret_cast<double*>(dyn);
+  int* stage_idx = reinterpret_cast<int*>(dyn + sizeof(double) * kSelectMaxChosen);
+  auto avail = [&](int64_t i) { return available[i] != 0; };
+  int64_t k = block_select_topk(keys, avail, n, slots, selected, chosen_out, sm, stage_key,
+                                stage_idx, status);
+  if (threadIdx.x == 0 && count_out) *count_out = k;
+}
+
+__global__ void __launch_bounds__(kSelectThreads)
+    commit_kernel(const int64_t* __restrict__ indices, int64_t a,
+                  const double* __restrict__ next_alpha, const double* __restrict__ cosv,
+                  double thr, int distance_mode, int64_t n, int64_t budget,
+                  const double* __restrict__ initial, double* alpha, uint8_t* candidate,
+                  uint8_t* selected, uint8_t* removed, int64_t* removed_out,
+                  int64_t* promoted_out, int64_t* counts_out, int32_t* status) {
+  extern __shared__ __align__(16) unsigned char dyn[];
+  __shared__ SelectSmem sm;
+  __shared__ int removed_count;
+  double* stage_key = reinterpret_cast<double*>(dyn);
+  int* stage_idx = reinterpret_cast<int*>(dyn + sizeof(double) * kSelectMaxChosen);
+  const int tid = threadIdx.x;
+  if (tid == 0) removed_count = 0;
+  __syncthreads();
+  // removal decisions use the selection state before this commit; the
+  // indices are sorted, so an ordered compaction lists removals ascending
+  for (int64_t base = 0; base < a; base += blockDim.x) {
+    int64_t r = base + tid;
+    int rm = 0;
+    int64_t idx = 0;
+    if (r < a) {
+      idx = indices[r];
+      if (cosv) {
+        double m = distance_mode ? 1.0 - cosv[r] : cosv[r];
+        rm = (selected[idx] && m < thr) ? 1 : 0;
+      }
+    }
+    int pos = block_inclusive_scan(rm, sm.warp_tot) - rm + removed_count;
+    __syncthreads();
+    if (r < a) {
+      alpha[idx] = next_alpha[r];
+      if (rm) {
+        selected[idx] = 0;
+        candidate[idx] = 0;
+        removed[idx] = 1;
+        if (removed_out) removed_out[pos] = idx;
+      }
+    }
+    __syncthreads();
+    if (tid == blockDim.x - 1) removed_count = pos + rm;
+    __syncthreads();
+  }
+  int local = 0;
+  for (int64_t i = tid; i < n; i += blockDim.x) local += selected[i] ? 1 : 0;
+  int64_t nsel = block_sum(local, sm.warp_tot);
+  int64_t slots = budget - nsel;
+  if (slots < 0) slots = 0;
+  auto avail = [&](int64_t i) { return candidate[i] && !selected[i] && !removed[i]; };
+  // `selected` changes only after the radix passes finish counting
+  int64_t k = block_select_topk(initial, avail, n, slots, selected, promoted_out, sm, stage_key,
+                                stage_idx, status);
+  if (tid == 0 && counts_out) {
+    counts_out[0] = removed_count;
+    counts_out[1] = k;
+  }
+}
+
+constexpr size_t kSelectDynSmem = (sizeof(double) + sizeof(int)) * kSelectMaxChosen;
+
+bool select_smem_ready() {
+  static bool done = false;
+  if (!done) {
+    if (cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kSelectDynSmem) != cudaSuccess)
+      return false;
+    if (cudaFuncSetAttribute(commit_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kSelectDynSmem) != cudaSuccess)
+      return false;
+    done = true;
+  }
+  return true;
+}
+
+int row_grid(int64_t rows, int warps_per_block) {
+  int64_t blocks = (rows + warps_per_block - 1) / warps_per_block;
+  int64_t cap = (int64_t)num_sms() * 8;
+  if (blocks > cap) blocks = cap;
+  return blocks < 1 ? 1 : (int)blocks;
+}
+
+template <typename T>
+Rows<T> rows_of(const void* p, int64_t srow, int64_t shead) {
+  return Rows<T>{static_cast<const char*>(p), srow * (int64_t)sizeof(T),
+                 shead * (int64_t)sizeof(T)};
+}
+
+}  // namespace
+}  // namespace cs
+
+using namespace cs;
+
+#define CS_DISPATCH_FLOAT(dt, T, ...)                       \
+  switch (dt) {                                             \
+    case CS_F32: { using T = float; __VA_ARGS__; break; }   \
+    case CS_F16: { using T = __half; __VA_ARGS__; break; }  \
+    case CS_BF16: { using T = __nv_bfloat16; __VA_ARGS__; break; } \
+    case CS_F64: { using T = double; __VA_ARGS__; break; }  \
+    default: return CS_ERR_INVALID;                         \
+  }
+
+extern "C" int cs_wca_deviation(const void* cached, int64_t c_stride_row, int64_t c_stride_head,
+                                const int64_t* cached_rows, const void* fresh,
+                                int64_t f_stride_row, int64_t f_stride_head, int64_t n,
+                                int64_t heads, int64_t dim, int32_t dtype, double epsilon,
+                                int32_t clamp, double* dev_out, double* alpha_out,
+                                int32_t* status, void* stream) {
+  CS_HOST_CHECK(n >= 0 && heads > 0 && dim > 0);
+  if (n == 0) return CS_OK;
+  CS_HOST_CHECK(cached && fresh);
+  const int threads = 256;
+  CS_DISPATCH_FLOAT(dtype, T, {
+    deviation_kernel<T><<<row_grid(n, threads / 32), threads, 0, as_stream(stream)>>>(
+        rows_of<T>(cached, c_stride_row, c_stride_head), cached_rows,
+        rows_of<T>(fresh, f_stride_row, f_stride_head), n, heads, dim, epsilon, clamp, dev_out,
+        alpha_out, nullptr, nullptr, nullptr, status);
+  });
+  CS_LAUNCH_CHECK();
+  return CS_OK;
+}
+
+extern "C" int cs_wca_initialize(const void* cached, int64_t c_stride_row, int64_t c_stride_head,
+                                 const void* fresh, int64_t f_stride_row, int64_t f_stride_head,
+                                 int64_t n, int64_t heads, int64_t dim, int32_t dtype,
+                                 const uint8_t* reused, double epsilon, int32_t clamp,
+                                 double* dev_out, double* alpha_out, uint8_t* candidate,
+                                 uint8_t* selected, uint8_t* removed, int64_t* counts_out,
+                                 int32_t* status, void* stream) {
+  CS_HOST_CHECK(n >= 0 && heads > 0 && dim > 0 && counts_out && candidate && reused);
+  auto s = as_stream(stream);
+  if (cudaMemsetAsync(counts_out, 0, 2 * sizeof(int64_t), s) != cudaSuccess) return CS_ERR_CUDA;
+  if (selected && n > 0 && cudaMemsetAsync(selected, 0, n, s) != cudaSuccess) return CS_ERR_CUDA;
+  if (removed && n > 0 && cudaMemsetAsync(removed, 0, n, s) != cudaSuccess) return CS_ERR_CUDA;
+  if (n == 0) return CS_OK;
+  CS_HOST_CHECK(cached && fresh);
+  const int threads = 256;
+  CS_DISPATCH_FLOAT(dtype, T, {
+    deviation_kernel<T><<<row_grid(n, threads / 32), threads, 0, s>>>(
+        rows_of<T>(cached, c_stride_row, c_stride_head), nullptr,
+        rows_of<T>(fresh, f_stride_row, f_stride_head), n, heads, dim, epsilon, clamp, dev_out,
+        alpha_out, reused, candidate, reinterpret_cast<unsigned long long*>(counts_out), status);
+  });
+  CS_LAUNCH_CHECK();
+  return CS_OK;
+}
+
+extern "C" int cs_wca_cosine(const void* a, int64_t a_stride_row, int64_t a_stride_head,
+                             const void* b, int64_t b_stride_row, int64_t b_stride_head,
+                             const int64_t* b_rows, int64_t n, int64_t heads, int64_t dim,
+                             int32_t dtype, double epsilon, double* cos_out, int32_t* status,
+                             void* stream) {
+  (void)status;
+  CS_HOST_CHECK(n >= 0 && heads > 0 && dim > 0);
+  if (n == 0) return CS_OK;
+  CS_HOST_CHECK(a && b && cos_out);
+  const int threads = 256;
+  CS_DISPATCH_FLOAT(dtype, T, {
+    cosine_kernel<T><<<row_grid(n, threads / 32), threads, 0, as_stream(stream)>>>(
+        rows_of<T>(a, a_stride_row, a_stride_head), rows_of<T>(b, b_stride_row, b_stride_head),
+        b_rows, n, heads, dim, epsilon, cos_out);
+  });
+  CS_LAUNCH_CHECK();
+  return CS_OK;
+}
+
+extern "C" int cs_wca_select_topk(const double* keys, const uint8_t* available, int64_t n,
+                                  int64_t slots, uint8_t* selected, int64_t* chosen_out,
+                                  int64_t* count_out, int32_t* status, void* stream) {
+  CS_HOST_CHECK(n >= 0 && slots >= 0);
+  if (chosen_out != nullptr && (slots < n ? slots : n) > kSelectMaxChosen)
+    return CS_ERR_UNSUPPORTED;
+  auto s = as_stream(stream);
+  if (n == 0) {
+    if (count_out && cudaMemsetAsync(count_out, 0, sizeof(int64_t), s) != cudaSuccess)
+      return CS_ERR_CUDA;
+    return CS_OK;
+  }
+  CS_HOST_CHECK(keys && available && selected);
+  if (!select_smem_ready()) return CS_ERR_CUDA;
+  select_kernel<<<1, kSelectThreads, kSelectDynSmem, s>>>(keys, available, n, slots, selected,
+                                                          chosen_out, count_out, status);
+  CS_LAUNCH_CHECK();
+  return CS_OK;
+}
+
+extern "C" int cs_wca_update(const void* cached_k, const void* cached_v, int64_t c_stride_row,
+                             int64_t c_stride_head, const void* fresh_k, const void* fresh_v,
+                             int64_t f_stride_row, int64_t f_stride_head, const int64_t* indices,
+                             int64_t a, int64_t heads, int64_t dim, int32_t dtype,
+                             const double* alpha, const uint8_t* mandatory, int32_t same_layer,
+                             double epsilon, int32_t clamp, void* fused_k, void* fused_v,
+                             double* next_alpha_out, double* used_alpha_out, double* cos_out,
+                             const cs_paged_kv* kv, const int64_t* slots, int32_t* status,
+                             void* stream) {
+  CS_HOST_CHECK(a >= 0 && heads > 0 && dim > 0);
+  if (a == 0) return CS_OK;
+  CS_HOST_CHECK(cached_k && cached_v && fresh_k && fresh_v && indices && alpha && mandatory);
+  CS_HOST_CHECK((fused_k == nullptr) == (fused_v == nullptr));
+  PagedView pv{};
+  int use_paged = 0;
+  if (kv != nullptr) {
+    CS_HOST_CHECK(slots && kv->cache && kv->dtype == dtype && kv->head_dim == dim &&
+                  kv->kv_heads == heads && kv->block_size > 0);
+    pv = PagedView::make(*kv);
+    use_paged = 1;
+  }
+  const int threads = 256;
+  CS_DISPATCH_FLOAT(dtype, T, {
+    update_kernel<T><<<row_grid(a, threads / 32), threads, 0, as_stream(stream)>>>(
+        rows_of<T>(cached_k, c_stride_row, c_stride_head),
+        rows_of<T>(cached_v, c_stride_row, c_stride_head),
+        rows_of<T>(fresh_k, f_stride_row, f_stride_head),
+        rows_of<T>(fresh_v, f_stride_row, f_stride_head), indices, a, heads, dim, alpha,
+        mandatory, same_layer, epsilon, clamp, static_cast<T*>(fused_k), static_cast<T*>(fused_v),
+        next_alpha_out, used_alpha_out, cos_out, pv, use_paged, slots, status);
+  });
+  CS_LAUNCH_CHECK();
+  return CS_OK;
+}
+
+extern "C" int cs_wca_commit(const int64_t* indices, int64_t a, const double* next_alpha,
+                             const double* cos, double threshold, int32_t distance_mode,
+                             int64_t n, int64_t budget, const double* initial_dev, double* alpha,
+                             uint8_t* candidate, uint8_t* selected, uint8_t* removed,
+                             int64_t* removed_out, int64_t* promoted_out, int64_t* counts_out,
+                             int32_t* status, void* stream) {
+  CS_HOST_CHECK(a >= 0 && n >= 0 && budget >= 0 && counts_out);
+  CS_HOST_CHECK(n == 0 || (initial_dev && alpha && candidate && selected && removed));
+  CS_HOST_CHECK(a == 0 || (indices && next_alpha));
+  if (promoted_out != nullptr && (budget < n ? budget : n) > kSelectMaxChosen)
+    return CS_ERR_UNSUPPORTED;
+  if (!select_smem_ready()) return CS_ERR_CUDA;
+  commit_kernel<<<1, kSelectThreads, kSelectDynSmem, as_stream(stream)>>>(
+      indices, a, next_alpha, cos, threshold, distance_mode, n, budget, initial_dev, alpha,
+      candidate, selected, removed, removed_out, promoted_out, counts_out, status);
+  CS_LAUNCH_CHECK();
+  return CS_OK;
+}

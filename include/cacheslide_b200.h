@@ -1,0 +1,344 @@
+/*
+ * cacheslide_b200.h -- C ABI of libcacheslide_sm100.so, the B200 (sm_100a)
+ * implementation of CacheSlide's reuse-time attention hot path.
+ *
+ * Every entry point takes plain device pointers, element strides, sizes and a
+ * cudaStream_t (passed as void*), enqueues its kernels on that stream and
+ * returns immediately with a cs_status code for host-side argument errors.
+ * Data-dependent failures (a slot outside the arena, a non-finite WCA value,
+ * an invalid contextual path, ...) are reported through an optional device
+ * status word: kernels OR the CS_ST_* bits below into *status and skip the
+ * offending access, they never trap.  The caller reads the word after the
+ * stream has drained and maps it to the reference's exception types.
+ *
+ * Tensor layouts follow the reference package `cacheslide_vllm`:
+ *   query [token, q_head, dim], key/value [token, kv_head, dim],
+ *   positions [head, query, key], learned table E [dim, npos],
+ *   native paged KV cache [block, kv_head, block_offset, 2*dim] (K | V).
+ * The innermost dimension of q/k/v/out must be contiguous unless a stride for
+ * it is taken explicitly.
+ */
+#ifndef CACHESLIDE_B200_H
+#define CACHESLIDE_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CS_API __attribute__((visibility("default")))
+#else
+#define CS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ codes */
+typedef enum {
+  CS_OK = 0,
+  CS_ERR_INVALID = 1,     /* bad argument; nothing was enqueued            */
+  CS_ERR_CUDA = 2,        /* a CUDA runtime call or launch failed          */
+  CS_ERR_UNSUPPORTED = 3  /* shape/dtype combination this build lacks      */
+} cs_status;
+
+typedef enum { CS_F32 = 0, CS_F16 = 1, CS_BF16 = 2, CS_F64 = 3 } cs_dtype;
+
+/* bits OR-ed into the optional device status word */
+#define CS_ST_SLOT_RANGE (1 << 0)     /* slot outside native + sidecar range   */
+#define CS_ST_NONFINITE (1 << 1)      /* non-finite WCA arithmetic / K,V       */
+#define CS_ST_LOGIT_NONFINITE (1 << 2)/* attention logits not finite           */
+#define CS_ST_POS_RANGE (1 << 3)      /* substituted position not in [0,npos-1]*/
+#define CS_ST_PATH_NEG (1 << 4)       /* strict path: negative count           */
+#define CS_ST_PATH_AVAIL (1 << 5)     /* strict path: count > available gates  */
+#define CS_ST_PATH_INCR (1 << 6)      /* strict path: increasing along keys    */
+#define CS_ST_PATH_GAP (1 << 7)       /* strict path: drop > coordinate gap    */
+#define CS_ST_TIMEOUT (1 << 8)        /* a bounded device wait expired         */
+#define CS_ST_INPUT_NONFINITE (1 << 9)/* non-finite query/key/value element    */
+
+/* ------------------------------------------------------- paged KV arena */
+/*
+ * One request/layer view of the native paged cache plus its sidecar.
+ * Replaces the tensor state of `NativePagedKV` (paged.py:57-128): slot s <
+ * num_blocks*block_size addresses cache[s / bs, :, s % bs, :] with K in the
+ * first head_dim elements and V in the next; s >= that addresses sidecar row
+ * s - num_blocks*block_size (paged.py:205-240).  All strides are in elements
+ * and may describe a non-contiguous view; the innermost stride may be != 1.
+ */
+typedef struct {
+  void* cache;
+  int64_t num_blocks, kv_heads, block_size, head_dim;
+  int64_t stride_block, stride_head, stride_offset, stride_elem;
+  void* side_k; /* [side_capacity, kv_heads, head_dim] or NULL */
+  void* side_v;
+  int64_t side_capacity;
+  int64_t side_stride_row, side_stride_head, side_stride_elem;
+  int32_t dtype; /* cs_dtype of cache and sidecar */
+} cs_paged_kv;
+
+/*
+ * SLIDE gather: out_k/out_v[r] = record of slots[r] (caller order).
+ * Replaces NativePagedKV.gather (paged.py:433-472).  out rows are
+ * [n, kv_heads, head_dim] with the given row/head strides (elem stride 1).
+ */
+CS_API int cs_slide_gather(const cs_paged_kv* kv, const int64_t* slots, int64_t n,
+                    void* out_k, void* out_v, int64_t out_stride_row,
+                    int64_t out_stride_head, int32_t* status, void* stream);
+
+/*
+ * SLIDE scatter: record of slots[r] = (k, v)[rows ? rows[r] : r].
+ * Replaces NativePagedKV._write_slots (paged.py:205-240) including the
+ * `key[selected]` row selection of promote/update (paged.py:300-312, 421-426).
+ */
+CS_API int cs_slide_scatter(const cs_paged_kv* kv, const int64_t* slots,
+                     const int64_t* rows, int64_t n, const void* k,
+                     const void* v, int64_t in_stride_row,
+                     int64_t in_stride_head, int32_t* status, void* stream);
+
+/*
+ * SLIDE relocate: record of dst_slots[r] = record of src_slots[r], copied
+ * paged-to-paged without a dense staging buffer (promotion into the sidecar,
+ * canonical mirror writes; paged.py:279-328, 474-524).  Source and
+ * destination sets must not overlap.
+ */
+CS_API int cs_slide_relocate(const cs_paged_kv* kv, const int64_t* src_slots,
+                      const int64_t* dst_slots, int64_t n, int32_t* status,
+                      void* stream);
+
+/* ------------------------------------------------------------------ WCA */
+/*
+ * Per-token squared deviation and adaptation weight in float64
+ * (wca.py:55-93): dev[r] = sum_{h,d} (fresh[r] - cached[c])^2,
+ * alpha[r] = dev[r] / (sum cached[c]^2 + epsilon), clamped to [0,1] when
+ * `clamp`; c = cached_rows ? cached_rows[r] : r.  Either output may be NULL.
+ * Non-finite inputs or results set CS_ST_NONFINITE.
+ */
+CS_API int cs_wca_deviation(const void* cached, int64_t c_stride_row,
+                     int64_t c_stride_head, const int64_t* cached_rows,
+                     const void* fresh, int64_t f_stride_row,
+                     int64_t f_stride_head, int64_t n, int64_t heads,
+                     int64_t dim, int32_t dtype, double epsilon, int32_t clamp,
+                     double* dev_out, double* alpha_out, int32_t* status,
+                     void* stream);
+
+/*
+ * Mean-head cosine (wca.py:96-112): per head, amax-scaled unit vectors,
+ * dot clamped to [-1,1], mean over heads; b row = b_rows ? b_rows[r] : r.
+ */
+CS_API int cs_wca_cosine(const void* a, int64_t a_stride_row, int64_t a_stride_head,
+                  const void* b, int64_t b_stride_row, int64_t b_stride_head,
+                  const int64_t* b_rows, int64_t n, int64_t heads, int64_t dim,
+                  int32_t dtype, double epsilon, double* cos_out,
+                  int32_t* status, void* stream);
+
+/*
+ * Block radix top-k (wca.py:202-215): among tokens with available[i] != 0,
+ * pick the `slots` largest keys[i] (float64, >= 0), descending with ties to the
+ * lower index, exactly like a stable descending argsort.  Sets selected[i]=1
+ * for each pick, writes the picks in that order to chosen_out (may be NULL)
+ * and their number to *count_out (device int64, may be NULL).
+ */
+CS_API int cs_wca_select_topk(const double* keys, const uint8_t* available, int64_t n,
+                       int64_t slots, uint8_t* selected, int64_t* chosen_out,
+                       int64_t* count_out, int32_t* status, void* stream);
+
+/*
+ * WCA initialize reductions (wca.py:152-191): deviation, alpha, candidate =
+ * reused & dev > 0, counts_out[0] = |reused|, counts_out[1] = |candidate|;
+ * selected/removed (may be NULL) are cleared, as a fresh state starts.
+ * cached/fresh are full [n, heads, dim] layers.
+ */
+CS_API int cs_wca_initialize(const void* cached, int64_t c_stride_row,
+                      int64_t c_stride_head, const void* fresh,
+                      int64_t f_stride_row, int64_t f_stride_head, int64_t n,
+                      int64_t heads, int64_t dim, int32_t dtype,
+                      const uint8_t* reused, double epsilon, int32_t clamp,
+                      double* dev_out, double* alpha_out, uint8_t* candidate,
+                      uint8_t* selected, uint8_t* removed,
+                      int64_t* counts_out, int32_t* status, void* stream);
+
+/*
+ * Fused WCA update for the active rows (wca.py:217-304), one pass:
+ *   old = cached[indices[r]], next_alpha[r] = adaptation weight(old, fresh[r]),
+ *   used = mandatory[indices[r]] ? 1 : (same_layer ? next_alpha[r]
+ *                                                   : alpha[indices[r]]),
+ *   fused = used*fresh + (1-used)*old  (float64, cast to dtype),
+ *   cosine[r] = mean-head cosine(fresh_k[r], old_k) when cos_out != NULL.
+ * fused rows go to fused_k/fused_v (dense [a, heads, dim], may be NULL) and,
+ * when `kv` is non-NULL, straight into the paged slots `slots[r]` (blend +
+ * scatter; replaces WCAState.update + NativePagedKV.update_selected's
+ * writes).  Non-finite fused values set CS_ST_NONFINITE.
+ */
+CS_API int cs_wca_update(const void* cached_k, const void* cached_v,
+                  int64_t c_stride_row, int64_t c_stride_head,
+                  const void* fresh_k, const void* fresh_v,
+                  int64_t f_stride_row, int64_t f_stride_head,
+                  const int64_t* indices, int64_t a, int64_t heads, int64_t dim,
+                  int32_t dtype, const double* alpha, const uint8_t* mandatory,
+                  int32_t same_layer, double epsilon, int32_t clamp,
+                  void* fused_k, void* fused_v, double* next_alpha_out,
+                  double* used_alpha_out, double* cos_out,
+                  const cs_paged_kv* kv, const int64_t* slots, int32_t* status,
+                  void* stream);
+
+/*
+ * WCA commit (wca.py:274-287 and 345-366): alpha[indices[r]] = next_alpha[r];
+ * rows with selected[idx] and metric < threshold (metric = cos, or 1-cos when
+ * distance_mode) are removed (selected=0, candidate=0, removed=1; listed in
+ * removed_out in index order, count in counts_out[0]); then the free budget
+ * slots are promoted by cs_wca_select_topk semantics over
+ * candidate & !selected & !removed (listed in promoted_out, count in
+ * counts_out[1]).  cos may be NULL (no gate at this layer).
+ */
+CS_API int cs_wca_commit(const int64_t* indices, int64_t a, const double* next_alpha,
+                  const double* cos, double threshold, int32_t distance_mode,
+                  int64_t n, int64_t budget, const double* initial_dev,
+                  double* alpha, uint8_t* candidate, uint8_t* selected,
+                  uint8_t* removed, int64_t* removed_out,
+                  int64_t* promoted_out, int64_t* counts_out, int32_t* status,
+                  void* stream);
+
+/* ------------------------------------------------------------ attention */
+typedef enum {
+  CS_POS_CONTEXTUAL = 0, /* CoPE gates (position.py:295-307)                 */
+  CS_POS_FIXED = 1,      /* caller positions [h,q,k] (position.py:495-499)   */
+  CS_POS_TABLE = 2,      /* canonical table substitution (attention.py:32-57)*/
+  CS_POS_CHUNK = 3       /* chunk-reset counts with carried per-chunk offsets*/
+} cs_pos_mode;
+
+/*
+ * Arguments of one CoPE/CCPE attention call (cope_attention,
+ * position.py:404-560).  Dense K/V are used when kv_slots == NULL, otherwise
+ * key j is read from paged slot kv_slots[j] of `paged` (no gather copy).
+ */
+typedef struct {
+  const void* q;
+  int64_t q_stride_tok, q_stride_head;
+  int32_t nq, hq, d;
+  const int64_t* qpos; /* [nq] distinct nonnegative coordinates */
+
+  const void* k;
+  const void* v;
+  int64_t k_stride_tok, k_stride_head, v_stride_tok, v_stride_head;
+  cs_paged_kv paged;
+  const int64_t* kv_slots; /* [nk] or NULL */
+  int32_t nk, hkv, dv;
+  const int64_t* kpos; /* [nk] strictly increasing or NULL (= 0..nk-1) */
+
+  const void* E; /* [d, npos] in the accumulation dtype (f64 iff in_dtype == F64) */
+  int64_t e_stride_d, e_stride_p;
+  int32_t npos;
+  double scale; /* 1/sqrt(d) */
+
+  int32_t pos_mode; /* cs_pos_mode */
+  /* FIXED: [h, q, k] in the accumulation dtype (f64 iff in_dtype == F64) */
+  const void* fixed_pos;
+  int64_t fp_stride_h, fp_stride_q, fp_stride_k;
+  /* TABLE: table[h, q_row[i], k_ord[j]] for q_row >= 0 and k_ord >= 0 */
+  const void* table;
+  int64_t tb_stride_h, tb_stride_r, tb_stride_c;
+  const int32_t* q_row;
+  const int32_t* k_ord;
+  /* CHUNK: key_chunk[nk] nondecreasing; chunk_off[h, i, c] (float32) >= 0
+     restarts the count entering chunk c (older than the query's chunk),
+     < 0 carries it */
+  const int32_t* key_chunk;
+  const float* chunk_off;
+  int64_t co_stride_h, co_stride_q;
+  int32_t nchunks;
+
+  /* optional bool masks (uint8, key stride 1; h stride 0 = broadcast):
+     gate_mask = attention_mask (gates and attention), vis_mask =
+     visibility_mask (attention only) */
+  const uint8_t* gate_mask;
+  int64_t gm_stride_h, gm_stride_q;
+  const uint8_t* vis_mask;
+  int64_t vm_stride_h, vm_stride_q;
+  /* SelectedAssociationPolicy (attention.py:61-72): non-NULL enables */
+  const uint8_t* q_selected; /* [nq] */
+  const uint8_t* k_fixed;    /* [nk] */
+
+  int32_t strict; /* validate_contextual_path (position.py:28-114) */
+  double atol;
+  int32_t positions_only; /* compute out_positions only, no softmax/PV */
+
+  void* out_positions; /* [h, q, k] accumulation dtype or NULL */
+  int64_t op_stride_h, op_stride_q;
+
+  void* out; /* [nq, hq, dv] */
+  int64_t o_stride_tok, o_stride_head;
+  int32_t in_dtype, out_dtype;
+  int32_t* status;
+} cs_attn_params;
+
+/*
+ * Generic CoPE/CCPE attention: every mode above, any query rows, float64 /
+ * float32 / bf16 / fp16 inputs (float64 accumulates in float64, the others in
+ * float32, as position.py:153-154).  One warp per (query row, KV head).
+ */
+CS_API int cs_cope_attn(const cs_attn_params* p, void* stream);
+
+/*
+ * Tensor-core prefill / reuse-prefill (sm_100a, tcgen05 + TMEM): bf16 or fp16
+ * inputs, head_dim 64 or 128, contextual or chunk-reset positions, optional
+ * association policy, paged or dense K/V.  Returns CS_ERR_UNSUPPORTED for
+ * any other combination (the caller then uses cs_cope_attn).
+ */
+CS_API int cs_cope_attn_prefill(const cs_attn_params* p, void* stream);
+
+/*
+ * Decode (one or a few query rows over a long paged context): split-key
+ * two-phase kernel.  phase 1 computes logits and per-split gate totals,
+ * phase 2 scans with the carry of newer splits, applies the bias and reduces
+ * split partials.  `workspace` must hold cs_cope_attn_decode_workspace(p)
+ * bytes of device memory.
+ */
+CS_API int64_t cs_cope_attn_decode_workspace(const cs_attn_params* p);
+CS_API int cs_cope_attn_decode(const cs_attn_params* p, void* workspace,
+                        void* stream);
+
+/* ------------------------------------------- standalone CoPE operators */
+/*
+ * CoPE.contextual_positions (position.py:295-307): positions of [h, q, k]
+ * float32/float64 logits under a uint8 allowed mask (key stride 1):
+ * masked gates, reverse cumulative sum over keys, clamp to [0, npos-1].
+ * Non-finite allowed logits set CS_ST_LOGIT_NONFINITE.
+ */
+CS_API int cs_cope_positions(const void* logits, int64_t ls_h, int64_t ls_q,
+                             const uint8_t* allowed, int64_t as_h, int64_t as_q,
+                             int32_t heads, int64_t nq, int64_t nk, int32_t npos,
+                             int32_t dtype, void* out, int64_t os_h, int64_t os_q,
+                             int32_t* status, void* stream);
+
+/*
+ * CoPE.positional_bias (position.py:309-344): per (head, query) the q.E
+ * table, then floor / floor+1 interpolation at every position.  query has
+ * dtype in_dtype; E, positions and out use the accumulation dtype.  Positions
+ * outside [0, npos-1] or non-finite set CS_ST_POS_RANGE.
+ */
+CS_API int cs_cope_bias(const void* query, int64_t qs_t, int64_t qs_h,
+                        const void* E, int64_t es_d, int64_t es_p, int32_t d,
+                        int32_t npos, const void* positions, int64_t ps_h,
+                        int64_t ps_q, int32_t heads, int64_t nq, int64_t nk,
+                        int32_t in_dtype, void* out, int64_t os_h, int64_t os_q,
+                        int32_t* status, void* stream);
+
+/*
+ * validate_contextual_path (position.py:28-114): OR-s CS_ST_PATH_* bits for
+ * failing causal cells / adjacent pairs and CS_ST_POS_RANGE for non-finite
+ * positions.  mask (uint8 [h|1, q, k], may be NULL) = attention_mask.
+ */
+CS_API int cs_cope_validate_path(const void* positions, int64_t ps_h,
+                                 int64_t ps_q, const int64_t* qpos,
+                                 const int64_t* kpos, const uint8_t* mask,
+                                 int64_t ms_h, int64_t ms_q, int32_t heads,
+                                 int64_t nq, int64_t nk, double atol,
+                                 int32_t dtype, int32_t* status, void* stream);
+
+/* library identification: compile-time arch string and ABI version */
+CS_API const char* cs_build_info(void);
+CS_API int32_t cs_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CACHESLIDE_B200_H */

@@ -1,0 +1,297 @@
+"""CoPE / CCPE attention on the GPU against the reference's golden vectors,
+the numpy oracle and the reference's known answers.
+
+Tolerances: float32 inputs vs the float32 reference 1e-4 (summation order);
+bf16 inputs 2e-2 abs / 1e-2 rel on the bf16 output;
+float64 known answers 1e-9.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import pytest
+import torch
+
+from cacheslide_b200.attention import CanonicalPositionPolicy, SelectedAssociationPolicy
+from cacheslide_b200.position import (
+    CCPEPositionError,
+    ChunkResetPositions,
+    CoPE,
+    cope_attention,
+    validate_contextual_path,
+)
+from oracle import cope as ocope
+from tests.conftest import golden
+
+pytestmark = pytest.mark.gpu
+G = golden("cope")
+F32 = dict(atol=1e-4, rtol=1e-4)
+BF16 = dict(atol=2e-2, rtol=1e-2)
+
+
+def _t(a, dev, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    return t if dtype is None else t.to(dtype)
+
+
+def _cope(E, dev, dtype=torch.float32):
+    c = CoPE(E.shape[0], E.shape[1], device=dev, dtype=dtype)
+    c.position_embeddings.data.copy_(_t(E, dev, dtype))
+    return c
+
+
+def _case(name, dev):
+    c = G[name]
+    return (_t(c["q"], dev), _t(c["k"], dev), _t(c["v"], dev), _cope(c["E"], dev),
+            _t(c["qpos"], dev).long(), c)
+
+
+def test_plain_matches_golden_with_trace(cuda):
+    q, k, v, cope, qpos, c = _case("plain", cuda)
+    out, pos = cope_attention(q, k, v, cope, qpos, return_positions=True)
+    np.testing.assert_allclose(out.cpu().numpy(), c["out"], **F32)
+    np.testing.assert_allclose(pos.cpu().numpy(), c["positions"], atol=1e-4, rtol=1e-5)
+
+
+def test_decode_and_sparse_keys_match_golden(cuda):
+    q, k, v, cope, qpos, c = _case("decode", cuda)
+    np.testing.assert_allclose(cope_attention(q, k, v, cope, qpos).cpu().numpy(), c["out"], **F32)
+    q, k, v, cope, qpos, c = _case("sparse_keys", cuda)
+    out = cope_attention(q, k, v, cope, qpos, _t(c["kpos"], cuda).long())
+    np.testing.assert_allclose(out.cpu().numpy(), c["out"], **F32)
+
+
+def test_association_matches_golden(cuda):
+    q, k, v, cope, qpos, c = _case("assoc", cuda)
+    policy = SelectedAssociationPolicy(tuple(int(x) for x in c["fixed"]),
+                                       _t(c["selected"], cuda).long())
+    out = cope_attention(q, k, v, cope, qpos, visibility_transform=policy)
+    np.testing.assert_allclose(out.cpu().numpy(), c["out"], **F32)
+    # the same policy evaluated as a generic callable (per-chunk mask path)
+    out2 = cope_attention(q, k, v, cope, qpos,
+                          visibility_transform=lambda a, b: policy(a, b), query_chunk_size=7)
+    np.testing.assert_allclose(out2.cpu().numpy(), c["out"], **F32)
+
+
+def test_masks_match_golden(cuda):
+    q, k, v, cope, qpos, c = _case("masks", cuda)
+    out = cope_attention(q, k, v, cope, qpos, attention_mask=_t(c["attention_mask"], cuda),
+                         visibility_mask=_t(c["visibility_mask"], cuda))
+    np.testing.assert_allclose(out.cpu().numpy(), c["out"], **F32)
+
+
+def test_fixed_positions_match_golden(cuda):
+    q, k, v, cope, qpos, c = _case("fixed_positions", cuda)
+    out = cope_attention(q, k, v, cope, qpos, fixed_positions=_t(c["positions"], cuda))
+    np.testing.assert_allclose(out.cpu().numpy(), c["out"], **F32)
+
+
+@dataclass(frozen=True)
+class _Plan:
+    fixed_indices: tuple
+    fixed_layout: tuple
+
+
+class _TableProfile:
+    """Profile stand-in with CCPEProfile.lookup's contract (position.py:701-748)."""
+
+    trained_profile_version = "golden-v1"
+    chunks = None
+
+    def __init__(self, table, query_positions):
+        self.table = torch.from_numpy(table)
+        self.known = {int(p): i for i, p in enumerate(query_positions)}
+
+    def lookup(self, chunks, query_positions, key_positions=None, *, checkpoint_id,
+               trained_profile_version, strict=True, device=None, dtype=None):
+        rows = torch.tensor([self.known[int(p)] for p in query_positions])
+        return self.table[:, rows].to(device=device, dtype=dtype)
+
+
+def _policy(c, mode):
+    fixed = tuple(int(x) for x in c["fixed"])
+    layout = tuple(("u0", "0" * 64, len(fixed)) for _ in range(1))
+    return CanonicalPositionPolicy(_Plan(fixed, layout),
+                                   _TableProfile(c["table"], c["table_query_positions"]),
+                                   "ck", mode=mode)
+
+
+def test_canonical_mixed_and_strict_match_golden(cuda):
+    q, k, v, cope, qpos, c = _case("canonical_mixed", cuda)
+    mixed = _policy(c, "mixed_bias_override")
+    out, pos = cope_attention(q, k, v, cope, qpos, positions_transform=mixed,
+                              return_positions=True)
+    np.testing.assert_allclose(out.cpu().numpy(), c["out"], **F32)
+    np.testing.assert_allclose(pos.cpu().numpy(), c["positions"], atol=1e-4, rtol=1e-5)
+    with pytest.raises(CCPEPositionError) as err:
+        cope_attention(q, k, v, cope, qpos, positions_transform=_policy(c, "strict_contextual"))
+    assert str(err.value) == str(c["strict_error"])
+    q, k, v, cope, qpos, c = _case("canonical_strict_ok", cuda)
+    out = cope_attention(q, k, v, cope, qpos, positions_transform=_policy(c, "strict_contextual"))
+    np.testing.assert_allclose(out.cpu().numpy(), c["out"], **F32)
+
+
+def test_generic_transform_callable_matches_kernel_table_mode(cuda):
+    q, k, v, cope, qpos, c = _case("canonical_mixed", cuda)
+    pol = _policy(c, "mixed_bias_override")
+    out = cope_attention(q, k, v, cope, qpos, positions_transform=lambda p, a, b: pol(p, a, b),
+                         query_chunk_size=5)
+    np.testing.assert_allclose(out.cpu().numpy(), c["out"], **F32)
+
+
+def _random(seed, nq, nk, hq, hkv, d, npos, dev, dtype):
+    g = torch.Generator().manual_seed(seed)
+    q = (torch.randn(nk, hq, d, generator=g) / d ** 0.5).to(dtype)
+    k = (torch.randn(nk, hkv, d, generator=g) / d ** 0.5).to(dtype)
+    v = torch.randn(nk, hkv, d, generator=g).to(dtype)
+    E = torch.randn(d, npos, generator=g) * 0.02
+    rows = torch.sort(torch.randperm(nk, generator=g)[:nq]).values
+    return q[rows], k, v, E, rows
+
+
+@pytest.mark.parametrize("nk,hq,hkv,d", [(300, 8, 2, 128), (129, 4, 4, 64), (64, 6, 2, 32)])
+def test_bf16_gqa_matches_oracle(cuda, nk, hq, hkv, d):
+    q, k, v, E, rows = _random(nk, min(nk, 100), nk, hq, hkv, d, 64, cuda, torch.bfloat16)
+    want = ocope.cope_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                                E.numpy(), rows.numpy())
+    got = cope_attention(q.to(cuda), k.to(cuda), v.to(cuda), _cope(E.numpy(), cuda),
+                         rows.to(cuda))
+    assert got.dtype == torch.bfloat16
+    np.testing.assert_allclose(got.float().cpu().numpy(), want, **BF16)
+
+
+def test_chunk_reset_matches_oracle_and_carry_is_plain(cuda):
+    nk, hq, hkv, d, npos = 256, 4, 2, 64, 64
+    q, k, v, E, rows = _random(3, 120, nk, hq, hkv, d, npos, cuda, torch.bfloat16)
+    key_chunk = torch.arange(nk) // 48
+    nch = int(key_chunk.max()) + 1
+    g = torch.Generator().manual_seed(5)
+    offsets = torch.rand(hq, nk, nch, generator=g) * 30
+    offsets[:, :, 1] = -1  # carry through chunk 1
+    args = [x.float().numpy() for x in (q, k, v)] + [E.numpy(), rows.numpy()]
+    want = ocope.cope_attention(*args, chunk_reset=(key_chunk.numpy(),
+                                                    offsets[:, rows].numpy()))
+    cope = _cope(E.numpy(), cuda)
+    policy = ChunkResetPositions(key_chunk.to(cuda), offsets.to(cuda))
+    got = cope_attention(q.to(cuda), k.to(cuda), v.to(cuda), cope, rows.to(cuda),
+                         positions_transform=policy)
+    np.testing.assert_allclose(got.float().cpu().numpy(), want, **BF16)
+    carry = ChunkResetPositions(key_chunk.to(cuda), -torch.ones(hq, nk, nch, device=cuda))
+    plain = cope_attention(q.to(cuda), k.to(cuda), v.to(cuda), cope, rows.to(cuda))
+    same = cope_attention(q.to(cuda), k.to(cuda), v.to(cuda), cope, rows.to(cuda),
+                          positions_transform=carry)
+    np.testing.assert_allclose(same.float().cpu().numpy(), plain.float().cpu().numpy(), **BF16)
+
+
+def test_paged_attention_reads_through_slots(cuda):
+    """Attention over a shuffled paged cache equals attention over dense K/V."""
+    from cacheslide_b200 import _native as N
+    from cacheslide_b200.position import _Holder, _base_params, _launch
+    import ctypes  # noqa: F401
+
+    nk, hq, hkv, d, bs = 200, 8, 2, 64, 16
+    q, k, v, E, rows = _random(11, 50, nk, hq, hkv, d, 64, cuda, torch.bfloat16)
+    q, k, v, rows = q.to(cuda), k.to(cuda), v.to(cuda), rows.to(cuda)
+    nb = (nk + bs - 1) // bs + 3
+    perm = torch.randperm(nb)[: (nk + bs - 1) // bs]
+    cache = torch.zeros(nb, hkv, bs, 2 * d, dtype=torch.bfloat16, device=cuda)
+    slots = (perm.to(cuda)[torch.arange(nk, device=cuda) // bs] * bs
+             + torch.arange(nk, device=cuda) % bs)
+    cache.view(-1, hkv, bs, 2 * d)[slots // bs, :, slots % bs, :d] = k
+    cache.view(-1, hkv, bs, 2 * d)[slots // bs, :, slots % bs, d:] = v
+    cope = _cope(E.numpy(), cuda)
+    dense = cope_attention(q, k, v, cope, rows)
+    out = torch.empty_like(dense)
+    p = _base_params(q, None, None, _Holder(cope, cope.position_embeddings.detach()),
+                     rows, None, nk, hkv, d)
+    p.paged = N.paged_view(cache)
+    p.kv_slots = slots.data_ptr()
+    p.out = out.data_ptr()
+    p.o_stride_tok, p.o_stride_head = out.stride(0), out.stride(1)
+    st = N.Status(cuda)
+    p.status = st.ptr
+    _launch(p, cuda, allow_fast=False)
+    assert st.read() == 0
+    np.testing.assert_allclose(out.float().cpu().numpy(), dense.float().cpu().numpy(), **BF16)
+
+
+# ----------------------------------------- reference known answers (float64)
+def test_known_visibility_after_gates(cuda):
+    cope = CoPE(1, 8, device=cuda, dtype=torch.float64)
+    q = torch.ones(1, 1, 1, dtype=torch.float64, device=cuda)
+    k = torch.zeros(3, 1, 1, dtype=torch.float64, device=cuda)
+    v = torch.tensor([1.0, 10.0, 100.0], dtype=torch.float64, device=cuda)[:, None, None]
+    out, trace = cope_attention(q, k, v, cope, torch.tensor([2], device=cuda),
+                                visibility_mask=torch.tensor([[True, False, True]], device=cuda),
+                                return_positions=True)
+    assert out.item() == pytest.approx(50.5, abs=1e-12)
+    np.testing.assert_allclose(trace.cpu().numpy(), [[[1.5, 1.0, 0.5]]])
+
+
+def test_known_association_outputs(cuda):
+    policy = SelectedAssociationPolicy((0, 2, 4), torch.tensor([4, 2], device=cuda))
+    queries = torch.tensor([4, 1, 2], device=cuda)
+    keys = torch.arange(6, device=cuda)
+    assert policy(queries, keys).tolist() == [
+        [False, True, False, True, True, True],
+        [True, True, True, True, True, True],
+        [False, True, True, True, False, True],
+    ]
+    cope = CoPE(1, 16, device=cuda, dtype=torch.float64)
+    q = torch.ones(3, 1, 1, dtype=torch.float64, device=cuda)
+    k = torch.zeros(6, 1, 1, dtype=torch.float64, device=cuda)
+    v = torch.arange(6, dtype=torch.float64, device=cuda)[:, None, None]
+    out = cope_attention(q, k, v, cope, queries, visibility_transform=policy)
+    np.testing.assert_allclose(out[:, 0, 0].cpu().numpy(), [8 / 3, 0.5, 1.5], atol=1e-12)
+
+
+def test_known_all_masked_rows_are_zero_and_errors(cuda):
+    cope = CoPE(2, 4, device=cuda)
+    q, k, v = [torch.ones(2, 1, 2, device=cuda) for _ in range(3)]
+    mask = torch.tensor([[False, False], [True, True]], device=cuda)
+    out = cope_attention(q, k, v, cope, torch.arange(2, device=cuda), attention_mask=mask)
+    assert out[0].abs().sum() == 0 and torch.isfinite(out).all()
+    with pytest.raises(ValueError, match="query-dependent"):
+        cope_attention(q, k, v, cope, torch.arange(2, device=cuda),
+                       fixed_positions=torch.arange(2, device=cuda))
+    with pytest.raises(ValueError, match="strictly increasing"):
+        cope(q, k, torch.arange(2, device=cuda), torch.tensor([1, 0], device=cuda))
+    with pytest.raises(ValueError, match="finite"):
+        cope(q * torch.nan, k, torch.arange(2, device=cuda))
+
+
+def test_known_positions_interpolation_and_validation(cuda):
+    cope = CoPE(2, 2, device=cuda)
+    logits = torch.zeros(1, 3, 3, device=cuda)
+    allowed = torch.ones(3, 3, dtype=torch.bool, device=cuda).tril().unsqueeze(0)
+    logits[~allowed] = 1000
+    np.testing.assert_allclose(cope.contextual_positions(logits, allowed).cpu().numpy(),
+                               [[[0.5, 0, 0], [1, 0.5, 0], [1, 1, 0.5]]])
+    c4 = CoPE(1, 4, device=cuda, dtype=torch.float64)
+    c4.position_embeddings.data.copy_(torch.tensor([[0, 2, 6, 10]], dtype=torch.float64))
+    bias = c4.positional_bias(torch.tensor([[[2.0]]], dtype=torch.float64, device=cuda),
+                              torch.tensor([[[0.25, 1.5, 3.0]]], dtype=torch.float64, device=cuda))
+    np.testing.assert_allclose(bias.cpu().numpy(), [[[1, 8, 20]]])
+    hybrid = torch.tensor([[[1.5, 2, 1.5, 1, 0.5]]], device=cuda)
+    with pytest.raises(CCPEPositionError, match="nonincreasing"):
+        validate_contextual_path(hybrid, torch.tensor([4], device=cuda),
+                                 torch.arange(5, device=cuda))
+    with pytest.raises(CCPEPositionError, match="one gate per token"):
+        validate_contextual_path(torch.tensor([[[2.75, 0.5]]], device=cuda),
+                                 torch.tensor([2], device=cuda), torch.tensor([0, 2], device=cuda))
+    validate_contextual_path(torch.tensor([[[2.25, 0.5]]], device=cuda),
+                             torch.tensor([2], device=cuda), torch.tensor([0, 2], device=cuda))
+
+
+def test_future_keys_do_not_change_earlier_rows(cuda):
+    g = torch.Generator().manual_seed(8)
+    cope = CoPE(2, 6, device=cuda)
+    cope.position_embeddings.data.copy_(torch.randn(2, 6, generator=g))
+    q, k, v = [torch.randn(4, 2, 2, generator=g).to(cuda) for _ in range(3)]
+    original = cope_attention(q, k, v, cope, torch.arange(4, device=cuda))
+    k[2:] *= -100
+    v[2:] += 100
+    changed = cope_attention(q, k, v, cope, torch.arange(4, device=cuda))
+    torch.testing.assert_close(changed[:2], original[:2])
