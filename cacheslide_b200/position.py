@@ -386,10 +386,22 @@ def _base_params(
     return p
 
 
+DECODE_MAX_ROWS = 8  # split-key decode for at most this many query rows ...
+DECODE_MIN_KEYS = 512  # ... over at least this many keys
+
+
 def _launch(p: N.AttnParams, device: torch.device, *, allow_fast: bool) -> None:
-    """Tensor-core prefill when the mode allows it, else the generic kernel."""
+    """Split-key decode for a few rows over a long context, the tensor-core
+    prefill when the mode allows it, else the generic kernel."""
     lib = N.load()
     stream = N.stream_of(device)
+    if allow_fast and p.nq <= DECODE_MAX_ROWS and p.nk >= DECODE_MIN_KEYS:
+        size = lib.cs_cope_attn_decode_workspace(ctypes.byref(p))
+        if size > 0:
+            workspace = torch.empty(size, dtype=torch.uint8, device=device)
+            N.check(lib.cs_cope_attn_decode(ctypes.byref(p), workspace.data_ptr(), stream),
+                    "cs_cope_attn_decode")
+            return
     if allow_fast:
         rc = lib.cs_cope_attn_prefill(ctypes.byref(p), stream)
         if rc == N.CS_OK:

@@ -217,6 +217,58 @@ def test_paged_attention_reads_through_slots(cuda):
     np.testing.assert_allclose(out.float().cpu().numpy(), dense.float().cpu().numpy(), **BF16)
 
 
+@pytest.mark.parametrize("nk,rows", [(4097, [4096]), (1500, [700, 1200, 1499]), (513, [512])])
+def test_split_key_decode_matches_oracle_and_generic(cuda, nk, rows):
+    """Decode rows through the paged cache: split-key kernel vs oracle and vs
+    the one-warp-per-row generic kernel."""
+    from cacheslide_b200 import _native as N
+    from cacheslide_b200.position import _Holder, _base_params
+
+    hq, hkv, d, bs = 32, 8, 128, 16
+    g = torch.Generator().manual_seed(nk)
+    q = (torch.randn(len(rows), hq, d, generator=g) / d ** 0.5).to(torch.bfloat16).to(cuda)
+    k = (torch.randn(nk, hkv, d, generator=g) / d ** 0.5).to(torch.bfloat16).to(cuda)
+    v = torch.randn(nk, hkv, d, generator=g).to(torch.bfloat16).to(cuda)
+    E = torch.randn(d, 64, generator=g) * 0.02
+    qpos = torch.tensor(rows, device=cuda)
+    nb = (nk + bs - 1) // bs + 5
+    perm = torch.randperm(nb, generator=g)[: (nk + bs - 1) // bs].to(cuda)
+    tok = torch.arange(nk, device=cuda)
+    slots = perm[tok // bs] * bs + tok % bs
+    cache = torch.zeros(nb, hkv, bs, 2 * d, dtype=torch.bfloat16, device=cuda)
+    cache[slots // bs, :, slots % bs, :d] = k
+    cache[slots // bs, :, slots % bs, d:] = v
+    cope = _cope(E.numpy(), cuda)
+    holder = _Holder(cope, cope.position_embeddings.detach())
+    outs = []
+    lib = N.load()
+    for use_decode in (True, False):
+        out = torch.empty(len(rows), hq, d, dtype=torch.bfloat16, device=cuda)
+        p = _base_params(q, None, None, holder, qpos, None, nk, hkv, d)
+        p.paged = N.paged_view(cache)
+        p.kv_slots = slots.data_ptr()
+        p.out = out.data_ptr()
+        p.o_stride_tok, p.o_stride_head = out.stride(0), out.stride(1)
+        st = N.Status(cuda)
+        p.status = st.ptr
+        import ctypes
+
+        if use_decode:
+            size = lib.cs_cope_attn_decode_workspace(ctypes.byref(p))
+            assert size > 0
+            ws = torch.empty(size, dtype=torch.uint8, device=cuda)
+            N.check(lib.cs_cope_attn_decode(ctypes.byref(p), ws.data_ptr(),
+                                            N.stream_of(cuda)), "decode")
+        else:
+            N.check(lib.cs_cope_attn(ctypes.byref(p), N.stream_of(cuda)), "generic")
+        assert st.read() == 0
+        outs.append(out.float().cpu().numpy())
+    want = ocope.cope_attention(q.float().cpu().numpy(), k.float().cpu().numpy(),
+                                v.float().cpu().numpy(), E.numpy(), np.array(rows))
+    np.testing.assert_allclose(outs[0], want, **BF16)
+    np.testing.assert_allclose(outs[0], outs[1], **BF16)
+
+
 # ----------------------------------------- reference known answers (float64)
 def test_known_visibility_after_gates(cuda):
     cope = CoPE(1, 8, device=cuda, dtype=torch.float64)

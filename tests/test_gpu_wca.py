@@ -63,8 +63,9 @@ def test_select_topk_matches_stable_argsort_with_ties(cuda, n):
     from cacheslide_b200 import _native as N
 
     st = N.Status(cuda)
+    keys_d, avail_d = _t(keys, cuda), _t(avail, cuda)  # alive across the launch
     N.check(N.load().cs_wca_select_topk(
-        _t(keys, cuda).data_ptr(), _t(avail, cuda).data_ptr(), n, slots, sel.data_ptr(),
+        keys_d.data_ptr(), avail_d.data_ptr(), n, slots, sel.data_ptr(),
         chosen.data_ptr(), count.data_ptr(), st.ptr, N.stream_of(cuda)), "select")
     k = int(count.item())
     assert k == len(expect)
