@@ -1,0 +1,686 @@
+// Tensor-core CoPE / CCPE prefill for sm_100a (tcgen05 + TMEM).
+//
+// One CTA computes a 128-row tile: R = 128 / G query rows x the G query heads
+// of one KV head (GQA packing: every row of the tile reads the same K/V).
+// Warp roles (288 threads):
+//   warps 0-3  softmax: thread r owns S row r (TMEM lane r).  For each key
+//              tile it reads S with tcgen05.ld, walks the 128 columns from
+//              the newest key backwards with a thread-local running gate count
+//              (the reverse cumulative sum of position.py:295-307, restarted
+//              at chunk boundaries in the chunk-reset mode), interpolates the
+//              q.E bias from a per-row table in shared memory, applies the
+//              causal / association masks, updates the online softmax and
+//              writes P (bf16) to shared memory.  Once a row's count has
+//              saturated at npos-1 every older key has the same bias and only
+//              the logit and the exponential are computed.
+//   warps 4-7  producer: Q tile, the E table split into bf16 hi + lo, and
+//              the K/V tiles of every key tile (double buffered), read through
+//              the per-key slot table with 16-byte cp.async into the 128-byte
+//              swizzled UMMA layout (paged, relocated and dense keys alike).
+//   warp 8     MMA issuer (one thread) and TMEM owner: T = Q E (hi + lo),
+//              S = Q K^T for tile t+1 while the softmax works on tile t, then
+//              O += P V; completions are tracked with tcgen05.commit.
+// TMEM (512 columns): S0 [0,128), S1 [128,256), O [256,384), T [384,448).
+// Every mbarrier wait is bounded; on expiry the CTA raises CS_ST_TIMEOUT,
+// drains its copies and MMAs, frees its TMEM and returns.
+#include <math.h>
+
+#include "common.cuh"
+
+namespace cs {
+
+int validate_attn_params(const cs_attn_params* p);
+
+namespace {
+
+constexpr int kThreads = 288;
+constexpr int kTileN = 128;  // keys per tile
+constexpr int kD = 128;      // head dim of this kernel
+constexpr int kMaxNpos = 64;
+
+// shared memory map (bytes from a 1024-aligned base)
+constexpr uint32_t kQ = 0;                   // 32 KB  Q tile   [2 cb][128 rows][128 B]
+constexpr uint32_t kK0 = 32768;              // 2 x 32 KB K tiles
+constexpr uint32_t kV0 = 98304;              // 2 x 32 KB V tiles
+constexpr uint32_t kP = 163840;              // 32 KB  P tile (E hi/lo staging at start)
+constexpr uint32_t kT = 196608;              // 32 KB  q.E table [128][64] fp32
+constexpr uint32_t kMeta = 229376;           // barriers + per-tile key metadata
+constexpr uint32_t kSmemBytes = kMeta + 1536 + 1024;  // + alignment slack
+
+// metadata block layout (offsets from kMeta)
+constexpr uint32_t kBarQ = 0;        // producer -> MMA: Q + E staged
+constexpr uint32_t kBarT = 8;        // MMA -> softmax: T ready
+constexpr uint32_t kBarKV = 16;      // [2] producer -> MMA: K/V tile staged
+constexpr uint32_t kBarS = 32;       // [2] MMA -> softmax: S tile ready
+constexpr uint32_t kBarP = 48;       // softmax -> MMA: P tile staged
+constexpr uint32_t kBarPV = 56;      // [2] MMA -> all: PV tile done
+constexpr uint32_t kBarEnd = 72;     // MMA drain
+constexpr uint32_t kTmemSlot = 80;   // TMEM base address
+constexpr uint32_t kAbort = 84;      // abort flag
+constexpr uint32_t kNtile = 88;      // key tiles of this CTA
+constexpr uint32_t kFixMask = 96;    // [2 stages][4 words] key is fixed
+constexpr uint32_t kBndMask = 128;   // [2 stages][4 words] last key of a chunk
+constexpr uint32_t kChunk = 160;     // [2 stages][128] chunk id per key (int32)
+// kChunk + 1024 = 1184 < 1536
+
+constexpr uint32_t kColS0 = 0, kColO = 256, kColT = 384;
+constexpr long long kWaitCycles = 1000000000ll;  // ~0.5 s at 1.9 GHz
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ------------------------------------------------------------------ mbarrier
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// bounded wait; returns false (and raises the abort flag) on expiry
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+  long long t0 = clock64();
+  while (!mbar_try(bar, parity)) {
+    if (*abort) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      *abort = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
+// ------------------------------------------------------------------ tcgen05
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+#define CS_TMEM_LD32(taddr, r)                                                                   \
+  asm volatile(                                                                                  \
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"    \
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"         \
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),     \
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), \
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),           \
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),           \
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])            \
+      : "r"(taddr))
+
+#define CS_TMEM_ST32(taddr, r)                                                                   \
+  asm volatile(                                                                                  \
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"     \
+      "%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"( \
+          taddr),                                                                                \
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),   \
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),          \
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),        \
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),        \
+      "r"(r[29]), "r"(r[30]), "r"(r[31]))
+
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// UMMA shared-memory descriptor, 128-byte swizzle (sm100 layout type 2)
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for sm100
+  d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+  return d;
+}
+
+// instruction descriptor: kind::f16, f32 accumulate, dense
+__device__ __forceinline__ uint32_t umma_idesc(int m, int n, int fmt, int a_mn, int b_mn) {
+  return (1u << 4) | ((uint32_t)fmt << 7) | ((uint32_t)fmt << 10) | ((uint32_t)a_mn << 15) |
+         ((uint32_t)b_mn << 16) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// byte offset of 16-byte chunk `c16` (0..15) of row `row` in a K-major
+// 128-byte-swizzled tile of `rows` rows and 128 bf16 columns
+__device__ __forceinline__ uint32_t sw128(int row, int c16, int rows) {
+  return (uint32_t)((c16 >> 3) * rows * 128 + row * 128 + (((c16 & 7) ^ (row & 7)) << 4));
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+struct Args {
+  cs_attn_params p;
+  PagedView pv;
+  int G, R, fmt;  // heads per KV head, rows per tile, 0 = f16 / 1 = bf16
+  int tiles_per_head;
+};
+
+template <typename T>
+__device__ __forceinline__ const char* kv_row(const Args& a, int64_t j, int g, int half,
+                                              bool& ok) {
+  const cs_attn_params& p = a.p;
+  if (p.kv_slots) {
+    const int64_t s = p.kv_slots[j];
+    ok = a.pv.valid(s);
+    return ok ? a.pv.addr(s, g, half ? kD : 0) : nullptr;
+  }
+  ok = true;
+  const char* base = static_cast<const char*>(half ? p.v : p.k);
+  const int64_t st = half ? p.v_stride_tok : p.k_stride_tok;
+  const int64_t sh = half ? p.v_stride_head : p.k_stride_head;
+  return base + (j * st + (int64_t)g * sh) * (int64_t)sizeof(T);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_constant__ Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const cs_attn_params& p = a.p;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  uint8_t* meta = smem + kMeta;
+  volatile int* abort = reinterpret_cast<volatile int*>(meta + kAbort);
+  const uint32_t mb = sbase + kMeta;
+
+  // tile coordinates: heavy (late) query tiles first
+  const int g = blockIdx.x / a.tiles_per_head;
+  const int tile = a.tiles_per_head - 1 - (blockIdx.x % a.tiles_per_head);
+  const int64_t i0 = (int64_t)tile * a.R;
+  const int G = a.G, R = a.R;
+  const float top = (float)(p.npos - 1);
+
+  if (tid == 0) {
+    mbar_init(mb + kBarQ, 128);
+    mbar_init(mb + kBarT, 1);
+    mbar_init(mb + kBarKV, 128);
+    mbar_init(mb + kBarKV + 8, 128);
+    mbar_init(mb + kBarS, 1);
+    mbar_init(mb + kBarS + 8, 1);
+    mbar_init(mb + kBarP, 128);
+    mbar_init(mb + kBarPV, 1);
+    mbar_init(mb + kBarPV + 8, 1);
+    mbar_init(mb + kBarEnd, 1);
+    *abort = 0;
+    // key tiles needed by the furthest row of this tile
+    int64_t nmax = 0;
+    for (int r = 0; r < R; ++r) {
+      const int64_t i = i0 + r;
+      if (i >= p.nq) break;
+      const int64_t qp = p.qpos[i];
+      const int64_t n = qp + 1 < p.nk ? qp + 1 : p.nk;
+      nmax = n > nmax ? n : nmax;
+    }
+    *reinterpret_cast<int*>(meta + kNtile) = (int)((nmax + kTileN - 1) / kTileN);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 8) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     mb + kTmemSlot),
+                 "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(meta + kTmemSlot);
+  const int ntile = *reinterpret_cast<volatile int*>(meta + kNtile);
+
+  if (warp >= 4 && warp < 8) {
+    // ================================================================ producer
+    const int pt = tid - 128;  // 0..127
+    // Q rows: row r = head-local * R + row-local
+    for (int idx = pt; idx < 128 * 16; idx += 128) {
+      const int r = idx >> 4, c16 = idx & 15;
+      const int64_t i = i0 + (r % R);
+      const int h = g * G + r / R;
+      const bool ok = i < p.nq;
+      const char* src = static_cast<const char*>(p.q) +
+                        ((ok ? i : 0) * p.q_stride_tok + (int64_t)h * p.q_stride_head) *
+                            (int64_t)sizeof(T) +
+                        c16 * 16;
+      cp_async16(sbase + kQ + sw128(r, c16, 128), src, ok);
+    }
+    // E^T split into hi + lo halves (rows = positions, cols = head dim)
+    const float* E = static_cast<const float*>(p.E);
+    for (int idx = pt; idx < kMaxNpos * kD; idx += 128) {
+      const int pp = idx / kD, dd = idx - pp * kD;
+      float e = pp < p.npos ? E[(int64_t)dd * p.e_stride_d + (int64_t)pp * p.e_stride_p] : 0.f;
+      T hi = Elem<T>::from_f(e);
+      T lo = Elem<T>::from_f(e - Elem<T>::to_f(hi));
+      const uint32_t off = sw128(pp, dd >> 3, kMaxNpos) + (dd & 7) * 2;
+      *reinterpret_cast<T*>(smem + kP + off) = hi;
+      *reinterpret_cast<T*>(smem + kP + 16384 + off) = lo;
+    }
+    cp_async_wait_all();
+    fence_async_smem();
+    mbar_arrive(mb + kBarQ);
+
+    for (int it = 0; it < ntile && !*abort; ++it) {
+      const int st = it & 1;
+      const int kt = ntile - 1 - it;
+      if (it >= 2 && !mbar_wait(mb + kBarPV + 8 * st, ((it - 2) >> 1) & 1, abort)) break;
+      // thread pt loads key row (pt >> 4) + 8*m, 16-byte chunk pt & 15
+      for (int m = 0; m < 16; ++m) {
+        const int row = (pt >> 4) + 8 * m, c16 = pt & 15;
+        const int64_t j = (int64_t)kt * kTileN + row;
+        bool ok = false;
+        const char* kr = nullptr;
+        const char* vr = nullptr;
+        if (j < p.nk) {
+          kr = kv_row<T>(a, j, g, 0, ok);
+          if (ok) vr = kv_row<T>(a, j, g, 1, ok);
+        }
+        const void* fallback = p.q;
+        cp_async16(sbase + kK0 + st * 32768 + sw128(row, c16, 128), ok ? kr + c16 * 16 : fallback,
+                   ok);
+        cp_async16(sbase + kV0 + st * 32768 + sw128(row, c16, 128), ok ? vr + c16 * 16 : fallback,
+                   ok);
+      }
+      // key metadata of this tile: fixed flag, chunk id, chunk-end flag
+      {
+        const int64_t j = (int64_t)kt * kTileN + pt;
+        const bool in = j < p.nk;
+        const bool fixed = in && p.k_fixed != nullptr && p.k_fixed[j] != 0;
+        int kc = -1;
+        bool bnd = false;
+        if (in && p.pos_mode == CS_POS_CHUNK) {
+          kc = p.key_chunk[j];
+          bnd = (j + 1 < p.nk) && p.key_chunk[j + 1] != kc;
+        }
+        reinterpret_cast<int*>(meta + kChunk)[st * 128 + pt] = kc;
+        const unsigned fm = __ballot_sync(0xffffffffu, fixed);
+        const unsigned bm = __ballot_sync(0xffffffffu, bnd);
+        if (lane == 0) {
+          reinterpret_cast<unsigned*>(meta + kFixMask)[st * 4 + (warp - 4)] = fm;
+          reinterpret_cast<unsigned*>(meta + kBndMask)[st * 4 + (warp - 4)] = bm;
+        }
+      }
+      cp_async_wait_all();
+      fence_async_smem();
+      mbar_arrive(mb + kBarKV + 8 * st);
+    }
+    cp_async_wait_all();
+  } else if (warp == 8) {
+    // ================================================================== MMA
+    if (lane == 0) {
+      const uint32_t id_s = umma_idesc(128, 128, a.fmt, 0, 0);   // S = Q K^T
+      const uint32_t id_t = umma_idesc(128, 64, a.fmt, 0, 0);    // T = Q E
+      const uint32_t id_o = umma_idesc(128, 128, a.fmt, 0, 1);   // O += P V (V MN-major)
+      bool ok = mbar_wait(mb + kBarQ, 0, abort);
+      if (ok) {
+        tc_fence_after();
+        for (int half = 0; half < 2; ++half) {
+          for (int kk = 0; kk < kD / 16; ++kk) {
+            const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
+            const uint32_t boff = half * 16384 + (kk >> 2) * 8192 + (kk & 3) * 32;
+            tc_mma(tmem + kColT, umma_desc(sbase + kQ + aoff, 16, 1024),
+                   umma_desc(sbase + kP + boff, 16, 1024), id_t, (half | kk) ? 1u : 0u);
+          }
+        }
+        tc_commit(mb + kBarT);
+      }
+      auto issue_qk = [&](int it) {
+        const int st = it & 1;
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          tc_mma(tmem + kColS0 + st * 128, umma_desc(sbase + kQ + off, 16, 1024),
+                 umma_desc(sbase + kK0 + st * 32768 + off, 16, 1024), id_s, kk ? 1u : 0u);
+        }
+        tc_commit(mb + kBarS + 8 * st);
+      };
+      if (ok && ntile > 0) {
+        ok = mbar_wait(mb + kBarKV, 0, abort);
+        if (ok) {
+          tc_fence_after();
+          issue_qk(0);
+        }
+      }
+      for (int it = 0; ok && it < ntile; ++it) {
+        const int st = it & 1;
+        if (it + 1 < ntile) {
+          if (!(ok = mbar_wait(mb + kBarKV + 8 * ((it + 1) & 1), ((it + 1) >> 1) & 1, abort)))
+            break;
+          tc_fence_after();
+          issue_qk(it + 1);
+        }
+        if (!(ok = mbar_wait(mb + kBarP, it & 1, abort))) break;
+        tc_fence_after();
+        for (int kk = 0; kk < kTileN / 16; ++kk) {
+          const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;    // P: K-major
+          const uint32_t boff = kk * 2048;                             // V: MN-major
+          tc_mma(tmem + kColO, umma_desc(sbase + kP + aoff, 16, 1024),
+                 umma_desc(sbase + kV0 + st * 32768 + boff, 16384, 1024), id_o,
+                 (it | kk) ? 1u : 0u);
+        }
+        tc_commit(mb + kBarPV + 8 * st);
+      }
+      // drain every MMA issued by this thread before TMEM is released
+      tc_commit(mb + kBarEnd);
+      long long t0 = clock64();
+      while (!mbar_try(mb + kBarEnd, 0) && clock64() - t0 < kWaitCycles) {
+      }
+    }
+    __syncwarp();
+  } else {
+    // ================================================================ softmax
+    const int r = tid;  // TMEM lane == tile row
+    const int64_t i = i0 + (r % R);
+    const int h = g * G + r / R;
+    const bool row_ok = i < p.nq;
+    const int64_t qp = row_ok ? p.qpos[i] : -1;
+    const int64_t nlim = row_ok ? (qp + 1 < p.nk ? qp + 1 : p.nk) : 0;
+    const bool qsel = row_ok && p.q_selected != nullptr && p.q_selected[i] != 0;
+    const int qchunk =
+        (row_ok && p.pos_mode == CS_POS_CHUNK && nlim > 0) ? p.key_chunk[nlim - 1] : -1;
+    const float* offrow = (row_ok && p.pos_mode == CS_POS_CHUNK)
+                              ? p.chunk_off + (int64_t)h * p.co_stride_h + i * p.co_stride_q
+                              : nullptr;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    float* Ts = reinterpret_cast<float*>(smem + kT) + r * kMaxNpos;
+    const int sw = r & 31;
+    const float inv_sqrt_d = (float)(1.0 / p.scale);
+    const float LOG2E = 1.4426950408889634f;
+    float tsat = 0.f;
+
+    bool ok = mbar_wait(mb + kBarT, 0, abort);
+    {
+      tc_fence_after();
+      uint32_t v[32];
+      for (int half = 0; half < 2; ++half) {
+        CS_TMEM_LD32(tmem + lane_base + kColT + half * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) Ts[(half * 32 + c) ^ sw] = __uint_as_float(v[c]);
+      }
+      tsat = Ts[(p.npos - 1) ^ sw];
+    }
+
+    float carry = 0.f;     // running count entering the newer edge of the tile
+    float mref = -INFINITY;  // softmax reference max (log2 domain)
+    float lsum = 0.f;
+    ok = __all_sync(0xffffffffu, ok);
+    for (int it = 0; ok && it < ntile; ++it) {
+      const int st = it & 1;
+      const int kt = ntile - 1 - it;
+      const int64_t key0 = (int64_t)kt * kTileN;
+      // S(it) from the MMA warp; the K/V barrier (already complete) publishes
+      // the producer's key metadata of this stage to this thread
+      ok = mbar_wait(mb + kBarS + 8 * st, (it >> 1) & 1, abort) &&
+           mbar_wait(mb + kBarKV + 8 * st, (it >> 1) & 1, abort);
+      if (!(ok = __all_sync(0xffffffffu, ok))) break;
+      tc_fence_after();
+      const unsigned* fixm = reinterpret_cast<const unsigned*>(meta + kFixMask) + st * 4;
+      const unsigned* bndm = reinterpret_cast<const unsigned*>(meta + kBndMask) + st * 4;
+      const int* kch = reinterpret_cast<const int*>(meta + kChunk) + st * 128;
+      const int nvalid = (int)(nlim - key0 < 0 ? 0 : (nlim - key0 > kTileN ? kTileN : nlim - key0));
+      // saturation: the count is already >= npos-1 and no boundary in this tile
+      // restarts it below that value
+      bool sat = carry >= top;
+      if (sat && offrow != nullptr) {
+        for (int w = 0; w < 4 && sat; ++w) {
+          unsigned bits = bndm[w];
+          while (bits && sat) {
+            const int c = w * 32 + __ffs(bits) - 1;
+            bits &= bits - 1;
+            if (c >= nvalid) continue;
+            const int kc = kch[c];
+            if (kc < qchunk) {
+              const float off = offrow[kc];
+              if (off >= 0.f && off < top) sat = false;
+            }
+          }
+        }
+      }
+      float sc[kTileN];
+      float tmax = -INFINITY;
+      float R = carry;
+#pragma unroll
+      for (int cc = 3; cc >= 0; --cc) {
+        uint32_t v[32];
+        CS_TMEM_LD32(tmem + lane_base + kColS0 + st * 128 + cc * 32, v);
+        tmem_wait_ld();
+        const unsigned fx = fixm[cc];
+        const unsigned bd = bndm[cc];
+#pragma unroll
+        for (int c = 31; c >= 0; --c) {
+          const int col = cc * 32 + c;
+          const float L = __uint_as_float(v[c]) * inv_sqrt_d;
+          float s2 = -INFINITY;
+          if (col < nvalid) {
+            float bias;
+            if (sat) {
+              bias = tsat;
+            } else {
+              const float e = ex2(-L * LOG2E);
+              const float gt = __fdividef(1.f, 1.f + e);
+              float base = R;
+              if ((bd >> c) & 1u) {
+                const int kc = kch[col];
+                if (kc < qchunk) {
+                  const float off = offrow[kc];
+                  if (off >= 0.f) base = off;
+                }
+              }
+              R = base + gt;
+              const float pos = fminf(R, top);
+              const float fl = floorf(pos);
+              const int lo = (int)fl;
+              const int hi = lo + 1 < p.npos ? lo + 1 : p.npos - 1;
+              const float tlo = Ts[lo ^ sw];
+              bias = fmaf(pos - fl, Ts[hi ^ sw] - tlo, tlo);
+            }
+            bool vis = true;
+            if (qsel && ((fx >> c) & 1u)) vis = (key0 + col) == qp;
+            if (vis) {
+              s2 = (L + bias) * LOG2E;
+              tmax = fmaxf(tmax, s2);
+            }
+          }
+          sc[col] = s2;
+        }
+      }
+      carry = sat ? fmaxf(carry, top) : R;
+      // PV of the previous tile must finish before O and P are touched
+      if (it > 0) {
+        ok = mbar_wait(mb + kBarPV + 8 * ((it - 1) & 1), ((it - 1) >> 1) & 1, abort);
+        if (!(ok = __all_sync(0xffffffffu, ok))) break;
+        tc_fence_after();
+      }
+      float mnew = mref;
+      bool rescale = false;
+      if (tmax > mref + 8.f) {  // lazy rescaling: keep the stale max unless it lags by 2^8
+        mnew = tmax;
+        rescale = mref > -INFINITY;
+      }
+      if (it > 0 && __any_sync(0xffffffffu, rescale)) {
+        const float f = rescale ? ex2(mref - mnew) : 1.f;
+        lsum *= f;
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t v[32];
+          CS_TMEM_LD32(tmem + lane_base + kColO + cc * 32, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) v[c] = __float_as_uint(__uint_as_float(v[c]) * f);
+          CS_TMEM_ST32(tmem + lane_base + kColO + cc * 32, v);
+        }
+        tmem_wait_st();
+      }
+      mref = mnew;
+      // P = 2^(s - mref) in bf16/f16, row r of the K-major swizzled P tile
+      float part = 0.f;
+#pragma unroll
+      for (int c16 = 0; c16 < 16; ++c16) {
+        uint32_t w[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int col = c16 * 8 + u * 2;
+          const float e0 = sc[col] > -INFINITY ? ex2(sc[col] - mref) : 0.f;
+          const float e1 = sc[col + 1] > -INFINITY ? ex2(sc[col + 1] - mref) : 0.f;
+          T t0 = Elem<T>::from_f(e0), t1 = Elem<T>::from_f(e1);
+          part += Elem<T>::to_f(t0) + Elem<T>::to_f(t1);
+          w[u] = (uint32_t)(*reinterpret_cast<uint16_t*>(&t0)) |
+                 ((uint32_t)(*reinterpret_cast<uint16_t*>(&t1)) << 16);
+        }
+        *reinterpret_cast<uint4*>(smem + kP + sw128(r, c16, 128)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      lsum += part;
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(mb + kBarP);
+    }
+    // epilogue: O / l for this row
+    if (ok && ntile > 0) {
+      ok = mbar_wait(mb + kBarPV + 8 * ((ntile - 1) & 1), ((ntile - 1) >> 1) & 1, abort);
+      ok = __all_sync(0xffffffffu, ok);
+      tc_fence_after();
+    }
+    int32_t bits = 0;
+    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+    for (int cc = 0; cc < 4; ++cc) {
+      uint32_t v[32];
+      if (ntile > 0) {
+        CS_TMEM_LD32(tmem + lane_base + kColO + cc * 32, v);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) v[c] = 0u;
+      }
+      if (row_ok && ok) {
+        char* orow = static_cast<char*>(p.out) +
+                     (i * p.o_stride_tok + (int64_t)h * p.o_stride_head) * dtype_size(p.out_dtype);
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          const float x0 = lsum > 0.f ? __uint_as_float(v[c]) * inv : 0.f;
+          const float x1 = lsum > 0.f ? __uint_as_float(v[c + 1]) * inv : 0.f;
+          if (!isfinite(x0) || !isfinite(x1)) bits |= CS_ST_LOGIT_NONFINITE;
+          const int e = cc * 32 + c;
+          if (p.out_dtype == CS_F32) {
+            reinterpret_cast<float2*>(orow)[e / 2] = make_float2(x0, x1);
+          } else {
+            T t0 = Elem<T>::from_f(x0), t1 = Elem<T>::from_f(x1);
+            const uint32_t packed = (uint32_t)(*reinterpret_cast<uint16_t*>(&t0)) |
+                                    ((uint32_t)(*reinterpret_cast<uint16_t*>(&t1)) << 16);
+            reinterpret_cast<uint32_t*>(orow)[e / 2] = packed;
+          }
+        }
+      }
+    }
+    if (bits) report(p.status, bits);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (tid == 0 && *abort) report(p.status, CS_ST_TIMEOUT);
+  if (warp == 8) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+  }
+}
+
+bool prefill_supported(const cs_attn_params* p) {
+  if (p->in_dtype != CS_BF16 && p->in_dtype != CS_F16) return false;
+  if (p->out_dtype != p->in_dtype && p->out_dtype != CS_F32) return false;
+  if (p->d != kD || p->dv != kD) return false;
+  if (p->npos > kMaxNpos) return false;
+  const int G = p->hq / p->hkv;
+  if (G < 1 || G > 128 || 128 % G) return false;
+  if (p->pos_mode != CS_POS_CONTEXTUAL && p->pos_mode != CS_POS_CHUNK) return false;
+  if (p->gate_mask || p->vis_mask || p->out_positions || p->positions_only || p->strict)
+    return false;
+  if (p->kpos != nullptr) return false;
+  const int es = 2;
+  auto al = [](int64_t x) { return (x % 16) == 0; };
+  if (!al(reinterpret_cast<uintptr_t>(p->q)) || !al(p->q_stride_tok * es) ||
+      !al(p->q_stride_head * es))
+    return false;
+  if (p->kv_slots) {
+    PagedView pv = PagedView::make(p->paged);
+    if (!pv.vec16()) return false;
+  } else {
+    if (!al(reinterpret_cast<uintptr_t>(p->k)) || !al(reinterpret_cast<uintptr_t>(p->v)) ||
+        !al(p->k_stride_tok * es) || !al(p->k_stride_head * es) || !al(p->v_stride_tok * es) ||
+        !al(p->v_stride_head * es))
+      return false;
+  }
+  return true;
+}
+
+}  // namespace
+}  // namespace cs
+
+using namespace cs;
+
+extern "C" int cs_cope_attn_prefill(const cs_attn_params* p, void* stream) {
+  int rc = validate_attn_params(p);
+  if (rc != CS_OK) return rc;
+  if (!prefill_supported(p)) return CS_ERR_UNSUPPORTED;
+  if (p->nq == 0) return CS_OK;
+  Args a;
+  a.p = *p;
+  a.pv = p->kv_slots ? PagedView::make(p->paged) : PagedView{};
+  a.G = p->hq / p->hkv;
+  a.R = 128 / a.G;
+  a.fmt = p->in_dtype == CS_BF16 ? 1 : 0;
+  a.tiles_per_head = (p->nq + a.R - 1) / a.R;
+  const int blocks = a.tiles_per_head * p->hkv;
+  static bool configured[2] = {false, false};
+  auto launch = [&](auto kern, int which) -> int {
+    if (!configured[which]) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)kSmemBytes) != cudaSuccess)
+        return CS_ERR_CUDA;
+      configured[which] = true;
+    }
+    kern<<<blocks, kThreads, kSmemBytes, as_stream(stream)>>>(a);
+    CS_LAUNCH_CHECK();
+    return CS_OK;
+  };
+  if (p->in_dtype == CS_BF16) return launch(cope_prefill_sm100<__nv_bfloat16>, 1);
+  return launch(cope_prefill_sm100<__half>, 0);
+}

@@ -217,6 +217,80 @@ def test_paged_attention_reads_through_slots(cuda):
     np.testing.assert_allclose(out.float().cpu().numpy(), dense.float().cpu().numpy(), **BF16)
 
 
+@pytest.mark.parametrize("assoc,chunk,paged", [(False, False, False), (True, False, True),
+                                               (False, True, True), (True, True, False)])
+@pytest.mark.parametrize("hq,hkv", [(32, 8), (8, 1)])
+def test_tensor_core_prefill_matches_generic_and_oracle(cuda, assoc, chunk, paged, hq, hkv):
+    """cs_cope_attn_prefill (tcgen05) vs cs_cope_attn and the oracle."""
+    import ctypes
+
+    from cacheslide_b200 import _native as N
+    from cacheslide_b200.position import _Holder, _base_params
+
+    nq, nk, d, bs = 300, 2000, 128, 16
+    g = torch.Generator().manual_seed(hq * 7 + assoc + 2 * chunk + 4 * paged)
+    q = (torch.randn(nq, hq, d, generator=g) / d ** 0.5).to(torch.bfloat16).to(cuda)
+    k = (torch.randn(nk, hkv, d, generator=g) / d ** 0.5).to(torch.bfloat16).to(cuda)
+    v = torch.randn(nk, hkv, d, generator=g).to(torch.bfloat16).to(cuda)
+    rows = torch.sort(torch.randperm(nk, generator=g)[:nq]).values.to(cuda)
+    E = torch.randn(d, 64, generator=g) * 0.02
+    cope = _cope(E.numpy(), cuda)
+    holder = _Holder(cope, cope.position_embeddings.detach())
+    fixed = torch.rand(nk, generator=g) < 0.7
+    selected = torch.nonzero(fixed & (torch.rand(nk, generator=g) < 0.3)).flatten()
+    q_sel = torch.isin(rows.cpu(), selected).to(torch.uint8).to(cuda)
+    k_fix = fixed.to(torch.uint8).to(cuda)
+    key_chunk = (torch.arange(nk) // 250).to(torch.int32)
+    nch = int(key_chunk.max()) + 1
+    offsets = torch.rand(hq, nk, nch, generator=g) * 8
+    offsets[:, :, 1::3] = -1
+    off_rows = offsets[:, rows.cpu()].contiguous().to(cuda)
+    kc_dev = key_chunk.to(cuda)
+    cache = slots = None
+    if paged:
+        nb = (nk + bs - 1) // bs + 7
+        perm = torch.randperm(nb, generator=g)[: (nk + bs - 1) // bs].to(cuda)
+        tok = torch.arange(nk, device=cuda)
+        slots = perm[tok // bs] * bs + tok % bs
+        cache = torch.zeros(nb, hkv, bs, 2 * d, dtype=torch.bfloat16, device=cuda)
+        cache[slots // bs, :, slots % bs, :d] = k
+        cache[slots // bs, :, slots % bs, d:] = v
+    lib = N.load()
+    outs = []
+    for fast in (True, False):
+        out = torch.empty(nq, hq, d, dtype=torch.bfloat16, device=cuda)
+        p = _base_params(q, None if paged else k, None if paged else v, holder, rows, None,
+                         nk, hkv, d)
+        if paged:
+            p.paged = N.paged_view(cache)
+            p.kv_slots = slots.data_ptr()
+        p.out = out.data_ptr()
+        p.o_stride_tok, p.o_stride_head = out.stride(0), out.stride(1)
+        if assoc:
+            p.q_selected, p.k_fixed = q_sel.data_ptr(), k_fix.data_ptr()
+        if chunk:
+            p.pos_mode = N.POS_CHUNK
+            p.key_chunk, p.chunk_off = kc_dev.data_ptr(), off_rows.data_ptr()
+            p.co_stride_h, p.co_stride_q = off_rows.stride(0), off_rows.stride(1)
+            p.nchunks = nch
+        st = N.Status(cuda)
+        p.status = st.ptr
+        fn = lib.cs_cope_attn_prefill if fast else lib.cs_cope_attn
+        N.check(fn(ctypes.byref(p), N.stream_of(cuda)), "prefill" if fast else "generic")
+        assert st.read() == 0
+        outs.append(out.float().cpu().numpy())
+    np.testing.assert_allclose(outs[0], outs[1], **BF16)
+    kw = {}
+    if assoc:
+        kw["visibility_fn"] = lambda a, b: ocope.association_mask(
+            a, b, np.nonzero(fixed.numpy())[0], selected.numpy())
+    if chunk:
+        kw["chunk_reset"] = (key_chunk.numpy(), off_rows.cpu().numpy())
+    want = ocope.cope_attention(q.float().cpu().numpy(), k.float().cpu().numpy(),
+                                v.float().cpu().numpy(), E.numpy(), rows.cpu().numpy(), **kw)
+    np.testing.assert_allclose(outs[0], want, **BF16)
+
+
 @pytest.mark.parametrize("nk,rows", [(4097, [4096]), (1500, [700, 1200, 1499]), (513, [512])])
 def test_split_key_decode_matches_oracle_and_generic(cuda, nk, rows):
     """Decode rows through the paged cache: split-key kernel vs oracle and vs
