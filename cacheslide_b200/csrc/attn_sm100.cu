@@ -4,21 +4,24 @@
 // of one KV head (GQA packing: every row of the tile reads the same K/V).
 // Warp roles (288 threads):
 //   warps 0-3  softmax: thread r owns S row r (TMEM lane r).  For each key
-//              tile it reads S with tcgen05.ld, walks the 128 columns from
-//              the newest key backwards with a thread-local running gate count
-//              (the reverse cumulative sum of position.py:295-307, restarted
-//              at chunk boundaries in the chunk-reset mode), interpolates the
-//              q.E bias from a per-row table in shared memory, applies the
-//              causal / association masks, updates the online softmax and
-//              writes P (bf16) to shared memory.  Once a row's count has
-//              saturated at npos-1 every older key has the same bias and only
-//              the logit and the exponential are computed.
+//              tile it reads S with tcgen05.ld in 32-column chunks, walks the
+//              columns from the newest key backwards with a thread-local
+//              running gate count (the reverse cumulative sum of
+//              position.py:295-307, restarted at chunk boundaries in the
+//              chunk-reset mode), interpolates the q.E bias from a per-row
+//              table in shared memory and applies the causal / association
+//              masks.  Scores go back to TMEM; a second pass forms
+//              P = 2^(s - m) (bf16) in shared memory and the row sums.  Once
+//              every row of a warp has a count >= npos-1 all older keys share
+//              one bias and only the logit and the exponential remain.
 //   warps 4-7  producer: Q tile, the E table split into bf16 hi + lo, and
-//              the K/V tiles of every key tile (double buffered), read through
-//              the per-key slot table with 16-byte cp.async into the 128-byte
-//              swizzled UMMA layout (paged, relocated and dense keys alike).
+//              the K and V tiles of every key tile (two stages each), read
+//              through the per-key slot table (paged, relocated and dense keys
+//              alike) with 16-byte cp.async into the 128-byte swizzled UMMA
+//              layout.  Copy completion arrives on the stage barriers
+//              asynchronously (cp.async.mbarrier.arrive.noinc).
 //   warp 8     MMA issuer (one thread) and TMEM owner: T = Q E (hi + lo),
-//              S = Q K^T for tile t+1 while the softmax works on tile t, then
+//              S(t+1) = Q K^T while the softmax works on tile t, then
 //              O += P V; completions are tracked with tcgen05.commit.
 // TMEM (512 columns): S0 [0,128), S1 [128,256), O [256,384), T [384,448).
 // Every mbarrier wait is bounded; on expiry the CTA raises CS_ST_TIMEOUT,
@@ -38,34 +41,35 @@ constexpr int kTileN = 128;  // keys per tile
 constexpr int kD = 128;      // head dim of this kernel
 constexpr int kMaxNpos = 64;
 
-// shared memory map (bytes from a 1024-aligned base)
-constexpr uint32_t kQ = 0;                   // 32 KB  Q tile   [2 cb][128 rows][128 B]
-constexpr uint32_t kK0 = 32768;              // 2 x 32 KB K tiles
-constexpr uint32_t kV0 = 98304;              // 2 x 32 KB V tiles
-constexpr uint32_t kP = 163840;              // 32 KB  P tile (E hi/lo staging at start)
-constexpr uint32_t kT = 196608;              // 32 KB  q.E table [128][64] fp32
-constexpr uint32_t kMeta = 229376;           // barriers + per-tile key metadata
-constexpr uint32_t kSmemBytes = kMeta + 1536 + 1024;  // + alignment slack
+// shared memory map (bytes from the 1024-aligned dynamic base)
+constexpr uint32_t kQ = 0;         // 32 KB  Q tile   [2 cb][128 rows][128 B]
+constexpr uint32_t kK0 = 32768;    // 2 x 32 KB K tiles
+constexpr uint32_t kV0 = 98304;    // 2 x 32 KB V tiles
+constexpr uint32_t kP = 163840;    // 32 KB  P tile (E hi/lo staging at start)
+constexpr uint32_t kT = 196608;    // 32 KB  q.E table [128][64] fp32
+constexpr uint32_t kMeta = 229376; // barriers, flags, key metadata, row addresses
 
-// metadata block layout (offsets from kMeta)
-constexpr uint32_t kBarQ = 0;        // producer -> MMA: Q + E staged
-constexpr uint32_t kBarT = 8;        // MMA -> softmax: T ready
-constexpr uint32_t kBarKV = 16;      // [2] producer -> MMA: K/V tile staged
-constexpr uint32_t kBarS = 32;       // [2] MMA -> softmax: S tile ready
-constexpr uint32_t kBarP = 48;       // softmax -> MMA: P tile staged
-constexpr uint32_t kBarPV = 56;      // [2] MMA -> all: PV tile done
-constexpr uint32_t kBarEnd = 72;     // MMA drain
-constexpr uint32_t kTmemSlot = 80;   // TMEM base address
-constexpr uint32_t kAbort = 84;      // abort flag
-constexpr uint32_t kNtile = 88;      // key tiles of this CTA
-constexpr uint32_t kFixMask = 96;    // [2 stages][4 words] key is fixed
-constexpr uint32_t kBndMask = 128;   // [2 stages][4 words] last key of a chunk
-constexpr uint32_t kChunk = 160;     // [2 stages][128] chunk id per key (int32)
-// kChunk + 1024 = 1184 < 1536
+// metadata block (offsets from kMeta)
+constexpr uint32_t kBarQ = 0;       // producer -> MMA: Q + E staged
+constexpr uint32_t kBarT = 8;       // MMA -> softmax: T ready
+constexpr uint32_t kBarK = 16;      // [2] producer -> MMA: K tile
+constexpr uint32_t kBarV = 32;      // [2] producer -> MMA: V tile
+constexpr uint32_t kBarS = 48;      // [2] MMA -> softmax/producer: S tile ready
+constexpr uint32_t kBarP = 64;      // softmax -> MMA: P tile staged
+constexpr uint32_t kBarPV = 72;     // [2] MMA -> all: PV tile done
+constexpr uint32_t kBarEnd = 88;    // MMA drain
+constexpr uint32_t kTmemSlot = 96;  // TMEM base address
+constexpr uint32_t kAbort = 100;    // abort flag
+constexpr uint32_t kNtile = 104;    // key tiles of this CTA
+constexpr uint32_t kFixMask = 112;  // [4 slots][4 words] key is fixed
+constexpr uint32_t kBndMask = 176;  // [4 slots][4 words] key is the last of its chunk
+constexpr uint32_t kBarMeta = 240;  // [4] producer -> softmax: key metadata of slot it % 4
+constexpr uint32_t kRowAddr = 272;  // [2 stages][128] K row address (bit 0: sidecar)
+constexpr uint32_t kMetaBytes = kRowAddr + 2 * 128 * 8;
+constexpr uint32_t kSmemBytes = kMeta + kMetaBytes;  // 231,696 B
 
 constexpr uint32_t kColS0 = 0, kColO = 256, kColT = 384;
 constexpr long long kWaitCycles = 1000000000ll;  // ~0.5 s at 1.9 GHz
-
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -193,37 +197,93 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void producer_sync() {  // the 128 producer threads
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+// floor of a nonnegative float below 2^22 with plain FP adds (round-down
+// add of 1.5 * 2^23 leaves the integer part in the low mantissa bits)
+__device__ __forceinline__ float floor_pos(float x, int& i) {
+  const float t = __fadd_rd(x, 12582912.0f);
+  i = __float_as_int(t) - 0x4B400000;
+  return t - 12582912.0f;
+}
+
+template <typename T> struct Pack2;
+template <> struct Pack2<__nv_bfloat16> {
+  static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+};
+template <> struct Pack2<__half> {
+  static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+};
+
 struct Args {
   cs_attn_params p;
   PagedView pv;
   int G, R, fmt;  // heads per KV head, rows per tile, 0 = f16 / 1 = bf16
   int tiles_per_head;
+  int bs_shift;   // log2(block size) when it is a power of two, else -1
 };
 
+// K row address of key j for KV head g (0 = no row: zero fill); bit 0 tags a
+// sidecar row, whose V lives at the same offset in side_v
 template <typename T>
-__device__ __forceinline__ const char* kv_row(const Args& a, int64_t j, int g, int half,
-                                              bool& ok) {
+__device__ __forceinline__ uint64_t key_row_addr(const Args& a, int64_t j, int g) {
   const cs_attn_params& p = a.p;
+  if (j >= p.nk) return 0;
   if (p.kv_slots) {
     const int64_t s = p.kv_slots[j];
-    ok = a.pv.valid(s);
-    return ok ? a.pv.addr(s, g, half ? kD : 0) : nullptr;
+    const PagedView& pv = a.pv;
+    if (!pv.valid(s)) return 0;
+    if (s < pv.native_total) {
+      int64_t b, o;
+      if (a.bs_shift >= 0) {
+        b = s >> a.bs_shift;
+        o = s - (b << a.bs_shift);
+      } else {
+        b = s / pv.bs;
+        o = s - b * pv.bs;
+      }
+      return reinterpret_cast<uint64_t>(pv.cache + b * pv.sb + g * pv.sh + o * pv.so);
+    }
+    const int64_t r = s - pv.native_total;
+    return reinterpret_cast<uint64_t>(pv.side_k + r * pv.ssr + g * pv.ssh) | 1ull;
   }
-  ok = true;
-  const char* base = static_cast<const char*>(half ? p.v : p.k);
-  const int64_t st = half ? p.v_stride_tok : p.k_stride_tok;
-  const int64_t sh = half ? p.v_stride_head : p.k_stride_head;
-  return base + (j * st + (int64_t)g * sh) * (int64_t)sizeof(T);
+  return reinterpret_cast<uint64_t>(static_cast<const char*>(p.k) +
+                                    (j * p.k_stride_tok + (int64_t)g * p.k_stride_head) *
+                                        (int64_t)sizeof(T));
+}
+
+template <typename T>
+__device__ __forceinline__ const char* value_row_addr(const Args& a, uint64_t kaddr, int64_t j,
+                                                      int g) {
+  const cs_attn_params& p = a.p;
+  if (p.kv_slots) {
+    if (kaddr & 1ull) return a.pv.side_v + ((kaddr & ~1ull) - reinterpret_cast<uint64_t>(a.pv.side_k));
+    return reinterpret_cast<const char*>(kaddr) + kD * a.pv.se;
+  }
+  return static_cast<const char*>(p.v) +
+         (j * p.v_stride_tok + (int64_t)g * p.v_stride_head) * (int64_t)sizeof(T);
 }
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_constant__ Args a) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
   const cs_attn_params& p = a.p;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (sbase & 1023) {  // the UMMA swizzle atoms need a 1024-byte aligned base
+    if (tid == 0) report(p.status, CS_ST_TIMEOUT);
+    return;
+  }
   uint8_t* meta = smem + kMeta;
   volatile int* abort = reinterpret_cast<volatile int*>(meta + kAbort);
   const uint32_t mb = sbase + kMeta;
@@ -238,17 +298,17 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
   if (tid == 0) {
     mbar_init(mb + kBarQ, 128);
     mbar_init(mb + kBarT, 1);
-    mbar_init(mb + kBarKV, 128);
-    mbar_init(mb + kBarKV + 8, 128);
-    mbar_init(mb + kBarS, 1);
-    mbar_init(mb + kBarS + 8, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(mb + kBarK + 8 * s, 128);  // one copy-completion arrival per producer thread
+      mbar_init(mb + kBarV + 8 * s, 128);
+      mbar_init(mb + kBarS + 8 * s, 1);
+      mbar_init(mb + kBarPV + 8 * s, 1);
+    }
+    for (int s = 0; s < 4; ++s) mbar_init(mb + kBarMeta + 8 * s, 128);
     mbar_init(mb + kBarP, 128);
-    mbar_init(mb + kBarPV, 1);
-    mbar_init(mb + kBarPV + 8, 1);
     mbar_init(mb + kBarEnd, 1);
     *abort = 0;
-    // key tiles needed by the furthest row of this tile
-    int64_t nmax = 0;
+    int64_t nmax = 0;  // keys needed by the furthest row of this tile
     for (int r = 0; r < R; ++r) {
       const int64_t i = i0 + r;
       if (i >= p.nq) break;
@@ -274,8 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
   if (warp >= 4 && warp < 8) {
     // ================================================================ producer
     const int pt = tid - 128;  // 0..127
-    // Q rows: row r = head-local * R + row-local
-    for (int idx = pt; idx < 128 * 16; idx += 128) {
+    for (int idx = pt; idx < 128 * 16; idx += 128) {  // Q: row r = head-local * R + row-local
       const int r = idx >> 4, c16 = idx & 15;
       const int64_t i = i0 + (r % R);
       const int h = g * G + r / R;
@@ -286,8 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
                         c16 * 16;
       cp_async16(sbase + kQ + sw128(r, c16, 128), src, ok);
     }
-    // E^T split into hi + lo halves (rows = positions, cols = head dim)
-    const float* E = static_cast<const float*>(p.E);
+    const float* E = static_cast<const float*>(p.E);  // E^T split into hi + lo
     for (int idx = pt; idx < kMaxNpos * kD; idx += 128) {
       const int pp = idx / kD, dd = idx - pp * kD;
       float e = pp < p.npos ? E[(int64_t)dd * p.e_stride_d + (int64_t)pp * p.e_stride_p] : 0.f;
@@ -301,57 +359,58 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
     fence_async_smem();
     mbar_arrive(mb + kBarQ);
 
-    for (int it = 0; it < ntile && !*abort; ++it) {
-      const int st = it & 1;
+    uint64_t* rowaddr = reinterpret_cast<uint64_t*>(meta + kRowAddr);
+    for (int it = 0; it < ntile; ++it) {
+      const int st = it & 1, slot = it & 3;
       const int kt = ntile - 1 - it;
-      if (it >= 2 && !mbar_wait(mb + kBarPV + 8 * st, ((it - 2) >> 1) & 1, abort)) break;
-      // thread pt loads key row (pt >> 4) + 8*m, 16-byte chunk pt & 15
-      for (int m = 0; m < 16; ++m) {
-        const int row = (pt >> 4) + 8 * m, c16 = pt & 15;
-        const int64_t j = (int64_t)kt * kTileN + row;
-        bool ok = false;
-        const char* kr = nullptr;
-        const char* vr = nullptr;
-        if (j < p.nk) {
-          kr = kv_row<T>(a, j, g, 0, ok);
-          if (ok) vr = kv_row<T>(a, j, g, 1, ok);
-        }
-        const void* fallback = p.q;
-        cp_async16(sbase + kK0 + st * 32768 + sw128(row, c16, 128), ok ? kr + c16 * 16 : fallback,
-                   ok);
-        cp_async16(sbase + kV0 + st * 32768 + sw128(row, c16, 128), ok ? vr + c16 * 16 : fallback,
-                   ok);
-      }
-      // key metadata of this tile: fixed flag, chunk id, chunk-end flag
+      const int64_t key0 = (int64_t)kt * kTileN;
+      // K stage free once QK(it-2) completed; metadata slot it%4 then too
+      if (it >= 2 && !mbar_wait(mb + kBarS + 8 * st, ((it - 2) >> 1) & 1, abort)) break;
       {
-        const int64_t j = (int64_t)kt * kTileN + pt;
+        const int64_t j = key0 + pt;
+        rowaddr[st * 128 + pt] = key_row_addr<T>(a, j, g);
         const bool in = j < p.nk;
         const bool fixed = in && p.k_fixed != nullptr && p.k_fixed[j] != 0;
-        int kc = -1;
-        bool bnd = false;
-        if (in && p.pos_mode == CS_POS_CHUNK) {
-          kc = p.key_chunk[j];
-          bnd = (j + 1 < p.nk) && p.key_chunk[j + 1] != kc;
-        }
-        reinterpret_cast<int*>(meta + kChunk)[st * 128 + pt] = kc;
+        const bool bnd = in && p.pos_mode == CS_POS_CHUNK && (j + 1 < p.nk) &&
+                         p.key_chunk[j + 1] != p.key_chunk[j];
         const unsigned fm = __ballot_sync(0xffffffffu, fixed);
         const unsigned bm = __ballot_sync(0xffffffffu, bnd);
         if (lane == 0) {
-          reinterpret_cast<unsigned*>(meta + kFixMask)[st * 4 + (warp - 4)] = fm;
-          reinterpret_cast<unsigned*>(meta + kBndMask)[st * 4 + (warp - 4)] = bm;
+          reinterpret_cast<unsigned*>(meta + kFixMask)[slot * 4 + (warp - 4)] = fm;
+          reinterpret_cast<unsigned*>(meta + kBndMask)[slot * 4 + (warp - 4)] = bm;
         }
       }
-      cp_async_wait_all();
-      fence_async_smem();
-      mbar_arrive(mb + kBarKV + 8 * st);
+      mbar_arrive(mb + kBarMeta + 8 * slot);  // metadata published (release)
+      producer_sync();                   // every row address visible
+      const int c16 = pt & 15;
+#pragma unroll 4
+      for (int m = 0; m < 16; ++m) {
+        const int row = (pt >> 4) + 8 * m;
+        const uint64_t ka = rowaddr[st * 128 + row];
+        const char* src = ka ? reinterpret_cast<const char*>(ka & ~1ull) + c16 * 16
+                             : static_cast<const char*>(p.q);
+        cp_async16(sbase + kK0 + st * 32768 + sw128(row, c16, 128), src, ka != 0);
+      }
+      cp_async_arrive_noinc(mb + kBarK + 8 * st);
+      // V stage free once PV(it-2) completed
+      if (it >= 2 && !mbar_wait(mb + kBarPV + 8 * st, ((it - 2) >> 1) & 1, abort)) break;
+#pragma unroll 4
+      for (int m = 0; m < 16; ++m) {
+        const int row = (pt >> 4) + 8 * m;
+        const uint64_t ka = rowaddr[st * 128 + row];
+        const char* src = ka ? value_row_addr<T>(a, ka, key0 + row, g) + c16 * 16
+                             : static_cast<const char*>(p.q);
+        cp_async16(sbase + kV0 + st * 32768 + sw128(row, c16, 128), src, ka != 0);
+      }
+      cp_async_arrive_noinc(mb + kBarV + 8 * st);
     }
     cp_async_wait_all();
   } else if (warp == 8) {
     // ================================================================== MMA
     if (lane == 0) {
-      const uint32_t id_s = umma_idesc(128, 128, a.fmt, 0, 0);   // S = Q K^T
-      const uint32_t id_t = umma_idesc(128, 64, a.fmt, 0, 0);    // T = Q E
-      const uint32_t id_o = umma_idesc(128, 128, a.fmt, 0, 1);   // O += P V (V MN-major)
+      const uint32_t id_s = umma_idesc(128, 128, a.fmt, 0, 0);  // S = Q K^T
+      const uint32_t id_t = umma_idesc(128, 64, a.fmt, 0, 0);   // T = Q E
+      const uint32_t id_o = umma_idesc(128, 128, a.fmt, 0, 1);  // O += P V (V MN-major)
       bool ok = mbar_wait(mb + kBarQ, 0, abort);
       if (ok) {
         tc_fence_after();
@@ -375,8 +434,9 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
         tc_commit(mb + kBarS + 8 * st);
       };
       if (ok && ntile > 0) {
-        ok = mbar_wait(mb + kBarKV, 0, abort);
+        ok = mbar_wait(mb + kBarK, 0, abort);
         if (ok) {
+          fence_async_smem();
           tc_fence_after();
           issue_qk(0);
         }
@@ -384,16 +444,19 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
       for (int it = 0; ok && it < ntile; ++it) {
         const int st = it & 1;
         if (it + 1 < ntile) {
-          if (!(ok = mbar_wait(mb + kBarKV + 8 * ((it + 1) & 1), ((it + 1) >> 1) & 1, abort)))
+          if (!(ok = mbar_wait(mb + kBarK + 8 * ((it + 1) & 1), ((it + 1) >> 1) & 1, abort)))
             break;
+          fence_async_smem();
           tc_fence_after();
           issue_qk(it + 1);
         }
         if (!(ok = mbar_wait(mb + kBarP, it & 1, abort))) break;
+        if (!(ok = mbar_wait(mb + kBarV + 8 * st, (it >> 1) & 1, abort))) break;
+        fence_async_smem();
         tc_fence_after();
         for (int kk = 0; kk < kTileN / 16; ++kk) {
-          const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;    // P: K-major
-          const uint32_t boff = kk * 2048;                             // V: MN-major
+          const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;  // P: K-major
+          const uint32_t boff = kk * 2048;                           // V: MN-major
           tc_mma(tmem + kColO, umma_desc(sbase + kP + aoff, 16, 1024),
                  umma_desc(sbase + kV0 + st * 32768 + boff, 16384, 1024), id_o,
                  (it | kk) ? 1u : 0u);
@@ -416,21 +479,22 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
     const int64_t qp = row_ok ? p.qpos[i] : -1;
     const int64_t nlim = row_ok ? (qp + 1 < p.nk ? qp + 1 : p.nk) : 0;
     const bool qsel = row_ok && p.q_selected != nullptr && p.q_selected[i] != 0;
-    const int qchunk =
-        (row_ok && p.pos_mode == CS_POS_CHUNK && nlim > 0) ? p.key_chunk[nlim - 1] : -1;
-    const float* offrow = (row_ok && p.pos_mode == CS_POS_CHUNK)
-                              ? p.chunk_off + (int64_t)h * p.co_stride_h + i * p.co_stride_q
-                              : nullptr;
+    const bool chunked = p.pos_mode == CS_POS_CHUNK;
+    const int qchunk = (row_ok && chunked && nlim > 0) ? p.key_chunk[nlim - 1] : -1;
+    const float* offrow =
+        (row_ok && chunked) ? p.chunk_off + (int64_t)h * p.co_stride_h + i * p.co_stride_q
+                            : nullptr;
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
     float* Ts = reinterpret_cast<float*>(smem + kT) + r * kMaxNpos;
     const int sw = r & 31;
     const float inv_sqrt_d = (float)(1.0 / p.scale);
     const float LOG2E = 1.4426950408889634f;
-    float tsat = 0.f;
+    const int hi_max = p.npos - 1;
 
     bool ok = mbar_wait(mb + kBarT, 0, abort);
+    tc_fence_after();
+    float tsat;
     {
-      tc_fence_after();
       uint32_t v[32];
       for (int half = 0; half < 2; ++half) {
         CS_TMEM_LD32(tmem + lane_base + kColT + half * 32, v);
@@ -440,36 +504,37 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
       }
       tsat = Ts[(p.npos - 1) ^ sw];
     }
+    const float tsat2 = tsat * LOG2E;
 
-    float carry = 0.f;     // running count entering the newer edge of the tile
+    float carry = 0.f;       // running count entering the newer edge of the tile
     float mref = -INFINITY;  // softmax reference max (log2 domain)
     float lsum = 0.f;
     ok = __all_sync(0xffffffffu, ok);
     for (int it = 0; ok && it < ntile; ++it) {
-      const int st = it & 1;
+      const int st = it & 1, slot = it & 3;
       const int kt = ntile - 1 - it;
       const int64_t key0 = (int64_t)kt * kTileN;
-      // S(it) from the MMA warp; the K/V barrier (already complete) publishes
-      // the producer's key metadata of this stage to this thread
+      // S(it) from the MMA warp; the metadata barrier of slot it % 4 cannot run
+      // ahead of this wait (slot reuse needs P(it) from this warpgroup)
       ok = mbar_wait(mb + kBarS + 8 * st, (it >> 1) & 1, abort) &&
-           mbar_wait(mb + kBarKV + 8 * st, (it >> 1) & 1, abort);
+           mbar_wait(mb + kBarMeta + 8 * slot, (it >> 2) & 1, abort);
       if (!(ok = __all_sync(0xffffffffu, ok))) break;
       tc_fence_after();
-      const unsigned* fixm = reinterpret_cast<const unsigned*>(meta + kFixMask) + st * 4;
-      const unsigned* bndm = reinterpret_cast<const unsigned*>(meta + kBndMask) + st * 4;
-      const int* kch = reinterpret_cast<const int*>(meta + kChunk) + st * 128;
-      const int nvalid = (int)(nlim - key0 < 0 ? 0 : (nlim - key0 > kTileN ? kTileN : nlim - key0));
-      // saturation: the count is already >= npos-1 and no boundary in this tile
-      // restarts it below that value
+      const unsigned* fixm = reinterpret_cast<const unsigned*>(meta + kFixMask) + slot * 4;
+      const unsigned* bndm = reinterpret_cast<const unsigned*>(meta + kBndMask) + slot * 4;
+      const int nvalid =
+          (int)(nlim - key0 < 0 ? 0 : (nlim - key0 > kTileN ? kTileN : nlim - key0));
+      // a row is saturated when its count is already >= npos-1 and no chunk
+      // boundary of this tile restarts it below that value
       bool sat = carry >= top;
-      if (sat && offrow != nullptr) {
+      if (chunked && sat) {
         for (int w = 0; w < 4 && sat; ++w) {
           unsigned bits = bndm[w];
           while (bits && sat) {
             const int c = w * 32 + __ffs(bits) - 1;
             bits &= bits - 1;
             if (c >= nvalid) continue;
-            const int kc = kch[c];
+            const int kc = p.key_chunk[key0 + c];
             if (kc < qchunk) {
               const float off = offrow[kc];
               if (off >= 0.f && off < top) sat = false;
@@ -477,55 +542,61 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
           }
         }
       }
-      float sc[kTileN];
+      const bool warp_sat = __all_sync(0xffffffffu, sat || nvalid == 0);
+      float Rc = carry;
       float tmax = -INFINITY;
-      float R = carry;
-#pragma unroll
       for (int cc = 3; cc >= 0; --cc) {
         uint32_t v[32];
-        CS_TMEM_LD32(tmem + lane_base + kColS0 + st * 128 + cc * 32, v);
+        const uint32_t taddr = tmem + lane_base + kColS0 + st * 128 + cc * 32;
+        CS_TMEM_LD32(taddr, v);
         tmem_wait_ld();
-        const unsigned fx = fixm[cc];
-        const unsigned bd = bndm[cc];
+        const unsigned fx = qsel ? fixm[cc] : 0u;
+        const int lim = nvalid - cc * 32;          // columns below lim are causal
+        const int self = (int)(qp - key0) - cc * 32;  // column of the query itself
+        if (warp_sat) {
 #pragma unroll
-        for (int c = 31; c >= 0; --c) {
-          const int col = cc * 32 + c;
-          const float L = __uint_as_float(v[c]) * inv_sqrt_d;
-          float s2 = -INFINITY;
-          if (col < nvalid) {
-            float bias;
-            if (sat) {
-              bias = tsat;
-            } else {
-              const float e = ex2(-L * LOG2E);
-              const float gt = __fdividef(1.f, 1.f + e);
-              float base = R;
-              if ((bd >> c) & 1u) {
-                const int kc = kch[col];
-                if (kc < qchunk) {
-                  const float off = offrow[kc];
-                  if (off >= 0.f) base = off;
-                }
-              }
-              R = base + gt;
-              const float pos = fminf(R, top);
-              const float fl = floorf(pos);
-              const int lo = (int)fl;
-              const int hi = lo + 1 < p.npos ? lo + 1 : p.npos - 1;
-              const float tlo = Ts[lo ^ sw];
-              bias = fmaf(pos - fl, Ts[hi ^ sw] - tlo, tlo);
-            }
-            bool vis = true;
-            if (qsel && ((fx >> c) & 1u)) vis = (key0 + col) == qp;
-            if (vis) {
-              s2 = (L + bias) * LOG2E;
-              tmax = fmaxf(tmax, s2);
-            }
+          for (int c = 0; c < 32; ++c) {
+            float s = fmaf(__uint_as_float(v[c]), inv_sqrt_d * LOG2E, tsat2);
+            const bool hide = (c >= lim) || (((fx >> c) & 1u) && c != self);
+            s = hide ? -INFINITY : s;
+            tmax = fmaxf(tmax, s);
+            v[c] = __float_as_uint(s);
           }
-          sc[col] = s2;
+        } else {
+          const unsigned bd = bndm[cc];
+#pragma unroll
+          for (int c = 31; c >= 0; --c) {
+            const float L = __uint_as_float(v[c]) * inv_sqrt_d;
+            const float e = ex2(-L * LOG2E);
+            const float gt = __fdividef(1.f, 1.f + e);
+            float base = Rc;
+            if ((bd >> c) & 1u) {  // warp-uniform: last key of a chunk
+              const int kc = p.key_chunk[key0 + cc * 32 + c];
+              if (kc < qchunk) {
+                const float off = offrow[kc];
+                base = off >= 0.f ? off : base;
+              }
+            }
+            const bool live = c < lim;
+            Rc = live ? base + gt : Rc;
+            const float pos = fminf(Rc, top);
+            int lo;
+            const float fl = floor_pos(pos, lo);
+            const int hi = lo < hi_max ? lo + 1 : hi_max;
+            const float tlo = Ts[lo ^ sw];
+            const float bias = fmaf(pos - fl, Ts[hi ^ sw] - tlo, tlo);
+            float s = (L + bias) * LOG2E;
+            const bool hide = !live || (((fx >> c) & 1u) && c != self);
+            s = hide ? -INFINITY : s;
+            tmax = fmaxf(tmax, s);
+            v[c] = __float_as_uint(s);
+          }
         }
+        CS_TMEM_ST32(taddr, v);  // scores back into the S buffer
       }
-      carry = sat ? fmaxf(carry, top) : R;
+      tmem_wait_st();
+      // rows whose keys all lie in the future of this tile keep their count
+      carry = warp_sat ? (sat ? fmaxf(carry, top) : carry) : Rc;
       // PV of the previous tile must finish before O and P are touched
       if (it > 0) {
         ok = mbar_wait(mb + kBarPV + 8 * ((it - 1) & 1), ((it - 1) >> 1) & 1, abort);
@@ -534,7 +605,7 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
       }
       float mnew = mref;
       bool rescale = false;
-      if (tmax > mref + 8.f) {  // lazy rescaling: keep the stale max unless it lags by 2^8
+      if (tmax > mref + 8.f) {  // lazy rescaling: keep a stale max unless it lags by 2^8
         mnew = tmax;
         rescale = mref > -INFINITY;
       }
@@ -552,22 +623,26 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
         tmem_wait_st();
       }
       mref = mnew;
-      // P = 2^(s - mref) in bf16/f16, row r of the K-major swizzled P tile
+      // P = 2^(s - mref) packed to bf16/f16 into row r of the swizzled P tile
+      const float mcur = mref > -INFINITY ? mref : 0.f;
       float part = 0.f;
+      for (int cc = 0; cc < 4; ++cc) {
+        uint32_t v[32];
+        CS_TMEM_LD32(tmem + lane_base + kColS0 + st * 128 + cc * 32, v);
+        tmem_wait_ld();
 #pragma unroll
-      for (int c16 = 0; c16 < 16; ++c16) {
-        uint32_t w[4];
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint32_t w[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int col = c16 * 8 + u * 2;
-          const float e0 = sc[col] > -INFINITY ? ex2(sc[col] - mref) : 0.f;
-          const float e1 = sc[col + 1] > -INFINITY ? ex2(sc[col + 1] - mref) : 0.f;
-          T t0 = Elem<T>::from_f(e0), t1 = Elem<T>::from_f(e1);
-          part += Elem<T>::to_f(t0) + Elem<T>::to_f(t1);
-          w[u] = (uint32_t)(*reinterpret_cast<uint16_t*>(&t0)) |
-                 ((uint32_t)(*reinterpret_cast<uint16_t*>(&t1)) << 16);
+          for (int u = 0; u < 4; ++u) {
+            const float e0 = ex2(__uint_as_float(v[q4 * 8 + 2 * u]) - mcur);
+            const float e1 = ex2(__uint_as_float(v[q4 * 8 + 2 * u + 1]) - mcur);
+            part += e0 + e1;
+            w[u] = Pack2<T>::pack(e0, e1);
+          }
+          *reinterpret_cast<uint4*>(smem + kP + sw128(r, cc * 4 + q4, 128)) =
+              make_uint4(w[0], w[1], w[2], w[3]);
         }
-        *reinterpret_cast<uint4*>(smem + kP + sw128(r, c16, 128)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
       lsum += part;
       fence_async_smem();
@@ -582,6 +657,10 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
     }
     int32_t bits = 0;
     const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+    char* orow = row_ok ? static_cast<char*>(p.out) + (i * p.o_stride_tok +
+                                                       (int64_t)h * p.o_stride_head) *
+                                                          dtype_size(p.out_dtype)
+                        : nullptr;
     for (int cc = 0; cc < 4; ++cc) {
       uint32_t v[32];
       if (ntile > 0) {
@@ -592,21 +671,29 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
         for (int c = 0; c < 32; ++c) v[c] = 0u;
       }
       if (row_ok && ok) {
-        char* orow = static_cast<char*>(p.out) +
-                     (i * p.o_stride_tok + (int64_t)h * p.o_stride_head) * dtype_size(p.out_dtype);
+        if (p.out_dtype == CS_F32) {
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          const float x0 = lsum > 0.f ? __uint_as_float(v[c]) * inv : 0.f;
-          const float x1 = lsum > 0.f ? __uint_as_float(v[c + 1]) * inv : 0.f;
-          if (!isfinite(x0) || !isfinite(x1)) bits |= CS_ST_LOGIT_NONFINITE;
-          const int e = cc * 32 + c;
-          if (p.out_dtype == CS_F32) {
-            reinterpret_cast<float2*>(orow)[e / 2] = make_float2(x0, x1);
-          } else {
-            T t0 = Elem<T>::from_f(x0), t1 = Elem<T>::from_f(x1);
-            const uint32_t packed = (uint32_t)(*reinterpret_cast<uint16_t*>(&t0)) |
-                                    ((uint32_t)(*reinterpret_cast<uint16_t*>(&t1)) << 16);
-            reinterpret_cast<uint32_t*>(orow)[e / 2] = packed;
+          for (int c = 0; c < 32; c += 4) {
+            float4 x = make_float4(__uint_as_float(v[c]) * inv, __uint_as_float(v[c + 1]) * inv,
+                                   __uint_as_float(v[c + 2]) * inv,
+                                   __uint_as_float(v[c + 3]) * inv);
+            if (!isfinite(x.x + x.y + x.z + x.w)) bits |= CS_ST_LOGIT_NONFINITE;
+            reinterpret_cast<float4*>(orow)[(cc * 32 + c) / 4] = x;
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; c += 8) {
+            uint32_t w[4];
+            float chk = 0.f;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const float x0 = __uint_as_float(v[c + 2 * u]) * inv;
+              const float x1 = __uint_as_float(v[c + 2 * u + 1]) * inv;
+              chk += x0 + x1;
+              w[u] = Pack2<T>::pack(x0, x1);
+            }
+            if (!isfinite(chk)) bits |= CS_ST_LOGIT_NONFINITE;
+            reinterpret_cast<uint4*>(orow)[(cc * 32 + c) / 8] = make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
       }
@@ -639,6 +726,9 @@ bool prefill_supported(const cs_attn_params* p) {
   if (!al(reinterpret_cast<uintptr_t>(p->q)) || !al(p->q_stride_tok * es) ||
       !al(p->q_stride_head * es))
     return false;
+  if (!al(reinterpret_cast<uintptr_t>(p->out)) || !al(p->o_stride_tok * dtype_size(p->out_dtype)) ||
+      !al(p->o_stride_head * dtype_size(p->out_dtype)))
+    return false;
   if (p->kv_slots) {
     PagedView pv = PagedView::make(p->paged);
     if (!pv.vec16()) return false;
@@ -668,6 +758,15 @@ extern "C" int cs_cope_attn_prefill(const cs_attn_params* p, void* stream) {
   a.R = 128 / a.G;
   a.fmt = p->in_dtype == CS_BF16 ? 1 : 0;
   a.tiles_per_head = (p->nq + a.R - 1) / a.R;
+  a.bs_shift = -1;
+  if (p->kv_slots) {
+    const int64_t bs = p->paged.block_size;
+    if ((bs & (bs - 1)) == 0) {
+      int s = 0;
+      while ((1ll << s) < bs) ++s;
+      a.bs_shift = s;
+    }
+  }
   const int blocks = a.tiles_per_head * p->hkv;
   static bool configured[2] = {false, false};
   auto launch = [&](auto kern, int which) -> int {
