@@ -15,7 +15,7 @@ import torch
 
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libcacheslide_sm100.so"
 
-CS_OK, CS_ERR_INVALID, CS_ERR_CUDA, CS_ERR_UNSUPPORTED = 0, 1, 2, 3
+CS_OK, CS_ERR_INVALID, CS_ERR_CUDA, CS_ERR_UNSUPPORTED, CS_ERR_TOO_LARGE = 0, 1, 2, 3, 4
 CS_F32, CS_F16, CS_BF16, CS_F64 = 0, 1, 2, 3
 
 ST_SLOT_RANGE = 1 << 0
@@ -107,6 +107,7 @@ _SIGNATURES = {
     "cs_cope_attn_prefill": [ctypes.POINTER(AttnParams), _p],
     "cs_cope_attn_decode_workspace": [ctypes.POINTER(AttnParams)],
     "cs_cope_attn_decode": [ctypes.POINTER(AttnParams), _p, _p],
+    "cs_cope_attn_decode_noalloc": [ctypes.POINTER(AttnParams), _p],
     "cs_cope_positions": [_p, _i64, _i64, _p, _i64, _i64, _i32, _i64, _i64, _i32, _i32, _p,
                           _i64, _i64, _p, _p],
     "cs_cope_bias": [_p, _i64, _i64, _p, _i64, _i64, _i32, _i32, _p, _i64, _i64, _i32, _i64,

@@ -38,7 +38,8 @@ typedef enum {
   CS_OK = 0,
   CS_ERR_INVALID = 1,     /* bad argument; nothing was enqueued            */
   CS_ERR_CUDA = 2,        /* a CUDA runtime call or launch failed          */
-  CS_ERR_UNSUPPORTED = 3  /* shape/dtype combination this build lacks      */
+  CS_ERR_UNSUPPORTED = 3, /* shape/dtype combination this build lacks      */
+  CS_ERR_TOO_LARGE = 4    /* needs more than a fixed internal capacity     */
 } cs_status;
 
 typedef enum { CS_F32 = 0, CS_F16 = 1, CS_BF16 = 2, CS_F64 = 3 } cs_dtype;
@@ -295,6 +296,24 @@ CS_API int cs_cope_attn_prefill(const cs_attn_params* p, void* stream);
 CS_API int64_t cs_cope_attn_decode_workspace(const cs_attn_params* p);
 CS_API int cs_cope_attn_decode(const cs_attn_params* p, void* workspace,
                         void* stream);
+
+/*
+ * Decode that allocates nothing (no counterpart in the reference; it exists
+ * for callers that must not allocate device memory, e.g. a plugin inside an
+ * inference engine that already gave all free HBM to its KV-cache pool, or a
+ * foreign-language host without a CUDA allocator).  Same kernels and results
+ * as cs_cope_attn_decode; the workspace comes from 16 MiB of static device
+ * memory inside this library, held by every GPU that loads it until exit.
+ * - Problems needing more than 16 MiB (cs_cope_attn_decode_workspace) return
+ *   CS_ERR_TOO_LARGE without launching anything.
+ * - The first call on a device resolves the array's device address with that
+ *   device current; make that first call before any stream capture, and make
+ *   the stream's device current for every call.
+ * - All calls on a device share the one array: calls that overlap on the GPU
+ *   (different streams, no ordering between them) race and corrupt each
+ *   other's results.  Nothing in it needs to start at zero.
+ */
+CS_API int cs_cope_attn_decode_noalloc(const cs_attn_params* p, void* stream);
 
 /* ------------------------------------------- standalone CoPE operators */
 /*
