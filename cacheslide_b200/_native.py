@@ -108,6 +108,8 @@ _SIGNATURES = {
     "cs_cope_attn_decode_workspace": [ctypes.POINTER(AttnParams)],
     "cs_cope_attn_decode": [ctypes.POINTER(AttnParams), _p, _p],
     "cs_cope_attn_decode_noalloc": [ctypes.POINTER(AttnParams), _p],
+    "cs_cope_attn_decode_batch_workspace": [ctypes.POINTER(AttnParams), _i32],
+    "cs_cope_attn_decode_batch": [ctypes.POINTER(AttnParams), _i32, _p, _p],
     "cs_cope_positions": [_p, _i64, _i64, _p, _i64, _i64, _i32, _i64, _i64, _i32, _i32, _p,
                           _i64, _i64, _p, _p],
     "cs_cope_bias": [_p, _i64, _i64, _p, _i64, _i64, _i32, _i32, _p, _i64, _i64, _i32, _i64,
@@ -118,7 +120,8 @@ _SIGNATURES = {
     "cs_abi_version": [],
 }
 _RESTYPES = {"cs_build_info": ctypes.c_char_p, "cs_abi_version": _i32,
-             "cs_cope_attn_decode_workspace": _i64}
+             "cs_cope_attn_decode_workspace": _i64,
+             "cs_cope_attn_decode_batch_workspace": _i64}
 
 EXPORTED = tuple(_SIGNATURES)
 

@@ -1,4 +1,5 @@
-// Split-key CoPE decode: a few query rows over a long paged context.
+// Split-key CoPE decode: a few query rows over a long paged context, for up
+// to kMaxBatch requests per launch.
 //
 // The contextual position of key j is the sum of the gates of all newer keys,
 // so a key split cannot finish on its own: phase 1 computes every split's
@@ -6,7 +7,9 @@
 // carried from the newer splits, finishes the reverse scan, the interpolated
 // bias and a partial softmax with its PV (reading V once), and a combine
 // kernel merges the split partials.  K and V each cross HBM once; the logits
-// and partials (a few hundred KB) stay in L2.
+// and partials (a few hundred KB per row) stay in L2.  All requests of a
+// batch share the three launches, so a decode step of a whole batch costs
+// three kernel launches instead of three per request.
 //
 // Modes: contextual positions, plain causal (the decode row of a CacheSlide
 // request is a dynamic token: no canonical substitution, no association
@@ -21,66 +24,90 @@ int validate_attn_params(const cs_attn_params* p);
 
 namespace {
 
-constexpr int kSplit = 128;    // keys per split == threads per CTA
-constexpr int kMaxG = 8;       // query heads per KV head handled by one CTA
+constexpr int kSplit = 128;  // keys per split == threads per CTA
+constexpr int kMaxG = 8;     // query heads per KV head handled by one CTA
 constexpr int kMaxD = 256;
+constexpr int kMaxBatch = 8;
 
-struct DecodeArgs {
-  cs_attn_params p;
+// one request of a batch (compact, so a batch fits the kernel parameters)
+struct DecodeReq {
+  const char* q;
+  int64_t q_st, q_sh;
+  const int64_t* qpos;
+  const int64_t* kpos;
+  const int64_t* slots;
+  const char* k;
+  const char* v;
+  int64_t k_st, k_sh, v_st, v_sh;
   PagedView pv;
-  int G, nsplit, nk_pad;
-  // workspace sections (floats), per query row
+  const float* E;
+  int64_t e_sd, e_sp;
+  char* out;
+  int64_t o_st, o_sh;
+  int32_t* status;
   float* logits;  // [nq][hq][nk_pad]
   float* gsum;    // [nq][hq][nsplit]
   float* table;   // [nq][hq][npos]
   float* po;      // [nq][hq][nsplit][dv]
   float* pm;      // [nq][hq][nsplit]
   float* pl;      // [nq][hq][nsplit]
+  int nq, nk, nsplit, nk_pad, row0;
 };
 
-__device__ __forceinline__ int64_t causal_limit(const cs_attn_params& p, int64_t qp) {
-  if (p.kpos == nullptr) return qp + 1 < p.nk ? qp + 1 : p.nk;
-  int64_t lo = 0, hi = p.nk;
+struct DecodeBatch {
+  int count, hq, hkv, d, dv, npos, G, out_dtype;
+  float inv_scale;
+  DecodeReq r[kMaxBatch];
+};
+
+__device__ __forceinline__ const DecodeReq& request_of(const DecodeBatch& b, int z, int64_t& i) {
+  int k = 0;
+  while (k + 1 < b.count && z >= b.r[k + 1].row0) ++k;
+  i = z - b.r[k].row0;
+  return b.r[k];
+}
+
+__device__ __forceinline__ int64_t causal_limit(const DecodeReq& r, int64_t qp) {
+  if (r.kpos == nullptr) return qp + 1 < r.nk ? qp + 1 : r.nk;
+  int64_t lo = 0, hi = r.nk;
   while (lo < hi) {
     int64_t mid = (lo + hi) >> 1;
-    if (p.kpos[mid] <= qp) lo = mid + 1; else hi = mid;
+    if (r.kpos[mid] <= qp) lo = mid + 1; else hi = mid;
   }
   return lo;
 }
 
 template <typename T>
-__device__ __forceinline__ const char* key_row(const DecodeArgs& a, int64_t j, int g, bool v,
-                                               bool& ok) {
-  const cs_attn_params& p = a.p;
-  if (p.kv_slots) {
-    int64_t s = p.kv_slots[j];
-    ok = a.pv.valid(s);
+__device__ __forceinline__ const char* kv_row(const DecodeReq& r, int64_t j, int g, bool v,
+                                              bool& ok, int d) {
+  if (r.slots) {
+    const int64_t s = r.slots[j];
+    ok = r.pv.valid(s);
     if (!ok) return nullptr;
-    return a.pv.addr(s, g, v ? a.pv.head_dim : 0);
+    return r.pv.addr(s, g, v ? r.pv.head_dim : 0);
   }
   ok = true;
-  const char* base = static_cast<const char*>(v ? p.v : p.k);
-  int64_t st = v ? p.v_stride_tok : p.k_stride_tok, sh = v ? p.v_stride_head : p.k_stride_head;
-  return base + (j * st + (int64_t)g * sh) * (int64_t)sizeof(T);
+  return (v ? r.v : r.k) +
+         (j * (v ? r.v_st : r.k_st) + (int64_t)g * (v ? r.v_sh : r.k_sh)) * (int64_t)sizeof(T);
 }
 
 // phase 1: logits of this split's keys for the G heads of KV head g, gate
 // totals, and (split 0) the q.E tables
 template <typename T>
-__global__ void __launch_bounds__(kSplit) decode_phase1(DecodeArgs a) {
-  const cs_attn_params& p = a.p;
+__global__ void __launch_bounds__(kSplit) decode_phase1(const __grid_constant__ DecodeBatch b) {
   const int s = blockIdx.x, g = blockIdx.y;
-  const int64_t i = blockIdx.z;
-  const int tid = threadIdx.x, G = a.G, d = p.d;
+  int64_t i;
+  const DecodeReq& r = request_of(b, blockIdx.z, i);
+  if (s >= r.nsplit) return;
+  const int tid = threadIdx.x, G = b.G, d = b.d;
   __shared__ float qs[kMaxG * kMaxD];
   __shared__ float red[kMaxG][kSplit / 32];
-  const int64_t qp = p.qpos[i];
-  const int64_t nlim = causal_limit(p, qp);
+  const int64_t qp = r.qpos[i];
+  const int64_t nlim = causal_limit(r, qp);
   for (int e = tid; e < G * d; e += kSplit) {
-    int hh = e / d, x = e - hh * d;
+    const int hh = e / d, x = e - hh * d;
     const T* qrow = reinterpret_cast<const T*>(
-        static_cast<const char*>(p.q) +
-        (i * p.q_stride_tok + (int64_t)(g * G + hh) * p.q_stride_head) * (int64_t)sizeof(T));
+        r.q + (i * r.q_st + (int64_t)(g * G + hh) * r.q_sh) * (int64_t)sizeof(T));
     qs[e] = Elem<T>::to_f(qrow[x]);
   }
   __syncthreads();
@@ -91,7 +118,7 @@ __global__ void __launch_bounds__(kSplit) decode_phase1(DecodeArgs a) {
   for (int hh = 0; hh < kMaxG; ++hh) gate[hh] = 0.f;
   if (j < nlim) {
     bool ok;
-    const char* kr = key_row<T>(a, j, g, false, ok);
+    const char* kr = kv_row<T>(r, j, g, false, ok, d);
     if (!ok) {
       bits |= CS_ST_SLOT_RANGE;
     } else {
@@ -99,14 +126,14 @@ __global__ void __launch_bounds__(kSplit) decode_phase1(DecodeArgs a) {
 #pragma unroll
       for (int hh = 0; hh < kMaxG; ++hh) acc[hh] = 0.f;
       constexpr int V = 16 / sizeof(T);
-      const int64_t se = p.kv_slots ? a.pv.se : (int64_t)sizeof(T);
+      const int64_t se = r.slots ? r.pv.se : (int64_t)sizeof(T);
       if (se == (int64_t)sizeof(T) && (reinterpret_cast<uintptr_t>(kr) & 15) == 0 && d % V == 0) {
         for (int e0 = 0; e0 < d; e0 += V) {
           uint4 raw = *reinterpret_cast<const uint4*>(kr + e0 * sizeof(T));
           const T* x = reinterpret_cast<const T*>(&raw);
 #pragma unroll
           for (int u = 0; u < V; ++u) {
-            float kv = Elem<T>::to_f(x[u]);
+            const float kv = Elem<T>::to_f(x[u]);
 #pragma unroll
             for (int hh = 0; hh < kMaxG; ++hh)
               if (hh < G) acc[hh] = fmaf(qs[hh * d + e0 + u], kv, acc[hh]);
@@ -114,7 +141,7 @@ __global__ void __launch_bounds__(kSplit) decode_phase1(DecodeArgs a) {
         }
       } else {
         for (int e = 0; e < d; ++e) {
-          float kv = Elem<T>::to_f(*reinterpret_cast<const T*>(kr + e * se));
+          const float kv = Elem<T>::to_f(*reinterpret_cast<const T*>(kr + e * se));
 #pragma unroll
           for (int hh = 0; hh < kMaxG; ++hh)
             if (hh < G) acc[hh] = fmaf(qs[hh * d + e], kv, acc[hh]);
@@ -123,80 +150,79 @@ __global__ void __launch_bounds__(kSplit) decode_phase1(DecodeArgs a) {
 #pragma unroll
       for (int hh = 0; hh < kMaxG; ++hh) {
         if (hh >= G) break;
-        float l = acc[hh] / (float)p.scale;
+        const float l = acc[hh] * b.inv_scale;
         if (!isfinite(l)) bits |= CS_ST_LOGIT_NONFINITE;
-        a.logits[(i * p.hq + g * G + hh) * a.nk_pad + j] = l;
+        r.logits[(i * b.hq + g * G + hh) * r.nk_pad + j] = l;
         gate[hh] = 1.f / (1.f + expf(-l));
       }
     }
   }
-  // gate totals of this split, per head
   const int lane = tid & 31, warp = tid >> 5;
 #pragma unroll
   for (int hh = 0; hh < kMaxG; ++hh) {
     if (hh >= G) break;
-    float v = warp_sum(gate[hh]);
+    const float v = warp_sum(gate[hh]);
     if (lane == 0) red[hh][warp] = v;
   }
   __syncthreads();
   if (tid < G) {
     float tot = 0.f;
     for (int w = kSplit / 32 - 1; w >= 0; --w) tot += red[tid][w];
-    a.gsum[(i * p.hq + g * G + tid) * a.nsplit + s] = tot;
+    r.gsum[(i * b.hq + g * G + tid) * r.nsplit + s] = tot;
   }
   if (s == 0) {
-    const float* E = static_cast<const float*>(p.E);
-    for (int e = tid; e < G * p.npos; e += kSplit) {
-      int hh = e / p.npos, pp = e - hh * p.npos;
+    for (int e = tid; e < G * b.npos; e += kSplit) {
+      const int hh = e / b.npos, pp = e - hh * b.npos;
       float t = 0.f;
-      for (int x = 0; x < d; ++x) t = fmaf(qs[hh * d + x], E[x * p.e_stride_d + pp * p.e_stride_p], t);
-      a.table[(i * p.hq + g * G + hh) * p.npos + pp] = t;
+      for (int x = 0; x < d; ++x) t = fmaf(qs[hh * d + x], r.E[x * r.e_sd + pp * r.e_sp], t);
+      r.table[(i * b.hq + g * G + hh) * b.npos + pp] = t;
     }
   }
   bits = (int32_t)__reduce_or_sync(0xffffffffu, (unsigned)bits);
-  if (lane == 0 && bits) report(p.status, bits);
+  if (lane == 0 && bits) report(r.status, bits);
 }
 
 // phase 2: carried count, reverse scan, bias, partial softmax and PV
 template <typename T>
-__global__ void __launch_bounds__(kSplit) decode_phase2(DecodeArgs a) {
-  const cs_attn_params& p = a.p;
+__global__ void __launch_bounds__(kSplit) decode_phase2(const __grid_constant__ DecodeBatch b) {
   const int s = blockIdx.x, g = blockIdx.y;
-  const int64_t i = blockIdx.z;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, G = a.G;
-  const int npos = p.npos, dv = p.dv;
+  int64_t i;
+  const DecodeReq& r = request_of(b, blockIdx.z, i);
+  if (s >= r.nsplit) return;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, G = b.G;
+  const int npos = b.npos, dv = b.dv;
   extern __shared__ __align__(16) float dyn[];
-  float* tab = dyn;                      // [G][npos]
-  float* wts = tab + G * npos;           // [G][kSplit]
+  float* tab = dyn;             // [G][npos]
+  float* wts = tab + G * npos;  // [G][kSplit]
   __shared__ float wtot[kMaxG][kSplit / 32];
   __shared__ float carry0[kMaxG];
   __shared__ float red[kMaxG][kSplit / 32];
   __shared__ float mmax[kMaxG];
   __shared__ const char* vrows[kSplit];
-  const int64_t qp = p.qpos[i];
-  const int64_t nlim = causal_limit(p, qp);
+  const int64_t qp = r.qpos[i];
+  const int64_t nlim = causal_limit(r, qp);
   const int64_t base = (int64_t)s * kSplit;
-  const int64_t rowh0 = i * p.hq + (int64_t)g * G;
+  const int64_t rowh0 = i * b.hq + (int64_t)g * G;
   if (base >= nlim) {  // split entirely in the future: empty partial
     if (tid < G) {
-      a.pm[(rowh0 + tid) * a.nsplit + s] = -INFINITY;
-      a.pl[(rowh0 + tid) * a.nsplit + s] = 0.f;
+      r.pm[(rowh0 + tid) * r.nsplit + s] = -INFINITY;
+      r.pl[(rowh0 + tid) * r.nsplit + s] = 0.f;
     }
     return;
   }
   const int last = (int)((nlim - 1) / kSplit);
   if (tid < G) {
     float c = 0.f;
-    for (int t = last; t > s; --t) c += a.gsum[(rowh0 + tid) * a.nsplit + t];
+    for (int t = last; t > s; --t) c += r.gsum[(rowh0 + tid) * r.nsplit + t];
     carry0[tid] = c;
   }
-  for (int e = tid; e < G * npos; e += kSplit) tab[e] = a.table[rowh0 * npos + e];
+  for (int e = tid; e < G * npos; e += kSplit) tab[e] = r.table[rowh0 * npos + e];
   const int64_t j = base + tid;
   const bool live = j < nlim;
   int32_t bits = 0;
   {
     bool ok = false;
-    const char* vr = live ? key_row<T>(a, j, g, true, ok) : nullptr;
+    const char* vr = live ? kv_row<T>(r, j, g, true, ok, b.d) : nullptr;
     if (live && !ok) bits |= CS_ST_SLOT_RANGE;
     vrows[tid] = ok ? vr : nullptr;
   }
@@ -206,7 +232,7 @@ __global__ void __launch_bounds__(kSplit) decode_phase2(DecodeArgs a) {
     lg[hh] = 0.f;
     gt[hh] = 0.f;
     if (hh < G && live) {
-      lg[hh] = a.logits[(rowh0 + hh) * a.nk_pad + j];
+      lg[hh] = r.logits[(rowh0 + hh) * r.nk_pad + j];
       gt[hh] = 1.f / (1.f + expf(-lg[hh]));
     }
   }
@@ -217,7 +243,7 @@ __global__ void __launch_bounds__(kSplit) decode_phase2(DecodeArgs a) {
     float v = gt[hh];
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      float t = __shfl_down_sync(0xffffffffu, v, o);
+      const float t = __shfl_down_sync(0xffffffffu, v, o);
       if (lane + o < 32) v += t;
     }
     suf[hh] = v;
@@ -232,19 +258,18 @@ __global__ void __launch_bounds__(kSplit) decode_phase2(DecodeArgs a) {
     if (hh >= G) continue;
     float c = carry0[hh];
     for (int w = kSplit / 32 - 1; w > warp; --w) c += wtot[hh][w];
-    float R = suf[hh] + c;
-    float pos = R < 0.f ? 0.f : (R > top ? top : R);
-    int lo = (int)floorf(pos);
-    int hi = lo + 1 < npos ? lo + 1 : npos - 1;
-    float f = pos - (float)lo;
-    float tlo = tab[hh * npos + lo];
+    const float R = suf[hh] + c;
+    const float pos = R < 0.f ? 0.f : (R > top ? top : R);
+    const int lo = (int)floorf(pos);
+    const int hi = lo + 1 < npos ? lo + 1 : npos - 1;
+    const float f = pos - (float)lo;
+    const float tlo = tab[hh * npos + lo];
     if (live) score[hh] = lg[hh] + (tlo + f * (tab[hh * npos + hi] - tlo));
   }
-  // split max and weights
 #pragma unroll
   for (int hh = 0; hh < kMaxG; ++hh) {
     if (hh >= G) break;
-    float v = warp_max(score[hh]);
+    const float v = warp_max(score[hh]);
     if (lane == 0) red[hh][warp] = v;
   }
   __syncthreads();
@@ -257,9 +282,9 @@ __global__ void __launch_bounds__(kSplit) decode_phase2(DecodeArgs a) {
 #pragma unroll
   for (int hh = 0; hh < kMaxG; ++hh) {
     if (hh >= G) break;
-    float w = live ? expf(score[hh] - mmax[hh]) : 0.f;
+    const float w = live ? expf(score[hh] - mmax[hh]) : 0.f;
     wts[hh * kSplit + tid] = w;
-    float v = warp_sum(w);
+    const float v = warp_sum(w);
     __syncwarp();
     if (lane == 0) wtot[hh][warp] = v;
   }
@@ -267,12 +292,12 @@ __global__ void __launch_bounds__(kSplit) decode_phase2(DecodeArgs a) {
   if (tid < G) {
     float l = 0.f;
     for (int w = 0; w < kSplit / 32; ++w) l += wtot[tid][w];
-    a.pm[(rowh0 + tid) * a.nsplit + s] = mmax[tid];
-    a.pl[(rowh0 + tid) * a.nsplit + s] = l;
+    r.pm[(rowh0 + tid) * r.nsplit + s] = mmax[tid];
+    r.pl[(rowh0 + tid) * r.nsplit + s] = l;
   }
   // PV: thread <-> output dimension, keys broadcast from shared memory
   const int nkeys = (int)((nlim - base) < kSplit ? (nlim - base) : kSplit);
-  const int64_t se = p.kv_slots ? a.pv.se : (int64_t)sizeof(T);
+  const int64_t se = r.slots ? r.pv.se : (int64_t)sizeof(T);
   for (int x = tid; x < dv; x += kSplit) {
     float acc[kMaxG];
 #pragma unroll
@@ -280,52 +305,51 @@ __global__ void __launch_bounds__(kSplit) decode_phase2(DecodeArgs a) {
     for (int kk = 0; kk < nkeys; ++kk) {
       const char* vr = vrows[kk];
       if (vr == nullptr) continue;
-      float vv = Elem<T>::to_f(*reinterpret_cast<const T*>(vr + x * se));
+      const float vv = Elem<T>::to_f(*reinterpret_cast<const T*>(vr + x * se));
 #pragma unroll
       for (int hh = 0; hh < kMaxG; ++hh)
         if (hh < G) acc[hh] = fmaf(wts[hh * kSplit + kk], vv, acc[hh]);
     }
 #pragma unroll
     for (int hh = 0; hh < kMaxG; ++hh)
-      if (hh < G) a.po[((rowh0 + hh) * a.nsplit + s) * dv + x] = acc[hh];
+      if (hh < G) r.po[((rowh0 + hh) * r.nsplit + s) * dv + x] = acc[hh];
   }
-  if (bits) report(p.status, bits);
+  if (bits) report(r.status, bits);
 }
 
 // combine split partials: one CTA per (query row, head)
-__global__ void decode_combine(DecodeArgs a) {
-  const cs_attn_params& p = a.p;
-  const int64_t i = blockIdx.x;
+__global__ void decode_combine(const __grid_constant__ DecodeBatch b) {
+  int64_t i;
+  const DecodeReq& r = request_of(b, blockIdx.x, i);
   const int h = blockIdx.y;
-  const int64_t rowh = i * p.hq + h;
-  const int64_t nlim = causal_limit(p, p.qpos[i]);
+  const int64_t rowh = i * b.hq + h;
+  const int64_t nlim = causal_limit(r, r.qpos[i]);
   const int nsp = nlim > 0 ? (int)((nlim - 1) / kSplit) + 1 : 0;
   float M = -INFINITY;
-  for (int s = 0; s < nsp; ++s) M = fmaxf(M, a.pm[rowh * a.nsplit + s]);
+  for (int s = 0; s < nsp; ++s) M = fmaxf(M, r.pm[rowh * r.nsplit + s]);
   float L = 0.f;
   for (int s = 0; s < nsp; ++s) {
-    float m = a.pm[rowh * a.nsplit + s];
-    if (m > -INFINITY) L += expf(m - M) * a.pl[rowh * a.nsplit + s];
+    const float m = r.pm[rowh * r.nsplit + s];
+    if (m > -INFINITY) L += expf(m - M) * r.pl[rowh * r.nsplit + s];
   }
   const float inv = L > 0.f ? 1.f / L : 0.f;
-  char* orow = static_cast<char*>(p.out) +
-               (i * p.o_stride_tok + (int64_t)h * p.o_stride_head) * dtype_size(p.out_dtype);
+  char* orow = r.out + (i * r.o_st + (int64_t)h * r.o_sh) * dtype_size(b.out_dtype);
   int32_t bits = 0;
-  for (int x = threadIdx.x; x < p.dv; x += blockDim.x) {
+  for (int x = threadIdx.x; x < b.dv; x += blockDim.x) {
     float acc = 0.f;
     for (int s = 0; s < nsp; ++s) {
-      float m = a.pm[rowh * a.nsplit + s];
-      if (m > -INFINITY) acc += expf(m - M) * a.po[(rowh * a.nsplit + s) * p.dv + x];
+      const float m = r.pm[rowh * r.nsplit + s];
+      if (m > -INFINITY) acc += expf(m - M) * r.po[(rowh * r.nsplit + s) * b.dv + x];
     }
-    float val = acc * inv;
+    const float val = acc * inv;
     if (!isfinite(val)) bits |= CS_ST_LOGIT_NONFINITE;
-    switch (p.out_dtype) {
+    switch (b.out_dtype) {
       case CS_F32: reinterpret_cast<float*>(orow)[x] = val; break;
       case CS_F16: reinterpret_cast<__half*>(orow)[x] = __float2half_rn(val); break;
       default: reinterpret_cast<__nv_bfloat16*>(orow)[x] = __float2bfloat16_rn(val); break;
     }
   }
-  if (bits) report(p.status, bits);
+  if (bits) report(r.status, bits);
 }
 
 bool decode_supported(const cs_attn_params* p) {
@@ -342,19 +366,18 @@ bool decode_supported(const cs_attn_params* p) {
 }
 
 struct Layout {
-  int G, nsplit, nk_pad;
+  int nsplit, nk_pad;
   int64_t logits, gsum, table, po, pm, pl, total;  // float offsets / count
 };
 
 Layout layout_of(const cs_attn_params* p) {
   Layout L;
-  L.G = p->hq / p->hkv;
   L.nsplit = (p->nk + kSplit - 1) / kSplit;
   L.nk_pad = L.nsplit * kSplit;
   const int64_t rows = (int64_t)p->nq * p->hq;
   int64_t off = 0;
   auto take = [&](int64_t n) {
-    int64_t o = off;
+    const int64_t o = off;
     off += (n + 63) / 64 * 64;  // 256-byte aligned sections
     return o;
   };
@@ -368,6 +391,96 @@ Layout layout_of(const cs_attn_params* p) {
   return L;
 }
 
+bool same_shape(const cs_attn_params* a, const cs_attn_params* b) {
+  return a->hq == b->hq && a->hkv == b->hkv && a->d == b->d && a->dv == b->dv &&
+         a->npos == b->npos && a->in_dtype == b->in_dtype && a->out_dtype == b->out_dtype &&
+         a->scale == b->scale;
+}
+
+void fill_request(DecodeReq& q, const cs_attn_params* p, float* ws, const Layout& L, int row0) {
+  q.q = static_cast<const char*>(p->q);
+  q.q_st = p->q_stride_tok;
+  q.q_sh = p->q_stride_head;
+  q.qpos = p->qpos;
+  q.kpos = p->kpos;
+  q.slots = p->kv_slots;
+  q.k = static_cast<const char*>(p->k);
+  q.v = static_cast<const char*>(p->v);
+  q.k_st = p->k_stride_tok;
+  q.k_sh = p->k_stride_head;
+  q.v_st = p->v_stride_tok;
+  q.v_sh = p->v_stride_head;
+  q.pv = p->kv_slots ? PagedView::make(p->paged) : PagedView{};
+  q.E = static_cast<const float*>(p->E);
+  q.e_sd = p->e_stride_d;
+  q.e_sp = p->e_stride_p;
+  q.out = static_cast<char*>(p->out);
+  q.o_st = p->o_stride_tok;
+  q.o_sh = p->o_stride_head;
+  q.status = p->status;
+  q.logits = ws + L.logits;
+  q.gsum = ws + L.gsum;
+  q.table = ws + L.table;
+  q.po = ws + L.po;
+  q.pm = ws + L.pm;
+  q.pl = ws + L.pl;
+  q.nq = p->nq;
+  q.nk = p->nk;
+  q.nsplit = L.nsplit;
+  q.nk_pad = L.nk_pad;
+  q.row0 = row0;
+}
+
+int launch_batch(const cs_attn_params* ps, int count, char* workspace, cudaStream_t stream) {
+  DecodeBatch b{};
+  const cs_attn_params* p0 = &ps[0];
+  b.count = 0;
+  b.hq = p0->hq;
+  b.hkv = p0->hkv;
+  b.d = p0->d;
+  b.dv = p0->dv;
+  b.npos = p0->npos;
+  b.G = p0->hq / p0->hkv;
+  b.out_dtype = p0->out_dtype;
+  b.inv_scale = (float)(1.0 / p0->scale);
+  int rows = 0, nsplit_max = 0;
+  int64_t off = 0;
+  for (int k = 0; k < count; ++k) {
+    const cs_attn_params* p = &ps[k];
+    if (p->nq == 0) continue;
+    const Layout L = layout_of(p);
+    fill_request(b.r[b.count], p, reinterpret_cast<float*>(workspace + off), L, rows);
+    off += L.total * (int64_t)sizeof(float);
+    rows += p->nq;
+    nsplit_max = L.nsplit > nsplit_max ? L.nsplit : nsplit_max;
+    ++b.count;
+  }
+  if (b.count == 0) return CS_OK;
+  const dim3 grid(nsplit_max, b.hkv, rows);
+  const size_t smem2 = (size_t)(b.G * b.npos + b.G * kSplit) * sizeof(float);
+  if (smem2 > 48 * 1024) return CS_ERR_UNSUPPORTED;
+  if (p0->in_dtype == CS_BF16) {
+    decode_phase1<__nv_bfloat16><<<grid, kSplit, 0, stream>>>(b);
+    decode_phase2<__nv_bfloat16><<<grid, kSplit, smem2, stream>>>(b);
+  } else {
+    decode_phase1<__half><<<grid, kSplit, 0, stream>>>(b);
+    decode_phase2<__half><<<grid, kSplit, smem2, stream>>>(b);
+  }
+  decode_combine<<<dim3(rows, b.hq), 128, 0, stream>>>(b);
+  CS_LAUNCH_CHECK();
+  return CS_OK;
+}
+
+int check_batch(const cs_attn_params* ps, int count) {
+  if (!ps || count < 1) return CS_ERR_INVALID;
+  for (int k = 0; k < count; ++k) {
+    const int rc = validate_attn_params(&ps[k]);
+    if (rc != CS_OK) return rc;
+    if (!decode_supported(&ps[k]) || !same_shape(&ps[0], &ps[k])) return CS_ERR_UNSUPPORTED;
+  }
+  return CS_OK;
+}
+
 }  // namespace
 
 // shared with the no-allocation variant
@@ -377,38 +490,11 @@ int64_t decode_workspace_bytes(const cs_attn_params* p) {
 }
 
 int launch_decode(const cs_attn_params* p, void* workspace, cudaStream_t stream) {
-  int rc = validate_attn_params(p);
+  const int rc = check_batch(p, 1);
   if (rc != CS_OK) return rc;
-  if (!decode_supported(p)) return CS_ERR_UNSUPPORTED;
   if (p->nq == 0) return CS_OK;
   if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255)) return CS_ERR_INVALID;
-  Layout L = layout_of(p);
-  DecodeArgs a;
-  a.p = *p;
-  a.pv = p->kv_slots ? PagedView::make(p->paged) : PagedView{};
-  a.G = L.G;
-  a.nsplit = L.nsplit;
-  a.nk_pad = L.nk_pad;
-  float* ws = static_cast<float*>(workspace);
-  a.logits = ws + L.logits;
-  a.gsum = ws + L.gsum;
-  a.table = ws + L.table;
-  a.po = ws + L.po;
-  a.pm = ws + L.pm;
-  a.pl = ws + L.pl;
-  dim3 grid(L.nsplit, p->hkv, p->nq);
-  size_t smem2 = (size_t)(L.G * p->npos + L.G * kSplit) * sizeof(float);
-  if (smem2 > 48 * 1024) return CS_ERR_UNSUPPORTED;
-  if (p->in_dtype == CS_BF16) {
-    decode_phase1<__nv_bfloat16><<<grid, kSplit, 0, stream>>>(a);
-    decode_phase2<__nv_bfloat16><<<grid, kSplit, smem2, stream>>>(a);
-  } else {
-    decode_phase1<__half><<<grid, kSplit, 0, stream>>>(a);
-    decode_phase2<__half><<<grid, kSplit, smem2, stream>>>(a);
-  }
-  decode_combine<<<dim3(p->nq, p->hq), 128, 0, stream>>>(a);
-  CS_LAUNCH_CHECK();
-  return CS_OK;
+  return launch_batch(p, 1, static_cast<char*>(workspace), stream);
 }
 
 }  // namespace cs
@@ -421,4 +507,27 @@ extern "C" int64_t cs_cope_attn_decode_workspace(const cs_attn_params* p) {
 
 extern "C" int cs_cope_attn_decode(const cs_attn_params* p, void* workspace, void* stream) {
   return launch_decode(p, workspace, as_stream(stream));
+}
+
+extern "C" int64_t cs_cope_attn_decode_batch_workspace(const cs_attn_params* params,
+                                                       int32_t count) {
+  if (check_batch(params, count) != CS_OK) return 0;
+  int64_t total = 0;
+  for (int k = 0; k < count; ++k) total += layout_of(&params[k]).total * (int64_t)sizeof(float);
+  return total;
+}
+
+extern "C" int cs_cope_attn_decode_batch(const cs_attn_params* params, int32_t count,
+                                         void* workspace, void* stream) {
+  const int rc = check_batch(params, count);
+  if (rc != CS_OK) return rc;
+  if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255)) return CS_ERR_INVALID;
+  char* ws = static_cast<char*>(workspace);
+  for (int first = 0; first < count; first += kMaxBatch) {
+    const int n = count - first < kMaxBatch ? count - first : kMaxBatch;
+    const int r = launch_batch(params + first, n, ws, as_stream(stream));
+    if (r != CS_OK) return r;
+    for (int k = first; k < first + n; ++k) ws += layout_of(&params[k]).total * sizeof(float);
+  }
+  return CS_OK;
 }

@@ -180,10 +180,15 @@ class ReuseStep:
             r.dec_out = torch.empty(1, hq, d, dtype=cfg.dtype, device=dev)
             r.dec_pos = torch.tensor([n], dtype=torch.int64, device=dev)
             r.dec_params = self._decode_params(r)
-            r.dec_ws = None
-            ws = self.lib.cs_cope_attn_decode_workspace(ctypes.byref(r.dec_params))
-            if ws > 0:
-                r.dec_ws = torch.empty(ws, dtype=torch.uint8, device=dev)
+        # decode of the whole batch: one scatter of the new tokens, one
+        # batched split-key decode (three launches for all requests)
+        reqs = work.requests
+        self.dec_params = (N.AttnParams * len(reqs))(*[r.dec_params for r in reqs])
+        size = self.lib.cs_cope_attn_decode_batch_workspace(self.dec_params, len(reqs))
+        self.dec_ws = torch.empty(max(size, 1), dtype=torch.uint8, device=dev) if size else None
+        self.dec_k = torch.cat([r.decode_k for r in reqs]).contiguous()
+        self.dec_v = torch.cat([r.decode_v for r in reqs]).contiguous()
+        self.dec_slots = torch.stack([r.slots_all[n] for r in reqs]).contiguous()
         self.gate_layer = True  # exercise the cosine gate in every timed step
 
     # -------------------------------------------------------------- pieces
@@ -309,22 +314,25 @@ class ReuseStep:
         self._select(r, s)
 
     def decode(self, stream: int | None = None) -> list[torch.Tensor]:
-        """One decode token per request: write its K/V, attend over n+1 keys."""
+        """One decode token per request: write the new K/V rows of all
+        requests (one scatter into the shared pool), then attend over n+1 keys
+        for every request in one batched split-key decode."""
         s = N.stream_of(self.work.device) if stream is None else stream
-        for r in self.work.requests:
-            slot = r.dec_slots[self.work.cfg.seq:]
-            N.check(self.lib.cs_slide_scatter(
-                ctypes.byref(self.kv), slot.data_ptr(), None, 1, r.decode_k.data_ptr(),
-                r.decode_v.data_ptr(), r.decode_k.stride(0), r.decode_k.stride(1),
-                r.status_ptr, s), "cs_slide_scatter")
-            rc = N.CS_ERR_UNSUPPORTED
-            if r.dec_ws is not None:
-                rc = self.lib.cs_cope_attn_decode(ctypes.byref(r.dec_params),
-                                                  r.dec_ws.data_ptr(), s)
-            if rc == N.CS_ERR_UNSUPPORTED:
-                rc = self.lib.cs_cope_attn(ctypes.byref(r.dec_params), s)
-            N.check(rc, "decode attention")
-        return [r.dec_out for r in self.work.requests]
+        reqs = self.work.requests
+        N.check(self.lib.cs_slide_scatter(
+            ctypes.byref(self.kv), self.dec_slots.data_ptr(), None, len(reqs),
+            self.dec_k.data_ptr(), self.dec_v.data_ptr(), self.dec_k.stride(0),
+            self.dec_k.stride(1), reqs[0].status_ptr, s), "cs_slide_scatter")
+        rc = N.CS_ERR_UNSUPPORTED
+        if self.dec_ws is not None:
+            rc = self.lib.cs_cope_attn_decode_batch(self.dec_params, len(reqs),
+                                                    self.dec_ws.data_ptr(), s)
+        if rc == N.CS_ERR_UNSUPPORTED:
+            for r in reqs:
+                N.check(self.lib.cs_cope_attn(ctypes.byref(r.dec_params), s), "decode")
+        else:
+            N.check(rc, "cs_cope_attn_decode_batch")
+        return [r.dec_out for r in reqs]
 
     def check_status(self) -> None:
         """Raise if any launch of any request reported a status bit."""

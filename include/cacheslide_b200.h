@@ -298,6 +298,19 @@ CS_API int cs_cope_attn_decode(const cs_attn_params* p, void* workspace,
                         void* stream);
 
 /*
+ * Decode of `count` requests in one set of launches (the per-step decode of
+ * a whole batch; the reference runs runtime.py:490-508 once per request).
+ * All requests must share head counts, head dims, npos, dtypes and scale;
+ * each has its own queries, positions, slot table, cache view, E table and
+ * output.  `workspace` holds cs_cope_attn_decode_batch_workspace(params,
+ * count) bytes (256-byte aligned); requests are packed in order.
+ */
+CS_API int64_t cs_cope_attn_decode_batch_workspace(const cs_attn_params* params,
+                                                   int32_t count);
+CS_API int cs_cope_attn_decode_batch(const cs_attn_params* params, int32_t count,
+                                     void* workspace, void* stream);
+
+/*
  * Decode that allocates nothing (no counterpart in the reference; it exists
  * for callers that must not allocate device memory, e.g. a plugin inside an
  * inference engine that already gave all free HBM to its KV-cache pool, or a

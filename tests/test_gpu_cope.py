@@ -343,6 +343,64 @@ def test_split_key_decode_matches_oracle_and_generic(cuda, nk, rows):
     np.testing.assert_allclose(outs[0], outs[1], **BF16)
 
 
+def test_batched_decode_matches_per_request_decode(cuda):
+    """cs_cope_attn_decode_batch over requests of different context lengths
+    (and more requests than one launch holds) equals decoding them one by one."""
+    import ctypes
+
+    from cacheslide_b200 import _native as N
+    from cacheslide_b200.position import _Holder, _base_params
+
+    hq, hkv, d, bs = 32, 8, 128, 16
+    lengths = [4097, 130, 1500, 2049, 777, 3000, 64, 900, 4096, 2500]
+    g = torch.Generator().manual_seed(5)
+    nb = sum((n + bs - 1) // bs for n in lengths) + 4
+    cache = torch.zeros(nb, hkv, bs, 2 * d, dtype=torch.bfloat16, device=cuda)
+    perm = torch.randperm(nb, generator=g).to(cuda)
+    cope = _cope((torch.randn(d, 64, generator=g) * 0.02).numpy(), cuda)
+    holder = _Holder(cope, cope.position_embeddings.detach())
+    keep, params, singles = [], [], []
+    used = 0
+    for n in lengths:
+        blocks = perm[used:used + (n + bs - 1) // bs]
+        used += (n + bs - 1) // bs
+        tok = torch.arange(n, device=cuda)
+        slots = blocks[tok // bs] * bs + tok % bs
+        k = (torch.randn(n, hkv, d, generator=g) / d ** 0.5).to(torch.bfloat16).to(cuda)
+        v = torch.randn(n, hkv, d, generator=g).to(torch.bfloat16).to(cuda)
+        cache[slots // bs, :, slots % bs, :d] = k
+        cache[slots // bs, :, slots % bs, d:] = v
+        q = (torch.randn(1, hq, d, generator=g) / d ** 0.5).to(torch.bfloat16).to(cuda)
+        qpos = torch.tensor([n - 1], device=cuda)
+        outs = [torch.empty(1, hq, d, dtype=torch.bfloat16, device=cuda) for _ in range(2)]
+        ps = []
+        for out in outs:
+            p = _base_params(q, None, None, holder, qpos, None, n, hkv, d)
+            p.paged = N.paged_view(cache)
+            p.kv_slots = slots.data_ptr()
+            p.out = out.data_ptr()
+            p.o_stride_tok, p.o_stride_head = out.stride(0), out.stride(1)
+            ps.append(p)
+        keep += [slots, q, qpos, *outs]
+        params.append(ps[0])
+        singles.append((ps[1], outs))
+    lib = N.load()
+    arr = (N.AttnParams * len(params))(*params)
+    size = lib.cs_cope_attn_decode_batch_workspace(arr, len(params))
+    assert size > 0
+    ws = torch.empty(size, dtype=torch.uint8, device=cuda)
+    N.check(lib.cs_cope_attn_decode_batch(arr, len(params), ws.data_ptr(), N.stream_of(cuda)),
+            "batch")
+    for p, outs in singles:
+        wsz = lib.cs_cope_attn_decode_workspace(ctypes.byref(p))
+        w1 = torch.empty(wsz, dtype=torch.uint8, device=cuda)
+        N.check(lib.cs_cope_attn_decode(ctypes.byref(p), w1.data_ptr(), N.stream_of(cuda)),
+                "single")
+    torch.cuda.synchronize()
+    for _, outs in singles:
+        assert torch.equal(outs[0], outs[1])
+
+
 # ----------------------------------------- reference known answers (float64)
 def test_known_visibility_after_gates(cuda):
     cope = CoPE(1, 8, device=cuda, dtype=torch.float64)
