@@ -36,7 +36,7 @@ int validate_attn_params(const cs_attn_params* p);
 
 namespace {
 
-constexpr int kThreads = 288;
+constexpr int kThreads = 416;  // 8 softmax + 4 producer + 1 MMA warps
 constexpr int kTileN = 128;  // keys per tile
 constexpr int kD = 128;      // head dim of this kernel
 constexpr int kMaxNpos = 64;
@@ -64,11 +64,18 @@ constexpr uint32_t kNtile = 104;    // key tiles of this CTA
 constexpr uint32_t kFixMask = 112;  // [4 slots][4 words] key is fixed
 constexpr uint32_t kBndMask = 176;  // [4 slots][4 words] key is the last of its chunk
 constexpr uint32_t kBarMeta = 240;  // [4] producer -> softmax: key metadata of slot it % 4
-constexpr uint32_t kRowAddr = 272;  // [2 stages][128] K row address (bit 0: sidecar)
-constexpr uint32_t kMetaBytes = kRowAddr + 2 * 128 * 8;
-constexpr uint32_t kSmemBytes = kMeta + kMetaBytes;  // 231,696 B
+constexpr uint32_t kRowAddr = 272;  // [128] K row address of the current tile (bit 0: sidecar)
+constexpr uint32_t kXc = 1296;      // [128] float: newer half -> older half count, and back
+constexpr uint32_t kXm = 1808;      // [128] float: newer half's tile max / row sums
+constexpr uint32_t kXm2 = 2320;     // [128] float: older half's tile max
+constexpr uint32_t kBndKc = 2832;   // [4 slots][4 chunks] int: chunk id of the newest boundary
+constexpr uint32_t kMetaBytes = kBndKc + 16 * 4;
+constexpr uint32_t kSmemBytes = kMeta + kMetaBytes;  // 232,272 B (limit 232,448)
 
-constexpr uint32_t kColS0 = 0, kColO = 256, kColT = 384;
+// TMEM columns: S double buffer, O, the q.E table (read once into shared
+// memory) and, from then on, the per-row counts of a contextual tile (kColR
+// overlays kColT)
+constexpr uint32_t kColS0 = 0, kColO = 256, kColT = 384, kColR = 384;
 constexpr long long kWaitCycles = 1000000000ll;  // ~0.5 s at 1.9 GHz
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -141,6 +148,23 @@ __device__ __forceinline__ void fence_async_smem() {
         "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])            \
       : "r"(taddr))
 
+#define CS_TMEM_LD16(taddr, r)                                                                   \
+  asm volatile(                                                                                  \
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"    \
+      "%14,%15}, [%16];"                                                                         \
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),     \
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), \
+        "=r"(r[14]), "=r"(r[15])                                                                 \
+      : "r"(taddr))
+
+#define CS_TMEM_ST16(taddr, r)                                                                   \
+  asm volatile(                                                                                  \
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"     \
+      "%13,%14,%15,%16};" ::"r"(taddr),                                                          \
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),   \
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),          \
+      "r"(r[15]))
+
 #define CS_TMEM_ST32(taddr, r)                                                                   \
   asm volatile(                                                                                  \
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"     \
@@ -200,8 +224,28 @@ __device__ __forceinline__ float ex2(float x) {
 __device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
 }
-__device__ __forceinline__ void producer_sync() {  // the 128 producer threads
-  asm volatile("bar.sync 1, 128;" ::: "memory");
+// named barriers: id 1 = the 128 producer threads, 2..5 = softmax warp pairs,
+// 6..9 = count handoff within a pair
+__device__ __forceinline__ void named_sync(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void named_arrive(uint32_t id, uint32_t count) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+// barrier that also ANDs a flag over its participants: every participant
+// leaves with the same answer, so exits from loops stay collective and no
+// partner is left waiting at a later barrier
+__device__ __forceinline__ bool named_and(uint32_t id, uint32_t count, bool v) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.and.pred p, %2, %3, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(out)
+      : "r"((uint32_t)v), "r"(id), "r"(count)
+      : "memory");
+  return out != 0;
 }
 // floor of a nonnegative float below 2^22 with plain FP adds (round-down
 // add of 1.5 * 2^23 leaves the integer part in the low mantissa bits)
@@ -305,7 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
       mbar_init(mb + kBarPV + 8 * s, 1);
     }
     for (int s = 0; s < 4; ++s) mbar_init(mb + kBarMeta + 8 * s, 128);
-    mbar_init(mb + kBarP, 128);
+    mbar_init(mb + kBarP, 256);  // both halves of every row
     mbar_init(mb + kBarEnd, 1);
     *abort = 0;
     int64_t nmax = 0;  // keys needed by the furthest row of this tile
@@ -319,7 +363,7 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
     *reinterpret_cast<int*>(meta + kNtile) = (int)((nmax + kTileN - 1) / kTileN);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 8) {
+  if (warp == 12) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      mb + kTmemSlot),
                  "r"(512));
@@ -331,9 +375,9 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(meta + kTmemSlot);
   const int ntile = *reinterpret_cast<volatile int*>(meta + kNtile);
 
-  if (warp >= 4 && warp < 8) {
+  if (warp >= 8 && warp < 12) {
     // ================================================================ producer
-    const int pt = tid - 128;  // 0..127
+    const int pt = tid - 256;  // 0..127
     for (int idx = pt; idx < 128 * 16; idx += 128) {  // Q: row r = head-local * R + row-local
       const int r = idx >> 4, c16 = idx & 15;
       const int64_t i = i0 + (r % R);
@@ -347,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
     }
     const float* E = static_cast<const float*>(p.E);  // E^T split into hi + lo
     for (int idx = pt; idx < kMaxNpos * kD; idx += 128) {
-      const int pp = idx / kD, dd = idx - pp * kD;
+      const int dd = idx / kMaxNpos, pp = idx - dd * kMaxNpos;  // consecutive threads: consecutive p
       float e = pp < p.npos ? E[(int64_t)dd * p.e_stride_d + (int64_t)pp * p.e_stride_p] : 0.f;
       T hi = Elem<T>::from_f(e);
       T lo = Elem<T>::from_f(e - Elem<T>::to_f(hi));
@@ -364,40 +408,46 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
       const int st = it & 1, slot = it & 3;
       const int kt = ntile - 1 - it;
       const int64_t key0 = (int64_t)kt * kTileN;
-      // K stage free once QK(it-2) completed; metadata slot it%4 then too
-      if (it >= 2 && !mbar_wait(mb + kBarS + 8 * st, ((it - 2) >> 1) & 1, abort)) break;
+      // K stage free once QK(it-2) completed, metadata slot it%4 then too; the
+      // barrier also means every producer thread finished the previous tile
+      bool ok = it < 2 || mbar_wait(mb + kBarS + 8 * st, ((it - 2) >> 1) & 1, abort);
+      if (!named_and(1, 128, ok)) break;
       {
         const int64_t j = key0 + pt;
-        rowaddr[st * 128 + pt] = key_row_addr<T>(a, j, g);
+        rowaddr[pt] = key_row_addr<T>(a, j, g);
         const bool in = j < p.nk;
         const bool fixed = in && p.k_fixed != nullptr && p.k_fixed[j] != 0;
-        const bool bnd = in && p.pos_mode == CS_POS_CHUNK && (j + 1 < p.nk) &&
-                         p.key_chunk[j + 1] != p.key_chunk[j];
+        const int kcj = in && p.pos_mode == CS_POS_CHUNK ? p.key_chunk[j] : -1;
+        const bool bnd = kcj >= 0 && (j + 1 < p.nk) && p.key_chunk[j + 1] != kcj;
         const unsigned fm = __ballot_sync(0xffffffffu, fixed);
         const unsigned bm = __ballot_sync(0xffffffffu, bnd);
+        // chunk id of the newest boundary of these 32 keys (-1: none)
+        const int kc_top = __shfl_sync(0xffffffffu, kcj, bm ? 31 - __clz(bm) : 0);
         if (lane == 0) {
-          reinterpret_cast<unsigned*>(meta + kFixMask)[slot * 4 + (warp - 4)] = fm;
-          reinterpret_cast<unsigned*>(meta + kBndMask)[slot * 4 + (warp - 4)] = bm;
+          reinterpret_cast<unsigned*>(meta + kFixMask)[slot * 4 + (warp - 8)] = fm;
+          reinterpret_cast<unsigned*>(meta + kBndMask)[slot * 4 + (warp - 8)] = bm;
+          reinterpret_cast<int*>(meta + kBndKc)[slot * 4 + (warp - 8)] = bm ? kc_top : -1;
         }
       }
       mbar_arrive(mb + kBarMeta + 8 * slot);  // metadata published (release)
-      producer_sync();                   // every row address visible
+      named_sync(1, 128);                     // every row address visible
       const int c16 = pt & 15;
 #pragma unroll 4
       for (int m = 0; m < 16; ++m) {
         const int row = (pt >> 4) + 8 * m;
-        const uint64_t ka = rowaddr[st * 128 + row];
+        const uint64_t ka = rowaddr[row];
         const char* src = ka ? reinterpret_cast<const char*>(ka & ~1ull) + c16 * 16
                              : static_cast<const char*>(p.q);
         cp_async16(sbase + kK0 + st * 32768 + sw128(row, c16, 128), src, ka != 0);
       }
       cp_async_arrive_noinc(mb + kBarK + 8 * st);
       // V stage free once PV(it-2) completed
-      if (it >= 2 && !mbar_wait(mb + kBarPV + 8 * st, ((it - 2) >> 1) & 1, abort)) break;
+      ok = it < 2 || mbar_wait(mb + kBarPV + 8 * st, ((it - 2) >> 1) & 1, abort);
+      if (!named_and(1, 128, ok)) break;
 #pragma unroll 4
       for (int m = 0; m < 16; ++m) {
         const int row = (pt >> 4) + 8 * m;
-        const uint64_t ka = rowaddr[st * 128 + row];
+        const uint64_t ka = rowaddr[row];
         const char* src = ka ? value_row_addr<T>(a, ka, key0 + row, g) + c16 * 16
                              : static_cast<const char*>(p.q);
         cp_async16(sbase + kV0 + st * 32768 + sw128(row, c16, 128), src, ka != 0);
@@ -405,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
       cp_async_arrive_noinc(mb + kBarV + 8 * st);
     }
     cp_async_wait_all();
-  } else if (warp == 8) {
+  } else if (warp == 12) {
     // ================================================================== MMA
     if (lane == 0) {
       const uint32_t id_s = umma_idesc(128, 128, a.fmt, 0, 0);  // S = Q K^T
@@ -472,7 +522,15 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
     __syncwarp();
   } else {
     // ================================================================ softmax
-    const int r = tid;  // TMEM lane == tile row
+    // Two threads per S row: warp q (0-3) takes the newer half of every key
+    // tile (columns 64-127), warp q+4 the older half (0-63).  Both address
+    // TMEM lanes 32q..32q+31 (a warp reaches only its own lane quarter).  The
+    // pair exchanges the running count and the tile maximum through shared
+    // memory; every exit from the tile loop is agreed with a reducing
+    // barrier so neither warp of a pair is left waiting.
+    const int q4 = warp & 3, hf = warp >> 2;  // hf 0: newer half, 1: older half
+    const uint32_t pair = 2 + q4;
+    const int r = q4 * 32 + lane;  // TMEM lane == tile row
     const int64_t i = i0 + (r % R);
     const int h = g * G + r / R;
     const bool row_ok = i < p.nq;
@@ -484,123 +542,232 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
     const float* offrow =
         (row_ok && chunked) ? p.chunk_off + (int64_t)h * p.co_stride_h + i * p.co_stride_q
                             : nullptr;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
     float* Ts = reinterpret_cast<float*>(smem + kT) + r * kMaxNpos;
+    float* xc = reinterpret_cast<float*>(meta + kXc);
+    float* xm = reinterpret_cast<float*>(meta + kXm);
     const int sw = r & 31;
     const float inv_sqrt_d = (float)(1.0 / p.scale);
     const float LOG2E = 1.4426950408889634f;
+    const float scale2 = inv_sqrt_d * LOG2E;
     const int hi_max = p.npos - 1;
+    const int cc_hi = hf ? 1 : 3;  // this half's 32-column chunks: cc_hi, cc_hi - 1
 
     bool ok = mbar_wait(mb + kBarT, 0, abort);
     tc_fence_after();
-    float tsat;
     {
       uint32_t v[32];
-      for (int half = 0; half < 2; ++half) {
-        CS_TMEM_LD32(tmem + lane_base + kColT + half * 32, v);
-        tmem_wait_ld();
+      CS_TMEM_LD32(tmem + lane_base + kColT + hf * 32, v);
+      tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 32; ++c) Ts[(half * 32 + c) ^ sw] = __uint_as_float(v[c]);
-      }
-      tsat = Ts[(p.npos - 1) ^ sw];
+      for (int c = 0; c < 32; ++c) Ts[(hf * 32 + c) ^ sw] = __uint_as_float(v[c]);
     }
+    ok = named_and(pair, 64, ok);  // both halves of the q.E table written
+    const float tsat = Ts[(p.npos - 1) ^ sw];
     const float tsat2 = tsat * LOG2E;
 
     float carry = 0.f;       // running count entering the newer edge of the tile
     float mref = -INFINITY;  // softmax reference max (log2 domain)
-    float lsum = 0.f;
-    ok = __all_sync(0xffffffffu, ok);
+    float lsum = 0.f;        // this half's share of the row sum
+    float* xm2 = reinterpret_cast<float*>(meta + kXm2);
+    const int* bndkc_all = reinterpret_cast<const int*>(meta + kBndKc);
+    // count restart at the chunk boundary ending at key j, or -1 for none
+    auto restart_at = [&](int64_t j) -> float {
+      const int kc = p.key_chunk[j];
+      return kc < qchunk ? offrow[kc] : -1.f;
+    };
     for (int it = 0; ok && it < ntile; ++it) {
       const int st = it & 1, slot = it & 3;
       const int kt = ntile - 1 - it;
       const int64_t key0 = (int64_t)kt * kTileN;
       // S(it) from the MMA warp; the metadata barrier of slot it % 4 cannot run
-      // ahead of this wait (slot reuse needs P(it) from this warpgroup)
+      // ahead of this wait (slot reuse needs P(it) from these warps)
       ok = mbar_wait(mb + kBarS + 8 * st, (it >> 1) & 1, abort) &&
            mbar_wait(mb + kBarMeta + 8 * slot, (it >> 2) & 1, abort);
-      if (!(ok = __all_sync(0xffffffffu, ok))) break;
+      if (!(ok = named_and(pair, 64, ok))) break;
       tc_fence_after();
       const unsigned* fixm = reinterpret_cast<const unsigned*>(meta + kFixMask) + slot * 4;
       const unsigned* bndm = reinterpret_cast<const unsigned*>(meta + kBndMask) + slot * 4;
+      const int* bndkc = bndkc_all + slot * 4;
       const int nvalid =
           (int)(nlim - key0 < 0 ? 0 : (nlim - key0 > kTileN ? kTileN : nlim - key0));
-      // a row is saturated when its count is already >= npos-1 and no chunk
-      // boundary of this tile restarts it below that value
+      // columns of this half hidden from the row (bit c of chunk k): past the
+      // causal / key limit, or fixed keys seen by a selected row (its own key
+      // stays visible)
+      unsigned hide0, hide1;
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int cc = cc_hi - k;
+        const int lim = nvalid - cc * 32;
+        unsigned m = lim >= 32 ? 0u : (lim <= 0 ? ~0u : (~0u << lim));
+        if (qsel) {
+          unsigned fx = fixm[cc];
+          const int64_t self = qp - key0 - cc * 32;
+          if (self >= 0 && self < 32) fx &= ~(1u << (int)self);
+          m |= fx;
+        }
+        (k ? hide1 : hide0) = m;
+      }
+      // count restart of the newest chunk boundary of each 32-key chunk (the
+      // producer publishes its chunk id); other boundaries are looked up
+      // where they are met
+      float roff0 = -1.f, roff1 = -1.f, roff2 = -1.f, roff3 = -1.f;
+      if (chunked) {
+        const int k0 = bndkc[0], k1 = bndkc[1], k2 = bndkc[2], k3 = bndkc[3];
+        if (k0 >= 0 && k0 < qchunk) roff0 = offrow[k0];
+        if (k1 >= 0 && k1 < qchunk) roff1 = offrow[k1];
+        if (k2 >= 0 && k2 < qchunk) roff2 = offrow[k2];
+        if (k3 >= 0 && k3 < qchunk) roff3 = offrow[k3];
+      }
+      auto roff_of = [&](int cc) {
+        return cc == 0 ? roff0 : (cc == 1 ? roff1 : (cc == 2 ? roff2 : roff3));
+      };
+      // the row is saturated for this tile when its count is already >= npos-1
+      // and no live chunk boundary of the tile restarts it below that value
       bool sat = carry >= top;
       if (chunked && sat) {
-        for (int w = 0; w < 4 && sat; ++w) {
-          unsigned bits = bndm[w];
+#pragma unroll 1
+        for (int cc = 0; cc < 4 && sat; ++cc) {
+          const unsigned bd = bndm[cc];
+          const int lim = nvalid - cc * 32;
+          unsigned bits = bd & (lim >= 32 ? ~0u : (lim <= 0 ? 0u : ((1u << lim) - 1u)));
+          const int cf = bd ? 31 - __clz(bd) : -1;
           while (bits && sat) {
-            const int c = w * 32 + __ffs(bits) - 1;
-            bits &= bits - 1;
-            if (c >= nvalid) continue;
-            const int kc = p.key_chunk[key0 + c];
-            if (kc < qchunk) {
-              const float off = offrow[kc];
-              if (off >= 0.f && off < top) sat = false;
-            }
+            const int c = 31 - __clz(bits);
+            bits &= ~(1u << c);
+            const float off = c == cf ? roff_of(cc) : restart_at(key0 + cc * 32 + c);
+            if (off >= 0.f && off < top) sat = false;
           }
         }
       }
-      const bool warp_sat = __all_sync(0xffffffffu, sat || nvalid == 0);
-      float Rc = carry;
-      float tmax = -INFINITY;
-      for (int cc = 3; cc >= 0; --cc) {
-        uint32_t v[32];
-        const uint32_t taddr = tmem + lane_base + kColS0 + st * 128 + cc * 32;
-        CS_TMEM_LD32(taddr, v);
-        tmem_wait_ld();
-        const unsigned fx = qsel ? fixm[cc] : 0u;
-        const int lim = nvalid - cc * 32;          // columns below lim are causal
-        const int self = (int)(qp - key0) - cc * 32;  // column of the query itself
-        if (warp_sat) {
+      // same rows in both warps of the pair, so both take the same path
+      const bool fast = __all_sync(0xffffffffu, sat || nvalid == 0);
+      float tmax;
+      if (fast) {
+        // saturated: every visible score is S * scale2 + tsat2, a monotone map
+        // of the raw S, so the tile max comes from the raw scores (which stay
+        // in TMEM); four accumulators keep the max chains short
+        float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const unsigned hm = k ? hide1 : hide0;
+          if (__all_sync(0xffffffffu, hm == ~0u)) continue;
+          const int cc = cc_hi - k;
+          uint32_t v[32];
+          CS_TMEM_LD32(tmem + lane_base + kColS0 + st * 128 + cc * 32, v);
+          tmem_wait_ld();
+          if (hm == 0u) {
+#pragma unroll
+            for (int c = 0; c < 32; c += 4) {
+              m0 = fmaxf(m0, __uint_as_float(v[c]));
+              m1 = fmaxf(m1, __uint_as_float(v[c + 1]));
+              m2 = fmaxf(m2, __uint_as_float(v[c + 2]));
+              m3 = fmaxf(m3, __uint_as_float(v[c + 3]));
+            }
+          } else {
+#pragma unroll
+            for (int c = 0; c < 32; c += 4) {
+              m0 = (hm >> c) & 1u ? m0 : fmaxf(m0, __uint_as_float(v[c]));
+              m1 = (hm >> (c + 1)) & 1u ? m1 : fmaxf(m1, __uint_as_float(v[c + 1]));
+              m2 = (hm >> (c + 2)) & 1u ? m2 : fmaxf(m2, __uint_as_float(v[c + 2]));
+              m3 = (hm >> (c + 3)) & 1u ? m3 : fmaxf(m3, __uint_as_float(v[c + 3]));
+            }
+          }
+        }
+        const float mraw = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+        tmax = mraw > -INFINITY ? fmaf(mraw, scale2, tsat2) : -INFINITY;
+        carry = sat ? fmaxf(carry, top) : carry;
+        (hf ? xm2 : xm)[r] = tmax;
+        named_sync(pair, 64);
+        tmax = fmaxf(xm[r], xm2[r]);
+      } else {
+        // phase A: gates and the thread-local reverse count.  The newer half
+        // starts from the count entering the tile; the older half from 0, and
+        // records the newest column where a chunk restart cut the dependence
+        // on the newer half (columns above it add that half's count in phase B)
+        float Rc = hf == 0 ? carry : 0.f;
+        int rst = -1;
+#pragma unroll 1
+        for (int k = 0; k < 2; ++k) {
+          const int cc = cc_hi - k;
+          uint32_t v[32];
+          CS_TMEM_LD32(tmem + lane_base + kColS0 + st * 128 + cc * 32, v);
+          tmem_wait_ld();
 #pragma unroll
           for (int c = 0; c < 32; ++c) {
-            float s = fmaf(__uint_as_float(v[c]), inv_sqrt_d * LOG2E, tsat2);
-            const bool hide = (c >= lim) || (((fx >> c) & 1u) && c != self);
-            s = hide ? -INFINITY : s;
-            tmax = fmaxf(tmax, s);
-            v[c] = __float_as_uint(s);
+            const float L = __uint_as_float(v[c]) * inv_sqrt_d;
+            v[c] = __float_as_uint(__fdividef(1.f, 1.f + ex2(-L * LOG2E)));
           }
-        } else {
+          const int lim = nvalid - cc * 32;
           const unsigned bd = bndm[cc];
+          const int cf = bd ? 31 - __clz(bd) : -1;
+          const float rf = roff_of(cc);
 #pragma unroll
           for (int c = 31; c >= 0; --c) {
-            const float L = __uint_as_float(v[c]) * inv_sqrt_d;
-            const float e = ex2(-L * LOG2E);
-            const float gt = __fdividef(1.f, 1.f + e);
             float base = Rc;
             if ((bd >> c) & 1u) {  // warp-uniform: last key of a chunk
-              const int kc = p.key_chunk[key0 + cc * 32 + c];
-              if (kc < qchunk) {
-                const float off = offrow[kc];
-                base = off >= 0.f ? off : base;
+              const float off = c == cf ? rf : restart_at(key0 + cc * 32 + c);
+              if (off >= 0.f) {
+                base = off;
+                if (c < lim && rst < 0) rst = cc * 32 + c;
               }
             }
-            const bool live = c < lim;
-            Rc = live ? base + gt : Rc;
-            const float pos = fminf(Rc, top);
+            Rc = c < lim ? base + __uint_as_float(v[c]) : Rc;
+            v[c] = __float_as_uint(Rc);
+          }
+          CS_TMEM_ST32(tmem + lane_base + kColR + cc * 32, v);
+        }
+        tmem_wait_st();
+        // the handoff has its own barrier: the newer half does not wait here,
+        // and its next arrival at `pair` must not complete this one
+        float cin = 0.f;  // count entering the older half from the newer one
+        if (hf == 0) {
+          xc[r] = Rc;
+          named_arrive(pair + 4, 64);
+        } else {
+          named_sync(pair + 4, 64);
+          cin = xc[r];
+        }
+        // phase B: positions, interpolated bias, masks; scores back into S
+        float tm = -INFINITY;
+#pragma unroll 1
+        for (int k = 0; k < 4; ++k) {  // 16-column pieces
+          const int col0 = (cc_hi - (k >> 1)) * 32 + (k & 1) * 16;
+          const unsigned hm = ((k >> 1) ? hide1 : hide0) >> ((k & 1) * 16);
+          const int dep = rst - col0;  // columns above dep add cin
+          uint32_t v[16], w[16];
+          CS_TMEM_LD16(tmem + lane_base + kColS0 + st * 128 + col0, v);
+          CS_TMEM_LD16(tmem + lane_base + kColR + col0, w);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const float Rv = __uint_as_float(w[c]) + (c > dep ? cin : 0.f);
+            const float pos = fminf(Rv, top);
             int lo;
             const float fl = floor_pos(pos, lo);
             const int hi = lo < hi_max ? lo + 1 : hi_max;
             const float tlo = Ts[lo ^ sw];
             const float bias = fmaf(pos - fl, Ts[hi ^ sw] - tlo, tlo);
+            const float L = __uint_as_float(v[c]) * inv_sqrt_d;
             float s = (L + bias) * LOG2E;
-            const bool hide = !live || (((fx >> c) & 1u) && c != self);
-            s = hide ? -INFINITY : s;
-            tmax = fmaxf(tmax, s);
+            s = (hm >> c) & 1u ? -INFINITY : s;
+            tm = fmaxf(tm, s);
             v[c] = __float_as_uint(s);
           }
+          CS_TMEM_ST16(tmem + lane_base + kColS0 + st * 128 + col0, v);
         }
-        CS_TMEM_ST32(taddr, v);  // scores back into the S buffer
+        tmem_wait_st();
+        // tile max of both halves, and the count leaving the tile (older half)
+        (hf ? xm2 : xm)[r] = tm;
+        if (hf) xc[r] = Rc + (rst < 0 ? cin : 0.f);
+        named_sync(pair, 64);
+        tmax = fmaxf(xm[r], xm2[r]);
+        carry = xc[r];
       }
-      tmem_wait_st();
-      // rows whose keys all lie in the future of this tile keep their count
-      carry = warp_sat ? (sat ? fmaxf(carry, top) : carry) : Rc;
       // PV of the previous tile must finish before O and P are touched
       if (it > 0) {
         ok = mbar_wait(mb + kBarPV + 8 * ((it - 1) & 1), ((it - 1) >> 1) & 1, abort);
-        if (!(ok = __all_sync(0xffffffffu, ok))) break;
+        if (!(ok = named_and(pair, 64, ok))) break;
         tc_fence_after();
       }
       float mnew = mref;
@@ -612,59 +779,87 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
       if (it > 0 && __any_sync(0xffffffffu, rescale)) {
         const float f = rescale ? ex2(mref - mnew) : 1.f;
         lsum *= f;
-        for (int cc = 0; cc < 4; ++cc) {
+        for (int k = 0; k < 2; ++k) {  // this half rescales 64 of the 128 O columns
+          const uint32_t taddr = tmem + lane_base + kColO + hf * 64 + k * 32;
           uint32_t v[32];
-          CS_TMEM_LD32(tmem + lane_base + kColO + cc * 32, v);
+          CS_TMEM_LD32(taddr, v);
           tmem_wait_ld();
 #pragma unroll
           for (int c = 0; c < 32; ++c) v[c] = __float_as_uint(__uint_as_float(v[c]) * f);
-          CS_TMEM_ST32(tmem + lane_base + kColO + cc * 32, v);
+          CS_TMEM_ST32(taddr, v);
         }
         tmem_wait_st();
       }
       mref = mnew;
-      // P = 2^(s - mref) packed to bf16/f16 into row r of the swizzled P tile
+      // P = 2^(s - mref) (bf16/f16) into this half's columns of row r; a
+      // saturated tile forms s - mref = S * scale2 + (tsat2 - mref) directly
       const float mcur = mref > -INFINITY ? mref : 0.f;
-      float part = 0.f;
-      for (int cc = 0; cc < 4; ++cc) {
+      const float fb = tsat2 - mcur;
+      float part0 = 0.f, part1 = 0.f;
+#pragma unroll 1
+      for (int k = 0; k < 2; ++k) {
+        const int cc = cc_hi - k;
+        const unsigned hm = k ? hide1 : hide0;
         uint32_t v[32];
-        CS_TMEM_LD32(tmem + lane_base + kColS0 + st * 128 + cc * 32, v);
-        tmem_wait_ld();
+        if (fast && __all_sync(0xffffffffu, hm == ~0u)) {
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
+          for (int c = 0; c < 32; ++c) v[c] = 0u;
+        } else {
+          CS_TMEM_LD32(tmem + lane_base + kColS0 + st * 128 + cc * 32, v);
+          tmem_wait_ld();
+          if (fast) {
+#pragma unroll
+            for (int c = 0; c < 32; ++c)
+              v[c] = __float_as_uint(ex2(fmaf(__uint_as_float(v[c]), scale2, fb)));
+            if (hm) {
+#pragma unroll
+              for (int c = 0; c < 32; ++c) v[c] = (hm >> c) & 1u ? 0u : v[c];
+            }
+          } else {
+#pragma unroll
+            for (int c = 0; c < 32; ++c) v[c] = __float_as_uint(ex2(__uint_as_float(v[c]) - mcur));
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
           uint32_t w[4];
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
-            const float e0 = ex2(__uint_as_float(v[q4 * 8 + 2 * u]) - mcur);
-            const float e1 = ex2(__uint_as_float(v[q4 * 8 + 2 * u + 1]) - mcur);
-            part += e0 + e1;
+            const float e0 = __uint_as_float(v[q * 8 + 2 * u]);
+            const float e1 = __uint_as_float(v[q * 8 + 2 * u + 1]);
+            part0 += e0;
+            part1 += e1;
             w[u] = Pack2<T>::pack(e0, e1);
           }
-          *reinterpret_cast<uint4*>(smem + kP + sw128(r, cc * 4 + q4, 128)) =
+          *reinterpret_cast<uint4*>(smem + kP + sw128(r, cc * 4 + q, 128)) =
               make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
-      lsum += part;
+      lsum += part0 + part1;
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(mb + kBarP);
     }
-    // epilogue: O / l for this row
+    // epilogue: O / l, each half writes 64 of the 128 output columns
     if (ok && ntile > 0) {
       ok = mbar_wait(mb + kBarPV + 8 * ((ntile - 1) & 1), ((ntile - 1) >> 1) & 1, abort);
-      ok = __all_sync(0xffffffffu, ok);
       tc_fence_after();
     }
+    ok = named_and(pair, 64, ok);
+    (hf == 0 ? xc : xm)[r] = lsum;
+    named_sync(pair, 64);
+    const float total = xc[r] + xm[r];
     int32_t bits = 0;
-    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+    const float inv = total > 0.f ? 1.f / total : 0.f;
     char* orow = row_ok ? static_cast<char*>(p.out) + (i * p.o_stride_tok +
                                                        (int64_t)h * p.o_stride_head) *
                                                           dtype_size(p.out_dtype)
                         : nullptr;
-    for (int cc = 0; cc < 4; ++cc) {
+    for (int k = 0; k < 2; ++k) {
+      const int col0 = hf * 64 + k * 32;
       uint32_t v[32];
       if (ntile > 0) {
-        CS_TMEM_LD32(tmem + lane_base + kColO + cc * 32, v);
+        CS_TMEM_LD32(tmem + lane_base + kColO + col0, v);
         tmem_wait_ld();
       } else {
 #pragma unroll
@@ -678,7 +873,7 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
                                    __uint_as_float(v[c + 2]) * inv,
                                    __uint_as_float(v[c + 3]) * inv);
             if (!isfinite(x.x + x.y + x.z + x.w)) bits |= CS_ST_LOGIT_NONFINITE;
-            reinterpret_cast<float4*>(orow)[(cc * 32 + c) / 4] = x;
+            reinterpret_cast<float4*>(orow)[(col0 + c) / 4] = x;
           }
         } else {
 #pragma unroll
@@ -693,7 +888,7 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
               w[u] = Pack2<T>::pack(x0, x1);
             }
             if (!isfinite(chk)) bits |= CS_ST_LOGIT_NONFINITE;
-            reinterpret_cast<uint4*>(orow)[(cc * 32 + c) / 8] = make_uint4(w[0], w[1], w[2], w[3]);
+            reinterpret_cast<uint4*>(orow)[(col0 + c) / 8] = make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
       }
@@ -704,7 +899,7 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
   tc_fence_before();
   __syncthreads();
   if (tid == 0 && *abort) report(p.status, CS_ST_TIMEOUT);
-  if (warp == 8) {
+  if (warp == 12) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
   }
