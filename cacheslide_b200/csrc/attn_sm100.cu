@@ -26,7 +26,12 @@
 // TMEM (512 columns): S0 [0,128), S1 [128,256), O [256,384), T [384,448).
 // Every mbarrier wait is bounded; on expiry the CTA raises CS_ST_TIMEOUT,
 // drains its copies and MMAs, frees its TMEM and returns.
+#include <cuda.h>
 #include <math.h>
+
+#include <cstdlib>
+#include <cstring>
+#include <numeric>
 
 #include "common.cuh"
 
@@ -61,6 +66,7 @@ constexpr uint32_t kBarEnd = 88;    // MMA drain
 constexpr uint32_t kTmemSlot = 96;  // TMEM base address
 constexpr uint32_t kAbort = 100;    // abort flag
 constexpr uint32_t kNtile = 104;    // key tiles of this CTA
+constexpr uint32_t kNmax = 108;     // keys needed by the furthest row of this CTA
 constexpr uint32_t kFixMask = 112;  // [4 slots][4 words] key is fixed
 constexpr uint32_t kBndMask = 176;  // [4 slots][4 words] key is the last of its chunk
 constexpr uint32_t kBarMeta = 240;  // [4] producer -> softmax: key metadata of slot it % 4
@@ -229,6 +235,20 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
 __device__ __forceinline__ void named_sync(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
+// tile::gather4: rows r0..r3 of a 2-D tensor map, 64 elements from column x,
+// into 4 consecutive 128-byte rows at dst (the map's 128-byte swizzle applies)
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* map, int x, int r0,
+                                            int r1, int r2, int r3, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
 __device__ __forceinline__ void named_arrive(uint32_t id, uint32_t count) {
   asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
@@ -270,18 +290,31 @@ template <> struct Pack2<__half> {
 };
 
 struct Args {
+  // K/V row maps of the TMA path (2-D: row x element, 128-byte swizzle, box
+  // 64 x 1 for tile::gather4): [0] primary K, [1] primary V, [2] sidecar K,
+  // [3] sidecar V.  The primary maps are the paged cache (K and V in one row,
+  // V from element vx0) or the dense K and V tensors.
+  CUtensorMap tm[4];
   cs_attn_params p;
   PagedView pv;
   int G, R, fmt;  // heads per KV head, rows per tile, 0 = f16 / 1 = bf16
   int tiles_per_head;
   int bs_shift;   // log2(block size) when it is a power of two, else -1
+  int tma;        // 1: K/V tiles by TMA gather4 (per-row cp.async otherwise)
+  int vx0;        // first V element of a primary V map row
+  int64_t nrb, nrh, nro;       // paged slot (b, o), head g -> map row b*nrb + g*nrh + o*nro
+  int64_t srr, srh;            // sidecar row r, head g -> map row r*srr + g*srh
+  int64_t krt, krh, vrt, vrh;  // dense key j, head g -> K row j*krt + g*krh, V row j*vrt + g*vrh
 };
 
 // K row address of key j for KV head g (0 = no row: zero fill); bit 0 tags a
-// sidecar row, whose V lives at the same offset in side_v
+// sidecar row, whose V lives at the same offset in side_v.  rk / rv receive the
+// row indices of the key's K and V in the tensor maps of the TMA path.
 template <typename T>
-__device__ __forceinline__ uint64_t key_row_addr(const Args& a, int64_t j, int g) {
+__device__ __forceinline__ uint64_t key_src(const Args& a, int64_t j, int g, int32_t& rk,
+                                            int32_t& rv) {
   const cs_attn_params& p = a.p;
+  rk = rv = 0;
   if (j >= p.nk) return 0;
   if (p.kv_slots) {
     const int64_t s = p.kv_slots[j];
@@ -296,11 +329,15 @@ __device__ __forceinline__ uint64_t key_row_addr(const Args& a, int64_t j, int g
         b = s / pv.bs;
         o = s - b * pv.bs;
       }
+      rk = rv = (int32_t)(b * a.nrb + g * a.nrh + o * a.nro);
       return reinterpret_cast<uint64_t>(pv.cache + b * pv.sb + g * pv.sh + o * pv.so);
     }
     const int64_t r = s - pv.native_total;
+    rk = rv = (int32_t)(r * a.srr + g * a.srh);
     return reinterpret_cast<uint64_t>(pv.side_k + r * pv.ssr + g * pv.ssh) | 1ull;
   }
+  rk = (int32_t)(j * a.krt + g * a.krh);
+  rv = (int32_t)(j * a.vrt + g * a.vrh);
   return reinterpret_cast<uint64_t>(static_cast<const char*>(p.k) +
                                     (j * p.k_stride_tok + (int64_t)g * p.k_stride_head) *
                                         (int64_t)sizeof(T));
@@ -361,6 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
       nmax = n > nmax ? n : nmax;
     }
     *reinterpret_cast<int*>(meta + kNtile) = (int)((nmax + kTileN - 1) / kTileN);
+    *reinterpret_cast<int*>(meta + kNmax) = (int)nmax;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 12) {
@@ -404,6 +442,28 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
     mbar_arrive(mb + kBarQ);
 
     uint64_t* rowaddr = reinterpret_cast<uint64_t*>(meta + kRowAddr);
+    const bool tma = a.tma != 0;
+    const unsigned kAll = 0xffffffffu;
+    // source and metadata of key key0 + pt, read one tile ahead so that their
+    // global loads overlap the stage waits
+    uint64_t ka = 0;
+    int32_t rk = 0, rv = 0;
+    bool fixed = false, bnd = false;
+    int kcj = -1;
+    bool slot_bad = false;  // a key some row sees has no valid slot (read as zeros)
+    const int64_t nmax = *reinterpret_cast<volatile int*>(meta + kNmax);
+    auto load_key = [&](int it2) {
+      const int64_t j = (int64_t)(ntile - 1 - it2) * kTileN + pt;
+      const bool in = j < p.nk;
+      // keys past the end: zero rows by cp.async; the TMA path repeats the
+      // last key's row (finite data, and its P column is zero)
+      ka = key_src<T>(a, tma && !in ? p.nk - 1 : j, g, rk, rv);
+      slot_bad |= j < nmax && ka == 0;
+      fixed = in && p.k_fixed != nullptr && p.k_fixed[j] != 0;
+      kcj = in && p.pos_mode == CS_POS_CHUNK ? p.key_chunk[j] : -1;
+      bnd = kcj >= 0 && (j + 1 < p.nk) && p.key_chunk[j + 1] != kcj;
+    };
+    if (ntile > 0) load_key(0);
     for (int it = 0; it < ntile; ++it) {
       const int st = it & 1, slot = it & 3;
       const int kt = ntile - 1 - it;
@@ -413,16 +473,10 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
       bool ok = it < 2 || mbar_wait(mb + kBarS + 8 * st, ((it - 2) >> 1) & 1, abort);
       if (!named_and(1, 128, ok)) break;
       {
-        const int64_t j = key0 + pt;
-        rowaddr[pt] = key_row_addr<T>(a, j, g);
-        const bool in = j < p.nk;
-        const bool fixed = in && p.k_fixed != nullptr && p.k_fixed[j] != 0;
-        const int kcj = in && p.pos_mode == CS_POS_CHUNK ? p.key_chunk[j] : -1;
-        const bool bnd = kcj >= 0 && (j + 1 < p.nk) && p.key_chunk[j + 1] != kcj;
-        const unsigned fm = __ballot_sync(0xffffffffu, fixed);
-        const unsigned bm = __ballot_sync(0xffffffffu, bnd);
+        const unsigned fm = __ballot_sync(kAll, fixed);
+        const unsigned bm = __ballot_sync(kAll, bnd);
         // chunk id of the newest boundary of these 32 keys (-1: none)
-        const int kc_top = __shfl_sync(0xffffffffu, kcj, bm ? 31 - __clz(bm) : 0);
+        const int kc_top = __shfl_sync(kAll, kcj, bm ? 31 - __clz(bm) : 0);
         if (lane == 0) {
           reinterpret_cast<unsigned*>(meta + kFixMask)[slot * 4 + (warp - 8)] = fm;
           reinterpret_cast<unsigned*>(meta + kBndMask)[slot * 4 + (warp - 8)] = bm;
@@ -430,30 +484,88 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
         }
       }
       mbar_arrive(mb + kBarMeta + 8 * slot);  // metadata published (release)
-      named_sync(1, 128);                     // every row address visible
-      const int c16 = pt & 15;
+      const uint64_t cka = ka;  // this tile's source; the registers are reloaded below
+      const int64_t jr = key0 + pt < p.nk ? key0 + pt : p.nk - 1;
+      // TMA: a group of 4 keys (lanes 4q..4q+3) whose rows all live in the
+      // primary map (grp 1) or all in the sidecar (grp 2) is fetched with two
+      // tile::gather4 loads per operand (64 columns x 4 rows each), issued by
+      // the group's first lane; other groups copy their rows with cp.async
+      int grp = 0;
+      uint32_t tx = 0;
+      int k1 = 0, k2 = 0, k3 = 0, v1 = 0, v2 = 0, v3 = 0;
+      const int crk = rk, crv = rv;
+      if (tma) {
+        const int cls = cka == 0 ? 0 : ((cka & 1ull) ? 2 : 1);
+        const unsigned b1 = __ballot_sync(kAll, cls == 1), b2 = __ballot_sync(kAll, cls == 2);
+        const int sh = lane & ~3;
+        grp = ((b1 >> sh) & 0xFu) == 0xFu ? 1 : (((b2 >> sh) & 0xFu) == 0xFu ? 2 : 0);
+        tx = __popc(__ballot_sync(kAll, grp != 0 && (lane & 3) == 0)) * 1024u;
+        k1 = __shfl_down_sync(kAll, crk, 1);
+        k2 = __shfl_down_sync(kAll, crk, 2);
+        k3 = __shfl_down_sync(kAll, crk, 3);
+        v1 = __shfl_down_sync(kAll, crv, 1);
+        v2 = __shfl_down_sync(kAll, crv, 2);
+        v3 = __shfl_down_sync(kAll, crv, 3);
+        if (lane == 0 && tx) mbar_expect_tx(mb + kBarK + 8 * st, tx);
+        if (grp && (lane & 3) == 0) {
+          const CUtensorMap* m = grp == 1 ? &a.tm[0] : &a.tm[2];
+          for (int cb = 0; cb < 2; ++cb)
+            tma_gather4(sbase + kK0 + st * 32768 + cb * 16384 + pt * 128, m, cb * 64, crk, k1, k2,
+                        k3, mb + kBarK + 8 * st);
+        }
+        if (!grp) {
+          for (int c16 = 0; c16 < 16; ++c16) {
+            const char* src = cka ? reinterpret_cast<const char*>(cka & ~1ull) + c16 * 16
+                                  : static_cast<const char*>(p.q);
+            cp_async16(sbase + kK0 + st * 32768 + sw128(pt, c16, 128), src, cka != 0);
+          }
+        }
+      } else {
+        rowaddr[pt] = cka;
+        named_sync(1, 128);  // every row address visible
+        const int c16 = pt & 15;
 #pragma unroll 4
-      for (int m = 0; m < 16; ++m) {
-        const int row = (pt >> 4) + 8 * m;
-        const uint64_t ka = rowaddr[row];
-        const char* src = ka ? reinterpret_cast<const char*>(ka & ~1ull) + c16 * 16
-                             : static_cast<const char*>(p.q);
-        cp_async16(sbase + kK0 + st * 32768 + sw128(row, c16, 128), src, ka != 0);
+        for (int m = 0; m < 16; ++m) {
+          const int row = (pt >> 4) + 8 * m;
+          const uint64_t ra = rowaddr[row];
+          const char* src = ra ? reinterpret_cast<const char*>(ra & ~1ull) + c16 * 16
+                               : static_cast<const char*>(p.q);
+          cp_async16(sbase + kK0 + st * 32768 + sw128(row, c16, 128), src, ra != 0);
+        }
       }
       cp_async_arrive_noinc(mb + kBarK + 8 * st);
+      if (it + 1 < ntile) load_key(it + 1);
       // V stage free once PV(it-2) completed
       ok = it < 2 || mbar_wait(mb + kBarPV + 8 * st, ((it - 2) >> 1) & 1, abort);
       if (!named_and(1, 128, ok)) break;
+      if (tma) {
+        if (lane == 0 && tx) mbar_expect_tx(mb + kBarV + 8 * st, tx);
+        if (grp && (lane & 3) == 0) {
+          const CUtensorMap* m = grp == 1 ? &a.tm[1] : &a.tm[3];
+          const int x0 = grp == 1 ? a.vx0 : 0;
+          for (int cb = 0; cb < 2; ++cb)
+            tma_gather4(sbase + kV0 + st * 32768 + cb * 16384 + pt * 128, m, x0 + cb * 64, crv,
+                        v1, v2, v3, mb + kBarV + 8 * st);
+        }
+        if (!grp) {
+          const char* vrow = cka ? value_row_addr<T>(a, cka, jr, g) : static_cast<const char*>(p.q);
+          for (int c16 = 0; c16 < 16; ++c16)
+            cp_async16(sbase + kV0 + st * 32768 + sw128(pt, c16, 128), vrow + c16 * 16, cka != 0);
+        }
+      } else {
+        const int c16 = pt & 15;
 #pragma unroll 4
-      for (int m = 0; m < 16; ++m) {
-        const int row = (pt >> 4) + 8 * m;
-        const uint64_t ka = rowaddr[row];
-        const char* src = ka ? value_row_addr<T>(a, ka, key0 + row, g) + c16 * 16
-                             : static_cast<const char*>(p.q);
-        cp_async16(sbase + kV0 + st * 32768 + sw128(row, c16, 128), src, ka != 0);
+        for (int m = 0; m < 16; ++m) {
+          const int row = (pt >> 4) + 8 * m;
+          const uint64_t ra = rowaddr[row];
+          const char* src = ra ? value_row_addr<T>(a, ra, key0 + row, g) + c16 * 16
+                               : static_cast<const char*>(p.q);
+          cp_async16(sbase + kV0 + st * 32768 + sw128(row, c16, 128), src, ra != 0);
+        }
       }
       cp_async_arrive_noinc(mb + kBarV + 8 * st);
     }
+    if (slot_bad) report(p.status, CS_ST_SLOT_RANGE);
     cp_async_wait_all();
   } else if (warp == 12) {
     // ================================================================== MMA
@@ -936,6 +1048,90 @@ bool prefill_supported(const cs_attn_params* p) {
   return true;
 }
 
+// 2-D row map over `rows` rows of `inner` 16-bit elements, `unit` bytes apart,
+// read in 64 x 1 boxes with the 128-byte swizzle of the UMMA operand tiles
+bool encode_rows(CUtensorMap* m, const void* base, bool bf16, int64_t inner, int64_t rows,
+                 int64_t unit) {
+  if (base == nullptr || reinterpret_cast<uintptr_t>(base) % 16 || unit % 16 ||
+      unit < inner * 2 || rows < 1 || rows > INT32_MAX || inner < 128)
+    return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)unit};
+  const cuuint32_t box[2] = {64, 1}, es[2] = {1, 1};
+  return cuTensorMapEncodeTiled(m,
+                                bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                                2, const_cast<void*>(base), dims, strides, box, es,
+                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Row structure of the K/V storage for the TMA path: every row the kernel
+// reads must be base + row * unit, with unit the gcd of the byte strides.
+// Returns false (per-row cp.async path) when a stride is negative or the
+// layout does not fit the rules of encode_rows.
+bool setup_tma(Args& a) {
+  const cs_attn_params& p = a.p;
+  const bool bf16 = p.in_dtype == CS_BF16;
+  const int64_t es = 2;
+  auto gcd3 = [](int64_t x, int64_t y, int64_t z) { return std::gcd(std::gcd(x, y), z); };
+  if (p.kv_slots) {
+    const PagedView& pv = a.pv;
+    if (pv.sb < 0 || pv.sh < 0 || pv.so < 0 || pv.se != es) return false;
+    const int64_t unit = gcd3(pv.sb, pv.sh, pv.so);
+    if (unit <= 0) return false;
+    const int64_t nb = pv.native_total / pv.bs;
+    const int64_t rows = ((nb - 1) * pv.sb + (pv.kv_heads - 1) * pv.sh + (pv.bs - 1) * pv.so) /
+                             unit + 1;
+    if (!encode_rows(&a.tm[0], pv.cache, bf16, 2 * pv.head_dim, rows, unit)) return false;
+    a.tm[1] = a.tm[0];
+    a.vx0 = (int)pv.head_dim;
+    a.nrb = pv.sb / unit;
+    a.nrh = pv.sh / unit;
+    a.nro = pv.so / unit;
+    if (pv.side_capacity > 0) {
+      if (pv.ssr < 0 || pv.ssh < 0 || pv.sse != es) return false;
+      const int64_t su = std::gcd(pv.ssr, pv.ssh);
+      if (su <= 0) return false;
+      const int64_t srows = ((pv.side_capacity - 1) * pv.ssr + (pv.kv_heads - 1) * pv.ssh) / su + 1;
+      if (!encode_rows(&a.tm[2], pv.side_k, bf16, pv.head_dim, srows, su) ||
+          !encode_rows(&a.tm[3], pv.side_v, bf16, pv.head_dim, srows, su))
+        return false;
+      a.srr = pv.ssr / su;
+      a.srh = pv.ssh / su;
+    } else {
+      a.tm[2] = a.tm[3] = a.tm[0];  // never addressed: no slot reaches the sidecar
+    }
+    return true;
+  }
+  const int64_t kt = p.k_stride_tok * es, kh = p.k_stride_head * es;
+  const int64_t vt = p.v_stride_tok * es, vh = p.v_stride_head * es;
+  if (kt < 0 || kh < 0 || vt < 0 || vh < 0) return false;
+  const int64_t ku = std::gcd(kt, kh), vu = std::gcd(vt, vh);
+  if (ku <= 0 || vu <= 0) return false;
+  const int64_t krows = ((int64_t)(p.nk - 1) * kt + (int64_t)(p.hkv - 1) * kh) / ku + 1;
+  const int64_t vrows = ((int64_t)(p.nk - 1) * vt + (int64_t)(p.hkv - 1) * vh) / vu + 1;
+  if (!encode_rows(&a.tm[0], p.k, bf16, p.d, krows, ku) ||
+      !encode_rows(&a.tm[1], p.v, bf16, p.dv, vrows, vu))
+    return false;
+  a.tm[2] = a.tm[0];
+  a.tm[3] = a.tm[1];
+  a.vx0 = 0;
+  a.krt = kt / ku;
+  a.krh = kh / ku;
+  a.vrt = vt / vu;
+  a.vrh = vh / vu;
+  return true;
+}
+
+// CACHESLIDE_PREFILL_COPY=cpasync selects the per-row cp.async K/V path
+// (the path taken anyway when the storage has no row structure for TMA)
+bool tma_enabled() {
+  const char* e = std::getenv("CACHESLIDE_PREFILL_COPY");
+  return !(e != nullptr && std::strcmp(e, "cpasync") == 0);
+}
+
 }  // namespace
 }  // namespace cs
 
@@ -947,6 +1143,7 @@ extern "C" int cs_cope_attn_prefill(const cs_attn_params* p, void* stream) {
   if (!prefill_supported(p)) return CS_ERR_UNSUPPORTED;
   if (p->nq == 0) return CS_OK;
   Args a;
+  memset(&a, 0, sizeof(a));
   a.p = *p;
   a.pv = p->kv_slots ? PagedView::make(p->paged) : PagedView{};
   a.G = p->hq / p->hkv;
@@ -962,6 +1159,7 @@ extern "C" int cs_cope_attn_prefill(const cs_attn_params* p, void* stream) {
       a.bs_shift = s;
     }
   }
+  a.tma = (p->nk > 0 && tma_enabled() && setup_tma(a)) ? 1 : 0;
   const int blocks = a.tiles_per_head * p->hkv;
   static bool configured[2] = {false, false};
   auto launch = [&](auto kern, int which) -> int {

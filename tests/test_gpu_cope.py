@@ -291,6 +291,94 @@ def test_tensor_core_prefill_matches_generic_and_oracle(cuda, assoc, chunk, page
     np.testing.assert_allclose(outs[0], want, **BF16)
 
 
+@pytest.mark.parametrize("layout", ["sidecar", "block_major", "dense_strided"])
+def test_tensor_core_prefill_copy_paths_agree(cuda, layout, monkeypatch):
+    """TMA gather4 and per-row cp.async K/V loads give the generic kernel's result.
+
+    sidecar: 4-key groups wholly in the paged cache, wholly in the sidecar, mixed,
+    and one key without a valid slot (zero row, CS_ST_SLOT_RANGE); block_major:
+    a [blocks, block_size, heads, 2D] cache seen through a permuted view; and
+    dense K/V that are strided views of one fused QKV tensor.
+    """
+    import ctypes
+
+    from cacheslide_b200 import _native as N
+    from cacheslide_b200.position import _Holder, _base_params
+
+    nq, nk, hq, hkv, d, bs = 200, 700, 8, 2, 128, 16
+    g = torch.Generator().manual_seed(41)
+    q = (torch.randn(nq, hq, d, generator=g) / d ** 0.5).to(torch.bfloat16).to(cuda)
+    k = (torch.randn(nk, hkv, d, generator=g) / d ** 0.5).to(torch.bfloat16).to(cuda)
+    v = torch.randn(nk, hkv, d, generator=g).to(torch.bfloat16).to(cuda)
+    rows = torch.sort(torch.randperm(nk, generator=g)[:nq]).values.to(cuda)
+    E = torch.randn(d, 64, generator=g) * 0.02
+    cope = _cope(E.numpy(), cuda)
+    holder = _Holder(cope, cope.position_embeddings.detach())
+    cache = slots = side_k = side_v = None
+    kd = vd = None
+    expect_status = 0
+    tok = torch.arange(nk, device=cuda)
+    if layout == "sidecar":
+        # 640 native slots: keys 0..599 native, 600..699 in sidecar rows 0..99;
+        # keys 2 mod 8 swap sides (native slots 600.., sidecar rows 100..),
+        # so 4-key groups are all native, all sidecar or mixed
+        nb, cap = 40, 200
+        slots = tok.clone()
+        slots[600:] = nb * bs + torch.arange(nk - 600, device=cuda)
+        sw = tok[2::8]
+        slots[2::8] = torch.where(sw >= 600, 600 + (sw - 600) // 8, nb * bs + 100 + sw // 8)
+        slots[313] = -1
+        expect_status = N.ST_SLOT_RANGE
+        cache = torch.randn(nb, hkv, bs, 2 * d, generator=g).to(torch.bfloat16).to(cuda)
+        side_k = torch.randn(cap, hkv, d, generator=g).to(torch.bfloat16).to(cuda)
+        side_v = torch.randn(cap, hkv, d, generator=g).to(torch.bfloat16).to(cuda)
+        nat = (slots >= 0) & (slots < nb * bs)
+        sn, jn = slots[nat], tok[nat]
+        cache[sn // bs, :, sn % bs, :d] = k[jn]
+        cache[sn // bs, :, sn % bs, d:] = v[jn]
+        sd = (slots >= nb * bs)
+        side_k[slots[sd] - nb * bs] = k[tok[sd]]
+        side_v[slots[sd] - nb * bs] = v[tok[sd]]
+    elif layout == "block_major":
+        nb = (nk + bs - 1) // bs + 5
+        perm = torch.randperm(nb, generator=g)[: (nk + bs - 1) // bs].to(cuda)
+        slots = perm[tok // bs] * bs + tok % bs
+        store = torch.zeros(nb, bs, hkv, 2 * d, dtype=torch.bfloat16, device=cuda)
+        store[slots // bs, slots % bs, :, :d] = k
+        store[slots // bs, slots % bs, :, d:] = v
+        cache = store.permute(0, 2, 1, 3)
+    else:
+        qkv = torch.zeros(nk, 3, hkv, d, dtype=torch.bfloat16, device=cuda)
+        qkv[:, 1], qkv[:, 2] = k, v
+        kd, vd = qkv[:, 1], qkv[:, 2]
+    lib = N.load()
+    outs = {}
+    for mode in ("tma", "cpasync", "generic"):
+        if mode == "cpasync":
+            monkeypatch.setenv("CACHESLIDE_PREFILL_COPY", "cpasync")
+        else:
+            monkeypatch.delenv("CACHESLIDE_PREFILL_COPY", raising=False)
+        out = torch.empty(nq, hq, d, dtype=torch.bfloat16, device=cuda)
+        p = _base_params(q, kd, vd, holder, rows, None, nk, hkv, d)
+        if cache is not None:
+            p.paged = N.paged_view(cache, side_k, side_v)
+            p.kv_slots = slots.data_ptr()
+        p.out = out.data_ptr()
+        p.o_stride_tok, p.o_stride_head = out.stride(0), out.stride(1)
+        st = N.Status(cuda)
+        p.status = st.ptr
+        fn = lib.cs_cope_attn if mode == "generic" else lib.cs_cope_attn_prefill
+        N.check(fn(ctypes.byref(p), N.stream_of(cuda)), mode)
+        assert st.read() == expect_status, mode
+        outs[mode] = out.float().cpu().numpy()
+    np.testing.assert_array_equal(outs["tma"], outs["cpasync"])
+    np.testing.assert_allclose(outs["tma"], outs["generic"], **BF16)
+    if layout != "sidecar":
+        want = ocope.cope_attention(q.float().cpu().numpy(), k.float().cpu().numpy(),
+                                    v.float().cpu().numpy(), E.numpy(), rows.cpu().numpy())
+        np.testing.assert_allclose(outs["tma"], want, **BF16)
+
+
 @pytest.mark.parametrize("nk,rows", [(4097, [4096]), (1500, [700, 1200, 1499]), (513, [512])])
 def test_split_key_decode_matches_oracle_and_generic(cuda, nk, rows):
     """Decode rows through the paged cache: split-key kernel vs oracle and vs
