@@ -1,29 +1,33 @@
-// Tensor-core CoPE / CCPE prefill for sm_100a (tcgen05 + TMEM).
+// Tensor-core CoPE / CCPE prefill for sm_100a (tcgen05 + TMEM + TMA).
 //
 // One CTA computes a 128-row tile: R = 128 / G query rows x the G query heads
 // of one KV head (GQA packing: every row of the tile reads the same K/V).
-// Warp roles (288 threads):
-//   warps 0-3  softmax: thread r owns S row r (TMEM lane r).  For each key
-//              tile it reads S with tcgen05.ld in 32-column chunks, walks the
-//              columns from the newest key backwards with a thread-local
-//              running gate count (the reverse cumulative sum of
-//              position.py:295-307, restarted at chunk boundaries in the
-//              chunk-reset mode), interpolates the q.E bias from a per-row
-//              table in shared memory and applies the causal / association
-//              masks.  Scores go back to TMEM; a second pass forms
-//              P = 2^(s - m) (bf16) in shared memory and the row sums.  Once
-//              every row of a warp has a count >= npos-1 all older keys share
-//              one bias and only the logit and the exponential remain.
-//   warps 4-7  producer: Q tile, the E table split into bf16 hi + lo, and
-//              the K and V tiles of every key tile (two stages each), read
-//              through the per-key slot table (paged, relocated and dense keys
-//              alike) with 16-byte cp.async into the 128-byte swizzled UMMA
-//              layout.  Copy completion arrives on the stage barriers
-//              asynchronously (cp.async.mbarrier.arrive.noinc).
-//   warp 8     MMA issuer (one thread) and TMEM owner: T = Q E (hi + lo),
-//              S(t+1) = Q K^T while the softmax works on tile t, then
-//              O += P V; completions are tracked with tcgen05.commit.
-// TMEM (512 columns): S0 [0,128), S1 [128,256), O [256,384), T [384,448).
+// Warp roles (416 threads):
+//   warps 0-7   softmax, two threads per S row (TMEM lane r): warp q (0-3)
+//               takes the newer 64 keys of every key tile, warp q+4 the older
+//               64.  Per tile: gates sigmoid(q.k / sqrt(d)), the reverse
+//               cumulative count of position.py:295-307 (restarted at chunk
+//               boundaries in the chunk-reset mode; the older half scans with
+//               a zero start and adds the newer half's count afterwards), the
+//               q.E bias interpolated from a per-row table in shared memory,
+//               causal / association masks, the tile max, then
+//               P = 2^(s - m) packed to 16-bit pairs back into TMEM over the
+//               tile's own S columns.  Once every row of a warp has a count
+//               >= npos-1 all older keys share one bias: only logit, max and
+//               exponential remain (saturated tiles).
+//   warps 8-11  producer: Q tile, the E table split into bf16 hi + lo, the key
+//               metadata of every tile (fixed keys, chunk boundaries), and the
+//               K and V tiles (two stages each, K one tile ahead of V) read
+//               through the per-key slot table: TMA 64 x 16 tile loads for
+//               runs of 16 keys in consecutive rows, tile::gather4 for groups
+//               of 4 keys, cp.async for the rest, all into the 128-byte
+//               swizzled UMMA layout.
+//   warp 12     MMA issuer (one thread) and TMEM owner: T = Q E (hi + lo),
+//               S(t+1) = Q K^T while the softmax works on tile t, then
+//               O += P V with P read from TMEM; completions are tracked with
+//               tcgen05.commit.
+// TMEM (512 columns): S0 [0,128), S1 [128,256) (P over them), O [256,384),
+// T [384,448) at start, then the per-row counts of contextual tiles [384,512).
 // Every mbarrier wait is bounded; on expiry the CTA raises CS_ST_TIMEOUT,
 // drains its copies and MMAs, frees its TMEM and returns.
 #include <cuda.h>
@@ -52,7 +56,7 @@ constexpr uint32_t kK0 = 32768;    // 2 x 32 KB K tiles
 constexpr uint32_t kV0 = 98304;    // 2 x 32 KB V tiles
 constexpr uint32_t kP = 163840;    // 32 KB  P tile (E hi/lo staging at start)
 constexpr uint32_t kT = 196608;    // 32 KB  q.E table [128][64] fp32
-constexpr uint32_t kMeta = 229376; // barriers, flags, key metadata, row addresses
+constexpr uint32_t kMeta = 229376; // barriers, flags, key metadata, pair exchange
 
 // metadata block (offsets from kMeta)
 constexpr uint32_t kBarQ = 0;       // producer -> MMA: Q + E staged
@@ -60,7 +64,7 @@ constexpr uint32_t kBarT = 8;       // MMA -> softmax: T ready
 constexpr uint32_t kBarK = 16;      // [2] producer -> MMA: K tile
 constexpr uint32_t kBarV = 32;      // [2] producer -> MMA: V tile
 constexpr uint32_t kBarS = 48;      // [2] MMA -> softmax/producer: S tile ready
-constexpr uint32_t kBarP = 64;      // softmax -> MMA: P tile staged
+constexpr uint32_t kSpare64 = 64;   // unused
 constexpr uint32_t kBarPV = 72;     // [2] MMA -> all: PV tile done
 constexpr uint32_t kBarEnd = 88;    // MMA drain
 constexpr uint32_t kTmemSlot = 96;  // TMEM base address
@@ -70,13 +74,17 @@ constexpr uint32_t kNmax = 108;     // keys needed by the furthest row of this C
 constexpr uint32_t kFixMask = 112;  // [4 slots][4 words] key is fixed
 constexpr uint32_t kBndMask = 176;  // [4 slots][4 words] key is the last of its chunk
 constexpr uint32_t kBarMeta = 240;  // [4] producer -> softmax: key metadata of slot it % 4
-constexpr uint32_t kRowAddr = 272;  // [128] K row address of the current tile (bit 0: sidecar)
-constexpr uint32_t kXc = 1296;      // [128] float: newer half -> older half count, and back
-constexpr uint32_t kXm = 1808;      // [128] float: newer half's tile max / row sums
-constexpr uint32_t kXm2 = 2320;     // [128] float: older half's tile max
-constexpr uint32_t kBndKc = 2832;   // [4 slots][4 chunks] int: chunk id of the newest boundary
-constexpr uint32_t kMetaBytes = kBndKc + 16 * 4;
-constexpr uint32_t kSmemBytes = kMeta + kMetaBytes;  // 232,272 B (limit 232,448)
+constexpr uint32_t kXc = 272;       // [128] float: newer half -> older half count, and back
+constexpr uint32_t kXm = 784;       // [128] float: newer half's tile max / row sums
+constexpr uint32_t kXm2 = 1296;     // [128] float: older half's tile max
+constexpr uint32_t kBndKc = 1808;   // [4 slots][4 chunks] int: chunk id of the newest boundary
+// [2] softmax -> MMA: P of tile it in TMEM, barrier it % 2.  The four warp
+// pairs do not wait for one another, so one pair may finish tile it+1 before
+// another finishes tile it (never further: S(it+2) needs PV(it)); alternating
+// barriers keep those arrivals out of tile it's count.
+constexpr uint32_t kBarP = 1872;
+constexpr uint32_t kMetaBytes = kBarP + 16;
+constexpr uint32_t kSmemBytes = kMeta + kMetaBytes;  // 231,264 B (limit 232,448)
 
 // TMEM columns: S double buffer, O, the q.E table (read once into shared
 // memory) and, from then on, the per-row counts of a contextual tile (kColR
@@ -137,6 +145,16 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// A from TMEM (K-major, two 16-bit elements per 32-bit column), B from shared memory
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 __device__ __forceinline__ void fence_async_smem() {
@@ -245,6 +263,16 @@ __device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* map
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(bar)
       : "memory");
 }
+// 2-D tile load: rows y..y+15, 64 elements from column x, into 16 consecutive
+// 128-byte rows at dst
+__device__ __forceinline__ void tma_tile2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                           uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes)
                : "memory");
@@ -290,11 +318,12 @@ template <> struct Pack2<__half> {
 };
 
 struct Args {
-  // K/V row maps of the TMA path (2-D: row x element, 128-byte swizzle, box
-  // 64 x 1 for tile::gather4): [0] primary K, [1] primary V, [2] sidecar K,
-  // [3] sidecar V.  The primary maps are the paged cache (K and V in one row,
-  // V from element vx0) or the dense K and V tensors.
-  CUtensorMap tm[4];
+  // K/V row maps of the TMA path (2-D: row x element, 128-byte swizzle):
+  // [0] primary K, [1] primary V, [2] sidecar K, [3] sidecar V with 64 x 1
+  // boxes for tile::gather4, and [4..7] the same maps with 64 x 16 boxes for
+  // runs of 16 keys in consecutive rows.  The primary maps are the paged cache
+  // (K and V in one row, V from element vx0) or the dense K and V tensors.
+  CUtensorMap tm[8];
   cs_attn_params p;
   PagedView pv;
   int G, R, fmt;  // heads per KV head, rows per tile, 0 = f16 / 1 = bf16
@@ -386,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
       mbar_init(mb + kBarPV + 8 * s, 1);
     }
     for (int s = 0; s < 4; ++s) mbar_init(mb + kBarMeta + 8 * s, 128);
-    mbar_init(mb + kBarP, 256);  // both halves of every row
+    for (int s = 0; s < 2; ++s) mbar_init(mb + kBarP + 8 * s, 256);  // both halves of every row
     mbar_init(mb + kBarEnd, 1);
     *abort = 0;
     int64_t nmax = 0;  // keys needed by the furthest row of this tile
@@ -441,9 +470,9 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
     fence_async_smem();
     mbar_arrive(mb + kBarQ);
 
-    uint64_t* rowaddr = reinterpret_cast<uint64_t*>(meta + kRowAddr);
     const bool tma = a.tma != 0;
     const unsigned kAll = 0xffffffffu;
+    const int wrow0 = 32 * (warp - 8);  // first tile row (key) of this warp
     // source and metadata of key key0 + pt, read one tile ahead so that their
     // global loads overlap the stage waits
     uint64_t ka = 0;
@@ -463,15 +492,17 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
       kcj = in && p.pos_mode == CS_POS_CHUNK ? p.key_chunk[j] : -1;
       bnd = kcj >= 0 && (j + 1 < p.nk) && p.key_chunk[j + 1] != kcj;
     };
-    if (ntile > 0) load_key(0);
-    for (int it = 0; it < ntile; ++it) {
-      const int st = it & 1, slot = it & 3;
-      const int kt = ntile - 1 - it;
-      const int64_t key0 = (int64_t)kt * kTileN;
-      // K stage free once QK(it-2) completed, metadata slot it%4 then too; the
-      // barrier also means every producer thread finished the previous tile
-      bool ok = it < 2 || mbar_wait(mb + kBarS + 8 * st, ((it - 2) >> 1) & 1, abort);
-      if (!named_and(1, 128, ok)) break;
+    // what the V copy of a tile needs from its K step
+    struct VSrc {
+      uint64_t ka;
+      int64_t key0;
+      int rv, v1, v2, v3, grp, run;
+      uint32_t tx;
+    };
+    // publish the key metadata of tile it2 (slot it2 % 4) and start its K copy
+    auto issue_k = [&](int it2, VSrc& vs) {
+      const int st = it2 & 1, slot = it2 & 3;
+      const int64_t key0 = (int64_t)(ntile - 1 - it2) * kTileN;
       {
         const unsigned fm = __ballot_sync(kAll, fixed);
         const unsigned bm = __ballot_sync(kAll, bnd);
@@ -484,86 +515,133 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
         }
       }
       mbar_arrive(mb + kBarMeta + 8 * slot);  // metadata published (release)
-      const uint64_t cka = ka;  // this tile's source; the registers are reloaded below
-      const int64_t jr = key0 + pt < p.nk ? key0 + pt : p.nk - 1;
-      // TMA: a group of 4 keys (lanes 4q..4q+3) whose rows all live in the
-      // primary map (grp 1) or all in the sidecar (grp 2) is fetched with two
-      // tile::gather4 loads per operand (64 columns x 4 rows each), issued by
-      // the group's first lane; other groups copy their rows with cp.async
-      int grp = 0;
-      uint32_t tx = 0;
-      int k1 = 0, k2 = 0, k3 = 0, v1 = 0, v2 = 0, v3 = 0;
-      const int crk = rk, crv = rv;
+      vs.ka = ka;
+      vs.key0 = key0;
+      vs.rv = rv;
+      vs.grp = vs.run = 0;
+      vs.tx = 0;
       if (tma) {
-        const int cls = cka == 0 ? 0 : ((cka & 1ull) ? 2 : 1);
+        // 16 keys (a half warp) in consecutive rows of one map are one 64 x 16
+        // tile load per operand and 64-column half (run 1: primary map, 2:
+        // sidecar); otherwise a group of 4 keys (lanes 4q..4q+3) whose rows
+        // all live in one map (grp 1 / 2) takes tile::gather4 loads, issued by
+        // the group's first lane; other groups copy their own rows by cp.async
+        const int cls = ka == 0 ? 0 : ((ka & 1ull) ? 2 : 1);
+        const int h0 = lane & ~15;
+        const int c0 = __shfl_sync(kAll, cls, h0);
+        const int r0k = __shfl_sync(kAll, rk, h0), r0v = __shfl_sync(kAll, rv, h0);
+        const unsigned bseq = __ballot_sync(
+            kAll, cls != 0 && cls == c0 && rk == r0k + (lane & 15) && rv == r0v + (lane & 15));
+        vs.run = ((bseq >> h0) & 0xFFFFu) == 0xFFFFu ? c0 : 0;
         const unsigned b1 = __ballot_sync(kAll, cls == 1), b2 = __ballot_sync(kAll, cls == 2);
         const int sh = lane & ~3;
-        grp = ((b1 >> sh) & 0xFu) == 0xFu ? 1 : (((b2 >> sh) & 0xFu) == 0xFu ? 2 : 0);
-        tx = __popc(__ballot_sync(kAll, grp != 0 && (lane & 3) == 0)) * 1024u;
-        k1 = __shfl_down_sync(kAll, crk, 1);
-        k2 = __shfl_down_sync(kAll, crk, 2);
-        k3 = __shfl_down_sync(kAll, crk, 3);
-        v1 = __shfl_down_sync(kAll, crv, 1);
-        v2 = __shfl_down_sync(kAll, crv, 2);
-        v3 = __shfl_down_sync(kAll, crv, 3);
-        if (lane == 0 && tx) mbar_expect_tx(mb + kBarK + 8 * st, tx);
-        if (grp && (lane & 3) == 0) {
-          const CUtensorMap* m = grp == 1 ? &a.tm[0] : &a.tm[2];
+        vs.grp = vs.run ? 0
+                        : (((b1 >> sh) & 0xFu) == 0xFu ? 1 : (((b2 >> sh) & 0xFu) == 0xFu ? 2 : 0));
+        vs.tx = __popc(__ballot_sync(kAll, vs.run != 0 && (lane & 15) == 0)) * 4096u +
+                __popc(__ballot_sync(kAll, vs.grp != 0 && (lane & 3) == 0)) * 1024u;
+        const int k1 = __shfl_down_sync(kAll, rk, 1);
+        const int k2 = __shfl_down_sync(kAll, rk, 2);
+        const int k3 = __shfl_down_sync(kAll, rk, 3);
+        vs.v1 = __shfl_down_sync(kAll, rv, 1);
+        vs.v2 = __shfl_down_sync(kAll, rv, 2);
+        vs.v3 = __shfl_down_sync(kAll, rv, 3);
+        if (lane == 0 && vs.tx) mbar_expect_tx(mb + kBarK + 8 * st, vs.tx);
+        if (vs.run && (lane & 15) == 0) {
+          const CUtensorMap* m = vs.run == 1 ? &a.tm[4] : &a.tm[6];
           for (int cb = 0; cb < 2; ++cb)
-            tma_gather4(sbase + kK0 + st * 32768 + cb * 16384 + pt * 128, m, cb * 64, crk, k1, k2,
+            tma_tile2d(sbase + kK0 + st * 32768 + cb * 16384 + pt * 128, m, cb * 64, rk,
+                       mb + kBarK + 8 * st);
+        }
+        if (vs.grp && (lane & 3) == 0) {
+          const CUtensorMap* m = vs.grp == 1 ? &a.tm[0] : &a.tm[2];
+          for (int cb = 0; cb < 2; ++cb)
+            tma_gather4(sbase + kK0 + st * 32768 + cb * 16384 + pt * 128, m, cb * 64, rk, k1, k2,
                         k3, mb + kBarK + 8 * st);
         }
-        if (!grp) {
+        if (!vs.run && !vs.grp) {
           for (int c16 = 0; c16 < 16; ++c16) {
-            const char* src = cka ? reinterpret_cast<const char*>(cka & ~1ull) + c16 * 16
-                                  : static_cast<const char*>(p.q);
-            cp_async16(sbase + kK0 + st * 32768 + sw128(pt, c16, 128), src, cka != 0);
+            const char* src = ka ? reinterpret_cast<const char*>(ka & ~1ull) + c16 * 16
+                                 : static_cast<const char*>(p.q);
+            cp_async16(sbase + kK0 + st * 32768 + sw128(pt, c16, 128), src, ka != 0);
           }
         }
       } else {
-        rowaddr[pt] = cka;
-        named_sync(1, 128);  // every row address visible
-        const int c16 = pt & 15;
+        // per-row cp.async: each warp copies its own 32 rows, two 256-byte
+        // rows per instruction (row addresses from the owning lanes)
+        const int c16 = lane & 15;
 #pragma unroll 4
         for (int m = 0; m < 16; ++m) {
-          const int row = (pt >> 4) + 8 * m;
-          const uint64_t ra = rowaddr[row];
+          const int src_lane = (lane >> 4) + 2 * m;
+          const uint64_t ra = __shfl_sync(kAll, ka, src_lane);
           const char* src = ra ? reinterpret_cast<const char*>(ra & ~1ull) + c16 * 16
                                : static_cast<const char*>(p.q);
-          cp_async16(sbase + kK0 + st * 32768 + sw128(row, c16, 128), src, ra != 0);
+          cp_async16(sbase + kK0 + st * 32768 + sw128(wrow0 + src_lane, c16, 128), src, ra != 0);
         }
       }
       cp_async_arrive_noinc(mb + kBarK + 8 * st);
-      if (it + 1 < ntile) load_key(it + 1);
-      // V stage free once PV(it-2) completed
-      ok = it < 2 || mbar_wait(mb + kBarPV + 8 * st, ((it - 2) >> 1) & 1, abort);
-      if (!named_and(1, 128, ok)) break;
+    };
+    auto issue_v = [&](int it2, const VSrc& vs) {
+      const int st = it2 & 1;
       if (tma) {
-        if (lane == 0 && tx) mbar_expect_tx(mb + kBarV + 8 * st, tx);
-        if (grp && (lane & 3) == 0) {
-          const CUtensorMap* m = grp == 1 ? &a.tm[1] : &a.tm[3];
-          const int x0 = grp == 1 ? a.vx0 : 0;
+        if (lane == 0 && vs.tx) mbar_expect_tx(mb + kBarV + 8 * st, vs.tx);
+        if (vs.run && (lane & 15) == 0) {
+          const CUtensorMap* m = vs.run == 1 ? &a.tm[5] : &a.tm[7];
+          const int x0 = vs.run == 1 ? a.vx0 : 0;
           for (int cb = 0; cb < 2; ++cb)
-            tma_gather4(sbase + kV0 + st * 32768 + cb * 16384 + pt * 128, m, x0 + cb * 64, crv,
-                        v1, v2, v3, mb + kBarV + 8 * st);
+            tma_tile2d(sbase + kV0 + st * 32768 + cb * 16384 + pt * 128, m, x0 + cb * 64, vs.rv,
+                       mb + kBarV + 8 * st);
         }
-        if (!grp) {
-          const char* vrow = cka ? value_row_addr<T>(a, cka, jr, g) : static_cast<const char*>(p.q);
+        if (vs.grp && (lane & 3) == 0) {
+          const CUtensorMap* m = vs.grp == 1 ? &a.tm[1] : &a.tm[3];
+          const int x0 = vs.grp == 1 ? a.vx0 : 0;
+          for (int cb = 0; cb < 2; ++cb)
+            tma_gather4(sbase + kV0 + st * 32768 + cb * 16384 + pt * 128, m, x0 + cb * 64, vs.rv,
+                        vs.v1, vs.v2, vs.v3, mb + kBarV + 8 * st);
+        }
+        if (!vs.run && !vs.grp) {
+          const int64_t jr = vs.key0 + pt < p.nk ? vs.key0 + pt : p.nk - 1;
+          const char* vrow =
+              vs.ka ? value_row_addr<T>(a, vs.ka, jr, g) : static_cast<const char*>(p.q);
           for (int c16 = 0; c16 < 16; ++c16)
-            cp_async16(sbase + kV0 + st * 32768 + sw128(pt, c16, 128), vrow + c16 * 16, cka != 0);
+            cp_async16(sbase + kV0 + st * 32768 + sw128(pt, c16, 128), vrow + c16 * 16,
+                       vs.ka != 0);
         }
       } else {
-        const int c16 = pt & 15;
+        const int c16 = lane & 15;
 #pragma unroll 4
         for (int m = 0; m < 16; ++m) {
-          const int row = (pt >> 4) + 8 * m;
-          const uint64_t ra = rowaddr[row];
-          const char* src = ra ? value_row_addr<T>(a, ra, key0 + row, g) + c16 * 16
+          const int src_lane = (lane >> 4) + 2 * m;
+          const uint64_t ra = __shfl_sync(kAll, vs.ka, src_lane);
+          const int row = wrow0 + src_lane;
+          const char* src = ra ? value_row_addr<T>(a, ra, vs.key0 + row, g) + c16 * 16
                                : static_cast<const char*>(p.q);
           cp_async16(sbase + kV0 + st * 32768 + sw128(row, c16, 128), src, ra != 0);
         }
       }
       cp_async_arrive_noinc(mb + kBarV + 8 * st);
+    };
+    // K runs one tile ahead of V: K(it+1) needs only QK(it-1) to be done,
+    // V(it) needs PV(it-2)
+    VSrc vcur{}, vnext{};
+    if (ntile > 0) {
+      load_key(0);
+      issue_k(0, vcur);
+      if (ntile > 1) load_key(1);
+    }
+    for (int it = 0; it < ntile; ++it) {
+      if (it + 1 < ntile) {
+        // K stage (it+1)&1 and metadata slot (it+1)%4 are free once QK(it-1)
+        // completed; the barrier also keeps the producer warps in step
+        bool ok = it < 1 || mbar_wait(mb + kBarS + 8 * ((it + 1) & 1), ((it - 1) >> 1) & 1, abort);
+        if (!named_and(1, 128, ok)) break;
+        issue_k(it + 1, vnext);
+        if (it + 2 < ntile) load_key(it + 2);
+      }
+      // V stage it&1 free once PV(it-2) completed
+      bool ok = it < 2 || mbar_wait(mb + kBarPV + 8 * (it & 1), ((it - 2) >> 1) & 1, abort);
+      if (!named_and(1, 128, ok)) break;
+      issue_v(it, vcur);
+      vcur = vnext;
     }
     if (slot_bad) report(p.status, CS_ST_SLOT_RANGE);
     cp_async_wait_all();
@@ -608,20 +686,26 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
         if (it + 1 < ntile) {
           if (!(ok = mbar_wait(mb + kBarK + 8 * ((it + 1) & 1), ((it + 1) >> 1) & 1, abort)))
             break;
+          // S(it+1) overwrites the TMEM columns where P(it-1) lives: PV(it-1)
+          // (another accumulator, so not ordered with this MMA) must be done
+          if (it >= 1 &&
+              !(ok = mbar_wait(mb + kBarPV + 8 * ((it - 1) & 1), ((it - 1) >> 1) & 1, abort)))
+            break;
           fence_async_smem();
           tc_fence_after();
           issue_qk(it + 1);
         }
-        if (!(ok = mbar_wait(mb + kBarP, it & 1, abort))) break;
+        if (!(ok = mbar_wait(mb + kBarP + 8 * (it & 1), (it >> 1) & 1, abort))) break;
         if (!(ok = mbar_wait(mb + kBarV + 8 * st, (it >> 1) & 1, abort))) break;
         fence_async_smem();
         tc_fence_after();
         for (int kk = 0; kk < kTileN / 16; ++kk) {
-          const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;  // P: K-major
-          const uint32_t boff = kk * 2048;                           // V: MN-major
-          tc_mma(tmem + kColO, umma_desc(sbase + kP + aoff, 16, 1024),
-                 umma_desc(sbase + kV0 + st * 32768 + boff, 16384, 1024), id_o,
-                 (it | kk) ? 1u : 0u);
+          // P of keys 16kk..16kk+15 (packed pairs, over the S columns of tile it)
+          const uint32_t pcol = kColS0 + st * 128 + (kk < 4 ? kk * 8 : 64 + (kk - 4) * 8);
+          const uint32_t boff = kk * 2048;  // V: MN-major
+          tc_mma_ts(tmem + kColO, tmem + pcol,
+                    umma_desc(sbase + kV0 + st * 32768 + boff, 16384, 1024), id_o,
+                    (it | kk) ? 1u : 0u);
         }
         tc_commit(mb + kBarPV + 8 * st);
       }
@@ -655,7 +739,7 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
         (row_ok && chunked) ? p.chunk_off + (int64_t)h * p.co_stride_h + i * p.co_stride_q
                             : nullptr;
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
-    float* Ts = reinterpret_cast<float*>(smem + kT) + r * kMaxNpos;
+    float* Ts = reinterpret_cast<float*>(smem + kT) + r * kMaxNpos;  // q.E * log2(e), XOR-swizzled
     float* xc = reinterpret_cast<float*>(meta + kXc);
     float* xm = reinterpret_cast<float*>(meta + kXm);
     const int sw = r & 31;
@@ -672,11 +756,10 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
       CS_TMEM_LD32(tmem + lane_base + kColT + hf * 32, v);
       tmem_wait_ld();
 #pragma unroll
-      for (int c = 0; c < 32; ++c) Ts[(hf * 32 + c) ^ sw] = __uint_as_float(v[c]);
+      for (int c = 0; c < 32; ++c) Ts[(hf * 32 + c) ^ sw] = __uint_as_float(v[c]) * LOG2E;
     }
     ok = named_and(pair, 64, ok);  // both halves of the q.E table written
-    const float tsat = Ts[(p.npos - 1) ^ sw];
-    const float tsat2 = tsat * LOG2E;
+    const float tsat2 = Ts[(p.npos - 1) ^ sw];  // saturated bias (log2 domain)
 
     float carry = 0.f;       // running count entering the newer edge of the tile
     float mref = -INFINITY;  // softmax reference max (log2 domain)
@@ -692,12 +775,11 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
       const int st = it & 1, slot = it & 3;
       const int kt = ntile - 1 - it;
       const int64_t key0 = (int64_t)kt * kTileN;
-      // S(it) from the MMA warp; the metadata barrier of slot it % 4 cannot run
-      // ahead of this wait (slot reuse needs P(it) from these warps)
-      ok = mbar_wait(mb + kBarS + 8 * st, (it >> 1) & 1, abort) &&
-           mbar_wait(mb + kBarMeta + 8 * slot, (it >> 2) & 1, abort);
-      if (!(ok = named_and(pair, 64, ok))) break;
-      tc_fence_after();
+      // key metadata of slot it % 4: the producer publishes it ahead of S(it),
+      // and the slot is not reused before P(it) from these warps.  Masks,
+      // chunk restarts and the fast / contextual decision are settled here,
+      // while QK(it) may still be running, so their latency hides behind it.
+      ok = mbar_wait(mb + kBarMeta + 8 * slot, (it >> 2) & 1, abort);
       const unsigned* fixm = reinterpret_cast<const unsigned*>(meta + kFixMask) + slot * 4;
       const unsigned* bndm = reinterpret_cast<const unsigned*>(meta + kBndMask) + slot * 4;
       const int* bndkc = bndkc_all + slot * 4;
@@ -724,7 +806,8 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
       // producer publishes its chunk id); other boundaries are looked up
       // where they are met
       float roff0 = -1.f, roff1 = -1.f, roff2 = -1.f, roff3 = -1.f;
-      if (chunked) {
+      const bool anyb = chunked && ok && (bndm[0] | bndm[1] | bndm[2] | bndm[3]) != 0u;
+      if (anyb) {
         const int k0 = bndkc[0], k1 = bndkc[1], k2 = bndkc[2], k3 = bndkc[3];
         if (k0 >= 0 && k0 < qchunk) roff0 = offrow[k0];
         if (k1 >= 0 && k1 < qchunk) roff1 = offrow[k1];
@@ -737,7 +820,7 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
       // the row is saturated for this tile when its count is already >= npos-1
       // and no live chunk boundary of the tile restarts it below that value
       bool sat = carry >= top;
-      if (chunked && sat) {
+      if (anyb && sat) {
 #pragma unroll 1
         for (int cc = 0; cc < 4 && sat; ++cc) {
           const unsigned bd = bndm[cc];
@@ -754,6 +837,10 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
       }
       // same rows in both warps of the pair, so both take the same path
       const bool fast = __all_sync(0xffffffffu, sat || nvalid == 0);
+      // S(it) from the MMA warp
+      ok = ok && mbar_wait(mb + kBarS + 8 * st, (it >> 1) & 1, abort);
+      if (!(ok = named_and(pair, 64, ok))) break;
+      tc_fence_after();
       float tmax;
       if (fast) {
         // saturated: every visible score is S * scale2 + tsat2, a monotone map
@@ -806,10 +893,8 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
           CS_TMEM_LD32(tmem + lane_base + kColS0 + st * 128 + cc * 32, v);
           tmem_wait_ld();
 #pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const float L = __uint_as_float(v[c]) * inv_sqrt_d;
-            v[c] = __float_as_uint(__fdividef(1.f, 1.f + ex2(-L * LOG2E)));
-          }
+          for (int c = 0; c < 32; ++c)  // gate = 1 / (1 + 2^(-S * scale2))
+            v[c] = __float_as_uint(__fdividef(1.f, 1.f + ex2(__uint_as_float(v[c]) * -scale2)));
           const int lim = nvalid - cc * 32;
           const unsigned bd = bndm[cc];
           const int cf = bd ? 31 - __clz(bd) : -1;
@@ -840,35 +925,48 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
           named_sync(pair + 4, 64);
           cin = xc[r];
         }
-        // phase B: positions, interpolated bias, masks; scores back into S
-        float tm = -INFINITY;
+        // phase B: positions, interpolated bias, masks; scores (log2 domain)
+        // back into S
+        float t0 = -INFINITY, t1 = -INFINITY, t2 = -INFINITY, t3 = -INFINITY;
 #pragma unroll 1
         for (int k = 0; k < 4; ++k) {  // 16-column pieces
           const int col0 = (cc_hi - (k >> 1)) * 32 + (k & 1) * 16;
-          const unsigned hm = ((k >> 1) ? hide1 : hide0) >> ((k & 1) * 16);
-          const int dep = rst - col0;  // columns above dep add cin
+          const unsigned hm = (((k >> 1) ? hide1 : hide0) >> ((k & 1) * 16)) & 0xFFFFu;
           uint32_t v[16], w[16];
           CS_TMEM_LD16(tmem + lane_base + kColS0 + st * 128 + col0, v);
           CS_TMEM_LD16(tmem + lane_base + kColR + col0, w);
           tmem_wait_ld();
+          if (hf) {  // older half: columns above the newest restart add cin
+            const int dep = rst - col0;
+#pragma unroll
+            for (int c = 0; c < 16; ++c)
+              w[c] = __float_as_uint(__uint_as_float(w[c]) + (c > dep ? cin : 0.f));
+          }
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
-            const float Rv = __uint_as_float(w[c]) + (c > dep ? cin : 0.f);
-            const float pos = fminf(Rv, top);
+            const float pos = fminf(__uint_as_float(w[c]), top);
             int lo;
             const float fl = floor_pos(pos, lo);
             const int hi = lo < hi_max ? lo + 1 : hi_max;
             const float tlo = Ts[lo ^ sw];
-            const float bias = fmaf(pos - fl, Ts[hi ^ sw] - tlo, tlo);
-            const float L = __uint_as_float(v[c]) * inv_sqrt_d;
-            float s = (L + bias) * LOG2E;
-            s = (hm >> c) & 1u ? -INFINITY : s;
-            tm = fmaxf(tm, s);
-            v[c] = __float_as_uint(s);
+            const float bias2 = fmaf(pos - fl, Ts[hi ^ sw] - tlo, tlo);
+            v[c] = __float_as_uint(fmaf(__uint_as_float(v[c]), scale2, bias2));
+          }
+          if (hm) {
+#pragma unroll
+            for (int c = 0; c < 16; ++c) v[c] = (hm >> c) & 1u ? __float_as_uint(-INFINITY) : v[c];
+          }
+#pragma unroll
+          for (int c = 0; c < 16; c += 4) {
+            t0 = fmaxf(t0, __uint_as_float(v[c]));
+            t1 = fmaxf(t1, __uint_as_float(v[c + 1]));
+            t2 = fmaxf(t2, __uint_as_float(v[c + 2]));
+            t3 = fmaxf(t3, __uint_as_float(v[c + 3]));
           }
           CS_TMEM_ST16(tmem + lane_base + kColS0 + st * 128 + col0, v);
         }
         tmem_wait_st();
+        const float tm = fmaxf(fmaxf(t0, t1), fmaxf(t2, t3));
         // tile max of both halves, and the count leaving the tile (older half)
         (hf ? xm2 : xm)[r] = tm;
         if (hf) xc[r] = Rc + (rst < 0 ? cin : 0.f);
@@ -876,19 +974,18 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
         tmax = fmaxf(xm[r], xm2[r]);
         carry = xc[r];
       }
-      // PV of the previous tile must finish before O and P are touched
-      if (it > 0) {
-        ok = mbar_wait(mb + kBarPV + 8 * ((it - 1) & 1), ((it - 1) >> 1) & 1, abort);
-        if (!(ok = named_and(pair, 64, ok))) break;
-        tc_fence_after();
-      }
       float mnew = mref;
       bool rescale = false;
       if (tmax > mref + 8.f) {  // lazy rescaling: keep a stale max unless it lags by 2^8
         mnew = tmax;
         rescale = mref > -INFINITY;
       }
+      // both warps of a pair hold the same rows and maxima, so they agree on
+      // whether O is rescaled; only then must PV of the previous tile be done
       if (it > 0 && __any_sync(0xffffffffu, rescale)) {
+        ok = mbar_wait(mb + kBarPV + 8 * ((it - 1) & 1), ((it - 1) >> 1) & 1, abort);
+        if (!(ok = named_and(pair, 64, ok))) break;
+        tc_fence_after();
         const float f = rescale ? ex2(mref - mnew) : 1.f;
         lsum *= f;
         for (int k = 0; k < 2; ++k) {  // this half rescales 64 of the 128 O columns
@@ -903,15 +1000,18 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
         tmem_wait_st();
       }
       mref = mnew;
-      // P = 2^(s - mref) (bf16/f16) into this half's columns of row r; a
-      // saturated tile forms s - mref = S * scale2 + (tsat2 - mref) directly
+      // P = 2^(s - mref) as packed 16-bit pairs over this half's own S
+      // columns (keys 0-63 -> columns 0-31, keys 64-127 -> columns 64-95),
+      // chunks in increasing order so no S value is overwritten before it is
+      // read; PV takes P from TMEM.  A saturated tile forms s - mref =
+      // S * scale2 + (tsat2 - mref) directly.
       const float mcur = mref > -INFINITY ? mref : 0.f;
       const float fb = tsat2 - mcur;
       float part0 = 0.f, part1 = 0.f;
 #pragma unroll 1
       for (int k = 0; k < 2; ++k) {
-        const int cc = cc_hi - k;
-        const unsigned hm = k ? hide1 : hide0;
+        const int cc = (hf ? 0 : 2) + k;
+        const unsigned hm = (cc & 1) ? hide0 : hide1;
         uint32_t v[32];
         if (fast && __all_sync(0xffffffffu, hm == ~0u)) {
 #pragma unroll
@@ -932,25 +1032,21 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
             for (int c = 0; c < 32; ++c) v[c] = __float_as_uint(ex2(__uint_as_float(v[c]) - mcur));
           }
         }
+        uint32_t w[16];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint32_t w[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const float e0 = __uint_as_float(v[q * 8 + 2 * u]);
-            const float e1 = __uint_as_float(v[q * 8 + 2 * u + 1]);
-            part0 += e0;
-            part1 += e1;
-            w[u] = Pack2<T>::pack(e0, e1);
-          }
-          *reinterpret_cast<uint4*>(smem + kP + sw128(r, cc * 4 + q, 128)) =
-              make_uint4(w[0], w[1], w[2], w[3]);
+        for (int u = 0; u < 16; ++u) {
+          const float e0 = __uint_as_float(v[2 * u]);
+          const float e1 = __uint_as_float(v[2 * u + 1]);
+          part0 += e0;
+          part1 += e1;
+          w[u] = Pack2<T>::pack(e0, e1);
         }
+        CS_TMEM_ST16(tmem + lane_base + kColS0 + st * 128 + (cc < 2 ? cc * 16 : 64 + (cc - 2) * 16), w);
       }
       lsum += part0 + part1;
-      fence_async_smem();
+      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(mb + kBarP);
+      mbar_arrive(mb + kBarP + 8 * st);
     }
     // epilogue: O / l, each half writes 64 of the 128 output columns
     if (ok && ntile > 0) {
@@ -1049,15 +1145,15 @@ bool prefill_supported(const cs_attn_params* p) {
 }
 
 // 2-D row map over `rows` rows of `inner` 16-bit elements, `unit` bytes apart,
-// read in 64 x 1 boxes with the 128-byte swizzle of the UMMA operand tiles
+// read in 64 x box_rows boxes with the 128-byte swizzle of the UMMA operand tiles
 bool encode_rows(CUtensorMap* m, const void* base, bool bf16, int64_t inner, int64_t rows,
-                 int64_t unit) {
+                 int64_t unit, uint32_t box_rows) {
   if (base == nullptr || reinterpret_cast<uintptr_t>(base) % 16 || unit % 16 ||
       unit < inner * 2 || rows < 1 || rows > INT32_MAX || inner < 128)
     return false;
   const cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)unit};
-  const cuuint32_t box[2] = {64, 1}, es[2] = {1, 1};
+  const cuuint32_t box[2] = {64, box_rows}, es[2] = {1, 1};
   return cuTensorMapEncodeTiled(m,
                                 bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
@@ -1075,6 +1171,11 @@ bool setup_tma(Args& a) {
   const cs_attn_params& p = a.p;
   const bool bf16 = p.in_dtype == CS_BF16;
   const int64_t es = 2;
+  // map i with 64 x 1 boxes (gather4) and map i + 4 with 64 x 16 boxes (runs)
+  auto encode = [&](int i, const void* base, int64_t inner, int64_t rows, int64_t unit) {
+    return encode_rows(&a.tm[i], base, bf16, inner, rows, unit, 1) &&
+           encode_rows(&a.tm[i + 4], base, bf16, inner, rows, unit, 16);
+  };
   auto gcd3 = [](int64_t x, int64_t y, int64_t z) { return std::gcd(std::gcd(x, y), z); };
   if (p.kv_slots) {
     const PagedView& pv = a.pv;
@@ -1084,8 +1185,9 @@ bool setup_tma(Args& a) {
     const int64_t nb = pv.native_total / pv.bs;
     const int64_t rows = ((nb - 1) * pv.sb + (pv.kv_heads - 1) * pv.sh + (pv.bs - 1) * pv.so) /
                              unit + 1;
-    if (!encode_rows(&a.tm[0], pv.cache, bf16, 2 * pv.head_dim, rows, unit)) return false;
+    if (!encode(0, pv.cache, 2 * pv.head_dim, rows, unit)) return false;
     a.tm[1] = a.tm[0];
+    a.tm[5] = a.tm[4];
     a.vx0 = (int)pv.head_dim;
     a.nrb = pv.sb / unit;
     a.nrh = pv.sh / unit;
@@ -1095,13 +1197,14 @@ bool setup_tma(Args& a) {
       const int64_t su = std::gcd(pv.ssr, pv.ssh);
       if (su <= 0) return false;
       const int64_t srows = ((pv.side_capacity - 1) * pv.ssr + (pv.kv_heads - 1) * pv.ssh) / su + 1;
-      if (!encode_rows(&a.tm[2], pv.side_k, bf16, pv.head_dim, srows, su) ||
-          !encode_rows(&a.tm[3], pv.side_v, bf16, pv.head_dim, srows, su))
+      if (!encode(2, pv.side_k, pv.head_dim, srows, su) ||
+          !encode(3, pv.side_v, pv.head_dim, srows, su))
         return false;
       a.srr = pv.ssr / su;
       a.srh = pv.ssh / su;
-    } else {
-      a.tm[2] = a.tm[3] = a.tm[0];  // never addressed: no slot reaches the sidecar
+    } else {  // never addressed: no slot reaches the sidecar
+      a.tm[2] = a.tm[3] = a.tm[0];
+      a.tm[6] = a.tm[7] = a.tm[4];
     }
     return true;
   }
@@ -1112,11 +1215,11 @@ bool setup_tma(Args& a) {
   if (ku <= 0 || vu <= 0) return false;
   const int64_t krows = ((int64_t)(p.nk - 1) * kt + (int64_t)(p.hkv - 1) * kh) / ku + 1;
   const int64_t vrows = ((int64_t)(p.nk - 1) * vt + (int64_t)(p.hkv - 1) * vh) / vu + 1;
-  if (!encode_rows(&a.tm[0], p.k, bf16, p.d, krows, ku) ||
-      !encode_rows(&a.tm[1], p.v, bf16, p.dv, vrows, vu))
-    return false;
+  if (!encode(0, p.k, p.d, krows, ku) || !encode(1, p.v, p.dv, vrows, vu)) return false;
   a.tm[2] = a.tm[0];
   a.tm[3] = a.tm[1];
+  a.tm[6] = a.tm[4];
+  a.tm[7] = a.tm[5];
   a.vx0 = 0;
   a.krt = kt / ku;
   a.krh = kh / ku;
