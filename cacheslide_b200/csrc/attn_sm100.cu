@@ -54,8 +54,8 @@ constexpr int kMaxNpos = 64;
 constexpr uint32_t kQ = 0;         // 32 KB  Q tile   [2 cb][128 rows][128 B]
 constexpr uint32_t kK0 = 32768;    // 2 x 32 KB K tiles
 constexpr uint32_t kV0 = 98304;    // 2 x 32 KB V tiles
-constexpr uint32_t kP = 163840;    // 32 KB  P tile (E hi/lo staging at start)
-constexpr uint32_t kT = 196608;    // 32 KB  q.E table [128][64] fp32
+constexpr uint32_t kP = 163840;    // 32 KB  E hi/lo staging for T = Q E at start
+constexpr uint32_t kTab = 163840;  // 64 KB  q.E table [128 rows][64] float2, after T is built
 constexpr uint32_t kMeta = 229376; // barriers, flags, key metadata, pair exchange
 
 // metadata block (offsets from kMeta)
@@ -64,7 +64,7 @@ constexpr uint32_t kBarT = 8;       // MMA -> softmax: T ready
 constexpr uint32_t kBarK = 16;      // [2] producer -> MMA: K tile
 constexpr uint32_t kBarV = 32;      // [2] producer -> MMA: V tile
 constexpr uint32_t kBarS = 48;      // [2] MMA -> softmax/producer: S tile ready
-constexpr uint32_t kSpare64 = 64;   // unused
+// offset 64: unused
 constexpr uint32_t kBarPV = 72;     // [2] MMA -> all: PV tile done
 constexpr uint32_t kBarEnd = 88;    // MMA drain
 constexpr uint32_t kTmemSlot = 96;  // TMEM base address
@@ -171,6 +171,9 @@ __device__ __forceinline__ void fence_async_smem() {
         "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),           \
         "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])            \
       : "r"(taddr))
+
+#define CS_TMEM_LD1(taddr, r)                                                                    \
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r[0]) : "r"(taddr))
 
 #define CS_TMEM_LD16(taddr, r)                                                                   \
   asm volatile(                                                                                  \
@@ -739,27 +742,37 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
         (row_ok && chunked) ? p.chunk_off + (int64_t)h * p.co_stride_h + i * p.co_stride_q
                             : nullptr;
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
-    float* Ts = reinterpret_cast<float*>(smem + kT) + r * kMaxNpos;  // q.E * log2(e), XOR-swizzled
+    // q.E table of row r: entry p = (T[p], T[p+1] - T[p]) in the log2 domain
+    // (T[npos] := T[npos-1]), at float2 index p ^ (r & 15) so that the 16
+    // rows of a half warp reading the same entry hit distinct banks
+    float2* Tab = reinterpret_cast<float2*>(smem + kTab) + r * kMaxNpos;
+    const int tsw = r & 15;
     float* xc = reinterpret_cast<float*>(meta + kXc);
     float* xm = reinterpret_cast<float*>(meta + kXm);
-    const int sw = r & 31;
     const float inv_sqrt_d = (float)(1.0 / p.scale);
     const float LOG2E = 1.4426950408889634f;
     const float scale2 = inv_sqrt_d * LOG2E;
-    const int hi_max = p.npos - 1;
     const int cc_hi = hf ? 1 : 3;  // this half's 32-column chunks: cc_hi, cc_hi - 1
 
     bool ok = mbar_wait(mb + kBarT, 0, abort);
     tc_fence_after();
     {
-      uint32_t v[32];
+      // this half builds entries hf*32 .. hf*32+31 (the newer half also
+      // needs T[32]); the E staging below the table is no longer read
+      uint32_t v[32], nx[1] = {0u};
       CS_TMEM_LD32(tmem + lane_base + kColT + hf * 32, v);
+      if (hf == 0) CS_TMEM_LD1(tmem + lane_base + kColT + 32, nx);
       tmem_wait_ld();
 #pragma unroll
-      for (int c = 0; c < 32; ++c) Ts[(hf * 32 + c) ^ sw] = __uint_as_float(v[c]) * LOG2E;
+      for (int c = 0; c < 32; ++c) {
+        const int pp = hf * 32 + c;
+        const float t0 = __uint_as_float(v[c]) * LOG2E;
+        const float tn = __uint_as_float(c < 31 ? v[c + 1] : (hf == 0 ? nx[0] : v[31])) * LOG2E;
+        Tab[pp ^ tsw] = make_float2(t0, pp + 1 < p.npos ? tn - t0 : 0.f);
+      }
     }
     ok = named_and(pair, 64, ok);  // both halves of the q.E table written
-    const float tsat2 = Ts[(p.npos - 1) ^ sw];  // saturated bias (log2 domain)
+    const float tsat2 = Tab[(p.npos - 1) ^ tsw].x;  // saturated bias (log2 domain)
 
     float carry = 0.f;       // running count entering the newer edge of the tile
     float mref = -INFINITY;  // softmax reference max (log2 domain)
@@ -947,9 +960,8 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
             const float pos = fminf(__uint_as_float(w[c]), top);
             int lo;
             const float fl = floor_pos(pos, lo);
-            const int hi = lo < hi_max ? lo + 1 : hi_max;
-            const float tlo = Ts[lo ^ sw];
-            const float bias2 = fmaf(pos - fl, Ts[hi ^ sw] - tlo, tlo);
+            const float2 tv = Tab[lo ^ tsw];
+            const float bias2 = fmaf(pos - fl, tv.y, tv.x);
             v[c] = __float_as_uint(fmaf(__uint_as_float(v[c]), scale2, bias2));
           }
           if (hm) {
