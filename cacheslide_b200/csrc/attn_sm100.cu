@@ -248,6 +248,12 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
 }
@@ -907,23 +913,35 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
           tmem_wait_ld();
 #pragma unroll
           for (int c = 0; c < 32; ++c)  // gate = 1 / (1 + 2^(-S * scale2))
-            v[c] = __float_as_uint(__fdividef(1.f, 1.f + ex2(__uint_as_float(v[c]) * -scale2)));
+            v[c] = __float_as_uint(rcp_approx(1.f + ex2(__uint_as_float(v[c]) * -scale2)));
           const int lim = nvalid - cc * 32;
           const unsigned bd = bndm[cc];
-          const int cf = bd ? 31 - __clz(bd) : -1;
-          const float rf = roff_of(cc);
+          if (bd == 0u) {  // warp-uniform: no chunk boundary, a plain suffix sum
+            if (lim < 32) {
 #pragma unroll
-          for (int c = 31; c >= 0; --c) {
-            float base = Rc;
-            if ((bd >> c) & 1u) {  // warp-uniform: last key of a chunk
-              const float off = c == cf ? rf : restart_at(key0 + cc * 32 + c);
-              if (off >= 0.f) {
-                base = off;
-                if (c < lim && rst < 0) rst = cc * 32 + c;
-              }
+              for (int c = 0; c < 32; ++c) v[c] = c < lim ? v[c] : 0u;  // +0: not counted
             }
-            Rc = c < lim ? base + __uint_as_float(v[c]) : Rc;
-            v[c] = __float_as_uint(Rc);
+#pragma unroll
+            for (int c = 31; c >= 0; --c) {
+              Rc += __uint_as_float(v[c]);
+              v[c] = __float_as_uint(Rc);
+            }
+          } else {
+            const int cf = 31 - __clz(bd);
+            const float rf = roff_of(cc);
+#pragma unroll
+            for (int c = 31; c >= 0; --c) {
+              float base = Rc;
+              if ((bd >> c) & 1u) {  // warp-uniform: last key of a chunk
+                const float off = c == cf ? rf : restart_at(key0 + cc * 32 + c);
+                if (off >= 0.f) {
+                  base = off;
+                  if (c < lim && rst < 0) rst = cc * 32 + c;
+                }
+              }
+              Rc = c < lim ? base + __uint_as_float(v[c]) : Rc;
+              v[c] = __float_as_uint(Rc);
+            }
           }
           CS_TMEM_ST32(tmem + lane_base + kColR + cc * 32, v);
         }
