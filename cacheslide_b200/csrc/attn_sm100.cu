@@ -407,9 +407,10 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
   volatile int* abort = reinterpret_cast<volatile int*>(meta + kAbort);
   const uint32_t mb = sbase + kMeta;
 
-  // tile coordinates: heavy (late) query tiles first
-  const int g = blockIdx.x / a.tiles_per_head;
-  const int tile = a.tiles_per_head - 1 - (blockIdx.x % a.tiles_per_head);
+  // tile coordinates: the heaviest (latest) query tiles of all KV heads are
+  // launched first, so the light tiles fill the tail of the grid
+  const int g = blockIdx.x % a.p.hkv;
+  const int tile = a.tiles_per_head - 1 - blockIdx.x / a.p.hkv;
   const int64_t i0 = (int64_t)tile * a.R;
   const int G = a.G, R = a.R;
   const float top = (float)(p.npos - 1);
