@@ -5,6 +5,9 @@
 // All reductions accumulate in float64 like the reference (wca.py:55-112).
 // Each token row is owned by one warp; rows are [heads, dim] with arbitrary
 // row/head strides and a contiguous innermost dimension.
+#include <initializer_list>
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace cs {
@@ -174,6 +177,62 @@ __device__ int64_t block_select_topk(const double* __restrict__ keys, Avail avai
   return k;
 }
 
+// Top-k by a block-wide bitonic sort in shared memory (n <= kSortMax): every
+// token gets the order code of its key (0 when unavailable) and its index;
+// sorting by (code descending, index ascending) gives the stable descending
+// order of wca.py:282-285 directly, so the first `want` entries are the picks
+// in rank order.  `dyn` holds kSortMax codes and kSortMax indices.
+constexpr int kSortMax = 16384;
+
+template <typename Avail>
+__device__ int64_t block_sort_topk(const double* __restrict__ keys, Avail avail, int64_t n,
+                                   int64_t slots, uint8_t* __restrict__ selected,
+                                   int64_t* __restrict__ chosen_out, SelectSmem& sm,
+                                   unsigned char* dyn) {
+  uint64_t* code = reinterpret_cast<uint64_t*>(dyn);
+  uint32_t* idx = reinterpret_cast<uint32_t*>(dyn + sizeof(uint64_t) * kSortMax);
+  const int tid = threadIdx.x;
+  int m = 1;
+  while (m < n) m <<= 1;
+  int local = 0;
+  for (int i = tid; i < m; i += blockDim.x) {
+    const bool av = i < n && avail(i);
+    local += av ? 1 : 0;
+    code[i] = av ? order_code(keys[i]) : 0ull;
+    // unavailable tokens after every available one with the same code;
+    // padding last of all
+    idx[i] = i < n ? ((uint32_t)i | (av ? 0u : 0x80000000u)) : 0xFFFFFFFFu;
+  }
+  const int64_t total = block_sum(local, sm.warp_tot);  // also orders the writes above
+  const int64_t want = slots < total ? slots : total;
+  if (want <= 0) return 0;
+  for (int k = 2; k <= m; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = tid; i < (m >> 1); i += blockDim.x) {
+        const int lo = 2 * i - (i & (j - 1)), hi = lo + j;
+        const uint64_t cl = code[lo], ch = code[hi];
+        const uint32_t il = idx[lo], ih = idx[hi];
+        const bool hi_first = ch > cl || (ch == cl && ih < il);
+        const bool lo_first = cl > ch || (cl == ch && il < ih);
+        if ((lo & k) == 0 ? hi_first : lo_first) {
+          code[lo] = ch;
+          code[hi] = cl;
+          idx[lo] = ih;
+          idx[hi] = il;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int64_t rk = tid; rk < want; rk += blockDim.x) {
+    const int i = (int)(idx[rk] & 0x7FFFFFFFu);
+    selected[i] = 1;
+    if (chosen_out) chosen_out[rk] = i;
+  }
+  __syncthreads();
+  return want;
+}
+
 // ------------------------------------------------------------ row reductions
 // one warp per row: dev = sum (f - c)^2, nrm = sum c^2 (float64)
 // returns true (in every lane) when all inputs of the row pair are finite
@@ -203,17 +262,136 @@ __device__ __forceinline__ bool row_dev_nrm(Rows<T> c, int64_t crow, Rows<T> f, 
 
 __device__ __forceinline__ bool finite(double x) { return isfinite(x); }
 
+// cosine of one head from its dot product and squared norms: the
+// reference's amax-scaled unit vectors (wca.py:96-112) reduce to
+// dot / (|a| |b|); a zero vector gives 0 there and here
+__device__ __forceinline__ double head_cos(double dot, double aa, double bb) {
+  if (!(aa > 0.0) || !(bb > 0.0)) return 0.0;
+  return fmin(fmax(dot / (sqrt(aa) * sqrt(bb)), -1.0), 1.0);
+}
+
+// mean-head cosine of one row pair, result valid in every lane
 template <typename T>
+__device__ double row_cosine(Rows<T> a, int64_t arow, Rows<T> b, int64_t brow, int64_t heads,
+                             int64_t dim) {
+  const int lane = threadIdx.x & 31;
+  double acc = 0.0;
+  for (int64_t h = 0; h < heads; ++h) {
+    const T* ap = a.ptr(arow, h);
+    const T* bp = b.ptr(brow, h);
+    double dot = 0.0, aa = 0.0, bb = 0.0;
+    for (int64_t e = lane; e < dim; e += 32) {
+      const double x = Elem<T>::to_d(ap[e]), y = Elem<T>::to_d(bp[e]);
+      dot = __dadd_rn(dot, __dmul_rn(x, y));
+      aa = __dadd_rn(aa, __dmul_rn(x, x));
+      bb = __dadd_rn(bb, __dmul_rn(y, y));
+    }
+    acc += head_cos(warp_sum(dot), warp_sum(aa), warp_sum(bb));
+  }
+  return acc / (double)heads;
+}
+
+// ------------------------------------------------------ 16-byte row vectors
+// Rows of 16-bit elements with 16-byte aligned heads: a warp reads a row as
+// heads x G8 vectors of 8 elements (G8 = dim / 8 divides 32), lane l taking
+// vectors l, l + 32, ...; in every step each aligned group of G8 lanes holds
+// one head.
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, double (&x)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) x[k] = Elem<T>::to_d(e[k]);
+}
+
+template <typename T, int G8>
+__device__ __forceinline__ bool row_dev_nrm_vec(Rows<T> c, int64_t crow, Rows<T> f, int64_t frow,
+                                                int64_t heads, double& dev, double& nrm) {
+  const int lane = threadIdx.x & 31;
+  double d_acc = 0.0, n_acc = 0.0;
+  bool ok = true;
+  const int64_t groups = heads * G8;
+#pragma unroll 4
+  for (int64_t g = lane; g < groups; g += 32) {
+    const int64_t h = g / G8;
+    const int e = (int)(g % G8) * 8;
+    double cv[8], fv[8];
+    load8(c.ptr(crow, h) + e, cv);
+    load8(f.ptr(frow, h) + e, fv);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      ok &= isfinite(cv[k]) && isfinite(fv[k]);
+      const double df = __dsub_rn(fv[k], cv[k]);
+      d_acc = __dadd_rn(d_acc, __dmul_rn(df, df));
+      n_acc = __dadd_rn(n_acc, __dmul_rn(cv[k], cv[k]));
+    }
+  }
+  dev = warp_sum(d_acc);
+  nrm = warp_sum(n_acc);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// per-head dot / squared norms of the G8-lane group, summed into lanes with
+// lane % G8 == 0
+template <int G8>
+__device__ __forceinline__ void group_sum3(double& x, double& y, double& z) {
+#pragma unroll
+  for (int o = G8 / 2; o > 0; o >>= 1) {
+    x += __shfl_xor_sync(0xffffffffu, x, o);
+    y += __shfl_xor_sync(0xffffffffu, y, o);
+    z += __shfl_xor_sync(0xffffffffu, z, o);
+  }
+}
+
+template <typename T, int G8>
+__device__ double row_cosine_vec(Rows<T> a, int64_t arow, Rows<T> b, int64_t brow,
+                                 int64_t heads) {
+  const int lane = threadIdx.x & 31;
+  double acc = 0.0;
+  const int64_t groups = heads * G8;
+  for (int64_t g0 = 0; g0 < groups; g0 += 32) {
+    const int64_t g = g0 + lane;
+    double dot = 0.0, aa = 0.0, bb = 0.0;
+    if (g < groups) {
+      const int64_t h = g / G8;
+      const int e = (int)(g % G8) * 8;
+      double x[8], y[8];
+      load8(a.ptr(arow, h) + e, x);
+      load8(b.ptr(brow, h) + e, y);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        dot = __dadd_rn(dot, __dmul_rn(x[k], y[k]));
+        aa = __dadd_rn(aa, __dmul_rn(x[k], x[k]));
+        bb = __dadd_rn(bb, __dmul_rn(y[k], y[k]));
+      }
+    }
+    group_sum3<G8>(dot, aa, bb);
+    if (g < groups && (lane % G8) == 0) acc += head_cos(dot, aa, bb);
+  }
+  return warp_sum(acc) / (double)heads;
+}
+
+// one warp per row; G8 > 0 selects the 16-byte vector path.  The reused /
+// candidate counts are gathered per block and added once per block.
+template <typename T, int G8>
 __global__ void deviation_kernel(Rows<T> c, const int64_t* __restrict__ crows, Rows<T> f,
                                  int64_t n, int64_t heads, int64_t dim, double eps, int clamp,
                                  double* dev_out, double* alpha_out,
                                  const uint8_t* __restrict__ reused, uint8_t* candidate,
                                  unsigned long long* counts, int32_t* status) {
+  __shared__ unsigned long long cnt[2];
+  if (threadIdx.x == 0) cnt[0] = cnt[1] = 0ull;
+  __syncthreads();
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < n;
        r += warps) {
     double dev, nrm;
-    bool in_ok = row_dev_nrm(c, crows ? crows[r] : r, f, r, heads, dim, dev, nrm);
+    const int64_t crow = crows ? crows[r] : r;
+    bool in_ok;
+    if constexpr (G8 > 0)
+      in_ok = row_dev_nrm_vec<T, G8>(c, crow, f, r, heads, dev, nrm);
+    else
+      in_ok = row_dev_nrm(c, crow, f, r, heads, dim, dev, nrm);
     if ((threadIdx.x & 31) == 0) {
       double den = nrm + eps;
       double a = dev / den;
@@ -226,63 +404,39 @@ __global__ void deviation_kernel(Rows<T> c, const int64_t* __restrict__ crows, R
         bool ru = reused[r] != 0;
         bool cand = ru && dev > 0.0;
         candidate[r] = cand ? 1 : 0;
-        if (ru) atomicAdd(&counts[0], 1ull);
-        if (cand) atomicAdd(&counts[1], 1ull);
+        if (ru) atomicAdd(&cnt[0], 1ull);
+        if (cand) atomicAdd(&cnt[1], 1ull);
       }
     }
   }
-}
-
-// mean-head cosine of one row pair, result valid in every lane
-template <typename T>
-__device__ double row_cosine(Rows<T> a, int64_t arow, Rows<T> b, int64_t brow, int64_t heads,
-                             int64_t dim, double eps) {
-  const int lane = threadIdx.x & 31;
-  const double tiny = 2.2250738585072014e-308;
-  double acc = 0.0;
-  for (int64_t h = 0; h < heads; ++h) {
-    const T* ap = a.ptr(arow, h);
-    const T* bp = b.ptr(brow, h);
-    double amax = 0.0, bmax = 0.0;
-    for (int64_t e = lane; e < dim; e += 32) {
-      amax = fmax(amax, fabs(Elem<T>::to_d(ap[e])));
-      bmax = fmax(bmax, fabs(Elem<T>::to_d(bp[e])));
+  if (candidate) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      if (cnt[0]) atomicAdd(&counts[0], cnt[0]);
+      if (cnt[1]) atomicAdd(&counts[1], cnt[1]);
     }
-    amax = fmax(warp_max(amax), eps);
-    bmax = fmax(warp_max(bmax), eps);
-    double na = 0.0, nb = 0.0;
-    for (int64_t e = lane; e < dim; e += 32) {
-      double x = Elem<T>::to_d(ap[e]) / amax, y = Elem<T>::to_d(bp[e]) / bmax;
-      na = __dadd_rn(na, __dmul_rn(x, x));
-      nb = __dadd_rn(nb, __dmul_rn(y, y));
-    }
-    na = fmax(sqrt(warp_sum(na)), tiny);
-    nb = fmax(sqrt(warp_sum(nb)), tiny);
-    double dot = 0.0;
-    for (int64_t e = lane; e < dim; e += 32) {
-      double x = (Elem<T>::to_d(ap[e]) / amax) / na, y = (Elem<T>::to_d(bp[e]) / bmax) / nb;
-      dot = __dadd_rn(dot, __dmul_rn(x, y));
-    }
-    dot = warp_sum(dot);
-    acc += fmin(fmax(dot, -1.0), 1.0);
   }
-  return acc / (double)heads;
 }
 
-template <typename T>
+template <typename T, int G8>
 __global__ void cosine_kernel(Rows<T> a, Rows<T> b, const int64_t* __restrict__ brows, int64_t n,
-                              int64_t heads, int64_t dim, double eps, double* out) {
+                              int64_t heads, int64_t dim, double* out) {
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < n;
        r += warps) {
-    double c = row_cosine(a, r, b, brows ? brows[r] : r, heads, dim, eps);
+    const int64_t br = brows ? brows[r] : r;
+    double c;
+    if constexpr (G8 > 0)
+      c = row_cosine_vec<T, G8>(a, r, b, br, heads);
+    else
+      c = row_cosine(a, r, b, br, heads, dim);
     if ((threadIdx.x & 31) == 0) out[r] = c;
   }
 }
 
 // fused update: weight, blend (float64, no contraction), cast, write dense
-// and/or paged records, optional cosine
-template <typename T>
+// and/or paged records, optional cosine; G8 > 0 selects the 16-byte vector path
+template <typename T, int G8>
 __global__ void update_kernel(Rows<T> ck, Rows<T> cv, Rows<T> fk, Rows<T> fv,
                               const int64_t* __restrict__ indices, int64_t a, int64_t heads,
                               int64_t dim, const double* __restrict__ alpha,
@@ -296,7 +450,11 @@ __global__ void update_kernel(Rows<T> ck, Rows<T> cv, Rows<T> fk, Rows<T> fv,
        r += warps) {
     const int64_t idx = indices[r];
     double dev, nrm;
-    bool bad = !row_dev_nrm(ck, idx, fk, r, heads, dim, dev, nrm);
+    bool bad;
+    if constexpr (G8 > 0)
+      bad = !row_dev_nrm_vec<T, G8>(ck, idx, fk, r, heads, dev, nrm);
+    else
+      bad = !row_dev_nrm(ck, idx, fk, r, heads, dim, dev, nrm);
     double den = nrm + eps;
     double nxt = dev / den;
     bad |= !finite(dev) || !finite(den) || !finite(nxt);
@@ -306,27 +464,72 @@ __global__ void update_kernel(Rows<T> ck, Rows<T> cv, Rows<T> fk, Rows<T> fv,
     int64_t slot = use_paged ? slots[r] : 0;
     bool slot_ok = !use_paged || pv.valid(slot);
     if (use_paged && !slot_ok && lane == 0) report(status, CS_ST_SLOT_RANGE);
-    for (int half = 0; half < 2; ++half) {
-      Rows<T> o = half ? cv : ck;
-      Rows<T> f = half ? fv : fk;
-      T* dst = half ? fused_v : fused_k;
-      for (int64_t h = 0; h < heads; ++h) {
-        const T* op = o.ptr(idx, h);
-        const T* fp = f.ptr(r, h);
-        for (int64_t e = lane; e < dim; e += 32) {
-          double x = __dadd_rn(__dmul_rn(w, Elem<T>::to_d(fp[e])),
-                               __dmul_rn(wo, Elem<T>::to_d(op[e])));
-          T y = Elem<T>::from_d(x);
-          bad |= !isfinite(Elem<T>::to_d(y));
-          if (dst) dst[(r * heads + h) * dim + e] = y;
-          if (use_paged && slot_ok)
-            *reinterpret_cast<T*>(pv.addr(slot, h, half * dim + e)) = y;
+    double cs = 0.0;
+    if constexpr (G8 > 0) {
+      // one read of the four rows: blend K and V, K cosine of fresh vs cached
+      double cacc = 0.0;
+      const int64_t groups = heads * G8;
+      for (int64_t g0 = 0; g0 < groups; g0 += 32) {
+        const int64_t g = g0 + lane;
+        double dot = 0.0, aa = 0.0, bb = 0.0;
+        if (g < groups) {
+          const int64_t h = g / G8;
+          const int e = (int)(g % G8) * 8;
+          double ok8[8], fk8[8], ov8[8], fv8[8];
+          load8(ck.ptr(idx, h) + e, ok8);
+          load8(fk.ptr(r, h) + e, fk8);
+          load8(cv.ptr(idx, h) + e, ov8);
+          load8(fv.ptr(r, h) + e, fv8);
+          alignas(16) T yk[8];
+          alignas(16) T yv[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            yk[k] = Elem<T>::from_d(__dadd_rn(__dmul_rn(w, fk8[k]), __dmul_rn(wo, ok8[k])));
+            yv[k] = Elem<T>::from_d(__dadd_rn(__dmul_rn(w, fv8[k]), __dmul_rn(wo, ov8[k])));
+            bad |= !isfinite(Elem<T>::to_d(yk[k])) || !isfinite(Elem<T>::to_d(yv[k]));
+            dot = __dadd_rn(dot, __dmul_rn(fk8[k], ok8[k]));
+            aa = __dadd_rn(aa, __dmul_rn(fk8[k], fk8[k]));
+            bb = __dadd_rn(bb, __dmul_rn(ok8[k], ok8[k]));
+          }
+          const uint4 uk = *reinterpret_cast<const uint4*>(yk);
+          const uint4 uv = *reinterpret_cast<const uint4*>(yv);
+          if (fused_k) {
+            *reinterpret_cast<uint4*>(fused_k + (r * heads + h) * dim + e) = uk;
+            *reinterpret_cast<uint4*>(fused_v + (r * heads + h) * dim + e) = uv;
+          }
+          if (use_paged && slot_ok) {
+            *reinterpret_cast<uint4*>(pv.addr(slot, h, e)) = uk;
+            *reinterpret_cast<uint4*>(pv.addr(slot, h, dim + e)) = uv;
+          }
+        }
+        if (cos_out) {
+          group_sum3<G8>(dot, aa, bb);
+          if (g < groups && (lane % G8) == 0) cacc += head_cos(dot, aa, bb);
         }
       }
+      if (cos_out) cs = warp_sum(cacc) / (double)heads;
+    } else {
+      for (int half = 0; half < 2; ++half) {
+        Rows<T> o = half ? cv : ck;
+        Rows<T> f = half ? fv : fk;
+        T* dst = half ? fused_v : fused_k;
+        for (int64_t h = 0; h < heads; ++h) {
+          const T* op = o.ptr(idx, h);
+          const T* fp = f.ptr(r, h);
+          for (int64_t e = lane; e < dim; e += 32) {
+            double x = __dadd_rn(__dmul_rn(w, Elem<T>::to_d(fp[e])),
+                                 __dmul_rn(wo, Elem<T>::to_d(op[e])));
+            T y = Elem<T>::from_d(x);
+            bad |= !isfinite(Elem<T>::to_d(y));
+            if (dst) dst[(r * heads + h) * dim + e] = y;
+            if (use_paged && slot_ok)
+              *reinterpret_cast<T*>(pv.addr(slot, h, half * dim + e)) = y;
+          }
+        }
+      }
+      if (cos_out) cs = row_cosine(fk, r, ck, idx, heads, dim);
     }
     bad = __any_sync(0xffffffffu, bad);
-    double cs = 0.0;
-    if (cos_out) cs = row_cosine(fk, r, ck, idx, heads, dim, eps);
     if (lane == 0) {
       if (bad) report(status, CS_ST_NONFINITE);
       if (next_alpha_out) next_alpha_out[r] = nxt;
@@ -346,8 +549,9 @@ __global__ void __launch_bounds__(kSelectThreads)
   double* stage_key = reinterpret_cast<double*>(dyn);
   int* stage_idx = reinterpret_cast<int*>(dyn + sizeof(double) * kSelectMaxChosen);
   auto avail = [&](int64_t i) { return available[i] != 0; };
-  int64_t k = block_select_topk(keys, avail, n, slots, selected, chosen_out, sm, stage_key,
-                                stage_idx, status);
+  int64_t k = n <= kSortMax ? block_sort_topk(keys, avail, n, slots, selected, chosen_out, sm, dyn)
+                            : block_select_topk(keys, avail, n, slots, selected, chosen_out, sm,
+                                                stage_key, stage_idx, status);
   if (threadIdx.x == 0 && count_out) *count_out = k;
 }
 
@@ -401,8 +605,10 @@ __global__ void __launch_bounds__(kSelectThreads)
   if (slots < 0) slots = 0;
   auto avail = [&](int64_t i) { return candidate[i] && !selected[i] && !removed[i]; };
   // `selected` changes only after the radix passes finish counting
-  int64_t k = block_select_topk(initial, avail, n, slots, selected, promoted_out, sm, stage_key,
-                                stage_idx, status);
+  int64_t k = n <= kSortMax
+                  ? block_sort_topk(initial, avail, n, slots, selected, promoted_out, sm, dyn)
+                  : block_select_topk(initial, avail, n, slots, selected, promoted_out, sm,
+                                      stage_key, stage_idx, status);
   if (tid == 0 && counts_out) {
     counts_out[0] = removed_count;
     counts_out[1] = k;
@@ -430,6 +636,37 @@ int row_grid(int64_t rows, int warps_per_block) {
   int64_t cap = (int64_t)num_sms() * 8;
   if (blocks > cap) blocks = cap;
   return blocks < 1 ? 1 : (int)blocks;
+}
+
+// vector width of the row kernels: G8 = dim / 8 when the rows are 16-bit
+// elements in 16-byte aligned heads (every base and byte stride a multiple
+// of 16) and G8 divides 32 with at least 4 lanes per head; 0 otherwise
+template <typename T>
+int vec_groups(int64_t dim, std::initializer_list<const void*> bases,
+               std::initializer_list<int64_t> elem_strides) {
+  if (sizeof(T) != 2 || dim % 8) return 0;
+  const int64_t g8 = dim / 8;
+  if (g8 != 4 && g8 != 8 && g8 != 16 && g8 != 32) return 0;
+  for (const void* b : bases)
+    if (b != nullptr && (reinterpret_cast<uintptr_t>(b) & 15)) return 0;
+  for (int64_t st : elem_strides)
+    if ((st * (int64_t)sizeof(T)) % 16) return 0;
+  return (int)g8;
+}
+
+// call f with std::integral_constant<int, G8> (0 = scalar path)
+template <typename T, typename F>
+void with_g8(int g8, F&& f) {
+  if constexpr (sizeof(T) == 2) {
+    switch (g8) {
+      case 4: f(std::integral_constant<int, 4>{}); return;
+      case 8: f(std::integral_constant<int, 8>{}); return;
+      case 16: f(std::integral_constant<int, 16>{}); return;
+      case 32: f(std::integral_constant<int, 32>{}); return;
+      default: break;
+    }
+  }
+  f(std::integral_constant<int, 0>{});
 }
 
 template <typename T>
@@ -463,10 +700,15 @@ extern "C" int cs_wca_deviation(const void* cached, int64_t c_stride_row, int64_
   CS_HOST_CHECK(cached && fresh);
   const int threads = 256;
   CS_DISPATCH_FLOAT(dtype, T, {
-    deviation_kernel<T><<<row_grid(n, threads / 32), threads, 0, as_stream(stream)>>>(
-        rows_of<T>(cached, c_stride_row, c_stride_head), cached_rows,
-        rows_of<T>(fresh, f_stride_row, f_stride_head), n, heads, dim, epsilon, clamp, dev_out,
-        alpha_out, nullptr, nullptr, nullptr, status);
+    const int g8 = vec_groups<T>(dim, {cached, fresh},
+                                 {c_stride_row, c_stride_head, f_stride_row, f_stride_head});
+    with_g8<T>(g8, [&](auto G) {
+      deviation_kernel<T, decltype(G)::value>
+          <<<row_grid(n, threads / 32), threads, 0, as_stream(stream)>>>(
+              rows_of<T>(cached, c_stride_row, c_stride_head), cached_rows,
+              rows_of<T>(fresh, f_stride_row, f_stride_head), n, heads, dim, epsilon, clamp,
+              dev_out, alpha_out, nullptr, nullptr, nullptr, status);
+    });
   });
   CS_LAUNCH_CHECK();
   return CS_OK;
@@ -488,10 +730,15 @@ extern "C" int cs_wca_initialize(const void* cached, int64_t c_stride_row, int64
   CS_HOST_CHECK(cached && fresh);
   const int threads = 256;
   CS_DISPATCH_FLOAT(dtype, T, {
-    deviation_kernel<T><<<row_grid(n, threads / 32), threads, 0, s>>>(
-        rows_of<T>(cached, c_stride_row, c_stride_head), nullptr,
-        rows_of<T>(fresh, f_stride_row, f_stride_head), n, heads, dim, epsilon, clamp, dev_out,
-        alpha_out, reused, candidate, reinterpret_cast<unsigned long long*>(counts_out), status);
+    const int g8 = vec_groups<T>(dim, {cached, fresh},
+                                 {c_stride_row, c_stride_head, f_stride_row, f_stride_head});
+    with_g8<T>(g8, [&](auto G) {
+      deviation_kernel<T, decltype(G)::value><<<row_grid(n, threads / 32), threads, 0, s>>>(
+          rows_of<T>(cached, c_stride_row, c_stride_head), nullptr,
+          rows_of<T>(fresh, f_stride_row, f_stride_head), n, heads, dim, epsilon, clamp,
+          dev_out, alpha_out, reused, candidate,
+          reinterpret_cast<unsigned long long*>(counts_out), status);
+    });
   });
   CS_LAUNCH_CHECK();
   return CS_OK;
@@ -507,10 +754,16 @@ extern "C" int cs_wca_cosine(const void* a, int64_t a_stride_row, int64_t a_stri
   if (n == 0) return CS_OK;
   CS_HOST_CHECK(a && b && cos_out);
   const int threads = 256;
+  (void)epsilon;  // scale-invariant: the reference's max clamp does not change the result
   CS_DISPATCH_FLOAT(dtype, T, {
-    cosine_kernel<T><<<row_grid(n, threads / 32), threads, 0, as_stream(stream)>>>(
-        rows_of<T>(a, a_stride_row, a_stride_head), rows_of<T>(b, b_stride_row, b_stride_head),
-        b_rows, n, heads, dim, epsilon, cos_out);
+    const int g8 = vec_groups<T>(dim, {a, b},
+                                 {a_stride_row, a_stride_head, b_stride_row, b_stride_head});
+    with_g8<T>(g8, [&](auto G) {
+      cosine_kernel<T, decltype(G)::value>
+          <<<row_grid(n, threads / 32), threads, 0, as_stream(stream)>>>(
+              rows_of<T>(a, a_stride_row, a_stride_head),
+              rows_of<T>(b, b_stride_row, b_stride_head), b_rows, n, heads, dim, cos_out);
+    });
   });
   CS_LAUNCH_CHECK();
   return CS_OK;
@@ -559,13 +812,20 @@ extern "C" int cs_wca_update(const void* cached_k, const void* cached_v, int64_t
   }
   const int threads = 256;
   CS_DISPATCH_FLOAT(dtype, T, {
-    update_kernel<T><<<row_grid(a, threads / 32), threads, 0, as_stream(stream)>>>(
-        rows_of<T>(cached_k, c_stride_row, c_stride_head),
-        rows_of<T>(cached_v, c_stride_row, c_stride_head),
-        rows_of<T>(fresh_k, f_stride_row, f_stride_head),
-        rows_of<T>(fresh_v, f_stride_row, f_stride_head), indices, a, heads, dim, alpha,
-        mandatory, same_layer, epsilon, clamp, static_cast<T*>(fused_k), static_cast<T*>(fused_v),
-        next_alpha_out, used_alpha_out, cos_out, pv, use_paged, slots, status);
+    int g8 = vec_groups<T>(dim, {cached_k, cached_v, fresh_k, fresh_v, fused_k, fused_v},
+                           {c_stride_row, c_stride_head, f_stride_row, f_stride_head});
+    if (use_paged && !pv.vec16()) g8 = 0;
+    with_g8<T>(g8, [&](auto G) {
+      update_kernel<T, decltype(G)::value>
+          <<<row_grid(a, threads / 32), threads, 0, as_stream(stream)>>>(
+              rows_of<T>(cached_k, c_stride_row, c_stride_head),
+              rows_of<T>(cached_v, c_stride_row, c_stride_head),
+              rows_of<T>(fresh_k, f_stride_row, f_stride_head),
+              rows_of<T>(fresh_v, f_stride_row, f_stride_head), indices, a, heads, dim, alpha,
+              mandatory, same_layer, epsilon, clamp, static_cast<T*>(fused_k),
+              static_cast<T*>(fused_v), next_alpha_out, used_alpha_out, cos_out, pv, use_paged,
+              slots, status);
+    });
   });
   CS_LAUNCH_CHECK();
   return CS_OK;

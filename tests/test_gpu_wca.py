@@ -50,6 +50,22 @@ def test_cosine_matches_reference_golden(cuda):
     np.testing.assert_allclose(got, c["cos"], rtol=1e-13, atol=1e-15)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_cosine_vector_rows_match_oracle(cuda, dtype):
+    """16-byte vector path (8 KV heads x 128): mean-head cosine vs the oracle,
+    including all-zero heads (cosine 0) and exactly parallel rows."""
+    g = torch.Generator().manual_seed(3)
+    n, h, d = 257, 8, 128
+    a = torch.randn(n, h, d, generator=g).to(dtype)
+    b = (a.float() + 0.3 * torch.randn(n, h, d, generator=g)).to(dtype)
+    a[5] = 0
+    b[6, 3] = 0
+    b[7] = a[7]
+    got = W.mean_head_cosine(a.to(cuda), b.to(cuda)).cpu().numpy()
+    want = owca.mean_head_cosine(a.float().numpy(), b.float().numpy())
+    np.testing.assert_allclose(got, want, rtol=1e-13, atol=1e-15)
+
+
 @pytest.mark.parametrize("n", [1, 33, 4096, 20000])
 def test_select_topk_matches_stable_argsort_with_ties(cuda, n):
     rng = np.random.default_rng(n)
