@@ -233,6 +233,210 @@ __device__ int64_t block_sort_topk(const double* __restrict__ keys, Avail avail,
   return want;
 }
 
+// Top-k for n <= kSortMax and at most kFastPicks picks: the order codes of
+// all tokens are staged in shared memory once; an MSB-first 8-bit radix
+// select finds the code of the k-th pick (warp-aggregated histogram, bin
+// search by one warp); an ordered compaction takes the picks, ties to the
+// lower index; only the picks are then sorted by (code descending, index
+// ascending), one per thread in registers (shuffles for partners within a
+// warp, shared memory beyond).  Larger pick counts use block_sort_topk.
+constexpr int kFastPicks = 1024;  // == kSelectThreads
+
+template <typename Avail>
+__device__ int64_t block_topk_staged(const double* __restrict__ keys, Avail avail, int64_t n,
+                                     int64_t slots, uint8_t* __restrict__ selected,
+                                     int64_t* __restrict__ chosen_out, SelectSmem& sm,
+                                     unsigned char* dyn) {
+  uint64_t* code = reinterpret_cast<uint64_t*>(dyn);  // [kSortMax], 0: unavailable
+  uint64_t* pcode = code + kSortMax;                   // [kFastPicks] picks, then exchange
+  uint32_t* pidx = reinterpret_cast<uint32_t*>(pcode + kFastPicks);
+  int* whist = reinterpret_cast<int*>(pidx + kFastPicks);  // [32 warps][256] private histograms
+  __shared__ int hist[256];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const unsigned full = 0xffffffffu;
+  int local = 0;
+#pragma unroll 4
+  for (int64_t i = tid; i < n; i += blockDim.x) {
+    const bool av = avail(i);
+    local += av ? 1 : 0;
+    code[i] = av ? order_code(keys[i]) : 0ull;
+  }
+  const int64_t total = block_sum(local, sm.warp_tot);  // also orders the writes above
+  const int64_t want = slots < total ? slots : total;
+  if (want <= 0) return 0;
+  if (want > kFastPicks)
+    return block_sort_topk(keys, avail, n, slots, selected, chosen_out, sm, dyn);
+  // the leading bytes shared by the smallest and largest available code are
+  // those of every available code: the radix passes start below them
+  uint64_t lo = ~0ull, hi = 0ull;
+  for (int64_t i = tid; i < n; i += blockDim.x) {
+    const uint64_t c = code[i];
+    if (c != 0ull) {
+      lo = c < lo ? c : lo;
+      hi = c > hi ? c : hi;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const uint64_t l2 = __shfl_xor_sync(full, lo, o), h2 = __shfl_xor_sync(full, hi, o);
+    lo = l2 < lo ? l2 : lo;
+    hi = h2 > hi ? h2 : hi;
+  }
+  uint64_t* wmin = reinterpret_cast<uint64_t*>(whist);  // [32] lo, [32] hi, scratch
+  if (lane == 0) {
+    wmin[warp] = lo;
+    wmin[32 + warp] = hi;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    lo = lane < nw ? wmin[lane] : ~0ull;
+    hi = lane < nw ? wmin[32 + lane] : 0ull;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const uint64_t l2 = __shfl_xor_sync(full, lo, o), h2 = __shfl_xor_sync(full, hi, o);
+      lo = l2 < lo ? l2 : lo;
+      hi = h2 > hi ? h2 : hi;
+    }
+    if (lane == 0) sm.mask = lo ^ hi;  // differing bits
+  }
+  __syncthreads();
+  const uint64_t diff = sm.mask;
+  int top = 56;  // first byte (from the top) where the codes differ
+  while (top > 0 && ((diff >> top) & 255ull) == 0ull) top -= 8;
+  // radix select: prefix / mask of the k-th code, `remaining` of its ties
+  uint64_t mask = top < 56 ? (~0ull << (top + 8)) : 0ull;
+  uint64_t prefix = hi & mask;
+  int remaining = (int)want;
+  int* mine = whist + warp * 256;
+  const int nwarps = blockDim.x >> 5;
+  __syncthreads();  // wmin (aliasing whist) read by all before the histograms
+  for (int shift = top; shift >= 0; shift -= 8) {
+    for (int b = lane; b < 256; b += 32) mine[b] = 0;
+    __syncwarp();
+    for (int64_t base = 0; base < n; base += blockDim.x) {
+      const int64_t i = base + tid;
+      const uint64_t c = i < n ? code[i] : 0ull;
+      if (c != 0ull && (c & mask) == prefix) atomicAdd(&mine[(c >> shift) & 255], 1);
+    }
+    __syncthreads();
+    for (int b = tid; b < 256; b += blockDim.x) {
+      int t = 0;
+      for (int w = 0; w < nwarps; ++w) t += whist[w * 256 + b];
+      hist[b] = t;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      // lane l owns bins 255-8l .. 248-8l (descending)
+      int cnt[8], sum = 0;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        cnt[q] = hist[255 - 8 * lane - q];
+        sum += cnt[q];
+      }
+      int inc = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(full, inc, o);
+        if (lane >= o) inc += t;
+      }
+      const int need = sm.remaining = remaining;  // every lane reads the same value
+      const unsigned hit = __ballot_sync(full, inc >= need);
+      const int owner = __ffs(hit) - 1;
+      if (lane == owner) {
+        int above = inc - sum, b = 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          if (above + cnt[q] >= need) {
+            b = 255 - 8 * lane - q;
+            break;
+          }
+          above += cnt[q];
+        }
+        sm.prefix = prefix | ((uint64_t)b << shift);
+        sm.remaining = need - above;
+      }
+    }
+    __syncthreads();
+    prefix = sm.prefix;
+    remaining = sm.remaining;
+    mask |= 255ull << shift;
+    __syncthreads();
+  }
+  // ordered compaction of the picks: code above the k-th, or equal to it
+  // among the first `remaining` by index
+  if (tid == 0) {
+    sm.chosen_count = 0;
+    sm.eq_taken = 0;
+  }
+  __syncthreads();
+  // one scan per step over (greater, equal) counts packed in 16-bit halves:
+  // a pick's slot is #greater before it + min(#equal before it, remaining)
+  for (int64_t base = 0; base < n; base += blockDim.x) {
+    const int64_t i = base + tid;
+    const uint64_t c = i < n ? code[i] : 0ull;
+    const int gt = (c != 0ull && c > prefix) ? 1 : 0;
+    const int eq = (c != 0ull && c == prefix) ? 1 : 0;
+    const int inc = block_inclusive_scan(gt | (eq << 16), sm.warp_tot);
+    const int gt_before = (inc & 0xFFFF) - gt + sm.chosen_count;  // greater ones so far
+    const int eq_before = (inc >> 16) - eq + sm.eq_taken;
+    const bool pick = gt || (eq && eq_before < remaining);
+    if (pick) {
+      const int slot = gt_before + (eq_before < remaining ? eq_before : remaining);
+      pcode[slot] = c;
+      pidx[slot] = (uint32_t)i;
+    }
+    __syncthreads();
+    if (tid == blockDim.x - 1) {
+      sm.chosen_count = gt_before + gt;
+      sm.eq_taken = eq_before + eq;
+    }
+    __syncthreads();
+  }
+  // bitonic sort of the picks, thread t holding position t
+  int P = 32;
+  while (P < want) P <<= 1;
+  const bool part = tid < P;  // warp-uniform (P is a multiple of 32)
+  uint64_t c = (tid < want) ? pcode[tid] : 0ull;
+  uint32_t id = (tid < want) ? pidx[tid] : 0xFFFFFFFFu;
+  __syncthreads();
+  for (int k = 2; k <= P; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      uint64_t pc;
+      uint32_t pi;
+      if (j >= 32) {  // block-uniform
+        if (part) {
+          pcode[tid] = c;
+          pidx[tid] = id;
+        }
+        __syncthreads();
+        if (part) {
+          pc = pcode[tid ^ j];
+          pi = pidx[tid ^ j];
+        }
+        __syncthreads();
+      } else if (part) {
+        pc = __shfl_xor_sync(full, c, j);
+        pi = __shfl_xor_sync(full, id, j);
+      }
+      if (part) {
+        const bool partner_first = pc > c || (pc == c && pi < id);
+        const bool keep_first = ((tid & j) == 0) == ((tid & k) == 0);
+        if (keep_first == partner_first) {
+          c = pc;
+          id = pi;
+        }
+      }
+    }
+  }
+  if (tid < want) {
+    selected[id] = 1;
+    if (chosen_out) chosen_out[tid] = id;
+  }
+  __syncthreads();
+  return want;
+}
+
 // ------------------------------------------------------------ row reductions
 // one warp per row: dev = sum (f - c)^2, nrm = sum c^2 (float64)
 // returns true (in every lane) when all inputs of the row pair are finite
@@ -549,9 +753,10 @@ __global__ void __launch_bounds__(kSelectThreads)
   double* stage_key = reinterpret_cast<double*>(dyn);
   int* stage_idx = reinterpret_cast<int*>(dyn + sizeof(double) * kSelectMaxChosen);
   auto avail = [&](int64_t i) { return available[i] != 0; };
-  int64_t k = n <= kSortMax ? block_sort_topk(keys, avail, n, slots, selected, chosen_out, sm, dyn)
-                            : block_select_topk(keys, avail, n, slots, selected, chosen_out, sm,
-                                                stage_key, stage_idx, status);
+  int64_t k = n <= kSortMax
+                  ? block_topk_staged(keys, avail, n, slots, selected, chosen_out, sm, dyn)
+                  : block_select_topk(keys, avail, n, slots, selected, chosen_out, sm, stage_key,
+                                      stage_idx, status);
   if (threadIdx.x == 0 && count_out) *count_out = k;
 }
 
@@ -606,7 +811,7 @@ __global__ void __launch_bounds__(kSelectThreads)
   auto avail = [&](int64_t i) { return candidate[i] && !selected[i] && !removed[i]; };
   // `selected` changes only after the radix passes finish counting
   int64_t k = n <= kSortMax
-                  ? block_sort_topk(initial, avail, n, slots, selected, promoted_out, sm, dyn)
+                  ? block_topk_staged(initial, avail, n, slots, selected, promoted_out, sm, dyn)
                   : block_select_topk(initial, avail, n, slots, selected, promoted_out, sm,
                                       stage_key, stage_idx, status);
   if (tid == 0 && counts_out) {

@@ -66,7 +66,7 @@ def test_cosine_vector_rows_match_oracle(cuda, dtype):
     np.testing.assert_allclose(got, want, rtol=1e-13, atol=1e-15)
 
 
-@pytest.mark.parametrize("n", [1, 33, 4096, 20000])
+@pytest.mark.parametrize("n", [1, 33, 4096, 12000, 20000])
 def test_select_topk_matches_stable_argsort_with_ties(cuda, n):
     rng = np.random.default_rng(n)
     keys = rng.integers(0, max(2, n // 8), n).astype(np.float64) * 0.25  # many exact ties
