@@ -6,8 +6,10 @@ runtime writes the cached K/V snapshot into the request's paged arena
 (``WCAState.update`` + ``update_selected``), gathers the whole logical K/V
 back into a dense copy and runs ``cope_attention`` with the canonical
 position policy and the selected-association policy.  ``ReuseStep`` runs the
-same layer as a fixed sequence of CUDA launches on one stream, with no host
-synchronisation and no dense gather:
+same layer as a fixed sequence of CUDA launches per request, with no host
+synchronisation and no dense gather; the requests' sequences are independent
+and run on one stream each, forked from and joined back into the caller's
+stream with events:
 
 1. ``cs_slide_scatter``   baseline snapshot -> canonical paged slots;
 2. ``cs_wca_initialize``  deviation / weight / candidates of the calibration
@@ -190,6 +192,11 @@ class ReuseStep:
         self.dec_v = torch.cat([r.decode_v for r in reqs]).contiguous()
         self.dec_slots = torch.stack([r.slots_all[n] for r in reqs]).contiguous()
         self.gate_layer = True  # exercise the cosine gate in every timed step
+        # one stream per request: the launch chains touch disjoint slots of the
+        # shared pool and their own WCA state, so they overlap on the device
+        self.streams = [torch.cuda.Stream(device=dev) for _ in reqs]
+        self._fork = torch.cuda.Event()
+        self._joins = [torch.cuda.Event() for _ in reqs]
 
     # -------------------------------------------------------------- pieces
     def _initialize_all(self, stream) -> None:
@@ -298,15 +305,28 @@ class ReuseStep:
         N.check(rc, "attention")
 
     def run(self, stream: int | None = None) -> list[torch.Tensor]:
-        """One reuse-prefill layer for every request; returns the outputs."""
-        s = N.stream_of(self.work.device) if stream is None else stream
-        for r in self.work.requests:
+        """One reuse-prefill layer for every request; returns the outputs.
+
+        Each request's launches go to its own stream, which first waits for
+        the caller's stream (``stream`` handle, default the current one); the
+        caller's stream then waits for every request, so work queued on it
+        afterwards sees all outputs."""
+        dev = self.work.device
+        main = (torch.cuda.current_stream(dev) if stream is None
+                else torch.cuda.ExternalStream(stream, device=dev))
+        self._fork.record(main)
+        for r, rs, done in zip(self.work.requests, self.streams, self._joins):
+            rs.wait_event(self._fork)
+            s = rs.cuda_stream
             self.baseline_write(r, s)
             self._initialize(r, s)
             self._select_async(r, s)
             self.wca_update(r, s)
             self.wca_commit(r, s)
             self.attention(r, s)
+            done.record(rs)
+        for done in self._joins:
+            main.wait_event(done)
         return [r.out for r in self.work.requests]
 
     def _select_async(self, r, s) -> None:
