@@ -24,9 +24,8 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
+import threading
 import time
 from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
@@ -96,43 +95,66 @@ def hot_bytes(work) -> dict:
 
 # --------------------------------------------------------------- clocks
 class Clocks:
-    def __init__(self, index: int):
-        self.path = Path(tempfile.mkstemp(prefix="clk", suffix=".csv")[1])
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock, its maximum and the active clock-event (throttle) reasons,
+    sampled about every millisecond from a background thread through NVML --
+    the counters `nvidia-smi --query-gpu=clocks.sm,clocks_event_reasons.*`
+    prints -- so that even a timed region of a few milliseconds has samples.
+    `mark()` opens and closes the window of the timed steps."""
+
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+               "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
+
+    def __init__(self, device: int):
+        self.samples: list[tuple[float, float, int]] = []
+        self.window: list[float] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            try:  # the NVML device of this CUDA ordinal, by UUID
+                uuid = str(torch.cuda.get_device_properties(device).uuid)
+                self.h = pynvml.nvmlDeviceGetHandleByUUID("GPU-" + uuid)
+            except Exception:
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(device)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
         except Exception:
-            self.proc = None
+            self.nv = None
+            return
+        self.thread = threading.Thread(target=self._loop, daemon=True)
+        self.thread.start()
+
+    def _loop(self) -> None:
+        nv, h = self.nv, self.h
+        while not self._stop.is_set():
+            try:
+                sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                rs = int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))
+                self.samples.append((time.perf_counter(), sm, rs))
+            except Exception:
+                pass
+            time.sleep(0.001)
+
+    def mark(self) -> None:
+        self.window.append(time.perf_counter())
 
     def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(5)
-        except Exception:
-            self.proc.kill()
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.path.read_text().splitlines():
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for name, val in zip(names, f[5:9]):
-                if val.lower() == "active":
-                    reasons.add(name)
-        self.path.unlink(missing_ok=True)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        if self.nv is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"],
+                    "samples": 0}
+        self._stop.set()
+        self.thread.join(2)
+        t0, t1 = (self.window + [0.0, float("inf")])[:2] if len(self.window) >= 2 else (0.0, float("inf"))
+        inside = [x for x in self.samples if t0 <= x[0] <= t1]
+        use = inside if inside else self.samples
+        reasons = sorted({name for _, _, rs in use for name, bit in self.REASONS.items()
+                          if rs & bit})
+        return {"sm_mhz": statistics.median(x[1] for x in use) if use else None,
+                "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(use), "samples_in_timed_steps": len(inside),
+                "source": "nvml, 1 ms"}
 
 
 # ------------------------------------------------------------- CPU legs
@@ -273,12 +295,16 @@ def main():
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]
     barrier()
+    if clocks:
+        clocks.mark()
     for i in range(args.steps):
         flush.fill_(i & 0xFF)
         ev[i][0].record(stream)
         step.run(s)
         ev[i][1].record(stream)
     barrier()
+    if clocks:
+        clocks.mark()
     step_ms = [a.elapsed_time(b) for a, b in ev]
     total_ms = sum(step_ms)
 
@@ -320,15 +346,19 @@ def main():
     e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
               for _ in range(args.steps)]
     barrier()
+    items = {id(r): item for r, item in zip(work.requests, host)}
+
+    def stage_in(r, rs):  # on the request's stream, before its launches
+        for name in ("cached_k", "cached_v", "q", "fk", "fv"):
+            getattr(r, name).copy_(items[id(r)][name], non_blocking=True)
+
+    def stage_out(r, rs):  # on the request's stream, after its attention
+        items[id(r)]["out"].copy_(r.out, non_blocking=True)
+
     for i in range(args.steps):
         flush.fill_(i & 0xFF)
         e2e_ev[i][0].record(stream)
-        for r, item in zip(work.requests, host):
-            for name in ("cached_k", "cached_v", "q", "fk", "fv"):
-                getattr(r, name).copy_(item[name], non_blocking=True)
-        step.run(s)
-        for r, item in zip(work.requests, host):
-            item["out"].copy_(r.out, non_blocking=True)
+        step.run(s, before=stage_in, after=stage_out)
         e2e_ev[i][1].record(stream)
     barrier()
     e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_ev)

@@ -74,7 +74,7 @@ def build(verbose: bool = False, extra: list[str] | None = None) -> Path:
     with ThreadPoolExecutor(max_workers=min(8, len(sources))) as pool:
         objs = list(pool.map(compile_one, sources))
     if not LIB.exists() or any(o.stat().st_mtime > LIB.stat().st_mtime for o in objs):
-        cmd = [compiler, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lcuda"]
+        cmd = [compiler, *ARCH, "-shared", "-o", str(LIB), *map(str, objs)]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f"link failed:\n{res.stdout}{res.stderr}")

@@ -1175,6 +1175,25 @@ bool prefill_supported(const cs_attn_params* p) {
   return true;
 }
 
+// cuTensorMapEncodeTiled from the driver, resolved at first use through the
+// runtime (the library does not link libcuda, so it loads on hosts without a GPU)
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled() {
+  static const EncodeTiledFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<EncodeTiledFn>(nullptr);
+    return reinterpret_cast<EncodeTiledFn>(f);
+  }();
+  return fn;
+}
+
 // 2-D row map over `rows` rows of `inner` 16-bit elements, `unit` bytes apart,
 // read in 64 x box_rows boxes with the 128-byte swizzle of the UMMA operand tiles
 bool encode_rows(CUtensorMap* m, const void* base, bool bf16, int64_t inner, int64_t rows,
@@ -1185,13 +1204,12 @@ bool encode_rows(CUtensorMap* m, const void* base, bool bf16, int64_t inner, int
   const cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)unit};
   const cuuint32_t box[2] = {64, box_rows}, es[2] = {1, 1};
-  return cuTensorMapEncodeTiled(m,
-                                bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                                2, const_cast<void*>(base), dims, strides, box, es,
-                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  const EncodeTiledFn encode = encode_tiled();
+  if (encode == nullptr) return false;
+  return encode(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // Row structure of the K/V storage for the TMA path: every row the kernel

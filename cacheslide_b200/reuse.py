@@ -304,13 +304,15 @@ class ReuseStep:
             rc = self.lib.cs_cope_attn(ctypes.byref(r.params), stream)
         N.check(rc, "attention")
 
-    def run(self, stream: int | None = None) -> list[torch.Tensor]:
+    def run(self, stream: int | None = None, before=None, after=None) -> list[torch.Tensor]:
         """One reuse-prefill layer for every request; returns the outputs.
 
         Each request's launches go to its own stream, which first waits for
         the caller's stream (``stream`` handle, default the current one); the
         caller's stream then waits for every request, so work queued on it
-        afterwards sees all outputs."""
+        afterwards sees all outputs.  ``before(request, stream)`` and
+        ``after(request, stream)`` run with that request's stream current
+        around its launches (host <-> device staging of its tensors)."""
         dev = self.work.device
         main = (torch.cuda.current_stream(dev) if stream is None
                 else torch.cuda.ExternalStream(stream, device=dev))
@@ -318,12 +320,18 @@ class ReuseStep:
         for r, rs, done in zip(self.work.requests, self.streams, self._joins):
             rs.wait_event(self._fork)
             s = rs.cuda_stream
+            if before is not None:
+                with torch.cuda.stream(rs):
+                    before(r, rs)
             self.baseline_write(r, s)
             self._initialize(r, s)
             self._select_async(r, s)
             self.wca_update(r, s)
             self.wca_commit(r, s)
             self.attention(r, s)
+            if after is not None:
+                with torch.cuda.stream(rs):
+                    after(r, rs)
             done.record(rs)
         for done in self._joins:
             main.wait_event(done)
