@@ -60,6 +60,12 @@ def peaks():
 
 
 # ----------------------------------------------------------- accounting
+# DRAM bytes of one C2 request launch of the prefill kernel (ncu --set full,
+# dram__bytes_read.sum 26.60 MB + dram__bytes_write.sum 1.28 MB): the K/V of the
+# request (16.8 MB) cross HBM once, plus Q, the slot table, metadata and O
+PREFILL_DRAM_BYTES_PER_LAUNCH = 27_879_424
+
+
 def attention_flops(work) -> float:
     """Algorithmic FLOPs of the attention launches of one step.
 
@@ -299,9 +305,11 @@ def main():
         clocks.mark()
     for i in range(args.steps):
         flush.fill_(i & 0xFF)
+        torch.cuda.nvtx.range_push("reuse_step")  # launch-list filter for ncu --nvtx
         ev[i][0].record(stream)
         step.run(s)
         ev[i][1].record(stream)
+        torch.cuda.nvtx.range_pop()
     barrier()
     if clocks:
         clocks.mark()
@@ -396,11 +404,15 @@ def main():
                        "parallelism": f"request-sharded x{world}"},
             "decode": {"value": decode_value, "unit": "tok/s",
                        "ms_per_step": dec_ms, "note": "one token per request over 4097 keys"},
-            "roofline": {"bound": "tensor", "kernel": "CCPE attention (all requests)",
+            "roofline": {"bound": "tensor", "kernel": "cope_prefill_sm100 (one request per launch)",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "peak_kind": pk_kind,
-                         "flops_per_launch_set": flops, "ms_per_launch_set": att_ms,
-                         "traffic": None},
+                         "flops_per_launch": flops / len(work.requests),
+                         "ms_per_launch": att_ms / len(work.requests),
+                         "launches_timed": len(work.requests) * args.steps,
+                         "traffic": PREFILL_DRAM_BYTES_PER_LAUNCH,
+                         "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum of one "
+                                         "C2 request launch (ncu --set full capture)"},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world},
