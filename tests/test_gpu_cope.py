@@ -305,7 +305,8 @@ def test_tensor_core_prefill_copy_paths_agree(cuda, layout, monkeypatch):
     from cacheslide_b200 import _native as N
     from cacheslide_b200.position import _Holder, _base_params
 
-    nq, nk, hq, hkv, d, bs = 200, 700, 8, 2, 128, 16
+    nq, nk, hq, d, bs = 200, 700, 8, 128, 16
+    hkv = 1 if layout == "sidecar" else 2  # one head: sidecar rows of a run are consecutive
     g = torch.Generator().manual_seed(41)
     q = (torch.randn(nq, hq, d, generator=g) / d ** 0.5).to(torch.bfloat16).to(cuda)
     k = (torch.randn(nk, hkv, d, generator=g) / d ** 0.5).to(torch.bfloat16).to(cuda)
@@ -320,13 +321,14 @@ def test_tensor_core_prefill_copy_paths_agree(cuda, layout, monkeypatch):
     tok = torch.arange(nk, device=cuda)
     if layout == "sidecar":
         # 640 native slots: keys 0..599 native, 600..699 in sidecar rows 0..99;
-        # keys 2 mod 8 swap sides (native slots 600.., sidecar rows 100..),
-        # so 4-key groups are all native, all sidecar or mixed
+        # in every third 16-key run, keys 2 mod 8 swap sides (native slots
+        # 600.., sidecar rows 100..), so there are 16-key runs on both sides and
+        # 4-key groups that are all native, all sidecar or mixed
         nb, cap = 40, 200
         slots = tok.clone()
         slots[600:] = nb * bs + torch.arange(nk - 600, device=cuda)
-        sw = tok[2::8]
-        slots[2::8] = torch.where(sw >= 600, 600 + (sw - 600) // 8, nb * bs + 100 + sw // 8)
+        sw = tok[(tok % 8 == 2) & ((tok // 16) % 3 == 0)]
+        slots[sw] = torch.where(sw >= 600, 600 + (sw - 600) // 8, nb * bs + 100 + sw // 8)
         slots[313] = -1
         expect_status = N.ST_SLOT_RANGE
         cache = torch.randn(nb, hkv, bs, 2 * d, generator=g).to(torch.bfloat16).to(cuda)
