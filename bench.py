@@ -330,9 +330,11 @@ def main():
            for _ in range(args.steps)]
     for i in range(args.steps):
         flush.fill_(i & 0xFF)
+        torch.cuda.nvtx.range_push("decode_step")  # launch-list filter for ncu --nvtx
         dec[i][0].record(stream)
         step.decode(s)
         dec[i][1].record(stream)
+        torch.cuda.nvtx.range_pop()
     barrier()
     clk = clocks.stop() if clocks else None
     step.check_status()

@@ -16,6 +16,8 @@
 // restriction).  Everything else reports CS_ERR_UNSUPPORTED.
 #include <math.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace cs {
@@ -317,31 +319,72 @@ __global__ void __launch_bounds__(kSplit) decode_phase2(const __grid_constant__ 
   if (bits) report(r.status, bits);
 }
 
-// combine split partials: one CTA per (query row, head)
-__global__ void decode_combine(const __grid_constant__ DecodeBatch b) {
+// combine split partials: one CTA per (query row, head).  The split weights
+// e^(m_s - M) are formed once per split, cooperatively, into shared memory
+// (chunks of kCombChunk splits), and each thread owns up to two output
+// dimensions.
+constexpr int kCombThreads = 128;
+constexpr int kCombChunk = 1024;
+static_assert(kMaxD <= 2 * kCombThreads, "two output dimensions per thread");
+
+__global__ void __launch_bounds__(kCombThreads) decode_combine(const __grid_constant__ DecodeBatch b) {
   int64_t i;
   const DecodeReq& r = request_of(b, blockIdx.x, i);
   const int h = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int nw = kCombThreads / 32;
   const int64_t rowh = i * b.hq + h;
   const int64_t nlim = causal_limit(r, r.qpos[i]);
   const int nsp = nlim > 0 ? (int)((nlim - 1) / kSplit) + 1 : 0;
+  const float* pm = r.pm + rowh * r.nsplit;
+  const float* pl = r.pl + rowh * r.nsplit;
+  const float* po = r.po + rowh * r.nsplit * (int64_t)b.dv;
+  __shared__ float wsp[kCombChunk];
+  __shared__ float red[nw];
+  float m = -INFINITY;
+  for (int s = tid; s < nsp; s += kCombThreads) m = fmaxf(m, pm[s]);
+  m = warp_max(m);
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
   float M = -INFINITY;
-  for (int s = 0; s < nsp; ++s) M = fmaxf(M, r.pm[rowh * r.nsplit + s]);
-  float L = 0.f;
-  for (int s = 0; s < nsp; ++s) {
-    const float m = r.pm[rowh * r.nsplit + s];
-    if (m > -INFINITY) L += expf(m - M) * r.pl[rowh * r.nsplit + s];
+#pragma unroll
+  for (int w = 0; w < nw; ++w) M = fmaxf(M, red[w]);
+  const int x0 = tid, x1 = tid + kCombThreads;
+  float l = 0.f, acc0 = 0.f, acc1 = 0.f;
+  for (int c0 = 0; c0 < nsp; c0 += kCombChunk) {
+    const int cn = nsp - c0 < kCombChunk ? nsp - c0 : kCombChunk;
+    __syncthreads();  // previous chunk's weights consumed (and red[] read)
+    for (int s = tid; s < cn; s += kCombThreads) {
+      const float ms = pm[c0 + s];
+      const float w = ms > -INFINITY ? expf(ms - M) : 0.f;
+      wsp[s] = w;
+      l = fmaf(w, pl[c0 + s], l);
+    }
+    __syncthreads();
+    if (x0 < b.dv) {
+#pragma unroll 8
+      for (int s = 0; s < cn; ++s) acc0 = fmaf(wsp[s], po[(int64_t)(c0 + s) * b.dv + x0], acc0);
+    }
+    if (x1 < b.dv) {
+#pragma unroll 8
+      for (int s = 0; s < cn; ++s) acc1 = fmaf(wsp[s], po[(int64_t)(c0 + s) * b.dv + x1], acc1);
+    }
   }
+  l = warp_sum(l);
+  __syncthreads();
+  if (lane == 0) red[warp] = l;
+  __syncthreads();
+  float L = 0.f;
+#pragma unroll
+  for (int w = 0; w < nw; ++w) L += red[w];
   const float inv = L > 0.f ? 1.f / L : 0.f;
   char* orow = r.out + (i * r.o_st + (int64_t)h * r.o_sh) * dtype_size(b.out_dtype);
   int32_t bits = 0;
-  for (int x = threadIdx.x; x < b.dv; x += blockDim.x) {
-    float acc = 0.f;
-    for (int s = 0; s < nsp; ++s) {
-      const float m = r.pm[rowh * r.nsplit + s];
-      if (m > -INFINITY) acc += expf(m - M) * r.po[(rowh * r.nsplit + s) * b.dv + x];
-    }
-    const float val = acc * inv;
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int x = u ? x1 : x0;
+    if (x >= b.dv) continue;
+    const float val = (u ? acc1 : acc0) * inv;
     if (!isfinite(val)) bits |= CS_ST_LOGIT_NONFINITE;
     switch (b.out_dtype) {
       case CS_F32: reinterpret_cast<float*>(orow)[x] = val; break;
@@ -350,6 +393,327 @@ __global__ void decode_combine(const __grid_constant__ DecodeBatch b) {
     }
   }
   if (bits) report(r.status, bits);
+}
+
+// ------------------------------------------------- fast path: D = DV = 128
+// 16-bit K/V rows with 8-byte aligned 4-element slices.  A warp owns 32 keys
+// of a split and reads each key row as one coalesced 256-byte line, lane l
+// holding elements 4l..4l+3 (q stays in registers).  Gates use the hardware
+// 2^x and reciprocal, identically in both phases.
+constexpr int kFastD = 128;
+
+__device__ __forceinline__ float fast_ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float fast_gate(float logit) {  // 1 / (1 + e^-logit)
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(1.f + fast_ex2(-logit * 1.4426950408889634f)));
+  return y;
+}
+
+__device__ __forceinline__ float2 unpack2(uint32_t w, __nv_bfloat16) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+__device__ __forceinline__ float2 unpack2(uint32_t w, __half) {
+  return make_float2(__half2float(__ushort_as_half((unsigned short)(w & 0xffffu))),
+                     __half2float(__ushort_as_half((unsigned short)(w >> 16))));
+}
+
+// reduce-scatter of 32 per-lane partial values: lane l ends with the sum over
+// all lanes of value l
+__device__ __forceinline__ float reduce_scatter32(float (&v)[32]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) {
+    const bool up = (lane & m) != 0;
+#pragma unroll
+    for (int k = 0; k < m; ++k) {
+      const float send = up ? v[k] : v[k + m];
+      const float keep = up ? v[k + m] : v[k];
+      v[k] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+    }
+  }
+  return v[0];
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack4(uint2 u, float (&x)[4]) {
+  const float2 a = unpack2(u.x, T{}), c = unpack2(u.y, T{});
+  x[0] = a.x; x[1] = a.y; x[2] = c.x; x[3] = c.y;
+}
+
+// lane l's 8-byte slice of the row whose address lane `src` holds (null: zeros)
+__device__ __forceinline__ uint2 slice_of(const char* row, int src, int lane) {
+  const char* p = reinterpret_cast<const char*>(
+      __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(row), src));
+  return p ? __ldg(reinterpret_cast<const uint2*>(p) + lane) : make_uint2(0u, 0u);
+}
+
+// phase 1: logits and gate totals of this split's keys for the G heads of KV
+// head g, and (split 0) the q.E tables.  Lane l resolves the slot of key
+// 32w + l; the warp then issues the 8-byte slices of all 32 key rows before
+// the first dot product, and reduces G heads x 32/G keys per reduce-scatter.
+template <typename T, int G>
+__global__ void __launch_bounds__(kSplit) decode_phase1_v(const __grid_constant__ DecodeBatch b) {
+  constexpr int KB = 32 / G;
+  const int s = blockIdx.x, g = blockIdx.y;
+  int64_t i;
+  const DecodeReq& r = request_of(b, blockIdx.z, i);
+  if (s >= r.nsplit) return;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ float gred[kSplit / 32][G];
+  __shared__ __align__(16) float qs[G][kFastD];
+  const int64_t qp = r.qpos[i];
+  const int64_t nlim = causal_limit(r, qp);
+  const int64_t kbase = (int64_t)s * kSplit + warp * 32;
+  int32_t bits = 0;
+  const char* krow = nullptr;
+  if (kbase + lane < nlim) {
+    bool ok;
+    krow = kv_row<T>(r, kbase + lane, g, false, ok, kFastD);
+    if (!ok) bits |= CS_ST_SLOT_RANGE;
+  }
+  uint2 raw[32];
+#pragma unroll
+  for (int kk = 0; kk < 32; ++kk) raw[kk] = slice_of(krow, kk, lane);
+  float q[G][4];
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh) {
+    const uint2 u = __ldg(reinterpret_cast<const uint2*>(
+        r.q + (i * r.q_st + (int64_t)(g * G + hh) * r.q_sh) * (int64_t)sizeof(T)) + lane);
+    unpack4<T>(u, q[hh]);
+  }
+  float gacc = 0.f;  // gates of head (lane % G) over the keys this lane finishes
+#pragma unroll
+  for (int kb = 0; kb < 32; kb += KB) {
+    float part[32];
+#pragma unroll
+    for (int kk = 0; kk < KB; ++kk) {
+      float kv[4];
+      unpack4<T>(raw[kb + kk], kv);
+#pragma unroll
+      for (int hh = 0; hh < G; ++hh)
+        part[kk * G + hh] = fmaf(q[hh][0], kv[0], fmaf(q[hh][1], kv[1],
+                            fmaf(q[hh][2], kv[2], q[hh][3] * kv[3])));
+    }
+    const float dot = reduce_scatter32(part);  // key kb + lane / G, head lane % G
+    const int64_t j = kbase + kb + lane / G;
+    if (j < nlim) {
+      const float l = dot * b.inv_scale;
+      if (!isfinite(l)) bits |= CS_ST_LOGIT_NONFINITE;
+      r.logits[(i * b.hq + g * G + lane % G) * r.nk_pad + j] = l;
+      gacc += fast_gate(l);
+    }
+  }
+  // gate totals per head: lanes with the same lane % G, then the warps
+#pragma unroll
+  for (int m = 16; m >= G; m >>= 1) gacc += __shfl_xor_sync(0xffffffffu, gacc, m);
+  if (lane < G) gred[warp][lane] = gacc;
+  if (s == 0 && warp == 0) {
+#pragma unroll
+    for (int hh = 0; hh < G; ++hh)
+      *reinterpret_cast<float4*>(&qs[hh][lane * 4]) = make_float4(q[hh][0], q[hh][1], q[hh][2], q[hh][3]);
+  }
+  __syncthreads();
+  if (tid < G) {
+    float tot = 0.f;
+    for (int w = kSplit / 32 - 1; w >= 0; --w) tot += gred[w][tid];
+    r.gsum[(i * b.hq + g * G + tid) * r.nsplit + s] = tot;
+  }
+  if (s == 0) {  // q.E table: T[h][p] = sum_x q[h][x] E[x][p], a thread per (h, p)
+    for (int e = tid; e < G * b.npos; e += kSplit) {
+      const int hh = e / b.npos, pp = e - hh * b.npos;
+      const float* ep = r.E + pp * r.e_sp;
+      float t0 = 0.f, t1 = 0.f;
+#pragma unroll 8
+      for (int x = 0; x < kFastD; x += 2) {
+        t0 = fmaf(qs[hh][x], ep[x * r.e_sd], t0);
+        t1 = fmaf(qs[hh][x + 1], ep[(x + 1) * r.e_sd], t1);
+      }
+      r.table[(i * b.hq + g * G + hh) * b.npos + pp] = t0 + t1;
+    }
+  }
+  bits = (int32_t)__reduce_or_sync(0xffffffffu, (unsigned)bits);
+  if (lane == 0 && bits) report(r.status, bits);
+}
+
+// phase 2: carried count, reverse scan, bias, partial softmax (thread per
+// key), then PV with warps over keys and lanes over the 128 dimensions.  The
+// V slices of the warp's keys are issued first, so their latency overlaps the
+// softmax (PRE keys in registers; the rest, for G = 8, after it).
+template <typename T, int G>
+__global__ void __launch_bounds__(kSplit) decode_phase2_v(const __grid_constant__ DecodeBatch b) {
+  constexpr int PRE = G >= 8 ? 16 : 32;
+  const int s = blockIdx.x, g = blockIdx.y;
+  int64_t i;
+  const DecodeReq& r = request_of(b, blockIdx.z, i);
+  if (s >= r.nsplit) return;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int npos = b.npos;
+  extern __shared__ __align__(16) float dyn[];
+  float* tab = dyn;                             // [G][npos]
+  float* wts = tab + ((G * npos + 3) & ~3);     // [G][kSplit] (16-byte aligned)
+  float* ored = wts + G * kSplit;               // [4 warps][G][128]
+  __shared__ float wtot[G][kSplit / 32];
+  __shared__ float carry0[G];
+  __shared__ float red[G][kSplit / 32];
+  __shared__ float mmax[G];
+  const int64_t qp = r.qpos[i];
+  const int64_t nlim = causal_limit(r, qp);
+  const int64_t base = (int64_t)s * kSplit;
+  const int64_t rowh0 = i * b.hq + (int64_t)g * G;
+  if (base >= nlim) {  // split entirely in the future: empty partial
+    if (tid < G) {
+      r.pm[(rowh0 + tid) * r.nsplit + s] = -INFINITY;
+      r.pl[(rowh0 + tid) * r.nsplit + s] = 0.f;
+    }
+    return;
+  }
+  const int64_t j = base + tid;
+  const bool live = j < nlim;
+  int32_t bits = 0;
+  const char* vrow = nullptr;
+  if (live) {
+    bool ok;
+    vrow = kv_row<T>(r, j, g, true, ok, kFastD);
+    if (!ok) bits |= CS_ST_SLOT_RANGE;
+  }
+  uint2 vraw[PRE];
+#pragma unroll
+  for (int kk = 0; kk < PRE; ++kk) vraw[kk] = slice_of(vrow, kk, lane);
+  const int last = (int)((nlim - 1) / kSplit);
+  if (tid < G) {
+    float c = 0.f;
+    for (int t = last; t > s; --t) c += r.gsum[(rowh0 + tid) * r.nsplit + t];
+    carry0[tid] = c;
+  }
+  for (int e = tid; e < G * npos; e += kSplit) tab[e] = r.table[rowh0 * npos + e];
+  float lg[G], suf[G];
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh) {
+    lg[hh] = live ? r.logits[(rowh0 + hh) * r.nk_pad + j] : 0.f;
+    float v = live ? fast_gate(lg[hh]) : 0.f;
+    // reverse inclusive scan within the warp (lane l sums lanes l..31)
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float t = __shfl_down_sync(0xffffffffu, v, o);
+      if (lane + o < 32) v += t;
+    }
+    suf[hh] = v;
+    if (lane == 0) wtot[hh][warp] = v;
+  }
+  __syncthreads();
+  const float top = (float)(npos - 1);
+  float score[G];
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh) {
+    float c = carry0[hh];
+    for (int w = kSplit / 32 - 1; w > warp; --w) c += wtot[hh][w];
+    const float R = suf[hh] + c;
+    const float pos = R < 0.f ? 0.f : (R > top ? top : R);
+    const int lo = (int)floorf(pos);
+    const int hi = lo + 1 < npos ? lo + 1 : npos - 1;
+    const float f = pos - (float)lo;
+    const float tlo = tab[hh * npos + lo];
+    score[hh] = live ? lg[hh] + (tlo + f * (tab[hh * npos + hi] - tlo)) : -INFINITY;
+    const float v = warp_max(score[hh]);
+    if (lane == 0) red[hh][warp] = v;
+  }
+  __syncthreads();
+  if (tid < G) {
+    float m = -INFINITY;
+    for (int w = 0; w < kSplit / 32; ++w) m = fmaxf(m, red[tid][w]);
+    mmax[tid] = m;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh) {
+    const float w = live ? expf(score[hh] - mmax[hh]) : 0.f;
+    wts[hh * kSplit + tid] = w;
+    const float v = warp_sum(w);
+    if (lane == 0) wtot[hh][warp] = v;
+  }
+  __syncthreads();
+  if (tid < G) {
+    float l = 0.f;
+    for (int w = 0; w < kSplit / 32; ++w) l += wtot[tid][w];
+    r.pm[(rowh0 + tid) * r.nsplit + s] = mmax[tid];
+    r.pl[(rowh0 + tid) * r.nsplit + s] = l;
+  }
+  // PV: warp w takes keys 32w..32w+31 (dead keys have weight 0 and zero
+  // slices), lane l dimensions 4l..4l+3
+  float acc[G][4];
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc[hh][k] = 0.f;
+  const float* wk = wts + warp * 32;
+#pragma unroll
+  for (int half = 0; half < 32 / PRE; ++half) {
+    if (half > 0) {
+#pragma unroll
+      for (int kk = 0; kk < PRE; ++kk) vraw[kk] = slice_of(vrow, half * PRE + kk, lane);
+    }
+#pragma unroll
+    for (int k4 = 0; k4 < PRE; k4 += 4) {
+      float4 w4[G];
+#pragma unroll
+      for (int hh = 0; hh < G; ++hh)
+        w4[hh] = *reinterpret_cast<const float4*>(wk + hh * kSplit + half * PRE + k4);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        float vv[4];
+        unpack4<T>(vraw[k4 + u], vv);
+#pragma unroll
+        for (int hh = 0; hh < G; ++hh) {
+          const float w = u == 0 ? w4[hh].x : u == 1 ? w4[hh].y : u == 2 ? w4[hh].z : w4[hh].w;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) acc[hh][k] = fmaf(w, vv[k], acc[hh][k]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh)
+    *reinterpret_cast<float4*>(ored + ((warp * G + hh) * kFastD) + lane * 4) =
+        make_float4(acc[hh][0], acc[hh][1], acc[hh][2], acc[hh][3]);
+  __syncthreads();
+  for (int e = tid; e < G * kFastD; e += kSplit) {
+    const int hh = e / kFastD, x = e - hh * kFastD;
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < kSplit / 32; ++w) t += ored[(w * G + hh) * kFastD + x];
+    r.po[((rowh0 + hh) * r.nsplit + s) * kFastD + x] = t;
+  }
+  if (bits) report(r.status, bits);
+}
+
+bool fast_decode_ok(const cs_attn_params* p) {
+  if (p->d != kFastD || p->dv != kFastD) return false;
+  const int G = p->hq / p->hkv;
+  if (G != 1 && G != 2 && G != 4 && G != 8) return false;
+  const int64_t es = 2;
+  auto al8 = [](int64_t x) { return (x % 8) == 0; };
+  if (!al8(reinterpret_cast<uintptr_t>(p->q)) || !al8(p->q_stride_tok * es) ||
+      !al8(p->q_stride_head * es))
+    return false;
+  if (p->kv_slots) {
+    const PagedView pv = PagedView::make(p->paged);
+    if (pv.se != es || !al8(reinterpret_cast<uintptr_t>(pv.cache)) || !al8(pv.sb) ||
+        !al8(pv.sh) || !al8(pv.so) || !al8(pv.head_dim * es))
+      return false;
+    if (pv.side_capacity > 0 &&
+        (pv.sse != es || !al8(reinterpret_cast<uintptr_t>(pv.side_k)) ||
+         !al8(reinterpret_cast<uintptr_t>(pv.side_v)) || !al8(pv.ssr) || !al8(pv.ssh)))
+      return false;
+  } else if (!al8(reinterpret_cast<uintptr_t>(p->k)) || !al8(reinterpret_cast<uintptr_t>(p->v)) ||
+             !al8(p->k_stride_tok * es) || !al8(p->k_stride_head * es) ||
+             !al8(p->v_stride_tok * es) || !al8(p->v_stride_head * es)) {
+    return false;
+  }
+  return true;
 }
 
 bool decode_supported(const cs_attn_params* p) {
@@ -457,16 +821,41 @@ int launch_batch(const cs_attn_params* ps, int count, char* workspace, cudaStrea
   }
   if (b.count == 0) return CS_OK;
   const dim3 grid(nsplit_max, b.hkv, rows);
-  const size_t smem2 = (size_t)(b.G * b.npos + b.G * kSplit) * sizeof(float);
-  if (smem2 > 48 * 1024) return CS_ERR_UNSUPPORTED;
-  if (p0->in_dtype == CS_BF16) {
-    decode_phase1<__nv_bfloat16><<<grid, kSplit, 0, stream>>>(b);
-    decode_phase2<__nv_bfloat16><<<grid, kSplit, smem2, stream>>>(b);
+  const size_t smem_fast =
+      (size_t)(((b.G * b.npos + 3) & ~3) + b.G * kSplit + (kSplit / 32) * b.G * kFastD) *
+      sizeof(float);
+  bool fast = smem_fast <= 48 * 1024;
+  for (int k = 0; k < count; ++k) fast = fast && (ps[k].nq == 0 || fast_decode_ok(&ps[k]));
+  if (fast) {
+    const size_t smem2 = smem_fast;
+    auto go = [&](auto tag, auto gtag) {
+      using T = decltype(tag);
+      constexpr int G = decltype(gtag)::value;
+      decode_phase1_v<T, G><<<grid, kSplit, 0, stream>>>(b);
+      decode_phase2_v<T, G><<<grid, kSplit, smem2, stream>>>(b);
+    };
+    auto by_g = [&](auto tag) {
+      switch (b.G) {
+        case 1: go(tag, std::integral_constant<int, 1>{}); break;
+        case 2: go(tag, std::integral_constant<int, 2>{}); break;
+        case 4: go(tag, std::integral_constant<int, 4>{}); break;
+        default: go(tag, std::integral_constant<int, 8>{}); break;
+      }
+    };
+    if (p0->in_dtype == CS_BF16) by_g(__nv_bfloat16{});
+    else by_g(__half{});
   } else {
-    decode_phase1<__half><<<grid, kSplit, 0, stream>>>(b);
-    decode_phase2<__half><<<grid, kSplit, smem2, stream>>>(b);
+    const size_t smem2 = (size_t)(b.G * b.npos + b.G * kSplit) * sizeof(float);
+    if (smem2 > 48 * 1024) return CS_ERR_UNSUPPORTED;
+    if (p0->in_dtype == CS_BF16) {
+      decode_phase1<__nv_bfloat16><<<grid, kSplit, 0, stream>>>(b);
+      decode_phase2<__nv_bfloat16><<<grid, kSplit, smem2, stream>>>(b);
+    } else {
+      decode_phase1<__half><<<grid, kSplit, 0, stream>>>(b);
+      decode_phase2<__half><<<grid, kSplit, smem2, stream>>>(b);
+    }
   }
-  decode_combine<<<dim3(rows, b.hq), 128, 0, stream>>>(b);
+  decode_combine<<<dim3(rows, b.hq), kCombThreads, 0, stream>>>(b);
   CS_LAUNCH_CHECK();
   return CS_OK;
 }

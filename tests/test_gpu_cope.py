@@ -433,6 +433,52 @@ def test_split_key_decode_matches_oracle_and_generic(cuda, nk, rows):
     np.testing.assert_allclose(outs[0], outs[1], **BF16)
 
 
+@pytest.mark.parametrize("hq,hkv,d,npos", [(8, 8, 128, 33), (16, 8, 128, 64), (64, 8, 128, 17),
+                                           (32, 8, 64, 64), (12, 4, 96, 40)])
+def test_split_key_decode_head_groups_and_widths(cuda, hq, hkv, d, npos):
+    """Split-key decode for 1, 2, 4 and 8 query heads per KV head, odd
+    position counts, and head widths other than 128 (the general kernels)
+    against the oracle."""
+    import ctypes
+
+    from cacheslide_b200 import _native as N
+    from cacheslide_b200.position import _Holder, _base_params
+
+    nk, bs, rows = 1000, 16, [999, 640]
+    g = torch.Generator().manual_seed(hq * 1000 + d + npos)
+    q = (torch.randn(len(rows), hq, d, generator=g) / d ** 0.5).to(torch.bfloat16).to(cuda)
+    k = (torch.randn(nk, hkv, d, generator=g) / d ** 0.5).to(torch.bfloat16).to(cuda)
+    v = torch.randn(nk, hkv, d, generator=g).to(torch.bfloat16).to(cuda)
+    E = torch.randn(d, npos, generator=g) * 0.05
+    nb = (nk + bs - 1) // bs + 3
+    perm = torch.randperm(nb, generator=g)[: (nk + bs - 1) // bs].to(cuda)
+    tok = torch.arange(nk, device=cuda)
+    slots = perm[tok // bs] * bs + tok % bs
+    cache = torch.zeros(nb, hkv, bs, 2 * d, dtype=torch.bfloat16, device=cuda)
+    cache[slots // bs, :, slots % bs, :d] = k
+    cache[slots // bs, :, slots % bs, d:] = v
+    cope = _cope(E.numpy(), cuda)
+    holder = _Holder(cope, cope.position_embeddings.detach())
+    out = torch.empty(len(rows), hq, d, dtype=torch.bfloat16, device=cuda)
+    qpos = torch.tensor(rows, device=cuda)  # held: the params keep only its pointer
+    p = _base_params(q, None, None, holder, qpos, None, nk, hkv, d)
+    p.paged = N.paged_view(cache)
+    p.kv_slots = slots.data_ptr()
+    p.out = out.data_ptr()
+    p.o_stride_tok, p.o_stride_head = out.stride(0), out.stride(1)
+    st = N.Status(cuda)
+    p.status = st.ptr
+    lib = N.load()
+    size = lib.cs_cope_attn_decode_workspace(ctypes.byref(p))
+    assert size > 0
+    ws = torch.empty(size, dtype=torch.uint8, device=cuda)
+    N.check(lib.cs_cope_attn_decode(ctypes.byref(p), ws.data_ptr(), N.stream_of(cuda)), "decode")
+    assert st.read() == 0
+    want = ocope.cope_attention(q.float().cpu().numpy(), k.float().cpu().numpy(),
+                                v.float().cpu().numpy(), E.numpy(), np.array(rows))
+    np.testing.assert_allclose(out.float().cpu().numpy(), want, **BF16)
+
+
 def test_batched_decode_matches_per_request_decode(cuda):
     """cs_cope_attn_decode_batch over requests of different context lengths
     (and more requests than one launch holds) equals decoding them one by one."""
