@@ -19,6 +19,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace cs {
 
@@ -395,167 +396,187 @@ __global__ void __launch_bounds__(kCombThreads) decode_combine(const __grid_cons
   if (bits) report(r.status, bits);
 }
 
-// ------------------------------------------------- fast path: D = DV = 128
-// 16-bit K/V rows with 8-byte aligned 4-element slices.  A warp owns 32 keys
-// of a split and reads each key row as one coalesced 256-byte line, lane l
-// holding elements 4l..4l+3 (q stays in registers).  Gates use the hardware
-// 2^x and reciprocal, identically in both phases.
+// ------------------------------------------------- tensor-core path: D = DV = 128
+// 16-bit K/V rows with 16-byte aligned 128-element records.  A CTA takes one
+// split (128 keys) of one KV head for one query row.  Thread t resolves the
+// slot of key t; the warps copy the 128 key rows (two 256-byte rows per warp
+// instruction, cp.async) into a 128-byte swizzled K-major tile, and one
+// tcgen05.mma chain computes the whole split:
+//   phase 1  S[key][h]  = K_split (M = 128 keys) x q^T (N = 16 heads, G used)
+//   phase 2  O^T[x][h]  = V_split^T (M = 128 dims, MN-major) x P^T (N = 16)
+// with the accumulator in 32 TMEM columns, read back one lane (key or
+// dimension) per thread.  Gates use the hardware 2^x and reciprocal,
+// identically in both phases.
 constexpr int kFastD = 128;
+constexpr int kTcN = 16;            // MMA N: the G query heads, zero-padded
+constexpr uint32_t kTcCols = 32;    // TMEM columns per CTA (allocation unit)
+constexpr uint32_t kTileB = 32768;  // 128 rows x 256 B
+constexpr uint32_t kSmallB = kTcN * 256;
+constexpr size_t kTcSmem = 1024 + kTileB + kSmallB;  // 1024: alignment slack
 
-__device__ __forceinline__ float fast_ex2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
 __device__ __forceinline__ float fast_gate(float logit) {  // 1 / (1 + e^-logit)
-  float y;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(1.f + fast_ex2(-logit * 1.4426950408889634f)));
-  return y;
+  return rcp_approx(1.f + ex2(-logit * 1.4426950408889634f));
 }
 
-__device__ __forceinline__ float2 unpack2(uint32_t w, __nv_bfloat16) {
-  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
-}
-__device__ __forceinline__ float2 unpack2(uint32_t w, __half) {
-  return make_float2(__half2float(__ushort_as_half((unsigned short)(w & 0xffffu))),
-                     __half2float(__ushort_as_half((unsigned short)(w >> 16))));
-}
-
-// reduce-scatter of 32 per-lane partial values: lane l ends with the sum over
-// all lanes of value l
-__device__ __forceinline__ float reduce_scatter32(float (&v)[32]) {
-  const int lane = threadIdx.x & 31;
+// rows 0..127 of the split (thread t resolved key t: `row`) into the swizzled
+// tile at `dst`; warp w copies its keys 32w..32w+31 two at a time.  Rows of
+// dead keys (null) are zero-filled from `dummy`, a valid global address.
+__device__ __forceinline__ void copy_split_rows(uint32_t dst, const char* row, const char* dummy) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
-  for (int m = 16; m >= 1; m >>= 1) {
-    const bool up = (lane & m) != 0;
-#pragma unroll
-    for (int k = 0; k < m; ++k) {
-      const float send = up ? v[k] : v[k + m];
-      const float keep = up ? v[k + m] : v[k];
-      v[k] = keep + __shfl_xor_sync(0xffffffffu, send, m);
-    }
+  for (int it = 0; it < 16; ++it) {
+    const int kl = 2 * it + (lane >> 4);
+    const char* src = reinterpret_cast<const char*>(
+        __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(row), kl));
+    const int c = lane & 15;
+    cp_async16(dst + sw128(warp * 32 + kl, c, 128), src ? src + c * 16 : dummy, src != nullptr);
   }
-  return v[0];
+}
+
+// bounded wait of every thread on the CTA's MMA barrier
+__device__ __forceinline__ bool wait_mma(uint32_t bar) {
+  const long long t0 = clock64();
+  while (!mbar_try(bar, 0)) {
+    if (clock64() - t0 > kWaitCycles) return false;
+  }
+  return true;
 }
 
 template <typename T>
-__device__ __forceinline__ void unpack4(uint2 u, float (&x)[4]) {
-  const float2 a = unpack2(u.x, T{}), c = unpack2(u.y, T{});
-  x[0] = a.x; x[1] = a.y; x[2] = c.x; x[3] = c.y;
-}
-
-// lane l's 8-byte slice of the row whose address lane `src` holds (null: zeros)
-__device__ __forceinline__ uint2 slice_of(const char* row, int src, int lane) {
-  const char* p = reinterpret_cast<const char*>(
-      __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(row), src));
-  return p ? __ldg(reinterpret_cast<const uint2*>(p) + lane) : make_uint2(0u, 0u);
+constexpr int umma_fmt() {
+  return std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
 }
 
 // phase 1: logits and gate totals of this split's keys for the G heads of KV
-// head g, and (split 0) the q.E tables.  Lane l resolves the slot of key
-// 32w + l; the warp then issues the 8-byte slices of all 32 key rows before
-// the first dot product, and reduces G heads x 32/G keys per reduce-scatter.
+// head g, and (split 0) the q.E tables
 template <typename T, int G>
-__global__ void __launch_bounds__(kSplit) decode_phase1_v(const __grid_constant__ DecodeBatch b) {
-  constexpr int KB = 32 / G;
+__global__ void __launch_bounds__(kSplit) decode_qk_tc(const __grid_constant__ DecodeBatch b) {
   const int s = blockIdx.x, g = blockIdx.y;
   int64_t i;
   const DecodeReq& r = request_of(b, blockIdx.z, i);
   if (s >= r.nsplit) return;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  extern __shared__ __align__(16) unsigned char dsm[];
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ uint32_t tslot;
   __shared__ float gred[kSplit / 32][G];
-  __shared__ __align__(16) float qs[G][kFastD];
   const int64_t qp = r.qpos[i];
   const int64_t nlim = causal_limit(r, qp);
-  const int64_t kbase = (int64_t)s * kSplit + warp * 32;
+  const int64_t base = (int64_t)s * kSplit;
+  const int64_t rowh0 = i * b.hq + (int64_t)g * G;
+  if (base >= nlim) {  // split entirely in the future: no keys, no gates
+    if (tid < G) r.gsum[(rowh0 + tid) * r.nsplit + s] = 0.f;
+    return;
+  }
+  const uint32_t sraw = smem_u32(dsm);
+  const uint32_t sK = (sraw + 1023u) & ~1023u, sQ = sK + kTileB;
+  const unsigned char* gQ = dsm + (sQ - sraw);
+  const uint32_t mb = smem_u32(&bar);
+  if (warp == 0) tmem_alloc(smem_u32(&tslot), kTcCols);
+  if (tid == 0) {
+    mbar_init(mb, 1);
+    mbar_init_fence();
+  }
+  const int64_t j = base + tid;
   int32_t bits = 0;
   const char* krow = nullptr;
-  if (kbase + lane < nlim) {
+  if (j < nlim) {
     bool ok;
-    krow = kv_row<T>(r, kbase + lane, g, false, ok, kFastD);
+    krow = kv_row<T>(r, j, g, false, ok, kFastD);
     if (!ok) bits |= CS_ST_SLOT_RANGE;
   }
-  uint2 raw[32];
+  const char* q0 = r.q + (i * r.q_st + (int64_t)g * G * r.q_sh) * (int64_t)sizeof(T);
+  copy_split_rows(sK, krow, q0);
+  for (int e = tid; e < kTcN * 16; e += kSplit) {  // q rows (heads), zero beyond G
+    const int hh = e >> 4, c = e & 15;
+    const char* src = q0 + (int64_t)hh * r.q_sh * (int64_t)sizeof(T) + c * 16;
+    cp_async16(sQ + sw128(hh, c, kTcN), hh < G ? src : q0, hh < G);
+  }
+  cp_async_wait_all();
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tslot;
+  if (tid == 0) {
+    const uint32_t idesc = umma_idesc(128, kTcN, umma_fmt<T>(), 0, 0);
 #pragma unroll
-  for (int kk = 0; kk < 32; ++kk) raw[kk] = slice_of(krow, kk, lane);
-  float q[G][4];
+    for (int kk = 0; kk < kFastD / 16; ++kk) {
+      const uint32_t ko = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
+      const uint32_t qo = (kk >> 2) * (kTcN * 128) + (kk & 3) * 32;
+      tc_mma(tmem, umma_desc(sK + ko, 16, 1024), umma_desc(sQ + qo, 16, 1024), idesc,
+             kk ? 1u : 0u);
+    }
+    tc_commit(mb);
+  }
+  const bool done = wait_mma(mb);
+  tc_fence_after();
+  uint32_t acc[16];
+  CS_TMEM_LD16(tmem + ((uint32_t)(warp * 32) << 16), acc);
+  tmem_wait_ld();
+  if (!done) bits |= CS_ST_TIMEOUT;
+  const bool live = j < nlim && done;
 #pragma unroll
   for (int hh = 0; hh < G; ++hh) {
-    const uint2 u = __ldg(reinterpret_cast<const uint2*>(
-        r.q + (i * r.q_st + (int64_t)(g * G + hh) * r.q_sh) * (int64_t)sizeof(T)) + lane);
-    unpack4<T>(u, q[hh]);
-  }
-  float gacc = 0.f;  // gates of head (lane % G) over the keys this lane finishes
-#pragma unroll
-  for (int kb = 0; kb < 32; kb += KB) {
-    float part[32];
-#pragma unroll
-    for (int kk = 0; kk < KB; ++kk) {
-      float kv[4];
-      unpack4<T>(raw[kb + kk], kv);
-#pragma unroll
-      for (int hh = 0; hh < G; ++hh)
-        part[kk * G + hh] = fmaf(q[hh][0], kv[0], fmaf(q[hh][1], kv[1],
-                            fmaf(q[hh][2], kv[2], q[hh][3] * kv[3])));
-    }
-    const float dot = reduce_scatter32(part);  // key kb + lane / G, head lane % G
-    const int64_t j = kbase + kb + lane / G;
-    if (j < nlim) {
-      const float l = dot * b.inv_scale;
+    float gt = 0.f;
+    if (live) {
+      const float l = __uint_as_float(acc[hh]) * b.inv_scale;
       if (!isfinite(l)) bits |= CS_ST_LOGIT_NONFINITE;
-      r.logits[(i * b.hq + g * G + lane % G) * r.nk_pad + j] = l;
-      gacc += fast_gate(l);
+      r.logits[(rowh0 + hh) * r.nk_pad + j] = l;
+      gt = fast_gate(l);
     }
+    gt = warp_sum(gt);
+    if (lane == 0) gred[warp][hh] = gt;
   }
-  // gate totals per head: lanes with the same lane % G, then the warps
-#pragma unroll
-  for (int m = 16; m >= G; m >>= 1) gacc += __shfl_xor_sync(0xffffffffu, gacc, m);
-  if (lane < G) gred[warp][lane] = gacc;
-  if (s == 0 && warp == 0) {
-#pragma unroll
-    for (int hh = 0; hh < G; ++hh)
-      *reinterpret_cast<float4*>(&qs[hh][lane * 4]) = make_float4(q[hh][0], q[hh][1], q[hh][2], q[hh][3]);
-  }
+  tc_fence_before();
   __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    if (!done) wait_mma(mb);  // drain before the columns are released
+    tmem_dealloc(tmem, kTcCols);
+  }
   if (tid < G) {
     float tot = 0.f;
     for (int w = kSplit / 32 - 1; w >= 0; --w) tot += gred[w][tid];
-    r.gsum[(i * b.hq + g * G + tid) * r.nsplit + s] = tot;
+    r.gsum[(rowh0 + tid) * r.nsplit + s] = tot;
   }
   if (s == 0) {  // q.E table: T[h][p] = sum_x q[h][x] E[x][p], a thread per (h, p)
     for (int e = tid; e < G * b.npos; e += kSplit) {
       const int hh = e / b.npos, pp = e - hh * b.npos;
       const float* ep = r.E + pp * r.e_sp;
       float t0 = 0.f, t1 = 0.f;
-#pragma unroll 8
-      for (int x = 0; x < kFastD; x += 2) {
-        t0 = fmaf(qs[hh][x], ep[x * r.e_sd], t0);
-        t1 = fmaf(qs[hh][x + 1], ep[(x + 1) * r.e_sd], t1);
+#pragma unroll 2
+      for (int c = 0; c < kFastD / 8; ++c) {  // q from the swizzled q tile, 8 at a time
+        const uint4 u = *reinterpret_cast<const uint4*>(gQ + sw128(hh, c, kTcN));
+        const T* qv = reinterpret_cast<const T*>(&u);
+#pragma unroll
+        for (int k = 0; k < 8; k += 2) {
+          t0 = fmaf(Elem<T>::to_f(qv[k]), ep[(c * 8 + k) * r.e_sd], t0);
+          t1 = fmaf(Elem<T>::to_f(qv[k + 1]), ep[(c * 8 + k + 1) * r.e_sd], t1);
+        }
       }
-      r.table[(i * b.hq + g * G + hh) * b.npos + pp] = t0 + t1;
+      r.table[(rowh0 + hh) * b.npos + pp] = t0 + t1;
     }
   }
   bits = (int32_t)__reduce_or_sync(0xffffffffu, (unsigned)bits);
   if (lane == 0 && bits) report(r.status, bits);
 }
 
-// phase 2: carried count, reverse scan, bias, partial softmax (thread per
-// key), then PV with warps over keys and lanes over the 128 dimensions.  The
-// V slices of the warp's keys are issued first, so their latency overlaps the
-// softmax (PRE keys in registers; the rest, for G = 8, after it).
+// phase 2: carried count, reverse scan, bias and partial softmax (thread per
+// key), P^T into shared memory as 16-bit weights (the row sums are taken over
+// the same rounded weights), then O^T = V^T P^T on the tensor cores.  The V
+// rows are copied before the softmax so their latency overlaps it.
 template <typename T, int G>
-__global__ void __launch_bounds__(kSplit) decode_phase2_v(const __grid_constant__ DecodeBatch b) {
-  constexpr int PRE = G >= 8 ? 16 : 32;
+__global__ void __launch_bounds__(kSplit) decode_pv_tc(const __grid_constant__ DecodeBatch b) {
   const int s = blockIdx.x, g = blockIdx.y;
   int64_t i;
   const DecodeReq& r = request_of(b, blockIdx.z, i);
   if (s >= r.nsplit) return;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int npos = b.npos;
-  extern __shared__ __align__(16) float dyn[];
-  float* tab = dyn;                             // [G][npos]
-  float* wts = tab + ((G * npos + 3) & ~3);     // [G][kSplit] (16-byte aligned)
-  float* ored = wts + G * kSplit;               // [4 warps][G][128]
+  extern __shared__ __align__(16) unsigned char dsm[];
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ uint32_t tslot;
   __shared__ float wtot[G][kSplit / 32];
   __shared__ float carry0[G];
   __shared__ float red[G][kSplit / 32];
@@ -571,6 +592,16 @@ __global__ void __launch_bounds__(kSplit) decode_phase2_v(const __grid_constant_
     }
     return;
   }
+  const uint32_t sraw = smem_u32(dsm);
+  const uint32_t sV = (sraw + 1023u) & ~1023u, sP = sV + kTileB;
+  unsigned char* gP = dsm + (sP - sraw);
+  float* tab = reinterpret_cast<float*>(gP + kSmallB);  // [G][npos]
+  const uint32_t mb = smem_u32(&bar);
+  if (warp == 0) tmem_alloc(smem_u32(&tslot), kTcCols);
+  if (tid == 0) {
+    mbar_init(mb, 1);
+    mbar_init_fence();
+  }
   const int64_t j = base + tid;
   const bool live = j < nlim;
   int32_t bits = 0;
@@ -580,9 +611,7 @@ __global__ void __launch_bounds__(kSplit) decode_phase2_v(const __grid_constant_
     vrow = kv_row<T>(r, j, g, true, ok, kFastD);
     if (!ok) bits |= CS_ST_SLOT_RANGE;
   }
-  uint2 vraw[PRE];
-#pragma unroll
-  for (int kk = 0; kk < PRE; ++kk) vraw[kk] = slice_of(vrow, kk, lane);
+  copy_split_rows(sV, vrow, reinterpret_cast<const char*>(r.logits));
   const int last = (int)((nlim - 1) / kSplit);
   if (tid < G) {
     float c = 0.f;
@@ -590,6 +619,8 @@ __global__ void __launch_bounds__(kSplit) decode_phase2_v(const __grid_constant_
     carry0[tid] = c;
   }
   for (int e = tid; e < G * npos; e += kSplit) tab[e] = r.table[rowh0 * npos + e];
+  for (int e = tid; e < (kTcN - G) * 16; e += kSplit)  // P rows beyond G: zero
+    *reinterpret_cast<uint4*>(gP + sw128(G + (e >> 4), e & 15, kTcN)) = make_uint4(0, 0, 0, 0);
   float lg[G], suf[G];
 #pragma unroll
   for (int hh = 0; hh < G; ++hh) {
@@ -630,87 +661,76 @@ __global__ void __launch_bounds__(kSplit) decode_phase2_v(const __grid_constant_
   __syncthreads();
 #pragma unroll
   for (int hh = 0; hh < G; ++hh) {
-    const float w = live ? expf(score[hh] - mmax[hh]) : 0.f;
-    wts[hh * kSplit + tid] = w;
-    const float v = warp_sum(w);
+    const T wq = Elem<T>::from_f(live ? expf(score[hh] - mmax[hh]) : 0.f);
+    *reinterpret_cast<T*>(gP + sw128(hh, tid >> 3, kTcN) + (tid & 7) * 2) = wq;
+    const float v = warp_sum(Elem<T>::to_f(wq));
     if (lane == 0) wtot[hh][warp] = v;
   }
+  cp_async_wait_all();
+  fence_async_smem();
+  tc_fence_before();
   __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tslot;
+  if (tid == 0) {
+    const uint32_t idesc = umma_idesc(128, kTcN, umma_fmt<T>(), 1, 0);  // A = V^T, MN-major
+#pragma unroll
+    for (int kk = 0; kk < kSplit / 16; ++kk) {
+      const uint32_t po = (kk >> 2) * (kTcN * 128) + (kk & 3) * 32;
+      tc_mma(tmem, umma_desc(sV + kk * 2048, 16384, 1024), umma_desc(sP + po, 16, 1024), idesc,
+             kk ? 1u : 0u);
+    }
+    tc_commit(mb);
+  }
   if (tid < G) {
     float l = 0.f;
     for (int w = 0; w < kSplit / 32; ++w) l += wtot[tid][w];
     r.pm[(rowh0 + tid) * r.nsplit + s] = mmax[tid];
     r.pl[(rowh0 + tid) * r.nsplit + s] = l;
   }
-  // PV: warp w takes keys 32w..32w+31 (dead keys have weight 0 and zero
-  // slices), lane l dimensions 4l..4l+3
-  float acc[G][4];
+  const bool done = wait_mma(mb);
+  tc_fence_after();
+  uint32_t acc[16];
+  CS_TMEM_LD16(tmem + ((uint32_t)(warp * 32) << 16), acc);
+  tmem_wait_ld();
+  if (!done) bits |= CS_ST_TIMEOUT;
 #pragma unroll
   for (int hh = 0; hh < G; ++hh)
-#pragma unroll
-    for (int k = 0; k < 4; ++k) acc[hh][k] = 0.f;
-  const float* wk = wts + warp * 32;
-#pragma unroll
-  for (int half = 0; half < 32 / PRE; ++half) {
-    if (half > 0) {
-#pragma unroll
-      for (int kk = 0; kk < PRE; ++kk) vraw[kk] = slice_of(vrow, half * PRE + kk, lane);
-    }
-#pragma unroll
-    for (int k4 = 0; k4 < PRE; k4 += 4) {
-      float4 w4[G];
-#pragma unroll
-      for (int hh = 0; hh < G; ++hh)
-        w4[hh] = *reinterpret_cast<const float4*>(wk + hh * kSplit + half * PRE + k4);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        float vv[4];
-        unpack4<T>(vraw[k4 + u], vv);
-#pragma unroll
-        for (int hh = 0; hh < G; ++hh) {
-          const float w = u == 0 ? w4[hh].x : u == 1 ? w4[hh].y : u == 2 ? w4[hh].z : w4[hh].w;
-#pragma unroll
-          for (int k = 0; k < 4; ++k) acc[hh][k] = fmaf(w, vv[k], acc[hh][k]);
-        }
-      }
-    }
-  }
-#pragma unroll
-  for (int hh = 0; hh < G; ++hh)
-    *reinterpret_cast<float4*>(ored + ((warp * G + hh) * kFastD) + lane * 4) =
-        make_float4(acc[hh][0], acc[hh][1], acc[hh][2], acc[hh][3]);
+    r.po[((rowh0 + hh) * r.nsplit + s) * kFastD + tid] = __uint_as_float(acc[hh]);
+  tc_fence_before();
   __syncthreads();
-  for (int e = tid; e < G * kFastD; e += kSplit) {
-    const int hh = e / kFastD, x = e - hh * kFastD;
-    float t = 0.f;
-#pragma unroll
-    for (int w = 0; w < kSplit / 32; ++w) t += ored[(w * G + hh) * kFastD + x];
-    r.po[((rowh0 + hh) * r.nsplit + s) * kFastD + x] = t;
+  if (warp == 0) {
+    tc_fence_after();
+    if (!done) wait_mma(mb);
+    tmem_dealloc(tmem, kTcCols);
   }
-  if (bits) report(r.status, bits);
+  bits = (int32_t)__reduce_or_sync(0xffffffffu, (unsigned)bits);
+  if (lane == 0 && bits) report(r.status, bits);
 }
 
+// whether the tensor-core kernels take this request: 128-element 16-bit
+// records whose rows start on 16-byte boundaries (cp.async), G in {1,2,4,8}
 bool fast_decode_ok(const cs_attn_params* p) {
   if (p->d != kFastD || p->dv != kFastD) return false;
   const int G = p->hq / p->hkv;
   if (G != 1 && G != 2 && G != 4 && G != 8) return false;
   const int64_t es = 2;
-  auto al8 = [](int64_t x) { return (x % 8) == 0; };
-  if (!al8(reinterpret_cast<uintptr_t>(p->q)) || !al8(p->q_stride_tok * es) ||
-      !al8(p->q_stride_head * es))
+  auto al16 = [](int64_t x) { return (x % 16) == 0; };
+  if (!al16(reinterpret_cast<uintptr_t>(p->q)) || !al16(p->q_stride_tok * es) ||
+      !al16(p->q_stride_head * es))
     return false;
   if (p->kv_slots) {
     const PagedView pv = PagedView::make(p->paged);
-    if (pv.se != es || !al8(reinterpret_cast<uintptr_t>(pv.cache)) || !al8(pv.sb) ||
-        !al8(pv.sh) || !al8(pv.so) || !al8(pv.head_dim * es))
+    if (pv.se != es || !al16(reinterpret_cast<uintptr_t>(pv.cache)) || !al16(pv.sb) ||
+        !al16(pv.sh) || !al16(pv.so) || !al16(pv.head_dim * es))
       return false;
     if (pv.side_capacity > 0 &&
-        (pv.sse != es || !al8(reinterpret_cast<uintptr_t>(pv.side_k)) ||
-         !al8(reinterpret_cast<uintptr_t>(pv.side_v)) || !al8(pv.ssr) || !al8(pv.ssh)))
+        (pv.sse != es || !al16(reinterpret_cast<uintptr_t>(pv.side_k)) ||
+         !al16(reinterpret_cast<uintptr_t>(pv.side_v)) || !al16(pv.ssr) || !al16(pv.ssh)))
       return false;
-  } else if (!al8(reinterpret_cast<uintptr_t>(p->k)) || !al8(reinterpret_cast<uintptr_t>(p->v)) ||
-             !al8(p->k_stride_tok * es) || !al8(p->k_stride_head * es) ||
-             !al8(p->v_stride_tok * es) || !al8(p->v_stride_head * es)) {
+  } else if (!al16(reinterpret_cast<uintptr_t>(p->k)) || !al16(reinterpret_cast<uintptr_t>(p->v)) ||
+             !al16(p->k_stride_tok * es) || !al16(p->k_stride_head * es) ||
+             !al16(p->v_stride_tok * es) || !al16(p->v_stride_head * es)) {
     return false;
   }
   return true;
@@ -821,18 +841,15 @@ int launch_batch(const cs_attn_params* ps, int count, char* workspace, cudaStrea
   }
   if (b.count == 0) return CS_OK;
   const dim3 grid(nsplit_max, b.hkv, rows);
-  const size_t smem_fast =
-      (size_t)(((b.G * b.npos + 3) & ~3) + b.G * kSplit + (kSplit / 32) * b.G * kFastD) *
-      sizeof(float);
-  bool fast = smem_fast <= 48 * 1024;
+  const size_t smem_pv = kTcSmem + (size_t)b.G * b.npos * sizeof(float);
+  bool fast = smem_pv <= 48 * 1024;
   for (int k = 0; k < count; ++k) fast = fast && (ps[k].nq == 0 || fast_decode_ok(&ps[k]));
   if (fast) {
-    const size_t smem2 = smem_fast;
     auto go = [&](auto tag, auto gtag) {
       using T = decltype(tag);
       constexpr int G = decltype(gtag)::value;
-      decode_phase1_v<T, G><<<grid, kSplit, 0, stream>>>(b);
-      decode_phase2_v<T, G><<<grid, kSplit, smem2, stream>>>(b);
+      decode_qk_tc<T, G><<<grid, kSplit, kTcSmem, stream>>>(b);
+      decode_pv_tc<T, G><<<grid, kSplit, smem_pv, stream>>>(b);
     };
     auto by_g = [&](auto tag) {
       switch (b.G) {
