@@ -5,11 +5,12 @@
 // so a key split cannot finish on its own: phase 1 computes every split's
 // logits and gate totals (reading K once), phase 2 gives each split the count
 // carried from the newer splits, finishes the reverse scan, the interpolated
-// bias and a partial softmax with its PV (reading V once), and a combine
-// kernel merges the split partials.  K and V each cross HBM once; the logits
-// and partials (a few hundred KB per row) stay in L2.  All requests of a
-// batch share the three launches, so a decode step of a whole batch costs
-// three kernel launches instead of three per request.
+// bias and a partial softmax with its PV (reading V once), and the split
+// partials are merged: on the tensor-core path (128-element heads) by the
+// last split of each (row, KV head) to finish, elsewhere by a combine kernel.
+// K and V each cross HBM once; the logits and partials (a few hundred KB per
+// row) stay in L2.  All requests of a batch share the launches, so a decode
+// step of a whole batch costs two (three) kernel launches, not per request.
 //
 // Modes: contextual positions, plain causal (the decode row of a CacheSlide
 // request is a dynamic token: no canonical substitution, no association
@@ -54,6 +55,7 @@ struct DecodeReq {
   float* po;      // [nq][hq][nsplit][dv]
   float* pm;      // [nq][hq][nsplit]
   float* pl;      // [nq][hq][nsplit]
+  int* cnt;       // [nq][hkv] finished splits (tensor-core path), zeroed by phase 1
   int nq, nk, nsplit, nk_pad, row0;
 };
 
@@ -451,11 +453,15 @@ constexpr int umma_fmt() {
 // head g, and (split 0) the q.E tables
 template <typename T, int G>
 __global__ void __launch_bounds__(kSplit) decode_qk_tc(const __grid_constant__ DecodeBatch b) {
+  // phase 2 may be scheduled once every CTA of this grid has started; it
+  // waits for this grid's completion before it reads what this grid writes
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int s = blockIdx.x, g = blockIdx.y;
   int64_t i;
   const DecodeReq& r = request_of(b, blockIdx.z, i);
   if (s >= r.nsplit) return;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (s == 0 && tid == 0) r.cnt[i * b.hkv + g] = 0;  // arrivals of phase 2
   extern __shared__ __align__(16) unsigned char dsm[];
   __shared__ __align__(8) uint64_t bar;
   __shared__ uint32_t tslot;
@@ -562,10 +568,87 @@ __global__ void __launch_bounds__(kSplit) decode_qk_tc(const __grid_constant__ D
   if (lane == 0 && bits) report(r.status, bits);
 }
 
+// Merge the split partials of the G heads of (row i, KV head g) into the
+// output rows.  Warp w finds the maximum M and the weights e^(m_s - M) of
+// heads w, w+4, ... (chunks of kCombChunk / G splits in shared memory);
+// thread x then accumulates output dimension x of all G heads at once.
+// Partials written by other CTAs are read through L2.
+template <int G>
+__device__ void combine_heads(const DecodeBatch& b, const DecodeReq& r, int64_t i, int g,
+                              int nsp, float* wsp, float* lsum, int32_t& bits) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int nw = kSplit / 32;
+  constexpr int CH = kCombChunk / G;  // splits per chunk
+  const int64_t rowh0 = i * b.hq + (int64_t)g * G;
+  float M[(G + nw - 1) / nw], l[(G + nw - 1) / nw];
+#pragma unroll
+  for (int k = 0; k * nw < G; ++k) {
+    const int hh = warp + k * nw;
+    M[k] = -INFINITY;
+    l[k] = 0.f;
+    if (hh < G) {
+      const float* pm = r.pm + (rowh0 + hh) * r.nsplit;
+      float m = -INFINITY;
+      for (int s = lane; s < nsp; s += 32) m = fmaxf(m, __ldcg(pm + s));
+      M[k] = warp_max(m);
+    }
+  }
+  float acc[G];
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh) acc[hh] = 0.f;
+  for (int c0 = 0; c0 < nsp; c0 += CH) {
+    const int cn = nsp - c0 < CH ? nsp - c0 : CH;
+    __syncthreads();  // previous chunk's weights consumed
+#pragma unroll
+    for (int k = 0; k * nw < G; ++k) {
+      const int hh = warp + k * nw;
+      if (hh >= G) continue;
+      const float* pm = r.pm + (rowh0 + hh) * r.nsplit + c0;
+      const float* pl = r.pl + (rowh0 + hh) * r.nsplit + c0;
+      for (int s = lane; s < cn; s += 32) {
+        const float ms = __ldcg(pm + s);
+        const float w = ms > -INFINITY ? expf(ms - M[k]) : 0.f;
+        wsp[hh * CH + s] = w;
+        l[k] = fmaf(w, __ldcg(pl + s), l[k]);
+      }
+    }
+    __syncthreads();
+    const float* po = r.po + (rowh0 * r.nsplit + c0) * (int64_t)kFastD + tid;
+#pragma unroll 4
+    for (int s = 0; s < cn; ++s) {
+#pragma unroll
+      for (int hh = 0; hh < G; ++hh)
+        acc[hh] = fmaf(wsp[hh * CH + s], __ldcg(po + ((int64_t)hh * r.nsplit + s) * kFastD),
+                       acc[hh]);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k * nw < G; ++k) {
+    const int hh = warp + k * nw;
+    const float v = warp_sum(l[k]);
+    if (hh < G && lane == 0) lsum[hh] = v;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh) {
+    const float L = lsum[hh];
+    const float val = acc[hh] * (L > 0.f ? 1.f / L : 0.f);
+    if (!isfinite(val)) bits |= CS_ST_LOGIT_NONFINITE;
+    char* orow = r.out + (i * r.o_st + (int64_t)(g * G + hh) * r.o_sh) * dtype_size(b.out_dtype);
+    switch (b.out_dtype) {
+      case CS_F32: reinterpret_cast<float*>(orow)[tid] = val; break;
+      case CS_F16: reinterpret_cast<__half*>(orow)[tid] = __float2half_rn(val); break;
+      default: reinterpret_cast<__nv_bfloat16*>(orow)[tid] = __float2bfloat16_rn(val); break;
+    }
+  }
+}
+
 // phase 2: carried count, reverse scan, bias and partial softmax (thread per
 // key), P^T into shared memory as 16-bit weights (the row sums are taken over
 // the same rounded weights), then O^T = V^T P^T on the tensor cores.  The V
-// rows are copied before the softmax so their latency overlaps it.
+// rows are copied first, before the wait for phase 1, so their latency
+// overlaps the end of phase 1 and the softmax.  The last split of (row, KV
+// head) to finish merges all splits into the output rows.
 template <typename T, int G>
 __global__ void __launch_bounds__(kSplit) decode_pv_tc(const __grid_constant__ DecodeBatch b) {
   const int s = blockIdx.x, g = blockIdx.y;
@@ -581,14 +664,24 @@ __global__ void __launch_bounds__(kSplit) decode_pv_tc(const __grid_constant__ D
   __shared__ float carry0[G];
   __shared__ float red[G][kSplit / 32];
   __shared__ float mmax[G];
+  __shared__ float wsp[kCombChunk];
+  __shared__ int last_split;
   const int64_t qp = r.qpos[i];
   const int64_t nlim = causal_limit(r, qp);
   const int64_t base = (int64_t)s * kSplit;
   const int64_t rowh0 = i * b.hq + (int64_t)g * G;
-  if (base >= nlim) {  // split entirely in the future: empty partial
-    if (tid < G) {
-      r.pm[(rowh0 + tid) * r.nsplit + s] = -INFINITY;
-      r.pl[(rowh0 + tid) * r.nsplit + s] = 0.f;
+  if (base >= nlim) {  // split entirely in the future: no partial
+    if (s == 0) {      // no visible key at all: zero output rows
+      for (int e = tid; e < G * kFastD; e += kSplit) {
+        char* orow = r.out + (i * r.o_st + (int64_t)(g * G + e / kFastD) * r.o_sh) *
+                                 dtype_size(b.out_dtype);
+        const int x = e % kFastD;
+        switch (b.out_dtype) {
+          case CS_F32: reinterpret_cast<float*>(orow)[x] = 0.f; break;
+          case CS_F16: reinterpret_cast<__half*>(orow)[x] = __float2half_rn(0.f); break;
+          default: reinterpret_cast<__nv_bfloat16*>(orow)[x] = __float2bfloat16_rn(0.f); break;
+        }
+      }
     }
     return;
   }
@@ -612,6 +705,9 @@ __global__ void __launch_bounds__(kSplit) decode_pv_tc(const __grid_constant__ D
     if (!ok) bits |= CS_ST_SLOT_RANGE;
   }
   copy_split_rows(sV, vrow, reinterpret_cast<const char*>(r.logits));
+  for (int e = tid; e < (kTcN - G) * 16; e += kSplit)  // P rows beyond G: zero
+    *reinterpret_cast<uint4*>(gP + sw128(G + (e >> 4), e & 15, kTcN)) = make_uint4(0, 0, 0, 0);
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // phase 1 complete and visible
   const int last = (int)((nlim - 1) / kSplit);
   if (tid < G) {
     float c = 0.f;
@@ -619,8 +715,6 @@ __global__ void __launch_bounds__(kSplit) decode_pv_tc(const __grid_constant__ D
     carry0[tid] = c;
   }
   for (int e = tid; e < G * npos; e += kSplit) tab[e] = r.table[rowh0 * npos + e];
-  for (int e = tid; e < (kTcN - G) * 16; e += kSplit)  // P rows beyond G: zero
-    *reinterpret_cast<uint4*>(gP + sw128(G + (e >> 4), e & 15, kTcN)) = make_uint4(0, 0, 0, 0);
   float lg[G], suf[G];
 #pragma unroll
   for (int hh = 0; hh < G; ++hh) {
@@ -697,12 +791,21 @@ __global__ void __launch_bounds__(kSplit) decode_pv_tc(const __grid_constant__ D
 #pragma unroll
   for (int hh = 0; hh < G; ++hh)
     r.po[((rowh0 + hh) * r.nsplit + s) * kFastD + tid] = __uint_as_float(acc[hh]);
+  __threadfence();  // this split's partial is visible before its arrival is counted
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
     if (!done) wait_mma(mb);
     tmem_dealloc(tmem, kTcCols);
+  }
+  const int nsp = last + 1;  // splits with visible keys
+  if (tid == 0) last_split = atomicAdd(&r.cnt[i * b.hkv + g], 1) == nsp - 1;
+  __syncthreads();
+  if (last_split) {
+    __threadfence();
+    combine_heads<G>(b, r, i, g, nsp, wsp, mmax, bits);
+    if (tid == 0) r.cnt[i * b.hkv + g] = 0;
   }
   bits = (int32_t)__reduce_or_sync(0xffffffffu, (unsigned)bits);
   if (lane == 0 && bits) report(r.status, bits);
@@ -751,7 +854,7 @@ bool decode_supported(const cs_attn_params* p) {
 
 struct Layout {
   int nsplit, nk_pad;
-  int64_t logits, gsum, table, po, pm, pl, total;  // float offsets / count
+  int64_t logits, gsum, table, po, pm, pl, cnt, total;  // 4-byte offsets / count
 };
 
 Layout layout_of(const cs_attn_params* p) {
@@ -771,6 +874,7 @@ Layout layout_of(const cs_attn_params* p) {
   L.po = take(rows * L.nsplit * p->dv);
   L.pm = take(rows * L.nsplit);
   L.pl = take(rows * L.nsplit);
+  L.cnt = take((int64_t)p->nq * p->hkv);
   L.total = off;
   return L;
 }
@@ -808,6 +912,7 @@ void fill_request(DecodeReq& q, const cs_attn_params* p, float* ws, const Layout
   q.po = ws + L.po;
   q.pm = ws + L.pm;
   q.pl = ws + L.pl;
+  q.cnt = reinterpret_cast<int*>(ws + L.cnt);
   q.nq = p->nq;
   q.nk = p->nk;
   q.nsplit = L.nsplit;
@@ -845,11 +950,24 @@ int launch_batch(const cs_attn_params* ps, int count, char* workspace, cudaStrea
   bool fast = smem_pv <= 48 * 1024;
   for (int k = 0; k < count; ++k) fast = fast && (ps[k].nq == 0 || fast_decode_ok(&ps[k]));
   if (fast) {
+    // phase 2 is a programmatic dependent launch: its CTAs may start (and
+    // issue their V copies) while the last CTAs of phase 1 run
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kSplit);
+    cfg.dynamicSmemBytes = smem_pv;
+    cfg.stream = stream;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    cudaError_t err = cudaSuccess;
     auto go = [&](auto tag, auto gtag) {
       using T = decltype(tag);
       constexpr int G = decltype(gtag)::value;
       decode_qk_tc<T, G><<<grid, kSplit, kTcSmem, stream>>>(b);
-      decode_pv_tc<T, G><<<grid, kSplit, smem_pv, stream>>>(b);
+      err = cudaLaunchKernelEx(&cfg, decode_pv_tc<T, G>, b);
     };
     auto by_g = [&](auto tag) {
       switch (b.G) {
@@ -861,6 +979,7 @@ int launch_batch(const cs_attn_params* ps, int count, char* workspace, cudaStrea
     };
     if (p0->in_dtype == CS_BF16) by_g(__nv_bfloat16{});
     else by_g(__half{});
+    if (err != cudaSuccess) return CS_ERR_CUDA;
   } else {
     const size_t smem2 = (size_t)(b.G * b.npos + b.G * kSplit) * sizeof(float);
     if (smem2 > 48 * 1024) return CS_ERR_UNSUPPORTED;
@@ -871,8 +990,8 @@ int launch_batch(const cs_attn_params* ps, int count, char* workspace, cudaStrea
       decode_phase1<__half><<<grid, kSplit, 0, stream>>>(b);
       decode_phase2<__half><<<grid, kSplit, smem2, stream>>>(b);
     }
+    decode_combine<<<dim3(rows, b.hq), kCombThreads, 0, stream>>>(b);
   }
-  decode_combine<<<dim3(rows, b.hq), kCombThreads, 0, stream>>>(b);
   CS_LAUNCH_CHECK();
   return CS_OK;
 }

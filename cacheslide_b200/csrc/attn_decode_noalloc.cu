@@ -9,7 +9,7 @@
 // or stall the step behind an implicit device synchronisation.  Hosts that
 // bind the C ABI from another language may also have no handle to a CUDA
 // allocator at all.  cs_cope_attn_decode_noalloc serves them: it runs the same
-// three kernels as cs_cope_attn_decode, with the workspace carved out of
+// kernels as cs_cope_attn_decode, with the workspace carved out of
 // kScratchBytes of static device memory that every GPU loading this library
 // holds until the process exits.
 #include <mutex>
