@@ -70,8 +70,6 @@ constexpr uint32_t kBarPV = 72;     // [2] MMA -> all: PV tile done
 constexpr uint32_t kBarEnd = 88;    // MMA drain
 constexpr uint32_t kTmemSlot = 96;  // TMEM base address
 constexpr uint32_t kAbort = 100;    // abort flag
-constexpr uint32_t kNtile = 104;    // key tiles of this CTA
-constexpr uint32_t kNmax = 108;     // keys needed by the furthest row of this CTA
 constexpr uint32_t kFixMask = 112;  // [4 slots][4 words] key is fixed
 constexpr uint32_t kBndMask = 176;  // [4 slots][4 words] key is the last of its chunk
 constexpr uint32_t kBarMeta = 240;  // [4] producer -> softmax: key metadata of slot it % 4
@@ -84,8 +82,9 @@ constexpr uint32_t kBndKc = 1808;   // [4 slots][4 chunks] int: chunk id of the 
 // another finishes tile it (never further: S(it+2) needs PV(it)); alternating
 // barriers keep those arrivals out of tile it's count.
 constexpr uint32_t kBarP = 1872;
-constexpr uint32_t kMetaBytes = kBarP + 16;
-constexpr uint32_t kSmemBytes = kMeta + kMetaBytes;  // 231,264 B (limit 232,448)
+constexpr uint32_t kRedN = kBarP + 16;  // [4] int64: per-warp key needs of the tile's rows
+constexpr uint32_t kMetaBytes = kRedN + 32;
+constexpr uint32_t kSmemBytes = kMeta + kMetaBytes;  // 231,296 B (limit 232,448)
 
 // TMEM columns: S double buffer, O, the q.E table (read once into shared
 // memory) and, from then on, the per-row counts of a contextual tile (kColR
@@ -162,6 +161,14 @@ template <> struct Pack2<__half> {
     return *reinterpret_cast<uint32_t*>(&v);
   }
 };
+// packed pair -> (lo, hi)
+__device__ __forceinline__ float2 unpack2(uint32_t w, __nv_bfloat16) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+__device__ __forceinline__ float2 unpack2(uint32_t w, __half) {
+  return make_float2(__half2float(__ushort_as_half((unsigned short)(w & 0xffffu))),
+                     __half2float(__ushort_as_half((unsigned short)(w >> 16))));
+}
 
 struct Args {
   // K/V row maps of the TMA path (2-D: row x element, 128-byte swizzle):
@@ -230,6 +237,67 @@ __device__ __forceinline__ const char* value_row_addr(const Args& a, uint64_t ka
          (j * p.v_stride_tok + (int64_t)g * p.v_stride_head) * (int64_t)sizeof(T);
 }
 
+// E^T split into bf16/f16 hi + lo in the swizzled B-operand layout of
+// T = Q E (row = position p, K = dimension), shared by the 384 producer and
+// softmax threads (`t` = 0..383).  When E's positions are contiguous and
+// 16-byte aligned a thread takes 4 positions x 8 dimensions: eight float4
+// loads, then one 16-byte shared store per position for hi and for lo.
+// Otherwise one element per step, all of a thread's loads issued before its
+// stores (the stores could alias the loads as far as the compiler knows).
+template <typename T>
+__device__ __forceinline__ void stage_e_split(uint8_t* smem, const cs_attn_params& p, int t) {
+  const float* E = static_cast<const float*>(p.E);
+  const bool vec = p.e_stride_p == 1 && p.npos % 4 == 0 && p.e_stride_d % 4 == 0 &&
+                   (reinterpret_cast<uintptr_t>(E) & 15) == 0;
+  if (vec) {
+    constexpr int kUnits = (kMaxNpos / 4) * (kD / 8);  // 256
+    if (t >= kUnits) return;
+    const int p0 = (t % (kMaxNpos / 4)) * 4, d0 = (t / (kMaxNpos / 4)) * 8;
+    float4 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      v[j] = p0 < p.npos ? __ldg(reinterpret_cast<const float4*>(E + (int64_t)(d0 + j) * p.e_stride_d + p0))
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint32_t hw[4], lw[4];
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        const float e0 = q == 0 ? v[j].x : q == 1 ? v[j].y : q == 2 ? v[j].z : v[j].w;
+        const float e1 = q == 0 ? v[j + 1].x : q == 1 ? v[j + 1].y : q == 2 ? v[j + 1].z : v[j + 1].w;
+        const float h0 = Elem<T>::to_f(Elem<T>::from_f(e0)), h1 = Elem<T>::to_f(Elem<T>::from_f(e1));
+        hw[j / 2] = Pack2<T>::pack(h0, h1);
+        lw[j / 2] = Pack2<T>::pack(e0 - h0, e1 - h1);
+      }
+      const uint32_t off = sw128(p0 + q, d0 >> 3, kMaxNpos);
+      *reinterpret_cast<uint4*>(smem + kP + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *reinterpret_cast<uint4*>(smem + kP + 16384 + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
+    return;
+  }
+  constexpr int kN = kMaxNpos * kD, kThr = 384, kPer = (kN + kThr - 1) / kThr;
+  float ev[kPer];
+#pragma unroll
+  for (int u = 0; u < kPer; ++u) {
+    const int idx = u * kThr + t;
+    const int dd = idx / kMaxNpos, pp = idx - dd * kMaxNpos;  // consecutive threads: consecutive p
+    ev[u] = idx < kN && pp < p.npos
+                ? __ldg(E + (int64_t)dd * p.e_stride_d + (int64_t)pp * p.e_stride_p)
+                : 0.f;
+  }
+#pragma unroll
+  for (int u = 0; u < kPer; ++u) {
+    const int idx = u * kThr + t;
+    if (idx >= kN) break;
+    const int dd = idx / kMaxNpos, pp = idx - dd * kMaxNpos;
+    const T hi = Elem<T>::from_f(ev[u]);
+    const T lo = Elem<T>::from_f(ev[u] - Elem<T>::to_f(hi));
+    const uint32_t off = sw128(pp, dd >> 3, kMaxNpos) + (dd & 7) * 2;
+    *reinterpret_cast<T*>(smem + kP + off) = hi;
+    *reinterpret_cast<T*>(smem + kP + 16384 + off) = lo;
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_constant__ Args a) {
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -253,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
   const float top = (float)(p.npos - 1);
 
   if (tid == 0) {
-    mbar_init(mb + kBarQ, 128);
+    mbar_init(mb + kBarQ, 384);  // Q copies (producer) + E split (producer and softmax)
     mbar_init(mb + kBarT, 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(mb + kBarK + 8 * s, 128);  // one copy-completion arrival per producer thread
@@ -265,18 +333,45 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
     for (int s = 0; s < 2; ++s) mbar_init(mb + kBarP + 8 * s, 256);  // both halves of every row
     mbar_init(mb + kBarEnd, 1);
     *abort = 0;
-    int64_t nmax = 0;  // keys needed by the furthest row of this tile
-    for (int r = 0; r < R; ++r) {
-      const int64_t i = i0 + r;
-      if (i >= p.nq) break;
-      const int64_t qp = p.qpos[i];
-      const int64_t n = qp + 1 < p.nk ? qp + 1 : p.nk;
-      nmax = n > nmax ? n : nmax;
-    }
-    *reinterpret_cast<int*>(meta + kNtile) = (int)((nmax + kTileN - 1) / kTileN);
-    *reinterpret_cast<int*>(meta + kNmax) = (int)nmax;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  if (warp < 4) {  // keys needed by the furthest row of this tile: one row per thread
+    int64_t n = 0;
+    if (tid < R && i0 + tid < p.nq) {
+      const int64_t qp = p.qpos[i0 + tid];
+      n = qp + 1 < p.nk ? qp + 1 : p.nk;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const int64_t m = __shfl_xor_sync(0xffffffffu, n, o);
+      n = m > n ? m : n;
+    }
+    if (lane == 0) reinterpret_cast<int64_t*>(meta + kRedN)[warp] = n;
+  }
+  // the Q tile and the E table need nothing from the set-up above: their
+  // copies start before the first barrier (the arrivals on kBarQ come after
+  // it, once the barrier is initialised)
+  if (warp >= 8 && warp < 12) {
+    // Q: row r = head-local * R + row-local; lane l of warp w resolves row
+    // 32(w-8) + l, then the warp copies its 32 rows two at a time (16 lanes x
+    // 16 bytes per 256-byte row)
+    const int pt = tid - 256;
+    const int64_t i = i0 + (pt % R);
+    const int h = g * G + pt / R;
+    const char* qrow = i < p.nq ? static_cast<const char*>(p.q) +
+                                      (i * p.q_stride_tok + (int64_t)h * p.q_stride_head) *
+                                          (int64_t)sizeof(T)
+                                : nullptr;
+#pragma unroll
+    for (int it = 0; it < 16; ++it) {
+      const int rl = 2 * it + (lane >> 4), c16 = lane & 15;
+      const char* src = reinterpret_cast<const char*>(
+          __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(qrow), rl));
+      cp_async16(sbase + kQ + sw128((warp - 8) * 32 + rl, c16, 128),
+                 src ? src + c16 * 16 : static_cast<const char*>(p.q), src != nullptr);
+    }
+  }
+  if (warp < 12) stage_e_split<T>(smem, p, tid);
   if (warp == 12) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      mb + kTmemSlot),
@@ -287,32 +382,16 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(meta + kTmemSlot);
-  const int ntile = *reinterpret_cast<volatile int*>(meta + kNtile);
+  int64_t nneed = 0;
+  for (int w = 0; w < 4; ++w) {
+    const int64_t n = reinterpret_cast<const volatile int64_t*>(meta + kRedN)[w];
+    nneed = n > nneed ? n : nneed;
+  }
+  const int ntile = (int)((nneed + kTileN - 1) / kTileN);
 
   if (warp >= 8 && warp < 12) {
     // ================================================================ producer
     const int pt = tid - 256;  // 0..127
-    for (int idx = pt; idx < 128 * 16; idx += 128) {  // Q: row r = head-local * R + row-local
-      const int r = idx >> 4, c16 = idx & 15;
-      const int64_t i = i0 + (r % R);
-      const int h = g * G + r / R;
-      const bool ok = i < p.nq;
-      const char* src = static_cast<const char*>(p.q) +
-                        ((ok ? i : 0) * p.q_stride_tok + (int64_t)h * p.q_stride_head) *
-                            (int64_t)sizeof(T) +
-                        c16 * 16;
-      cp_async16(sbase + kQ + sw128(r, c16, 128), src, ok);
-    }
-    const float* E = static_cast<const float*>(p.E);  // E^T split into hi + lo
-    for (int idx = pt; idx < kMaxNpos * kD; idx += 128) {
-      const int dd = idx / kMaxNpos, pp = idx - dd * kMaxNpos;  // consecutive threads: consecutive p
-      float e = pp < p.npos ? E[(int64_t)dd * p.e_stride_d + (int64_t)pp * p.e_stride_p] : 0.f;
-      T hi = Elem<T>::from_f(e);
-      T lo = Elem<T>::from_f(e - Elem<T>::to_f(hi));
-      const uint32_t off = sw128(pp, dd >> 3, kMaxNpos) + (dd & 7) * 2;
-      *reinterpret_cast<T*>(smem + kP + off) = hi;
-      *reinterpret_cast<T*>(smem + kP + 16384 + off) = lo;
-    }
     cp_async_wait_all();
     fence_async_smem();
     mbar_arrive(mb + kBarQ);
@@ -327,7 +406,7 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
     bool fixed = false, bnd = false;
     int kcj = -1;
     bool slot_bad = false;  // a key some row sees has no valid slot (read as zeros)
-    const int64_t nmax = *reinterpret_cast<volatile int*>(meta + kNmax);
+    const int64_t nmax = nneed;
     auto load_key = [&](int it2) {
       const int64_t j = (int64_t)(ntile - 1 - it2) * kTileN + pt;
       const bool in = j < p.nk;
@@ -596,8 +675,11 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
     const float inv_sqrt_d = (float)(1.0 / p.scale);
     const float LOG2E = 1.4426950408889634f;
     const float scale2 = inv_sqrt_d * LOG2E;
+    const float half_scale = 0.5f * inv_sqrt_d;
     const int cc_hi = hf ? 1 : 3;  // this half's 32-column chunks: cc_hi, cc_hi - 1
 
+    fence_async_smem();  // this thread's share of the E table (staged before the barrier)
+    mbar_arrive(mb + kBarQ);
     bool ok = mbar_wait(mb + kBarT, 0, abort);
     tc_fence_after();
     {
@@ -699,6 +781,133 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
       if (!(ok = named_and(pair, 64, ok))) break;
       tc_fence_after();
       float tmax;
+      // warp-uniform, and pair-uniform (both warps hold the same rows and
+      // decide on row-level values only): a row that has not yet seen a
+      // visible key keeps its warp on the two-pass path, unless it sees none
+      // in this tile either (padding rows past nq, rows before their first key)
+      if (fast && __all_sync(0xffffffffu, mref > -INFINITY || nvalid == 0)) {
+        // Saturated tile after the first: no separate max pass.  Every
+        // visible score is x = S * scale2 + tsat2 - mref; the exponentials use
+        // mref directly unless a chunk's own maximum cm exceeds the lazy-rescale
+        // limit (2^8), in which case that chunk is exponentiated relative to
+        // cm.  The pair then compares its largest x; if it passed the limit
+        // (rare) the reference moves to the tile maximum as in the two-pass
+        // path: O and the row sum are rescaled (after PV of the previous
+        // tile), and so are this tile's P chunks (2^(sh - trel)).
+        carry = sat ? fmaxf(carry, top) : carry;
+        const float fb = tsat2 - mref;
+        float pk[2] = {0.f, 0.f}, sh[2] = {0.f, 0.f};
+        float lm = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const int cc = (hf ? 0 : 2) + k;
+          const unsigned hm = (cc & 1) ? hide0 : hide1;
+          uint32_t v[32];
+          if (__all_sync(0xffffffffu, hm == ~0u)) {
+#pragma unroll
+            for (int c = 0; c < 32; ++c) v[c] = 0u;
+          } else {
+            const uint32_t saddr = tmem + lane_base + kColS0 + st * 128 + cc * 32;
+            CS_TMEM_LD32(saddr, v);
+            tmem_wait_ld();
+            // one pass: x, its running maximum and 2^x (S stays in TMEM until
+            // the P store below, so a chunk whose maximum passes the limit is
+            // reloaded and redone relative to that maximum)
+            float c0 = -INFINITY, c1 = -INFINITY, c2 = -INFINITY, c3 = -INFINITY;
+            if (__all_sync(0xffffffffu, hm == 0u)) {
+#pragma unroll
+              for (int c = 0; c < 32; ++c) {
+                const float x = fmaf(__uint_as_float(v[c]), scale2, fb);
+                v[c] = __float_as_uint(ex2(x));
+                if ((c & 3) == 0) c0 = fmaxf(c0, x);
+                else if ((c & 3) == 1) c1 = fmaxf(c1, x);
+                else if ((c & 3) == 2) c2 = fmaxf(c2, x);
+                else c3 = fmaxf(c3, x);
+              }
+            } else {
+#pragma unroll
+              for (int c = 0; c < 32; ++c) {
+                const float x =
+                    (hm >> c) & 1u ? -INFINITY : fmaf(__uint_as_float(v[c]), scale2, fb);
+                v[c] = __float_as_uint(ex2(x));
+                if ((c & 3) == 0) c0 = fmaxf(c0, x);
+                else if ((c & 3) == 1) c1 = fmaxf(c1, x);
+                else if ((c & 3) == 2) c2 = fmaxf(c2, x);
+                else c3 = fmaxf(c3, x);
+              }
+            }
+            const float cm = fmaxf(fmaxf(c0, c1), fmaxf(c2, c3));
+            lm = fmaxf(lm, cm);
+            if (__any_sync(0xffffffffu, cm > 8.f)) {  // rare: redo relative to cm
+              sh[k] = cm > 8.f ? cm : 0.f;
+              CS_TMEM_LD32(saddr, v);
+              tmem_wait_ld();
+#pragma unroll
+              for (int c = 0; c < 32; ++c) {
+                const float x =
+                    (hm >> c) & 1u ? -INFINITY : fmaf(__uint_as_float(v[c]), scale2, fb);
+                v[c] = __float_as_uint(ex2(x - sh[k]));
+              }
+            }
+          }
+          uint32_t w[16];
+          float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+          for (int u = 0; u < 16; ++u) {
+            const float e0 = __uint_as_float(v[2 * u]);
+            const float e1 = __uint_as_float(v[2 * u + 1]);
+            s0 += e0;
+            s1 += e1;
+            w[u] = Pack2<T>::pack(e0, e1);
+          }
+          pk[k] = s0 + s1;
+          CS_TMEM_ST16(tmem + lane_base + kColS0 + st * 128 + (cc < 2 ? cc * 16 : 64 + (cc - 2) * 16), w);
+        }
+        (hf ? xm2 : xm)[r] = lm;
+        named_sync(pair, 64);
+        const float trel = fmaxf(xm[r], xm2[r]);
+        if (__any_sync(0xffffffffu, trel > 8.f)) {
+          const bool mv = trel > 8.f;
+          tmem_wait_st();
+          ok = mbar_wait(mb + kBarPV + 8 * ((it - 1) & 1), ((it - 1) >> 1) & 1, abort);
+          if (!(ok = named_and(pair, 64, ok))) break;
+          tc_fence_after();
+          const float f = mv ? ex2(-trel) : 1.f;
+          lsum *= f;
+          for (int k = 0; k < 2; ++k) {  // this half rescales 64 of the 128 O columns
+            const uint32_t taddr = tmem + lane_base + kColO + hf * 64 + k * 32;
+            uint32_t v[32];
+            CS_TMEM_LD32(taddr, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) v[c] = __float_as_uint(__uint_as_float(v[c]) * f);
+            CS_TMEM_ST32(taddr, v);
+          }
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {  // this tile's P, chunk k: 2^(sh - trel)
+            const int cc = (hf ? 0 : 2) + k;
+            const float fk = mv ? ex2(sh[k] - trel) : 1.f;
+            pk[k] *= fk;
+            const uint32_t taddr =
+                tmem + lane_base + kColS0 + st * 128 + (cc < 2 ? cc * 16 : 64 + (cc - 2) * 16);
+            uint32_t w[16];
+            CS_TMEM_LD16(taddr, w);
+            tmem_wait_ld();
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+              const float2 e = unpack2(w[u], T{});
+              w[u] = Pack2<T>::pack(e.x * fk, e.y * fk);
+            }
+            CS_TMEM_ST16(taddr, w);
+          }
+          mref = mv ? mref + trel : mref;
+        }
+        lsum += pk[0] + pk[1];
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(mb + kBarP + 8 * st);
+        continue;
+      }
       if (fast) {
         // saturated: every visible score is S * scale2 + tsat2, a monotone map
         // of the raw S, so the tile max comes from the raw scores (which stay
@@ -750,8 +959,8 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
           CS_TMEM_LD32(tmem + lane_base + kColS0 + st * 128 + cc * 32, v);
           tmem_wait_ld();
 #pragma unroll
-          for (int c = 0; c < 32; ++c)  // gate = 1 / (1 + 2^(-S * scale2))
-            v[c] = __float_as_uint(rcp_approx(1.f + ex2(__uint_as_float(v[c]) * -scale2)));
+          for (int c = 0; c < 32; ++c)  // gate = sigmoid(z) = (1 + tanh(z / 2)) / 2: one MUFU op
+            v[c] = __float_as_uint(fmaf(0.5f, tanh_approx(__uint_as_float(v[c]) * half_scale), 0.5f));
           const int lim = nvalid - cc * 32;
           const unsigned bd = bndm[cc];
           if (bd == 0u) {  // warp-uniform: no chunk boundary, a plain suffix sum
