@@ -807,47 +807,22 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
 #pragma unroll
             for (int c = 0; c < 32; ++c) v[c] = 0u;
           } else {
-            const uint32_t saddr = tmem + lane_base + kColS0 + st * 128 + cc * 32;
-            CS_TMEM_LD32(saddr, v);
+            CS_TMEM_LD32(tmem + lane_base + kColS0 + st * 128 + cc * 32, v);
             tmem_wait_ld();
-            // one pass: x, its running maximum and 2^x (S stays in TMEM until
-            // the P store below, so a chunk whose maximum passes the limit is
-            // reloaded and redone relative to that maximum)
-            float c0 = -INFINITY, c1 = -INFINITY, c2 = -INFINITY, c3 = -INFINITY;
+            // one pass: x and 2^x.  A chunk with an x above the limit (2^8)
+            // has a sum above 2^8, so only such chunks (rare) are checked
+            // exactly: S is still in TMEM until the P store below, so the
+            // chunk is reloaded, its maximum cm found and, if past the limit,
+            // the chunk redone relative to cm.
             if (__all_sync(0xffffffffu, hm == 0u)) {
 #pragma unroll
-              for (int c = 0; c < 32; ++c) {
-                const float x = fmaf(__uint_as_float(v[c]), scale2, fb);
-                v[c] = __float_as_uint(ex2(x));
-                if ((c & 3) == 0) c0 = fmaxf(c0, x);
-                else if ((c & 3) == 1) c1 = fmaxf(c1, x);
-                else if ((c & 3) == 2) c2 = fmaxf(c2, x);
-                else c3 = fmaxf(c3, x);
-              }
+              for (int c = 0; c < 32; ++c)
+                v[c] = __float_as_uint(ex2(fmaf(__uint_as_float(v[c]), scale2, fb)));
             } else {
 #pragma unroll
-              for (int c = 0; c < 32; ++c) {
-                const float x =
-                    (hm >> c) & 1u ? -INFINITY : fmaf(__uint_as_float(v[c]), scale2, fb);
-                v[c] = __float_as_uint(ex2(x));
-                if ((c & 3) == 0) c0 = fmaxf(c0, x);
-                else if ((c & 3) == 1) c1 = fmaxf(c1, x);
-                else if ((c & 3) == 2) c2 = fmaxf(c2, x);
-                else c3 = fmaxf(c3, x);
-              }
-            }
-            const float cm = fmaxf(fmaxf(c0, c1), fmaxf(c2, c3));
-            lm = fmaxf(lm, cm);
-            if (__any_sync(0xffffffffu, cm > 8.f)) {  // rare: redo relative to cm
-              sh[k] = cm > 8.f ? cm : 0.f;
-              CS_TMEM_LD32(saddr, v);
-              tmem_wait_ld();
-#pragma unroll
-              for (int c = 0; c < 32; ++c) {
-                const float x =
-                    (hm >> c) & 1u ? -INFINITY : fmaf(__uint_as_float(v[c]), scale2, fb);
-                v[c] = __float_as_uint(ex2(x - sh[k]));
-              }
+              for (int c = 0; c < 32; ++c)
+                v[c] = __float_as_uint(
+                    (hm >> c) & 1u ? 0.f : ex2(fmaf(__uint_as_float(v[c]), scale2, fb)));
             }
           }
           uint32_t w[16];
@@ -861,6 +836,30 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
             w[u] = Pack2<T>::pack(e0, e1);
           }
           pk[k] = s0 + s1;
+          if (__any_sync(0xffffffffu, !(pk[k] <= 256.f))) {  // rare (NaN counts as suspicious)
+            const uint32_t saddr = tmem + lane_base + kColS0 + st * 128 + cc * 32;
+            CS_TMEM_LD32(saddr, v);
+            tmem_wait_ld();
+            float cm = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+              const float x = (hm >> c) & 1u ? -INFINITY : fmaf(__uint_as_float(v[c]), scale2, fb);
+              v[c] = __float_as_uint(x);
+              cm = fmaxf(cm, x);
+            }
+            lm = fmaxf(lm, cm);
+            sh[k] = cm > 8.f ? cm : 0.f;
+            float r0 = 0.f, r1 = 0.f;
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+              const float e0 = ex2(__uint_as_float(v[2 * u]) - sh[k]);
+              const float e1 = ex2(__uint_as_float(v[2 * u + 1]) - sh[k]);
+              r0 += e0;
+              r1 += e1;
+              w[u] = Pack2<T>::pack(e0, e1);
+            }
+            pk[k] = r0 + r1;
+          }
           CS_TMEM_ST16(tmem + lane_base + kColS0 + st * 128 + (cc < 2 ? cc * 16 : 64 + (cc - 2) * 16), w);
         }
         (hf ? xm2 : xm)[r] = lm;
