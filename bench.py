@@ -61,9 +61,10 @@ def peaks():
 
 # ----------------------------------------------------------- accounting
 # DRAM bytes of one C2 request launch of the prefill kernel (ncu --set full,
-# dram__bytes_read.sum 26.60 MB + dram__bytes_write.sum 1.28 MB): the K/V of the
-# request (16.8 MB) cross HBM once, plus Q, the slot table, metadata and O
-PREFILL_DRAM_BYTES_PER_LAUNCH = 27_879_424
+# dram__bytes_read.sum 26.63 MB + dram__bytes_write.sum 0.02 MB): the K/V of the
+# request (16.8 MB) cross HBM once, plus Q, the slot table and metadata; the
+# outputs stay in L2 at the end of the launch
+PREFILL_DRAM_BYTES_PER_LAUNCH = 26_643_712
 
 
 def attention_flops(work) -> float:
