@@ -814,16 +814,10 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
             // exactly: S is still in TMEM until the P store below, so the
             // chunk is reloaded, its maximum cm found and, if past the limit,
             // the chunk redone relative to cm.
-            if (__all_sync(0xffffffffu, hm == 0u)) {
 #pragma unroll
-              for (int c = 0; c < 32; ++c)
-                v[c] = __float_as_uint(ex2(fmaf(__uint_as_float(v[c]), scale2, fb)));
-            } else {
-#pragma unroll
-              for (int c = 0; c < 32; ++c)
-                v[c] = __float_as_uint(
-                    (hm >> c) & 1u ? 0.f : ex2(fmaf(__uint_as_float(v[c]), scale2, fb)));
-            }
+            for (int c = 0; c < 32; ++c)
+              v[c] = __float_as_uint(
+                  (hm >> c) & 1u ? 0.f : ex2(fmaf(__uint_as_float(v[c]), scale2, fb)));
           }
           uint32_t w[16];
           float s0 = 0.f, s1 = 0.f;
