@@ -95,6 +95,9 @@ _SIGNATURES = {
                          _i32, _p, _p, _p, _p],
     "cs_wca_cosine": [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64, _i32, _f64, _p,
                       _p, _p],
+    "cs_wca_row_sums": [_p, _i64, _i64, _p, _p, _i64, _i64, _i64, _i64, _i64, _i32, _i64, _p,
+                        _p, _p, _p, _p],
+    "cs_wca_weights": [_p, _p, _i64, _f64, _i32, _p, _p, _p, _p, _p, _p],
     "cs_wca_select_topk": [_p, _p, _i64, _i64, _p, _p, _p, _p, _p],
     "cs_wca_initialize": [_p, _i64, _i64, _p, _i64, _i64, _i64, _i64, _i64, _i32, _p, _f64,
                           _i32, _p, _p, _p, _p, _p, _p, _p, _p],

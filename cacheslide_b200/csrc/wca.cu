@@ -638,6 +638,78 @@ __global__ void cosine_kernel(Rows<T> a, Rows<T> b, const int64_t* __restrict__ 
   }
 }
 
+// Per-row partial sums for a rank that holds `heads` of `heads_total` KV
+// heads (KV-head tensor parallelism): dev = sum over its heads and dims of
+// (f - c)^2, nrm = sum of c^2, cos = sum over its heads of the head cosine /
+// heads_total.  Summed over the ranks these are the squared deviation, the
+// norm and the head-mean cosine of all heads (wca.py:55-112).
+template <typename T, int G8>
+__global__ void row_sums_kernel(Rows<T> c, const int64_t* __restrict__ crows, Rows<T> f, int64_t n,
+                                int64_t heads, int64_t dim, int64_t heads_total, double* dev_out,
+                                double* nrm_out, double* cos_out, int32_t* status) {
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < n;
+       r += warps) {
+    const int64_t crow = crows ? crows[r] : r;
+    double dev = 0.0, nrm = 0.0, cs = 0.0;
+    bool in_ok = true;
+    if (dev_out || nrm_out) {
+      if constexpr (G8 > 0)
+        in_ok = row_dev_nrm_vec<T, G8>(c, crow, f, r, heads, dev, nrm);
+      else
+        in_ok = row_dev_nrm(c, crow, f, r, heads, dim, dev, nrm);
+    }
+    if (cos_out) {
+      if constexpr (G8 > 0)
+        cs = row_cosine_vec<T, G8>(f, r, c, crow, heads);
+      else
+        cs = row_cosine(f, r, c, crow, heads, dim);
+      cs = cs * (double)heads / (double)heads_total;
+    }
+    if ((threadIdx.x & 31) == 0) {
+      if (!in_ok) report(status, CS_ST_INPUT_NONFINITE);
+      if (!finite(dev) || !finite(nrm)) report(status, CS_ST_NONFINITE);
+      if (dev_out) dev_out[r] = dev;
+      if (nrm_out) nrm_out[r] = nrm;
+      if (cos_out) cos_out[r] = cs;
+    }
+  }
+}
+
+// adaptation weights (and, with `reused`, candidates and their counts) from
+// complete row sums: alpha = dev / (nrm + eps), optionally clamped to [0, 1]
+// (wca.py:65-93); candidate = reused and dev > 0 (wca.py:152-200)
+__global__ void weights_kernel(const double* __restrict__ dev, const double* __restrict__ nrm,
+                               int64_t n, double eps, int clamp, const uint8_t* __restrict__ reused,
+                               double* alpha_out, uint8_t* candidate, unsigned long long* counts,
+                               int32_t* status) {
+  __shared__ unsigned long long cnt[2];
+  if (threadIdx.x == 0) cnt[0] = cnt[1] = 0ull;
+  __syncthreads();
+  for (int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; r < n;
+       r += (int64_t)gridDim.x * blockDim.x) {
+    const double den = nrm[r] + eps;
+    double a = dev[r] / den;
+    if (!finite(dev[r]) || !finite(den) || !finite(a)) report(status, CS_ST_NONFINITE);
+    if (clamp) a = fmin(fmax(a, 0.0), 1.0);
+    if (alpha_out) alpha_out[r] = a;
+    if (candidate) {
+      const bool ru = reused[r] != 0;
+      const bool cand = ru && dev[r] > 0.0;
+      candidate[r] = cand ? 1 : 0;
+      if (ru) atomicAdd(&cnt[0], 1ull);
+      if (cand) atomicAdd(&cnt[1], 1ull);
+    }
+  }
+  if (candidate) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      if (cnt[0]) atomicAdd(&counts[0], cnt[0]);
+      if (cnt[1]) atomicAdd(&counts[1], cnt[1]);
+    }
+  }
+}
+
 // fused update: weight, blend (float64, no contraction), cast, write dense
 // and/or paged records, optional cosine; G8 > 0 selects the 16-byte vector path
 template <typename T, int G8>
@@ -970,6 +1042,52 @@ extern "C" int cs_wca_cosine(const void* a, int64_t a_stride_row, int64_t a_stri
               rows_of<T>(b, b_stride_row, b_stride_head), b_rows, n, heads, dim, cos_out);
     });
   });
+  CS_LAUNCH_CHECK();
+  return CS_OK;
+}
+
+extern "C" int cs_wca_row_sums(const void* cached, int64_t c_stride_row, int64_t c_stride_head,
+                               const int64_t* cached_rows, const void* fresh,
+                               int64_t f_stride_row, int64_t f_stride_head, int64_t n,
+                               int64_t heads, int64_t dim, int32_t dtype, int64_t heads_total,
+                               double* dev_out, double* nrm_out, double* cos_out,
+                               int32_t* status, void* stream) {
+  CS_HOST_CHECK(n >= 0 && heads > 0 && dim > 0 && heads_total >= heads);
+  if (n == 0) return CS_OK;
+  CS_HOST_CHECK(cached && fresh);
+  const int threads = 256;
+  CS_DISPATCH_FLOAT(dtype, T, {
+    const int g8 = vec_groups<T>(dim, {cached, fresh},
+                                 {c_stride_row, c_stride_head, f_stride_row, f_stride_head});
+    with_g8<T>(g8, [&](auto G) {
+      row_sums_kernel<T, decltype(G)::value>
+          <<<row_grid(n, threads / 32), threads, 0, as_stream(stream)>>>(
+              rows_of<T>(cached, c_stride_row, c_stride_head), cached_rows,
+              rows_of<T>(fresh, f_stride_row, f_stride_head), n, heads, dim, heads_total,
+              dev_out, nrm_out, cos_out, status);
+    });
+  });
+  CS_LAUNCH_CHECK();
+  return CS_OK;
+}
+
+extern "C" int cs_wca_weights(const double* dev, const double* nrm, int64_t n, double epsilon,
+                              int32_t clamp, const uint8_t* reused, double* alpha_out,
+                              uint8_t* candidate, int64_t* counts_out, int32_t* status,
+                              void* stream) {
+  CS_HOST_CHECK(n >= 0 && (candidate == nullptr || (reused && counts_out)));
+  auto s = as_stream(stream);
+  if (candidate && cudaMemsetAsync(counts_out, 0, 2 * sizeof(int64_t), s) != cudaSuccess)
+    return CS_ERR_CUDA;
+  if (n == 0) return CS_OK;
+  CS_HOST_CHECK(dev && nrm);
+  const int threads = 256;
+  int blocks = (int)((n + threads - 1) / threads);
+  blocks = blocks > 1184 ? 1184 : blocks;
+  weights_kernel<<<blocks, threads, 0, s>>>(dev, nrm, n, epsilon, clamp, reused, alpha_out,
+                                            candidate,
+                                            reinterpret_cast<unsigned long long*>(counts_out),
+                                            status);
   CS_LAUNCH_CHECK();
   return CS_OK;
 }

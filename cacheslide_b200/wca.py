@@ -80,6 +80,13 @@ def _raise_numeric(bits: int, what: str) -> None:
         raise WCANumericalError(what)
 
 
+def _raise_update(bits: int) -> None:
+    if bits & N.ST_SLOT_RANGE:
+        raise ValueError("paged KV slot outside the arena")
+    if bits & (N.ST_NONFINITE | N.ST_INPUT_NONFINITE):
+        raise WCANumericalError("weighted K/V overflowed the cache dtype")
+
+
 def _deviation(cached: Tensor, fresh: Tensor, epsilon: float, clamp: bool, want_alpha: bool):
     device = N.require_cuda(cached, fresh)
     c, f = _inner(cached), _inner(fresh)
@@ -263,22 +270,10 @@ class WCAState:
     def _promote(self) -> Tensor:
         return self._commit(None, None, None)[1]
 
-    def update(
-        self,
-        layer_index: int,
-        cached_k: Tensor,
-        cached_v: Tensor,
-        recomputed_k: Tensor,
-        recomputed_v: Tensor,
-        computed_indices: Tensor | None = None,
-        *,
-        paged=None,
-    ) -> WCAUpdate:
-        """Fuse sparse recomputed rows against full current-layer cached K/V.
-
-        ``paged=(NativePagedKV, slots)`` additionally writes the fused rows to
-        their paged slots in the same kernel (blend + scatter).
-        """
+    def _check_update(self, layer_index, cached_k, cached_v, recomputed_k, recomputed_v,
+                      computed_indices):
+        """Argument checks of ``update`` (wca.py:217-250); returns the active
+        indices and the row views the kernels read."""
         if layer_index != self.last_layer + 1:
             raise ValueError("layers must update consecutively after full layer one")
         _kv("cached_k", cached_k)
@@ -301,7 +296,7 @@ class WCAState:
             if (tuple(t.shape), t.dtype, t.device) != (expected, cached_k.dtype, cached_k.device):
                 raise ValueError(f"{name} shape, dtype and device must match its reference")
             _kv(name, t)
-        device = N.require_cuda(cached_k)
+        N.require_cuda(cached_k)
         ck, cv = _inner(cached_k), _inner(cached_v)
         if ck.stride() != cv.stride():
             cv = cv.contiguous()
@@ -309,12 +304,22 @@ class WCAState:
         fk, fv = _inner(recomputed_k), _inner(recomputed_v)
         if fk.stride() != fv.stride():
             fk, fv = fk.contiguous(), fv.contiguous()
-        fused_k = torch.empty(expected, dtype=cached_k.dtype, device=device)
+        return indices, ck, cv, fk, fv
+
+    def _blend(self, indices, ck, cv, fk, fv, *, same_layer: bool, cosine, paged,
+               alpha: Tensor | None = None, check: bool = True):
+        """One fused pass over the active rows (cs_wca_update): next weight,
+        float64 blend with the used weight (``alpha[index]`` unless
+        ``same_layer``; mandatory rows 1), cast, optional cosine and paged
+        scatter.  Returns (fused_k, fused_v, next_alpha, used_alpha), plus the
+        status bits instead of raising when ``check`` is false."""
+        alpha = self.alpha if alpha is None else alpha
+        device = ck.device
+        a = indices.numel()
+        fused_k = torch.empty((a, *ck.shape[1:]), dtype=ck.dtype, device=device)
         fused_v = torch.empty_like(fused_k)
         next_alpha = torch.empty(a, dtype=torch.float64, device=device)
         used = torch.empty_like(next_alpha)
-        gate = layer_index % self.config.gate_interval == 0
-        cosine = torch.empty_like(next_alpha) if gate else None
         kv = slots = None
         if paged is not None:
             arena, slots = paged
@@ -324,8 +329,8 @@ class WCAState:
             N.load().cs_wca_update(
                 ck.data_ptr(), cv.data_ptr(), ck.stride(0), ck.stride(1), fk.data_ptr(),
                 fv.data_ptr(), fk.stride(0), fk.stride(1), indices.data_ptr(), a,
-                ck.shape[1], ck.shape[2], N.DTYPES[ck.dtype], self.alpha.data_ptr(),
-                self.mandatory_mask.data_ptr(), int(self.config.weight_update == "same_layer"),
+                ck.shape[1], ck.shape[2], N.DTYPES[ck.dtype], alpha.data_ptr(),
+                self.mandatory_mask.data_ptr(), int(same_layer),
                 float(self.config.epsilon), int(self.config.clamp_alpha), fused_k.data_ptr(),
                 fused_v.data_ptr(), next_alpha.data_ptr(), used.data_ptr(), N.ptr(cosine),
                 None if kv is None else ctypes.byref(kv), N.ptr(slots),
@@ -334,10 +339,35 @@ class WCAState:
             "cs_wca_update",
         )
         bits = status.read()
-        if bits & N.ST_SLOT_RANGE:
-            raise ValueError("paged KV slot outside the arena")
-        if bits & (N.ST_NONFINITE | N.ST_INPUT_NONFINITE):
-            raise WCANumericalError("weighted K/V overflowed the cache dtype")
+        if not check:
+            return fused_k, fused_v, next_alpha, used, bits
+        _raise_update(bits)
+        return fused_k, fused_v, next_alpha, used
+
+    def update(
+        self,
+        layer_index: int,
+        cached_k: Tensor,
+        cached_v: Tensor,
+        recomputed_k: Tensor,
+        recomputed_v: Tensor,
+        computed_indices: Tensor | None = None,
+        *,
+        paged=None,
+    ) -> WCAUpdate:
+        """Fuse sparse recomputed rows against full current-layer cached K/V.
+
+        ``paged=(NativePagedKV, slots)`` additionally writes the fused rows to
+        their paged slots in the same kernel (blend + scatter).
+        """
+        indices, ck, cv, fk, fv = self._check_update(
+            layer_index, cached_k, cached_v, recomputed_k, recomputed_v, computed_indices)
+        gate = layer_index % self.config.gate_interval == 0
+        cosine = torch.empty(indices.numel(), dtype=torch.float64,
+                             device=ck.device) if gate else None
+        fused_k, fused_v, next_alpha, used = self._blend(
+            indices, ck, cv, fk, fv, same_layer=self.config.weight_update == "same_layer",
+            cosine=cosine, paged=paged)
         removed, promoted = self._commit(indices, next_alpha, cosine)
         self.last_layer = layer_index
         return WCAUpdate(

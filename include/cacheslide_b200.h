@@ -132,6 +132,37 @@ CS_API int cs_wca_cosine(const void* a, int64_t a_stride_row, int64_t a_stride_h
                   int32_t* status, void* stream);
 
 /*
+ * Row sums of one KV-head shard, for KV-head tensor parallelism (the C5
+ * layout: each rank holds `heads` of `heads_total` heads).  Replaces the
+ * head reductions inside squared_deviation / adaptation_weight /
+ * mean_head_cosine (wca.py:55-112) with per-shard partial sums that the
+ * caller all-reduces across ranks:
+ *   dev[r] = sum over the shard's heads and dims of (fresh[r] - cached[c])^2,
+ *   nrm[r] = sum of cached[c]^2,
+ *   cos[r] = sum over the shard's heads of the head cosine / heads_total,
+ * with c = cached_rows ? cached_rows[r] : r.  Any output may be NULL.
+ */
+CS_API int cs_wca_row_sums(const void* cached, int64_t c_stride_row,
+                    int64_t c_stride_head, const int64_t* cached_rows,
+                    const void* fresh, int64_t f_stride_row,
+                    int64_t f_stride_head, int64_t n, int64_t heads,
+                    int64_t dim, int32_t dtype, int64_t heads_total,
+                    double* dev_out, double* nrm_out, double* cos_out,
+                    int32_t* status, void* stream);
+
+/*
+ * Adaptation weights from complete (all-reduced) row sums (wca.py:65-93,
+ * 152-191): alpha[r] = dev[r] / (nrm[r] + epsilon), clamped to [0,1] when
+ * `clamp`; with `candidate` (then `reused` and `counts_out` are required):
+ * candidate = reused & dev > 0, counts_out[0] = |reused|,
+ * counts_out[1] = |candidate|.  alpha_out may be NULL.
+ */
+CS_API int cs_wca_weights(const double* dev, const double* nrm, int64_t n,
+                   double epsilon, int32_t clamp, const uint8_t* reused,
+                   double* alpha_out, uint8_t* candidate, int64_t* counts_out,
+                   int32_t* status, void* stream);
+
+/*
  * Block radix top-k (wca.py:202-215): among tokens with available[i] != 0,
  * pick the `slots` largest keys[i] (float64, >= 0), descending with ties to the
  * lower index, exactly like a stable descending argsort.  Sets selected[i]=1
