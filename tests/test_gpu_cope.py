@@ -479,6 +479,69 @@ def test_split_key_decode_head_groups_and_widths(cuda, hq, hkv, d, npos):
     np.testing.assert_allclose(out.float().cpu().numpy(), want, **BF16)
 
 
+@pytest.mark.parametrize("layout", ["dense", "paged_sidecar"])
+def test_fp16_prefill_and_decode_match_oracle(cuda, layout):
+    """float16 inputs through the tensor-core prefill and the tensor-core
+    split-key decode (f16 MMA operands), with dense K/V or a paged cache whose
+    newest keys live in the sidecar."""
+    import ctypes
+
+    from cacheslide_b200 import _native as N
+    from cacheslide_b200.position import _Holder, _base_params
+
+    hq, hkv, d, bs, nk = 16, 4, 128, 16, 1100
+    g = torch.Generator().manual_seed(97 + (layout == "dense"))
+    f16 = torch.float16
+    q = (torch.randn(200, hq, d, generator=g) / d ** 0.5).to(f16).to(cuda)
+    k = (torch.randn(nk, hkv, d, generator=g) / d ** 0.5).to(f16).to(cuda)
+    v = torch.randn(nk, hkv, d, generator=g).to(f16).to(cuda)
+    E = torch.randn(d, 64, generator=g) * 0.02
+    cope = _cope(E.numpy(), cuda)
+    holder = _Holder(cope, cope.position_embeddings.detach())
+    pre_rows = torch.sort(torch.randperm(nk, generator=g)[:200]).values.to(cuda)
+    dec_rows = torch.tensor([nk - 1, 700], device=cuda)
+    cache = slots = side_k = side_v = None
+    if layout == "paged_sidecar":
+        n_side = 160  # the newest keys are sidecar rows (slots past the native blocks)
+        n_native = nk - n_side
+        nb = (n_native + bs - 1) // bs + 3
+        perm = torch.randperm(nb, generator=g)[: (n_native + bs - 1) // bs].to(cuda)
+        tok = torch.arange(n_native, device=cuda)
+        native = perm[tok // bs] * bs + tok % bs
+        slots = torch.cat([native, nb * bs + torch.arange(n_side, device=cuda)])
+        cache = torch.zeros(nb, hkv, bs, 2 * d, dtype=f16, device=cuda)
+        cache[native // bs, :, native % bs, :d] = k[:n_native]
+        cache[native // bs, :, native % bs, d:] = v[:n_native]
+        side_k, side_v = k[n_native:].clone(), v[n_native:].clone()
+    lib = N.load()
+    keep = []
+    for rows, kind in ((pre_rows, "prefill"), (dec_rows, "decode")):
+        qq = q[: rows.numel()]
+        out = torch.empty(rows.numel(), hq, d, dtype=f16, device=cuda)
+        paged = layout != "dense"
+        p = _base_params(qq, None if paged else k, None if paged else v, holder, rows, None,
+                         nk, hkv, d)
+        if paged:
+            p.paged = N.paged_view(cache, side_k, side_v)
+            p.kv_slots = slots.data_ptr()
+        p.out = out.data_ptr()
+        p.o_stride_tok, p.o_stride_head = out.stride(0), out.stride(1)
+        st = N.Status(cuda)
+        p.status = st.ptr
+        if kind == "prefill":
+            N.check(lib.cs_cope_attn_prefill(ctypes.byref(p), N.stream_of(cuda)), kind)
+        else:
+            size = lib.cs_cope_attn_decode_workspace(ctypes.byref(p))
+            ws = torch.empty(size, dtype=torch.uint8, device=cuda)
+            keep.append(ws)
+            N.check(lib.cs_cope_attn_decode(ctypes.byref(p), ws.data_ptr(), N.stream_of(cuda)),
+                    kind)
+        assert st.read() == 0, kind
+        want = ocope.cope_attention(qq.float().cpu().numpy(), k.float().cpu().numpy(),
+                                    v.float().cpu().numpy(), E.numpy(), rows.cpu().numpy())
+        np.testing.assert_allclose(out.float().cpu().numpy(), want, **BF16, err_msg=kind)
+
+
 def test_batched_decode_matches_per_request_decode(cuda):
     """cs_cope_attn_decode_batch over requests of different context lengths
     (and more requests than one launch holds) equals decoding them one by one."""
