@@ -216,10 +216,12 @@ __global__ void __launch_bounds__(kSplit) decode_phase2(const __grid_constant__ 
     return;
   }
   const int last = (int)((nlim - 1) / kSplit);
-  if (tid < G) {
+  // count carried from the newer splits: a warp per head, lanes over splits
+  for (int hh = warp; hh < G; hh += kSplit / 32) {
     float c = 0.f;
-    for (int t = last; t > s; --t) c += r.gsum[(rowh0 + tid) * r.nsplit + t];
-    carry0[tid] = c;
+    for (int t = s + 1 + lane; t <= last; t += 32) c += r.gsum[(rowh0 + hh) * r.nsplit + t];
+    c = warp_sum(c);
+    if (lane == 0) carry0[hh] = c;
   }
   for (int e = tid; e < G * npos; e += kSplit) tab[e] = r.table[rowh0 * npos + e];
   const int64_t j = base + tid;
@@ -546,22 +548,66 @@ __global__ void __launch_bounds__(kSplit) decode_qk_tc(const __grid_constant__ D
     for (int w = kSplit / 32 - 1; w >= 0; --w) tot += gred[w][tid];
     r.gsum[(rowh0 + tid) * r.nsplit + s] = tot;
   }
-  if (s == 0) {  // q.E table: T[h][p] = sum_x q[h][x] E[x][p], a thread per (h, p)
-    for (int e = tid; e < G * b.npos; e += kSplit) {
-      const int hh = e / b.npos, pp = e - hh * b.npos;
-      const float* ep = r.E + pp * r.e_sp;
-      float t0 = 0.f, t1 = 0.f;
-#pragma unroll 2
-      for (int c = 0; c < kFastD / 8; ++c) {  // q from the swizzled q tile, 8 at a time
-        const uint4 u = *reinterpret_cast<const uint4*>(gQ + sw128(hh, c, kTcN));
-        const T* qv = reinterpret_cast<const T*>(&u);
+  if (s == 0) {  // q.E table: T[h][p] = sum_x q[h][x] E[x][p]
+    const int npos = b.npos, p4 = npos / 4;
+    const bool vec = r.e_sp == 1 && (npos & 3) == 0 && (r.e_sd & 3) == 0 && p4 <= kSplit &&
+                     kSplit % p4 == 0 && kFastD % (kSplit / p4) == 0 &&
+                     (reinterpret_cast<uintptr_t>(r.E) & 15) == 0;
+    auto qx = [&](int hh, int x) {  // q[hh][x] from the swizzled q tile
+      return Elem<T>::to_f(*reinterpret_cast<const T*>(gQ + sw128(hh, x >> 3, kTcN) + (x & 7) * 2));
+    };
+    if (vec) {
+      // thread t: positions 4(t % p4) .. +3 over a group of dimensions (one
+      // float4 load per dimension, all issued together); the groups'
+      // partials meet in the K tile's shared memory, free after the MMA
+      const int ng = kSplit / p4, dpg = kFastD / ng;
+      float* part = reinterpret_cast<float*>(dsm + (sK - sraw));  // [ng][G][npos]
+      const int p0 = (tid % p4) * 4, grp = tid / p4, x0 = grp * dpg;
+      float acc[G][4];
 #pragma unroll
-        for (int k = 0; k < 8; k += 2) {
-          t0 = fmaf(Elem<T>::to_f(qv[k]), ep[(c * 8 + k) * r.e_sd], t0);
-          t1 = fmaf(Elem<T>::to_f(qv[k + 1]), ep[(c * 8 + k + 1) * r.e_sd], t1);
+      for (int hh = 0; hh < G; ++hh) acc[hh][0] = acc[hh][1] = acc[hh][2] = acc[hh][3] = 0.f;
+      for (int x = x0; x < x0 + dpg; x += 8) {
+        float4 ev[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          ev[u] = x + u < x0 + dpg
+                      ? __ldg(reinterpret_cast<const float4*>(r.E + (int64_t)(x + u) * r.e_sd + p0))
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          if (x + u >= x0 + dpg) break;
+#pragma unroll
+          for (int hh = 0; hh < G; ++hh) {
+            const float qv = qx(hh, x + u);
+            acc[hh][0] = fmaf(qv, ev[u].x, acc[hh][0]);
+            acc[hh][1] = fmaf(qv, ev[u].y, acc[hh][1]);
+            acc[hh][2] = fmaf(qv, ev[u].z, acc[hh][2]);
+            acc[hh][3] = fmaf(qv, ev[u].w, acc[hh][3]);
+          }
         }
       }
-      r.table[(rowh0 + hh) * b.npos + pp] = t0 + t1;
+#pragma unroll
+      for (int hh = 0; hh < G; ++hh)
+        *reinterpret_cast<float4*>(part + (grp * G + hh) * npos + p0) =
+            make_float4(acc[hh][0], acc[hh][1], acc[hh][2], acc[hh][3]);
+      __syncthreads();
+      for (int e = tid; e < G * npos; e += kSplit) {
+        float t = 0.f;
+        for (int k = 0; k < ng; ++k) t += part[k * G * npos + e];
+        r.table[rowh0 * npos + e] = t;
+      }
+    } else {  // a thread per (h, p)
+      for (int e = tid; e < G * npos; e += kSplit) {
+        const int hh = e / npos, pp = e - hh * npos;
+        const float* ep = r.E + pp * r.e_sp;
+        float t0 = 0.f, t1 = 0.f;
+#pragma unroll 8
+        for (int x = 0; x < kFastD; x += 2) {
+          t0 = fmaf(qx(hh, x), ep[x * r.e_sd], t0);
+          t1 = fmaf(qx(hh, x + 1), ep[(x + 1) * r.e_sd], t1);
+        }
+        r.table[rowh0 * npos + e] = t0 + t1;
+      }
     }
   }
   bits = (int32_t)__reduce_or_sync(0xffffffffu, (unsigned)bits);
@@ -709,10 +755,12 @@ __global__ void __launch_bounds__(kSplit) decode_pv_tc(const __grid_constant__ D
     *reinterpret_cast<uint4*>(gP + sw128(G + (e >> 4), e & 15, kTcN)) = make_uint4(0, 0, 0, 0);
   asm volatile("griddepcontrol.wait;" ::: "memory");  // phase 1 complete and visible
   const int last = (int)((nlim - 1) / kSplit);
-  if (tid < G) {
+  // count carried from the newer splits: a warp per head, lanes over splits
+  for (int hh = warp; hh < G; hh += kSplit / 32) {
     float c = 0.f;
-    for (int t = last; t > s; --t) c += r.gsum[(rowh0 + tid) * r.nsplit + t];
-    carry0[tid] = c;
+    for (int t = s + 1 + lane; t <= last; t += 32) c += r.gsum[(rowh0 + hh) * r.nsplit + t];
+    c = warp_sum(c);
+    if (lane == 0) carry0[hh] = c;
   }
   for (int e = tid; e < G * npos; e += kSplit) tab[e] = r.table[rowh0 * npos + e];
   float lg[G], suf[G];
