@@ -72,6 +72,7 @@ struct SelectSmem {
   int warp_tot[32];
   uint64_t prefix, mask;
   int remaining;
+  int whole_bin;  // the k-th pick's bin is taken whole: no finer digits needed
   int chosen_count;
   int eq_taken;
 };
@@ -308,12 +309,13 @@ __device__ int64_t block_topk_staged(const double* __restrict__ keys, Avail avai
   uint64_t mask = top < 56 ? (~0ull << (top + 8)) : 0ull;
   uint64_t prefix = hi & mask;
   int remaining = (int)want;
-  int* mine = whist + warp * 256;
-  const int nwarps = blockDim.x >> 5;
+  // four histogram copies, shared by warps w, w+4, ...: few enough to sum
+  // quickly, enough to spread the atomics of equal digits
+  int* mine = whist + (warp & 3) * 256;
   __syncthreads();  // wmin (aliasing whist) read by all before the histograms
+  for (int b = tid; b < 4 * 256; b += blockDim.x) whist[b] = 0;
+  __syncthreads();
   for (int shift = top; shift >= 0; shift -= 8) {
-    for (int b = lane; b < 256; b += 32) mine[b] = 0;
-    __syncwarp();
     for (int64_t base = 0; base < n; base += blockDim.x) {
       const int64_t i = base + tid;
       const uint64_t c = i < n ? code[i] : 0ull;
@@ -321,9 +323,8 @@ __device__ int64_t block_topk_staged(const double* __restrict__ keys, Avail avai
     }
     __syncthreads();
     for (int b = tid; b < 256; b += blockDim.x) {
-      int t = 0;
-      for (int w = 0; w < nwarps; ++w) t += whist[w * 256 + b];
-      hist[b] = t;
+      hist[b] = whist[b] + whist[256 + b] + whist[512 + b] + whist[768 + b];
+      whist[b] = whist[256 + b] = whist[512 + b] = whist[768 + b] = 0;  // for the next pass
     }
     __syncthreads();
     if (warp == 0) {
@@ -344,24 +345,30 @@ __device__ int64_t block_topk_staged(const double* __restrict__ keys, Avail avai
       const unsigned hit = __ballot_sync(full, inc >= need);
       const int owner = __ffs(hit) - 1;
       if (lane == owner) {
-        int above = inc - sum, b = 0;
+        int above = inc - sum, b = 0, inbin = 0;
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           if (above + cnt[q] >= need) {
             b = 255 - 8 * lane - q;
+            inbin = cnt[q];
             break;
           }
           above += cnt[q];
         }
         sm.prefix = prefix | ((uint64_t)b << shift);
         sm.remaining = need - above;
+        sm.whole_bin = need - above == inbin;
       }
     }
     __syncthreads();
     prefix = sm.prefix;
     remaining = sm.remaining;
     mask |= 255ull << shift;
+    const bool whole = sm.whole_bin != 0;
     __syncthreads();
+    // every code whose leading bytes equal the prefix is a pick: the
+    // compaction below compares leading bytes only
+    if (whole) break;
   }
   // ordered compaction of the picks: code above the k-th, or equal to it
   // among the first `remaining` by index
@@ -375,8 +382,8 @@ __device__ int64_t block_topk_staged(const double* __restrict__ keys, Avail avai
   for (int64_t base = 0; base < n; base += blockDim.x) {
     const int64_t i = base + tid;
     const uint64_t c = i < n ? code[i] : 0ull;
-    const int gt = (c != 0ull && c > prefix) ? 1 : 0;
-    const int eq = (c != 0ull && c == prefix) ? 1 : 0;
+    const int gt = (c != 0ull && (c & mask) > prefix) ? 1 : 0;
+    const int eq = (c != 0ull && (c & mask) == prefix) ? 1 : 0;
     const int inc = block_inclusive_scan(gt | (eq << 16), sm.warp_tot);
     const int gt_before = (inc & 0xFFFF) - gt + sm.chosen_count;  // greater ones so far
     const int eq_before = (inc >> 16) - eq + sm.eq_taken;
@@ -393,40 +400,60 @@ __device__ int64_t block_topk_staged(const double* __restrict__ keys, Avail avai
     }
     __syncthreads();
   }
-  // bitonic sort of the picks, thread t holding position t
+  // sort of the picks by (code descending, index ascending), a strict total
+  // order (the padding entries get distinct indices too): each warp sorts 32
+  // entries with a shuffle bitonic network, then rounds of pairwise merges,
+  // where an entry's place in the merged run is its place in its own run plus
+  // the number of entries of the partner run before it (binary search).
   int P = 32;
   while (P < want) P <<= 1;
   const bool part = tid < P;  // warp-uniform (P is a multiple of 32)
+  auto before = [](uint64_t ca, uint32_t ia, uint64_t cb, uint32_t ib) {
+    return ca > cb || (ca == cb && ia < ib);
+  };
   uint64_t c = (tid < want) ? pcode[tid] : 0ull;
-  uint32_t id = (tid < want) ? pidx[tid] : 0xFFFFFFFFu;
-  __syncthreads();
-  for (int k = 2; k <= P; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      uint64_t pc;
-      uint32_t pi;
-      if (j >= 32) {  // block-uniform
-        if (part) {
-          pcode[tid] = c;
-          pidx[tid] = id;
-        }
-        __syncthreads();
-        if (part) {
-          pc = pcode[tid ^ j];
-          pi = pidx[tid ^ j];
-        }
-        __syncthreads();
-      } else if (part) {
-        pc = __shfl_xor_sync(full, c, j);
-        pi = __shfl_xor_sync(full, id, j);
-      }
-      if (part) {
-        const bool partner_first = pc > c || (pc == c && pi < id);
-        const bool keep_first = ((tid & j) == 0) == ((tid & k) == 0);
+  uint32_t id = (tid < want) ? pidx[tid] : 0xFFFFFFFFu - (uint32_t)tid;
+  if (part) {
+    for (int k = 2; k <= 32; k <<= 1) {
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        const uint64_t pc = __shfl_xor_sync(full, c, j);
+        const uint32_t pi = __shfl_xor_sync(full, id, j);
+        const bool partner_first = before(pc, pi, c, id);
+        // lane, not tid: every warp's run ends up in the same (ascending) order
+        const bool keep_first = ((lane & j) == 0) == ((lane & k) == 0);
         if (keep_first == partner_first) {
           c = pc;
           id = pi;
         }
       }
+    }
+  }
+  uint64_t* scode = reinterpret_cast<uint64_t*>(whist);  // merge buffer (histograms done)
+  uint32_t* sidx = reinterpret_cast<uint32_t*>(scode + kFastPicks);
+  for (int w = 32; w < P; w <<= 1) {
+    __syncthreads();  // previous readers of the runs are done
+    if (part) {
+      scode[tid] = c;
+      sidx[tid] = id;
+    }
+    __syncthreads();
+    if (part) {
+      const int run = tid & ~(w - 1), pos = tid - run;
+      const int other = run ^ w;  // partner run [other, other + w)
+      int lo = 0, hi = w;
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (before(scode[other + mid], sidx[other + mid], c, id)) lo = mid + 1;
+        else hi = mid;
+      }
+      const int dst = (run & ~(2 * w - 1)) + pos + lo;
+      pcode[dst] = c;
+      pidx[dst] = id;
+    }
+    __syncthreads();
+    if (part) {
+      c = pcode[tid];
+      id = pidx[tid];
     }
   }
   if (tid < want) {
