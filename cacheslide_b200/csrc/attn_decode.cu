@@ -615,70 +615,104 @@ __global__ void __launch_bounds__(kSplit) decode_qk_tc(const __grid_constant__ D
 }
 
 // Merge the split partials of the G heads of (row i, KV head g) into the
-// output rows.  Warp w finds the maximum M and the weights e^(m_s - M) of
-// heads w, w+4, ... (chunks of kCombChunk / G splits in shared memory);
-// thread x then accumulates output dimension x of all G heads at once.
+// output rows in one online pass.  A warp takes up to four heads (G = 8: two
+// warps share a split, four heads each) and every NS-th split, lane x
+// dimensions 4x..4x+3; a batch of U splits is loaded at once (float4
+// partial rows), and the warp's running maximum per head rescales its sums
+// when a batch raises it.  The warps' (maximum, sum, accumulator) per head
+// are then merged through `buf` (G * NS * 130 floats of shared memory).
 // Partials written by other CTAs are read through L2.
 template <int G>
 __device__ void combine_heads(const DecodeBatch& b, const DecodeReq& r, int64_t i, int g,
-                              int nsp, float* wsp, float* lsum, int32_t& bits) {
+                              int nsp, float* buf, int32_t& bits) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int nw = kSplit / 32;
-  constexpr int CH = kCombChunk / G;  // splits per chunk
-  const int64_t rowh0 = i * b.hq + (int64_t)g * G;
-  float M[(G + nw - 1) / nw], l[(G + nw - 1) / nw];
+  constexpr int GH = G > 4 ? 4 : G;  // heads per warp
+  constexpr int NS = nw / (G / GH);  // warps per head, each taking every NS-th split
+  constexpr int U = 8 / GH;          // splits per batch: 8 partial rows in flight
+  static_assert(G * NS * (kFastD + 2) * 4 <= (int)kTileB, "the merge buffer fits the V tile");
+  const int h0 = (warp / NS) * GH, sw = warp % NS;
+  const int64_t rowh0 = i * b.hq + (int64_t)g * G + h0;
+  float m[GH], l[GH];
+  float4 acc[GH];
 #pragma unroll
-  for (int k = 0; k * nw < G; ++k) {
-    const int hh = warp + k * nw;
-    M[k] = -INFINITY;
-    l[k] = 0.f;
-    if (hh < G) {
-      const float* pm = r.pm + (rowh0 + hh) * r.nsplit;
-      float m = -INFINITY;
-      for (int s = lane; s < nsp; s += 32) m = fmaxf(m, __ldcg(pm + s));
-      M[k] = warp_max(m);
-    }
+  for (int hh = 0; hh < GH; ++hh) {
+    m[hh] = -INFINITY;
+    l[hh] = 0.f;
+    acc[hh] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  float acc[G];
+  for (int s0 = sw; s0 < nsp; s0 += NS * U) {
+    float ms[U][GH], ls[U][GH];
+    float4 o[U][GH];
 #pragma unroll
-  for (int hh = 0; hh < G; ++hh) acc[hh] = 0.f;
-  for (int c0 = 0; c0 < nsp; c0 += CH) {
-    const int cn = nsp - c0 < CH ? nsp - c0 : CH;
-    __syncthreads();  // previous chunk's weights consumed
+    for (int u = 0; u < U; ++u) {
+      const int s = s0 + u * NS;
 #pragma unroll
-    for (int k = 0; k * nw < G; ++k) {
-      const int hh = warp + k * nw;
-      if (hh >= G) continue;
-      const float* pm = r.pm + (rowh0 + hh) * r.nsplit + c0;
-      const float* pl = r.pl + (rowh0 + hh) * r.nsplit + c0;
-      for (int s = lane; s < cn; s += 32) {
-        const float ms = __ldcg(pm + s);
-        const float w = ms > -INFINITY ? expf(ms - M[k]) : 0.f;
-        wsp[hh * CH + s] = w;
-        l[k] = fmaf(w, __ldcg(pl + s), l[k]);
+      for (int hh = 0; hh < GH; ++hh) {
+        const int64_t rs = (rowh0 + hh) * r.nsplit + s;
+        if (s < nsp) {
+          ms[u][hh] = __ldcg(r.pm + rs);
+          ls[u][hh] = __ldcg(r.pl + rs);
+          o[u][hh] = __ldcg(reinterpret_cast<const float4*>(r.po + rs * kFastD) + lane);
+        } else {
+          ms[u][hh] = -INFINITY;
+          ls[u][hh] = 0.f;
+          o[u][hh] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
       }
     }
-    __syncthreads();
-    const float* po = r.po + (rowh0 * r.nsplit + c0) * (int64_t)kFastD + tid;
-#pragma unroll 4
-    for (int s = 0; s < cn; ++s) {
 #pragma unroll
-      for (int hh = 0; hh < G; ++hh)
-        acc[hh] = fmaf(wsp[hh * CH + s], __ldcg(po + ((int64_t)hh * r.nsplit + s) * kFastD),
-                       acc[hh]);
+    for (int hh = 0; hh < GH; ++hh) {
+      float mb = m[hh];
+#pragma unroll
+      for (int u = 0; u < U; ++u) mb = fmaxf(mb, ms[u][hh]);
+      if (mb > m[hh]) {  // uniform over the warp: its lanes read the same split maxima
+        const float c = expf(m[hh] - mb);  // 0 while nothing was accumulated
+        acc[hh].x *= c;
+        acc[hh].y *= c;
+        acc[hh].z *= c;
+        acc[hh].w *= c;
+        l[hh] *= c;
+        m[hh] = mb;
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const float w = ms[u][hh] > -INFINITY ? expf(ms[u][hh] - m[hh]) : 0.f;
+        acc[hh].x = fmaf(w, o[u][hh].x, acc[hh].x);
+        acc[hh].y = fmaf(w, o[u][hh].y, acc[hh].y);
+        acc[hh].z = fmaf(w, o[u][hh].z, acc[hh].z);
+        acc[hh].w = fmaf(w, o[u][hh].w, acc[hh].w);
+        l[hh] = fmaf(w, ls[u][hh], l[hh]);
+      }
     }
   }
+  // buf: [G][NS][128] accumulators, then [G][NS] maxima and [G][NS] sums
+  float* wm = buf + G * NS * kFastD;
+  float* wl = wm + G * NS;
 #pragma unroll
-  for (int k = 0; k * nw < G; ++k) {
-    const int hh = warp + k * nw;
-    const float v = warp_sum(l[k]);
-    if (hh < G && lane == 0) lsum[hh] = v;
+  for (int hh = 0; hh < GH; ++hh) {
+    const int e = (h0 + hh) * NS + sw;
+    reinterpret_cast<float4*>(buf + e * kFastD)[lane] = acc[hh];
+    if (lane == 0) {
+      wm[e] = m[hh];
+      wl[e] = l[hh];
+    }
   }
   __syncthreads();
 #pragma unroll
   for (int hh = 0; hh < G; ++hh) {
-    const float L = lsum[hh];
-    const float val = acc[hh] * (L > 0.f ? 1.f / L : 0.f);
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NS; ++w) M = fmaxf(M, wm[hh * NS + w]);
+    float L = 0.f, v = 0.f;
+#pragma unroll
+    for (int w = 0; w < NS; ++w) {
+      const float mw = wm[hh * NS + w];
+      const float c = mw > -INFINITY ? expf(mw - M) : 0.f;
+      L = fmaf(c, wl[hh * NS + w], L);
+      v = fmaf(c, buf[(hh * NS + w) * kFastD + tid], v);
+    }
+    const float val = v * (L > 0.f ? 1.f / L : 0.f);
     if (!isfinite(val)) bits |= CS_ST_LOGIT_NONFINITE;
     char* orow = r.out + (i * r.o_st + (int64_t)(g * G + hh) * r.o_sh) * dtype_size(b.out_dtype);
     switch (b.out_dtype) {
@@ -710,7 +744,6 @@ __global__ void __launch_bounds__(kSplit) decode_pv_tc(const __grid_constant__ D
   __shared__ float carry0[G];
   __shared__ float red[G][kSplit / 32];
   __shared__ float mmax[G];
-  __shared__ float wsp[kCombChunk];
   __shared__ int last_split;
   const int64_t qp = r.qpos[i];
   const int64_t nlim = causal_limit(r, qp);
@@ -852,7 +885,8 @@ __global__ void __launch_bounds__(kSplit) decode_pv_tc(const __grid_constant__ D
   __syncthreads();
   if (last_split) {
     __threadfence();
-    combine_heads<G>(b, r, i, g, nsp, wsp, mmax, bits);
+    // the V tile is idle: this CTA's product was read back above
+    combine_heads<G>(b, r, i, g, nsp, reinterpret_cast<float*>(dsm + (sV - sraw)), bits);
     if (tid == 0) r.cnt[i * b.hkv + g] = 0;
   }
   bits = (int32_t)__reduce_or_sync(0xffffffffu, (unsigned)bits);
