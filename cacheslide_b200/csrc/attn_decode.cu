@@ -2,21 +2,26 @@
 // to kMaxBatch requests per launch.
 //
 // The contextual position of key j is the sum of the gates of all newer keys,
-// so a key split cannot finish on its own: phase 1 computes every split's
-// logits and gate totals (reading K once), phase 2 gives each split the count
-// carried from the newer splits, finishes the reverse scan, the interpolated
-// bias and a partial softmax with its PV (reading V once), and the split
-// partials are merged: on the tensor-core path (128-element heads) by the
-// last split of each (row, KV head) to finish, elsewhere by a combine kernel.
-// K and V each cross HBM once; the logits and partials (a few hundred KB per
-// row) stay in L2.  All requests of a batch share the launches, so a decode
-// step of a whole batch costs two (three) kernel launches, not per request.
+// so a key split cannot finish on its own: it needs the gate total of every
+// newer split.  On the tensor-core path (128-element 16-bit heads) one
+// kernel does it in a single pass over the token records: each split
+// publishes its gate totals and takes the count carried from the newer
+// splits by a decoupled look-back, then finishes the interpolated bias, a
+// partial softmax and its PV, and the last split of each (row, KV head) to
+// finish merges the partials (decode_onepass_tc).  Other shapes run two
+// CUDA-core phases and a combine kernel: phase 1 writes every split's logits
+// and gate totals (reading K once), phase 2 gives each split the carried
+// count and its partial softmax and PV (reading V once).  K and V cross HBM
+// once; logits and partials stay in L2.  All requests of a batch share the
+// launches.
 //
 // Modes: contextual positions, plain causal (the decode row of a CacheSlide
 // request is a dynamic token: no canonical substitution, no association
 // restriction).  Everything else reports CS_ERR_UNSUPPORTED.
 #include <math.h>
 
+#include <algorithm>
+#include <atomic>
 #include <type_traits>
 
 #include "common.cuh"
@@ -55,12 +60,14 @@ struct DecodeReq {
   float* po;      // [nq][hq][nsplit][dv]
   float* pm;      // [nq][hq][nsplit]
   float* pl;      // [nq][hq][nsplit]
-  int* cnt;       // [nq][hkv] finished splits (tensor-core path), zeroed by phase 1
+  int* cnt;       // [nq][hkv] finished splits (one-pass path)
+  uint64_t* lb;   // [nq][hq][nsplit] split state words (one-pass path)
+  uint32_t* tstat;  // [nq][hkv] q.E tables published (one-pass path)
   int nq, nk, nsplit, nk_pad, row0;
 };
 
 struct DecodeBatch {
-  int count, hq, hkv, d, dv, npos, G, out_dtype;
+  int count, hq, hkv, d, dv, npos, G, out_dtype, rows;
   float inv_scale;
   DecodeReq r[kMaxBatch];
 };
@@ -403,20 +410,19 @@ __global__ void __launch_bounds__(kCombThreads) decode_combine(const __grid_cons
 // ------------------------------------------------- tensor-core path: D = DV = 128
 // 16-bit K/V rows with 16-byte aligned 128-element records.  A CTA takes one
 // split (128 keys) of one KV head for one query row.  Thread t resolves the
-// slot of key t; the warps copy the 128 key rows (two 256-byte rows per warp
-// instruction, cp.async) into a 128-byte swizzled K-major tile, and one
-// tcgen05.mma chain computes the whole split:
-//   phase 1  S[key][h]  = K_split (M = 128 keys) x q^T (N = 16 heads, G used)
-//   phase 2  O^T[x][h]  = V_split^T (M = 128 dims, MN-major) x P^T (N = 16)
+// slot of key t; the warps copy the 128 key rows, later the 128 value rows
+// (two 256-byte rows per warp instruction, cp.async), into one 128-byte
+// swizzled tile, and two tcgen05.mma chains compute the split:
+//   S[key][h]  = K_split (M = 128 keys) x q^T (N = 16 heads, G used)
+//   O^T[x][h]  = V_split^T (M = 128 dims, MN-major) x P^T (N = 16)
 // with the accumulator in 32 TMEM columns, read back one lane (key or
-// dimension) per thread.  Gates use the hardware 2^x and reciprocal,
-// identically in both phases.
+// dimension) per thread.  Gates use the hardware 2^x and reciprocal.
 constexpr int kFastD = 128;
 constexpr int kTcN = 16;            // MMA N: the G query heads, zero-padded
 constexpr uint32_t kTcCols = 32;    // TMEM columns per CTA (allocation unit)
 constexpr uint32_t kTileB = 32768;  // 128 rows x 256 B
 constexpr uint32_t kSmallB = kTcN * 256;
-constexpr size_t kTcSmem = 1024 + kTileB + kSmallB;  // 1024: alignment slack
+constexpr size_t kOnepassSmem = 1024 + kTileB + kSmallB;  // the K / V tile and the q / P tile
 
 __device__ __forceinline__ float fast_gate(float logit) {  // 1 / (1 + e^-logit)
   return rcp_approx(1.f + ex2(-logit * 1.4426950408889634f));
@@ -437,10 +443,10 @@ __device__ __forceinline__ void copy_split_rows(uint32_t dst, const char* row, c
   }
 }
 
-// bounded wait of every thread on the CTA's MMA barrier
-__device__ __forceinline__ bool wait_mma(uint32_t bar) {
+// bounded wait of every thread on the CTA's MMA barrier (phase `parity`)
+__device__ __forceinline__ bool wait_mma(uint32_t bar, uint32_t parity = 0) {
   const long long t0 = clock64();
-  while (!mbar_try(bar, 0)) {
+  while (!mbar_try(bar, parity)) {
     if (clock64() - t0 > kWaitCycles) return false;
   }
   return true;
@@ -451,185 +457,92 @@ constexpr int umma_fmt() {
   return std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
 }
 
-// phase 1: logits and gate totals of this split's keys for the G heads of KV
-// head g, and (split 0) the q.E tables
+// q.E tables of the G heads of (row i, KV head g): T[h][p] = sum_x q[h][x]
+// E[x][p] into r.table, q from the swizzled q tile `gQ`.  `part` is 16 KB of
+// free shared memory (the vectorised path's per-group partials).  Called by
+// all threads of the CTA.
 template <typename T, int G>
-__global__ void __launch_bounds__(kSplit) decode_qk_tc(const __grid_constant__ DecodeBatch b) {
-  // phase 2 may be scheduled once every CTA of this grid has started; it
-  // waits for this grid's completion before it reads what this grid writes
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  const int s = blockIdx.x, g = blockIdx.y;
-  int64_t i;
-  const DecodeReq& r = request_of(b, blockIdx.z, i);
-  if (s >= r.nsplit) return;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (s == 0 && tid == 0) r.cnt[i * b.hkv + g] = 0;  // arrivals of phase 2
-  extern __shared__ __align__(16) unsigned char dsm[];
-  __shared__ __align__(8) uint64_t bar;
-  __shared__ uint32_t tslot;
-  __shared__ float gred[kSplit / 32][G];
-  const int64_t qp = r.qpos[i];
-  const int64_t nlim = causal_limit(r, qp);
-  const int64_t base = (int64_t)s * kSplit;
-  const int64_t rowh0 = i * b.hq + (int64_t)g * G;
-  if (base >= nlim) {  // split entirely in the future: no keys, no gates
-    if (tid < G) r.gsum[(rowh0 + tid) * r.nsplit + s] = 0.f;
-    return;
-  }
-  const uint32_t sraw = smem_u32(dsm);
-  const uint32_t sK = (sraw + 1023u) & ~1023u, sQ = sK + kTileB;
-  const unsigned char* gQ = dsm + (sQ - sraw);
-  const uint32_t mb = smem_u32(&bar);
-  if (warp == 0) tmem_alloc(smem_u32(&tslot), kTcCols);
-  if (tid == 0) {
-    mbar_init(mb, 1);
-    mbar_init_fence();
-  }
-  const int64_t j = base + tid;
-  int32_t bits = 0;
-  const char* krow = nullptr;
-  if (j < nlim) {
-    bool ok;
-    krow = kv_row<T>(r, j, g, false, ok, kFastD);
-    if (!ok) bits |= CS_ST_SLOT_RANGE;
-  }
-  const char* q0 = r.q + (i * r.q_st + (int64_t)g * G * r.q_sh) * (int64_t)sizeof(T);
-  copy_split_rows(sK, krow, q0);
-  for (int e = tid; e < kTcN * 16; e += kSplit) {  // q rows (heads), zero beyond G
-    const int hh = e >> 4, c = e & 15;
-    const char* src = q0 + (int64_t)hh * r.q_sh * (int64_t)sizeof(T) + c * 16;
-    cp_async16(sQ + sw128(hh, c, kTcN), hh < G ? src : q0, hh < G);
-  }
-  cp_async_wait_all();
-  fence_async_smem();
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = tslot;
-  if (tid == 0) {
-    const uint32_t idesc = umma_idesc(128, kTcN, umma_fmt<T>(), 0, 0);
+__device__ void qe_table(const DecodeBatch& b, const DecodeReq& r, int64_t rowh0,
+                         const unsigned char* gQ, float* part) {
+  const int tid = threadIdx.x;
+  const int npos = b.npos, p4 = npos / 4;
+  const bool vec = r.e_sp == 1 && (npos & 3) == 0 && (r.e_sd & 3) == 0 && p4 <= kSplit &&
+                   kSplit % p4 == 0 && kFastD % (kSplit / p4) == 0 &&
+                   (reinterpret_cast<uintptr_t>(r.E) & 15) == 0;
+  auto qx = [&](int hh, int x) {  // q[hh][x] from the swizzled q tile
+    return Elem<T>::to_f(*reinterpret_cast<const T*>(gQ + sw128(hh, x >> 3, kTcN) + (x & 7) * 2));
+  };
+  if (vec) {
+    // thread t: positions 4(t % p4) .. +3 over a group of dimensions (one
+    // float4 load per dimension, all issued together); the groups'
+    // partials meet in `part` as [ng][G][npos]
+    const int ng = kSplit / p4, dpg = kFastD / ng;
+    const int p0 = (tid % p4) * 4, grp = tid / p4, x0 = grp * dpg;
+    float acc[G][4];
 #pragma unroll
-    for (int kk = 0; kk < kFastD / 16; ++kk) {
-      const uint32_t ko = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
-      const uint32_t qo = (kk >> 2) * (kTcN * 128) + (kk & 3) * 32;
-      tc_mma(tmem, umma_desc(sK + ko, 16, 1024), umma_desc(sQ + qo, 16, 1024), idesc,
-             kk ? 1u : 0u);
-    }
-    tc_commit(mb);
-  }
-  const bool done = wait_mma(mb);
-  tc_fence_after();
-  uint32_t acc[16];
-  CS_TMEM_LD16(tmem + ((uint32_t)(warp * 32) << 16), acc);
-  tmem_wait_ld();
-  if (!done) bits |= CS_ST_TIMEOUT;
-  const bool live = j < nlim && done;
+    for (int hh = 0; hh < G; ++hh) acc[hh][0] = acc[hh][1] = acc[hh][2] = acc[hh][3] = 0.f;
+    for (int x = x0; x < x0 + dpg; x += 8) {
+      float4 ev[8];
 #pragma unroll
-  for (int hh = 0; hh < G; ++hh) {
-    float gt = 0.f;
-    if (live) {
-      const float l = __uint_as_float(acc[hh]) * b.inv_scale;
-      if (!isfinite(l)) bits |= CS_ST_LOGIT_NONFINITE;
-      r.logits[(rowh0 + hh) * r.nk_pad + j] = l;
-      gt = fast_gate(l);
-    }
-    gt = warp_sum(gt);
-    if (lane == 0) gred[warp][hh] = gt;
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) {
-    tc_fence_after();
-    if (!done) wait_mma(mb);  // drain before the columns are released
-    tmem_dealloc(tmem, kTcCols);
-  }
-  if (tid < G) {
-    float tot = 0.f;
-    for (int w = kSplit / 32 - 1; w >= 0; --w) tot += gred[w][tid];
-    r.gsum[(rowh0 + tid) * r.nsplit + s] = tot;
-  }
-  if (s == 0) {  // q.E table: T[h][p] = sum_x q[h][x] E[x][p]
-    const int npos = b.npos, p4 = npos / 4;
-    const bool vec = r.e_sp == 1 && (npos & 3) == 0 && (r.e_sd & 3) == 0 && p4 <= kSplit &&
-                     kSplit % p4 == 0 && kFastD % (kSplit / p4) == 0 &&
-                     (reinterpret_cast<uintptr_t>(r.E) & 15) == 0;
-    auto qx = [&](int hh, int x) {  // q[hh][x] from the swizzled q tile
-      return Elem<T>::to_f(*reinterpret_cast<const T*>(gQ + sw128(hh, x >> 3, kTcN) + (x & 7) * 2));
-    };
-    if (vec) {
-      // thread t: positions 4(t % p4) .. +3 over a group of dimensions (one
-      // float4 load per dimension, all issued together); the groups'
-      // partials meet in the K tile's shared memory, free after the MMA
-      const int ng = kSplit / p4, dpg = kFastD / ng;
-      float* part = reinterpret_cast<float*>(dsm + (sK - sraw));  // [ng][G][npos]
-      const int p0 = (tid % p4) * 4, grp = tid / p4, x0 = grp * dpg;
-      float acc[G][4];
+      for (int u = 0; u < 8; ++u)
+        ev[u] = x + u < x0 + dpg
+                    ? __ldg(reinterpret_cast<const float4*>(r.E + (int64_t)(x + u) * r.e_sd + p0))
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int hh = 0; hh < G; ++hh) acc[hh][0] = acc[hh][1] = acc[hh][2] = acc[hh][3] = 0.f;
-      for (int x = x0; x < x0 + dpg; x += 8) {
-        float4 ev[8];
+      for (int u = 0; u < 8; ++u) {
+        if (x + u >= x0 + dpg) break;
 #pragma unroll
-        for (int u = 0; u < 8; ++u)
-          ev[u] = x + u < x0 + dpg
-                      ? __ldg(reinterpret_cast<const float4*>(r.E + (int64_t)(x + u) * r.e_sd + p0))
-                      : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          if (x + u >= x0 + dpg) break;
-#pragma unroll
-          for (int hh = 0; hh < G; ++hh) {
-            const float qv = qx(hh, x + u);
-            acc[hh][0] = fmaf(qv, ev[u].x, acc[hh][0]);
-            acc[hh][1] = fmaf(qv, ev[u].y, acc[hh][1]);
-            acc[hh][2] = fmaf(qv, ev[u].z, acc[hh][2]);
-            acc[hh][3] = fmaf(qv, ev[u].w, acc[hh][3]);
-          }
+        for (int hh = 0; hh < G; ++hh) {
+          const float qv = qx(hh, x + u);
+          acc[hh][0] = fmaf(qv, ev[u].x, acc[hh][0]);
+          acc[hh][1] = fmaf(qv, ev[u].y, acc[hh][1]);
+          acc[hh][2] = fmaf(qv, ev[u].z, acc[hh][2]);
+          acc[hh][3] = fmaf(qv, ev[u].w, acc[hh][3]);
         }
       }
+    }
 #pragma unroll
-      for (int hh = 0; hh < G; ++hh)
-        *reinterpret_cast<float4*>(part + (grp * G + hh) * npos + p0) =
-            make_float4(acc[hh][0], acc[hh][1], acc[hh][2], acc[hh][3]);
-      __syncthreads();
-      for (int e = tid; e < G * npos; e += kSplit) {
-        float t = 0.f;
-        for (int k = 0; k < ng; ++k) t += part[k * G * npos + e];
-        r.table[rowh0 * npos + e] = t;
-      }
-    } else {  // a thread per (h, p)
-      for (int e = tid; e < G * npos; e += kSplit) {
-        const int hh = e / npos, pp = e - hh * npos;
-        const float* ep = r.E + pp * r.e_sp;
-        float t0 = 0.f, t1 = 0.f;
+    for (int hh = 0; hh < G; ++hh)
+      *reinterpret_cast<float4*>(part + (grp * G + hh) * npos + p0) =
+          make_float4(acc[hh][0], acc[hh][1], acc[hh][2], acc[hh][3]);
+    __syncthreads();
+    for (int e = tid; e < G * npos; e += kSplit) {
+      float t = 0.f;
+      for (int k = 0; k < ng; ++k) t += part[k * G * npos + e];
+      r.table[rowh0 * npos + e] = t;
+    }
+  } else {  // a thread per (h, p)
+    for (int e = tid; e < G * npos; e += kSplit) {
+      const int hh = e / npos, pp = e - hh * npos;
+      const float* ep = r.E + pp * r.e_sp;
+      float t0 = 0.f, t1 = 0.f;
 #pragma unroll 8
-        for (int x = 0; x < kFastD; x += 2) {
-          t0 = fmaf(qx(hh, x), ep[x * r.e_sd], t0);
-          t1 = fmaf(qx(hh, x + 1), ep[(x + 1) * r.e_sd], t1);
-        }
-        r.table[rowh0 * npos + e] = t0 + t1;
+      for (int x = 0; x < kFastD; x += 2) {
+        t0 = fmaf(qx(hh, x), ep[x * r.e_sd], t0);
+        t1 = fmaf(qx(hh, x + 1), ep[(x + 1) * r.e_sd], t1);
       }
+      r.table[rowh0 * npos + e] = t0 + t1;
     }
   }
-  bits = (int32_t)__reduce_or_sync(0xffffffffu, (unsigned)bits);
-  if (lane == 0 && bits) report(r.status, bits);
 }
 
 // Merge the split partials of the G heads of (row i, KV head g) into the
 // output rows in one online pass.  A warp takes up to four heads (G = 8: two
 // warps share a split, four heads each) and every NS-th split, lane x
-// dimensions 4x..4x+3; a batch of U splits is loaded at once (float4
-// partial rows), and the warp's running maximum per head rescales its sums
+// dimensions 4x..4x+3; a batch of U = ROWS / 4 splits is loaded at once
+// (ROWS float4 partial rows), and the warp's running maximum per head
+// rescales its sums
 // when a batch raises it.  The warps' (maximum, sum, accumulator) per head
 // are then merged through `buf` (G * NS * 130 floats of shared memory).
 // Partials written by other CTAs are read through L2.
-template <int G>
+template <int G, int ROWS>
 __device__ void combine_heads(const DecodeBatch& b, const DecodeReq& r, int64_t i, int g,
                               int nsp, float* buf, int32_t& bits) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int nw = kSplit / 32;
   constexpr int GH = G > 4 ? 4 : G;  // heads per warp
   constexpr int NS = nw / (G / GH);  // warps per head, each taking every NS-th split
-  constexpr int U = 8 / GH;          // splits per batch: 8 partial rows in flight
+  constexpr int U = ROWS / GH;       // splits per batch: ROWS partial rows in flight
   static_assert(G * NS * (kFastD + 2) * 4 <= (int)kTileB, "the merge buffer fits the V tile");
   const int h0 = (warp / NS) * GH, sw = warp % NS;
   const int64_t rowh0 = i * b.hq + (int64_t)g * G + h0;
@@ -723,33 +636,114 @@ __device__ void combine_heads(const DecodeBatch& b, const DecodeReq& r, int64_t 
   }
 }
 
-// phase 2: carried count, reverse scan, bias and partial softmax (thread per
-// key), P^T into shared memory as 16-bit weights (the row sums are taken over
-// the same rounded weights), then O^T = V^T P^T on the tensor cores.  The V
-// rows are copied first, before the wait for phase 1, so their latency
-// overlaps the end of phase 1 and the softmax.  The last split of (row, KV
-// head) to finish merges all splits into the output rows.
+// ----------------------------------------------------------- one-pass decode
+// Split state words for the count carried between splits: bits 32..33 hold
+// the state (0 not yet published, 1 the split's own gate total, 2 the total
+// of this split and every newer one), bits 0..31 the float value.
+constexpr uint64_t kAggregate = 1ull << 32, kInclusive = 2ull << 32;
+
+__device__ __forceinline__ void st_relaxed_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Count carried into split s from splits s+1..last of one head (`words`:
+// that head's state words), called by a whole warp: the look-back of a
+// single-pass scan (Merrill and Garland, "Single-pass Parallel Prefix Scan
+// with Decoupled Look-back", 2016).  Lane l reads split t0 + l; a window
+// ends at its first split that holds an inclusive total, the splits before
+// it add their own totals.  Splits past `last` have no keys (inclusive 0).
+// Waits are bounded and record CS_ST_TIMEOUT on expiry.
+__device__ float look_back(const uint64_t* words, int s, int last, int32_t& bits) {
+  const int lane = threadIdx.x & 31;
+  float carry = 0.f;
+  for (int t0 = s + 1; t0 <= last; t0 += 32) {
+    const int t = t0 + lane;
+    uint64_t w = t <= last ? ld_relaxed_u64(words + t) : kInclusive;
+    const long long c0 = clock64();
+    while (__any_sync(0xffffffffu, (w >> 32) == 0)) {
+      if ((w >> 32) == 0) {
+        w = ld_relaxed_u64(words + t);
+        if ((w >> 32) == 0 && clock64() - c0 > kWaitCycles) {
+          bits |= CS_ST_TIMEOUT;
+          w = kInclusive;
+        }
+      }
+    }
+    const unsigned incl = __ballot_sync(0xffffffffu, (w >> 32) == 2);
+    const int first = incl ? __ffs(incl) - 1 : 32;
+    carry += warp_sum(lane <= first ? __uint_as_float((uint32_t)w) : 0.f);
+    if (incl) break;
+  }
+  return carry;
+}
+
+// Zeroes the one-pass flags (the first n16 16-byte words of the batch
+// workspace) and lets the dependent decode grid start at once.
+__global__ void __launch_bounds__(256) decode_zero_flags(uint4* p, int64_t n16) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  for (int64_t e = (int64_t)blockIdx.x * 256 + threadIdx.x; e < n16; e += (int64_t)gridDim.x * 256)
+    p[e] = make_uint4(0u, 0u, 0u, 0u);
+}
+
+// One-pass decode for the tensor-core shapes: a CTA takes one 128-key split
+// of one (row, KV head).  Its K rows land in the tile, S = K q^T runs on the
+// tensor cores and stays in registers, and the V rows are then copied into
+// the same tile while the CTA publishes the split's gate totals, takes the
+// count carried from the newer splits by a look-back over their state
+// words, and computes the interpolated bias and a partial softmax; O^T =
+// V^T P^T follows, and the last split of (row, KV head) to finish merges the
+// partials.  One 32 KB tile keeps five CTAs on an SM.
+//
+// Block k takes split nsplit - 1 - k / groups of group k % groups, so the
+// newest splits of every group come first and a CTA only waits on blocks of
+// lower index, which the hardware dispatches no later than its own (the
+// order single-pass scans rely on); every wait is bounded all the same.
+// The group's newest split with visible keys computes the q.E tables and
+// publishes them with a flag; a split whose carried count already reaches
+// the last position for every head needs only T[h][npos - 1], which it
+// computes itself from the last column of E.  The state words, table flags
+// and arrival counters are zeroed by decode_zero_flags, the grid before
+// this one; this grid is its programmatic dependent, so the copies and S
+// start at once and only the first flag access waits for the zeroing.
 template <typename T, int G>
-__global__ void __launch_bounds__(kSplit) decode_pv_tc(const __grid_constant__ DecodeBatch b) {
-  const int s = blockIdx.x, g = blockIdx.y;
-  int64_t i;
-  const DecodeReq& r = request_of(b, blockIdx.z, i);
-  if (s >= r.nsplit) return;
+__global__ void __launch_bounds__(kSplit, 5) decode_onepass_tc(const __grid_constant__ DecodeBatch b) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int npos = b.npos;
   extern __shared__ __align__(16) unsigned char dsm[];
   __shared__ __align__(8) uint64_t bar;
   __shared__ uint32_t tslot;
-  __shared__ float wtot[G][kSplit / 32];
-  __shared__ float carry0[G];
-  __shared__ float red[G][kSplit / 32];
-  __shared__ float mmax[G];
   __shared__ int last_split;
+  __shared__ float wtot[G][kSplit / 32];
+  __shared__ float red[G][kSplit / 32];
+  __shared__ float tsp[G][kSplit / 32];
+  __shared__ float carry0[G];
+  __shared__ float mmax[G];
+  const int groups = b.rows * b.hkv;
+  const int si = (int)(blockIdx.x / groups), grp = (int)(blockIdx.x - si * groups);
+  const int g = grp % b.hkv;
+  int64_t i;
+  const DecodeReq& r = request_of(b, grp / b.hkv, i);
+  if (si >= r.nsplit) return;
+  const int s = r.nsplit - 1 - si;
+  const int npos = b.npos;
   const int64_t qp = r.qpos[i];
   const int64_t nlim = causal_limit(r, qp);
   const int64_t base = (int64_t)s * kSplit;
   const int64_t rowh0 = i * b.hq + (int64_t)g * G;
-  if (base >= nlim) {  // split entirely in the future: no partial
+  const int64_t gl = i * b.hkv + g;
+  if (base >= nlim) {  // split entirely in the future: nothing to publish
     if (s == 0) {      // no visible key at all: zero output rows
       for (int e = tid; e < G * kFastD; e += kSplit) {
         char* orow = r.out + (i * r.o_st + (int64_t)(g * G + e / kFastD) * r.o_sh) *
@@ -764,10 +758,11 @@ __global__ void __launch_bounds__(kSplit) decode_pv_tc(const __grid_constant__ D
     }
     return;
   }
+  const int last = (int)((nlim - 1) / kSplit);  // newest split with visible keys
   const uint32_t sraw = smem_u32(dsm);
-  const uint32_t sV = (sraw + 1023u) & ~1023u, sP = sV + kTileB;
-  unsigned char* gP = dsm + (sP - sraw);
-  float* tab = reinterpret_cast<float*>(gP + kSmallB);  // [G][npos]
+  const uint32_t sT = (sraw + 1023u) & ~1023u, sQ = sT + kTileB;  // K, then V; q, then P
+  unsigned char* gQ = dsm + (sQ - sraw);
+  float* tile = reinterpret_cast<float*>(dsm + (sT - sraw));
   const uint32_t mb = smem_u32(&bar);
   if (warp == 0) tmem_alloc(smem_u32(&tslot), kTcCols);
   if (tid == 0) {
@@ -777,31 +772,72 @@ __global__ void __launch_bounds__(kSplit) decode_pv_tc(const __grid_constant__ D
   const int64_t j = base + tid;
   const bool live = j < nlim;
   int32_t bits = 0;
+  // E[tid][npos - 1], for T[h][npos - 1] of saturated splits
+  const float elast = __ldg(r.E + (int64_t)tid * r.e_sd + (int64_t)(npos - 1) * r.e_sp);
+  const char* krow = nullptr;
   const char* vrow = nullptr;
   if (live) {
-    bool ok;
-    vrow = kv_row<T>(r, j, g, true, ok, kFastD);
-    if (!ok) bits |= CS_ST_SLOT_RANGE;
+    bool okk, okv;
+    krow = kv_row<T>(r, j, g, false, okk, kFastD);
+    vrow = kv_row<T>(r, j, g, true, okv, kFastD);
+    if (!okk || !okv) bits |= CS_ST_SLOT_RANGE;
   }
-  copy_split_rows(sV, vrow, reinterpret_cast<const char*>(r.logits));
-  for (int e = tid; e < (kTcN - G) * 16; e += kSplit)  // P rows beyond G: zero
-    *reinterpret_cast<uint4*>(gP + sw128(G + (e >> 4), e & 15, kTcN)) = make_uint4(0, 0, 0, 0);
-  asm volatile("griddepcontrol.wait;" ::: "memory");  // phase 1 complete and visible
-  const int last = (int)((nlim - 1) / kSplit);
-  // count carried from the newer splits: a warp per head, lanes over splits
-  for (int hh = warp; hh < G; hh += kSplit / 32) {
-    float c = 0.f;
-    for (int t = s + 1 + lane; t <= last; t += 32) c += r.gsum[(rowh0 + hh) * r.nsplit + t];
-    c = warp_sum(c);
-    if (lane == 0) carry0[hh] = c;
+  const char* q0 = r.q + (i * r.q_st + (int64_t)g * G * r.q_sh) * (int64_t)sizeof(T);
+  copy_split_rows(sT, krow, q0);
+  for (int e = tid; e < kTcN * 16; e += kSplit) {  // q rows (heads), zero beyond G
+    const int hh = e >> 4, c = e & 15;
+    const char* src = q0 + (int64_t)hh * r.q_sh * (int64_t)sizeof(T) + c * 16;
+    cp_async16(sQ + sw128(hh, c, kTcN), hh < G ? src : q0, hh < G);
   }
-  for (int e = tid; e < G * npos; e += kSplit) tab[e] = r.table[rowh0 * npos + e];
+  cp_async_wait_all();
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tslot;
+  if (tid == 0) {
+    const uint32_t idesc = umma_idesc(128, kTcN, umma_fmt<T>(), 0, 0);
+#pragma unroll
+    for (int kk = 0; kk < kFastD / 16; ++kk) {
+      const uint32_t ko = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
+      const uint32_t qo = (kk >> 2) * (kTcN * 128) + (kk & 3) * 32;
+      tc_mma(tmem, umma_desc(sT + ko, 16, 1024), umma_desc(sQ + qo, 16, 1024), idesc,
+             kk ? 1u : 0u);
+    }
+    tc_commit(mb);
+  }
+  // partial sums of T[h][npos - 1] = q[h] . E[:, npos - 1] while S runs
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh) {
+    const float qv = Elem<T>::to_f(
+        *reinterpret_cast<const T*>(gQ + sw128(hh, tid >> 3, kTcN) + (tid & 7) * 2));
+    const float v = warp_sum(qv * elast);
+    if (lane == 0) tsp[hh][warp] = v;
+  }
+  const bool done1 = wait_mma(mb, 0);  // S complete: the tile's K rows are read
+  tc_fence_after();
+  uint32_t acc[16];
+  CS_TMEM_LD16(tmem + ((uint32_t)(warp * 32) << 16), acc);
+  tmem_wait_ld();
+  if (!done1) bits |= CS_ST_TIMEOUT;
+  if (s == last) {  // q.E tables, with the tile as scratch before V arrives
+    qe_table<T, G>(b, r, rowh0, gQ, tile);
+    __threadfence();
+    __syncthreads();
+  }
+  copy_split_rows(sT, vrow, q0);  // in flight until the PV product
+  cp_async_commit();
+  // logits, gates and the reverse scan of the gates within each warp
   float lg[G], suf[G];
 #pragma unroll
   for (int hh = 0; hh < G; ++hh) {
-    lg[hh] = live ? r.logits[(rowh0 + hh) * r.nk_pad + j] : 0.f;
-    float v = live ? fast_gate(lg[hh]) : 0.f;
-    // reverse inclusive scan within the warp (lane l sums lanes l..31)
+    float l = 0.f, v = 0.f;
+    if (live && done1) {
+      l = __uint_as_float(acc[hh]) * b.inv_scale;
+      if (!isfinite(l)) bits |= CS_ST_LOGIT_NONFINITE;
+      v = fast_gate(l);
+    }
+    lg[hh] = l;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const float t = __shfl_down_sync(0xffffffffu, v, o);
@@ -810,20 +846,72 @@ __global__ void __launch_bounds__(kSplit) decode_pv_tc(const __grid_constant__ D
     suf[hh] = v;
     if (lane == 0) wtot[hh][warp] = v;
   }
+  tc_fence_before();
   __syncthreads();
+  // the flags were zeroed by the preceding grid (decode_zero_flags)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // publish the split's gate totals, then look back for the carried count
+  // (a warp per head)
+  for (int hh = warp; hh < G; hh += kSplit / 32) {
+    float agg = 0.f;
+#pragma unroll
+    for (int w = 0; w < kSplit / 32; ++w) agg += wtot[hh][w];
+    uint64_t* words = r.lb + (rowh0 + hh) * r.nsplit;
+    float carry = 0.f;
+    if (s < last) {
+      if (lane == 0) st_relaxed_u64(words + s, kAggregate | __float_as_uint(agg));
+      carry = look_back(words, s, last, bits);
+    }
+    if (lane == 0) {
+      st_relaxed_u64(words + s, kInclusive | __float_as_uint(carry + agg));
+      carry0[hh] = carry;
+    }
+  }
+  __syncthreads();
+  // the q.E tables are read by the splits whose counts stay below the last
+  // position for some head
   const float top = (float)(npos - 1);
+  bool saturated = s != last;
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh) saturated = saturated && carry0[hh] >= top;
+  if (!saturated) {
+    if (tid == 0) {
+      if (s == last) {
+        st_release_u32(r.tstat + gl, 1u);
+      } else {
+        const long long c0 = clock64();
+        while (ld_acquire_u32(r.tstat + gl) == 0u) {
+          if (clock64() - c0 > kWaitCycles) {
+            bits |= CS_ST_TIMEOUT;
+            break;
+          }
+        }
+      }
+    }
+    __syncthreads();
+  }
+  // counts, bias and the split's softmax
   float score[G];
 #pragma unroll
   for (int hh = 0; hh < G; ++hh) {
     float c = carry0[hh];
     for (int w = kSplit / 32 - 1; w > warp; --w) c += wtot[hh][w];
-    const float R = suf[hh] + c;
-    const float pos = R < 0.f ? 0.f : (R > top ? top : R);
-    const int lo = (int)floorf(pos);
-    const int hi = lo + 1 < npos ? lo + 1 : npos - 1;
-    const float f = pos - (float)lo;
-    const float tlo = tab[hh * npos + lo];
-    score[hh] = live ? lg[hh] + (tlo + f * (tab[hh * npos + hi] - tlo)) : -INFINITY;
+    float bias;
+    if (saturated) {  // every count >= carry >= npos - 1: the last table entry
+      bias = 0.f;
+#pragma unroll
+      for (int w = 0; w < kSplit / 32; ++w) bias += tsp[hh][w];
+    } else {
+      const float R = suf[hh] + c;
+      const float pos = R < 0.f ? 0.f : (R > top ? top : R);
+      const int lo = (int)floorf(pos);
+      const int hi = lo + 1 < npos ? lo + 1 : npos - 1;
+      const float f = pos - (float)lo;
+      const float* trow = r.table + (rowh0 + hh) * npos;
+      const float tlo = __ldcg(trow + lo);
+      bias = tlo + f * (__ldcg(trow + hi) - tlo);
+    }
+    score[hh] = live ? lg[hh] + bias : -INFINITY;
     const float v = warp_max(score[hh]);
     if (lane == 0) red[hh][warp] = v;
   }
@@ -834,25 +922,25 @@ __global__ void __launch_bounds__(kSplit) decode_pv_tc(const __grid_constant__ D
     mmax[tid] = m;
   }
   __syncthreads();
+  // P^T over the q tile (free after S; its rows beyond G stay zero)
 #pragma unroll
   for (int hh = 0; hh < G; ++hh) {
     const T wq = Elem<T>::from_f(live ? expf(score[hh] - mmax[hh]) : 0.f);
-    *reinterpret_cast<T*>(gP + sw128(hh, tid >> 3, kTcN) + (tid & 7) * 2) = wq;
+    *reinterpret_cast<T*>(gQ + sw128(hh, tid >> 3, kTcN) + (tid & 7) * 2) = wq;
     const float v = warp_sum(Elem<T>::to_f(wq));
     if (lane == 0) wtot[hh][warp] = v;
   }
-  cp_async_wait_all();
+  cp_async_wait_all();  // V
   fence_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = tslot;
   if (tid == 0) {
     const uint32_t idesc = umma_idesc(128, kTcN, umma_fmt<T>(), 1, 0);  // A = V^T, MN-major
 #pragma unroll
     for (int kk = 0; kk < kSplit / 16; ++kk) {
       const uint32_t po = (kk >> 2) * (kTcN * 128) + (kk & 3) * 32;
-      tc_mma(tmem, umma_desc(sV + kk * 2048, 16384, 1024), umma_desc(sP + po, 16, 1024), idesc,
+      tc_mma(tmem, umma_desc(sT + kk * 2048, 16384, 1024), umma_desc(sQ + po, 16, 1024), idesc,
              kk ? 1u : 0u);
     }
     tc_commit(mb);
@@ -863,32 +951,31 @@ __global__ void __launch_bounds__(kSplit) decode_pv_tc(const __grid_constant__ D
     r.pm[(rowh0 + tid) * r.nsplit + s] = mmax[tid];
     r.pl[(rowh0 + tid) * r.nsplit + s] = l;
   }
-  const bool done = wait_mma(mb);
+  const bool done2 = wait_mma(mb, 1);
   tc_fence_after();
-  uint32_t acc[16];
   CS_TMEM_LD16(tmem + ((uint32_t)(warp * 32) << 16), acc);
   tmem_wait_ld();
-  if (!done) bits |= CS_ST_TIMEOUT;
+  if (!done2) bits |= CS_ST_TIMEOUT;
 #pragma unroll
   for (int hh = 0; hh < G; ++hh)
     r.po[((rowh0 + hh) * r.nsplit + s) * kFastD + tid] = __uint_as_float(acc[hh]);
-  __threadfence();  // this split's partial is visible before its arrival is counted
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    if (!done) wait_mma(mb);
+    if (!done2) wait_mma(mb, 1);  // drain before the columns are released
     tmem_dealloc(tmem, kTcCols);
   }
-  const int nsp = last + 1;  // splits with visible keys
-  if (tid == 0) last_split = atomicAdd(&r.cnt[i * b.hkv + g], 1) == nsp - 1;
-  __syncthreads();
-  if (last_split) {
+  if (tid == 0) {
+    // the CTA's partial (ordered before this thread by the barrier) is
+    // visible before its arrival is counted
     __threadfence();
-    // the V tile is idle: this CTA's product was read back above
-    combine_heads<G>(b, r, i, g, nsp, reinterpret_cast<float*>(dsm + (sV - sraw)), bits);
-    if (tid == 0) r.cnt[i * b.hkv + g] = 0;
+    last_split = atomicAdd(&r.cnt[gl], 1) == last;
+    if (last_split) __threadfence();
   }
+  __syncthreads();
+  if (last_split)  // the tile is idle: this CTA's product was read back above
+    combine_heads<G, 8>(b, r, i, g, last + 1, tile, bits);
   bits = (int32_t)__reduce_or_sync(0xffffffffu, (unsigned)bits);
   if (lane == 0 && bits) report(r.status, bits);
 }
@@ -934,9 +1021,15 @@ bool decode_supported(const cs_attn_params* p) {
   return true;
 }
 
+// Workspace of one request, in floats.  The first `zero` floats are zeroed
+// before each one-pass launch (split state words, table flags, arrival
+// counters); a batch places the zeroed parts of all its requests first, then
+// their data parts.
 struct Layout {
   int nsplit, nk_pad;
-  int64_t logits, gsum, table, po, pm, pl, cnt, total;  // 4-byte offsets / count
+  int64_t lb, tstat, cnt, zero;                   // offsets in the zeroed part
+  int64_t logits, gsum, table, po, pm, pl, data;  // offsets in the data part
+  int64_t total;
 };
 
 Layout layout_of(const cs_attn_params* p) {
@@ -950,14 +1043,19 @@ Layout layout_of(const cs_attn_params* p) {
     off += (n + 63) / 64 * 64;  // 256-byte aligned sections
     return o;
   };
+  L.lb = take(rows * L.nsplit * 2);  // 64-bit words
+  L.tstat = take((int64_t)p->nq * p->hkv);
+  L.cnt = take((int64_t)p->nq * p->hkv);
+  L.zero = off;
+  off = 0;
   L.logits = take(rows * L.nk_pad);
   L.gsum = take(rows * L.nsplit);
   L.table = take(rows * p->npos);
   L.po = take(rows * L.nsplit * p->dv);
   L.pm = take(rows * L.nsplit);
   L.pl = take(rows * L.nsplit);
-  L.cnt = take((int64_t)p->nq * p->hkv);
-  L.total = off;
+  L.data = off;
+  L.total = L.zero + L.data;
   return L;
 }
 
@@ -967,7 +1065,8 @@ bool same_shape(const cs_attn_params* a, const cs_attn_params* b) {
          a->scale == b->scale;
 }
 
-void fill_request(DecodeReq& q, const cs_attn_params* p, float* ws, const Layout& L, int row0) {
+void fill_request(DecodeReq& q, const cs_attn_params* p, float* zs, float* ws, const Layout& L,
+                  int row0) {
   q.q = static_cast<const char*>(p->q);
   q.q_st = p->q_stride_tok;
   q.q_sh = p->q_stride_head;
@@ -994,12 +1093,30 @@ void fill_request(DecodeReq& q, const cs_attn_params* p, float* ws, const Layout
   q.po = ws + L.po;
   q.pm = ws + L.pm;
   q.pl = ws + L.pl;
-  q.cnt = reinterpret_cast<int*>(ws + L.cnt);
+  q.cnt = reinterpret_cast<int*>(zs + L.cnt);
+  q.lb = reinterpret_cast<uint64_t*>(zs + L.lb);
+  q.tstat = reinterpret_cast<uint32_t*>(zs + L.tstat);
   q.nq = p->nq;
   q.nk = p->nk;
   q.nsplit = L.nsplit;
   q.nk_pad = L.nk_pad;
   q.row0 = row0;
+}
+
+// Raises the dynamic shared memory limit of `kern` on the current device,
+// once per device.
+template <typename K>
+bool smem_configured(K kern, int bytes) {
+  static std::atomic<uint64_t> done{0};  // bit d: device d configured
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return true;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
+      cudaSuccess)
+    return false;
+  done.fetch_or(bit, std::memory_order_release);
+  return true;
 }
 
 int launch_batch(const cs_attn_params* ps, int count, char* workspace, cudaStream_t stream) {
@@ -1014,42 +1131,56 @@ int launch_batch(const cs_attn_params* ps, int count, char* workspace, cudaStrea
   b.G = p0->hq / p0->hkv;
   b.out_dtype = p0->out_dtype;
   b.inv_scale = (float)(1.0 / p0->scale);
+  Layout L[kMaxBatch];
+  int64_t zero = 0, data = 0;  // floats
+  for (int k = 0; k < count; ++k) {
+    L[k] = layout_of(&ps[k]);
+    zero += L[k].zero;
+  }
+  float* ws = reinterpret_cast<float*>(workspace);
   int rows = 0, nsplit_max = 0;
-  int64_t off = 0;
+  int64_t zoff = 0;
   for (int k = 0; k < count; ++k) {
     const cs_attn_params* p = &ps[k];
+    float* zs = ws + zoff;
+    float* ds = ws + zero + data;
+    zoff += L[k].zero;
+    data += L[k].data;
     if (p->nq == 0) continue;
-    const Layout L = layout_of(p);
-    fill_request(b.r[b.count], p, reinterpret_cast<float*>(workspace + off), L, rows);
-    off += L.total * (int64_t)sizeof(float);
+    fill_request(b.r[b.count], p, zs, ds, L[k], rows);
     rows += p->nq;
-    nsplit_max = L.nsplit > nsplit_max ? L.nsplit : nsplit_max;
+    nsplit_max = L[k].nsplit > nsplit_max ? L[k].nsplit : nsplit_max;
     ++b.count;
   }
   if (b.count == 0) return CS_OK;
-  const dim3 grid(nsplit_max, b.hkv, rows);
-  const size_t smem_pv = kTcSmem + (size_t)b.G * b.npos * sizeof(float);
-  bool fast = smem_pv <= 48 * 1024;
+  b.rows = rows;
+  bool fast = true;
   for (int k = 0; k < count; ++k) fast = fast && (ps[k].nq == 0 || fast_decode_ok(&ps[k]));
   if (fast) {
-    // phase 2 is a programmatic dependent launch: its CTAs may start (and
-    // issue their V copies) while the last CTAs of phase 1 run
+    const int64_t n16 = zero / 4;  // zero is a multiple of 64 floats
+    decode_zero_flags<<<(unsigned)std::min<int64_t>((n16 + 255) / 256, 148), 256, 0, stream>>>(
+        reinterpret_cast<uint4*>(workspace), n16);
+    // the decode grid is a programmatic dependent of the zeroing grid
     cudaLaunchAttribute pdl[1];
     pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     pdl[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = grid;
+    cfg.gridDim = dim3((unsigned)((int64_t)rows * b.hkv * nsplit_max));
     cfg.blockDim = dim3(kSplit);
-    cfg.dynamicSmemBytes = smem_pv;
+    cfg.dynamicSmemBytes = kOnepassSmem;
     cfg.stream = stream;
     cfg.attrs = pdl;
     cfg.numAttrs = 1;
-    cudaError_t err = cudaSuccess;
+    int rc = CS_OK;
     auto go = [&](auto tag, auto gtag) {
       using T = decltype(tag);
       constexpr int G = decltype(gtag)::value;
-      decode_qk_tc<T, G><<<grid, kSplit, kTcSmem, stream>>>(b);
-      err = cudaLaunchKernelEx(&cfg, decode_pv_tc<T, G>, b);
+      auto kern = decode_onepass_tc<T, G>;
+      if (!smem_configured(kern, (int)kOnepassSmem)) {
+        rc = CS_ERR_CUDA;
+        return;
+      }
+      if (cudaLaunchKernelEx(&cfg, kern, b) != cudaSuccess) rc = CS_ERR_CUDA;
     };
     auto by_g = [&](auto tag) {
       switch (b.G) {
@@ -1061,8 +1192,9 @@ int launch_batch(const cs_attn_params* ps, int count, char* workspace, cudaStrea
     };
     if (p0->in_dtype == CS_BF16) by_g(__nv_bfloat16{});
     else by_g(__half{});
-    if (err != cudaSuccess) return CS_ERR_CUDA;
+    if (rc != CS_OK) return rc;
   } else {
+    const dim3 grid(nsplit_max, b.hkv, rows);
     const size_t smem2 = (size_t)(b.G * b.npos + b.G * kSplit) * sizeof(float);
     if (smem2 > 48 * 1024) return CS_ERR_UNSUPPORTED;
     if (p0->in_dtype == CS_BF16) {
