@@ -89,18 +89,24 @@ __device__ __forceinline__ int64_t causal_limit(const DecodeReq& r, int64_t qp) 
   return lo;
 }
 
+// K (v false) or V row of key j, head g; `slot` is slots[j] on the paged path
 template <typename T>
-__device__ __forceinline__ const char* kv_row(const DecodeReq& r, int64_t j, int g, bool v,
-                                              bool& ok, int d) {
+__device__ __forceinline__ const char* kv_row_at(const DecodeReq& r, int64_t slot, int64_t j,
+                                                 int g, bool v, bool& ok, int d) {
   if (r.slots) {
-    const int64_t s = r.slots[j];
-    ok = r.pv.valid(s);
+    ok = r.pv.valid(slot);
     if (!ok) return nullptr;
-    return r.pv.addr(s, g, v ? r.pv.head_dim : 0);
+    return r.pv.addr(slot, g, v ? r.pv.head_dim : 0);
   }
   ok = true;
   return (v ? r.v : r.k) +
          (j * (v ? r.v_st : r.k_st) + (int64_t)g * (v ? r.v_sh : r.k_sh)) * (int64_t)sizeof(T);
+}
+
+template <typename T>
+__device__ __forceinline__ const char* kv_row(const DecodeReq& r, int64_t j, int g, bool v,
+                                              bool& ok, int d) {
+  return kv_row_at<T>(r, r.slots ? r.slots[j] : 0, j, g, v, ok, d);
 }
 
 // phase 1: logits of this split's keys for the G heads of KV head g, gate
@@ -481,15 +487,16 @@ __device__ void qe_table(const DecodeBatch& b, const DecodeReq& r, int64_t rowh0
     float acc[G][4];
 #pragma unroll
     for (int hh = 0; hh < G; ++hh) acc[hh][0] = acc[hh][1] = acc[hh][2] = acc[hh][3] = 0.f;
-    for (int x = x0; x < x0 + dpg; x += 8) {
-      float4 ev[8];
+    constexpr int UB = G >= 8 ? 4 : 8;  // float4 loads in flight (registers)
+    for (int x = x0; x < x0 + dpg; x += UB) {
+      float4 ev[UB];
 #pragma unroll
-      for (int u = 0; u < 8; ++u)
+      for (int u = 0; u < UB; ++u)
         ev[u] = x + u < x0 + dpg
                     ? __ldg(reinterpret_cast<const float4*>(r.E + (int64_t)(x + u) * r.e_sd + p0))
                     : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
+      for (int u = 0; u < UB; ++u) {
         if (x + u >= x0 + dpg) break;
 #pragma unroll
         for (int hh = 0; hh < G; ++hh) {
@@ -738,6 +745,9 @@ __global__ void __launch_bounds__(kSplit, 5) decode_onepass_tc(const __grid_cons
   if (si >= r.nsplit) return;
   const int s = r.nsplit - 1 - si;
   const int npos = b.npos;
+  const int64_t j = (int64_t)s * kSplit + tid;
+  // the key's slot, loaded beside the query position it is masked by
+  const int64_t slot = r.slots != nullptr && j < r.nk ? __ldg(r.slots + j) : 0;
   const int64_t qp = r.qpos[i];
   const int64_t nlim = causal_limit(r, qp);
   const int64_t base = (int64_t)s * kSplit;
@@ -769,7 +779,6 @@ __global__ void __launch_bounds__(kSplit, 5) decode_onepass_tc(const __grid_cons
     mbar_init(mb, 1);
     mbar_init_fence();
   }
-  const int64_t j = base + tid;
   const bool live = j < nlim;
   int32_t bits = 0;
   // E[tid][npos - 1], for T[h][npos - 1] of saturated splits
@@ -778,8 +787,8 @@ __global__ void __launch_bounds__(kSplit, 5) decode_onepass_tc(const __grid_cons
   const char* vrow = nullptr;
   if (live) {
     bool okk, okv;
-    krow = kv_row<T>(r, j, g, false, okk, kFastD);
-    vrow = kv_row<T>(r, j, g, true, okv, kFastD);
+    krow = kv_row_at<T>(r, slot, j, g, false, okk, kFastD);
+    vrow = kv_row_at<T>(r, slot, j, g, true, okv, kFastD);
     if (!okk || !okv) bits |= CS_ST_SLOT_RANGE;
   }
   const char* q0 = r.q + (i * r.q_st + (int64_t)g * G * r.q_sh) * (int64_t)sizeof(T);
@@ -820,13 +829,9 @@ __global__ void __launch_bounds__(kSplit, 5) decode_onepass_tc(const __grid_cons
   CS_TMEM_LD16(tmem + ((uint32_t)(warp * 32) << 16), acc);
   tmem_wait_ld();
   if (!done1) bits |= CS_ST_TIMEOUT;
-  if (s == last) {  // q.E tables, with the tile as scratch before V arrives
-    qe_table<T, G>(b, r, rowh0, gQ, tile);
-    __threadfence();
-    __syncthreads();
-  }
-  copy_split_rows(sT, vrow, q0);  // in flight until the PV product
-  cp_async_commit();
+  // V rows into the tile, in flight until the PV product (the newest split
+  // first uses the tile for its q.E tables, after publishing its totals)
+  if (s != last) copy_split_rows(sT, vrow, q0);
   // logits, gates and the reverse scan of the gates within each warp
   float lg[G], suf[G];
 #pragma unroll
@@ -866,6 +871,12 @@ __global__ void __launch_bounds__(kSplit, 5) decode_onepass_tc(const __grid_cons
       st_relaxed_u64(words + s, kInclusive | __float_as_uint(carry + agg));
       carry0[hh] = carry;
     }
+  }
+  if (s == last) {  // q.E tables, with the tile as scratch before V arrives
+    qe_table<T, G>(b, r, rowh0, gQ, tile);
+    __threadfence();
+    __syncthreads();
+    copy_split_rows(sT, vrow, q0);
   }
   __syncthreads();
   // the q.E tables are read by the splits whose counts stay below the last
