@@ -736,7 +736,6 @@ __global__ void __launch_bounds__(kSplit, 5) decode_onepass_tc(const __grid_cons
   __shared__ float red[G][kSplit / 32];
   __shared__ float tsp[G][kSplit / 32];
   __shared__ float carry0[G];
-  __shared__ float mmax[G];
   const int groups = b.rows * b.hkv;
   const int si = (int)(blockIdx.x / groups), grp = (int)(blockIdx.x - si * groups);
   const int g = grp % b.hkv;
@@ -855,18 +854,28 @@ __global__ void __launch_bounds__(kSplit, 5) decode_onepass_tc(const __grid_cons
   __syncthreads();
   // the flags were zeroed by the preceding grid (decode_zero_flags)
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  // publish the split's gate totals, then look back for the carried count
-  // (a warp per head)
+  // publish the split's gate totals (warp h, head h), take the per-warp
+  // maxima of the logits while the newer splits publish theirs, then look
+  // back for the carried count (a warp per head)
+  if (s < last && lane == 0) {
+    for (int hh = warp; hh < G; hh += kSplit / 32) {
+      float agg = 0.f;
+#pragma unroll
+      for (int w = 0; w < kSplit / 32; ++w) agg += wtot[hh][w];
+      st_relaxed_u64(r.lb + (rowh0 + hh) * r.nsplit + s, kAggregate | __float_as_uint(agg));
+    }
+  }
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh) {
+    const float v = warp_max(live ? lg[hh] : -INFINITY);
+    if (lane == 0) red[hh][warp] = v;
+  }
   for (int hh = warp; hh < G; hh += kSplit / 32) {
     float agg = 0.f;
 #pragma unroll
     for (int w = 0; w < kSplit / 32; ++w) agg += wtot[hh][w];
     uint64_t* words = r.lb + (rowh0 + hh) * r.nsplit;
-    float carry = 0.f;
-    if (s < last) {
-      if (lane == 0) st_relaxed_u64(words + s, kAggregate | __float_as_uint(agg));
-      carry = look_back(words, s, last, bits);
-    }
+    const float carry = s < last ? look_back(words, s, last, bits) : 0.f;
     if (lane == 0) {
       st_relaxed_u64(words + s, kInclusive | __float_as_uint(carry + agg));
       carry0[hh] = carry;
@@ -901,18 +910,27 @@ __global__ void __launch_bounds__(kSplit, 5) decode_onepass_tc(const __grid_cons
     }
     __syncthreads();
   }
-  // counts, bias and the split's softmax
-  float score[G];
+  // counts, bias and the split's softmax maximum
+  float score[G], m[G];
+  if (saturated) {
+    // every count >= carry >= npos - 1: the last table entry, the same for
+    // all keys of the head, so the maximum is the logits' maximum plus it
 #pragma unroll
-  for (int hh = 0; hh < G; ++hh) {
-    float c = carry0[hh];
-    for (int w = kSplit / 32 - 1; w > warp; --w) c += wtot[hh][w];
-    float bias;
-    if (saturated) {  // every count >= carry >= npos - 1: the last table entry
-      bias = 0.f;
+    for (int hh = 0; hh < G; ++hh) {
+      float tb = 0.f, mx = -INFINITY;
 #pragma unroll
-      for (int w = 0; w < kSplit / 32; ++w) bias += tsp[hh][w];
-    } else {
+      for (int w = 0; w < kSplit / 32; ++w) {
+        tb += tsp[hh][w];
+        mx = fmaxf(mx, red[hh][w]);
+      }
+      score[hh] = lg[hh] + tb;  // every key of a saturated split is visible
+      m[hh] = mx + tb;
+    }
+  } else {
+#pragma unroll
+    for (int hh = 0; hh < G; ++hh) {
+      float c = carry0[hh];
+      for (int w = kSplit / 32 - 1; w > warp; --w) c += wtot[hh][w];
       const float R = suf[hh] + c;
       const float pos = R < 0.f ? 0.f : (R > top ? top : R);
       const int lo = (int)floorf(pos);
@@ -920,26 +938,25 @@ __global__ void __launch_bounds__(kSplit, 5) decode_onepass_tc(const __grid_cons
       const float f = pos - (float)lo;
       const float* trow = r.table + (rowh0 + hh) * npos;
       const float tlo = __ldcg(trow + lo);
-      bias = tlo + f * (__ldcg(trow + hi) - tlo);
+      score[hh] = live ? lg[hh] + (tlo + f * (__ldcg(trow + hi) - tlo)) : -INFINITY;
+      const float v = warp_max(score[hh]);
+      if (lane == 0) red[hh][warp] = v;  // the logit maxima are not read on this path
     }
-    score[hh] = live ? lg[hh] + bias : -INFINITY;
-    const float v = warp_max(score[hh]);
-    if (lane == 0) red[hh][warp] = v;
+    __syncthreads();
+#pragma unroll
+    for (int hh = 0; hh < G; ++hh) {
+      m[hh] = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kSplit / 32; ++w) m[hh] = fmaxf(m[hh], red[hh][w]);
+    }
   }
-  __syncthreads();
-  if (tid < G) {
-    float m = -INFINITY;
-    for (int w = 0; w < kSplit / 32; ++w) m = fmaxf(m, red[tid][w]);
-    mmax[tid] = m;
-  }
-  __syncthreads();
   // P^T over the q tile (free after S; its rows beyond G stay zero)
+  float pw[G];
 #pragma unroll
   for (int hh = 0; hh < G; ++hh) {
-    const T wq = Elem<T>::from_f(live ? expf(score[hh] - mmax[hh]) : 0.f);
+    const T wq = Elem<T>::from_f(live ? expf(score[hh] - m[hh]) : 0.f);
     *reinterpret_cast<T*>(gQ + sw128(hh, tid >> 3, kTcN) + (tid & 7) * 2) = wq;
-    const float v = warp_sum(Elem<T>::to_f(wq));
-    if (lane == 0) wtot[hh][warp] = v;
+    pw[hh] = Elem<T>::to_f(wq);
   }
   cp_async_wait_all();  // V
   fence_async_smem();
@@ -956,10 +973,20 @@ __global__ void __launch_bounds__(kSplit, 5) decode_onepass_tc(const __grid_cons
     }
     tc_commit(mb);
   }
+  // row sums of the rounded weights while the product runs
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh) {
+    const float v = warp_sum(pw[hh]);
+    if (lane == 0) wtot[hh][warp] = v;
+  }
+  __syncthreads();
   if (tid < G) {
-    float l = 0.f;
+    float l = 0.f, mt = m[0];
     for (int w = 0; w < kSplit / 32; ++w) l += wtot[tid][w];
-    r.pm[(rowh0 + tid) * r.nsplit + s] = mmax[tid];
+#pragma unroll
+    for (int hh = 1; hh < G; ++hh)
+      if (hh == tid) mt = m[hh];
+    r.pm[(rowh0 + tid) * r.nsplit + s] = mt;
     r.pl[(rowh0 + tid) * r.nsplit + s] = l;
   }
   const bool done2 = wait_mma(mb, 1);
