@@ -319,10 +319,13 @@ CS_API int cs_cope_attn_prefill(const cs_attn_params* p, void* stream);
 
 /*
  * Decode (one or a few query rows over a long paged context): split-key
- * two-phase kernel.  phase 1 computes logits and per-split gate totals,
- * phase 2 scans with the carry of newer splits, applies the bias and reduces
- * split partials.  `workspace` must hold cs_cope_attn_decode_workspace(p)
- * bytes of device memory.
+ * kernel.  On the tensor-core path (head_dim 128, 16-bit, 16-byte aligned
+ * rows) one pass over the records: each split publishes its gate totals,
+ * takes the count carried from the newer splits, applies the bias, and the
+ * split partials are merged; other shapes run two CUDA-core phases (logits
+ * and gate totals, then the carried scan, bias and partials) and a combine.
+ * `workspace` must hold cs_cope_attn_decode_workspace(p) bytes of device
+ * memory (256-byte aligned); its contents need no initialisation.
  */
 CS_API int64_t cs_cope_attn_decode_workspace(const cs_attn_params* p);
 CS_API int cs_cope_attn_decode(const cs_attn_params* p, void* workspace,
