@@ -381,8 +381,14 @@ def test_tensor_core_prefill_copy_paths_agree(cuda, layout, monkeypatch):
         np.testing.assert_allclose(outs["tma"], want, **BF16)
 
 
-@pytest.mark.parametrize("nk,rows", [(4097, [4096]), (1500, [700, 1200, 1499]), (513, [512])])
-def test_split_key_decode_matches_oracle_and_generic(cuda, nk, rows):
+@pytest.mark.parametrize("nk,rows,npos", [
+    (4097, [4096], 64), (1500, [700, 1200, 1499], 64), (513, [512], 64),
+    # 71 splits: look-back windows of 32 newer splits, three causal limits
+    (9000, [8999, 4500, 100], 64),
+    # counts below the last position over most splits: the q.E table path
+    (5000, [4999, 2600], 512),
+])
+def test_split_key_decode_matches_oracle_and_generic(cuda, nk, rows, npos):
     """Decode rows through the paged cache: split-key kernel vs oracle and vs
     the one-warp-per-row generic kernel."""
     from cacheslide_b200 import _native as N
@@ -393,7 +399,7 @@ def test_split_key_decode_matches_oracle_and_generic(cuda, nk, rows):
     q = (torch.randn(len(rows), hq, d, generator=g) / d ** 0.5).to(torch.bfloat16).to(cuda)
     k = (torch.randn(nk, hkv, d, generator=g) / d ** 0.5).to(torch.bfloat16).to(cuda)
     v = torch.randn(nk, hkv, d, generator=g).to(torch.bfloat16).to(cuda)
-    E = torch.randn(d, 64, generator=g) * 0.02
+    E = torch.randn(d, npos, generator=g) * 0.02
     qpos = torch.tensor(rows, device=cuda)
     nb = (nk + bs - 1) // bs + 5
     perm = torch.randperm(nb, generator=g)[: (nk + bs - 1) // bs].to(cuda)
