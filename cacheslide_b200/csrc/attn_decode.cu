@@ -698,11 +698,16 @@ __device__ float look_back(const uint64_t* words, int s, int last, int32_t& bits
 }
 
 // Zeroes the one-pass flags (the first n16 16-byte words of the batch
-// workspace) and lets the dependent decode grid start at once.
+// workspace) and lets the dependent decode grid start at once.  It is itself
+// launched as a programmatic dependent of the preceding grid (which starts it
+// early only if that grid signals so, as the paged-cache scatter does) and
+// waits for that grid before it exits, so its completion implies the
+// preceding grid's: the decode grid's griddepcontrol.wait covers both.
 __global__ void __launch_bounds__(256) decode_zero_flags(uint4* p, int64_t n16) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   for (int64_t e = (int64_t)blockIdx.x * 256 + threadIdx.x; e < n16; e += (int64_t)gridDim.x * 256)
     p[e] = make_uint4(0u, 0u, 0u, 0u);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 // One-pass decode for the tensor-core shapes: a CTA takes one 128-key split
@@ -723,8 +728,10 @@ __global__ void __launch_bounds__(256) decode_zero_flags(uint4* p, int64_t n16) 
 // the last position for every head needs only T[h][npos - 1], which it
 // computes itself from the last column of E.  The state words, table flags
 // and arrival counters are zeroed by decode_zero_flags, the grid before
-// this one; this grid is its programmatic dependent, so the copies and S
-// start at once and only the first flag access waits for the zeroing.
+// this one; this grid is its programmatic dependent: a CTA reads the slots,
+// query position and E column at once, and waits (griddepcontrol.wait, which
+// also covers the grid before the zeroing one) before it reads any K / V row
+// or flag or writes any output.
 template <typename T, int G>
 __global__ void __launch_bounds__(kSplit, 5) decode_onepass_tc(const __grid_constant__ DecodeBatch b) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -754,6 +761,7 @@ __global__ void __launch_bounds__(kSplit, 5) decode_onepass_tc(const __grid_cons
   const int64_t gl = i * b.hkv + g;
   if (base >= nlim) {  // split entirely in the future: nothing to publish
     if (s == 0) {      // no visible key at all: zero output rows
+      asm volatile("griddepcontrol.wait;" ::: "memory");
       for (int e = tid; e < G * kFastD; e += kSplit) {
         char* orow = r.out + (i * r.o_st + (int64_t)(g * G + e / kFastD) * r.o_sh) *
                                  dtype_size(b.out_dtype);
@@ -791,6 +799,9 @@ __global__ void __launch_bounds__(kSplit, 5) decode_onepass_tc(const __grid_cons
     if (!okk || !okv) bits |= CS_ST_SLOT_RANGE;
   }
   const char* q0 = r.q + (i * r.q_st + (int64_t)g * G * r.q_sh) * (int64_t)sizeof(T);
+  // the preceding grids (flag zeroing, and the one before it, e.g. the write
+  // of the newest rows) are complete and visible from here on
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   copy_split_rows(sT, krow, q0);
   for (int e = tid; e < kTcN * 16; e += kSplit) {  // q rows (heads), zero beyond G
     const int hh = e >> 4, c = e & 15;
@@ -852,8 +863,6 @@ __global__ void __launch_bounds__(kSplit, 5) decode_onepass_tc(const __grid_cons
   }
   tc_fence_before();
   __syncthreads();
-  // the flags were zeroed by the preceding grid (decode_zero_flags)
-  asm volatile("griddepcontrol.wait;" ::: "memory");
   // publish the split's gate totals (warp h, head h), take the per-warp
   // maxima of the logits while the newer splits publish theirs, then look
   // back for the carried count (a warp per head)
@@ -1196,12 +1205,20 @@ int launch_batch(const cs_attn_params* ps, int count, char* workspace, cudaStrea
   for (int k = 0; k < count; ++k) fast = fast && (ps[k].nq == 0 || fast_decode_ok(&ps[k]));
   if (fast) {
     const int64_t n16 = zero / 4;  // zero is a multiple of 64 floats
-    decode_zero_flags<<<(unsigned)std::min<int64_t>((n16 + 255) / 256, 148), 256, 0, stream>>>(
-        reinterpret_cast<uint4*>(workspace), n16);
-    // the decode grid is a programmatic dependent of the zeroing grid
+    // the zeroing grid is a programmatic dependent of the preceding grid,
+    // the decode grid one of the zeroing grid
     cudaLaunchAttribute pdl[1];
     pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t zcfg{};
+    zcfg.gridDim = dim3((unsigned)std::min<int64_t>((n16 + 255) / 256, 148));
+    zcfg.blockDim = dim3(256);
+    zcfg.stream = stream;
+    zcfg.attrs = pdl;
+    zcfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&zcfg, decode_zero_flags, reinterpret_cast<uint4*>(workspace), n16) !=
+        cudaSuccess)
+      return CS_ERR_CUDA;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)((int64_t)rows * b.hkv * nsplit_max));
     cfg.blockDim = dim3(kSplit);

@@ -53,6 +53,10 @@ __global__ void scatter_kernel(PagedView pv, const int64_t* __restrict__ slots,
                                const int64_t* __restrict__ rows, int64_t n,
                                const char* __restrict__ in_k, const char* __restrict__ in_v,
                                int64_t i_row, int64_t i_head, int32_t* status) {
+  // a grid launched after this one as its programmatic dependent (the
+  // decode's flag-zeroing grid) may start now; it waits for this grid's
+  // completion before anything reads the rows written here
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int64_t per_half = pv.head_dim * pv.esize / (int64_t)sizeof(V);
   const int64_t per_rec = 2 * per_half;
   const int64_t total = n * pv.kv_heads * per_rec;
