@@ -436,16 +436,20 @@ __device__ __forceinline__ float fast_gate(float logit) {  // 1 / (1 + e^-logit)
 
 // rows 0..127 of the split (thread t resolved key t: `row`) into the swizzled
 // tile at `dst`; warp w copies its keys 32w..32w+31 two at a time.  Rows of
-// dead keys (null) are zero-filled from `dummy`, a valid global address.
+// dead keys (null) are zero-filled from `dummy`, a valid global address.  The
+// rows are read once: they go through L2 as first to be evicted, so the
+// split partials written meanwhile stay there for the merge.
 __device__ __forceinline__ void copy_split_rows(uint32_t dst, const char* row, const char* dummy) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint64_t pol = l2_evict_first_policy();
 #pragma unroll
   for (int it = 0; it < 16; ++it) {
     const int kl = 2 * it + (lane >> 4);
     const char* src = reinterpret_cast<const char*>(
         __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(row), kl));
     const int c = lane & 15;
-    cp_async16(dst + sw128(warp * 32 + kl, c, 128), src ? src + c * 16 : dummy, src != nullptr);
+    cp_async16_hint(dst + sw128(warp * 32 + kl, c, 128), src ? src + c * 16 : dummy,
+                    src != nullptr, pol);
   }
 }
 

@@ -150,6 +150,19 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool v
                "r"(valid ? 16 : 0)
                : "memory");
 }
+// L2 policy for data read once (streamed K / V records): first to be evicted,
+// so it does not push out data that is read again soon
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ void cp_async16_hint(uint32_t dst, const void* src, bool valid,
+                                                uint64_t policy) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;" ::"r"(dst),
+               "l"(src), "r"(valid ? 16 : 0), "l"(policy)
+               : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() {
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
