@@ -701,6 +701,41 @@ __device__ float look_back(const uint64_t* words, int s, int last, int32_t& bits
   return carry;
 }
 
+// Sum (or maximum) over the warp of G values per lane, all G at once: a
+// transposed butterfly halves the values each lane holds per exchange (lanes
+// with the offset bit set keep the upper half), then reduces the one left,
+// (G - 1) + (5 - log2 G) shuffles in all instead of 5 G.  Every lane gets the
+// total of value `head`; the lanes with lane % (32 / G) == 0 hold heads
+// 0..G-1 once each.
+template <int G, bool MAX>
+__device__ __forceinline__ float warp_reduce_g(const float (&v)[G], int& head) {
+  static_assert(G == 1 || G == 2 || G == 4 || G == 8, "G is a power of two up to 8");
+  const int lane = threadIdx.x & 31;
+  float w[G];
+#pragma unroll
+  for (int j = 0; j < G; ++j) w[j] = v[j];
+  head = 0;
+  int o = 16;
+#pragma unroll
+  for (int W = G; W > 1; W >>= 1, o >>= 1) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int j = 0; j < W / 2; ++j) {
+      const float send = up ? w[j] : w[j + W / 2];
+      const float keep = up ? w[j + W / 2] : w[j];
+      const float got = __shfl_xor_sync(0xffffffffu, send, o);
+      w[j] = MAX ? fmaxf(keep, got) : keep + got;
+    }
+    if (up) head += W / 2;
+  }
+#pragma unroll
+  for (; o >= 1; o >>= 1) {
+    const float got = __shfl_xor_sync(0xffffffffu, w[0], o);
+    w[0] = MAX ? fmaxf(w[0], got) : w[0] + got;
+  }
+  return w[0];
+}
+
 // Zeroes the one-pass flags (the first n16 16-byte words of the batch
 // workspace) and lets the dependent decode grid start at once.  It is itself
 // launched as a programmatic dependent of the preceding grid (which starts it
@@ -830,12 +865,15 @@ __global__ void __launch_bounds__(kSplit, 5) decode_onepass_tc(const __grid_cons
     tc_commit(mb);
   }
   // partial sums of T[h][npos - 1] = q[h] . E[:, npos - 1] while S runs
+  {
+    float pq[G];
 #pragma unroll
-  for (int hh = 0; hh < G; ++hh) {
-    const float qv = Elem<T>::to_f(
-        *reinterpret_cast<const T*>(gQ + sw128(hh, tid >> 3, kTcN) + (tid & 7) * 2));
-    const float v = warp_sum(qv * elast);
-    if (lane == 0) tsp[hh][warp] = v;
+    for (int hh = 0; hh < G; ++hh)
+      pq[hh] = elast * Elem<T>::to_f(*reinterpret_cast<const T*>(
+                           gQ + sw128(hh, tid >> 3, kTcN) + (tid & 7) * 2));
+    int hw;
+    const float v = warp_reduce_g<G, false>(pq, hw);
+    if ((lane & (32 / G - 1)) == 0) tsp[hw][warp] = v;
   }
   const bool done1 = wait_mma(mb, 0);  // S complete: the tile's K rows are read
   tc_fence_after();
@@ -878,10 +916,13 @@ __global__ void __launch_bounds__(kSplit, 5) decode_onepass_tc(const __grid_cons
       st_relaxed_u64(r.lb + (rowh0 + hh) * r.nsplit + s, kAggregate | __float_as_uint(agg));
     }
   }
+  {
+    float lv[G];
 #pragma unroll
-  for (int hh = 0; hh < G; ++hh) {
-    const float v = warp_max(live ? lg[hh] : -INFINITY);
-    if (lane == 0) red[hh][warp] = v;
+    for (int hh = 0; hh < G; ++hh) lv[hh] = live ? lg[hh] : -INFINITY;
+    int hw;
+    const float v = warp_reduce_g<G, true>(lv, hw);
+    if ((lane & (32 / G - 1)) == 0) red[hw][warp] = v;
   }
   for (int hh = warp; hh < G; hh += kSplit / 32) {
     float agg = 0.f;
@@ -987,10 +1028,10 @@ __global__ void __launch_bounds__(kSplit, 5) decode_onepass_tc(const __grid_cons
     tc_commit(mb);
   }
   // row sums of the rounded weights while the product runs
-#pragma unroll
-  for (int hh = 0; hh < G; ++hh) {
-    const float v = warp_sum(pw[hh]);
-    if (lane == 0) wtot[hh][warp] = v;
+  {
+    int hw;
+    const float v = warp_reduce_g<G, false>(pw, hw);
+    if ((lane & (32 / G - 1)) == 0) wtot[hw][warp] = v;
   }
   __syncthreads();
   if (tid < G) {
