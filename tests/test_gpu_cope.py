@@ -381,20 +381,23 @@ def test_tensor_core_prefill_copy_paths_agree(cuda, layout, monkeypatch):
         np.testing.assert_allclose(outs["tma"], want, **BF16)
 
 
-@pytest.mark.parametrize("nk,rows,npos", [
-    (4097, [4096], 64), (1500, [700, 1200, 1499], 64), (513, [512], 64),
+@pytest.mark.parametrize("nk,rows,npos,hq,hkv", [
+    (4097, [4096], 64, 32, 8), (1500, [700, 1200, 1499], 64, 32, 8), (513, [512], 64, 32, 8),
     # 71 splits: look-back windows of 32 newer splits, three causal limits
-    (9000, [8999, 4500, 100], 64),
+    (9000, [8999, 4500, 100], 64, 32, 8),
     # counts below the last position over most splits: the q.E table path
-    (5000, [4999, 2600], 512),
+    (5000, [4999, 2600], 512, 32, 8),
+    # one GPU's slice of the Llama-70B TP8 layout: 8 query heads on 1 KV head,
+    # npos 128, a 64K context (513 splits)
+    (65537, [65536, 30000], 128, 8, 1),
 ])
-def test_split_key_decode_matches_oracle_and_generic(cuda, nk, rows, npos):
+def test_split_key_decode_matches_oracle_and_generic(cuda, nk, rows, npos, hq, hkv):
     """Decode rows through the paged cache: split-key kernel vs oracle and vs
     the one-warp-per-row generic kernel."""
     from cacheslide_b200 import _native as N
     from cacheslide_b200.position import _Holder, _base_params
 
-    hq, hkv, d, bs = 32, 8, 128, 16
+    d, bs = 128, 16
     g = torch.Generator().manual_seed(nk)
     q = (torch.randn(len(rows), hq, d, generator=g) / d ** 0.5).to(torch.bfloat16).to(cuda)
     k = (torch.randn(nk, hkv, d, generator=g) / d ** 0.5).to(torch.bfloat16).to(cuda)
