@@ -430,6 +430,9 @@ constexpr uint32_t kTileB = 32768;  // 128 rows x 256 B
 constexpr uint32_t kSmallB = kTcN * 256;
 constexpr size_t kOnepassSmem = 1024 + kTileB + kSmallB;  // the K / V tile and the q / P tile
 
+// e^x = 2^(x log2 e) on the hardware 2^x (exp_fast(-inf) = 0)
+__device__ __forceinline__ float exp_fast(float x) { return ex2(x * 1.4426950408889634f); }
+
 __device__ __forceinline__ float fast_gate(float logit) {  // 1 / (1 + e^-logit)
   return rcp_approx(1.f + ex2(-logit * 1.4426950408889634f));
 }
@@ -591,7 +594,7 @@ __device__ void combine_heads(const DecodeBatch& b, const DecodeReq& r, int64_t 
 #pragma unroll
       for (int u = 0; u < U; ++u) mb = fmaxf(mb, ms[u][hh]);
       if (mb > m[hh]) {  // uniform over the warp: its lanes read the same split maxima
-        const float c = expf(m[hh] - mb);  // 0 while nothing was accumulated
+        const float c = exp_fast(m[hh] - mb);  // 0 while nothing was accumulated
         acc[hh].x *= c;
         acc[hh].y *= c;
         acc[hh].z *= c;
@@ -601,7 +604,7 @@ __device__ void combine_heads(const DecodeBatch& b, const DecodeReq& r, int64_t 
       }
 #pragma unroll
       for (int u = 0; u < U; ++u) {
-        const float w = ms[u][hh] > -INFINITY ? expf(ms[u][hh] - m[hh]) : 0.f;
+        const float w = ms[u][hh] > -INFINITY ? exp_fast(ms[u][hh] - m[hh]) : 0.f;
         acc[hh].x = fmaf(w, o[u][hh].x, acc[hh].x);
         acc[hh].y = fmaf(w, o[u][hh].y, acc[hh].y);
         acc[hh].z = fmaf(w, o[u][hh].z, acc[hh].z);
@@ -632,7 +635,7 @@ __device__ void combine_heads(const DecodeBatch& b, const DecodeReq& r, int64_t 
 #pragma unroll
     for (int w = 0; w < NS; ++w) {
       const float mw = wm[hh * NS + w];
-      const float c = mw > -INFINITY ? expf(mw - M) : 0.f;
+      const float c = mw > -INFINITY ? exp_fast(mw - M) : 0.f;
       L = fmaf(c, wl[hh * NS + w], L);
       v = fmaf(c, buf[(hh * NS + w) * kFastD + tid], v);
     }
@@ -1008,7 +1011,7 @@ __global__ void __launch_bounds__(kSplit, 5) decode_onepass_tc(const __grid_cons
   float pw[G];
 #pragma unroll
   for (int hh = 0; hh < G; ++hh) {
-    const T wq = Elem<T>::from_f(live ? expf(score[hh] - m[hh]) : 0.f);
+    const T wq = Elem<T>::from_f(live ? exp_fast(score[hh] - m[hh]) : 0.f);
     *reinterpret_cast<T*>(gQ + sw128(hh, tid >> 3, kTcN) + (tid & 7) * 2) = wq;
     pw[hh] = Elem<T>::to_f(wq);
   }
