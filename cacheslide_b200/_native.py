@@ -30,6 +30,7 @@ ST_TIMEOUT = 1 << 8
 ST_INPUT_NONFINITE = 1 << 9
 
 POS_CONTEXTUAL, POS_FIXED, POS_TABLE, POS_CHUNK = 0, 1, 2, 3
+LAUNCH_OVERLAP_PREV = 1
 
 DTYPES = {
     torch.float32: CS_F32,
@@ -84,6 +85,7 @@ class AttnParams(ctypes.Structure):
         ("out", _p), ("o_stride_tok", _i64), ("o_stride_head", _i64),
         ("in_dtype", _i32), ("out_dtype", _i32),
         ("status", _p),
+        ("launch_flags", _i32),
     ]
 
 

@@ -740,11 +740,16 @@ __device__ __forceinline__ float warp_reduce_g(const float (&v)[G], int& head) {
 }
 
 // Zeroes the one-pass flags (the first n16 16-byte words of the batch
-// workspace) and lets the dependent decode grid start at once.  It is itself
-// launched as a programmatic dependent of the preceding grid (which starts it
-// early only if that grid signals so, as the paged-cache scatter does) and
-// waits for that grid before it exits, so its completion implies the
-// preceding grid's: the decode grid's griddepcontrol.wait covers both.
+// workspace) and lets the dependent decode grid start at once.  When the
+// caller allows it (CS_LAUNCH_OVERLAP_PREV) it is itself launched as a
+// programmatic dependent of the preceding grid (which starts it early only
+// if that grid signals so, as the paged-cache scatter does) and waits for
+// that grid before it exits, so its completion implies the preceding grid's:
+// the decode grid's griddepcontrol.wait covers both.  Its stores come before
+// that wait, so a preceding grid that uses the same workspace (an earlier
+// decode) must not signal early: decode_onepass_tc never executes
+// griddepcontrol.launch_dependents, and must not, or the flags of a decode
+// still running could be cleared under it.
 __global__ void __launch_bounds__(256) decode_zero_flags(uint4* p, int64_t n16) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   for (int64_t e = (int64_t)blockIdx.x * 256 + threadIdx.x; e < n16; e += (int64_t)gridDim.x * 256)
@@ -1253,8 +1258,12 @@ int launch_batch(const cs_attn_params* ps, int count, char* workspace, cudaStrea
   for (int k = 0; k < count; ++k) fast = fast && (ps[k].nq == 0 || fast_decode_ok(&ps[k]));
   if (fast) {
     const int64_t n16 = zero / 4;  // zero is a multiple of 64 floats
-    // the zeroing grid is a programmatic dependent of the preceding grid,
-    // the decode grid one of the zeroing grid
+    // the decode grid is always a programmatic dependent of the zeroing
+    // grid (which writes only the flags).  The zeroing grid is one of the
+    // preceding grid only when the caller says that grid writes none of the
+    // inputs the decode CTAs read before their griddepcontrol.wait (slots,
+    // query positions, E), e.g. cs_slide_scatter of the newest records;
+    // otherwise it starts in plain stream order, after that grid completes.
     cudaLaunchAttribute pdl[1];
     pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     pdl[0].val.programmaticStreamSerializationAllowed = 1;
@@ -1263,7 +1272,7 @@ int launch_batch(const cs_attn_params* ps, int count, char* workspace, cudaStrea
     zcfg.blockDim = dim3(256);
     zcfg.stream = stream;
     zcfg.attrs = pdl;
-    zcfg.numAttrs = 1;
+    zcfg.numAttrs = (p0->launch_flags & CS_LAUNCH_OVERLAP_PREV) ? 1 : 0;
     if (cudaLaunchKernelEx(&zcfg, decode_zero_flags, reinterpret_cast<uint4*>(workspace), n16) !=
         cudaSuccess)
       return CS_ERR_CUDA;

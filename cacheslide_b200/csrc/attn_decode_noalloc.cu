@@ -36,7 +36,9 @@ std::mutex g_mutex;
 void* g_scratch[kMaxDevices] = {};
 
 // Device address of the scratch array on the current device, resolved once
-// per device (with that device current) and cached.
+// per device (with that device current) and cached for the life of the
+// process; a device reset, which re-creates the context and the array, makes
+// the cached address stale (documented at the entry point's declaration).
 int scratch_for_current_device(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return CS_ERR_CUDA;

@@ -267,6 +267,9 @@ class ReuseStep:
         p.o_stride_tok, p.o_stride_head = r.dec_out.stride(0), r.dec_out.stride(1)
         p.in_dtype = p.out_dtype = N.DTYPES[cfg.dtype]
         p.status = r.status_ptr
+        # decode() launches it right after the scatter of the newest records,
+        # which writes no input the decode reads before waiting for it
+        p.launch_flags = N.LAUNCH_OVERLAP_PREV
         return p
 
     # ------------------------------------------------------------- launches

@@ -300,7 +300,16 @@ typedef struct {
   int64_t o_stride_tok, o_stride_head;
   int32_t in_dtype, out_dtype;
   int32_t* status;
+  /* decode only: CS_LAUNCH_OVERLAP_PREV lets the decode start while the grid
+     launched just before it on the stream still runs (a programmatic
+     dependent launch).  Set it only when that grid writes none of q, qpos,
+     kv_slots and E, or writes them before it signals its dependents; the
+     library's cs_slide_scatter qualifies (it writes only K/V records, which
+     the decode reads after waiting for it).  0 = plain stream order. */
+  int32_t launch_flags;
 } cs_attn_params;
+
+#define CS_LAUNCH_OVERLAP_PREV 1
 
 /*
  * Generic CoPE/CCPE attention: every mode above, any query rows, float64 /
@@ -355,7 +364,10 @@ CS_API int cs_cope_attn_decode_batch(const cs_attn_params* params, int32_t count
  *   CS_ERR_TOO_LARGE without launching anything.
  * - The first call on a device resolves the array's device address with that
  *   device current; make that first call before any stream capture, and make
- *   the stream's device current for every call.
+ *   the stream's device current for every call.  The address is kept for the
+ *   life of the process: after cudaDeviceReset (or anything else that
+ *   re-creates the device's primary context) it is stale, so do not call
+ *   this entry point again in that process after such a reset.
  * - All calls on a device share the one array: calls that overlap on the GPU
  *   (different streams, no ordering between them) race and corrupt each
  *   other's results.  Nothing in it needs to start at zero.

@@ -86,6 +86,28 @@ def test_noalloc_decode_matches_workspace_decode_on_two_calls(cuda):
         np.testing.assert_allclose(got, want, **BF16)
 
 
+def test_noalloc_decode_calls_queued_back_to_back_on_one_stream(cuda):
+    # the supported way to share the array: stream-ordered calls, one sync
+    probs = [_problem(cuda, 4, 2500, [2499]), _problem(cuda, 5, 900, [300, 899])]
+    lib = N.load()
+    outs, holds = [], []
+    for keep in probs:
+        q = keep[0]
+        out = torch.full(q.shape, float("nan"), dtype=torch.bfloat16, device=cuda)
+        p = _params(keep, out)
+        st = N.Status(cuda)
+        p.status = st.ptr
+        assert lib.cs_cope_attn_decode_noalloc(ctypes.byref(p), N.stream_of(cuda)) == N.CS_OK
+        outs.append(out)
+        holds.append((p, st))
+    torch.cuda.synchronize(cuda)
+    for (_, st), out, keep in zip(holds, outs, probs):
+        assert st.read() == 0
+        got = out.float().cpu().numpy()
+        assert np.isfinite(got).all()
+        np.testing.assert_allclose(got, _run(keep, noalloc=False), **BF16)
+
+
 def test_noalloc_decode_rejects_problems_beyond_the_static_capacity(cuda):
     keep = _problem(cuda, 3, 33000, [32999] * 1 + [32998])  # ~9 MB per row pair
     q = keep[0]
