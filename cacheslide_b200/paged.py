@@ -1,19 +1,32 @@
-"""SLIDE indirection over the native paged KV cache (reference ``paged.py``).
+"""SLIDE indirection over the caller's native paged KV cache.
 
-``NativePagedKV`` keeps the reference's API and slot semantics; its device
-work is the CUDA SLIDE kernels (``cs_slide_scatter`` / ``cs_slide_gather``)
-over the caller's cache view ``[block, kv_head, block_offset, 2*D]``, which
-may be non-contiguous (all four strides are honoured; nothing is reshaped or
-copied).  Selected rows that are relocated live in a lazily allocated sidecar.
+Public contract (``src/cacheslide_vllm/paged.py:57-581``): ``NativePagedKV``
+with the reference's constructor, methods, slot choices, statistics and error
+messages, so a runtime written against the reference switches without edits.
+The implementation is this module's own:
+
+* tensor data moves only through the CUDA SLIDE kernels
+  (``cs_slide_scatter`` / ``cs_slide_gather``) over the caller's view
+  ``[block, kv_head, block_offset, 2*D]`` with all four strides honoured
+  (nothing is reshaped or copied); relocated rows live in a sidecar that is
+  allocated on the first relocation;
+* every device write or read is enqueued together with an asynchronous copy
+  of its status word into pinned host memory and a CUDA event, so one event
+  wait gives both completion and the kernel's status (``_Launch``);
+* asynchronous completions (a promotion whose mapping is published when its
+  copies have run) are resolved by one shared waiter thread per process that
+  takes events in order (``_Waiter``), not a thread per write;
+* the canonical (block-table) slot of each token is a list indexed by token.
 
 Beyond the reference it exposes ``device_view()`` and ``slot_table()``, with
-which the attention kernel reads K/V straight through the slot map instead of
-gathering a dense copy each step.
+which the attention kernels read K/V through the slot map instead of
+gathering a dense copy every step.
 """
 
 from __future__ import annotations
 
 import ctypes
+import queue
 import threading
 from collections.abc import Iterable, Sequence
 from concurrent.futures import Future
@@ -24,50 +37,96 @@ from . import _native as N
 from .errors import StaleCompletionError  # noqa: F401  (re-exported for callers)
 from .slide import LayerSlotMap, SlotWrite
 
+_ROW_BYTES = 8  # a promotion record names a row of the caller's K/V tensors
 
-def _indices(value: Sequence[int] | torch.Tensor, name: str) -> list[int]:
-    """paged.py:21-32."""
+
+def _positions(value: Sequence[int] | torch.Tensor, name: str) -> list[int]:
+    """Distinct nonnegative token positions from a list or an integer vector
+    (the reference's argument contract, paged.py:21-32)."""
     if isinstance(value, torch.Tensor):
         if value.ndim != 1 or value.dtype not in (torch.int32, torch.int64):
             raise ValueError(f"{name} must be an integer vector")
         value = value.detach().cpu().tolist()
-    result = list(value)
-    if any(type(item) is not int or item < 0 for item in result):
-        raise ValueError(f"{name} must contain nonnegative integer positions")
-    if len(set(result)) != len(result):
+    out = list(value)
+    for item in out:
+        if type(item) is not int or item < 0:
+            raise ValueError(f"{name} must contain nonnegative integer positions")
+    if len(set(out)) != len(out):
         raise ValueError(f"{name} must contain distinct positions")
-    return result
+    return out
 
 
-def _completion_future(device: torch.device) -> Future:
-    """Publish only after the device has executed the enqueued copies
-    (paged.py:35-54): a CUDA event waited on by a daemon thread."""
-    completed: Future = Future()
-    completed.set_running_or_notify_cancel()
-    if device.type != "cuda":
-        completed.set_result(None)
-        return completed
-    event = torch.cuda.Event()
-    event.record(torch.cuda.current_stream(device))
+class _Launch:
+    """A device operation in flight: its event and its status word, copied to
+    pinned host memory behind the kernel on the same stream."""
 
-    def finish() -> None:
-        try:
-            event.synchronize()
-        except BaseException as error:  # pragma: no cover - device failure path
-            completed.set_exception(error)
-        else:
-            completed.set_result(None)
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.word = torch.zeros(1, dtype=torch.int32, device=device)
+        self.host = torch.empty(1, dtype=torch.int32, pin_memory=True)
+        self.event = torch.cuda.Event()
 
-    threading.Thread(target=finish, name="cacheslide-kv-write", daemon=True).start()
-    return completed
+    @property
+    def status_ptr(self) -> int:
+        return self.word.data_ptr()
+
+    def enqueue_done(self) -> "_Launch":
+        stream = torch.cuda.current_stream(self.device)
+        self.host.copy_(self.word, non_blocking=True)
+        self.event.record(stream)
+        return self
+
+    def bits(self) -> int:
+        """Status bits; valid once the event has completed."""
+        return int(self.host[0])
+
+    def check(self) -> None:
+        if self.bits() & N.ST_SLOT_RANGE:
+            raise ValueError("slot outside the native cache and sidecar")
+
+    def wait(self) -> None:
+        self.event.synchronize()
+        self.check()
+
+
+class _Waiter:
+    """One daemon thread resolving futures when their launches complete."""
+
+    _lock = threading.Lock()
+    _queue: queue.SimpleQueue | None = None
+
+    @classmethod
+    def submit(cls, launch: _Launch) -> Future:
+        done: Future = Future()
+        done.set_running_or_notify_cancel()
+        with cls._lock:
+            if cls._queue is None:
+                cls._queue = queue.SimpleQueue()
+                threading.Thread(target=cls._run, args=(cls._queue,),
+                                 name="cacheslide-kv-completion", daemon=True).start()
+            cls._queue.put((launch, done))
+        return done
+
+    @staticmethod
+    def _run(q: queue.SimpleQueue) -> None:
+        while True:
+            launch, done = q.get()
+            try:
+                launch.wait()
+            except BaseException as error:  # device failure or bad slot
+                done.set_exception(error)
+            else:
+                done.set_result(None)
 
 
 class NativePagedKV:
     """One request/layer's native slots plus its selected-token sidecar.
 
-    See reference paged.py:57-581 for the contract; block ownership and pool
-    capacity stay with the caller (vLLM), which may extend the block table
-    through ``update_block_table`` before decode crosses a block boundary.
+    Block ownership and pool capacity stay with the caller (vLLM): the arena
+    writes only slots its block table names, never frees a block, and the
+    caller extends the table through ``update_block_table`` before decode
+    crosses a block boundary.  Once a selected row has been relocated,
+    attention must read through this map (``gather`` or ``slot_table``).
     """
 
     def __init__(
@@ -81,156 +140,146 @@ class NativePagedKV:
         layer_index: int = 0,
         shared_slots: Iterable[int] = (),
     ):
-        if (
-            not isinstance(cache, torch.Tensor)
-            or cache.ndim != 4
-            or min(cache.shape) < 1
-            or cache.shape[-1] % 2
-            or cache.dtype not in N.DTYPES
-        ):
+        shape_ok = (isinstance(cache, torch.Tensor) and cache.ndim == 4
+                    and min(cache.shape) >= 1 and cache.shape[-1] % 2 == 0
+                    and cache.dtype in N.DTYPES)
+        if not shape_ok:
             raise ValueError("cache must be floating [blocks,KV heads,block size,2*D]")
         if cache.device.type != "cuda":
             raise ValueError("NativePagedKV runs on CUDA caches only (no CPU fallback)")
-        if type(prompt_length) is not int or prompt_length < 1:
-            raise ValueError("prompt_length must be a positive integer")
-        if type(max_selected) is not int or max_selected < 0:
-            raise ValueError("max_selected must be a nonnegative integer")
-        if type(layer_index) is not int or layer_index < 0:
-            raise ValueError("layer_index must be a nonnegative integer")
+        for name, value, low in (("prompt_length", prompt_length, 1),
+                                 ("max_selected", max_selected, 0),
+                                 ("layer_index", layer_index, 0)):
+            if type(value) is not int or value < low:
+                kind = "a positive" if low else "a nonnegative"
+                raise ValueError(f"{name} must be {kind} integer")
         self.cache = cache
         self.prompt_length = prompt_length
         self.request_id = request_id
         self.layer_index = layer_index
-        self.block_size = cache.shape[2]
         self.kv_heads = cache.shape[1]
+        self.block_size = cache.shape[2]
         self.head_dim = cache.shape[3] // 2
         self.native_total_slots = cache.shape[0] * self.block_size
         self.max_selected = max_selected
-        self._mutex = threading.RLock()
-        self._block_table = self._table(block_table)
-        self._canonical = {t: self._canonical_slot(t) for t in range(prompt_length)}
-        if len(set(self._canonical.values())) != prompt_length:
+        self._lock = threading.RLock()
+        self._blocks = self._parse_table(block_table)
+        self._home = [self._slot_in(self._blocks, t) for t in range(prompt_length)]
+        self._home_set = set(self._home)
+        if len(self._home_set) != prompt_length:
             raise ValueError("active logical blocks must name distinct native slots")
         self._shared = set(shared_slots)
         self.slot_map = LayerSlotMap(
-            self._canonical,
+            dict(enumerate(self._home)),
             shared_slots=self._shared,
             allocation_floor=self.native_total_slots,
             max_slots=self.native_total_slots + max_selected,
         )
         self._side_key: torch.Tensor | None = None
         self._side_value: torch.Tensor | None = None
-        self._baseline_ready: set[int] = set()
+        self._baseline = bytearray(prompt_length)  # 1 = device write completed
+        self._baseline_count = 0
         self._loads: list[Future] = []
         self._promotions: list[Future] = []
         self._selected: set[int] = set()
         self._decoded = False
-        self._hole_reuses = 0
-        self._native_binds = 0
-        self._canonical_mirrors = 0
-        self._ready_inplace_writes = 0
+        self._counts = dict(hole_reuse=0, native_bind=0, mirrors=0, ready_inplace=0)
 
     # ------------------------------------------------------------ geometry
-    def _table(self, block_table) -> tuple[int, ...]:
+    def _parse_table(self, block_table) -> tuple[int, ...]:
         if isinstance(block_table, torch.Tensor):
             if block_table.ndim != 1 or block_table.dtype not in (torch.int32, torch.int64):
                 raise ValueError("block_table must be a one-dimensional integer row")
             block_table = block_table.detach().cpu().tolist()
         row = tuple(block_table)
-        if not row or any(
-            type(b) is not int or not -1 <= b < self.cache.shape[0] for b in row
-        ):
+        limit = self.cache.shape[0]
+        if not row or not all(type(b) is int and -1 <= b < limit for b in row):
             raise ValueError("block_table contains invalid native block IDs")
         return row
 
-    def _canonical_slot(self, token: int, row: tuple[int, ...] | None = None) -> int:
-        row = self._block_table if row is None else row
-        block_index, offset = divmod(token, self.block_size)
-        if block_index >= len(row) or row[block_index] < 0:
+    def _slot_in(self, row: tuple[int, ...], token: int) -> int:
+        block, offset = divmod(token, self.block_size)
+        if block >= len(row) or row[block] < 0:
             raise ValueError("logical token has no caller-owned native block")
-        return row[block_index] * self.block_size + offset
+        return row[block] * self.block_size + offset
 
     def update_block_table(self, block_table) -> None:
-        row = self._table(block_table)
-        with self._mutex:
-            self.slot_map.snapshot()
-            if any(self._canonical_slot(t, row) != s for t, s in self._canonical.items()):
-                raise ValueError("block-table update moved an existing native token")
-            self._block_table = row
+        """Adopt a longer caller-owned table; existing tokens must not move."""
+        row = self._parse_table(block_table)
+        with self._lock:
+            self.slot_map.snapshot()  # raises once retired
+            for token, slot in enumerate(self._home):
+                if self._slot_in(row, token) != slot:
+                    raise ValueError("block-table update moved an existing native token")
+            self._blocks = row
 
     def canonical_slot(self, token: int) -> int:
         if type(token) is not int or token < 0:
             raise ValueError("token must be a nonnegative integer")
-        with self._mutex:
+        with self._lock:
             self.slot_map.snapshot()
-            return self._canonical_slot(token)
+            return self._slot_in(self._blocks, token)
 
     # ------------------------------------------------------- device access
     def device_view(self) -> N.PagedKV:
-        """C-ABI description of the cache view and sidecar."""
+        """C-ABI description of the cache view and its sidecar."""
         return N.paged_view(self.cache, self._side_key, self._side_value)
 
     def slot_table(self, logical_positions) -> torch.Tensor:
         """Current physical slot of each token as a device int64 vector."""
-        positions = _indices(logical_positions, "logical_positions")
-        with self._mutex:
+        positions = _positions(logical_positions, "logical_positions")
+        with self._lock:
             mapping = self.slot_map.snapshot()
-            return torch.tensor(
-                [mapping[t] for t in positions], dtype=torch.int64, device=self.cache.device
-            )
+            return torch.tensor([mapping[t] for t in positions], dtype=torch.int64,
+                                device=self.cache.device)
 
-    def _ensure_sidecar(self) -> None:
-        if self._side_key is None:
+    def _check_rows(self, count: int, key, value) -> None:
+        want = (count, self.kv_heads, self.head_dim)
+        for t in (key, value):
+            if (not isinstance(t, torch.Tensor) or tuple(t.shape) != want
+                    or t.device != self.cache.device or t.dtype != self.cache.dtype):
+                raise ValueError("K/V must match cache device/dtype and [token,KV head,D]")
+
+    def _scatter(self, slots: list[int], key, value, rows: list[int] | None = None) -> _Launch:
+        """Enqueue record of slots[i] = (key, value)[rows[i] if rows else i]."""
+        device = self.cache.device
+        launch = _Launch(device)
+        if not slots:
+            return launch.enqueue_done()
+        if self._side_key is None and max(slots) >= self.native_total_slots:
             shape = (self.max_selected, self.kv_heads, self.head_dim)
             self._side_key = self.cache.new_empty(shape)
             self._side_value = self.cache.new_empty(shape)
-
-    def _records(self, positions: list[int], key, value):
-        expected = (len(positions), self.kv_heads, self.head_dim)
-        for t in (key, value):
-            if (
-                not isinstance(t, torch.Tensor)
-                or tuple(t.shape) != expected
-                or t.device != self.cache.device
-                or t.dtype != self.cache.dtype
-            ):
-                raise ValueError("K/V must match cache device/dtype and [token,KV head,D]")
-        return key, value
-
-    def _write_slots(self, slots: list[int], key, value, rows: list[int] | None = None) -> None:
-        """cs_slide_scatter: record of slots[i] = (key, value)[rows[i] or i]."""
-        if not slots:
-            return
-        if any(s >= self.native_total_slots for s in slots):
-            self._ensure_sidecar()
-        device = self.cache.device
         k = key if key.stride(-1) == 1 else key.contiguous()
         v = value if value.stride(-1) == 1 else value.contiguous()
         if k.stride() != v.stride():
             k, v = k.contiguous(), v.contiguous()
-        slot_t = torch.tensor(slots, dtype=torch.int64, device=device)
-        row_t = None if rows is None else torch.tensor(rows, dtype=torch.int64, device=device)
-        status = N.Status(device)
-        kv = self.device_view()
-        N.check(
-            N.load().cs_slide_scatter(
-                ctypes.byref(kv), slot_t.data_ptr(), N.ptr(row_t), len(slots), k.data_ptr(),
-                v.data_ptr(), k.stride(0), k.stride(1), status.ptr, N.stream_of(device),
-            ),
-            "cs_slide_scatter",
-        )
-        if status.read() & N.ST_SLOT_RANGE:
-            raise ValueError("slot outside the native cache and sidecar")
+        slot_t = torch.tensor(slots, dtype=torch.int64).to(device, non_blocking=True)
+        row_t = (None if rows is None
+                 else torch.tensor(rows, dtype=torch.int64).to(device, non_blocking=True))
+        view = self.device_view()
+        N.check(N.load().cs_slide_scatter(
+            ctypes.byref(view), slot_t.data_ptr(), N.ptr(row_t), len(slots), k.data_ptr(),
+            v.data_ptr(), k.stride(0), k.stride(1), launch.status_ptr, N.stream_of(device)),
+            "cs_slide_scatter")
+        return launch.enqueue_done()
 
-    def _check_loads(self, *, allow_pending: bool = False) -> None:
-        for loading in self._loads:
-            if not loading.done():
-                if allow_pending:
-                    continue
+    def _sync_write(self, slots: list[int], key, value, rows=None) -> None:
+        with self.slot_map.write_guard(slots):
+            try:
+                self._scatter(slots, key, value, rows).wait()
+            except BaseException:
+                self.slot_map.invalidate()
+                raise
+
+    def _loads_settled(self, pending_ok: bool = False) -> None:
+        for load in self._loads:
+            if load.done():
+                load.result()  # a failed load re-raises here
+            elif not pending_ok:
                 raise RuntimeError("source KV load must complete before baseline/mirror writes")
-            loading.result()
 
-    def _check_promotions(self) -> None:
+    def _promotions_settled(self) -> None:
         for promotion in self._promotions:
             if not promotion.done():
                 raise RuntimeError("selected writes must complete before updating them")
@@ -238,45 +287,44 @@ class NativePagedKV:
 
     # --------------------------------------------------------------- writes
     def write(self, logical_positions, key: torch.Tensor, value: torch.Tensor) -> None:
-        """Load baseline KV into original native slots (paged.py:242-274)."""
-        positions = _indices(logical_positions, "logical_positions")
-        self._records(positions, key, value)
-        with self._mutex:
+        """Baseline KV into the tokens' own native slots, whatever the current
+        redirection (paged.py:242-274); waits for the device write."""
+        positions = _positions(logical_positions, "logical_positions")
+        self._check_rows(len(positions), key, value)
+        with self._lock:
             self.slot_map.snapshot()
-            self._check_loads()
+            self._loads_settled()
             if self._decoded:
                 raise RuntimeError("baseline writes cannot overwrite slots after decode")
-            if any(t not in self._canonical for t in positions):
+            if any(t >= len(self._home) for t in positions):
                 raise KeyError("baseline writes require existing logical tokens")
-            slots = [self._canonical[t] for t in positions]
-            if self._shared.intersection(slots):
+            slots = [self._home[t] for t in positions]
+            if not self._shared.isdisjoint(slots):
                 raise ValueError("baseline writes cannot mutate shared native slots")
-            with self.slot_map.write_guard(slots):
-                try:
-                    self._write_slots(slots, key, value)
-                    _completion_future(self.cache.device).result()
-                except BaseException:
-                    self.slot_map.invalidate()
-                    raise
-            self._baseline_ready.update(positions)
+            self._sync_write(slots, key, value)
+            for t in positions:
+                if t < self.prompt_length and not self._baseline[t]:
+                    self._baseline[t] = 1
+                    self._baseline_count += 1
 
     load_baseline = write
 
     def write_prefill(self, key: torch.Tensor, value: torch.Tensor) -> None:
         self.write(range(self.prompt_length), key, value)
 
-    def promote_selected(
-        self, logical_positions, key, value, *, load_future: Future | None = None
-    ) -> Future:
-        """Stage selected KV in the sidecar while a baseline load is pending."""
-        positions = _indices(logical_positions, "logical_positions")
-        self._records(positions, key, value)
+    def promote_selected(self, logical_positions, key, value, *,
+                         load_future: Future | None = None) -> Future:
+        """Copy-on-write of selected rows into the sidecar while a baseline
+        load may still be pending; the returned future resolves to the
+        published map once the copies have run (paged.py:276-328)."""
+        positions = _positions(logical_positions, "logical_positions")
+        self._check_rows(len(positions), key, value)
         if load_future is not None and not isinstance(load_future, Future):
             raise TypeError("load_future must be a concurrent Future")
-        with self._mutex:
+        with self._lock:
             if self._decoded:
                 raise RuntimeError("selected promotion must precede decode")
-            if self._selected.intersection(positions):
+            if not self._selected.isdisjoint(positions):
                 raise ValueError("already staged tokens must use update_selected")
             if load_future is not None and load_future.done():
                 load_future.result()
@@ -286,223 +334,202 @@ class NativePagedKV:
                 for run in runs:
                     for i in range(run.slot_count):
                         slots.append(run.start_slot + i)
-                        rows.append(int.from_bytes(run.payload[8 * i : 8 * i + 8], "little"))
-                self._write_slots(slots, key, value, rows)
-                return _completion_future(self.cache.device)
+                        rec = run.payload[i * _ROW_BYTES:(i + 1) * _ROW_BYTES]
+                        rows.append(int.from_bytes(rec, "little"))
+                return _Waiter.submit(self._scatter(slots, key, value, rows))
 
-            # 8-byte payloads name tensor rows: no KV bytes leave the device
-            updates = {t: row.to_bytes(8, "little") for row, t in enumerate(positions)}
+            # the records name rows of key/value; no KV byte leaves the device
+            records = {t: row.to_bytes(_ROW_BYTES, "little") for row, t in enumerate(positions)}
             promotion = self.slot_map.promote_selected(
-                updates, writer, load_future=load_future, allow_inplace=False
-            )
+                records, writer, load_future=load_future, allow_inplace=False)
             self._selected.update(positions)
             self._promotions.append(promotion)
-            if load_future is not None and load_future not in self._loads:
+            if load_future is not None and all(f is not load_future for f in self._loads):
                 self._loads.append(load_future)
             return promotion
 
     stage_selected = promote_selected
 
     def write_selected_ready(self, logical_positions, key, value) -> dict[int, int]:
-        """Load-first branch: overwrite original native slots in place."""
-        positions = _indices(logical_positions, "logical_positions")
-        self._records(positions, key, value)
-        with self._mutex:
+        """Load-first branch: overwrite the selected tokens' own native slots
+        once the whole baseline is on the device (paged.py:330-374)."""
+        positions = _positions(logical_positions, "logical_positions")
+        self._check_rows(len(positions), key, value)
+        with self._lock:
             mapping = self.slot_map.snapshot()
-            self._check_loads()
-            self._check_promotions()
+            self._loads_settled()
+            self._promotions_settled()
             if self._decoded:
                 raise RuntimeError("ready selected writes must precede decode")
-            if len(self._baseline_ready) != self.prompt_length:
+            if self._baseline_count != self.prompt_length:
                 raise RuntimeError("native baseline device writes must complete first")
-            if not set(positions) <= set(self._canonical):
+            if any(t >= len(self._home) for t in positions):
                 raise ValueError("ready selected tokens require original native slots")
-            if self._selected.intersection(positions) or any(
-                mapping[t] != self._canonical[t] for t in positions
-            ):
+            moved = any(mapping[t] != self._home[t] for t in positions)
+            if moved or not self._selected.isdisjoint(positions):
                 raise ValueError("already selected tokens must use update_selected")
-            slots = [self._canonical[t] for t in positions]
-            with self.slot_map.write_guard(slots):
-                try:
-                    self._write_slots(slots, key, value)
-                    _completion_future(self.cache.device).result()
-                except BaseException:
-                    self.slot_map.invalidate()
-                    raise
+            self._sync_write([self._home[t] for t in positions], key, value)
             self._selected.update(positions)
-            self._ready_inplace_writes += len(positions)
+            self._counts["ready_inplace"] += len(positions)
             return self.slot_map.snapshot()
 
-    def _update_targets(self, positions: list[int]):
-        """Current slots and the canonical mirrors worth attempting."""
+    def _targets(self, positions: list[int]) -> tuple[list[int], list[int]]:
+        """Current slots of the rows, and the rows whose own native slot is
+        worth mirroring to (relocated and not shared)."""
         mapping = self.slot_map.snapshot()
-        if not set(positions) <= set(mapping):
+        if any(t not in mapping for t in positions):
             raise ValueError("updated rows must already have logical mappings")
-        if any(mapping[t] in self._shared for t in positions):
+        current = [mapping[t] for t in positions]
+        if not self._shared.isdisjoint(current):
             raise ValueError("updated rows cannot mutate shared native slots")
-        mirrors = [
-            row
-            for row, t in enumerate(positions)
-            if self._canonical[t] not in self._shared and self._canonical[t] != mapping[t]
-        ]
-        return [mapping[t] for t in positions], mirrors
+        mirrors = [r for r, t in enumerate(positions)
+                   if self._home[t] != current[r] and self._home[t] not in self._shared]
+        return current, mirrors
+
+    def _ready_for_update(self) -> None:
+        self._loads_settled()
+        self._promotions_settled()
+        if self._decoded:
+            raise RuntimeError("selected updates must precede decode hole reuse")
 
     def update_selected(self, logical_positions, key, value) -> None:
-        """Write fused selected / fresh mandatory rows to their current slots,
-        mirroring relocated rows into unpinned canonical slots."""
-        positions = _indices(logical_positions, "logical_positions")
-        self._records(positions, key, value)
-        with self._mutex:
-            self._check_loads()
-            self._check_promotions()
-            if self._decoded:
-                raise RuntimeError("selected updates must precede decode hole reuse")
-            slots, mirrors = self._update_targets(positions)
-            optional = [self._canonical[positions[r]] for r in mirrors]
-            with self.slot_map.write_guard(slots, optional_slots=optional) as writable:
-                mirror_rows = [r for r in mirrors if self._canonical[positions[r]] in writable]
+        """Fused rows into their current slots, mirrored into their own native
+        slots where those are free (paged.py:376-431); one scatter."""
+        positions = _positions(logical_positions, "logical_positions")
+        self._check_rows(len(positions), key, value)
+        with self._lock:
+            self._ready_for_update()
+            current, mirrors = self._targets(positions)
+            homes = [self._home[positions[r]] for r in mirrors]
+            with self.slot_map.write_guard(current, optional_slots=homes) as free:
+                mirror_rows = [r for r in mirrors if self._home[positions[r]] in free]
+                slots = current + [self._home[positions[r]] for r in mirror_rows]
+                rows = list(range(len(current))) + mirror_rows
                 try:
-                    # one scatter for the current slots plus the mirrors
-                    all_slots = slots + [self._canonical[positions[r]] for r in mirror_rows]
-                    rows = list(range(len(slots))) + mirror_rows
-                    self._write_slots(all_slots, key, value, rows)
-                    _completion_future(self.cache.device).result()
+                    self._scatter(slots, key, value, rows).wait()
                 except BaseException:
                     self.slot_map.invalidate()
                     raise
-                self._canonical_mirrors += len(mirror_rows)
+                self._counts["mirrors"] += len(mirror_rows)
 
     def update_fused(self, logical_positions, wca_state, layer_index, cached_k, cached_v,
                      recomputed_k, recomputed_v):
-        """WCA update with the blend and the paged writes fused in one kernel.
-
-        Equivalent to ``wca_state.update(...)`` followed by
-        ``update_selected(positions, fused_k, fused_v)`` when no canonical
-        mirror is needed (every row still maps to its own canonical slot);
-        otherwise the mirrors are written by a second scatter.
-        """
-        positions = _indices(logical_positions, "logical_positions")
-        with self._mutex:
-            self._check_loads()
-            self._check_promotions()
-            if self._decoded:
-                raise RuntimeError("selected updates must precede decode hole reuse")
-            slots, mirrors = self._update_targets(positions)
-            optional = [self._canonical[positions[r]] for r in mirrors]
-            slot_t = torch.tensor(slots, dtype=torch.int64, device=self.cache.device)
-            if any(s >= self.native_total_slots for s in slots):
-                self._ensure_sidecar()
-            with self.slot_map.write_guard(slots, optional_slots=optional) as writable:
+        """``wca_state.update`` with the blend written straight into the rows'
+        current paged slots by the same kernel, then the mirrors.  Equal to
+        ``update`` followed by ``update_selected(positions, fused_k, fused_v)``."""
+        positions = _positions(logical_positions, "logical_positions")
+        with self._lock:
+            self._ready_for_update()
+            current, mirrors = self._targets(positions)
+            homes = [self._home[positions[r]] for r in mirrors]
+            slot_t = torch.tensor(current, dtype=torch.int64, device=self.cache.device)
+            if self._side_key is None and current and max(current) >= self.native_total_slots:
+                shape = (self.max_selected, self.kv_heads, self.head_dim)
+                self._side_key = self.cache.new_empty(shape)
+                self._side_value = self.cache.new_empty(shape)
+            with self.slot_map.write_guard(current, optional_slots=homes) as free:
                 try:
-                    update = wca_state.update(
+                    result = wca_state.update(
                         layer_index, cached_k, cached_v, recomputed_k, recomputed_v,
                         computed_indices=torch.tensor(positions, device=self.cache.device),
-                        paged=(self, slot_t),
-                    )
-                    mirror_rows = [r for r in mirrors if self._canonical[positions[r]] in writable]
-                    if mirror_rows:
-                        self._write_slots(
-                            [self._canonical[positions[r]] for r in mirror_rows],
-                            update.fused_k, update.fused_v, mirror_rows,
-                        )
-                    _completion_future(self.cache.device).result()
+                        paged=(self, slot_t))
+                    mirror_rows = [r for r in mirrors if self._home[positions[r]] in free]
+                    self._scatter([self._home[positions[r]] for r in mirror_rows],
+                                  result.fused_k, result.fused_v, mirror_rows).wait()
                 except BaseException:
                     self.slot_map.invalidate()
                     raise
-                self._canonical_mirrors += len(mirror_rows)
-            return update
+                self._counts["mirrors"] += len(mirror_rows)
+            return result
 
     # ---------------------------------------------------------------- reads
     def gather(self, logical_positions) -> tuple[torch.Tensor, torch.Tensor]:
-        """Gather logical KV in caller order with atomic mapping pins."""
-        positions = _indices(logical_positions, "logical_positions")
-        with self._mutex, self.slot_map.pinned_mapping(positions) as mapping:
-            self._check_loads(allow_pending=True)
+        """Logical KV in caller order; the mappings stay pinned until the
+        device reads have completed (paged.py:433-472)."""
+        positions = _positions(logical_positions, "logical_positions")
+        with self._lock, self.slot_map.pinned_mapping(positions) as mapping:
+            self._loads_settled(pending_ok=True)
             shape = (len(positions), self.kv_heads, self.head_dim)
             key, value = self.cache.new_empty(shape), self.cache.new_empty(shape)
+            device = self.cache.device
+            launch = _Launch(device)
             if positions:
-                device = self.cache.device
-                slot_t = torch.tensor(
-                    [mapping[t] for t in positions], dtype=torch.int64, device=device
-                )
-                status = N.Status(device)
-                kv = self.device_view()
-                N.check(
-                    N.load().cs_slide_gather(
-                        ctypes.byref(kv), slot_t.data_ptr(), len(positions), key.data_ptr(),
-                        value.data_ptr(), key.stride(0), key.stride(1), status.ptr,
-                        N.stream_of(device),
-                    ),
-                    "cs_slide_gather",
-                )
-                if status.read() & N.ST_SLOT_RANGE:
-                    raise ValueError("slot outside the native cache and sidecar")
-            _completion_future(self.cache.device).result()
+                slot_t = torch.tensor([mapping[t] for t in positions],
+                                      dtype=torch.int64).to(device, non_blocking=True)
+                view = self.device_view()
+                N.check(N.load().cs_slide_gather(
+                    ctypes.byref(view), slot_t.data_ptr(), len(positions), key.data_ptr(),
+                    value.data_ptr(), key.stride(0), key.stride(1), launch.status_ptr,
+                    N.stream_of(device)), "cs_slide_gather")
+            launch.enqueue_done().wait()
             return key, value
 
     # --------------------------------------------------------------- decode
     def decode(self, token: int, key, value, canonical_slot: int | None = None) -> int:
-        """Reuse an eligible native hole, else bind the caller's slot; mirror."""
+        """Append decode token ``token``: the lowest idle native hole if any,
+        else the caller's native slot for it, plus a mirror into that slot
+        when a hole was taken (paged.py:474-524).  Returns the slot chosen."""
         if type(token) is not int or token < 0:
             raise ValueError("decode token must be a nonnegative integer")
-        if key.ndim == 2:
-            key = key.unsqueeze(0)
-        if value.ndim == 2:
-            value = value.unsqueeze(0)
-        self._records([token], key, value)
-        with self._mutex:
-            self._check_loads(allow_pending=True)
-            self._check_promotions()
-            if token != len(self._canonical):
+        key = key.unsqueeze(0) if key.ndim == 2 else key
+        value = value.unsqueeze(0) if value.ndim == 2 else value
+        self._check_rows(1, key, value)
+        with self._lock:
+            self._loads_settled(pending_ok=True)
+            self._promotions_settled()
+            if token != len(self._home):
                 raise ValueError("decode must append the next logical token")
-            expected = self._canonical_slot(token)
+            own = self._slot_in(self._blocks, token)
             if canonical_slot is None:
-                canonical_slot = expected
-            if type(canonical_slot) is not int or canonical_slot != expected:
+                canonical_slot = own
+            if type(canonical_slot) is not int or canonical_slot != own:
                 raise ValueError("decode canonical slot is not owned by its block table")
-            if canonical_slot in self._canonical.values():
+            if canonical_slot in self._home_set:
                 raise ValueError("decode native slot aliases an existing canonical token")
-            with self.slot_map.decode_write_guard(
-                token, canonical_slot, reuse_vacated=True
-            ) as chosen:
-                targets = [chosen] if chosen == canonical_slot else [chosen, canonical_slot]
-                self._write_slots(targets, key, value, [0] * len(targets))
-                _completion_future(self.cache.device).result()
-            reused = chosen != canonical_slot
-            self._hole_reuses += int(reused)
-            self._canonical_mirrors += int(reused)
-            self._native_binds += int(not reused)
-            self._canonical[token] = canonical_slot
+            with self.slot_map.decode_write_guard(token, canonical_slot,
+                                                  reuse_vacated=True) as chosen:
+                targets = sorted({chosen, canonical_slot})
+                self._scatter(targets, key, value, [0] * len(targets)).wait()
+            hole = chosen != canonical_slot
+            self._counts["hole_reuse"] += hole
+            self._counts["mirrors"] += hole
+            self._counts["native_bind"] += not hole
+            self._home.append(canonical_slot)
+            self._home_set.add(canonical_slot)
             self._decoded = True
             return chosen
 
     # ------------------------------------------------------------- metadata
     def snapshot(self) -> dict[int, int]:
-        with self._mutex:
+        with self._lock:
             return self.slot_map.snapshot()
 
     def page_metadata(self) -> tuple[dict[str, int | bool], ...]:
-        with self._mutex:
+        """Per mapped physical page of this arena: token / selected counts
+        and guards (``dirty`` = holds a selected token)."""
+        with self._lock:
             return self.slot_map.page_metadata(self.block_size, self._selected)
 
     def spill_order(self) -> tuple[int, ...]:
-        """Advisory clean-first, most-selected-first page order (paged.py:540-559)."""
-        pages = [p for p in self.page_metadata() if p["spill_eligible"]]
-        pages.sort(key=lambda p: (p["dirty"], -p["selected_count"], p["page_id"]))
-        return tuple(p["page_id"] for p in pages)
+        """Advisory page order for a spill (paged.py:530-559): guarded pages
+        excluded, clean before dirty, then more selected tokens first, then
+        page id.  Reserves nothing."""
+        eligible = [p for p in self.page_metadata() if p["spill_eligible"]]
+        ranked = sorted(eligible,
+                        key=lambda p: (p["dirty"], -p["selected_count"], p["page_id"]))
+        return tuple(p["page_id"] for p in ranked)
 
     def stats(self) -> dict[str, int]:
-        with self._mutex:
+        with self._lock:
+            c = self._counts
             return {
                 **self.slot_map.stats(),
-                "physical_hole_reuse": self._hole_reuses,
-                "decode_native_bind": self._native_binds,
-                "canonical_mirror_writes": self._canonical_mirrors,
+                "physical_hole_reuse": c["hole_reuse"],
+                "decode_native_bind": c["native_bind"],
+                "canonical_mirror_writes": c["mirrors"],
                 "sidecar_capacity_slots": self.max_selected,
-                "sidecar_allocated_slots": (
-                    self.max_selected if self._side_key is not None else 0
-                ),
-                "selected_ready_inplace_writes": self._ready_inplace_writes,
+                "sidecar_allocated_slots": 0 if self._side_key is None else self.max_selected,
+                "selected_ready_inplace_writes": c["ready_inplace"],
                 "native_pool_capacity_slots": self.native_total_slots,
                 "native_pool_capacity_blocks": self.cache.shape[0],
                 "native_pool_capacity_delta": 0,
@@ -510,5 +537,5 @@ class NativePagedKV:
             }
 
     def invalidate(self) -> None:
-        with self._mutex:
+        with self._lock:
             self.slot_map.invalidate()

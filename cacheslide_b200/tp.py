@@ -31,7 +31,7 @@ import torch.distributed as dist
 from torch import Tensor
 
 from . import _native as N
-from .policy import WCAConfig
+from .policy import WCAConfig, as_config
 from .wca import (WCAState, WCAUpdate, _inner, _kv, _mask, _matching, _raise_numeric,
                   _raise_update)
 
@@ -89,7 +89,7 @@ class ShardedWCAState(WCAState):
         heads_total: int,
         group=None,
     ) -> ShardedWCAState:
-        config = config or WCAConfig()
+        config = as_config(config)
         _kv("cached_k", cached_k)
         _matching("recomputed_k", recomputed_k, cached_k)
         if heads_total < cached_k.shape[1]:

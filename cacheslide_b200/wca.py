@@ -23,7 +23,7 @@ import torch
 from torch import Tensor
 
 from . import _native as N
-from .policy import WCAConfig, _finite_number
+from .policy import WCAConfig, as_config, check_real
 
 __all__ = [
     "WCAConfig",
@@ -68,7 +68,7 @@ def _inner(t: Tensor) -> Tensor:
 
 
 def _epsilon(epsilon) -> None:
-    _finite_number("epsilon", epsilon)
+    check_real("epsilon", epsilon)
     if epsilon <= 0:
         raise ValueError("epsilon must be finite and positive")
 
@@ -190,7 +190,7 @@ class WCAState:
         mandatory_mask: Tensor,
         config: WCAConfig | None = None,
     ) -> WCAState:
-        config = config or WCAConfig()
+        config = as_config(config)
         _kv("cached_k", cached_k)
         _matching("recomputed_k", recomputed_k, cached_k)
         n = cached_k.shape[0]

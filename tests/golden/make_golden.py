@@ -260,21 +260,49 @@ def paged_cases(ref):
     return out
 
 
-def main(src: str) -> None:
+SLOT_TRACE_SEEDS = 400
+
+
+def slot_traces(ref) -> dict:
+    """The reference's LayerSlotMap driven through the seeded random traces of
+    ``tests/slot_trace.py``: per seed the number of trace lines and the
+    SHA-256 of the trace text (every return value and exception)."""
+    import hashlib
+
+    sys.path.insert(0, str(HERE.parent))
+    import slot_trace
+    from cacheslide_vllm.slide import LayerSlotMap
+
+    seeds = {}
+    for seed in range(SLOT_TRACE_SEEDS):
+        lines = slot_trace.drive(LayerSlotMap, seed)
+        seeds[str(seed)] = dict(lines=len(lines),
+                                sha256=hashlib.sha256("\n".join(lines).encode()).hexdigest())
+    return dict(steps=120, seeds=seeds)
+
+
+def main(src: str, only: list[str]) -> None:
     sys.path.insert(0, src)
     import cacheslide_vllm as ref
 
     torch.set_num_threads(4)
     for name, fn in (("cope", cope_cases), ("wca", wca_cases),
                      ("paged", paged_cases)):
+        if only and name not in only:
+            continue
         cases = fn(ref)
         flat = {f"{case}__{key}": np.asarray(val)
                 for case, fields in cases.items() for key, val in fields.items()}
         np.savez_compressed(HERE / f"{name}.npz", **flat)
         print(name, len(flat), "arrays")
+    if not only or "slot_trace" in only:
+        traces = slot_traces(ref)
+        (HERE / "slot_trace.json").write_text(json.dumps(traces, indent=0, sort_keys=True))
+        print("slot_trace", len(traces["seeds"]), "seeds")
 
 
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
-        raise SystemExit("usage: make_golden.py <CacheSlide checkout>/src")
-    main(sys.argv[1])
+    if len(sys.argv) < 2:
+        raise SystemExit("usage: make_golden.py <CacheSlide checkout>/src "
+                         "[cope|wca|paged|slot_trace ...]")
+    main(sys.argv[1], sys.argv[2:])

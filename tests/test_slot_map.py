@@ -134,3 +134,25 @@ def test_page_metadata_counts_and_guards():
     assert meta[1]["shared"] and not meta[1]["spill_eligible"]
     with layer.pin_slots([0]):
         assert next(p for p in layer.page_metadata(4, []) if p["page_id"] == 0)["pinned"]
+
+
+def test_random_traces_match_the_reference_slot_map():
+    """Seeded random operation traces (tests/slot_trace.py) give exactly the
+    reference LayerSlotMap's outcomes: every slot number, published map,
+    guard decision, statistic and exception (tests/golden/slot_trace.json,
+    recorded from the reference by tests/golden/make_golden.py)."""
+    import hashlib
+    import json
+    from pathlib import Path
+
+    import slot_trace
+
+    golden = json.loads((Path(__file__).parent / "golden" / "slot_trace.json").read_text())
+    assert golden["steps"] == 120
+    bad = []
+    for seed, want in golden["seeds"].items():
+        lines = slot_trace.drive(LayerSlotMap, int(seed))
+        got = hashlib.sha256("\n".join(lines).encode()).hexdigest()
+        if len(lines) != want["lines"] or got != want["sha256"]:
+            bad.append(int(seed))
+    assert not bad, f"traces differ from the reference for seeds {bad[:10]}"
