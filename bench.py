@@ -13,7 +13,8 @@ inputs resident in HBM; ``e2e`` repeats the step with the per-layer snapshot
 and the fresh rows copied from pinned host memory and the outputs copied back.
 
 ``--impl reference`` times the reference algorithm on the host cores (the
-numpy restatement of the reference's CPU path) on a bounded sample.
+numpy restatement of the reference's CPU path) on whole requests of the same
+workload (every active row; a step is one eighth of a request).
 Multi-GPU (torchrun): requests are sharded by rank, no data-path collective.
 """
 
@@ -48,7 +49,6 @@ def parse():
     ap.add_argument("--requests", type=int, default=8)
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-sample-rows", type=int, default=128)
     return ap.parse_args()
 
 
@@ -165,66 +165,94 @@ class Clocks:
 
 
 # ------------------------------------------------------------- CPU legs
-def cpu_layer_sample(work, b: int, rows: int, threads: int):
-    """Reference algorithm for one request on the host (numpy restatement of
-    the reference CPU path): SLIDE baseline write, WCA initialize + select +
-    update, fused rows written back, logical gather, CCPE attention on `rows`
-    of the active query rows.  Returns (seconds for the full request, with the
-    attention extrapolated by causal cells, description, sample wall time)."""
-    from oracle import cope as ocope
-    from oracle import slide as oslide
-    from oracle import wca as owca
+class CpuRequest:
+    """The reference algorithm for one request on the host (the numpy
+    restatement of the reference's CPU path), split into SLICES equal steps:
+    slice 0 runs the SLIDE baseline write, WCA initialize + select + update,
+    the write-back of the fused rows and the logical gather; slice s then runs
+    the CCPE attention of active rows s, s + SLICES, ...  The SLICES slices
+    together are one whole request: every active row, nothing extrapolated."""
 
-    r = work.requests[b]
-    c = work.cfg
-    f32 = lambda t: t.float().cpu().numpy()  # noqa: E731
-    cached_k, cached_v = f32(r.cached_k), f32(r.cached_v)
-    calib_k = f32(r.calib_k)
-    q_all, fresh_k, fresh_v = f32(r.q_all), f32(r.fresh_k), f32(r.fresh_v)
-    cache = np.zeros((work.cache.shape[0], c.kv_heads, c.block, 2 * c.head_dim), np.float32)
-    slots = r.slots.cpu().numpy()
-    E = work.E.float().cpu().numpy()
-    key_chunk = r.key_chunk.cpu().numpy()
-    offsets = r.offsets.cpu().numpy()
-    fixed = r.fixed.cpu().numpy()
-    reused, mandatory = r.reused.cpu().numpy(), r.mandatory.cpu().numpy()
+    SLICES = 8
 
-    t0 = time.perf_counter()
-    oslide.scatter(cache, None, None, slots, cached_k, cached_v)
-    st = owca.OracleWCA(correction_fraction=c.fraction).initialize(
-        cached_k, calib_k, reused, mandatory)
-    active = st.active
-    sel_prev = np.nonzero(st.selected & ~mandatory)[0]
-    q = q_all[active]
-    upd = st.update(2, cached_k, cached_v, fresh_k[active], fresh_v[active])
-    oslide.scatter(cache, None, None, slots[active], upd["fused_k"].astype(np.float32),
-                   upd["fused_v"].astype(np.float32))
-    k, v = oslide.gather(cache, None, None, slots)
-    t_wca = time.perf_counter() - t0
-    pick = np.linspace(0, len(active) - 1, min(rows, len(active))).astype(np.int64)
+    def __init__(self, work, b: int, threads: int):
+        r = work.requests[b]
+        c = work.cfg
+        f32 = lambda t: t.float().cpu().numpy()  # noqa: E731
+        self.cached_k, self.cached_v = f32(r.cached_k), f32(r.cached_v)
+        self.calib_k = f32(r.calib_k)
+        self.q_all, self.fresh_k, self.fresh_v = f32(r.q_all), f32(r.fresh_k), f32(r.fresh_v)
+        self.cache_shape = (work.cache.shape[0], c.kv_heads, c.block, 2 * c.head_dim)
+        self.slots = r.slots.cpu().numpy()
+        self.E = work.E.float().cpu().numpy()
+        self.key_chunk = r.key_chunk.cpu().numpy()
+        self.offsets = r.offsets.cpu().numpy()
+        self.fixed = r.fixed.cpu().numpy()
+        self.reused, self.mandatory = r.reused.cpu().numpy(), r.mandatory.cpu().numpy()
+        self.fraction = c.fraction
+        self.tokens = c.seq
+        self.threads = threads
 
-    def part(idx):
-        return ocope.cope_attention(
-            q[idx], k, v, E, active[idx],
-            visibility_fn=lambda a_, b_: ocope.association_mask(a_, b_, fixed, sel_prev),
-            chunk_reset=(key_chunk, offsets[:, active[idx]]), chunk=16)
+    def layer_state(self) -> None:
+        from oracle import slide as oslide
+        from oracle import wca as owca
 
-    t1 = time.perf_counter()
-    groups = np.array_split(pick, max(1, threads))
-    with ThreadPoolExecutor(max_workers=threads) as pool:
-        list(pool.map(part, [g for g in groups if len(g)]))
-    t_att = time.perf_counter() - t1
-    cells_all = float((active + 1).sum())
-    cells_s = float((active[pick] + 1).sum())
-    seconds = t_wca + t_att * cells_all / cells_s
-    desc = (f"request {b}: full SLIDE write + WCA init/update + gather; attention on "
-            f"{len(pick)} of {len(active)} active rows, extrapolated by causal cells; "
-            f"{threads} threads")
-    return seconds, desc, t_wca + t_att
+        cache = np.zeros(self.cache_shape, np.float32)
+        oslide.scatter(cache, None, None, self.slots, self.cached_k, self.cached_v)
+        st = owca.OracleWCA(correction_fraction=self.fraction).initialize(
+            self.cached_k, self.calib_k, self.reused, self.mandatory)
+        self.active = st.active
+        self.sel_prev = np.nonzero(st.selected & ~self.mandatory)[0]
+        upd = st.update(2, self.cached_k, self.cached_v, self.fresh_k[self.active],
+                        self.fresh_v[self.active])
+        oslide.scatter(cache, None, None, self.slots[self.active],
+                       upd["fused_k"].astype(np.float32), upd["fused_v"].astype(np.float32))
+        self.k, self.v = oslide.gather(cache, None, None, self.slots)
+
+    def attention(self, rows: np.ndarray) -> None:
+        from oracle import cope as ocope
+
+        active = self.active
+
+        def part(idx):
+            return ocope.cope_attention(
+                self.q_all[active[idx]], self.k, self.v, self.E, active[idx],
+                visibility_fn=lambda a_, b_: ocope.association_mask(a_, b_, self.fixed,
+                                                                    self.sel_prev),
+                chunk_reset=(self.key_chunk, self.offsets[:, active[idx]]), chunk=16)
+
+        groups = [g for g in np.array_split(rows, max(1, self.threads)) if len(g)]
+        with ThreadPoolExecutor(max_workers=self.threads) as pool:
+            list(pool.map(part, groups))
+
+    def step(self, s: int) -> float:
+        """Slice s % SLICES of the request; returns its seconds."""
+        t0 = time.perf_counter()
+        k = s % self.SLICES
+        if k == 0:
+            self.layer_state()
+        self.attention(np.arange(k, len(self.active), self.SLICES))
+        return time.perf_counter() - t0
+
+    def describe(self, requests: int) -> str:
+        return (f"{requests} whole request(s) of the workload (request 0, {self.tokens} tokens: "
+                f"SLIDE write, WCA initialize/select/update, gather, CCPE attention of all "
+                f"{len(self.active)} active rows), each timed as {self.SLICES} slices; "
+                f"nothing extrapolated; {self.threads} host threads")
+
+
+def cpu_requests(work, requests: int, threads: int):
+    """Seconds per request of the reference algorithm over `requests` whole
+    requests, and the sample description."""
+    cpu = CpuRequest(work, 0, threads)
+    total = sum(cpu.step(s) for s in range(requests * CpuRequest.SLICES))
+    return total / requests, cpu.describe(requests)
 
 
 def run_reference(args):
-    """--impl reference: the reference algorithm on host cores (numpy port)."""
+    """--impl reference: the reference algorithm on host cores (numpy port).
+    A step is one slice (1/8) of a whole request; the timed steps are rounded
+    up to whole requests, so at least one request is timed unextrapolated."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -236,19 +264,21 @@ def run_reference(args):
     cfg = WorkloadConfig(requests=1, seq=args.seq)
     # inputs are built on the host; nothing of this package runs on this arm
     work = SyntheticWorkload(cfg, torch.device("cpu"))
-    times = []
-    for i in range(args.warmup + args.steps):
-        sec, desc, _ = cpu_layer_sample(work, 0, max(16, args.cpu_sample_rows // 4), threads)
-        if i >= args.warmup:
-            times.append(sec)
-    per_req = statistics.median(times)
+    cpu = CpuRequest(work, 0, threads)
+    cpu.layer_state()  # warm-up: the request's WCA / SLIDE part (no attention)
+    slices = CpuRequest.SLICES
+    requests = max(1, -(-args.steps // slices))
+    times = [cpu.step(s) for s in range(requests * slices)]
+    per_req = sum(times) / requests
     value = cfg.seq / per_req
+    desc = cpu.describe(requests)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": per_req * 8 * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "sample": desc},
+        "n_gpus": args.gpus, "steps": len(times), "warmup": 1,
+        "ms_per_step": statistics.mean(times) * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "sample": desc, "sample_fraction": 1.0,
+                   "per": "one host process (rank 0), whatever the number of GPUs"},
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
                          "sample": desc},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0,
@@ -399,9 +429,9 @@ def main():
         cpu = None
         if not args.no_cpu_baseline:
             threads = os.cpu_count() or 1
-            sec, desc, wall = cpu_layer_sample(work, 0, args.cpu_sample_rows, threads)
+            sec, desc = cpu_requests(work, 1, threads)
             cpu = {"value": cfg.seq / sec, "unit": "tok/s", "cores": threads, "kind": "port",
-                   "sample": desc + f"; sample wall {wall:.1f}s"}
+                   "sample": desc, "sample_fraction": 1.0}
         launches_per_step = len(work.requests) * 6
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,

@@ -156,3 +156,30 @@ def test_random_traces_match_the_reference_slot_map():
         if len(lines) != want["lines"] or got != want["sha256"]:
             bad.append(int(seed))
     assert not bad, f"traces differ from the reference for seeds {bad[:10]}"
+
+
+def test_errors_are_the_reference_classes_when_it_is_importable():
+    """With the reference package on the path, the slot map raises the
+    reference's own storage errors, so its runtime's fallbacks catch them
+    unedited; without it, classes of the same names and bases are used."""
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    from cacheslide_b200 import errors
+
+    assert issubclass(errors.CacheCapacityError, RuntimeError)
+    stub = Path(__file__).parent / "_stub_reference"
+    code = (
+        "import sys; sys.path.insert(0, %r)\n"
+        "from cacheslide_vllm.storage import CacheCapacityError as Ref\n"
+        "from cacheslide_b200 import errors\n"
+        "from cacheslide_b200.slide import LayerSlotMap\n"
+        "assert errors.SHARED_WITH_REFERENCE and errors.CacheCapacityError is Ref\n"
+        "m = LayerSlotMap({0: 0}, max_slots=1)\n"
+        "try:\n    m.allocate_decode(1)\nexcept Ref:\n    print('caught')\n"
+    ) % str(stub)
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                         cwd=str(Path(__file__).parents[1]))
+    assert out.returncode == 0, out.stderr
+    assert out.stdout.strip() == "caught"
