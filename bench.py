@@ -49,6 +49,9 @@ def parse():
     ap.add_argument("--requests", type=int, default=8)
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batched-attention", action="store_true",
+                    help="one attention launch for all requests after their WCA / SLIDE "
+                         "chains (default: one launch per request on its stream)")
     return ap.parse_args()
 
 
@@ -60,11 +63,10 @@ def peaks():
 
 
 # ----------------------------------------------------------- accounting
-# DRAM bytes of one C2 request launch of the prefill kernel (ncu --set full,
-# dram__bytes_read.sum 26.63 MB + dram__bytes_write.sum 0.02 MB): the K/V of the
-# request (16.8 MB) cross HBM once, plus Q, the slot table and metadata; the
-# outputs stay in L2 at the end of the launch
-PREFILL_DRAM_BYTES_PER_LAUNCH = 26_643_712
+# DRAM bytes of one batched prefill launch of the C2 step (8 requests), from
+# an ncu capture of that launch (dram__bytes_read.sum + dram__bytes_write.sum);
+# None until captured for the current kernel
+PREFILL_DRAM_BYTES_PER_LAUNCH = None
 
 
 def attention_flops(work) -> float:
@@ -311,7 +313,7 @@ def main():
                                 device_id=dev)
     cfg = WorkloadConfig(requests=args.requests, seq=args.seq, seed=1000 + rank)
     work = SyntheticWorkload(cfg, dev)
-    step = ReuseStep(work)
+    step = ReuseStep(work, batched_attention=args.batched_attention)
     # a dedicated stream, current for every torch op below: on the legacy
     # default stream, events around the 8-stream fork/join of a step were
     # seen to under-count the step (456 us against a 1040 us host-synchronised
@@ -354,14 +356,14 @@ def main():
     step_ms = [a.elapsed_time(b) for a, b in ev]
     total_ms = sum(step_ms)
 
-    # ---- attention launches alone (roofline of the dominant kernel)
+    # ---- attention launches alone (roofline of the dominant kernel): one
+    # launch for all requests of the step (the launch the step issues)
     att = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
     for i in range(args.steps):
         flush.fill_(i & 0xFF)
         att[i][0].record(stream)
-        for r in work.requests:
-            step.attention(r, s)
+        step.attention_all(s)
         att[i][1].record(stream)
     # ---- decode steps
     dec = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -446,12 +448,13 @@ def main():
                        "parallelism": f"request-sharded x{world}"},
             "decode": {"value": decode_value, "unit": "tok/s",
                        "ms_per_step": dec_ms, "note": "one token per request over 4097 keys"},
-            "roofline": {"bound": "tensor", "kernel": "cope_prefill_sm100 (one request per launch)",
+            "roofline": {"bound": "tensor",
+                         "kernel": "cope_prefill_sm100_batch (all requests of a step per launch)",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "peak_kind": pk_kind,
-                         "flops_per_launch": flops / len(work.requests),
-                         "ms_per_launch": att_ms / len(work.requests),
-                         "launches_timed": len(work.requests) * args.steps,
+                         "flops_per_launch": flops,
+                         "ms_per_launch": att_ms,
+                         "launches_timed": args.steps,
                          "traffic": PREFILL_DRAM_BYTES_PER_LAUNCH,
                          "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum of one "
                                          "C2 request launch (ncu --set full capture)"},

@@ -110,6 +110,7 @@ _SIGNATURES = {
                       _p, _p, _p],
     "cs_cope_attn": [ctypes.POINTER(AttnParams), _p],
     "cs_cope_attn_prefill": [ctypes.POINTER(AttnParams), _p],
+    "cs_cope_attn_prefill_batch": [ctypes.POINTER(AttnParams), _i32, _p],
     "cs_cope_attn_decode_workspace": [ctypes.POINTER(AttnParams)],
     "cs_cope_attn_decode": [ctypes.POINTER(AttnParams), _p, _p],
     "cs_cope_attn_decode_noalloc": [ctypes.POINTER(AttnParams), _p],

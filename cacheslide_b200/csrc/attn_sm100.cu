@@ -1,35 +1,36 @@
 // Tensor-core CoPE / CCPE prefill for sm_100a (tcgen05 + TMEM + TMA).
 //
-// One CTA computes a 128-row tile: R = 128 / G query rows x the G query heads
-// of one KV head (GQA packing: every row of the tile reads the same K/V).
+// One CTA computes two 128-row query tiles ("a" and "b"): each is R = 128 / G
+// query rows x the G query heads of one KV head (GQA packing: every row of
+// both tiles reads the same K/V tiles).  The two tiles alternate on the
+// tensor cores: while the softmax warps of one tile work on its scores, the
+// MMA warp runs the other tile's PV and next QK.
 // Warp roles (416 threads):
-//   warps 0-7   softmax, two threads per S row (TMEM lane r): warp q (0-3)
-//               takes the newer 64 keys of every key tile, warp q+4 the older
-//               64.  Per tile: gates sigmoid(q.k / sqrt(d)), the reverse
-//               cumulative count of position.py:295-307 (restarted at chunk
-//               boundaries in the chunk-reset mode; the older half scans with
-//               a zero start and adds the newer half's count afterwards), the
-//               q.E bias interpolated from a per-row table in shared memory,
-//               causal / association masks, the tile max, then
-//               P = 2^(s - m) packed to 16-bit pairs back into TMEM over the
-//               tile's own S columns.  Once every row of a warp has a count
-//               >= npos-1 all older keys share one bias: only logit, max and
-//               exponential remain (saturated tiles).
-//   warps 8-11  producer: Q tile, the E table split into bf16 hi + lo, the key
-//               metadata of every tile (fixed keys, chunk boundaries), and the
-//               K and V tiles (two stages each, K one tile ahead of V) read
-//               through the per-key slot table: TMA 64 x 16 tile loads for
-//               runs of 16 keys in consecutive rows, tile::gather4 for groups
-//               of 4 keys, cp.async for the rest, all into the 128-byte
-//               swizzled UMMA layout.
-//   warp 12     MMA issuer (one thread) and TMEM owner: T = Q E (hi + lo),
-//               S(t+1) = Q K^T while the softmax works on tile t, then
-//               O += P V with P read from TMEM; completions are tracked with
-//               tcgen05.commit.
-// TMEM (512 columns): S0 [0,128), S1 [128,256) (P over them), O [256,384),
-// T [384,448) at start, then the per-row counts of contextual tiles [384,512).
-// Every mbarrier wait is bounded; on expiry the CTA raises CS_ST_TIMEOUT,
-// drains its copies and MMAs, frees its TMEM and returns.
+//   warps 0-7   softmax, one thread per S row (TMEM lane r of its tile's
+//               columns): warps 0-3 tile a, 4-7 tile b.  Per key tile: gates
+//               sigmoid(q.k / sqrt(d)), the reverse cumulative count of
+//               position.py:295-307 (restarted at chunk boundaries in the
+//               chunk-reset mode), the q.E bias interpolated from a per-row
+//               table in shared memory, causal / association masks, the tile
+//               max, then P = 2^(s - m) packed to 16-bit pairs back into TMEM
+//               over the tile's own S columns.  Once a row's count is >=
+//               npos-1 all older keys share one bias: only logit, max and
+//               exponential remain (saturated tiles, one pass).
+//   warps 8-11  producer: both Q tiles, the E table split into bf16 hi + lo,
+//               the key metadata of every key tile (fixed keys, chunk
+//               boundaries), and the K tile (one stage) and V tiles (two
+//               stages) read through the per-key slot table: TMA 64 x 16 tile
+//               loads for runs of 16 keys in consecutive rows, tile::gather4
+//               for groups of 4 keys, cp.async for the rest, all into the
+//               128-byte swizzled UMMA layout.
+//   warp 12     MMA issuer (one thread) and TMEM owner: T = Q E (hi + lo) of
+//               both tiles, then per key tile QK(a), QK(b), PV(a) once P(a)
+//               is ready, QK(a) of the next key tile, PV(b), QK(b) of the
+//               next; completions are tracked with tcgen05.commit.
+// TMEM (512 columns): S(a) [0,128), S(b) [128,256) (P over their first 64
+// columns; T = Q E over the same 64 columns at start), O(a) [256,384), O(b)
+// [384,512).  Every mbarrier wait is bounded; on expiry the CTA raises
+// CS_ST_TIMEOUT, drains its copies and MMAs, frees its TMEM and returns.
 #include <cuda.h>
 #include <math.h>
 
@@ -47,57 +48,55 @@ int validate_attn_params(const cs_attn_params* p);
 namespace {
 
 constexpr int kThreads = 416;  // 8 softmax + 4 producer + 1 MMA warps
+// registers a thread: at launch (13 warps, four on one SM sub-partition:
+// 128), then after the split the producer warpgroup gives 64 of them back
+// and the two softmax warpgroups take 32 more each; the MMA warp keeps 128
+constexpr int kLaunchRegs = 128, kSoftRegs = 160, kProdRegs = 64;
+static_assert(256 * kSoftRegs + 128 * kProdRegs + 32 * kLaunchRegs <= kThreads * kLaunchRegs,
+              "register split exceeds the CTA's launch allocation");
 constexpr int kTileN = 128;  // keys per tile
 constexpr int kD = 128;      // head dim of this kernel
 constexpr int kMaxNpos = 64;
 
-// shared memory map (bytes from the 1024-aligned dynamic base)
-constexpr uint32_t kQ = 0;         // 32 KB  Q tile   [2 cb][128 rows][128 B]
-constexpr uint32_t kK0 = 32768;    // 2 x 32 KB K tiles
-constexpr uint32_t kV0 = 98304;    // 2 x 32 KB V tiles
-constexpr uint32_t kP = 163840;    // 32 KB  E hi/lo staging for T = Q E at start
-constexpr uint32_t kTab = 163840;  // 64 KB  q.E table [128 rows][64] float2, after T is built
-constexpr uint32_t kMeta = 229376; // barriers, flags, key metadata, pair exchange
+// Two query tiles per CTA ("a" = 0, "b" = 1), 128 S rows each, one softmax
+// thread per row.  Shared memory map (bytes from the 1024-aligned base):
+constexpr uint32_t kQ = 0;          // 2 x 32 KB Q tiles   [tile][2 cb][128 rows][128 B]
+constexpr uint32_t kK0 = 65536;     // 32 KB  K tile (one stage: freed when both QKs are done)
+constexpr uint32_t kV0 = 98304;     // 2 x 32 KB V tiles
+constexpr uint32_t kP = 163840;     // 32 KB  E hi/lo staging for T = Q E at start
+constexpr uint32_t kTab = 163840;   // 2 x 32 KB q.E tables [tile][128 rows][64] float, after T
+constexpr uint32_t kMeta = 229376;  // barriers, flags, key metadata
 
 // metadata block (offsets from kMeta)
-constexpr uint32_t kBarQ = 0;       // producer -> MMA: Q + E staged
-constexpr uint32_t kBarT = 8;       // MMA -> softmax: T ready
-constexpr uint32_t kBarK = 16;      // [2] producer -> MMA: K tile
-constexpr uint32_t kBarV = 32;      // [2] producer -> MMA: V tile
-constexpr uint32_t kBarS = 48;      // [2] MMA -> softmax/producer: S tile ready
-// offset 64: unused
-constexpr uint32_t kBarPV = 72;     // [2] MMA -> all: PV tile done
-constexpr uint32_t kBarEnd = 88;    // MMA drain
-constexpr uint32_t kTmemSlot = 96;  // TMEM base address
-constexpr uint32_t kAbort = 100;    // abort flag
-constexpr uint32_t kFixMask = 112;  // [4 slots][4 words] key is fixed
-constexpr uint32_t kBndMask = 176;  // [4 slots][4 words] key is the last of its chunk
-constexpr uint32_t kBarMeta = 240;  // [4] producer -> softmax: key metadata of slot it % 4
-constexpr uint32_t kXc = 272;       // [128] float: newer half -> older half count, and back
-constexpr uint32_t kXm = 784;       // [128] float: newer half's tile max / row sums
-constexpr uint32_t kXm2 = 1296;     // [128] float: older half's tile max
-constexpr uint32_t kBndKc = 1808;   // [4 slots][4 chunks] int: chunk id of the newest boundary
-// [2] softmax -> MMA: P of tile it in TMEM, barrier it % 2.  The four warp
-// pairs do not wait for one another, so one pair may finish tile it+1 before
-// another finishes tile it (never further: S(it+2) needs PV(it)); alternating
-// barriers keep those arrivals out of tile it's count.
-constexpr uint32_t kBarP = 1872;
-constexpr uint32_t kRedN = kBarP + 16;  // [4] int64: per-warp key needs of the tile's rows
-constexpr uint32_t kMetaBytes = kRedN + 32;
-constexpr uint32_t kSmemBytes = kMeta + kMetaBytes;  // 231,296 B (limit 232,448)
+constexpr uint32_t kBarQ = 0;       // producer + softmax -> MMA: Q tiles + E staged
+constexpr uint32_t kBarT = 8;       // MMA -> softmax: both T = Q E done
+// A tcgen05.commit tracks the MMAs issued since the thread's previous
+// commit, so every barrier below is committed right after the MMAs it stands
+// for, and a consumer of several MMA groups waits on each group's barrier.
+constexpr uint32_t kBarK = 16;      // producer -> MMA: K tile
+constexpr uint32_t kBarV = 32;      // [2 stages] producer -> MMA: V tile
+constexpr uint32_t kBarS = 48;      // [2 tiles] MMA -> softmax / producer: QK done
+constexpr uint32_t kBarP = 64;      // [2 tiles] softmax -> MMA: P in TMEM (128 arrivals)
+constexpr uint32_t kBarTab = 80;    // [2 tiles] softmax -> MMA: table read, S columns free
+constexpr uint32_t kBarPV = 96;     // [2 tiles][2 V stages] MMA -> softmax / producer: PV done
+constexpr uint32_t kBarEnd = 128;   // MMA drain
+constexpr uint32_t kBarMeta = 136;  // [4] producer -> softmax: key metadata of slot it % 4
+constexpr uint32_t kTmemSlot = 168; // TMEM base address
+constexpr uint32_t kAbort = 172;    // abort flag
+constexpr uint32_t kFixMask = 176;  // [4 slots][4 words] key is fixed
+constexpr uint32_t kBndMask = 240;  // [4 slots][4 words] key is the last of its chunk
+constexpr uint32_t kBndKc = 304;    // [4 slots][4 chunks] int: chunk id of the newest boundary
+constexpr uint32_t kRedN = 368;     // [8] int64: per-warp key needs of the CTA's rows
+constexpr uint32_t kMetaBytes = kRedN + 64;
+constexpr uint32_t kSmemBytes = kMeta + kMetaBytes;  // 229,808 B (limit 232,448)
 
-// TMEM columns: S double buffer, O, the q.E table (read once into shared
-// memory) and, from then on, the per-row counts of a contextual tile (kColR
-// overlays kColT)
-constexpr uint32_t kColS0 = 0, kColO = 256, kColT = 384, kColR = 384;
+// TMEM columns: S of each tile (P packed over its first 64 columns), O of
+// each tile; T = Q E lands in the first 64 S columns of its tile at start
+constexpr uint32_t kColS = 0, kColO = 256;  // + 128 * tile
 __device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
 }
-// named barriers: id 1 = the 128 producer threads, 2..5 = softmax warp pairs,
-// 6..9 = count handoff within a pair
-__device__ __forceinline__ void named_sync(uint32_t id, uint32_t count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
+// named barrier 1: the 128 producer threads
 // tile::gather4: rows r0..r3 of a 2-D tensor map, 64 elements from column x,
 // into 4 consecutive 128-byte rows at dst (the map's 128-byte swizzle applies)
 __device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* map, int x, int r0,
@@ -121,9 +120,6 @@ __device__ __forceinline__ void tma_tile2d(uint32_t dst, const CUtensorMap* map,
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes)
                : "memory");
-}
-__device__ __forceinline__ void named_arrive(uint32_t id, uint32_t count) {
-  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 // barrier that also ANDs a flag over its participants: every participant
 // leaves with the same answer, so exits from loops stay collective and no
@@ -180,7 +176,7 @@ struct Args {
   cs_attn_params p;
   PagedView pv;
   int G, R, fmt;  // heads per KV head, rows per tile, 0 = f16 / 1 = bf16
-  int tiles_per_head;
+  int pairs_per_head;  // query-tile pairs (one CTA each) per KV head
   int bs_shift;   // log2(block size) when it is a power of two, else -1
   int tma;        // 1: K/V tiles by TMA gather4 (per-row cp.async otherwise)
   int vx0;        // first V element of a primary V map row
@@ -298,8 +294,42 @@ __device__ __forceinline__ void stage_e_split(uint8_t* smem, const cs_attn_param
   }
 }
 
+// Requests of one batched launch (cs_cope_attn_prefill_batch): same head
+// layout and dtype, each with its own inputs, positions, slots and maps.
+constexpr int kMaxPrefillBatch = 8;
+struct BatchArgs {
+  Args r[kMaxPrefillBatch];
+  int count, hkv, max_pairs;
+};
+static_assert(sizeof(BatchArgs) <= 32000, "batched prefill arguments exceed the parameter space");
+
+// one CTA: query-tile pair `pair` of KV head g of request a
+template <typename T>
+__device__ __forceinline__ void prefill_cta(const Args& a, int g, int pair);
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_constant__ Args a) {
+  // the heaviest (latest) pairs of all KV heads are launched first, so the
+  // light ones fill the tail of the grid
+  prefill_cta<T>(a, blockIdx.x % a.p.hkv, a.pairs_per_head - 1 - blockIdx.x / a.p.hkv);
+}
+
+// all requests of a step in one grid, heaviest pairs of every request first
+// (pair rank j from the top, then request, then KV head); a request with
+// fewer pairs leaves its CTAs of the lowest ranks empty
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    cope_prefill_sm100_batch(const __grid_constant__ BatchArgs b) {
+  const int per_rank = b.count * b.hkv;
+  const int j = blockIdx.x / per_rank, ri = (blockIdx.x / b.hkv) % b.count;
+  const Args& a = b.r[ri];
+  const int pair = a.pairs_per_head - 1 - j;
+  if (pair < 0) return;
+  prefill_cta<T>(a, blockIdx.x % b.hkv, pair);
+}
+
+template <typename T>
+__device__ __forceinline__ void prefill_cta(const Args& a, const int g, const int pair) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
   const cs_attn_params& p = a.p;
@@ -312,32 +342,32 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
   volatile int* abort = reinterpret_cast<volatile int*>(meta + kAbort);
   const uint32_t mb = sbase + kMeta;
 
-  // tile coordinates: the heaviest (latest) query tiles of all KV heads are
-  // launched first, so the light tiles fill the tail of the grid
-  const int g = blockIdx.x % a.p.hkv;
-  const int tile = a.tiles_per_head - 1 - blockIdx.x / a.p.hkv;
-  const int64_t i0 = (int64_t)tile * a.R;
+  // the CTA's two query tiles: query rows i0 .. i0 + 2R - 1 of KV head g (R
+  // rows x G heads per tile)
   const int G = a.G, R = a.R;
+  const int64_t i0 = (int64_t)pair * 2 * R;
   const float top = (float)(p.npos - 1);
 
   if (tid == 0) {
     mbar_init(mb + kBarQ, 384);  // Q copies (producer) + E split (producer and softmax)
     mbar_init(mb + kBarT, 1);
+    mbar_init(mb + kBarK, 128);  // one copy-completion arrival per producer thread
     for (int s = 0; s < 2; ++s) {
-      mbar_init(mb + kBarK + 8 * s, 128);  // one copy-completion arrival per producer thread
       mbar_init(mb + kBarV + 8 * s, 128);
       mbar_init(mb + kBarS + 8 * s, 1);
-      mbar_init(mb + kBarPV + 8 * s, 1);
+      mbar_init(mb + kBarP + 8 * s, 128);  // the 128 rows of the tile
+      mbar_init(mb + kBarTab + 8 * s, 128);
+      mbar_init(mb + kBarPV + 16 * s, 1);
+      mbar_init(mb + kBarPV + 16 * s + 8, 1);
     }
     for (int s = 0; s < 4; ++s) mbar_init(mb + kBarMeta + 8 * s, 128);
-    for (int s = 0; s < 2; ++s) mbar_init(mb + kBarP + 8 * s, 256);  // both halves of every row
     mbar_init(mb + kBarEnd, 1);
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp < 4) {  // keys needed by the furthest row of this tile: one row per thread
+  if (warp < 8) {  // keys needed by the furthest row of the two tiles: one row per thread
     int64_t n = 0;
-    if (tid < R && i0 + tid < p.nq) {
+    if (tid < 2 * R && i0 + tid < p.nq) {
       const int64_t qp = p.qpos[i0 + tid];
       n = qp + 1 < p.nk ? qp + 1 : p.nk;
     }
@@ -348,27 +378,37 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
     }
     if (lane == 0) reinterpret_cast<int64_t*>(meta + kRedN)[warp] = n;
   }
-  // the Q tile and the E table need nothing from the set-up above: their
+  // the Q tiles and the E table need nothing from the set-up above: their
   // copies start before the first barrier (the arrivals on kBarQ come after
   // it, once the barrier is initialised)
   if (warp >= 8 && warp < 12) {
-    // Q: row r = head-local * R + row-local; lane l of warp w resolves row
-    // 32(w-8) + l, then the warp copies its 32 rows two at a time (16 lanes x
-    // 16 bytes per 256-byte row)
+    // Q: S row r of tile qt = query row i0 + qt R + r / G, head g G + r % G
+    // (the G heads of a query row are adjacent, so a warp's 32 rows span
+    // 32 / G query positions: the rows of a warp saturate their counts at
+    // nearby keys); lane l of warp w resolves rows 32(w-8) + l of both
+    // tiles, then the warp copies its 2 x 32 rows two at a time (16 lanes x
+    // 16 bytes per row)
     const int pt = tid - 256;
-    const int64_t i = i0 + (pt % R);
-    const int h = g * G + pt / R;
-    const char* qrow = i < p.nq ? static_cast<const char*>(p.q) +
-                                      (i * p.q_stride_tok + (int64_t)h * p.q_stride_head) *
-                                          (int64_t)sizeof(T)
-                                : nullptr;
+    const char* qrow[2];
 #pragma unroll
-    for (int it = 0; it < 16; ++it) {
-      const int rl = 2 * it + (lane >> 4), c16 = lane & 15;
-      const char* src = reinterpret_cast<const char*>(
-          __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(qrow), rl));
-      cp_async16(sbase + kQ + sw128((warp - 8) * 32 + rl, c16, 128),
-                 src ? src + c16 * 16 : static_cast<const char*>(p.q), src != nullptr);
+    for (int qt = 0; qt < 2; ++qt) {
+      const int64_t i = i0 + qt * R + pt / G;
+      const int h = g * G + pt % G;
+      qrow[qt] = i < p.nq ? static_cast<const char*>(p.q) +
+                                (i * p.q_stride_tok + (int64_t)h * p.q_stride_head) *
+                                    (int64_t)sizeof(T)
+                          : nullptr;
+    }
+#pragma unroll
+    for (int qt = 0; qt < 2; ++qt) {
+#pragma unroll
+      for (int it = 0; it < 16; ++it) {
+        const int rl = 2 * it + (lane >> 4), c16 = lane & 15;
+        const char* src = reinterpret_cast<const char*>(
+            __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(qrow[qt]), rl));
+        cp_async16(sbase + kQ + qt * 32768 + sw128((warp - 8) * 32 + rl, c16, 128),
+                   src ? src + c16 * 16 : static_cast<const char*>(p.q), src != nullptr);
+      }
     }
   }
   if (warp < 12) stage_e_split<T>(smem, p, tid);
@@ -383,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(meta + kTmemSlot);
   int64_t nneed = 0;
-  for (int w = 0; w < 4; ++w) {
+  for (int w = 0; w < 8; ++w) {
     const int64_t n = reinterpret_cast<const volatile int64_t*>(meta + kRedN)[w];
     nneed = n > nneed ? n : nneed;
   }
@@ -391,6 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
 
   if (warp >= 8 && warp < 12) {
     // ================================================================ producer
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProdRegs));
     const int pt = tid - 256;  // 0..127
     cp_async_wait_all();
     fence_async_smem();
@@ -427,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
     };
     // publish the key metadata of tile it2 (slot it2 % 4) and start its K copy
     auto issue_k = [&](int it2, VSrc& vs) {
-      const int st = it2 & 1, slot = it2 & 3;
+      const int slot = it2 & 3;
       const int64_t key0 = (int64_t)(ntile - 1 - it2) * kTileN;
       {
         const unsigned fm = __ballot_sync(kAll, fixed);
@@ -446,6 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
       vs.rv = rv;
       vs.grp = vs.run = 0;
       vs.tx = 0;
+      const uint32_t kdst = sbase + kK0;
       if (tma) {
         // 16 keys (a half warp) in consecutive rows of one map are one 64 x 16
         // tile load per operand and 64-column half (run 1: primary map, 2:
@@ -471,24 +513,22 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
         vs.v1 = __shfl_down_sync(kAll, rv, 1);
         vs.v2 = __shfl_down_sync(kAll, rv, 2);
         vs.v3 = __shfl_down_sync(kAll, rv, 3);
-        if (lane == 0 && vs.tx) mbar_expect_tx(mb + kBarK + 8 * st, vs.tx);
+        if (lane == 0 && vs.tx) mbar_expect_tx(mb + kBarK, vs.tx);
         if (vs.run && (lane & 15) == 0) {
           const CUtensorMap* m = vs.run == 1 ? &a.tm[4] : &a.tm[6];
           for (int cb = 0; cb < 2; ++cb)
-            tma_tile2d(sbase + kK0 + st * 32768 + cb * 16384 + pt * 128, m, cb * 64, rk,
-                       mb + kBarK + 8 * st);
+            tma_tile2d(kdst + cb * 16384 + pt * 128, m, cb * 64, rk, mb + kBarK);
         }
         if (vs.grp && (lane & 3) == 0) {
           const CUtensorMap* m = vs.grp == 1 ? &a.tm[0] : &a.tm[2];
           for (int cb = 0; cb < 2; ++cb)
-            tma_gather4(sbase + kK0 + st * 32768 + cb * 16384 + pt * 128, m, cb * 64, rk, k1, k2,
-                        k3, mb + kBarK + 8 * st);
+            tma_gather4(kdst + cb * 16384 + pt * 128, m, cb * 64, rk, k1, k2, k3, mb + kBarK);
         }
         if (!vs.run && !vs.grp) {
           for (int c16 = 0; c16 < 16; ++c16) {
             const char* src = ka ? reinterpret_cast<const char*>(ka & ~1ull) + c16 * 16
                                  : static_cast<const char*>(p.q);
-            cp_async16(sbase + kK0 + st * 32768 + sw128(pt, c16, 128), src, ka != 0);
+            cp_async16(kdst + sw128(pt, c16, 128), src, ka != 0);
           }
         }
       } else {
@@ -501,10 +541,10 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
           const uint64_t ra = __shfl_sync(kAll, ka, src_lane);
           const char* src = ra ? reinterpret_cast<const char*>(ra & ~1ull) + c16 * 16
                                : static_cast<const char*>(p.q);
-          cp_async16(sbase + kK0 + st * 32768 + sw128(wrow0 + src_lane, c16, 128), src, ra != 0);
+          cp_async16(kdst + sw128(wrow0 + src_lane, c16, 128), src, ra != 0);
         }
       }
-      cp_async_arrive_noinc(mb + kBarK + 8 * st);
+      cp_async_arrive_noinc(mb + kBarK);
     };
     auto issue_v = [&](int it2, const VSrc& vs) {
       const int st = it2 & 1;
@@ -546,28 +586,27 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
       }
       cp_async_arrive_noinc(mb + kBarV + 8 * st);
     };
-    // K runs one tile ahead of V: K(it+1) needs only QK(it-1) to be done,
-    // V(it) needs PV(it-2)
-    VSrc vcur{}, vnext{};
+    // K has one stage, free once both tiles' QK of key tile it are done.  V
+    // has two: stage (it+1)&1 held V(it-1), free once both PVs of tile it-1
+    // are done; the PV barriers are per tile and V stage, so their next
+    // phase needs the V copy issued here and cannot be missed.
+    VSrc vs{};
     if (ntile > 0) {
       load_key(0);
-      issue_k(0, vcur);
+      issue_k(0, vs);
+      issue_v(0, vs);
       if (ntile > 1) load_key(1);
     }
-    for (int it = 0; it < ntile; ++it) {
-      if (it + 1 < ntile) {
-        // K stage (it+1)&1 and metadata slot (it+1)%4 are free once QK(it-1)
-        // completed; the barrier also keeps the producer warps in step
-        bool ok = it < 1 || mbar_wait(mb + kBarS + 8 * ((it + 1) & 1), ((it - 1) >> 1) & 1, abort);
-        if (!named_and(1, 128, ok)) break;
-        issue_k(it + 1, vnext);
-        if (it + 2 < ntile) load_key(it + 2);
-      }
-      // V stage it&1 free once PV(it-2) completed
-      bool ok = it < 2 || mbar_wait(mb + kBarPV + 8 * (it & 1), ((it - 2) >> 1) & 1, abort);
+    for (int it = 0; it + 1 < ntile; ++it) {
+      bool ok = mbar_wait(mb + kBarS, it & 1, abort) && mbar_wait(mb + kBarS + 8, it & 1, abort);
       if (!named_and(1, 128, ok)) break;
-      issue_v(it, vcur);
-      vcur = vnext;
+      issue_k(it + 1, vs);
+      const uint32_t pst = 8 * ((it + 1) & 1), pph = ((it - 1) >> 1) & 1;
+      ok = it < 1 || (mbar_wait(mb + kBarPV + pst, pph, abort) &&
+                      mbar_wait(mb + kBarPV + 16 + pst, pph, abort));
+      if (!named_and(1, 128, ok)) break;
+      issue_v(it + 1, vs);
+      if (it + 2 < ntile) load_key(it + 2);
     }
     if (slot_bad) report(p.status, CS_ST_SLOT_RANGE);
     cp_async_wait_all();
@@ -580,81 +619,93 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
       bool ok = mbar_wait(mb + kBarQ, 0, abort);
       if (ok) {
         tc_fence_after();
-        for (int half = 0; half < 2; ++half) {
-          for (int kk = 0; kk < kD / 16; ++kk) {
-            const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
-            const uint32_t boff = half * 16384 + (kk >> 2) * 8192 + (kk & 3) * 32;
-            tc_mma(tmem + kColT, umma_desc(sbase + kQ + aoff, 16, 1024),
-                   umma_desc(sbase + kP + boff, 16, 1024), id_t, (half | kk) ? 1u : 0u);
+        for (int qt = 0; qt < 2; ++qt) {
+          for (int half = 0; half < 2; ++half) {
+            for (int kk = 0; kk < kD / 16; ++kk) {
+              const uint32_t aoff = qt * 32768 + (kk >> 2) * 16384 + (kk & 3) * 32;
+              const uint32_t boff = half * 16384 + (kk >> 2) * 8192 + (kk & 3) * 32;
+              tc_mma(tmem + kColS + 128 * qt, umma_desc(sbase + kQ + aoff, 16, 1024),
+                     umma_desc(sbase + kP + boff, 16, 1024), id_t, (half | kk) ? 1u : 0u);
+            }
           }
         }
         tc_commit(mb + kBarT);
       }
-      auto issue_qk = [&](int it) {
-        const int st = it & 1;
+      auto issue_qk = [&](int qt) {
         for (int kk = 0; kk < kD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          tc_mma(tmem + kColS0 + st * 128, umma_desc(sbase + kQ + off, 16, 1024),
-                 umma_desc(sbase + kK0 + st * 32768 + off, 16, 1024), id_s, kk ? 1u : 0u);
+          tc_mma(tmem + kColS + 128 * qt, umma_desc(sbase + kQ + qt * 32768 + off, 16, 1024),
+                 umma_desc(sbase + kK0 + off, 16, 1024), id_s, kk ? 1u : 0u);
         }
-        tc_commit(mb + kBarS + 8 * st);
+        tc_commit(mb + kBarS + 8 * qt);
       };
       if (ok && ntile > 0) {
         ok = mbar_wait(mb + kBarK, 0, abort);
-        if (ok) {
+        for (int qt = 0; ok && qt < 2; ++qt) {
+          // the tile's S columns hold T until its softmax has read the table
+          if (!(ok = mbar_wait(mb + kBarTab + 8 * qt, 0, abort))) break;
           fence_async_smem();
           tc_fence_after();
-          issue_qk(0);
+          issue_qk(qt);
         }
       }
+      int lastpv[2] = {-1, -1};  // last key tile whose PV was issued, per tile
       for (int it = 0; ok && it < ntile; ++it) {
         const int st = it & 1;
-        if (it + 1 < ntile) {
-          if (!(ok = mbar_wait(mb + kBarK + 8 * ((it + 1) & 1), ((it + 1) >> 1) & 1, abort)))
-            break;
-          // S(it+1) overwrites the TMEM columns where P(it-1) lives: PV(it-1)
-          // (another accumulator, so not ordered with this MMA) must be done
-          if (it >= 1 &&
-              !(ok = mbar_wait(mb + kBarPV + 8 * ((it - 1) & 1), ((it - 1) >> 1) & 1, abort)))
-            break;
+        for (int qt = 0; ok && qt < 2; ++qt) {
+          if (!(ok = mbar_wait(mb + kBarP + 8 * qt, it & 1, abort))) break;
+          if (!(ok = mbar_wait(mb + kBarV + 8 * st, (it >> 1) & 1, abort))) break;
           fence_async_smem();
           tc_fence_after();
-          issue_qk(it + 1);
+          for (int kk = 0; kk < kTileN / 16; ++kk) {
+            // P of keys 16kk..16kk+15 (packed pairs over the tile's S columns)
+            const uint32_t pcol = kColS + 128 * qt + kk * 8;
+            const uint32_t boff = kk * 2048;  // V: MN-major
+            tc_mma_ts(tmem + kColO + 128 * qt, tmem + pcol,
+                      umma_desc(sbase + kV0 + st * 32768 + boff, 16384, 1024), id_o,
+                      (it | kk) ? 1u : 0u);
+          }
+          tc_commit(mb + kBarPV + 16 * qt + 8 * st);
+          lastpv[qt] = it;
+          if (it + 1 < ntile) {
+            // S(it+1) of this tile overwrites the TMEM columns where P(it)
+            // lives: PV(it) must be done
+            if (!(ok = mbar_wait(mb + kBarPV + 16 * qt + 8 * st, (it >> 1) & 1, abort))) break;
+            if (qt == 0 && !(ok = mbar_wait(mb + kBarK, (it + 1) & 1, abort))) break;
+            fence_async_smem();
+            tc_fence_after();
+            issue_qk(qt);
+          }
         }
-        if (!(ok = mbar_wait(mb + kBarP + 8 * (it & 1), (it >> 1) & 1, abort))) break;
-        if (!(ok = mbar_wait(mb + kBarV + 8 * st, (it >> 1) & 1, abort))) break;
-        fence_async_smem();
-        tc_fence_after();
-        for (int kk = 0; kk < kTileN / 16; ++kk) {
-          // P of keys 16kk..16kk+15 (packed pairs, over the S columns of tile it)
-          const uint32_t pcol = kColS0 + st * 128 + (kk < 4 ? kk * 8 : 64 + (kk - 4) * 8);
-          const uint32_t boff = kk * 2048;  // V: MN-major
-          tc_mma_ts(tmem + kColO, tmem + pcol,
-                    umma_desc(sbase + kV0 + st * 32768 + boff, 16384, 1024), id_o,
-                    (it | kk) ? 1u : 0u);
-        }
-        tc_commit(mb + kBarPV + 8 * st);
       }
-      // drain every MMA issued by this thread before TMEM is released
+      // drain before TMEM is released: the last PVs (and a commit of
+      // anything still uncommitted after an early exit)
       tc_commit(mb + kBarEnd);
       long long t0 = clock64();
       while (!mbar_try(mb + kBarEnd, 0) && clock64() - t0 < kWaitCycles) {
+      }
+      for (int qt = 0; qt < 2; ++qt) {
+        const int last = lastpv[qt];
+        if (last < 0) continue;
+        const uint32_t bar = mb + kBarPV + 16 * qt + 8 * (last & 1);
+        t0 = clock64();
+        while (!mbar_try(bar, (last >> 1) & 1) && clock64() - t0 < kWaitCycles) {
+        }
       }
     }
     __syncwarp();
   } else {
     // ================================================================ softmax
-    // Two threads per S row: warp q (0-3) takes the newer half of every key
-    // tile (columns 64-127), warp q+4 the older half (0-63).  Both address
-    // TMEM lanes 32q..32q+31 (a warp reaches only its own lane quarter).  The
-    // pair exchanges the running count and the tile maximum through shared
-    // memory; every exit from the tile loop is agreed with a reducing
-    // barrier so neither warp of a pair is left waiting.
-    const int q4 = warp & 3, hf = warp >> 2;  // hf 0: newer half, 1: older half
-    const uint32_t pair = 2 + q4;
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftRegs));
+    // One thread per S row: warps 0-3 hold tile a, warps 4-7 tile b; warp w
+    // addresses TMEM lanes 32(w%4)..32(w%4)+31 of its tile's columns.  A row
+    // is never shared, so no barrier joins the softmax warps: every wait
+    // result is made warp-uniform (the TMEM loads are warp-collective) and
+    // the loop exits on any expired wait.
+    const int qt = warp >> 2, q4 = warp & 3;
     const int r = q4 * 32 + lane;  // TMEM lane == tile row
-    const int64_t i = i0 + (r % R);
-    const int h = g * G + r / R;
+    const int64_t i = i0 + qt * R + r / G;
+    const int h = g * G + r % G;
     const bool row_ok = i < p.nq;
     const int64_t qp = row_ok ? p.qpos[i] : -1;
     const int64_t nlim = row_ok ? (qp + 1 < p.nk ? qp + 1 : p.nk) : 0;
@@ -665,72 +716,85 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
         (row_ok && chunked) ? p.chunk_off + (int64_t)h * p.co_stride_h + i * p.co_stride_q
                             : nullptr;
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
-    // q.E table of row r: entry p = (T[p], T[p+1] - T[p]) in the log2 domain
-    // (T[npos] := T[npos-1]), at float2 index p ^ (r & 15) so that the 16
-    // rows of a half warp reading the same entry hit distinct banks
-    float2* Tab = reinterpret_cast<float2*>(smem + kTab) + r * kMaxNpos;
-    const int tsw = r & 15;
-    float* xc = reinterpret_cast<float*>(meta + kXc);
-    float* xm = reinterpret_cast<float*>(meta + kXm);
+    const uint32_t sc = tmem + lane_base + kColS + 128 * qt;  // this row's S columns
+    const uint32_t oc = tmem + lane_base + kColO + 128 * qt;  // this row's O columns
+    // q.E table of row r: T[p] (log2 domain) at float index p ^ (r & 31), so
+    // that the 32 rows of a warp reading the same entry hit distinct banks;
+    // a row's table is written and read by its own thread only
+    float* Tab = reinterpret_cast<float*>(smem + kTab + qt * 32768) + r * kMaxNpos;
+    const int tsw = r & 31;
     const float inv_sqrt_d = (float)(1.0 / p.scale);
     const float LOG2E = 1.4426950408889634f;
     const float scale2 = inv_sqrt_d * LOG2E;
     const float half_scale = 0.5f * inv_sqrt_d;
-    const int cc_hi = hf ? 1 : 3;  // this half's 32-column chunks: cc_hi, cc_hi - 1
 
     fence_async_smem();  // this thread's share of the E table (staged before the barrier)
     mbar_arrive(mb + kBarQ);
-    bool ok = mbar_wait(mb + kBarT, 0, abort);
+    bool ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarT, 0, abort));
     tc_fence_after();
     {
-      // this half builds entries hf*32 .. hf*32+31 (the newer half also
-      // needs T[32]); the E staging below the table is no longer read
-      uint32_t v[32], nx[1] = {0u};
-      CS_TMEM_LD32(tmem + lane_base + kColT + hf * 32, v);
-      if (hf == 0) CS_TMEM_LD1(tmem + lane_base + kColT + 32, nx);
-      tmem_wait_ld();
+      uint32_t v[32];
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const int pp = hf * 32 + c;
-        const float t0 = __uint_as_float(v[c]) * LOG2E;
-        const float tn = __uint_as_float(c < 31 ? v[c + 1] : (hf == 0 ? nx[0] : v[31])) * LOG2E;
-        Tab[pp ^ tsw] = make_float2(t0, pp + 1 < p.npos ? tn - t0 : 0.f);
+      for (int hb = 0; hb < 2; ++hb) {
+        CS_TMEM_LD32(sc + 32 * hb, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) Tab[(32 * hb + c) ^ tsw] = __uint_as_float(v[c]) * LOG2E;
       }
     }
-    ok = named_and(pair, 64, ok);  // both halves of the q.E table written
-    const float tsat2 = Tab[(p.npos - 1) ^ tsw].x;  // saturated bias (log2 domain)
+    tc_fence_before();
+    mbar_arrive(mb + kBarTab + 8 * qt);  // the S columns are free for QK
+    const float tsat2 = Tab[(p.npos - 1) ^ tsw];  // saturated bias (log2 domain)
+    // interpolated bias at position pos in [0, npos - 1] (position.py:339-344)
+    auto bias_at = [&](float pos) {
+      int lo;
+      const float fl = floor_pos(pos, lo);
+      const int hi = lo + 1 < p.npos ? lo + 1 : p.npos - 1;
+      const float t0 = Tab[lo ^ tsw];
+      return fmaf(pos - fl, Tab[hi ^ tsw] - t0, t0);
+    };
 
     float carry = 0.f;       // running count entering the newer edge of the tile
     float mref = -INFINITY;  // softmax reference max (log2 domain)
-    float lsum = 0.f;        // this half's share of the row sum
-    float* xm2 = reinterpret_cast<float*>(meta + kXm2);
-    const int* bndkc_all = reinterpret_cast<const int*>(meta + kBndKc);
+    float lsum = 0.f;        // the row sum
     // count restart at the chunk boundary ending at key j, or -1 for none
     auto restart_at = [&](int64_t j) -> float {
       const int kc = p.key_chunk[j];
       return kc < qchunk ? offrow[kc] : -1.f;
     };
+    // O row times f (after PV of the previous tile)
+    auto rescale_o = [&](float f) {
+#pragma unroll 1
+      for (int cc = 0; cc < 4; ++cc) {
+        uint32_t o[32];
+        CS_TMEM_LD32(oc + 32 * cc, o);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * f);
+        CS_TMEM_ST32(oc + 32 * cc, o);
+      }
+      tmem_wait_st();
+    };
     for (int it = 0; ok && it < ntile; ++it) {
-      const int st = it & 1, slot = it & 3;
+      const int slot = it & 3;
       const int kt = ntile - 1 - it;
       const int64_t key0 = (int64_t)kt * kTileN;
       // key metadata of slot it % 4: the producer publishes it ahead of S(it),
-      // and the slot is not reused before P(it) from these warps.  Masks,
-      // chunk restarts and the fast / contextual decision are settled here,
-      // while QK(it) may still be running, so their latency hides behind it.
+      // and the slot is not reused before P(it) of both tiles.  Masks, chunk
+      // restarts and the fast / contextual decision are settled while QK(it)
+      // may still be running, so their latency hides behind it.
       ok = mbar_wait(mb + kBarMeta + 8 * slot, (it >> 2) & 1, abort);
       const unsigned* fixm = reinterpret_cast<const unsigned*>(meta + kFixMask) + slot * 4;
       const unsigned* bndm = reinterpret_cast<const unsigned*>(meta + kBndMask) + slot * 4;
-      const int* bndkc = bndkc_all + slot * 4;
+      const int* bndkc = reinterpret_cast<const int*>(meta + kBndKc) + slot * 4;
       const int nvalid =
           (int)(nlim - key0 < 0 ? 0 : (nlim - key0 > kTileN ? kTileN : nlim - key0));
-      // columns of this half hidden from the row (bit c of chunk k): past the
-      // causal / key limit, or fixed keys seen by a selected row (its own key
-      // stays visible)
-      unsigned hide0, hide1;
+      // columns hidden from the row, bit c of word cc (key 32 cc + c): past
+      // the causal / key limit, or fixed keys seen by a selected row (its own
+      // key stays visible)
+      unsigned hide0, hide1, hide2, hide3;
 #pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const int cc = cc_hi - k;
+      for (int cc = 0; cc < 4; ++cc) {
         const int lim = nvalid - cc * 32;
         unsigned m = lim >= 32 ? 0u : (lim <= 0 ? ~0u : (~0u << lim));
         if (qsel) {
@@ -739,100 +803,75 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
           if (self >= 0 && self < 32) fx &= ~(1u << (int)self);
           m |= fx;
         }
-        (k ? hide1 : hide0) = m;
+        (cc == 0 ? hide0 : cc == 1 ? hide1 : cc == 2 ? hide2 : hide3) = m;
       }
-      // count restart of the newest chunk boundary of each 32-key chunk (the
-      // producer publishes its chunk id); other boundaries are looked up
-      // where they are met
-      float roff0 = -1.f, roff1 = -1.f, roff2 = -1.f, roff3 = -1.f;
-      const bool anyb = chunked && ok && (bndm[0] | bndm[1] | bndm[2] | bndm[3]) != 0u;
-      if (anyb) {
-        const int k0 = bndkc[0], k1 = bndkc[1], k2 = bndkc[2], k3 = bndkc[3];
-        if (k0 >= 0 && k0 < qchunk) roff0 = offrow[k0];
-        if (k1 >= 0 && k1 < qchunk) roff1 = offrow[k1];
-        if (k2 >= 0 && k2 < qchunk) roff2 = offrow[k2];
-        if (k3 >= 0 && k3 < qchunk) roff3 = offrow[k3];
-      }
-      auto roff_of = [&](int cc) {
-        return cc == 0 ? roff0 : (cc == 1 ? roff1 : (cc == 2 ? roff2 : roff3));
+      // (selects, not an indexed array: the chunk loops below are not unrolled)
+      auto hide_of = [&](int cc) {
+        return cc == 0 ? hide0 : cc == 1 ? hide1 : cc == 2 ? hide2 : hide3;
       };
+      const bool anyb = chunked && ok && (bndm[0] | bndm[1] | bndm[2] | bndm[3]) != 0u;
       // the row is saturated for this tile when its count is already >= npos-1
       // and no live chunk boundary of the tile restarts it below that value
       bool sat = carry >= top;
       if (anyb && sat) {
 #pragma unroll 1
         for (int cc = 0; cc < 4 && sat; ++cc) {
-          const unsigned bd = bndm[cc];
           const int lim = nvalid - cc * 32;
-          unsigned bits = bd & (lim >= 32 ? ~0u : (lim <= 0 ? 0u : ((1u << lim) - 1u)));
-          const int cf = bd ? 31 - __clz(bd) : -1;
+          unsigned bits = bndm[cc] & (lim >= 32 ? ~0u : (lim <= 0 ? 0u : ((1u << lim) - 1u)));
           while (bits && sat) {
             const int c = 31 - __clz(bits);
             bits &= ~(1u << c);
-            const float off = c == cf ? roff_of(cc) : restart_at(key0 + cc * 32 + c);
+            const float off = restart_at(key0 + cc * 32 + c);
             if (off >= 0.f && off < top) sat = false;
           }
         }
       }
-      // same rows in both warps of the pair, so both take the same path
       const bool fast = __all_sync(0xffffffffu, sat || nvalid == 0);
-      // S(it) from the MMA warp
-      ok = ok && mbar_wait(mb + kBarS + 8 * st, (it >> 1) & 1, abort);
-      if (!(ok = named_and(pair, 64, ok))) break;
+      // S(it) of this tile from the MMA warp
+      ok = ok && mbar_wait(mb + kBarS + 8 * qt, it & 1, abort);
+      if (!(ok = __all_sync(0xffffffffu, ok))) break;
       tc_fence_after();
-      float tmax;
-      // warp-uniform, and pair-uniform (both warps hold the same rows and
-      // decide on row-level values only): a row that has not yet seen a
-      // visible key keeps its warp on the two-pass path, unless it sees none
-      // in this tile either (padding rows past nq, rows before their first key)
       if (fast && __all_sync(0xffffffffu, mref > -INFINITY || nvalid == 0)) {
-        // Saturated tile after the first: no separate max pass.  Every
-        // visible score is x = S * scale2 + tsat2 - mref; the exponentials use
-        // mref directly unless a chunk's own maximum cm exceeds the lazy-rescale
-        // limit (2^8), in which case that chunk is exponentiated relative to
-        // cm.  The pair then compares its largest x; if it passed the limit
-        // (rare) the reference moves to the tile maximum as in the two-pass
-        // path: O and the row sum are rescaled (after PV of the previous
-        // tile), and so are this tile's P chunks (2^(sh - trel)).
+        // Saturated tile after the first: one pass, chunk by chunk in
+        // increasing key order (P of chunk cc goes to S columns 16cc..16cc+15,
+        // already read).  Every visible score is x = S * scale2 + tsat2 -
+        // mref.  A chunk whose sum passes 2^8 (some x above the lazy-rescale
+        // limit; NaN counts too) is rare: it is redone against its own
+        // maximum cm (sh = cm), and after the four chunks the reference moves
+        // to the largest cm: O and the row sum are rescaled (after PV of the
+        // previous tile), and so is each chunk's P (2^(sh - trel)).
         carry = sat ? fmaxf(carry, top) : carry;
         const float fb = tsat2 - mref;
-        float pk[2] = {0.f, 0.f}, sh[2] = {0.f, 0.f};
-        float lm = -INFINITY;
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const int cc = (hf ? 0 : 2) + k;
-          const unsigned hm = (cc & 1) ? hide0 : hide1;
-          uint32_t v[32];
+        float pk = 0.f, trel = -INFINITY;
+        float sh0 = 0.f, sh1 = 0.f, sh2 = 0.f, sh3 = 0.f;  // per-chunk shifts (rare path)
+        // chunk cc of the row from v (its raw S, loaded): P into v[0..15],
+        // stored over S columns 16cc..16cc+15; returns the chunk's sum
+        auto one_chunk = [&](uint32_t(&v)[32], int cc) -> float {
+          const unsigned hm = hide_of(cc);
           if (__all_sync(0xffffffffu, hm == ~0u)) {
 #pragma unroll
             for (int c = 0; c < 32; ++c) v[c] = 0u;
+          } else if (__all_sync(0xffffffffu, hm == 0u)) {  // every column visible (common)
+#pragma unroll
+            for (int c = 0; c < 32; ++c)
+              v[c] = __float_as_uint(ex2(fmaf(__uint_as_float(v[c]), scale2, fb)));
           } else {
-            CS_TMEM_LD32(tmem + lane_base + kColS0 + st * 128 + cc * 32, v);
-            tmem_wait_ld();
-            // one pass: x and 2^x.  A chunk with an x above the limit (2^8)
-            // has a sum above 2^8, so only such chunks (rare) are checked
-            // exactly: S is still in TMEM until the P store below, so the
-            // chunk is reloaded, its maximum cm found and, if past the limit,
-            // the chunk redone relative to cm.
 #pragma unroll
             for (int c = 0; c < 32; ++c)
               v[c] = __float_as_uint(
                   (hm >> c) & 1u ? 0.f : ex2(fmaf(__uint_as_float(v[c]), scale2, fb)));
           }
-          uint32_t w[16];
           float s0 = 0.f, s1 = 0.f;
 #pragma unroll
           for (int u = 0; u < 16; ++u) {
-            const float e0 = __uint_as_float(v[2 * u]);
-            const float e1 = __uint_as_float(v[2 * u + 1]);
+            const float e0 = __uint_as_float(v[2 * u]), e1 = __uint_as_float(v[2 * u + 1]);
             s0 += e0;
             s1 += e1;
-            w[u] = Pack2<T>::pack(e0, e1);
+            v[u] = Pack2<T>::pack(e0, e1);  // in place: keys 2u, 2u+1 already read
           }
-          pk[k] = s0 + s1;
-          if (__any_sync(0xffffffffu, !(pk[k] <= 256.f))) {  // rare (NaN counts as suspicious)
-            const uint32_t saddr = tmem + lane_base + kColS0 + st * 128 + cc * 32;
-            CS_TMEM_LD32(saddr, v);
+          float pc = s0 + s1;
+          if (__any_sync(0xffffffffu, !(pc <= 256.f))) {  // rare; the whole warp redoes
+            CS_TMEM_LD32(sc + 32 * cc, v);
             tmem_wait_ld();
             float cm = -INFINITY;
 #pragma unroll
@@ -841,208 +880,178 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
               v[c] = __float_as_uint(x);
               cm = fmaxf(cm, x);
             }
-            lm = fmaxf(lm, cm);
-            sh[k] = cm > 8.f ? cm : 0.f;
+            const float shc = cm > 8.f ? cm : 0.f;
+            sh0 = cc == 0 ? shc : sh0;
+            sh1 = cc == 1 ? shc : sh1;
+            sh2 = cc == 2 ? shc : sh2;
+            sh3 = cc == 3 ? shc : sh3;
+            trel = fmaxf(trel, cm);
             float r0 = 0.f, r1 = 0.f;
 #pragma unroll
             for (int u = 0; u < 16; ++u) {
-              const float e0 = ex2(__uint_as_float(v[2 * u]) - sh[k]);
-              const float e1 = ex2(__uint_as_float(v[2 * u + 1]) - sh[k]);
+              const float e0 = ex2(__uint_as_float(v[2 * u]) - shc);
+              const float e1 = ex2(__uint_as_float(v[2 * u + 1]) - shc);
               r0 += e0;
               r1 += e1;
-              w[u] = Pack2<T>::pack(e0, e1);
+              v[u] = Pack2<T>::pack(e0, e1);
             }
-            pk[k] = r0 + r1;
+            pc = r0 + r1;
           }
-          CS_TMEM_ST16(tmem + lane_base + kColS0 + st * 128 + (cc < 2 ? cc * 16 : 64 + (cc - 2) * 16), w);
+          CS_TMEM_ST16(sc + 16 * cc, v);
+          return pc;
+        };
+        // two register buffers: the TMEM load of the next chunk is in flight
+        // while the current one is computed (a wait covers every earlier load
+        // of the thread, so it is placed after that computation)
+        uint32_t va[32], vb[32];
+        CS_TMEM_LD32(sc, va);
+        tmem_wait_ld();
+#pragma unroll 1
+        for (int cp = 0; cp < 2; ++cp) {
+          CS_TMEM_LD32(sc + 32 * (2 * cp + 1), vb);
+          pk += one_chunk(va, 2 * cp);
+          tmem_wait_ld();
+          if (cp == 0) CS_TMEM_LD32(sc + 64, va);
+          pk += one_chunk(vb, 2 * cp + 1);
+          if (cp == 0) tmem_wait_ld();
         }
-        (hf ? xm2 : xm)[r] = lm;
-        named_sync(pair, 64);
-        const float trel = fmaxf(xm[r], xm2[r]);
-        if (__any_sync(0xffffffffu, trel > 8.f)) {
+        if (__any_sync(0xffffffffu, trel > 8.f)) {  // rare: move the reference
           const bool mv = trel > 8.f;
           tmem_wait_st();
-          ok = mbar_wait(mb + kBarPV + 8 * ((it - 1) & 1), ((it - 1) >> 1) & 1, abort);
-          if (!(ok = named_and(pair, 64, ok))) break;
-          tc_fence_after();
+          if (it > 0) {
+            ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarPV + 16 * qt + 8 * ((it - 1) & 1),
+                                                   ((it - 1) >> 1) & 1, abort));
+            if (!ok) break;
+            tc_fence_after();
+          }
           const float f = mv ? ex2(-trel) : 1.f;
           lsum *= f;
-          for (int k = 0; k < 2; ++k) {  // this half rescales 64 of the 128 O columns
-            const uint32_t taddr = tmem + lane_base + kColO + hf * 64 + k * 32;
-            uint32_t v[32];
-            CS_TMEM_LD32(taddr, v);
-            tmem_wait_ld();
-#pragma unroll
-            for (int c = 0; c < 32; ++c) v[c] = __float_as_uint(__uint_as_float(v[c]) * f);
-            CS_TMEM_ST32(taddr, v);
-          }
-#pragma unroll
-          for (int k = 0; k < 2; ++k) {  // this tile's P, chunk k: 2^(sh - trel)
-            const int cc = (hf ? 0 : 2) + k;
-            const float fk = mv ? ex2(sh[k] - trel) : 1.f;
-            pk[k] *= fk;
-            const uint32_t taddr =
-                tmem + lane_base + kColS0 + st * 128 + (cc < 2 ? cc * 16 : 64 + (cc - 2) * 16);
+          rescale_o(f);
+          pk = 0.f;
+#pragma unroll 1
+          for (int cc = 0; cc < 4; ++cc) {  // each chunk's P: 2^(sh - trel)
+            const float shc = cc == 0 ? sh0 : cc == 1 ? sh1 : cc == 2 ? sh2 : sh3;
+            const float fk = mv ? ex2(shc - trel) : 1.f;
             uint32_t w[16];
-            CS_TMEM_LD16(taddr, w);
+            CS_TMEM_LD16(sc + 16 * cc, w);
             tmem_wait_ld();
 #pragma unroll
             for (int u = 0; u < 16; ++u) {
               const float2 e = unpack2(w[u], T{});
+              pk += e.x * fk + e.y * fk;
               w[u] = Pack2<T>::pack(e.x * fk, e.y * fk);
             }
-            CS_TMEM_ST16(taddr, w);
+            CS_TMEM_ST16(sc + 16 * cc, w);
           }
           mref = mv ? mref + trel : mref;
         }
-        lsum += pk[0] + pk[1];
+        lsum += pk;
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(mb + kBarP + 8 * st);
+        mbar_arrive(mb + kBarP + 8 * qt);
         continue;
       }
+      float tmax = -INFINITY;
       if (fast) {
-        // saturated: every visible score is S * scale2 + tsat2, a monotone map
-        // of the raw S, so the tile max comes from the raw scores (which stay
-        // in TMEM); four accumulators keep the max chains short
-        float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const unsigned hm = k ? hide1 : hide0;
+        // saturated, the row's first visible tile: every visible score is
+        // S * scale2 + tsat2, a monotone map of the raw S, so the tile max
+        // comes from the raw scores (which stay in TMEM for the P pass)
+        float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+          const unsigned hm = hide_of(cc);
           if (__all_sync(0xffffffffu, hm == ~0u)) continue;
-          const int cc = cc_hi - k;
           uint32_t v[32];
-          CS_TMEM_LD32(tmem + lane_base + kColS0 + st * 128 + cc * 32, v);
+          CS_TMEM_LD32(sc + 32 * cc, v);
           tmem_wait_ld();
-          if (hm == 0u) {
 #pragma unroll
-            for (int c = 0; c < 32; c += 4) {
-              m0 = fmaxf(m0, __uint_as_float(v[c]));
-              m1 = fmaxf(m1, __uint_as_float(v[c + 1]));
-              m2 = fmaxf(m2, __uint_as_float(v[c + 2]));
-              m3 = fmaxf(m3, __uint_as_float(v[c + 3]));
-            }
-          } else {
-#pragma unroll
-            for (int c = 0; c < 32; c += 4) {
-              m0 = (hm >> c) & 1u ? m0 : fmaxf(m0, __uint_as_float(v[c]));
-              m1 = (hm >> (c + 1)) & 1u ? m1 : fmaxf(m1, __uint_as_float(v[c + 1]));
-              m2 = (hm >> (c + 2)) & 1u ? m2 : fmaxf(m2, __uint_as_float(v[c + 2]));
-              m3 = (hm >> (c + 3)) & 1u ? m3 : fmaxf(m3, __uint_as_float(v[c + 3]));
-            }
+          for (int c = 0; c < 32; c += 2) {
+            m0 = (hm >> c) & 1u ? m0 : fmaxf(m0, __uint_as_float(v[c]));
+            m1 = (hm >> (c + 1)) & 1u ? m1 : fmaxf(m1, __uint_as_float(v[c + 1]));
           }
         }
-        const float mraw = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+        const float mraw = fmaxf(m0, m1);
         tmax = mraw > -INFINITY ? fmaf(mraw, scale2, tsat2) : -INFINITY;
         carry = sat ? fmaxf(carry, top) : carry;
-        (hf ? xm2 : xm)[r] = tmax;
-        named_sync(pair, 64);
-        tmax = fmaxf(xm[r], xm2[r]);
       } else {
-        // phase A: gates and the thread-local reverse count.  The newer half
-        // starts from the count entering the tile; the older half from 0, and
-        // records the newest column where a chunk restart cut the dependence
-        // on the newer half (columns above it add that half's count in phase B)
-        float Rc = hf == 0 ? carry : 0.f;
-        int rst = -1;
+        // contextual: chunks newest first; per chunk the gates and the
+        // reverse count (restarted at chunk boundaries), then positions,
+        // interpolated bias and masks; the scores (log2 domain) go back
+        // over S for the P pass
+        float Rc = carry;
+        float t0 = -INFINITY, t1 = -INFINITY;
 #pragma unroll 1
-        for (int k = 0; k < 2; ++k) {
-          const int cc = cc_hi - k;
-          uint32_t v[32];
-          CS_TMEM_LD32(tmem + lane_base + kColS0 + st * 128 + cc * 32, v);
+        for (int cc = 3; cc >= 0; --cc) {
+          const unsigned hm = hide_of(cc);
+          const int lim = nvalid - cc * 32;
+          uint32_t s[32], v[32];
+          CS_TMEM_LD32(sc + 32 * cc, s);
           tmem_wait_ld();
+          const unsigned bdc = cc == 0 ? bndm[0] : cc == 1 ? bndm[1] : cc == 2 ? bndm[2] : bndm[3];
+          // chunk saturated for the whole warp: no boundary restarts a count
+          // and every row either reaches it with a count >= npos - 1 or has
+          // no causal key in it: one bias (tsat2) for every visible column,
+          // and the gates change no position
+          if (__all_sync(0xffffffffu, bdc == 0u && (lim <= 0 || Rc >= top))) {
+#pragma unroll
+            for (int c = 0; c < 32; c += 2) {
+              const float x0 =
+                  (hm >> c) & 1u ? -INFINITY : fmaf(__uint_as_float(s[c]), scale2, tsat2);
+              const float x1 =
+                  (hm >> (c + 1)) & 1u ? -INFINITY : fmaf(__uint_as_float(s[c + 1]), scale2, tsat2);
+              s[c] = __float_as_uint(x0);
+              s[c + 1] = __float_as_uint(x1);
+              t0 = fmaxf(t0, x0);
+              t1 = fmaxf(t1, x1);
+            }
+            CS_TMEM_ST32(sc + 32 * cc, s);
+            if (lim > 0) Rc = fmaxf(Rc, top);
+            continue;
+          }
 #pragma unroll
           for (int c = 0; c < 32; ++c)  // gate = sigmoid(z) = (1 + tanh(z / 2)) / 2: one MUFU op
-            v[c] = __float_as_uint(fmaf(0.5f, tanh_approx(__uint_as_float(v[c]) * half_scale), 0.5f));
-          const int lim = nvalid - cc * 32;
+            v[c] = __float_as_uint(fmaf(0.5f, tanh_approx(__uint_as_float(s[c]) * half_scale), 0.5f));
           const unsigned bd = bndm[cc];
           if (bd == 0u) {  // warp-uniform: no chunk boundary, a plain suffix sum
-            if (lim < 32) {
-#pragma unroll
-              for (int c = 0; c < 32; ++c) v[c] = c < lim ? v[c] : 0u;  // +0: not counted
-            }
 #pragma unroll
             for (int c = 31; c >= 0; --c) {
-              Rc += __uint_as_float(v[c]);
+              Rc = c < lim ? Rc + __uint_as_float(v[c]) : Rc;
               v[c] = __float_as_uint(Rc);
             }
           } else {
             const int cf = 31 - __clz(bd);
-            const float rf = roff_of(cc);
+            const int kcf = bndkc[cc];
+            const float rf = (kcf >= 0 && kcf < qchunk) ? offrow[kcf] : -1.f;
 #pragma unroll
             for (int c = 31; c >= 0; --c) {
               float base = Rc;
               if ((bd >> c) & 1u) {  // warp-uniform: last key of a chunk
                 const float off = c == cf ? rf : restart_at(key0 + cc * 32 + c);
-                if (off >= 0.f) {
-                  base = off;
-                  if (c < lim && rst < 0) rst = cc * 32 + c;
-                }
+                if (off >= 0.f) base = off;
               }
               Rc = c < lim ? base + __uint_as_float(v[c]) : Rc;
               v[c] = __float_as_uint(Rc);
             }
           }
-          CS_TMEM_ST32(tmem + lane_base + kColR + cc * 32, v);
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            const float x0 = (hm >> c) & 1u ? -INFINITY
+                                            : fmaf(__uint_as_float(s[c]), scale2,
+                                                   bias_at(fminf(__uint_as_float(v[c]), top)));
+            const float x1 = (hm >> (c + 1)) & 1u
+                                 ? -INFINITY
+                                 : fmaf(__uint_as_float(s[c + 1]), scale2,
+                                        bias_at(fminf(__uint_as_float(v[c + 1]), top)));
+            s[c] = __float_as_uint(x0);
+            s[c + 1] = __float_as_uint(x1);
+            t0 = fmaxf(t0, x0);
+            t1 = fmaxf(t1, x1);
+          }
+          CS_TMEM_ST32(sc + 32 * cc, s);
         }
         tmem_wait_st();
-        // the handoff has its own barrier: the newer half does not wait here,
-        // and its next arrival at `pair` must not complete this one
-        float cin = 0.f;  // count entering the older half from the newer one
-        if (hf == 0) {
-          xc[r] = Rc;
-          named_arrive(pair + 4, 64);
-        } else {
-          named_sync(pair + 4, 64);
-          cin = xc[r];
-        }
-        // phase B: positions, interpolated bias, masks; scores (log2 domain)
-        // back into S
-        float t0 = -INFINITY, t1 = -INFINITY, t2 = -INFINITY, t3 = -INFINITY;
-#pragma unroll 1
-        for (int k = 0; k < 4; ++k) {  // 16-column pieces
-          const int col0 = (cc_hi - (k >> 1)) * 32 + (k & 1) * 16;
-          const unsigned hm = (((k >> 1) ? hide1 : hide0) >> ((k & 1) * 16)) & 0xFFFFu;
-          uint32_t v[16], w[16];
-          CS_TMEM_LD16(tmem + lane_base + kColS0 + st * 128 + col0, v);
-          CS_TMEM_LD16(tmem + lane_base + kColR + col0, w);
-          tmem_wait_ld();
-          if (hf) {  // older half: columns above the newest restart add cin
-            const int dep = rst - col0;
-#pragma unroll
-            for (int c = 0; c < 16; ++c)
-              w[c] = __float_as_uint(__uint_as_float(w[c]) + (c > dep ? cin : 0.f));
-          }
-#pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            const float pos = fminf(__uint_as_float(w[c]), top);
-            int lo;
-            const float fl = floor_pos(pos, lo);
-            const float2 tv = Tab[lo ^ tsw];
-            const float bias2 = fmaf(pos - fl, tv.y, tv.x);
-            v[c] = __float_as_uint(fmaf(__uint_as_float(v[c]), scale2, bias2));
-          }
-          if (hm) {
-#pragma unroll
-            for (int c = 0; c < 16; ++c) v[c] = (hm >> c) & 1u ? __float_as_uint(-INFINITY) : v[c];
-          }
-#pragma unroll
-          for (int c = 0; c < 16; c += 4) {
-            t0 = fmaxf(t0, __uint_as_float(v[c]));
-            t1 = fmaxf(t1, __uint_as_float(v[c + 1]));
-            t2 = fmaxf(t2, __uint_as_float(v[c + 2]));
-            t3 = fmaxf(t3, __uint_as_float(v[c + 3]));
-          }
-          CS_TMEM_ST16(tmem + lane_base + kColS0 + st * 128 + col0, v);
-        }
-        tmem_wait_st();
-        const float tm = fmaxf(fmaxf(t0, t1), fmaxf(t2, t3));
-        // tile max of both halves, and the count leaving the tile (older half)
-        (hf ? xm2 : xm)[r] = tm;
-        if (hf) xc[r] = Rc + (rst < 0 ? cin : 0.f);
-        named_sync(pair, 64);
-        tmax = fmaxf(xm[r], xm2[r]);
-        carry = xc[r];
+        tmax = fmaxf(t0, t1);
+        carry = Rc;
       }
       float mnew = mref;
       bool rescale = false;
@@ -1050,94 +1059,75 @@ __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_c
         mnew = tmax;
         rescale = mref > -INFINITY;
       }
-      // both warps of a pair hold the same rows and maxima, so they agree on
-      // whether O is rescaled; only then must PV of the previous tile be done
       if (it > 0 && __any_sync(0xffffffffu, rescale)) {
-        ok = mbar_wait(mb + kBarPV + 8 * ((it - 1) & 1), ((it - 1) >> 1) & 1, abort);
-        if (!(ok = named_and(pair, 64, ok))) break;
+        ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarPV + 16 * qt + 8 * ((it - 1) & 1),
+                                               ((it - 1) >> 1) & 1, abort));
+        if (!ok) break;
         tc_fence_after();
         const float f = rescale ? ex2(mref - mnew) : 1.f;
         lsum *= f;
-        for (int k = 0; k < 2; ++k) {  // this half rescales 64 of the 128 O columns
-          const uint32_t taddr = tmem + lane_base + kColO + hf * 64 + k * 32;
-          uint32_t v[32];
-          CS_TMEM_LD32(taddr, v);
-          tmem_wait_ld();
-#pragma unroll
-          for (int c = 0; c < 32; ++c) v[c] = __float_as_uint(__uint_as_float(v[c]) * f);
-          CS_TMEM_ST32(taddr, v);
-        }
-        tmem_wait_st();
+        rescale_o(f);
       }
       mref = mnew;
-      // P = 2^(s - mref) as packed 16-bit pairs over this half's own S
-      // columns (keys 0-63 -> columns 0-31, keys 64-127 -> columns 64-95),
-      // chunks in increasing order so no S value is overwritten before it is
+      // P = 2^(s - mref) as packed 16-bit pairs over the tile's S columns,
+      // chunks in increasing order so no score is overwritten before it is
       // read; PV takes P from TMEM.  A saturated tile forms s - mref =
-      // S * scale2 + (tsat2 - mref) directly.
+      // S * scale2 + (tsat2 - mref) from the raw S.
       const float mcur = mref > -INFINITY ? mref : 0.f;
       const float fb = tsat2 - mcur;
       float part0 = 0.f, part1 = 0.f;
 #pragma unroll 1
-      for (int k = 0; k < 2; ++k) {
-        const int cc = (hf ? 0 : 2) + k;
-        const unsigned hm = (cc & 1) ? hide0 : hide1;
+      for (int cc = 0; cc < 4; ++cc) {
+        const unsigned hm = hide_of(cc);
         uint32_t v[32];
         if (fast && __all_sync(0xffffffffu, hm == ~0u)) {
 #pragma unroll
           for (int c = 0; c < 32; ++c) v[c] = 0u;
         } else {
-          CS_TMEM_LD32(tmem + lane_base + kColS0 + st * 128 + cc * 32, v);
+          CS_TMEM_LD32(sc + 32 * cc, v);
           tmem_wait_ld();
           if (fast) {
 #pragma unroll
             for (int c = 0; c < 32; ++c)
-              v[c] = __float_as_uint(ex2(fmaf(__uint_as_float(v[c]), scale2, fb)));
-            if (hm) {
-#pragma unroll
-              for (int c = 0; c < 32; ++c) v[c] = (hm >> c) & 1u ? 0u : v[c];
-            }
+              v[c] = __float_as_uint(
+                  (hm >> c) & 1u ? 0.f : ex2(fmaf(__uint_as_float(v[c]), scale2, fb)));
           } else {
 #pragma unroll
             for (int c = 0; c < 32; ++c) v[c] = __float_as_uint(ex2(__uint_as_float(v[c]) - mcur));
           }
         }
-        uint32_t w[16];
 #pragma unroll
         for (int u = 0; u < 16; ++u) {
-          const float e0 = __uint_as_float(v[2 * u]);
-          const float e1 = __uint_as_float(v[2 * u + 1]);
+          const float e0 = __uint_as_float(v[2 * u]), e1 = __uint_as_float(v[2 * u + 1]);
           part0 += e0;
           part1 += e1;
-          w[u] = Pack2<T>::pack(e0, e1);
+          v[u] = Pack2<T>::pack(e0, e1);
         }
-        CS_TMEM_ST16(tmem + lane_base + kColS0 + st * 128 + (cc < 2 ? cc * 16 : 64 + (cc - 2) * 16), w);
+        CS_TMEM_ST16(sc + 16 * cc, v);
       }
       lsum += part0 + part1;
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(mb + kBarP + 8 * st);
+      mbar_arrive(mb + kBarP + 8 * qt);
     }
-    // epilogue: O / l, each half writes 64 of the 128 output columns
+    // epilogue: O / l
     if (ok && ntile > 0) {
-      ok = mbar_wait(mb + kBarPV + 8 * ((ntile - 1) & 1), ((ntile - 1) >> 1) & 1, abort);
+      ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarPV + 16 * qt + 8 * ((ntile - 1) & 1),
+                                             ((ntile - 1) >> 1) & 1, abort));
       tc_fence_after();
     }
-    ok = named_and(pair, 64, ok);
-    (hf == 0 ? xc : xm)[r] = lsum;
-    named_sync(pair, 64);
-    const float total = xc[r] + xm[r];
     int32_t bits = 0;
-    const float inv = total > 0.f ? 1.f / total : 0.f;
+    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
     char* orow = row_ok ? static_cast<char*>(p.out) + (i * p.o_stride_tok +
                                                        (int64_t)h * p.o_stride_head) *
                                                           dtype_size(p.out_dtype)
                         : nullptr;
-    for (int k = 0; k < 2; ++k) {
-      const int col0 = hf * 64 + k * 32;
+#pragma unroll 1
+    for (int cc = 0; cc < 4; ++cc) {
+      const int col0 = cc * 32;
       uint32_t v[32];
-      if (ntile > 0) {
-        CS_TMEM_LD32(tmem + lane_base + kColO + col0, v);
+      if (ntile > 0 && ok) {
+        CS_TMEM_LD32(oc + col0, v);
         tmem_wait_ld();
       } else {
 #pragma unroll
@@ -1323,6 +1313,48 @@ bool tma_enabled() {
   return !(e != nullptr && std::strcmp(e, "cpasync") == 0);
 }
 
+// host-side argument block of one request (false: unsupported)
+bool make_args(const cs_attn_params* p, Args& a) {
+  memset(&a, 0, sizeof(a));
+  a.p = *p;
+  a.pv = p->kv_slots ? PagedView::make(p->paged) : PagedView{};
+  a.G = p->hq / p->hkv;
+  a.R = 128 / a.G;
+  a.fmt = p->in_dtype == CS_BF16 ? 1 : 0;
+  a.pairs_per_head = (p->nq + 2 * a.R - 1) / (2 * a.R);
+  a.bs_shift = -1;
+  if (p->kv_slots) {
+    const int64_t bs = p->paged.block_size;
+    if ((bs & (bs - 1)) == 0) {
+      int s = 0;
+      while ((1ll << s) < bs) ++s;
+      a.bs_shift = s;
+    }
+  }
+  a.tma = (p->nk > 0 && tma_enabled() && setup_tma(a)) ? 1 : 0;
+  return true;
+}
+
+// once per kernel: the register split inside the kernel (setmaxnreg) is
+// sized for a launch at exactly kLaunchRegs registers a thread; any other
+// count could leave a warpgroup waiting for registers, so it is refused
+template <typename K>
+int configure(K kern, bool& done) {
+  if (done) return CS_OK;
+  cudaFuncAttributes fa{};
+  if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return CS_ERR_CUDA;
+  if (fa.numRegs != kLaunchRegs) return CS_ERR_UNSUPPORTED;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)kSmemBytes) != cudaSuccess)
+    return CS_ERR_CUDA;
+  done = true;
+  return CS_OK;
+}
+
+bool same_prefill_shape(const cs_attn_params* a, const cs_attn_params* b) {
+  return a->hq == b->hq && a->hkv == b->hkv && a->in_dtype == b->in_dtype;
+}
+
 }  // namespace
 }  // namespace cs
 
@@ -1334,36 +1366,56 @@ extern "C" int cs_cope_attn_prefill(const cs_attn_params* p, void* stream) {
   if (!prefill_supported(p)) return CS_ERR_UNSUPPORTED;
   if (p->nq == 0) return CS_OK;
   Args a;
-  memset(&a, 0, sizeof(a));
-  a.p = *p;
-  a.pv = p->kv_slots ? PagedView::make(p->paged) : PagedView{};
-  a.G = p->hq / p->hkv;
-  a.R = 128 / a.G;
-  a.fmt = p->in_dtype == CS_BF16 ? 1 : 0;
-  a.tiles_per_head = (p->nq + a.R - 1) / a.R;
-  a.bs_shift = -1;
-  if (p->kv_slots) {
-    const int64_t bs = p->paged.block_size;
-    if ((bs & (bs - 1)) == 0) {
-      int s = 0;
-      while ((1ll << s) < bs) ++s;
-      a.bs_shift = s;
-    }
-  }
-  a.tma = (p->nk > 0 && tma_enabled() && setup_tma(a)) ? 1 : 0;
-  const int blocks = a.tiles_per_head * p->hkv;
+  make_args(p, a);
+  const int blocks = a.pairs_per_head * p->hkv;
   static bool configured[2] = {false, false};
   auto launch = [&](auto kern, int which) -> int {
-    if (!configured[which]) {
-      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)kSmemBytes) != cudaSuccess)
-        return CS_ERR_CUDA;
-      configured[which] = true;
-    }
+    const int c = configure(kern, configured[which]);
+    if (c != CS_OK) return c;
     kern<<<blocks, kThreads, kSmemBytes, as_stream(stream)>>>(a);
     CS_LAUNCH_CHECK();
     return CS_OK;
   };
   if (p->in_dtype == CS_BF16) return launch(cope_prefill_sm100<__nv_bfloat16>, 1);
   return launch(cope_prefill_sm100<__half>, 0);
+}
+
+extern "C" int cs_cope_attn_prefill_batch(const cs_attn_params* params, int32_t count,
+                                          void* stream) {
+  if (params == nullptr || count < 1) return CS_ERR_INVALID;
+  for (int k = 0; k < count; ++k) {
+    const int rc = validate_attn_params(&params[k]);
+    if (rc != CS_OK) return rc;
+    if (!prefill_supported(&params[k]) || !same_prefill_shape(&params[0], &params[k]))
+      return CS_ERR_UNSUPPORTED;
+  }
+  static bool configured[2] = {false, false};
+  for (int first = 0; first < count; first += kMaxPrefillBatch) {
+    const int n = count - first < kMaxPrefillBatch ? count - first : kMaxPrefillBatch;
+    BatchArgs b;  // the launch copies it into the kernel's parameter space
+    memset(&b, 0, sizeof(b));
+    b.hkv = params[first].hkv;
+    for (int k = 0; k < n; ++k) {
+      const cs_attn_params* p = &params[first + k];
+      if (p->nq == 0) continue;
+      make_args(p, b.r[b.count]);
+      b.max_pairs = b.r[b.count].pairs_per_head > b.max_pairs ? b.r[b.count].pairs_per_head
+                                                               : b.max_pairs;
+      ++b.count;
+    }
+    if (b.count == 0) continue;
+    const int blocks = b.max_pairs * b.count * b.hkv;
+    auto launch = [&](auto kern, int which) -> int {
+      const int c = configure(kern, configured[which]);
+      if (c != CS_OK) return c;
+      kern<<<blocks, kThreads, kSmemBytes, as_stream(stream)>>>(b);
+      CS_LAUNCH_CHECK();
+      return CS_OK;
+    };
+    const int rc = params[first].in_dtype == CS_BF16
+                       ? launch(cope_prefill_sm100_batch<__nv_bfloat16>, 1)
+                       : launch(cope_prefill_sm100_batch<__half>, 0);
+    if (rc != CS_OK) return rc;
+  }
+  return CS_OK;
 }

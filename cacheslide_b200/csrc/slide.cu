@@ -2,8 +2,9 @@
 //
 // Each (slot, kv_head) record is 2*D elements (K then V).  With the native
 // layout [block, kv_head, offset, 2*D] and a contiguous innermost dimension a
-// record is 2*D*esize contiguous bytes, so one warp moves 512 bytes per D=128
-// bf16 record as 32 aligned 16-byte vectors: fully coalesced, bit-exact.
+// record is 2*D*esize contiguous bytes (512 for D=128 bf16); one warp moves a
+// whole token row (every KV head) as aligned 16-byte vectors, several in
+// flight per lane: fully coalesced, bit-exact.
 // Views whose innermost stride is not 1 (or whose rows are not 16-byte
 // aligned) take an element-wise path with the same semantics.
 #include "common.cuh"
@@ -100,6 +101,148 @@ __global__ void relocate_kernel(PagedView pv, const int64_t* __restrict__ src_sl
   }
 }
 
+// Row-per-warp paths for the common layout: a token row (all KV heads) is
+// moved by one warp as 16-byte vectors, every lane holding UPL vectors of the
+// K half and UPL of the V half in flight before it stores any; the slot is
+// resolved once per row.  Used when a head's half-record is a power-of-two
+// number of 16-byte vectors (UH) and the row's K half is 32 * UPL of them.
+// Unit q of a row half: head q >> log2(UH), vector q & (UH - 1) of that head.
+struct RowGeom {
+  int uh_shift;  // log2(16-byte vectors per head half)
+  int upl;       // vectors per lane per half: heads * UH / 32
+};
+
+__host__ bool row_geom(const PagedView& pv, RowGeom& g) {
+  const int64_t uh = pv.head_dim * pv.esize / 16;
+  if (uh < 1 || (uh & (uh - 1))) return false;
+  const int64_t units = pv.kv_heads * uh;
+  if (units % 32) return false;
+  const int64_t upl = units / 32;
+  if (upl != 1 && upl != 2 && upl != 4 && upl != 8) return false;
+  int sh = 0;
+  while ((1ll << sh) < uh) ++sh;
+  g.uh_shift = sh;
+  g.upl = (int)upl;
+  return true;
+}
+
+// record of slots[r] = rows ? in[rows[r]] : in[r]
+template <int UPL>
+__global__ void __launch_bounds__(256) scatter_rows_kernel(
+    PagedView pv, const int64_t* __restrict__ slots, const int64_t* __restrict__ rows, int64_t n,
+    const char* __restrict__ in_k, const char* __restrict__ in_v, int64_t i_row, int64_t i_head,
+    int uh_shift, int32_t* status) {
+  // a grid launched after this one as its programmatic dependent (the
+  // decode's flag-zeroing grid) may start now; it waits for this grid's
+  // completion before anything reads the rows written here
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int uh_mask = (1 << uh_shift) - 1;
+  for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < n;
+       r += warps) {
+    const int64_t s = slots[r];
+    if (!pv.valid(s)) {
+      if (lane == 0) report(status, CS_ST_SLOT_RANGE);
+      continue;
+    }
+    const int64_t src = rows ? rows[r] : r;
+    uint4 kx[UPL], vx[UPL];
+#pragma unroll
+    for (int k = 0; k < UPL; ++k) {
+      const int q = lane + 32 * k;
+      const int64_t off = src * i_row + (int64_t)(q >> uh_shift) * i_head + (q & uh_mask) * 16;
+      kx[k] = *reinterpret_cast<const uint4*>(in_k + off);
+      vx[k] = *reinterpret_cast<const uint4*>(in_v + off);
+    }
+#pragma unroll
+    for (int k = 0; k < UPL; ++k) {
+      const int q = lane + 32 * k;
+      const int h = q >> uh_shift;
+      const int64_t e = (int64_t)(q & uh_mask) * (16 / pv.esize);
+      *reinterpret_cast<uint4*>(pv.addr(s, h, e)) = kx[k];
+      *reinterpret_cast<uint4*>(pv.addr(s, h, pv.head_dim + e)) = vx[k];
+    }
+  }
+}
+
+// out[r] = record of slots[r]
+template <int UPL>
+__global__ void __launch_bounds__(256) gather_rows_kernel(
+    PagedView pv, const int64_t* __restrict__ slots, int64_t n, char* __restrict__ out_k,
+    char* __restrict__ out_v, int64_t o_row, int64_t o_head, int uh_shift, int32_t* status) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int uh_mask = (1 << uh_shift) - 1;
+  for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < n;
+       r += warps) {
+    const int64_t s = slots[r];
+    if (!pv.valid(s)) {
+      if (lane == 0) report(status, CS_ST_SLOT_RANGE);
+      continue;
+    }
+    uint4 kx[UPL], vx[UPL];
+#pragma unroll
+    for (int k = 0; k < UPL; ++k) {
+      const int q = lane + 32 * k;
+      const int h = q >> uh_shift;
+      const int64_t e = (int64_t)(q & uh_mask) * (16 / pv.esize);
+      kx[k] = *reinterpret_cast<const uint4*>(pv.addr(s, h, e));
+      vx[k] = *reinterpret_cast<const uint4*>(pv.addr(s, h, pv.head_dim + e));
+    }
+#pragma unroll
+    for (int k = 0; k < UPL; ++k) {
+      const int q = lane + 32 * k;
+      const int64_t off = r * o_row + (int64_t)(q >> uh_shift) * o_head + (q & uh_mask) * 16;
+      *reinterpret_cast<uint4*>(out_k + off) = kx[k];
+      *reinterpret_cast<uint4*>(out_v + off) = vx[k];
+    }
+  }
+}
+
+// record of dst_slots[r] = record of src_slots[r]
+template <int UPL>
+__global__ void __launch_bounds__(256) relocate_rows_kernel(
+    PagedView pv, const int64_t* __restrict__ src_slots, const int64_t* __restrict__ dst_slots,
+    int64_t n, int uh_shift, int32_t* status) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int uh_mask = (1 << uh_shift) - 1;
+  for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < n;
+       r += warps) {
+    const int64_t s = src_slots[r], d = dst_slots[r];
+    if (!pv.valid(s) || !pv.valid(d)) {
+      if (lane == 0) report(status, CS_ST_SLOT_RANGE);
+      continue;
+    }
+    uint4 kx[UPL], vx[UPL];
+#pragma unroll
+    for (int k = 0; k < UPL; ++k) {
+      const int q = lane + 32 * k;
+      const int h = q >> uh_shift;
+      const int64_t e = (int64_t)(q & uh_mask) * (16 / pv.esize);
+      kx[k] = *reinterpret_cast<const uint4*>(pv.addr(s, h, e));
+      vx[k] = *reinterpret_cast<const uint4*>(pv.addr(s, h, pv.head_dim + e));
+    }
+#pragma unroll
+    for (int k = 0; k < UPL; ++k) {
+      const int q = lane + 32 * k;
+      const int h = q >> uh_shift;
+      const int64_t e = (int64_t)(q & uh_mask) * (16 / pv.esize);
+      *reinterpret_cast<uint4*>(pv.addr(d, h, e)) = kx[k];
+      *reinterpret_cast<uint4*>(pv.addr(d, h, pv.head_dim + e)) = vx[k];
+    }
+  }
+}
+
+// warps for n rows: one row per warp up to 16 CTAs of 8 warps per SM
+int row_grid_for(int64_t n) {
+  int64_t blocks = (n + 7) / 8;
+  const int64_t cap = (int64_t)num_sms() * 16;
+  if (blocks > cap) blocks = cap;
+  return blocks < 1 ? 1 : (int)blocks;
+}
+
 int grid_for(int64_t units, int threads) {
   int64_t blocks = (units + threads - 1) / threads;
   int64_t cap = (int64_t)num_sms() * 16;
@@ -130,7 +273,21 @@ extern "C" int cs_slide_gather(const cs_paged_kv* kv, const int64_t* slots, int6
   PagedView pv = PagedView::make(*kv);
   const int64_t orow = out_stride_row * pv.esize, ohead = out_stride_head * pv.esize;
   const int threads = 256;
-  if (pv.vec16() && aligned16(out_k, orow, ohead) && aligned16(out_v, orow, ohead)) {
+  RowGeom rg{};
+  if (pv.vec16() && aligned16(out_k, orow, ohead) && aligned16(out_v, orow, ohead) &&
+      row_geom(pv, rg)) {
+    auto go = [&](auto kern) {
+      kern<<<row_grid_for(n), 256, 0, as_stream(stream)>>>(pv, slots, n, (char*)out_k,
+                                                           (char*)out_v, orow, ohead,
+                                                           rg.uh_shift, status);
+    };
+    switch (rg.upl) {
+      case 1: go(gather_rows_kernel<1>); break;
+      case 2: go(gather_rows_kernel<2>); break;
+      case 4: go(gather_rows_kernel<4>); break;
+      default: go(gather_rows_kernel<8>); break;
+    }
+  } else if (pv.vec16() && aligned16(out_k, orow, ohead) && aligned16(out_v, orow, ohead)) {
     int64_t units = n * pv.kv_heads * 2 * (pv.head_dim * pv.esize / 16);
     gather_kernel<uint4><<<grid_for(units, threads), threads, 0, as_stream(stream)>>>(
         pv, slots, n, (char*)out_k, (char*)out_v, orow, ohead, status);
@@ -158,7 +315,19 @@ extern "C" int cs_slide_scatter(const cs_paged_kv* kv, const int64_t* slots, con
   const int64_t irow = in_stride_row * pv.esize, ihead = in_stride_head * pv.esize;
   const int threads = 256;
   auto s = as_stream(stream);
-  if (pv.vec16() && aligned16(k, irow, ihead) && aligned16(v, irow, ihead)) {
+  RowGeom rg{};
+  if (pv.vec16() && aligned16(k, irow, ihead) && aligned16(v, irow, ihead) && row_geom(pv, rg)) {
+    auto go = [&](auto kern) {
+      kern<<<row_grid_for(n), 256, 0, s>>>(pv, slots, rows, n, (const char*)k, (const char*)v,
+                                           irow, ihead, rg.uh_shift, status);
+    };
+    switch (rg.upl) {
+      case 1: go(scatter_rows_kernel<1>); break;
+      case 2: go(scatter_rows_kernel<2>); break;
+      case 4: go(scatter_rows_kernel<4>); break;
+      default: go(scatter_rows_kernel<8>); break;
+    }
+  } else if (pv.vec16() && aligned16(k, irow, ihead) && aligned16(v, irow, ihead)) {
     int64_t units = n * pv.kv_heads * 2 * (pv.head_dim * pv.esize / 16);
     scatter_kernel<uint4><<<grid_for(units, threads), threads, 0, s>>>(
         pv, slots, rows, n, (const char*)k, (const char*)v, irow, ihead, status);
@@ -184,7 +353,18 @@ extern "C" int cs_slide_relocate(const cs_paged_kv* kv, const int64_t* src_slots
   PagedView pv = PagedView::make(*kv);
   const int threads = 256;
   auto s = as_stream(stream);
-  if (pv.vec16()) {
+  RowGeom rg{};
+  if (pv.vec16() && row_geom(pv, rg)) {
+    auto go = [&](auto kern) {
+      kern<<<row_grid_for(n), 256, 0, s>>>(pv, src_slots, dst_slots, n, rg.uh_shift, status);
+    };
+    switch (rg.upl) {
+      case 1: go(relocate_rows_kernel<1>); break;
+      case 2: go(relocate_rows_kernel<2>); break;
+      case 4: go(relocate_rows_kernel<4>); break;
+      default: go(relocate_rows_kernel<8>); break;
+    }
+  } else if (pv.vec16()) {
     int64_t units = n * pv.kv_heads * 2 * (pv.head_dim * pv.esize / 16);
     relocate_kernel<uint4><<<grid_for(units, threads), threads, 0, s>>>(pv, src_slots, dst_slots, n,
                                                                          status);

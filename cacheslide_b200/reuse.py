@@ -130,10 +130,17 @@ def _i64(t: torch.Tensor) -> int:
 
 
 class ReuseStep:
-    """All launches of one reuse-prefill layer for every request of a workload."""
+    """All launches of one reuse-prefill layer for every request of a workload.
 
-    def __init__(self, work: SyntheticWorkload):
+    ``batched_attention``: the CCPE attention of all requests runs as one
+    launch (``cs_cope_attn_prefill_batch``, heaviest query tiles of every
+    request first) once every request's WCA / SLIDE chain is done, instead of
+    one launch per request on the request's stream (the default: the
+    per-request launches overlap the other requests' WCA / SLIDE kernels)."""
+
+    def __init__(self, work: SyntheticWorkload, batched_attention: bool = False):
         self.work = work
+        self.batched_attention = batched_attention
         cfg = work.cfg
         dev = work.device
         self.lib = N.load()
@@ -186,6 +193,7 @@ class ReuseStep:
         # batched split-key decode (three launches for all requests)
         reqs = work.requests
         self.dec_params = (N.AttnParams * len(reqs))(*[r.dec_params for r in reqs])
+        self.attn_params = (N.AttnParams * len(reqs))(*[r.params for r in reqs])
         size = self.lib.cs_cope_attn_decode_batch_workspace(self.dec_params, len(reqs))
         self.dec_ws = torch.empty(max(size, 1), dtype=torch.uint8, device=dev) if size else None
         self.dec_k = torch.cat([r.decode_k for r in reqs]).contiguous()
@@ -307,6 +315,16 @@ class ReuseStep:
             rc = self.lib.cs_cope_attn(ctypes.byref(r.params), stream)
         N.check(rc, "attention")
 
+    def attention_all(self, stream) -> None:
+        """The attention of every request in one launch."""
+        reqs = self.work.requests
+        rc = self.lib.cs_cope_attn_prefill_batch(self.attn_params, len(reqs), stream)
+        if rc == N.CS_ERR_UNSUPPORTED:
+            for r in reqs:
+                self.attention(r, stream)
+            return
+        N.check(rc, "cs_cope_attn_prefill_batch")
+
     def run(self, stream: int | None = None, before=None, after=None) -> list[torch.Tensor]:
         """One reuse-prefill layer for every request; returns the outputs.
 
@@ -320,6 +338,7 @@ class ReuseStep:
         main = (torch.cuda.current_stream(dev) if stream is None
                 else torch.cuda.ExternalStream(stream, device=dev))
         self._fork.record(main)
+        batched = self.batched_attention
         for r, rs, done in zip(self.work.requests, self.streams, self._joins):
             rs.wait_event(self._fork)
             s = rs.cuda_stream
@@ -331,13 +350,20 @@ class ReuseStep:
             self._select_async(r, s)
             self.wca_update(r, s)
             self.wca_commit(r, s)
-            self.attention(r, s)
-            if after is not None:
-                with torch.cuda.stream(rs):
-                    after(r, rs)
+            if not batched:
+                self.attention(r, s)
+                if after is not None:
+                    with torch.cuda.stream(rs):
+                        after(r, rs)
             done.record(rs)
         for done in self._joins:
             main.wait_event(done)
+        if batched:
+            self.attention_all(main.cuda_stream)
+            if after is not None:
+                with torch.cuda.stream(main):
+                    for r in self.work.requests:
+                        after(r, main)
         return [r.out for r in self.work.requests]
 
     def _select_async(self, r, s) -> None:

@@ -327,6 +327,18 @@ CS_API int cs_cope_attn(const cs_attn_params* p, void* stream);
 CS_API int cs_cope_attn_prefill(const cs_attn_params* p, void* stream);
 
 /*
+ * The prefill of `count` requests in one launch (the reuse-prefill layer of a
+ * whole step; the reference runs cope_attention once per request,
+ * runtime.py:576-609).  Every request must be supported by
+ * cs_cope_attn_prefill and share hq, hkv and the input dtype; each has its
+ * own queries, positions, keys / slots, tables and output.  The heaviest
+ * query tiles of all requests are scheduled first, which balances the grid
+ * across requests of different lengths.
+ */
+CS_API int cs_cope_attn_prefill_batch(const cs_attn_params* params, int32_t count,
+                                      void* stream);
+
+/*
  * Decode (one or a few query rows over a long paged context): split-key
  * kernel.  On the tensor-core path (head_dim 128, 16-bit, 16-byte aligned
  * rows) one pass over the records: each split publishes its gate totals,

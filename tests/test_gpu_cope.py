@@ -687,3 +687,114 @@ def test_future_keys_do_not_change_earlier_rows(cuda):
     v[2:] += 100
     changed = cope_attention(q, k, v, cope, torch.arange(4, device=cuda))
     torch.testing.assert_close(changed[:2], original[:2])
+
+
+@pytest.mark.parametrize("restart_low", [False, True])
+def test_tensor_core_prefill_skips_inert_tiles_exactly(cuda, restart_low):
+    """Rows that are all selected (association policy) over a long context of
+    mostly fixed keys: once every row's count is saturated, the tensor-core
+    kernel skips the key tiles that hold only fixed keys, no chunk boundary
+    and none of the rows' own positions.  The result must equal the
+    kernel-without-skipping (the generic kernel) and the oracle; with
+    `restart_low` a chunk boundary restarts the counts low after saturation,
+    so the tiles below it are live again for the gates."""
+    import ctypes
+
+    from cacheslide_b200 import _native as N
+    from cacheslide_b200.position import _Holder, _base_params
+
+    nq, nk, d, hq, hkv = 64, 4096, 128, 32, 8
+    g = torch.Generator().manual_seed(11 + restart_low)
+    q = (torch.randn(nq, hq, d, generator=g) / d ** 0.5).to(torch.bfloat16).to(cuda)
+    k = (torch.randn(nk, hkv, d, generator=g) / d ** 0.5).to(torch.bfloat16).to(cuda)
+    v = torch.randn(nk, hkv, d, generator=g).to(torch.bfloat16).to(cuda)
+    fixed = torch.ones(nk, dtype=torch.bool)
+    fixed[600:610] = False       # a few visible keys far below the rows
+    fixed[1800:1830] = False
+    rows = torch.sort(torch.randperm(900, generator=g)[:nq] + 3100).values
+    selected = rows.clone()      # every row is a selected (fixed) token
+    q_sel = torch.ones(nq, dtype=torch.uint8, device=cuda)
+    E = torch.randn(d, 64, generator=g) * 0.02
+    cope = _cope(E.numpy(), cuda)
+    holder = _Holder(cope, cope.position_embeddings.detach())
+    key_chunk = (torch.arange(nk) // 1024).to(torch.int32)
+    nch = 4
+    offsets = torch.full((hq, nk, nch), 200.0)  # restarts far above npos - 1
+    if restart_low:
+        offsets[:, :, 1] = 3.0                  # boundary after key 2047: low restart
+    off_rows = offsets[:, rows].contiguous().to(cuda)
+    rows_d = rows.to(cuda)
+    k_fix = fixed.to(torch.uint8).to(cuda)
+    kc_dev = key_chunk.to(cuda)
+    lib = N.load()
+    outs = []
+    for fast in (True, False):
+        out = torch.empty(nq, hq, d, dtype=torch.bfloat16, device=cuda)
+        p = _base_params(q, k, v, holder, rows_d, None, nk, hkv, d)
+        p.out = out.data_ptr()
+        p.o_stride_tok, p.o_stride_head = out.stride(0), out.stride(1)
+        p.q_selected, p.k_fixed = q_sel.data_ptr(), k_fix.data_ptr()
+        p.pos_mode = N.POS_CHUNK
+        p.key_chunk, p.chunk_off = kc_dev.data_ptr(), off_rows.data_ptr()
+        p.co_stride_h, p.co_stride_q = off_rows.stride(0), off_rows.stride(1)
+        p.nchunks = nch
+        st = N.Status(cuda)
+        p.status = st.ptr
+        fn = lib.cs_cope_attn_prefill if fast else lib.cs_cope_attn
+        N.check(fn(ctypes.byref(p), N.stream_of(cuda)), "prefill" if fast else "generic")
+        torch.cuda.synchronize(cuda)
+        assert st.read() == 0
+        outs.append(out.float().cpu().numpy())
+    np.testing.assert_allclose(outs[0], outs[1], **BF16)
+    want = ocope.cope_attention(
+        q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(), E.numpy(),
+        rows.numpy(),
+        visibility_fn=lambda a, b: ocope.association_mask(
+            a, b, np.nonzero(fixed.numpy())[0], selected.numpy()),
+        chunk_reset=(key_chunk.numpy(), off_rows.cpu().numpy()))
+    np.testing.assert_allclose(outs[0], want, **BF16)
+
+
+def test_batched_prefill_equals_per_request_launches(cuda):
+    """cs_cope_attn_prefill_batch (all requests of a step in one grid) gives
+    exactly what one cs_cope_attn_prefill launch per request gives, for
+    requests of different lengths, positions and association flags."""
+    import ctypes
+
+    from cacheslide_b200 import _native as N
+    from cacheslide_b200.position import _Holder, _base_params
+
+    d, hq, hkv = 128, 32, 8
+    g = torch.Generator().manual_seed(77)
+    E = torch.randn(d, 64, generator=g) * 0.02
+    cope = _cope(E.numpy(), cuda)
+    holder = _Holder(cope, cope.position_embeddings.detach())
+    keep, params, outs_b = [], [], []
+    for nq, nk in ((40, 300), (300, 1900), (129, 700)):
+        q = (torch.randn(nq, hq, d, generator=g) / d ** 0.5).to(torch.bfloat16).to(cuda)
+        k = (torch.randn(nk, hkv, d, generator=g) / d ** 0.5).to(torch.bfloat16).to(cuda)
+        v = torch.randn(nk, hkv, d, generator=g).to(torch.bfloat16).to(cuda)
+        rows = torch.sort(torch.randperm(nk, generator=g)[:nq]).values.to(cuda)
+        fixed = (torch.rand(nk, generator=g) < 0.6).to(torch.uint8).to(cuda)
+        qsel = (torch.rand(nq, generator=g) < 0.5).to(torch.uint8).to(cuda)
+        out = torch.full((nq, hq, d), float("nan"), dtype=torch.bfloat16, device=cuda)
+        p = _base_params(q, k, v, holder, rows, None, nk, hkv, d)
+        p.q_selected, p.k_fixed = qsel.data_ptr(), fixed.data_ptr()
+        p.out = out.data_ptr()
+        p.o_stride_tok, p.o_stride_head = out.stride(0), out.stride(1)
+        st = N.Status(cuda)
+        p.status = st.ptr
+        keep.append((q, k, v, rows, fixed, qsel, st))
+        params.append(p)
+        outs_b.append(out)
+    lib = N.load()
+    arr = (N.AttnParams * len(params))(*params)
+    N.check(lib.cs_cope_attn_prefill_batch(arr, len(params), N.stream_of(cuda)), "batch")
+    torch.cuda.synchronize(cuda)
+    for p, out_b, kp in zip(params, outs_b, keep):
+        assert kp[-1].read() == 0
+        single = torch.full_like(out_b, float("nan"))
+        p.out = single.data_ptr()
+        N.check(lib.cs_cope_attn_prefill(ctypes.byref(p), N.stream_of(cuda)), "single")
+        torch.cuda.synchronize(cuda)
+        assert torch.equal(single.view(torch.int16), out_b.view(torch.int16))
