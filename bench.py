@@ -102,6 +102,24 @@ def hot_bytes(work) -> dict:
     return out
 
 
+def hbm_report(work, kernel_ms: dict, dec_ms: float, peak_gbs: float) -> dict:
+    """Per HBM-bound kernel: algorithmic bytes of one launch per request x the
+    requests, over the CUDA-event time of those launches back to back."""
+    hb = hot_bytes(work)
+    n = len(work.requests)
+    out = {}
+    for name, ms in kernel_ms.items():
+        if name in hb:
+            gbs = hb[name] * n / (ms * 1e-3) / 1e9
+            out[name] = {"us_per_request": ms * 1e3 / n, "gbs": gbs, "frac": gbs / peak_gbs}
+        else:  # the top-k selections: latency bound, no byte roofline
+            out[name] = {"us_per_request": ms * 1e3 / n}
+    gbs = hb["decode_attention"] * n / (dec_ms * 1e-3) / 1e9  # scatter of the new rows included
+    out["decode_step"] = {"us": dec_ms * 1e3, "gbs": gbs, "frac": gbs / peak_gbs}
+    out["peak_gbs"] = peak_gbs
+    return out
+
+
 # --------------------------------------------------------------- clocks
 class Clocks:
     """SM clock, its maximum and the active clock-event (throttle) reasons,
@@ -365,6 +383,27 @@ def main():
         att[i][0].record(stream)
         step.attention_all(s)
         att[i][1].record(stream)
+    # ---- the HBM-bound kernels of a step, each launched for all requests back
+    # to back on the timed stream after an L2 flush (achieved GB/s per kernel)
+    hbm_ms = {}
+    kinds = {
+        "slide_scatter": lambda r: step.baseline_write(r, s),
+        "wca_initialize": lambda r: step._initialize(r, s),
+        "wca_select": lambda r: step._select(r, s),
+        "wca_update": lambda r: step.wca_update(r, s),
+        "wca_commit": lambda r: step.wca_commit(r, s),
+    }
+    for name, fn in kinds.items():
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)
+            evs[i][0].record(stream)
+            for r in work.requests:
+                fn(r)
+            evs[i][1].record(stream)
+        torch.cuda.synchronize(dev)
+        hbm_ms[name] = statistics.mean(a.elapsed_time(b) for a, b in evs)
     # ---- decode steps
     dec = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
@@ -464,6 +503,7 @@ def main():
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
             "hot_bytes": hot_bytes(work),
+            "hbm_kernels": hbm_report(work, hbm_ms, dec_ms, float(pk.get("hbm_gbs", 6650.0))),
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -35,7 +35,7 @@ from .policy import WCAConfig, as_config
 from .wca import (WCAState, WCAUpdate, _inner, _kv, _mask, _matching, _raise_numeric,
                   _raise_update)
 
-__all__ = ["ShardedWCAState", "head_shard"]
+__all__ = ["ShardedWCAState", "head_shard", "exchange_row_sums", "agree_status", "shard_budget"]
 
 
 def head_shard(heads_total: int, world: int, rank: int) -> slice:
@@ -47,6 +47,30 @@ def head_shard(heads_total: int, world: int, rank: int) -> slice:
         raise ValueError("heads_total must be a positive multiple of the world size")
     per = heads_total // world
     return slice(rank * per, (rank + 1) * per)
+
+
+def exchange_row_sums(partial: Tensor, group=None) -> Tensor:
+    """This rank's partial row sums ``[k, n]`` (float64: deviation, norm and,
+    at a gate layer, cosine / heads_total) summed over the group in place:
+    afterwards every rank holds the sums over all heads (wca.py:55-112)."""
+    if partial.dtype != torch.float64 or partial.ndim != 2:
+        raise ValueError("row sums must be a float64 [k, n] tensor")
+    dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=group)
+    return partial
+
+
+def agree_status(bits: int, device, group=None) -> int:
+    """The union (bitwise max) of every rank's status bits, so that every rank
+    raises the same error or none does before anything is committed."""
+    flag = torch.tensor([int(bits)], dtype=torch.int32, device=device)
+    dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=group)
+    return int(flag.item())
+
+
+def shard_budget(fraction: float, reused_count: int, candidate_count: int) -> int:
+    """The selection budget every rank derives from the complete counts
+    (wca.py:152-191): min(ceil(fraction * |reused|), |candidates|)."""
+    return min(math.ceil(fraction * int(reused_count)), int(candidate_count))
 
 
 def _row_sums(cached: Tensor, rows: Tensor | None, fresh: Tensor, heads_total: int,
@@ -102,7 +126,7 @@ class ShardedWCAState(WCAState):
             raise ValueError("every dynamic/non-reused token must be mandatory")
         sums = torch.empty(2, n, dtype=torch.float64, device=device)
         bits = _row_sums(cached_k, None, recomputed_k, heads_total, sums, False)
-        dist.all_reduce(sums, group=group)
+        exchange_row_sums(sums, group)
         dev, nrm = sums[0], sums[1]
         reused = reused_mask.clone()
         alpha = torch.empty(n, dtype=torch.float64, device=device)
@@ -119,11 +143,10 @@ class ShardedWCAState(WCAState):
         )
         # the nonfinite decision is the same on every rank (complete sums), or
         # comes from a rank's own inputs: agree on it before raising
-        flag = torch.tensor([bits | status.read()], dtype=torch.int32, device=device)
-        dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=group)
-        _raise_numeric(int(flag.item()), "squared deviation overflowed float64")
+        _raise_numeric(agree_status(bits | status.read(), device, group),
+                       "squared deviation overflowed float64")
         reused_count, candidate_count = counts.tolist()
-        budget = min(math.ceil(config.correction_fraction * reused_count), candidate_count)
+        budget = shard_budget(config.correction_fraction, reused_count, candidate_count)
         state = cls(
             config=config,
             reused_mask=reused,
@@ -160,7 +183,7 @@ class ShardedWCAState(WCAState):
         gate = layer_index % self.config.gate_interval == 0
         sums = torch.empty(3 if gate else 2, a, dtype=torch.float64, device=device)
         bits = _row_sums(ck, indices, fk, self.heads_total, sums, gate) if a else 0
-        dist.all_reduce(sums, group=self.group)
+        exchange_row_sums(sums, self.group)
         next_alpha = torch.empty(a, dtype=torch.float64, device=device)
         status = N.Status(device)
         N.check(
@@ -182,10 +205,7 @@ class ShardedWCAState(WCAState):
             check=False)
         # every rank raises, or none does (the update is all-or-nothing on
         # every rank): agree on the status bits before committing
-        flag = torch.tensor([bits | status.read() | blend_bits], dtype=torch.int32,
-                            device=device)
-        dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=self.group)
-        _raise_update(int(flag.item()))
+        _raise_update(agree_status(bits | status.read() | blend_bits, device, self.group))
         removed, promoted = self._commit(indices, next_alpha, cosine)
         self.last_layer = layer_index
         return WCAUpdate(

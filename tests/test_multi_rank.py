@@ -2,17 +2,18 @@
 
 * KV-head tensor parallelism of WCA (``cacheslide_b200.tp``): the head
   shards' partial row sums (deviation, norm, cosine / heads_total), summed by
-  an all-reduce, reproduce the full-head reductions of the reference
-  (``wca.py:55-112``), so every rank selects, removes and promotes the same
-  tokens as an unsharded state.  The sharded state machine below follows
-  ``ShardedWCAState`` step for step on top of the numpy oracle.
+  ``tp.exchange_row_sums``, reproduce the full-head reductions of the
+  reference (``wca.py:55-112``), so every rank selects, removes and promotes
+  the same tokens as an unsharded state.  The partial sums are the host
+  values ``cs_wca_row_sums`` computes on the device (each rank's heads); the
+  exchange, the budget (``tp.shard_budget``) and the status agreement
+  (``tp.agree_status``) are ``tp.py``'s own functions, run over gloo.
 * Request sharding (``bench.py --gpus N``): ranks build independent request
   sets from per-rank seeds and the job time is the maximum over ranks.
 """
 
 from __future__ import annotations
 
-import math
 import os
 import socket
 
@@ -22,7 +23,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from cacheslide_b200.tp import head_shard
+from cacheslide_b200.tp import agree_status, exchange_row_sums, head_shard, shard_budget
 from oracle import wca as owca
 
 WORLD = 2
@@ -62,26 +63,28 @@ def _entry(rank, port, fn, args):
         dist.destroy_process_group()
 
 
-def _allreduce(x: np.ndarray) -> np.ndarray:
-    t = torch.from_numpy(np.ascontiguousarray(x))
-    dist.all_reduce(t)
+def _exchange(parts: list[np.ndarray]) -> np.ndarray:
+    """This rank's partial row sums through ``tp.exchange_row_sums``."""
+    t = torch.from_numpy(np.ascontiguousarray(np.stack(parts), dtype=np.float64))
+    out = exchange_row_sums(t)
+    assert out is t  # summed in place, as the device path relies on
     return t.numpy()
 
 
 class ShardedOracleWCA(owca.OracleWCA):
-    """The sharded WCA state machine of ``ShardedWCAState`` on the oracle:
-    this rank's heads only, row sums all-reduced before any decision."""
+    """The decisions of ``ShardedWCAState`` on host inputs: this rank's heads
+    only, partial row sums exchanged by ``tp.exchange_row_sums`` before any
+    decision, the budget from ``tp.shard_budget``."""
 
     def initialize(self, cached, fresh, reused, mandatory, heads_total):
         self.heads_total = heads_total
         c64, f64 = cached.astype(np.float64), fresh.astype(np.float64)
-        sums = np.stack([np.square(f64 - c64).sum((1, 2)), np.square(c64).sum((1, 2))])
-        dev, nrm = _allreduce(sums)
+        dev, nrm = _exchange([np.square(f64 - c64).sum((1, 2)), np.square(c64).sum((1, 2))])
         self.reused, self.mandatory = reused.copy(), mandatory.copy()
         self.initial = dev.copy()
         self.candidate = reused & (dev > 0)
-        self.budget = min(math.ceil(self.correction_fraction * int(reused.sum())),
-                          int(self.candidate.sum()))
+        self.budget = shard_budget(self.correction_fraction, int(reused.sum()),
+                                   int(self.candidate.sum()))
         self.selected = np.zeros_like(self.candidate)
         self.removed = np.zeros_like(self.candidate)
         self.alpha = dev / (nrm + self.epsilon)
@@ -99,7 +102,7 @@ class ShardedOracleWCA(owca.OracleWCA):
             heads = fresh_k.shape[1]
             parts.append(owca.mean_head_cosine(fresh_k, old_k, self.epsilon) * heads
                          / self.heads_total)
-        sums = _allreduce(np.stack(parts))
+        sums = _exchange(parts)
         nxt = sums[0] / (sums[1] + self.epsilon)
         used = self.alpha[idx] if self.weight_update == "previous_layer" else nxt
         used = np.where(self.mandatory[idx], 1.0, used)
@@ -160,6 +163,35 @@ def _tp_ranks(rank, weight_update):
 @pytest.mark.parametrize("weight_update", ["previous_layer", "same_layer"])
 def test_head_sharded_wca_selects_like_the_full_state(weight_update):
     _run(_tp_ranks, weight_update)
+
+
+def _agreement_ranks(rank):
+    cpu = torch.device("cpu")
+    # a status bit raised on one rank only reaches every rank
+    assert agree_status(0x4 if rank == 1 else 0, cpu) == 0x4
+    assert agree_status(0x1 if rank == 0 else 0x2, cpu) == 0x2  # max, as the device flags
+    assert agree_status(0, cpu) == 0
+    # partial sums of disjoint head shards add up to the full-head sums
+    part = torch.full((3, 5), float(rank + 1), dtype=torch.float64)
+    exchange_row_sums(part)
+    assert torch.equal(part, torch.full((3, 5), 3.0, dtype=torch.float64))
+    # a malformed buffer is rejected on every rank before any collective
+    for bad in (torch.zeros(2, 4, dtype=torch.float32), torch.zeros(4, dtype=torch.float64)):
+        with pytest.raises(ValueError):
+            exchange_row_sums(bad)
+    # the ranks are still in step: one more collective completes
+    assert agree_status(rank, cpu) == WORLD - 1
+
+
+def test_status_agreement_and_row_sum_exchange_over_gloo():
+    _run(_agreement_ranks)
+
+
+def test_shard_budget_follows_the_reference_rounding():
+    assert shard_budget(0.15, 3584, 3584) == 538  # C2: ceil(0.15 * 3584)
+    assert shard_budget(0.2, 10, 1) == 1           # capped by the candidates
+    assert shard_budget(0.0, 10, 10) == 0
+    assert shard_budget(1.0, 7, 9) == 7
 
 
 def test_head_shard_splits_evenly_and_rejects_bad_layouts():
