@@ -52,6 +52,9 @@ def parse():
     ap.add_argument("--batched-attention", action="store_true",
                     help="one attention launch for all requests after their WCA / SLIDE "
                          "chains (default: one launch per request on its stream)")
+    ap.add_argument("--batched", action="store_true",
+                    help="every stage of the step as one launch for all requests (seven "
+                         "launches per step); e2e keeps the per-request streams")
     return ap.parse_args()
 
 
@@ -331,7 +334,7 @@ def main():
                                 device_id=dev)
     cfg = WorkloadConfig(requests=args.requests, seq=args.seq, seed=1000 + rank)
     work = SyntheticWorkload(cfg, dev)
-    step = ReuseStep(work, batched_attention=args.batched_attention)
+    step = ReuseStep(work, batched_attention=args.batched_attention, batched=args.batched)
     # a dedicated stream, current for every torch op below: on the legacy
     # default stream, events around the 8-stream fork/join of a step were
     # seen to under-count the step (456 us against a 1040 us host-synchronised
@@ -386,21 +389,26 @@ def main():
     # ---- the HBM-bound kernels of a step, each launched for all requests back
     # to back on the timed stream after an L2 flush (achieved GB/s per kernel)
     hbm_ms = {}
-    kinds = {
-        "slide_scatter": lambda r: step.baseline_write(r, s),
-        "wca_initialize": lambda r: step._initialize(r, s),
-        "wca_select": lambda r: step._select(r, s),
-        "wca_update": lambda r: step.wca_update(r, s),
-        "wca_commit": lambda r: step.wca_commit(r, s),
-    }
+    if args.batched:  # one launch for all requests
+        kinds = {"slide_scatter": lambda: step.scatter_all(s),
+                 "wca_initialize": lambda: step.initialize_all(s),
+                 "wca_select": lambda: step.select_all(s),
+                 "wca_update": lambda: step.update_all(s),
+                 "wca_commit": lambda: step.commit_all(s)}
+    else:  # one launch per request
+        each = lambda f: lambda: [f(r, s) for r in work.requests]  # noqa: E731
+        kinds = {"slide_scatter": each(step.baseline_write),
+                 "wca_initialize": each(step._initialize),
+                 "wca_select": each(step._select),
+                 "wca_update": each(step.wca_update),
+                 "wca_commit": each(step.wca_commit)}
     for name, fn in kinds.items():
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                for _ in range(args.steps)]
         for i in range(args.steps):
             flush.fill_(i & 0xFF)
             evs[i][0].record(stream)
-            for r in work.requests:
-                fn(r)
+            fn()
             evs[i][1].record(stream)
         torch.cuda.synchronize(dev)
         hbm_ms[name] = statistics.mean(a.elapsed_time(b) for a, b in evs)
@@ -447,7 +455,8 @@ def main():
     for i in range(args.steps):
         flush.fill_(i & 0xFF)
         e2e_ev[i][0].record(stream)
-        step.run(s, before=stage_in, after=stage_out)
+        # per-request streams: each request's copies overlap the others' kernels
+        step.run(s, before=stage_in, after=stage_out, batched=False)
         e2e_ev[i][1].record(stream)
     barrier()
     e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_ev)
@@ -473,7 +482,9 @@ def main():
             sec, desc = cpu_requests(work, 1, threads)
             cpu = {"value": cfg.seq / sec, "unit": "tok/s", "cores": threads, "kind": "port",
                    "sample": desc, "sample_fraction": 1.0}
-        launches_per_step = len(work.requests) * 6
+        # batched: scatter, counts reset, initialize, select, update, commit,
+        # attention; per request: those five WCA / SLIDE kernels and attention
+        launches_per_step = 7 if args.batched else len(work.requests) * 6
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
@@ -484,7 +495,13 @@ def main():
             "data": "synthetic (seeded random-init inputs of the C2 shapes)",
             "config": {"workload": WORKLOAD, "requests_per_gpu": args.requests,
                        "l2": "flushed (256 MB write) between timed steps",
-                       "parallelism": f"request-sharded x{world}"},
+                       "parallelism": f"request-sharded x{world}",
+                       "schedule": ("batched: one launch per stage for all requests"
+                                    if args.batched else
+                                    "per-request streams" + (", one attention launch"
+                                                             if args.batched_attention else "")),
+                       "e2e_schedule": "per-request streams (each request's copies overlap "
+                                       "the other requests' kernels)"},
             "decode": {"value": decode_value, "unit": "tok/s",
                        "ms_per_step": dec_ms, "note": "one token per request over 4097 keys"},
             "roofline": {"bound": "tensor",

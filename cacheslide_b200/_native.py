@@ -89,10 +89,55 @@ class AttnParams(ctypes.Structure):
     ]
 
 
+class ScatterItem(ctypes.Structure):
+    """cs_slide_scatter_item: one request of cs_slide_scatter_batch."""
+    _fields_ = [
+        ("slots", _p), ("rows", _p), ("n", _i64), ("k", _p), ("v", _p),
+        ("in_stride_row", _i64), ("in_stride_head", _i64), ("status", _p),
+    ]
+
+
+class InitializeItem(ctypes.Structure):
+    """cs_wca_initialize_item: one request of cs_wca_initialize_batch."""
+    _fields_ = [
+        ("cached", _p), ("c_stride_row", _i64), ("c_stride_head", _i64),
+        ("fresh", _p), ("f_stride_row", _i64), ("f_stride_head", _i64),
+        ("n", _i64), ("reused", _p), ("dev_out", _p), ("alpha_out", _p), ("candidate", _p),
+        ("selected", _p), ("removed", _p), ("counts_out", _p), ("status", _p),
+    ]
+
+
+class UpdateItem(ctypes.Structure):
+    """cs_wca_update_item: one request of cs_wca_update_batch."""
+    _fields_ = [
+        ("cached_k", _p), ("cached_v", _p), ("c_stride_row", _i64), ("c_stride_head", _i64),
+        ("fresh_k", _p), ("fresh_v", _p), ("f_stride_row", _i64), ("f_stride_head", _i64),
+        ("indices", _p), ("a", _i64), ("alpha", _p), ("mandatory", _p),
+        ("fused_k", _p), ("fused_v", _p), ("next_alpha_out", _p), ("used_alpha_out", _p),
+        ("cos_out", _p), ("slots", _p), ("status", _p),
+    ]
+
+
+class CommitItem(ctypes.Structure):
+    """cs_wca_commit_item: one request of cs_wca_commit_batch."""
+    _fields_ = [
+        ("indices", _p), ("a", _i64), ("next_alpha", _p), ("cos", _p), ("n", _i64),
+        ("budget", _i64), ("initial_dev", _p), ("alpha", _p), ("candidate", _p),
+        ("selected", _p), ("removed", _p), ("removed_out", _p), ("promoted_out", _p),
+        ("counts_out", _p), ("status", _p),
+    ]
+
+
 _SIGNATURES = {
     "cs_slide_gather": [ctypes.POINTER(PagedKV), _p, _i64, _p, _p, _i64, _i64, _p, _p],
     "cs_slide_scatter": [ctypes.POINTER(PagedKV), _p, _p, _i64, _p, _p, _i64, _i64, _p, _p],
     "cs_slide_relocate": [ctypes.POINTER(PagedKV), _p, _p, _i64, _p, _p],
+    "cs_slide_scatter_batch": [ctypes.POINTER(PagedKV), ctypes.POINTER(ScatterItem), _i32, _p],
+    "cs_wca_initialize_batch": [ctypes.POINTER(InitializeItem), _i32, _i64, _i64, _i32, _f64,
+                                _i32, _p],
+    "cs_wca_update_batch": [ctypes.POINTER(UpdateItem), _i32, _i64, _i64, _i32, _i32, _f64,
+                            _i32, ctypes.POINTER(PagedKV), _p],
+    "cs_wca_commit_batch": [ctypes.POINTER(CommitItem), _i32, _f64, _i32, _p],
     "cs_wca_deviation": [_p, _i64, _i64, _p, _p, _i64, _i64, _i64, _i64, _i64, _i32, _f64,
                          _i32, _p, _p, _p, _p],
     "cs_wca_cosine": [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64, _i32, _f64, _p,

@@ -134,6 +134,22 @@ struct PagedView {
     if (e < head_dim) return side_k + r * ssr + h * ssh + e * sse;
     return side_v + r * ssr + h * ssh + (e - head_dim) * sse;
   }
+  // the K and V halves of slot s's records (head 0, element 0) and the
+  // byte stride between heads: element e of head h of the K half is at
+  // k + h * hstride + e * (element stride); slot must be valid
+  __device__ __forceinline__ void record(int64_t s, char*& k, char*& v, int64_t& hstride) const {
+    if (s < native_total) {
+      const int64_t b = s / bs, o = s - b * bs;
+      k = cache + b * sb + o * so;
+      v = k + head_dim * se;
+      hstride = sh;
+    } else {
+      const int64_t r = s - native_total;
+      k = side_k + r * ssr;
+      v = side_v + r * ssr;
+      hstride = ssh;
+    }
+  }
   // whether records can move as aligned 16-byte vectors
   __host__ bool vec16() const {
     if (se != esize) return false;
@@ -168,6 +184,22 @@ __device__ __forceinline__ A warp_max(A x) {
     x = y > x ? y : x;
   }
   return x;
+}
+
+// Batched launches: up to kBatchItems requests per launch, request i owning
+// the global rows [start[i], start[i + 1]).  The request of global row r is
+// the largest i with start[i] <= r (binary search; warp-uniform when a warp
+// owns a row).  Requests with no rows are never found.
+constexpr int kBatchItems = 64;
+
+__device__ __forceinline__ int batch_item(const int64_t* start, int count, int64_t r) {
+  int lo = 0, hi = count - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (start[mid] <= r) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
 }
 
 inline int num_sms() {

@@ -235,6 +235,63 @@ __global__ void __launch_bounds__(256) relocate_rows_kernel(
   }
 }
 
+// Several requests' scatters in one launch: request i owns the global rows
+// [start[i], start[i + 1]); a warp finds its request by binary search over
+// the prefix (uniform across the warp, read from the parameter space).
+constexpr int kBatch = kBatchItems;
+
+struct ScatterRows {
+  const int64_t* slots;
+  const int64_t* rows;
+  const char* k;
+  const char* v;
+  int64_t irow, ihead;  // byte strides
+  int32_t* status;
+};
+
+struct ScatterBatch {
+  ScatterRows it[kBatch];
+  int64_t start[kBatch + 1];
+  int count;
+};
+
+template <int UPL>
+__global__ void __launch_bounds__(256) scatter_rows_batch_kernel(
+    PagedView pv, const __grid_constant__ ScatterBatch b, int uh_shift) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int uh_mask = (1 << uh_shift) - 1;
+  const int64_t total = b.start[b.count];
+  for (int64_t g = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); g < total;
+       g += warps) {
+    const int i = batch_item(b.start, b.count, g);
+    const ScatterRows& q = b.it[i];
+    const int64_t r = g - b.start[i];
+    const int64_t s = q.slots[r];
+    if (!pv.valid(s)) {
+      if (lane == 0) report(q.status, CS_ST_SLOT_RANGE);
+      continue;
+    }
+    const int64_t src = q.rows ? q.rows[r] : r;
+    uint4 kx[UPL], vx[UPL];
+#pragma unroll
+    for (int k = 0; k < UPL; ++k) {
+      const int u = lane + 32 * k;
+      const int64_t off = src * q.irow + (int64_t)(u >> uh_shift) * q.ihead + (u & uh_mask) * 16;
+      kx[k] = *reinterpret_cast<const uint4*>(q.k + off);
+      vx[k] = *reinterpret_cast<const uint4*>(q.v + off);
+    }
+#pragma unroll
+    for (int k = 0; k < UPL; ++k) {
+      const int u = lane + 32 * k;
+      const int h = u >> uh_shift;
+      const int64_t e = (int64_t)(u & uh_mask) * (16 / pv.esize);
+      *reinterpret_cast<uint4*>(pv.addr(s, h, e)) = kx[k];
+      *reinterpret_cast<uint4*>(pv.addr(s, h, pv.head_dim + e)) = vx[k];
+    }
+  }
+}
+
 // warps for n rows: one row per warp up to 16 CTAs of 8 warps per SM
 int row_grid_for(int64_t n) {
   int64_t blocks = (n + 7) / 8;
@@ -378,5 +435,53 @@ extern "C" int cs_slide_relocate(const cs_paged_kv* kv, const int64_t* src_slots
     }
   }
   CS_LAUNCH_CHECK();
+  return CS_OK;
+}
+
+extern "C" int cs_slide_scatter_batch(const cs_paged_kv* kv, const cs_slide_scatter_item* items,
+                                      int32_t count, void* stream) {
+  CS_HOST_CHECK(check_view(kv) && count >= 0 && (count == 0 || items));
+  PagedView pv = PagedView::make(*kv);
+  RowGeom rg{};
+  bool rows_path = pv.vec16() && row_geom(pv, rg);
+  for (int32_t i = 0; i < count; ++i) {
+    const cs_slide_scatter_item& it = items[i];
+    CS_HOST_CHECK(it.n >= 0 && (it.n == 0 || (it.slots && it.k && it.v)));
+    const int64_t irow = it.in_stride_row * pv.esize, ihead = it.in_stride_head * pv.esize;
+    if (it.n > 0 && !(aligned16(it.k, irow, ihead) && aligned16(it.v, irow, ihead)))
+      rows_path = false;
+  }
+  if (!rows_path) {  // the general layouts: one launch per request
+    for (int32_t i = 0; i < count; ++i) {
+      const cs_slide_scatter_item& it = items[i];
+      const int rc = cs_slide_scatter(kv, it.slots, it.rows, it.n, it.k, it.v, it.in_stride_row,
+                                      it.in_stride_head, it.status, stream);
+      if (rc != CS_OK) return rc;
+    }
+    return CS_OK;
+  }
+  auto s = as_stream(stream);
+  for (int32_t first = 0; first < count; first += kBatch) {
+    ScatterBatch b{};  // copied into the kernel's parameter space by the launch
+    b.count = count - first < kBatch ? count - first : kBatch;
+    b.start[0] = 0;
+    for (int j = 0; j < b.count; ++j) {
+      const cs_slide_scatter_item& it = items[first + j];
+      b.it[j] = ScatterRows{it.slots, it.rows, static_cast<const char*>(it.k),
+                            static_cast<const char*>(it.v), it.in_stride_row * pv.esize,
+                            it.in_stride_head * pv.esize, it.status};
+      b.start[j + 1] = b.start[j] + it.n;
+    }
+    const int64_t total = b.start[b.count];
+    if (total == 0) continue;
+    auto go = [&](auto kern) { kern<<<row_grid_for(total), 256, 0, s>>>(pv, b, rg.uh_shift); };
+    switch (rg.upl) {
+      case 1: go(scatter_rows_batch_kernel<1>); break;
+      case 2: go(scatter_rows_batch_kernel<2>); break;
+      case 4: go(scatter_rows_batch_kernel<4>); break;
+      default: go(scatter_rows_batch_kernel<8>); break;
+    }
+    CS_LAUNCH_CHECK();
+  }
   return CS_OK;
 }

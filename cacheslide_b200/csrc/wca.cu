@@ -527,12 +527,31 @@ __device__ double row_cosine(Rows<T> a, int64_t arow, Rows<T> b, int64_t brow, i
 // heads x G8 vectors of 8 elements (G8 = dim / 8 divides 32), lane l taking
 // vectors l, l + 32, ...; in every step each aligned group of G8 lanes holds
 // one head.
+//
+// Finiteness of 16-bit inputs is read off the row sums: a sum of squares of
+// finite 16-bit values (or of their differences) cannot overflow float64,
+// and any infinity or NaN among them makes the sum infinite or NaN.
+template <typename T>
+__device__ __forceinline__ void widen8(const uint4& u, double (&x)[8]) {
+  const T* el = reinterpret_cast<const T*>(&u);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) x[k] = Elem<T>::to_d(el[k]);
+}
+
+// whether a 16-bit float's bits hold an infinity or a NaN
+template <typename T>
+__device__ __forceinline__ bool nonfinite_bits(T y) {
+  if constexpr (sizeof(T) == 2) {
+    constexpr uint32_t kExp = std::is_same<T, __nv_bfloat16>::value ? 0x7F80u : 0x7C00u;
+    return (*reinterpret_cast<const uint16_t*>(&y) & kExp) == kExp;
+  } else {
+    return !isfinite(Elem<T>::to_d(y));
+  }
+}
+
 template <typename T>
 __device__ __forceinline__ void load8(const T* p, double (&x)[8]) {
-  const uint4 u = *reinterpret_cast<const uint4*>(p);
-  const T* e = reinterpret_cast<const T*>(&u);
-#pragma unroll
-  for (int k = 0; k < 8; ++k) x[k] = Elem<T>::to_d(e[k]);
+  widen8<T>(*reinterpret_cast<const uint4*>(p), x);
 }
 
 template <typename T, int G8>
@@ -540,7 +559,6 @@ __device__ __forceinline__ bool row_dev_nrm_vec(Rows<T> c, int64_t crow, Rows<T>
                                                 int64_t heads, double& dev, double& nrm) {
   const int lane = threadIdx.x & 31;
   double d_acc = 0.0, n_acc = 0.0;
-  bool ok = true;
   const int64_t groups = heads * G8;
 #pragma unroll 4
   for (int64_t g = lane; g < groups; g += 32) {
@@ -551,7 +569,6 @@ __device__ __forceinline__ bool row_dev_nrm_vec(Rows<T> c, int64_t crow, Rows<T>
     load8(f.ptr(frow, h) + e, fv);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      ok &= isfinite(cv[k]) && isfinite(fv[k]);
       const double df = __dsub_rn(fv[k], cv[k]);
       d_acc = __dadd_rn(d_acc, __dmul_rn(df, df));
       n_acc = __dadd_rn(n_acc, __dmul_rn(cv[k], cv[k]));
@@ -559,7 +576,76 @@ __device__ __forceinline__ bool row_dev_nrm_vec(Rows<T> c, int64_t crow, Rows<T>
   }
   dev = warp_sum(d_acc);
   nrm = warp_sum(n_acc);
-  return __all_sync(0xffffffffu, ok);
+  return isfinite(dev) && isfinite(nrm);  // 16-bit rows: the inputs' finiteness
+}
+
+// A row held in registers: IT = heads * G8 / 32 vectors per lane (vector
+// g = it * 32 + lane: head g / G8, elements (g % G8) * 8 ..), every load of
+// the row issued before any arithmetic, so a warp keeps whole rows in flight.
+template <typename T, int G8, int IT>
+__device__ __forceinline__ void load_row(Rows<T> x, int64_t row, uint4 (&v)[IT]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int it = 0; it < IT; ++it) {
+    const int g = it * 32 + lane;
+    v[it] = *reinterpret_cast<const uint4*>(x.ptr(row, g / G8) + (g % G8) * 8);
+  }
+}
+
+// pairwise sum of per-vector partial sums (IT a power of two)
+template <int IT>
+__device__ __forceinline__ double tree_sum(const double (&p)[IT]) {
+  if constexpr (IT == 1) {
+    return p[0];
+  } else {
+    double h[IT / 2];
+#pragma unroll
+    for (int i = 0; i < IT / 2; ++i) h[i] = __dadd_rn(p[2 * i], p[2 * i + 1]);
+    return tree_sum<IT / 2>(h);
+  }
+}
+
+// dev / nrm of a register-resident row pair: one partial sum per vector (so
+// the dependent float64 chains are 8 long), pairwise over the vectors, then
+// the butterfly over the lanes (any summation order is within the
+// tolerance of the reference's own float64 reduction); true when both sums
+// are finite, i.e. all inputs are (16-bit rows)
+template <typename T, int IT>
+__device__ __forceinline__ bool dev_nrm_regs(const uint4 (&c)[IT], const uint4 (&f)[IT],
+                                             double& dev, double& nrm) {
+  double dp[IT], np[IT];
+#pragma unroll
+  for (int it = 0; it < IT; ++it) {
+    double cv[8], fv[8];
+    widen8<T>(c[it], cv);
+    widen8<T>(f[it], fv);
+    dp[it] = np[it] = 0.0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const double df = __dsub_rn(fv[k], cv[k]);
+      dp[it] = __dadd_rn(dp[it], __dmul_rn(df, df));
+      np[it] = __dadd_rn(np[it], __dmul_rn(cv[k], cv[k]));
+    }
+  }
+  dev = warp_sum(tree_sum<IT>(dp));
+  nrm = warp_sum(tree_sum<IT>(np));
+  return isfinite(dev) && isfinite(nrm);
+}
+
+// the deviation / norm of one row pair on the widest path the layout allows
+template <typename T, int G8, int IT>
+__device__ __forceinline__ bool row_dev(Rows<T> c, int64_t crow, Rows<T> f, int64_t frow,
+                                        int64_t heads, int64_t dim, double& dev, double& nrm) {
+  if constexpr (IT > 0) {
+    uint4 cv[IT], fv[IT];
+    load_row<T, G8, IT>(c, crow, cv);
+    load_row<T, G8, IT>(f, frow, fv);
+    return dev_nrm_regs<T, IT>(cv, fv, dev, nrm);
+  } else if constexpr (G8 > 0) {
+    return row_dev_nrm_vec<T, G8>(c, crow, f, frow, heads, dev, nrm);
+  } else {
+    return row_dev_nrm(c, crow, f, frow, heads, dim, dev, nrm);
+  }
 }
 
 // per-head dot / squared norms of the G8-lane group, summed into lanes with
@@ -602,10 +688,31 @@ __device__ double row_cosine_vec(Rows<T> a, int64_t arow, Rows<T> b, int64_t bro
   return warp_sum(acc) / (double)heads;
 }
 
-// one warp per row; G8 > 0 selects the 16-byte vector path.  The reused /
-// candidate counts are gathered per block and added once per block.
-template <typename T, int G8>
-__global__ void deviation_kernel(Rows<T> c, const int64_t* __restrict__ crows, Rows<T> f,
+// lane 0 of a row's warp: weight, status bits, outputs; returns the row's
+// reused (bit 0) and candidate (bit 1) flags for the counts
+__device__ __forceinline__ int dev_epilogue(int64_t r, double dev, double nrm, bool in_ok,
+                                            double eps, int clamp, double* dev_out,
+                                            double* alpha_out, const uint8_t* reused,
+                                            uint8_t* candidate, int32_t* status) {
+  const double den = nrm + eps;
+  double a = dev / den;
+  if (!in_ok) report(status, CS_ST_INPUT_NONFINITE);
+  if (!finite(dev) || !finite(den) || !finite(a)) report(status, CS_ST_NONFINITE);
+  if (clamp) a = fmin(fmax(a, 0.0), 1.0);
+  if (dev_out) dev_out[r] = dev;
+  if (alpha_out) alpha_out[r] = a;
+  if (!candidate) return 0;
+  const bool ru = reused[r] != 0;
+  const bool cand = ru && dev > 0.0;
+  candidate[r] = cand ? 1 : 0;
+  return (ru ? 1 : 0) | (cand ? 2 : 0);
+}
+
+// one warp per row; G8 > 0 selects the 16-byte vector path, IT > 0 the
+// register-resident rows.  The reused / candidate counts are gathered per
+// block and added once per block.
+template <typename T, int G8, int IT>
+__global__ void __launch_bounds__(256, IT > 0 ? 3 : 1) deviation_kernel(Rows<T> c, const int64_t* __restrict__ crows, Rows<T> f,
                                  int64_t n, int64_t heads, int64_t dim, double eps, int clamp,
                                  double* dev_out, double* alpha_out,
                                  const uint8_t* __restrict__ reused, uint8_t* candidate,
@@ -618,26 +725,12 @@ __global__ void deviation_kernel(Rows<T> c, const int64_t* __restrict__ crows, R
        r += warps) {
     double dev, nrm;
     const int64_t crow = crows ? crows[r] : r;
-    bool in_ok;
-    if constexpr (G8 > 0)
-      in_ok = row_dev_nrm_vec<T, G8>(c, crow, f, r, heads, dev, nrm);
-    else
-      in_ok = row_dev_nrm(c, crow, f, r, heads, dim, dev, nrm);
+    const bool in_ok = row_dev<T, G8, IT>(c, crow, f, r, heads, dim, dev, nrm);
     if ((threadIdx.x & 31) == 0) {
-      double den = nrm + eps;
-      double a = dev / den;
-      if (!in_ok) report(status, CS_ST_INPUT_NONFINITE);
-      if (!finite(dev) || !finite(den) || !finite(a)) report(status, CS_ST_NONFINITE);
-      if (clamp) a = fmin(fmax(a, 0.0), 1.0);
-      if (dev_out) dev_out[r] = dev;
-      if (alpha_out) alpha_out[r] = a;
-      if (candidate) {
-        bool ru = reused[r] != 0;
-        bool cand = ru && dev > 0.0;
-        candidate[r] = cand ? 1 : 0;
-        if (ru) atomicAdd(&cnt[0], 1ull);
-        if (cand) atomicAdd(&cnt[1], 1ull);
-      }
+      const int fl = dev_epilogue(r, dev, nrm, in_ok, eps, clamp, dev_out, alpha_out, reused,
+                                  candidate, status);
+      if (fl & 1) atomicAdd(&cnt[0], 1ull);
+      if (fl & 2) atomicAdd(&cnt[1], 1ull);
     }
   }
   if (candidate) {
@@ -737,39 +830,121 @@ __global__ void weights_kernel(const double* __restrict__ dev, const double* __r
   }
 }
 
-// fused update: weight, blend (float64, no contraction), cast, write dense
-// and/or paged records, optional cosine; G8 > 0 selects the 16-byte vector path
-template <typename T, int G8>
-__global__ void update_kernel(Rows<T> ck, Rows<T> cv, Rows<T> fk, Rows<T> fv,
-                              const int64_t* __restrict__ indices, int64_t a, int64_t heads,
-                              int64_t dim, const double* __restrict__ alpha,
-                              const uint8_t* __restrict__ mandatory, int same_layer, double eps,
-                              int clamp, T* fused_k, T* fused_v, double* next_alpha_out,
-                              double* used_out, double* cos_out, PagedView pv, int use_paged,
-                              const int64_t* __restrict__ slots, int32_t* status) {
+// 128 threads per update block, three blocks per SM for the
+// register-resident rows (their four rows' raw vectors stay live across the
+// deviation pass)
+constexpr int kUpdThreads = 128;
+
+// fused update of one active row r (cached row indices[r]): weight, blend
+// (float64, no contraction), cast, write dense and/or paged records,
+// optional cosine.  G8 > 0 selects the 16-byte vector path, IT > 0 the
+// register-resident rows: the four rows are loaded once, before any
+// arithmetic, and -- when the blend weight is the stored one (previous_layer
+// mode) -- the deviation, the blend and the cosine share one pass over them.
+template <typename T, int G8, int IT>
+__device__ __forceinline__ void update_row(
+    Rows<T> ck, Rows<T> cv, Rows<T> fk, Rows<T> fv, int64_t idx, int64_t r, int64_t heads,
+    int64_t dim, const double* __restrict__ alpha, const uint8_t* __restrict__ mandatory,
+    int same_layer, double eps, int clamp, T* fused_k, T* fused_v, double* next_alpha_out,
+    double* used_out, double* cos_out, PagedView pv, int use_paged, int64_t slot,
+    int32_t* status) {
   const int lane = threadIdx.x & 31;
-  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < a;
-       r += warps) {
-    const int64_t idx = indices[r];
-    double dev, nrm;
-    bool bad;
+  const bool slot_ok = !use_paged || pv.valid(slot);
+  if (use_paged && !slot_ok && lane == 0) report(status, CS_ST_SLOT_RANGE);
+  const bool man = mandatory[idx] != 0;
+  double dev, nrm, w, cs = 0.0;
+  bool bad = false;
+  // the weight from this row's deviation / norm (wca.py:65-93)
+  auto next_weight = [&]() {
+    double nx = dev / (nrm + eps);
+    if (clamp) nx = fmin(fmax(nx, 0.0), 1.0);
+    return nx;
+  };
+  if constexpr (IT > 0) {  // heads * G8 == 32 * IT: every lane holds IT vectors
+    uint4 okr[IT], fkr[IT], ovr[IT], fvr[IT];
+    load_row<T, G8, IT>(ck, idx, okr);
+    load_row<T, G8, IT>(fk, r, fkr);
+    load_row<T, G8, IT>(cv, idx, ovr);
+    load_row<T, G8, IT>(fv, r, fvr);
+    // the pool has unit element strides on the vector path (vec16): head h
+    // element e of a record half is at base + h * hstride + e * sizeof(T)
+    char *pk = nullptr, *pvv = nullptr;
+    int64_t hstride = 0;
+    if (use_paged && slot_ok) pv.record(slot, pk, pvv, hstride);
+    double dp[IT], np[IT], cacc = 0.0;  // per-vector partial sums of dev / nrm
+    // vector `it` of the four rows: the K blend with its cosine partials (and
+    // the deviation sums when `acc`), then the V blend; V's inputs are
+    // checked through the fused values
+    auto vec = [&](int it, double wv, bool acc) {
+      const int g = it * 32 + lane;
+      const int64_t h = g / G8;
+      const int e = (g % G8) * 8;
+      const double wo = __dsub_rn(1.0, wv);
+      double dot = 0.0, aa = 0.0, bb = 0.0;
+      alignas(16) T y[8];
+      if (acc) dp[it] = np[it] = 0.0;
+      {
+        double o8[8], f8[8];
+        widen8<T>(okr[it], o8);
+        widen8<T>(fkr[it], f8);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          if (acc) {
+            const double df = __dsub_rn(f8[k], o8[k]);
+            dp[it] = __dadd_rn(dp[it], __dmul_rn(df, df));
+            np[it] = __dadd_rn(np[it], __dmul_rn(o8[k], o8[k]));
+          }
+          y[k] = Elem<T>::from_d(__dadd_rn(__dmul_rn(wv, f8[k]), __dmul_rn(wo, o8[k])));
+          bad |= nonfinite_bits(y[k]);
+          dot = __dadd_rn(dot, __dmul_rn(f8[k], o8[k]));
+          aa = __dadd_rn(aa, __dmul_rn(f8[k], f8[k]));
+          bb = __dadd_rn(bb, __dmul_rn(o8[k], o8[k]));
+        }
+        const uint4 uk = *reinterpret_cast<const uint4*>(y);
+        if (fused_k) *reinterpret_cast<uint4*>(fused_k + (r * heads + h) * dim + e) = uk;
+        if (pk) *reinterpret_cast<uint4*>(pk + h * hstride + e * (int64_t)sizeof(T)) = uk;
+      }
+      {
+        double o8[8], f8[8];
+        widen8<T>(ovr[it], o8);
+        widen8<T>(fvr[it], f8);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          y[k] = Elem<T>::from_d(__dadd_rn(__dmul_rn(wv, f8[k]), __dmul_rn(wo, o8[k])));
+          bad |= nonfinite_bits(y[k]);
+        }
+        const uint4 uv = *reinterpret_cast<const uint4*>(y);
+        if (fused_v) *reinterpret_cast<uint4*>(fused_v + (r * heads + h) * dim + e) = uv;
+        if (pvv) *reinterpret_cast<uint4*>(pvv + h * hstride + e * (int64_t)sizeof(T)) = uv;
+      }
+      if (cos_out) {
+        group_sum3<G8>(dot, aa, bb);
+        if ((lane % G8) == 0) cacc += head_cos(dot, aa, bb);
+      }
+    };
+    if (!same_layer) {  // the stored weight: one pass
+      w = man ? 1.0 : alpha[idx];
+#pragma unroll
+      for (int it = 0; it < IT; ++it) vec(it, w, true);
+      dev = warp_sum(tree_sum<IT>(dp));
+      nrm = warp_sum(tree_sum<IT>(np));
+    } else {  // this layer's weight: the deviation first
+      bad |= !dev_nrm_regs<T, IT>(okr, fkr, dev, nrm);
+      w = man ? 1.0 : next_weight();
+#pragma unroll
+      for (int it = 0; it < IT; ++it) vec(it, w, false);
+    }
+    bad |= !isfinite(dev) || !isfinite(nrm);  // 16-bit rows: the inputs' finiteness
+    if (cos_out) cs = warp_sum(cacc) / (double)heads;
+  } else {
     if constexpr (G8 > 0)
       bad = !row_dev_nrm_vec<T, G8>(ck, idx, fk, r, heads, dev, nrm);
     else
       bad = !row_dev_nrm(ck, idx, fk, r, heads, dim, dev, nrm);
-    double den = nrm + eps;
-    double nxt = dev / den;
-    bad |= !finite(dev) || !finite(den) || !finite(nxt);
-    if (clamp) nxt = fmin(fmax(nxt, 0.0), 1.0);
-    double w = mandatory[idx] ? 1.0 : (same_layer ? nxt : alpha[idx]);
-    double wo = __dsub_rn(1.0, w);
-    int64_t slot = use_paged ? slots[r] : 0;
-    bool slot_ok = !use_paged || pv.valid(slot);
-    if (use_paged && !slot_ok && lane == 0) report(status, CS_ST_SLOT_RANGE);
-    double cs = 0.0;
+    w = man ? 1.0 : (same_layer ? next_weight() : alpha[idx]);
+    const double wo = __dsub_rn(1.0, w);
     if constexpr (G8 > 0) {
-      // one read of the four rows: blend K and V, K cosine of fresh vs cached
+      // blend K and V, K cosine of fresh vs cached, from one read of the rows
       double cacc = 0.0;
       const int64_t groups = heads * G8;
       for (int64_t g0 = 0; g0 < groups; g0 += 32) {
@@ -789,7 +964,7 @@ __global__ void update_kernel(Rows<T> ck, Rows<T> cv, Rows<T> fk, Rows<T> fv,
           for (int k = 0; k < 8; ++k) {
             yk[k] = Elem<T>::from_d(__dadd_rn(__dmul_rn(w, fk8[k]), __dmul_rn(wo, ok8[k])));
             yv[k] = Elem<T>::from_d(__dadd_rn(__dmul_rn(w, fv8[k]), __dmul_rn(wo, ov8[k])));
-            bad |= !isfinite(Elem<T>::to_d(yk[k])) || !isfinite(Elem<T>::to_d(yv[k]));
+            bad |= nonfinite_bits(yk[k]) || nonfinite_bits(yv[k]);
             dot = __dadd_rn(dot, __dmul_rn(fk8[k], ok8[k]));
             aa = __dadd_rn(aa, __dmul_rn(fk8[k], fk8[k]));
             bb = __dadd_rn(bb, __dmul_rn(ok8[k], ok8[k]));
@@ -823,7 +998,7 @@ __global__ void update_kernel(Rows<T> ck, Rows<T> cv, Rows<T> fk, Rows<T> fv,
             double x = __dadd_rn(__dmul_rn(w, Elem<T>::to_d(fp[e])),
                                  __dmul_rn(wo, Elem<T>::to_d(op[e])));
             T y = Elem<T>::from_d(x);
-            bad |= !isfinite(Elem<T>::to_d(y));
+            bad |= nonfinite_bits(y);
             if (dst) dst[(r * heads + h) * dim + e] = y;
             if (use_paged && slot_ok)
               *reinterpret_cast<T*>(pv.addr(slot, h, half * dim + e)) = y;
@@ -832,13 +1007,33 @@ __global__ void update_kernel(Rows<T> ck, Rows<T> cv, Rows<T> fk, Rows<T> fv,
       }
       if (cos_out) cs = row_cosine(fk, r, ck, idx, heads, dim);
     }
-    bad = __any_sync(0xffffffffu, bad);
-    if (lane == 0) {
-      if (bad) report(status, CS_ST_NONFINITE);
-      if (next_alpha_out) next_alpha_out[r] = nxt;
-      if (used_out) used_out[r] = w;
-      if (cos_out) cos_out[r] = cs;
-    }
+  }
+  const double den = nrm + eps;
+  const double nxt = next_weight();
+  bad |= !finite(dev) || !finite(den) || !finite(dev / den);
+  bad = __any_sync(0xffffffffu, bad);
+  if (lane == 0) {
+    if (bad) report(status, CS_ST_NONFINITE);
+    if (next_alpha_out) next_alpha_out[r] = nxt;
+    if (used_out) used_out[r] = w;
+    if (cos_out) cos_out[r] = cs;
+  }
+}
+
+template <typename T, int G8, int IT>
+__global__ void __launch_bounds__(kUpdThreads, IT > 0 ? 2 : 1) update_kernel(Rows<T> ck, Rows<T> cv, Rows<T> fk, Rows<T> fv,
+                              const int64_t* __restrict__ indices, int64_t a, int64_t heads,
+                              int64_t dim, const double* __restrict__ alpha,
+                              const uint8_t* __restrict__ mandatory, int same_layer, double eps,
+                              int clamp, T* fused_k, T* fused_v, double* next_alpha_out,
+                              double* used_out, double* cos_out, PagedView pv, int use_paged,
+                              const int64_t* __restrict__ slots, int32_t* status) {
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < a;
+       r += warps) {
+    update_row<T, G8, IT>(ck, cv, fk, fv, indices[r], r, heads, dim, alpha, mandatory,
+                          same_layer, eps, clamp, fused_k, fused_v, next_alpha_out, used_out,
+                          cos_out, pv, use_paged, use_paged ? slots[r] : 0, status);
   }
 }
 
@@ -859,13 +1054,13 @@ __global__ void __launch_bounds__(kSelectThreads)
   if (threadIdx.x == 0 && count_out) *count_out = k;
 }
 
-__global__ void __launch_bounds__(kSelectThreads)
-    commit_kernel(const int64_t* __restrict__ indices, int64_t a,
-                  const double* __restrict__ next_alpha, const double* __restrict__ cosv,
-                  double thr, int distance_mode, int64_t n, int64_t budget,
-                  const double* __restrict__ initial, double* alpha, uint8_t* candidate,
-                  uint8_t* selected, uint8_t* removed, int64_t* removed_out,
-                  int64_t* promoted_out, int64_t* counts_out, int32_t* status) {
+// the commit of one request by the whole block (kSelectThreads threads)
+__device__ __forceinline__ void commit_block(
+    const int64_t* __restrict__ indices, int64_t a, const double* __restrict__ next_alpha,
+    const double* __restrict__ cosv, double thr, int distance_mode, int64_t n, int64_t budget,
+    const double* __restrict__ initial, double* alpha, uint8_t* candidate, uint8_t* selected,
+    uint8_t* removed, int64_t* removed_out, int64_t* promoted_out, int64_t* counts_out,
+    int32_t* status) {
   extern __shared__ __align__(16) unsigned char dyn[];
   __shared__ SelectSmem sm;
   __shared__ int removed_count;
@@ -919,6 +1114,141 @@ __global__ void __launch_bounds__(kSelectThreads)
   }
 }
 
+__global__ void __launch_bounds__(kSelectThreads)
+    commit_kernel(const int64_t* __restrict__ indices, int64_t a,
+                  const double* __restrict__ next_alpha, const double* __restrict__ cosv,
+                  double thr, int distance_mode, int64_t n, int64_t budget,
+                  const double* __restrict__ initial, double* alpha, uint8_t* candidate,
+                  uint8_t* selected, uint8_t* removed, int64_t* removed_out,
+                  int64_t* promoted_out, int64_t* counts_out, int32_t* status) {
+  commit_block(indices, a, next_alpha, cosv, thr, distance_mode, n, budget, initial, alpha,
+               candidate, selected, removed, removed_out, promoted_out, counts_out, status);
+}
+
+// ------------------------------------------------------------ batched kernels
+// Several requests per launch (the calls of one step): each item holds one
+// request's arguments, rows are numbered across the requests (batch_item).
+constexpr int kBatch = kBatchItems;
+
+template <typename T>
+struct InitItem {
+  Rows<T> c, f;
+  const uint8_t* reused;
+  double* dev;
+  double* alpha;
+  uint8_t* candidate;
+  uint8_t* selected;
+  uint8_t* removed;
+  unsigned long long* counts;
+  int32_t* status;
+};
+
+template <typename T>
+struct InitBatch {
+  InitItem<T> it[kBatch];
+  int64_t start[kBatch + 1];
+  int count;
+};
+
+struct CountsBatch {
+  unsigned long long* counts[kBatch];
+  int count;
+};
+
+__global__ void zero_counts_kernel(const __grid_constant__ CountsBatch b) {
+  const int i = threadIdx.x;
+  if (i < b.count) b.counts[i][0] = b.counts[i][1] = 0ull;
+}
+
+// cs_wca_initialize of every item: one warp per row, the counts gathered
+// per block and request
+template <typename T, int G8, int IT>
+__global__ void __launch_bounds__(256, IT > 0 ? 3 : 1)
+    initialize_batch_kernel(const __grid_constant__ InitBatch<T> b, int64_t heads, int64_t dim,
+                            double eps, int clamp) {
+  __shared__ unsigned long long cnt[kBatch][2];
+  for (int i = threadIdx.x; i < 2 * kBatch; i += blockDim.x) cnt[i >> 1][i & 1] = 0ull;
+  __syncthreads();
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int64_t total = b.start[b.count];
+  for (int64_t g = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); g < total;
+       g += warps) {
+    const int i = batch_item(b.start, b.count, g);
+    const InitItem<T>& q = b.it[i];
+    const int64_t r = g - b.start[i];
+    double dev, nrm;
+    const bool in_ok = row_dev<T, G8, IT>(q.c, r, q.f, r, heads, dim, dev, nrm);
+    if ((threadIdx.x & 31) == 0) {
+      if (q.selected) q.selected[r] = 0;
+      if (q.removed) q.removed[r] = 0;
+      const int fl = dev_epilogue(r, dev, nrm, in_ok, eps, clamp, q.dev, q.alpha, q.reused,
+                                  q.candidate, q.status);
+      if (fl & 1) atomicAdd(&cnt[i][0], 1ull);
+      if (fl & 2) atomicAdd(&cnt[i][1], 1ull);
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 2 * b.count; i += blockDim.x) {
+    const unsigned long long v = cnt[i >> 1][i & 1];
+    if (v) atomicAdd(&b.it[i >> 1].counts[i & 1], v);
+  }
+}
+
+template <typename T>
+struct UpdItem {
+  Rows<T> ck, cv, fk, fv;
+  const int64_t* indices;
+  const double* alpha;
+  const uint8_t* mandatory;
+  T* fused_k;
+  T* fused_v;
+  double* next_alpha;
+  double* used;
+  double* cos;
+  const int64_t* slots;
+  int32_t* status;
+};
+
+template <typename T>
+struct UpdBatch {
+  UpdItem<T> it[kBatch];
+  int64_t start[kBatch + 1];
+  int count;
+};
+static_assert(sizeof(UpdBatch<double>) <= 32000, "batched update arguments exceed the parameter space");
+
+template <typename T, int G8, int IT>
+__global__ void __launch_bounds__(kUpdThreads, IT > 0 ? 3 : 1)
+    update_batch_kernel(const __grid_constant__ UpdBatch<T> b, int64_t heads, int64_t dim,
+                        int same_layer, double eps, int clamp, PagedView pv, int use_paged) {
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int64_t total = b.start[b.count];
+  for (int64_t g = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); g < total;
+       g += warps) {
+    const int i = batch_item(b.start, b.count, g);
+    const UpdItem<T>& q = b.it[i];
+    const int64_t r = g - b.start[i];
+    update_row<T, G8, IT>(q.ck, q.cv, q.fk, q.fv, q.indices[r], r, heads, dim, q.alpha,
+                          q.mandatory, same_layer, eps, clamp, q.fused_k, q.fused_v,
+                          q.next_alpha, q.used, q.cos, pv, use_paged,
+                          use_paged ? q.slots[r] : 0, q.status);
+  }
+}
+
+struct CommitBatch {
+  cs_wca_commit_item it[kBatch];
+  int count;
+};
+
+// one block per request
+__global__ void __launch_bounds__(kSelectThreads)
+    commit_batch_kernel(const __grid_constant__ CommitBatch b, double thr, int distance_mode) {
+  const cs_wca_commit_item& q = b.it[blockIdx.x];
+  commit_block(q.indices, q.a, q.next_alpha, q.cos, thr, distance_mode, q.n, q.budget,
+               q.initial_dev, q.alpha, q.candidate, q.selected, q.removed, q.removed_out,
+               q.promoted_out, q.counts_out, q.status);
+}
+
 constexpr size_t kSelectDynSmem = (sizeof(double) + sizeof(int)) * kSelectMaxChosen;
 
 bool select_smem_ready() {
@@ -928,6 +1258,9 @@ bool select_smem_ready() {
                              (int)kSelectDynSmem) != cudaSuccess)
       return false;
     if (cudaFuncSetAttribute(commit_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kSelectDynSmem) != cudaSuccess)
+      return false;
+    if (cudaFuncSetAttribute(commit_batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)kSelectDynSmem) != cudaSuccess)
       return false;
     done = true;
@@ -973,6 +1306,38 @@ void with_g8(int g8, F&& f) {
   f(std::integral_constant<int, 0>{});
 }
 
+// vectors per lane of a register-resident row: IT = heads * G8 / 32 when it
+// is exact and small (1, 2 or 4) and G8 is 8 or 16; 0 otherwise
+inline int row_iters(int g8, int64_t heads) {
+  if (g8 != 8 && g8 != 16) return 0;
+  const int64_t groups = heads * g8;
+  if (groups % 32) return 0;
+  const int64_t it = groups / 32;
+  return (it == 1 || it == 2 || it == 4) ? (int)it : 0;
+}
+
+// call f(G8, IT) with std::integral_constant arguments (0, 0: scalar path)
+template <typename T, typename F>
+void with_vec(int g8, int it, F&& f) {
+  using std::integral_constant;
+  if constexpr (sizeof(T) == 2) {
+    switch (g8 * 8 + it) {
+      case 4 * 8: f(integral_constant<int, 4>{}, integral_constant<int, 0>{}); return;
+      case 8 * 8: f(integral_constant<int, 8>{}, integral_constant<int, 0>{}); return;
+      case 8 * 8 + 1: f(integral_constant<int, 8>{}, integral_constant<int, 1>{}); return;
+      case 8 * 8 + 2: f(integral_constant<int, 8>{}, integral_constant<int, 2>{}); return;
+      case 8 * 8 + 4: f(integral_constant<int, 8>{}, integral_constant<int, 4>{}); return;
+      case 16 * 8: f(integral_constant<int, 16>{}, integral_constant<int, 0>{}); return;
+      case 16 * 8 + 1: f(integral_constant<int, 16>{}, integral_constant<int, 1>{}); return;
+      case 16 * 8 + 2: f(integral_constant<int, 16>{}, integral_constant<int, 2>{}); return;
+      case 16 * 8 + 4: f(integral_constant<int, 16>{}, integral_constant<int, 4>{}); return;
+      case 32 * 8: f(integral_constant<int, 32>{}, integral_constant<int, 0>{}); return;
+      default: break;
+    }
+  }
+  f(integral_constant<int, 0>{}, integral_constant<int, 0>{});
+}
+
 template <typename T>
 Rows<T> rows_of(const void* p, int64_t srow, int64_t shead) {
   return Rows<T>{static_cast<const char*>(p), srow * (int64_t)sizeof(T),
@@ -1006,8 +1371,8 @@ extern "C" int cs_wca_deviation(const void* cached, int64_t c_stride_row, int64_
   CS_DISPATCH_FLOAT(dtype, T, {
     const int g8 = vec_groups<T>(dim, {cached, fresh},
                                  {c_stride_row, c_stride_head, f_stride_row, f_stride_head});
-    with_g8<T>(g8, [&](auto G) {
-      deviation_kernel<T, decltype(G)::value>
+    with_vec<T>(g8, row_iters(g8, heads), [&](auto G, auto I) {
+      deviation_kernel<T, decltype(G)::value, decltype(I)::value>
           <<<row_grid(n, threads / 32), threads, 0, as_stream(stream)>>>(
               rows_of<T>(cached, c_stride_row, c_stride_head), cached_rows,
               rows_of<T>(fresh, f_stride_row, f_stride_head), n, heads, dim, epsilon, clamp,
@@ -1036,8 +1401,9 @@ extern "C" int cs_wca_initialize(const void* cached, int64_t c_stride_row, int64
   CS_DISPATCH_FLOAT(dtype, T, {
     const int g8 = vec_groups<T>(dim, {cached, fresh},
                                  {c_stride_row, c_stride_head, f_stride_row, f_stride_head});
-    with_g8<T>(g8, [&](auto G) {
-      deviation_kernel<T, decltype(G)::value><<<row_grid(n, threads / 32), threads, 0, s>>>(
+    with_vec<T>(g8, row_iters(g8, heads), [&](auto G, auto I) {
+      deviation_kernel<T, decltype(G)::value, decltype(I)::value>
+          <<<row_grid(n, threads / 32), threads, 0, s>>>(
           rows_of<T>(cached, c_stride_row, c_stride_head), nullptr,
           rows_of<T>(fresh, f_stride_row, f_stride_head), n, heads, dim, epsilon, clamp,
           dev_out, alpha_out, reused, candidate,
@@ -1160,14 +1526,13 @@ extern "C" int cs_wca_update(const void* cached_k, const void* cached_v, int64_t
     pv = PagedView::make(*kv);
     use_paged = 1;
   }
-  const int threads = 256;
   CS_DISPATCH_FLOAT(dtype, T, {
     int g8 = vec_groups<T>(dim, {cached_k, cached_v, fresh_k, fresh_v, fused_k, fused_v},
                            {c_stride_row, c_stride_head, f_stride_row, f_stride_head});
     if (use_paged && !pv.vec16()) g8 = 0;
-    with_g8<T>(g8, [&](auto G) {
-      update_kernel<T, decltype(G)::value>
-          <<<row_grid(a, threads / 32), threads, 0, as_stream(stream)>>>(
+    with_vec<T>(g8, row_iters(g8, heads), [&](auto G, auto I) {
+      update_kernel<T, decltype(G)::value, decltype(I)::value>
+          <<<row_grid(a, kUpdThreads / 32), kUpdThreads, 0, as_stream(stream)>>>(
               rows_of<T>(cached_k, c_stride_row, c_stride_head),
               rows_of<T>(cached_v, c_stride_row, c_stride_head),
               rows_of<T>(fresh_k, f_stride_row, f_stride_head),
@@ -1197,5 +1562,140 @@ extern "C" int cs_wca_commit(const int64_t* indices, int64_t a, const double* ne
       indices, a, next_alpha, cos, threshold, distance_mode, n, budget, initial_dev, alpha,
       candidate, selected, removed, removed_out, promoted_out, counts_out, status);
   CS_LAUNCH_CHECK();
+  return CS_OK;
+}
+
+// ------------------------------------------------------------ batched calls
+extern "C" int cs_wca_initialize_batch(const cs_wca_initialize_item* items, int32_t count,
+                                       int64_t heads, int64_t dim, int32_t dtype, double epsilon,
+                                       int32_t clamp, void* stream) {
+  CS_HOST_CHECK(count >= 0 && (count == 0 || items) && heads > 0 && dim > 0);
+  for (int32_t i = 0; i < count; ++i) {
+    const cs_wca_initialize_item& q = items[i];
+    CS_HOST_CHECK(q.n >= 0 && q.counts_out && q.candidate && q.reused);
+    CS_HOST_CHECK(q.n == 0 || (q.cached && q.fresh));
+  }
+  auto s = as_stream(stream);
+  CS_DISPATCH_FLOAT(dtype, T, {
+    for (int32_t first = 0; first < count; first += kBatch) {
+      const int m = count - first < kBatch ? count - first : kBatch;
+      CountsBatch z{};
+      z.count = m;
+      InitBatch<T> b{};  // copied into the kernel's parameter space by the launch
+      b.count = m;
+      b.start[0] = 0;
+      int g8 = -1;
+      for (int j = 0; j < m; ++j) {
+        const cs_wca_initialize_item& q = items[first + j];
+        z.counts[j] = reinterpret_cast<unsigned long long*>(q.counts_out);
+        b.it[j] = InitItem<T>{rows_of<T>(q.cached, q.c_stride_row, q.c_stride_head),
+                              rows_of<T>(q.fresh, q.f_stride_row, q.f_stride_head),
+                              q.reused, q.dev_out, q.alpha_out, q.candidate, q.selected,
+                              q.removed, z.counts[j], q.status};
+        b.start[j + 1] = b.start[j] + q.n;
+        if (q.n == 0) continue;
+        const int gj = vec_groups<T>(dim, {q.cached, q.fresh},
+                                     {q.c_stride_row, q.c_stride_head, q.f_stride_row,
+                                      q.f_stride_head});
+        g8 = g8 < 0 ? gj : (g8 == gj ? g8 : 0);
+      }
+      zero_counts_kernel<<<1, kBatch, 0, s>>>(z);
+      CS_LAUNCH_CHECK();
+      const int64_t total = b.start[m];
+      if (total == 0) continue;
+      const int threads = 256;
+      with_vec<T>(g8 < 0 ? 0 : g8, row_iters(g8 < 0 ? 0 : g8, heads), [&](auto G, auto I) {
+        initialize_batch_kernel<T, decltype(G)::value, decltype(I)::value>
+            <<<row_grid(total, threads / 32), threads, 0, s>>>(b, heads, dim, epsilon, clamp);
+      });
+      CS_LAUNCH_CHECK();
+    }
+  });
+  return CS_OK;
+}
+
+extern "C" int cs_wca_update_batch(const cs_wca_update_item* items, int32_t count, int64_t heads,
+                                   int64_t dim, int32_t dtype, int32_t same_layer, double epsilon,
+                                   int32_t clamp, const cs_paged_kv* kv, void* stream) {
+  CS_HOST_CHECK(count >= 0 && (count == 0 || items) && heads > 0 && dim > 0);
+  PagedView pv{};
+  int use_paged = 0;
+  if (kv != nullptr) {
+    CS_HOST_CHECK(kv->cache && kv->dtype == dtype && kv->head_dim == dim &&
+                  kv->kv_heads == heads && kv->block_size > 0);
+    pv = PagedView::make(*kv);
+    use_paged = 1;
+  }
+  for (int32_t i = 0; i < count; ++i) {
+    const cs_wca_update_item& q = items[i];
+    CS_HOST_CHECK(q.a >= 0);
+    if (q.a == 0) continue;
+    CS_HOST_CHECK(q.cached_k && q.cached_v && q.fresh_k && q.fresh_v && q.indices && q.alpha &&
+                  q.mandatory);
+    CS_HOST_CHECK((q.fused_k == nullptr) == (q.fused_v == nullptr));
+    CS_HOST_CHECK(!use_paged || q.slots);
+  }
+  auto s = as_stream(stream);
+  CS_DISPATCH_FLOAT(dtype, T, {
+    for (int32_t first = 0; first < count; first += kBatch) {
+      const int m = count - first < kBatch ? count - first : kBatch;
+      UpdBatch<T> b{};  // copied into the kernel's parameter space by the launch
+      b.count = m;
+      b.start[0] = 0;
+      int g8 = -1;
+      for (int j = 0; j < m; ++j) {
+        const cs_wca_update_item& q = items[first + j];
+        b.it[j] = UpdItem<T>{rows_of<T>(q.cached_k, q.c_stride_row, q.c_stride_head),
+                             rows_of<T>(q.cached_v, q.c_stride_row, q.c_stride_head),
+                             rows_of<T>(q.fresh_k, q.f_stride_row, q.f_stride_head),
+                             rows_of<T>(q.fresh_v, q.f_stride_row, q.f_stride_head),
+                             q.indices, q.alpha, q.mandatory, static_cast<T*>(q.fused_k),
+                             static_cast<T*>(q.fused_v), q.next_alpha_out, q.used_alpha_out,
+                             q.cos_out, q.slots, q.status};
+        b.start[j + 1] = b.start[j] + q.a;
+        if (q.a == 0) continue;
+        int gj = vec_groups<T>(dim, {q.cached_k, q.cached_v, q.fresh_k, q.fresh_v, q.fused_k,
+                                     q.fused_v},
+                               {q.c_stride_row, q.c_stride_head, q.f_stride_row,
+                                q.f_stride_head});
+        g8 = g8 < 0 ? gj : (g8 == gj ? g8 : 0);
+      }
+      const int64_t total = b.start[m];
+      if (total == 0) continue;
+      if (g8 < 0 || (use_paged && !pv.vec16())) g8 = 0;
+      with_vec<T>(g8, row_iters(g8, heads), [&](auto G, auto I) {
+        update_batch_kernel<T, decltype(G)::value, decltype(I)::value>
+            <<<row_grid(total, kUpdThreads / 32), kUpdThreads, 0, s>>>(
+                b, heads, dim, same_layer, epsilon, clamp, pv, use_paged);
+      });
+      CS_LAUNCH_CHECK();
+    }
+  });
+  return CS_OK;
+}
+
+extern "C" int cs_wca_commit_batch(const cs_wca_commit_item* items, int32_t count,
+                                   double threshold, int32_t distance_mode, void* stream) {
+  CS_HOST_CHECK(count >= 0 && (count == 0 || items));
+  for (int32_t i = 0; i < count; ++i) {
+    const cs_wca_commit_item& q = items[i];
+    CS_HOST_CHECK(q.a >= 0 && q.n >= 0 && q.budget >= 0 && q.counts_out);
+    CS_HOST_CHECK(q.n == 0 || (q.initial_dev && q.alpha && q.candidate && q.selected &&
+                               q.removed));
+    CS_HOST_CHECK(q.a == 0 || (q.indices && q.next_alpha));
+    if (q.promoted_out != nullptr && (q.budget < q.n ? q.budget : q.n) > kSelectMaxChosen)
+      return CS_ERR_UNSUPPORTED;
+  }
+  if (count == 0) return CS_OK;
+  if (!select_smem_ready()) return CS_ERR_CUDA;
+  auto s = as_stream(stream);
+  for (int32_t first = 0; first < count; first += kBatch) {
+    CommitBatch b{};
+    b.count = count - first < kBatch ? count - first : kBatch;
+    for (int j = 0; j < b.count; ++j) b.it[j] = items[first + j];
+    commit_batch_kernel<<<b.count, kSelectThreads, kSelectDynSmem, s>>>(b, threshold,
+                                                                        distance_mode);
+    CS_LAUNCH_CHECK();
+  }
   return CS_OK;
 }

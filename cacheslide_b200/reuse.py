@@ -136,11 +136,18 @@ class ReuseStep:
     launch (``cs_cope_attn_prefill_batch``, heaviest query tiles of every
     request first) once every request's WCA / SLIDE chain is done, instead of
     one launch per request on the request's stream (the default: the
-    per-request launches overlap the other requests' WCA / SLIDE kernels)."""
+    per-request launches overlap the other requests' WCA / SLIDE kernels).
 
-    def __init__(self, work: SyntheticWorkload, batched_attention: bool = False):
+    ``batched``: every stage runs as one launch for all requests on the
+    caller's stream -- snapshot scatter (``cs_slide_scatter_batch``), WCA
+    initialize, select, update and commit (``cs_wca_*_batch``) and the
+    attention -- seven launches per step whatever the request count."""
+
+    def __init__(self, work: SyntheticWorkload, batched_attention: bool = False,
+                 batched: bool = False):
         self.work = work
-        self.batched_attention = batched_attention
+        self.batched = batched
+        self.batched_attention = batched_attention or batched
         cfg = work.cfg
         dev = work.device
         self.lib = N.load()
@@ -172,7 +179,7 @@ class ReuseStep:
             r.active = torch.nonzero(r.selected | r.mandatory).flatten()
             a = r.active.numel()
             r.a = a
-            r.q =r.q_all[r.active].contiguous()
+            r.q = r.q_all[r.active].contiguous()
             r.fk = r.fresh_k[r.active].contiguous()
             r.fv = r.fresh_v[r.active].contiguous()
             r.active_slots = r.slots[r.active].contiguous()
@@ -200,11 +207,67 @@ class ReuseStep:
         self.dec_v = torch.cat([r.decode_v for r in reqs]).contiguous()
         self.dec_slots = torch.stack([r.slots_all[n] for r in reqs]).contiguous()
         self.gate_layer = True  # exercise the cosine gate in every timed step
+        self._batch_items()
         # one stream per request: the launch chains touch disjoint slots of the
         # shared pool and their own WCA state, so they overlap on the device
         self.streams = [torch.cuda.Stream(device=dev) for _ in reqs]
         self._fork = torch.cuda.Event()
         self._joins = [torch.cuda.Event() for _ in reqs]
+
+    def _batch_items(self) -> None:
+        """The per-request arguments of the batched launches (all pointers
+        stay valid for the step's lifetime)."""
+        c, reqs = self.work.cfg, self.work.requests
+        p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+        self.scatter_items = (N.ScatterItem * len(reqs))(*[N.ScatterItem(
+            p(r.slots), None, c.seq, p(r.cached_k), p(r.cached_v), r.cached_k.stride(0),
+            r.cached_k.stride(1), r.status_ptr) for r in reqs])
+        self.init_items = (N.InitializeItem * len(reqs))(*[N.InitializeItem(
+            p(r.cached_k), r.cached_k.stride(0), r.cached_k.stride(1), p(r.calib_k),
+            r.calib_k.stride(0), r.calib_k.stride(1), c.seq, p(r.reused), p(r.dev), p(r.alpha),
+            p(r.candidate), p(r.selected), p(r.removed), p(r.counts), r.status_ptr)
+            for r in reqs])
+        self.select_items = (N.CommitItem * len(reqs))(*[N.CommitItem(
+            None, 0, None, None, c.seq, r.budget, p(r.dev), p(r.alpha), p(r.candidate),
+            p(r.selected), p(r.removed), None, p(r.promoted), p(r.counts2), r.status_ptr)
+            for r in reqs])
+        self.update_items = (N.UpdateItem * len(reqs))(*[N.UpdateItem(
+            p(r.cached_k), p(r.cached_v), r.cached_k.stride(0), r.cached_k.stride(1), p(r.fk),
+            p(r.fv), r.fk.stride(0), r.fk.stride(1), p(r.active), r.a, p(r.alpha),
+            p(r.mandatory), None, None, p(r.next_alpha), p(r.used_alpha),
+            p(r.cos) if self.gate_layer else None, p(r.active_slots), r.status_ptr)
+            for r in reqs])
+        self.commit_items = (N.CommitItem * len(reqs))(*[N.CommitItem(
+            p(r.active), r.a, p(r.next_alpha), p(r.cos) if self.gate_layer else None, c.seq,
+            r.budget, p(r.dev), p(r.alpha), p(r.candidate), p(r.selected), p(r.removed),
+            p(r.removed_list), p(r.promoted), p(r.counts2), r.status_ptr) for r in reqs])
+
+    # -------------------------------------------------------------- batched
+    def scatter_all(self, stream) -> None:
+        N.check(self.lib.cs_slide_scatter_batch(
+            ctypes.byref(self.kv), self.scatter_items, len(self.scatter_items), stream),
+            "cs_slide_scatter_batch")
+
+    def initialize_all(self, stream) -> None:
+        c = self.work.cfg
+        N.check(self.lib.cs_wca_initialize_batch(
+            self.init_items, len(self.init_items), c.kv_heads, c.head_dim, N.DTYPES[c.dtype],
+            1e-8, 0, stream), "cs_wca_initialize_batch")
+
+    def select_all(self, stream) -> None:
+        N.check(self.lib.cs_wca_commit_batch(
+            self.select_items, len(self.select_items), 0.12, 0, stream), "cs_wca_commit_batch")
+
+    def update_all(self, stream) -> None:
+        c = self.work.cfg
+        N.check(self.lib.cs_wca_update_batch(
+            self.update_items, len(self.update_items), c.kv_heads, c.head_dim,
+            N.DTYPES[c.dtype], 0, 1e-8, 0, ctypes.byref(self.kv), stream),
+            "cs_wca_update_batch")
+
+    def commit_all(self, stream) -> None:
+        N.check(self.lib.cs_wca_commit_batch(
+            self.commit_items, len(self.commit_items), 0.12, 0, stream), "cs_wca_commit_batch")
 
     # -------------------------------------------------------------- pieces
     def _initialize_all(self, stream) -> None:
@@ -325,7 +388,8 @@ class ReuseStep:
             return
         N.check(rc, "cs_cope_attn_prefill_batch")
 
-    def run(self, stream: int | None = None, before=None, after=None) -> list[torch.Tensor]:
+    def run(self, stream: int | None = None, before=None, after=None,
+            batched: bool | None = None) -> list[torch.Tensor]:
         """One reuse-prefill layer for every request; returns the outputs.
 
         Each request's launches go to its own stream, which first waits for
@@ -333,12 +397,30 @@ class ReuseStep:
         caller's stream then waits for every request, so work queued on it
         afterwards sees all outputs.  ``before(request, stream)`` and
         ``after(request, stream)`` run with that request's stream current
-        around its launches (host <-> device staging of its tensors)."""
+        around its launches (host <-> device staging of its tensors).
+        ``batched`` overrides the step's schedule for this call (the batched
+        launches, or the per-request streams whose staging copies overlap
+        the other requests' kernels)."""
         dev = self.work.device
         main = (torch.cuda.current_stream(dev) if stream is None
                 else torch.cuda.ExternalStream(stream, device=dev))
+        if self.batched if batched is None else batched:
+            s = main.cuda_stream
+            if before is not None:
+                for r in self.work.requests:
+                    before(r, main)
+            self.scatter_all(s)
+            self.initialize_all(s)
+            self.select_all(s)
+            self.update_all(s)
+            self.commit_all(s)
+            self.attention_all(s)
+            if after is not None:
+                for r in self.work.requests:
+                    after(r, main)
+            return [r.out for r in self.work.requests]
         self._fork.record(main)
-        batched = self.batched_attention
+        batched = self.batched_attention and batched is not False
         for r, rs, done in zip(self.work.requests, self.streams, self._joins):
             rs.wait_event(self._fork)
             s = rs.cuda_stream

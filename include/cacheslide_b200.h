@@ -105,6 +105,30 @@ CS_API int cs_slide_relocate(const cs_paged_kv* kv, const int64_t* src_slots,
                       const int64_t* dst_slots, int64_t n, int32_t* status,
                       void* stream);
 
+/*
+ * One request of a batched SLIDE scatter: the arguments of cs_slide_scatter
+ * that differ between requests (strides in elements).
+ */
+typedef struct {
+  const int64_t* slots;
+  const int64_t* rows; /* or NULL */
+  int64_t n;
+  const void* k;
+  const void* v;
+  int64_t in_stride_row, in_stride_head;
+  int32_t* status;
+} cs_slide_scatter_item;
+
+/*
+ * cs_slide_scatter for `count` requests into one shared paged pool, in one
+ * launch per 64 requests: the baseline-snapshot writes of every
+ * request of a step (NativePagedKV.load_baseline -> _write_slots,
+ * paged.py:205-240, once per request in the reference).  The requests'
+ * slot sets must be disjoint.
+ */
+CS_API int cs_slide_scatter_batch(const cs_paged_kv* kv, const cs_slide_scatter_item* items,
+                                  int32_t count, void* stream);
+
 /* ------------------------------------------------------------------ WCA */
 /*
  * Per-token squared deviation and adaptation weight in float64
@@ -228,6 +252,79 @@ CS_API int cs_wca_commit(const int64_t* indices, int64_t a, const double* next_a
                   uint8_t* removed, int64_t* removed_out,
                   int64_t* promoted_out, int64_t* counts_out, int32_t* status,
                   void* stream);
+
+/*
+ * Batched WCA: the per-request calls of one step (one WCAState per request
+ * in the reference, wca.py:152-366) as one launch per 64 requests.  Each
+ * item holds the arguments of the single call
+ * that differ between requests; the shared ones are function arguments.
+ * Results are identical to `count` single calls.
+ */
+typedef struct {
+  const void* cached;
+  int64_t c_stride_row, c_stride_head;
+  const void* fresh;
+  int64_t f_stride_row, f_stride_head;
+  int64_t n;
+  const uint8_t* reused;
+  double* dev_out;
+  double* alpha_out;
+  uint8_t* candidate;
+  uint8_t* selected; /* or NULL */
+  uint8_t* removed;  /* or NULL */
+  int64_t* counts_out;
+  int32_t* status;
+} cs_wca_initialize_item;
+
+CS_API int cs_wca_initialize_batch(const cs_wca_initialize_item* items, int32_t count,
+                                   int64_t heads, int64_t dim, int32_t dtype, double epsilon,
+                                   int32_t clamp, void* stream);
+
+typedef struct {
+  const void* cached_k;
+  const void* cached_v;
+  int64_t c_stride_row, c_stride_head;
+  const void* fresh_k;
+  const void* fresh_v;
+  int64_t f_stride_row, f_stride_head;
+  const int64_t* indices;
+  int64_t a;
+  const double* alpha;
+  const uint8_t* mandatory;
+  void* fused_k; /* or NULL (then fused_v NULL too) */
+  void* fused_v;
+  double* next_alpha_out;
+  double* used_alpha_out;
+  double* cos_out; /* or NULL */
+  const int64_t* slots; /* paged destination rows when kv != NULL */
+  int32_t* status;
+} cs_wca_update_item;
+
+/* all items share heads, dim, dtype, the update options and the paged pool */
+CS_API int cs_wca_update_batch(const cs_wca_update_item* items, int32_t count, int64_t heads,
+                               int64_t dim, int32_t dtype, int32_t same_layer, double epsilon,
+                               int32_t clamp, const cs_paged_kv* kv, void* stream);
+
+typedef struct {
+  const int64_t* indices; /* or NULL when a == 0 */
+  int64_t a;
+  const double* next_alpha;
+  const double* cos; /* or NULL */
+  int64_t n, budget;
+  const double* initial_dev;
+  double* alpha;
+  uint8_t* candidate;
+  uint8_t* selected;
+  uint8_t* removed;
+  int64_t* removed_out;  /* or NULL */
+  int64_t* promoted_out; /* or NULL */
+  int64_t* counts_out;
+  int32_t* status;
+} cs_wca_commit_item;
+
+/* one thread block per request; threshold and distance_mode are shared */
+CS_API int cs_wca_commit_batch(const cs_wca_commit_item* items, int32_t count, double threshold,
+                               int32_t distance_mode, void* stream);
 
 /* ------------------------------------------------------------ attention */
 typedef enum {
