@@ -99,6 +99,8 @@ def hot_bytes(work) -> dict:
     n = c.seq
     a = sum(r.a for r in work.requests) / len(work.requests)
     out["slide_scatter"] = 2 * 2 * n * rec  # read dense K,V + write paged K,V
+    out["slide_gather"] = 2 * 2 * n * rec  # read paged K,V + write dense K,V
+    out["slide_relocate"] = 2 * 2 * n * rec  # read and write paged K,V
     out["wca_initialize"] = 2 * n * rec  # read cached K + calib K
     out["wca_update"] = 3 * 2 * a * rec  # old + fresh + fused (K and V)
     out["decode_attention"] = (n + 1) * 2 * rec + c.q_heads * c.head_dim * 2 + (n + 1) * 8
@@ -402,6 +404,36 @@ def main():
                  "wca_select": each(step._select),
                  "wca_update": each(step.wca_update),
                  "wca_commit": each(step.wca_commit)}
+    # SLIDE gather and relocation of every request's records (n per request):
+    # gather into dense rows; relocate within a pool of twice the step's
+    # blocks, from the request's slots to the same slots in the second half
+    import ctypes
+
+    lib = N.load()
+    nblk = work.cache.shape[0]
+    pool = torch.zeros((2 * nblk,) + tuple(work.cache.shape[1:]), dtype=work.cache.dtype,
+                       device=dev)
+    pool[:nblk].copy_(work.cache)
+    pool_kv = N.paged_view(pool)
+    slots_per_pool = nblk * cfg.block
+    dst_slots = [(r.slots + slots_per_pool).contiguous() for r in work.requests]
+    gk = torch.empty(cfg.seq, cfg.kv_heads, cfg.head_dim, dtype=cfg.dtype, device=dev)
+    gv = torch.empty_like(gk)
+
+    def gather_all():
+        for r in work.requests:
+            N.check(lib.cs_slide_gather(ctypes.byref(step.kv), r.slots.data_ptr(), cfg.seq,
+                                        gk.data_ptr(), gv.data_ptr(), gk.stride(0),
+                                        gk.stride(1), r.status_ptr, s), "cs_slide_gather")
+
+    def relocate_all():
+        for r, d in zip(work.requests, dst_slots):
+            N.check(lib.cs_slide_relocate(ctypes.byref(pool_kv), r.slots.data_ptr(),
+                                          d.data_ptr(), cfg.seq, r.status_ptr, s),
+                    "cs_slide_relocate")
+
+    kinds["slide_gather"] = gather_all
+    kinds["slide_relocate"] = relocate_all
     for name, fn in kinds.items():
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                for _ in range(args.steps)]

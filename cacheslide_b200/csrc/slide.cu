@@ -155,13 +155,15 @@ __global__ void __launch_bounds__(256) scatter_rows_kernel(
       kx[k] = *reinterpret_cast<const uint4*>(in_k + off);
       vx[k] = *reinterpret_cast<const uint4*>(in_v + off);
     }
+    char *dk, *dv;
+    int64_t hs;
+    pv.record(s, dk, dv, hs);  // one block / sidecar lookup per row
 #pragma unroll
     for (int k = 0; k < UPL; ++k) {
       const int q = lane + 32 * k;
-      const int h = q >> uh_shift;
-      const int64_t e = (int64_t)(q & uh_mask) * (16 / pv.esize);
-      *reinterpret_cast<uint4*>(pv.addr(s, h, e)) = kx[k];
-      *reinterpret_cast<uint4*>(pv.addr(s, h, pv.head_dim + e)) = vx[k];
+      const int64_t off = (int64_t)(q >> uh_shift) * hs + (q & uh_mask) * 16;
+      *reinterpret_cast<uint4*>(dk + off) = kx[k];
+      *reinterpret_cast<uint4*>(dv + off) = vx[k];
     }
   }
 }
@@ -181,14 +183,16 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(
       if (lane == 0) report(status, CS_ST_SLOT_RANGE);
       continue;
     }
+    char *sk, *sv;
+    int64_t hs;
+    pv.record(s, sk, sv, hs);  // one block / sidecar lookup per row
     uint4 kx[UPL], vx[UPL];
 #pragma unroll
     for (int k = 0; k < UPL; ++k) {
       const int q = lane + 32 * k;
-      const int h = q >> uh_shift;
-      const int64_t e = (int64_t)(q & uh_mask) * (16 / pv.esize);
-      kx[k] = *reinterpret_cast<const uint4*>(pv.addr(s, h, e));
-      vx[k] = *reinterpret_cast<const uint4*>(pv.addr(s, h, pv.head_dim + e));
+      const int64_t off = (int64_t)(q >> uh_shift) * hs + (q & uh_mask) * 16;
+      kx[k] = *reinterpret_cast<const uint4*>(sk + off);
+      vx[k] = *reinterpret_cast<const uint4*>(sv + off);
     }
 #pragma unroll
     for (int k = 0; k < UPL; ++k) {
@@ -215,22 +219,24 @@ __global__ void __launch_bounds__(256) relocate_rows_kernel(
       if (lane == 0) report(status, CS_ST_SLOT_RANGE);
       continue;
     }
+    char *sk, *sv, *dk, *dv;
+    int64_t shs, dhs;
+    pv.record(s, sk, sv, shs);  // one block / sidecar lookup per row and side
+    pv.record(d, dk, dv, dhs);
     uint4 kx[UPL], vx[UPL];
 #pragma unroll
     for (int k = 0; k < UPL; ++k) {
       const int q = lane + 32 * k;
-      const int h = q >> uh_shift;
-      const int64_t e = (int64_t)(q & uh_mask) * (16 / pv.esize);
-      kx[k] = *reinterpret_cast<const uint4*>(pv.addr(s, h, e));
-      vx[k] = *reinterpret_cast<const uint4*>(pv.addr(s, h, pv.head_dim + e));
+      const int64_t off = (int64_t)(q >> uh_shift) * shs + (q & uh_mask) * 16;
+      kx[k] = *reinterpret_cast<const uint4*>(sk + off);
+      vx[k] = *reinterpret_cast<const uint4*>(sv + off);
     }
 #pragma unroll
     for (int k = 0; k < UPL; ++k) {
       const int q = lane + 32 * k;
-      const int h = q >> uh_shift;
-      const int64_t e = (int64_t)(q & uh_mask) * (16 / pv.esize);
-      *reinterpret_cast<uint4*>(pv.addr(d, h, e)) = kx[k];
-      *reinterpret_cast<uint4*>(pv.addr(d, h, pv.head_dim + e)) = vx[k];
+      const int64_t off = (int64_t)(q >> uh_shift) * dhs + (q & uh_mask) * 16;
+      *reinterpret_cast<uint4*>(dk + off) = kx[k];
+      *reinterpret_cast<uint4*>(dv + off) = vx[k];
     }
   }
 }
@@ -281,13 +287,15 @@ __global__ void __launch_bounds__(256) scatter_rows_batch_kernel(
       kx[k] = *reinterpret_cast<const uint4*>(q.k + off);
       vx[k] = *reinterpret_cast<const uint4*>(q.v + off);
     }
+    char *dk, *dv;
+    int64_t hs;
+    pv.record(s, dk, dv, hs);  // one block / sidecar lookup per row
 #pragma unroll
     for (int k = 0; k < UPL; ++k) {
       const int u = lane + 32 * k;
-      const int h = u >> uh_shift;
-      const int64_t e = (int64_t)(u & uh_mask) * (16 / pv.esize);
-      *reinterpret_cast<uint4*>(pv.addr(s, h, e)) = kx[k];
-      *reinterpret_cast<uint4*>(pv.addr(s, h, pv.head_dim + e)) = vx[k];
+      const int64_t off = (int64_t)(u >> uh_shift) * hs + (u & uh_mask) * 16;
+      *reinterpret_cast<uint4*>(dk + off) = kx[k];
+      *reinterpret_cast<uint4*>(dv + off) = vx[k];
     }
   }
 }
