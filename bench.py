@@ -50,12 +50,15 @@ def parse():
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batched-attention", action="store_true",
-                    help="one attention launch for all requests after their WCA / SLIDE "
-                         "chains (default: one launch per request on its stream)")
-    ap.add_argument("--batched", action="store_true",
-                    help="every stage of the step as one launch for all requests (seven "
-                         "launches per step); e2e keeps the per-request streams")
-    return ap.parse_args()
+                    help="with --per-request-streams: one attention launch for all requests "
+                         "after their WCA / SLIDE chains")
+    ap.add_argument("--per-request-streams", action="store_true",
+                    help="one launch per request and stage, each request on its own stream "
+                         "(default: every stage of the step as one launch for all requests, "
+                         "seven launches per step; e2e always uses the per-request streams)")
+    args = ap.parse_args()
+    args.batched = not args.per_request_streams
+    return args
 
 
 def peaks():

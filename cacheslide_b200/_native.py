@@ -165,6 +165,9 @@ _SIGNATURES = {
                           _i64, _i64, _p, _p],
     "cs_cope_bias": [_p, _i64, _i64, _p, _i64, _i64, _i32, _i32, _p, _i64, _i64, _i32, _i64,
                      _i64, _i32, _p, _i64, _i64, _p, _p],
+    "cs_cope_chunk_offsets": [_p, _i64, _i64, _i32, _i32, _i32, _p, _p, _p, _p, _i64, _i64,
+                              _i32, _p, _p, _p, _i32, _p, _i64, _i64, _i64, _i32, _i32, _i32,
+                              _p, _i64, _i64, _i32, _p, _p],
     "cs_cope_validate_path": [_p, _i64, _i64, _p, _p, _p, _i64, _i64, _i32, _i64, _i64, _f64,
                               _i32, _p, _p],
     "cs_build_info": [],

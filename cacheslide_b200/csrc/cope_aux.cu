@@ -2,6 +2,7 @@
 //   cs_cope_positions      CoPE.contextual_positions   (position.py:295-307)
 //   cs_cope_bias           CoPE.positional_bias        (position.py:309-344)
 //   cs_cope_validate_path  validate_contextual_path    (position.py:28-114)
+//   cs_cope_chunk_offsets  CCPEProfile tables -> per-chunk carried counts
 // One warp per (head, query) row; keys are walked newest-first in tiles of 32
 // with a warp-shuffle suffix scan and a carried count.
 #include <math.h>
@@ -145,6 +146,60 @@ int rows_grid(int64_t rows, int warps_per_block) {
   return b < 1 ? 1 : (int)b;
 }
 
+// One warp per (head, query row): the row's offsets are first set to -1
+// (carry the running count), then, for a fixed query, every fixed chunk older
+// than the query's segment gets the canonical position of its last key minus
+// that key's own gate sigmoid(q . k / sqrt(d)) (fp32 logits, as position.py's
+// _logits accumulates bf16 / fp16 / fp32 inputs).
+template <typename T>
+__global__ void chunk_offsets_kernel(const T* __restrict__ q, int64_t qs_t, int64_t qs_h, int nq,
+                                     int hq, int d, const int64_t* __restrict__ qpos,
+                                     const int32_t* __restrict__ q_ord,
+                                     const int32_t* __restrict__ q_seg, const T* __restrict__ k,
+                                     int64_t ks_t, int64_t ks_h, int hkv,
+                                     const int64_t* __restrict__ last_key,
+                                     const int32_t* __restrict__ last_ord,
+                                     const int32_t* __restrict__ seg_of_chunk, int nfc,
+                                     const float* __restrict__ table, int64_t tb_h, int64_t tb_r,
+                                     int64_t tb_c, int tb_rows, int tb_cols, float* offsets,
+                                     int64_t of_h, int64_t of_t, int nseg, int32_t* status) {
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = (int64_t)hq * nq;
+  const int group = hq / hkv;
+  const float inv = 1.f / sqrtf((float)d);
+  for (int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; row < rows;
+       row += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int h = (int)(row / nq), r = (int)(row - (int64_t)h * nq);
+    float* out = offsets + h * of_h + qpos[r] * of_t;
+    for (int c = lane; c < nseg; c += 32) out[c] = -1.f;
+    __syncwarp();
+    const int qo = q_ord[r], qs = q_seg[r];
+    if (qo < 0) continue;  // a dynamic query: contextual counts
+    if (qo >= tb_rows) {
+      if (lane == 0) report(status, CS_ST_POS_RANGE);
+      continue;
+    }
+    const T* qr = q + r * qs_t + h * qs_h;
+    for (int f = 0; f < nfc; ++f) {
+      const int seg = seg_of_chunk[f];
+      if (seg >= qs) continue;  // the query's own chunk and newer: no reset
+      const int ko = last_ord[f];
+      const T* kr = k + last_key[f] * ks_t + (h / group) * ks_h;
+      float dot = 0.f;
+      for (int e = lane; e < d; e += 32) dot += Elem<T>::to_f(qr[e]) * Elem<T>::to_f(kr[e]);
+      dot = warp_sum(dot);
+      if (lane == 0) {
+        if (ko < 0 || ko >= tb_cols || seg < 0 || seg >= nseg) {
+          report(status, CS_ST_POS_RANGE);
+        } else {
+          const float gate = 1.f / (1.f + expf(-(dot * inv)));
+          out[seg] = table[h * tb_h + (int64_t)qo * tb_r + (int64_t)ko * tb_c] - gate;
+        }
+      }
+    }
+  }
+}
+
 }  // namespace
 }  // namespace cs
 
@@ -229,6 +284,41 @@ extern "C" CS_API int cs_cope_validate_path(const void* positions, int64_t ps_h,
                                                  status);
   else
     return CS_ERR_INVALID;
+  CS_LAUNCH_CHECK();
+  return CS_OK;
+}
+
+extern "C" CS_API int cs_cope_chunk_offsets(
+    const void* q, int64_t q_stride_tok, int64_t q_stride_head, int32_t nq, int32_t hq,
+    int32_t d, const int64_t* qpos, const int32_t* q_ord, const int32_t* q_seg, const void* k,
+    int64_t k_stride_tok, int64_t k_stride_head, int32_t hkv, const int64_t* last_key,
+    const int32_t* last_ord, const int32_t* seg_of_chunk, int32_t nfixed_chunks,
+    const float* table, int64_t tb_stride_h, int64_t tb_stride_r, int64_t tb_stride_c,
+    int32_t tb_rows, int32_t tb_cols, int32_t dtype, float* offsets, int64_t off_stride_h,
+    int64_t off_stride_t, int32_t nseg, int32_t* status, void* stream) {
+  CS_HOST_CHECK(nq >= 0 && hq > 0 && hkv > 0 && hq % hkv == 0 && d > 0 && nseg > 0 &&
+                nfixed_chunks >= 0 && tb_rows >= 0 && tb_cols >= 0);
+  if (nq == 0) return CS_OK;
+  CS_HOST_CHECK(q && qpos && q_ord && q_seg && offsets);
+  CS_HOST_CHECK(nfixed_chunks == 0 || (k && last_key && last_ord && seg_of_chunk && table));
+  const int threads = 256;
+  int64_t blocks = ((int64_t)hq * nq * 32 + threads - 1) / threads;
+  if (blocks > (int64_t)num_sms() * 16) blocks = (int64_t)num_sms() * 16;
+  auto s = as_stream(stream);
+  auto go = [&](auto tag) {
+    using T = decltype(tag);
+    chunk_offsets_kernel<T><<<(int)blocks, threads, 0, s>>>(
+        static_cast<const T*>(q), q_stride_tok, q_stride_head, nq, hq, d, qpos, q_ord, q_seg,
+        static_cast<const T*>(k), k_stride_tok, k_stride_head, hkv, last_key, last_ord,
+        seg_of_chunk, nfixed_chunks, table, tb_stride_h, tb_stride_r, tb_stride_c, tb_rows,
+        tb_cols, offsets, off_stride_h, off_stride_t, nseg, status);
+  };
+  switch (dtype) {
+    case CS_F32: go(float{}); break;
+    case CS_F16: go(__half{}); break;
+    case CS_BF16: go(__nv_bfloat16{}); break;
+    default: return CS_ERR_INVALID;
+  }
   CS_LAUNCH_CHECK();
   return CS_OK;
 }

@@ -352,6 +352,108 @@ class ChunkResetPositions:
             "pass it as cope_attention(positions_transform=...)"
         )
 
+    @classmethod
+    def from_profile(
+        cls,
+        table: Tensor,
+        fixed_indices,
+        chunk_lengths,
+        num_tokens: int,
+        query: Tensor,
+        query_positions: Tensor,
+        key: Tensor,
+        *,
+        table_query_positions: Tensor | None = None,
+    ) -> ChunkResetPositions:
+        """The compressed form of a canonical CCPE table for one prompt.
+
+        ``table`` is a CCPEProfile's ``canonical_positions`` ``[head, Fq, F]``
+        (position.py:581-748): row ``i`` holds fixed query ordinal
+        ``table_query_positions[i]`` (default ``i``), column ``j`` fixed key
+        ordinal ``j``.  ``fixed_indices`` are the prompt positions of the fixed
+        tokens in order and ``chunk_lengths`` the lengths of the fixed chunks
+        (a plan's ``fixed_indices`` and ``fixed_layout``, attention.py:32-57);
+        ``query`` ``[nq, hq, d]`` at ``query_positions`` and ``key``
+        ``[num_tokens, hkv, d]`` are the prompt's current rows.
+
+        The prompt is cut into segments -- each fixed chunk and each run of
+        dynamic tokens -- and for a fixed query and a fixed chunk older than
+        the query's segment the offset is the carried count into the chunk:
+        the table's position of the chunk's last key minus that key's gate
+        (``cs_cope_chunk_offsets``, on the device).  Inside the fixed chunks
+        the kernels then recount the current gates, so with the calibration's
+        fixed content every fixed x fixed position equals its table entry;
+        dynamic keys carry the running count.
+        """
+        device = N.require_cuda(query)
+        n = int(num_tokens)
+        lengths = [int(x) for x in chunk_lengths]
+        fixed = [int(x) for x in fixed_indices]
+        if sum(lengths) != len(fixed) or any(x <= 0 for x in lengths):
+            raise ValueError("fixed chunk lengths must be positive and cover fixed_indices")
+        if any(b <= a for a, b in zip(fixed, fixed[1:])) or (fixed and not 0 <= fixed[0] <= fixed[-1] < n):
+            raise ValueError("fixed_indices must be increasing positions inside the prompt")
+        if query.ndim != 3 or key.ndim != 3 or key.shape[0] != n:
+            raise ValueError("query must be [nq, hq, d] and key [num_tokens, hkv, d]")
+        if query.dtype != key.dtype or query.dtype not in (torch.float32, torch.float16,
+                                                          torch.bfloat16):
+            raise ValueError("query and key must share a float32 / float16 / bfloat16 dtype")
+        hq, d, hkv = query.shape[1], query.shape[2], key.shape[1]
+        if key.shape[2] != d or hq % hkv:
+            raise ValueError("query / key heads or head dims do not match")
+        if table.ndim != 3 or table.shape[0] != hq or table.shape[2] != len(fixed):
+            raise ValueError("table must be [query heads, profiled rows, fixed keys]")
+        # segments: fixed chunks and dynamic runs, in prompt order
+        chunk_of = [-1] * n
+        start = 0
+        for f, length in enumerate(lengths):
+            for pos in fixed[start:start + length]:
+                chunk_of[pos] = f
+            start += length
+        key_seg, seg = [], -1
+        for t in range(n):
+            if t == 0 or chunk_of[t] != chunk_of[t - 1]:
+                seg += 1
+            key_seg.append(seg)
+        nseg = seg + 1
+        ends = [sum(lengths[:f + 1]) for f in range(len(lengths))]
+        last_key = [fixed[e - 1] for e in ends]
+        last_ord = [e - 1 for e in ends]
+        seg_of_chunk = [key_seg[t] for t in last_key]
+        ordinal = {pos: i for i, pos in enumerate(fixed)}
+        if table_query_positions is None:
+            rows = {i: i for i in range(table.shape[1])}
+        else:
+            rows = {int(o): i for i, o in enumerate(table_query_positions.tolist())}
+        qpos = [int(x) for x in query_positions.tolist()]
+        if len(qpos) != query.shape[0] or any(not 0 <= t < n for t in qpos):
+            raise ValueError("query_positions must give one prompt position per query row")
+        q_ord = []
+        for t in qpos:
+            o = ordinal.get(t, -1)
+            if o >= 0 and o not in rows:
+                raise ValueError("CCPE profile has no contextual trace for these query positions")
+            q_ord.append(rows[o] if o >= 0 else -1)
+        i32 = lambda v: torch.tensor(v, dtype=torch.int32, device=device)  # noqa: E731
+        qpos_t = torch.tensor(qpos, dtype=torch.int64, device=device)
+        tab = table.to(device=device, dtype=torch.float32)
+        offsets = torch.full((hq, n, nseg), -1.0, dtype=torch.float32, device=device)
+        args = dict(q_ord=i32(q_ord), q_seg=i32([key_seg[t] for t in qpos]),
+                    last_key=torch.tensor(last_key, dtype=torch.int64, device=device),
+                    last_ord=i32(last_ord), seg_of_chunk=i32(seg_of_chunk))
+        status = N.Status(device)
+        N.check(N.load().cs_cope_chunk_offsets(
+            query.data_ptr(), query.stride(0), query.stride(1), query.shape[0], hq, d,
+            qpos_t.data_ptr(), args["q_ord"].data_ptr(), args["q_seg"].data_ptr(),
+            key.data_ptr(), key.stride(0), key.stride(1), hkv, args["last_key"].data_ptr(),
+            args["last_ord"].data_ptr(), args["seg_of_chunk"].data_ptr(), len(lengths),
+            tab.data_ptr(), tab.stride(0), tab.stride(1), tab.stride(2), tab.shape[1],
+            tab.shape[2], N.DTYPES[query.dtype], offsets.data_ptr(), offsets.stride(0),
+            offsets.stride(1), nseg, status.ptr, N.stream_of(device)), "cs_cope_chunk_offsets")
+        if status.read():
+            raise ValueError("table ordinals out of range")
+        return cls(key_chunk=i32(key_seg), offsets=offsets)
+
 
 def _base_params(
     query: Tensor,

@@ -510,6 +510,35 @@ CS_API int cs_cope_bias(const void* query, int64_t qs_t, int64_t qs_h,
                         int32_t* status, void* stream);
 
 /*
+ * Compressed CCPE positions from a canonical profile: the [head, F, F]
+ * tables of CCPEProfile (position.py:581-748, applied by
+ * CanonicalPositionPolicy, attention.py:32-57) turned into the per-chunk
+ * offsets of CS_POS_CHUNK (offsets[h, t, segment], float32).  For query row
+ * r (token position qpos[r], fixed ordinal q_ord[r] or -1, segment
+ * q_seg[r]) and fixed chunk f (segment seg_of_chunk[f], last token at key
+ * index last_key[f] with fixed ordinal last_ord[f]) older than the query's
+ * segment:
+ *   offsets[h, qpos[r], seg_of_chunk[f]] = table[h, q_ord[r], last_ord[f]]
+ *       - sigmoid(q[r, h] . k[last_key[f], h / (hq / hkv)] / sqrt(d)),
+ * the count carried into the chunk (its last key's canonical position minus
+ * that key's own gate); every other entry of the rows qpos[r] is -1 (the
+ * running count is carried).  With the calibration's gates inside the fixed
+ * chunks, the chunk-reset positions of fixed x fixed cells equal the table.
+ * q, k in bf16 / fp16 / fp32; out-of-range ordinals set CS_ST_POS_RANGE.
+ */
+CS_API int cs_cope_chunk_offsets(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
+                                 int32_t nq, int32_t hq, int32_t d, const int64_t* qpos,
+                                 const int32_t* q_ord, const int32_t* q_seg, const void* k,
+                                 int64_t k_stride_tok, int64_t k_stride_head, int32_t hkv,
+                                 const int64_t* last_key, const int32_t* last_ord,
+                                 const int32_t* seg_of_chunk, int32_t nfixed_chunks,
+                                 const float* table, int64_t tb_stride_h, int64_t tb_stride_r,
+                                 int64_t tb_stride_c, int32_t tb_rows, int32_t tb_cols,
+                                 int32_t dtype, float* offsets, int64_t off_stride_h,
+                                 int64_t off_stride_t, int32_t nseg, int32_t* status,
+                                 void* stream);
+
+/*
  * validate_contextual_path (position.py:28-114): OR-s CS_ST_PATH_* bits for
  * failing causal cells / adjacent pairs and CS_ST_POS_RANGE for non-finite
  * positions.  mask (uint8 [h|1, q, k], may be NULL) = attention_mask.

@@ -273,3 +273,55 @@ def canonical_transform(fixed_indices, table, table_rows, strict=False):
         return result
 
     return transform
+
+
+def ccpe_segments(fixed_indices, chunk_lengths, n: int):
+    """The segments of an n-token prompt: each fixed chunk (``chunk_lengths``
+    consecutive entries of ``fixed_indices``, contiguous in the prompt) and each
+    maximal run of dynamic tokens, numbered in prompt order.  Returns
+    (key_seg[n], seg_of_chunk[f], last_key[f], last_ord[f], ordinal[n]) with
+    ordinal = the token's index in ``fixed_indices`` or -1 (the ordinal map
+    of CanonicalPositionPolicy, attention.py:32-57)."""
+    fixed_indices = np.asarray(fixed_indices, dtype=np.int64)
+    ordinal = np.full(n, -1, dtype=np.int64)
+    ordinal[fixed_indices] = np.arange(fixed_indices.size)
+    chunk_of = np.full(n, -1, dtype=np.int64)
+    ends = np.cumsum(chunk_lengths)
+    starts = ends - np.asarray(chunk_lengths)
+    for f, (a, b) in enumerate(zip(starts, ends)):
+        chunk_of[fixed_indices[a:b]] = f
+    key_seg = np.zeros(n, dtype=np.int64)
+    seg = -1
+    for t in range(n):
+        if t == 0 or chunk_of[t] != chunk_of[t - 1] or (chunk_of[t] < 0) != (chunk_of[t - 1] < 0):
+            seg += 1
+        key_seg[t] = seg
+    last_key = fixed_indices[ends - 1]
+    return key_seg, key_seg[last_key], last_key, ends - 1, ordinal
+
+
+def chunk_offsets_from_table(q, k, qpos, q_ord, q_seg, last_key, last_ord, seg_of_chunk,
+                             table, n: int, nseg: int) -> np.ndarray:
+    """Per-chunk carried counts from a canonical CCPE table (the compressed
+    form of the CCPEProfile tables, position.py:581-748): for a fixed query
+    row r and a fixed chunk f older than the query's segment, the table's
+    position of the chunk's last key minus that key's gate
+    sigmoid(q . k / sqrt(d)) in float32 (position.py:157-164); -1 elsewhere
+    (the running count is carried).  Rows of tokens that are not queries stay
+    -1 here."""
+    H, d = q.shape[1], q.shape[2]
+    G = H // k.shape[1]
+    out = np.full((H, n, nseg), -1.0, dtype=np.float32)
+    q32, k32 = q.astype(np.float32), k.astype(np.float32)
+    inv = np.float32(1.0) / np.float32(np.sqrt(np.float32(d)))
+    for r in range(q.shape[0]):
+        if q_ord[r] < 0:
+            continue
+        for f in range(len(last_key)):
+            if seg_of_chunk[f] >= q_seg[r]:
+                continue
+            kk = k32[last_key[f], np.arange(H) // G]                   # [H, d]
+            logit = np.einsum("hd,hd->h", q32[r], kk).astype(np.float32) * inv
+            gate = (np.float32(1) / (np.float32(1) + np.exp(-logit))).astype(np.float32)
+            out[:, qpos[r], seg_of_chunk[f]] = table[:, q_ord[r], last_ord[f]] - gate
+    return out

@@ -260,6 +260,61 @@ def paged_cases(ref):
     return out
 
 
+def profile_cases(ref):
+    """A CCPE profile calibrated by the reference from three prompts that
+    share their fixed chunks (the same Q/K rows) and differ in their dynamic
+    tokens, and the reference's canonical-table attention
+    (CanonicalPositionPolicy, mixed_bias_override) on each prompt: the
+    fixtures of the compressed per-chunk form (cs_cope_chunk_offsets)."""
+    from cacheslide_vllm.attention import CanonicalPositionPolicy
+    from cacheslide_vllm.contracts import RequestPlan
+    from cacheslide_vllm.position import CCPEProfile, ChunkIdentity, CoPE, cope_attention
+
+    g = torch.Generator().manual_seed(7)
+    hq, hkv, d, npos = 4, 2, 32, 16
+    layout = [("reuse", 12), ("recompute", 5), ("reuse", 9), ("reuse", 10), ("recompute", 4)]
+    chunks, cursor = [], 0
+    for i, (role, length) in enumerate(layout):
+        chunks.append({"id": f"c{i}", "role": role, "start": cursor, "end": cursor + length})
+        cursor += length
+    n = cursor
+    ids = [(5 * j + 1) % 40 for j in range(n)]
+    plan = RequestPlan.parse({"version": 1, "namespace": "golden", "task_id": "ccpe-compressed",
+                              "operation": "reuse", "chunks": chunks}, ids)
+    fixed = torch.tensor(plan.fixed_indices)
+    E = _bf16(torch.randn(d, npos, generator=g) * 0.5)
+    cope = CoPE(d, npos)
+    with torch.no_grad():
+        cope.position_embeddings.copy_(E)
+    qf = _bf16(torch.randn(fixed.numel(), hq, d, generator=g))
+    kf = _bf16(torch.randn(fixed.numel(), hkv, d, generator=g))
+    vf = _bf16(torch.randn(fixed.numel(), hkv, d, generator=g))
+    prompts, traces = [], []
+    for _ in range(3):
+        q = _bf16(torch.randn(n, hq, d, generator=g))
+        k = _bf16(torch.randn(n, hkv, d, generator=g))
+        v = _bf16(torch.randn(n, hkv, d, generator=g))
+        q[fixed], k[fixed], v[fixed] = qf, kf, vf  # same fixed content
+        prompts.append((q, k, v))
+        trace = cope.position_trace(q, k, torch.arange(n), checkpoint_id="ck")
+        traces.append(trace.project(fixed, fixed))
+    profile = CCPEProfile.calibrate(traces, [ChunkIdentity(*e) for e in plan.fixed_layout],
+                                    trained_profile_version="golden-v1")
+    rep = [i for i, t in enumerate(traces)
+           if torch.equal(t.positions, profile.canonical_positions)][0]
+    out = {"meta": dict(fixed=_np(fixed),
+                        chunk_lengths=np.array([e[2] for e in plan.fixed_layout]),
+                        n=np.array(n), E=_np(E), representative=np.array(rep),
+                        table=_np(profile.canonical_positions),
+                        table_query_positions=_np(profile.query_positions))}
+    policy = CanonicalPositionPolicy(plan, profile, "ck", mode="mixed_bias_override")
+    for i, (q, k, v) in enumerate(prompts):
+        o, p = cope_attention(q, k, v, cope, torch.arange(n), positions_transform=policy,
+                              query_chunk_size=11, return_positions=True)
+        out[f"prompt{i}"] = dict(q=_np(q), k=_np(k), v=_np(v), out=_np(o), positions=_np(p))
+    return out
+
+
 SLOT_TRACE_SEEDS = 400
 
 
@@ -287,7 +342,7 @@ def main(src: str, only: list[str]) -> None:
 
     torch.set_num_threads(4)
     for name, fn in (("cope", cope_cases), ("wca", wca_cases),
-                     ("paged", paged_cases)):
+                     ("paged", paged_cases), ("profile", profile_cases)):
         if only and name not in only:
             continue
         cases = fn(ref)
@@ -304,5 +359,5 @@ def main(src: str, only: list[str]) -> None:
 if __name__ == "__main__":
     if len(sys.argv) < 2:
         raise SystemExit("usage: make_golden.py <CacheSlide checkout>/src "
-                         "[cope|wca|paged|slot_trace ...]")
+                         "[cope|wca|paged|profile|slot_trace ...]")
     main(sys.argv[1], sys.argv[2:])
