@@ -28,7 +28,7 @@
 //               is ready, QK(a) of the next key tile, PV(b), QK(b) of the
 //               next; completions are tracked with tcgen05.commit.
 // TMEM (512 columns): S(a) [0,128), S(b) [128,256) (P over their first 64
-// columns; T = Q E over the same 64 columns at start), O(a) [256,384), O(b)
+// columns; T = Q E over their first NP columns at start), O(a) [256,384), O(b)
 // [384,512).  Every mbarrier wait is bounded; on expiry the CTA raises
 // CS_ST_TIMEOUT, drains its copies and MMAs, frees its TMEM and returns.
 #include <cuda.h>
@@ -37,6 +37,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <numeric>
+#include <type_traits>
 
 #include "common.cuh"
 #include "sm100.cuh"
@@ -56,15 +57,18 @@ static_assert(256 * kSoftRegs + 128 * kProdRegs + 32 * kLaunchRegs <= kThreads *
               "register split exceeds the CTA's launch allocation");
 constexpr int kTileN = 128;  // keys per tile
 constexpr int kD = 128;      // head dim of this kernel
-constexpr int kMaxNpos = 64;
+// npos up to 64: a float q.E table per row; up to 128: a half table per row
+// (the same 32 KB a tile; fp16 keeps 11 significant bits of the log2-domain
+// bias, below the bf16 rounding of P that the PV MMA already applies)
+constexpr int kMaxNpos = 128;
 
 // Two query tiles per CTA ("a" = 0, "b" = 1), 128 S rows each, one softmax
 // thread per row.  Shared memory map (bytes from the 1024-aligned base):
 constexpr uint32_t kQ = 0;          // 2 x 32 KB Q tiles   [tile][2 cb][128 rows][128 B]
 constexpr uint32_t kK0 = 65536;     // 32 KB  K tile (one stage: freed when both QKs are done)
 constexpr uint32_t kV0 = 98304;     // 2 x 32 KB V tiles
-constexpr uint32_t kP = 163840;     // 32 KB  E hi/lo staging for T = Q E at start
-constexpr uint32_t kTab = 163840;   // 2 x 32 KB q.E tables [tile][128 rows][64] float, after T
+constexpr uint32_t kP = 163840;     // 32 / 64 KB  E hi/lo staging for T = Q E at start (NP 64 / 128)
+constexpr uint32_t kTab = 163840;   // 2 x 32 KB q.E tables [tile][128 rows][NP] float / half, after T
 constexpr uint32_t kMeta = 229376;  // barriers, flags, key metadata
 
 // metadata block (offsets from kMeta)
@@ -91,7 +95,7 @@ constexpr uint32_t kMetaBytes = kRedN + 64;
 constexpr uint32_t kSmemBytes = kMeta + kMetaBytes;  // 229,808 B (limit 232,448)
 
 // TMEM columns: S of each tile (P packed over its first 64 columns), O of
-// each tile; T = Q E lands in the first 64 S columns of its tile at start
+// each tile; T = Q E lands in the first NP S columns of its tile at start
 constexpr uint32_t kColS = 0, kColO = 256;  // + 128 * tile
 __device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
@@ -240,57 +244,65 @@ __device__ __forceinline__ const char* value_row_addr(const Args& a, uint64_t ka
 // loads, then one 16-byte shared store per position for hi and for lo.
 // Otherwise one element per step, all of a thread's loads issued before its
 // stores (the stores could alias the loads as far as the compiler knows).
-template <typename T>
+template <typename T, int NP>
 __device__ __forceinline__ void stage_e_split(uint8_t* smem, const cs_attn_params& p, int t) {
   const float* E = static_cast<const float*>(p.E);
+  constexpr uint32_t kLo = NP * 256;  // lo half after the NP rows x 256 B of hi
   const bool vec = p.e_stride_p == 1 && p.npos % 4 == 0 && p.e_stride_d % 4 == 0 &&
                    (reinterpret_cast<uintptr_t>(E) & 15) == 0;
   if (vec) {
-    constexpr int kUnits = (kMaxNpos / 4) * (kD / 8);  // 256
-    if (t >= kUnits) return;
-    const int p0 = (t % (kMaxNpos / 4)) * 4, d0 = (t / (kMaxNpos / 4)) * 8;
-    float4 v[8];
+    constexpr int kUnits = (NP / 4) * (kD / 8);  // 256 or 512 units of 4 x 8
+#pragma unroll 1
+    for (int u = t; u < kUnits; u += 384) {
+      const int p0 = (u % (NP / 4)) * 4, d0 = (u / (NP / 4)) * 8;
+      float4 v[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      v[j] = p0 < p.npos ? __ldg(reinterpret_cast<const float4*>(E + (int64_t)(d0 + j) * p.e_stride_d + p0))
-                         : make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int j = 0; j < 8; ++j)
+        v[j] = p0 < p.npos
+                   ? __ldg(reinterpret_cast<const float4*>(E + (int64_t)(d0 + j) * p.e_stride_d + p0))
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint32_t hw[4], lw[4];
+      for (int q = 0; q < 4; ++q) {
+        uint32_t hw[4], lw[4];
 #pragma unroll
-      for (int j = 0; j < 8; j += 2) {
-        const float e0 = q == 0 ? v[j].x : q == 1 ? v[j].y : q == 2 ? v[j].z : v[j].w;
-        const float e1 = q == 0 ? v[j + 1].x : q == 1 ? v[j + 1].y : q == 2 ? v[j + 1].z : v[j + 1].w;
-        const float h0 = Elem<T>::to_f(Elem<T>::from_f(e0)), h1 = Elem<T>::to_f(Elem<T>::from_f(e1));
-        hw[j / 2] = Pack2<T>::pack(h0, h1);
-        lw[j / 2] = Pack2<T>::pack(e0 - h0, e1 - h1);
+        for (int j = 0; j < 8; j += 2) {
+          const float e0 = q == 0 ? v[j].x : q == 1 ? v[j].y : q == 2 ? v[j].z : v[j].w;
+          const float e1 = q == 0 ? v[j + 1].x : q == 1 ? v[j + 1].y : q == 2 ? v[j + 1].z : v[j + 1].w;
+          const float h0 = Elem<T>::to_f(Elem<T>::from_f(e0)), h1 = Elem<T>::to_f(Elem<T>::from_f(e1));
+          hw[j / 2] = Pack2<T>::pack(h0, h1);
+          lw[j / 2] = Pack2<T>::pack(e0 - h0, e1 - h1);
+        }
+        const uint32_t off = sw128(p0 + q, d0 >> 3, NP);
+        *reinterpret_cast<uint4*>(smem + kP + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4*>(smem + kP + kLo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
       }
-      const uint32_t off = sw128(p0 + q, d0 >> 3, kMaxNpos);
-      *reinterpret_cast<uint4*>(smem + kP + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-      *reinterpret_cast<uint4*>(smem + kP + 16384 + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
     }
     return;
   }
-  constexpr int kN = kMaxNpos * kD, kThr = 384, kPer = (kN + kThr - 1) / kThr;
-  float ev[kPer];
+  // general strides: groups of 8 elements a thread, loads before stores
+  constexpr int kN = NP * kD, kThr = 384;
+#pragma unroll 1
+  for (int base = 0; base < kN; base += 8 * kThr) {
+    float ev[8];
 #pragma unroll
-  for (int u = 0; u < kPer; ++u) {
-    const int idx = u * kThr + t;
-    const int dd = idx / kMaxNpos, pp = idx - dd * kMaxNpos;  // consecutive threads: consecutive p
-    ev[u] = idx < kN && pp < p.npos
-                ? __ldg(E + (int64_t)dd * p.e_stride_d + (int64_t)pp * p.e_stride_p)
-                : 0.f;
-  }
+    for (int u = 0; u < 8; ++u) {
+      const int idx = base + u * kThr + t;
+      const int dd = idx / NP, pp = idx - dd * NP;  // consecutive threads: consecutive p
+      ev[u] = idx < kN && pp < p.npos
+                  ? __ldg(E + (int64_t)dd * p.e_stride_d + (int64_t)pp * p.e_stride_p)
+                  : 0.f;
+    }
 #pragma unroll
-  for (int u = 0; u < kPer; ++u) {
-    const int idx = u * kThr + t;
-    if (idx >= kN) break;
-    const int dd = idx / kMaxNpos, pp = idx - dd * kMaxNpos;
-    const T hi = Elem<T>::from_f(ev[u]);
-    const T lo = Elem<T>::from_f(ev[u] - Elem<T>::to_f(hi));
-    const uint32_t off = sw128(pp, dd >> 3, kMaxNpos) + (dd & 7) * 2;
-    *reinterpret_cast<T*>(smem + kP + off) = hi;
-    *reinterpret_cast<T*>(smem + kP + 16384 + off) = lo;
+    for (int u = 0; u < 8; ++u) {
+      const int idx = base + u * kThr + t;
+      if (idx >= kN) break;
+      const int dd = idx / NP, pp = idx - dd * NP;
+      const T hi = Elem<T>::from_f(ev[u]);
+      const T lo = Elem<T>::from_f(ev[u] - Elem<T>::to_f(hi));
+      const uint32_t off = sw128(pp, dd >> 3, NP) + (dd & 7) * 2;
+      *reinterpret_cast<T*>(smem + kP + off) = hi;
+      *reinterpret_cast<T*>(smem + kP + kLo + off) = lo;
+    }
   }
 }
 
@@ -303,21 +315,22 @@ struct BatchArgs {
 };
 static_assert(sizeof(BatchArgs) <= 32000, "batched prefill arguments exceed the parameter space");
 
-// one CTA: query-tile pair `pair` of KV head g of request a
-template <typename T>
+// one CTA: query-tile pair `pair` of KV head g of request a; NP = 64 or 128
+// bounds npos (the q.E table's width)
+template <typename T, int NP>
 __device__ __forceinline__ void prefill_cta(const Args& a, int g, int pair);
 
-template <typename T>
+template <typename T, int NP>
 __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_constant__ Args a) {
   // the heaviest (latest) pairs of all KV heads are launched first, so the
   // light ones fill the tail of the grid
-  prefill_cta<T>(a, blockIdx.x % a.p.hkv, a.pairs_per_head - 1 - blockIdx.x / a.p.hkv);
+  prefill_cta<T, NP>(a, blockIdx.x % a.p.hkv, a.pairs_per_head - 1 - blockIdx.x / a.p.hkv);
 }
 
 // all requests of a step in one grid, heaviest pairs of every request first
 // (pair rank j from the top, then request, then KV head); a request with
 // fewer pairs leaves its CTAs of the lowest ranks empty
-template <typename T>
+template <typename T, int NP>
 __global__ void __launch_bounds__(kThreads, 1)
     cope_prefill_sm100_batch(const __grid_constant__ BatchArgs b) {
   const int per_rank = b.count * b.hkv;
@@ -325,10 +338,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const Args& a = b.r[ri];
   const int pair = a.pairs_per_head - 1 - j;
   if (pair < 0) return;
-  prefill_cta<T>(a, blockIdx.x % b.hkv, pair);
+  prefill_cta<T, NP>(a, blockIdx.x % b.hkv, pair);
 }
 
-template <typename T>
+template <typename T, int NP>
 __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const int pair) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
@@ -411,7 +424,7 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
       }
     }
   }
-  if (warp < 12) stage_e_split<T>(smem, p, tid);
+  if (warp < 12) stage_e_split<T, NP>(smem, p, tid);
   if (warp == 12) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      mb + kTmemSlot),
@@ -614,7 +627,7 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
     // ================================================================== MMA
     if (lane == 0) {
       const uint32_t id_s = umma_idesc(128, 128, a.fmt, 0, 0);  // S = Q K^T
-      const uint32_t id_t = umma_idesc(128, 64, a.fmt, 0, 0);   // T = Q E
+      const uint32_t id_t = umma_idesc(128, NP, a.fmt, 0, 0);   // T = Q E
       const uint32_t id_o = umma_idesc(128, 128, a.fmt, 0, 1);  // O += P V (V MN-major)
       bool ok = mbar_wait(mb + kBarQ, 0, abort);
       if (ok) {
@@ -623,7 +636,7 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
           for (int half = 0; half < 2; ++half) {
             for (int kk = 0; kk < kD / 16; ++kk) {
               const uint32_t aoff = qt * 32768 + (kk >> 2) * 16384 + (kk & 3) * 32;
-              const uint32_t boff = half * 16384 + (kk >> 2) * 8192 + (kk & 3) * 32;
+              const uint32_t boff = half * (NP * 256) + (kk >> 2) * (NP * 128) + (kk & 3) * 32;
               tc_mma(tmem + kColS + 128 * qt, umma_desc(sbase + kQ + aoff, 16, 1024),
                      umma_desc(sbase + kP + boff, 16, 1024), id_t, (half | kk) ? 1u : 0u);
             }
@@ -718,11 +731,17 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
     const uint32_t sc = tmem + lane_base + kColS + 128 * qt;  // this row's S columns
     const uint32_t oc = tmem + lane_base + kColO + 128 * qt;  // this row's O columns
-    // q.E table of row r: T[p] (log2 domain) at float index p ^ (r & 31), so
+    // q.E table of row r: T[p] (log2 domain) at index p ^ tsw -- float with
+    // tsw = r & 31 (NP = 64), half with tsw = 2 (r & 31) (NP = 128) -- so
     // that the 32 rows of a warp reading the same entry hit distinct banks;
     // a row's table is written and read by its own thread only
-    float* Tab = reinterpret_cast<float*>(smem + kTab + qt * 32768) + r * kMaxNpos;
-    const int tsw = r & 31;
+    using TabT = typename std::conditional<NP == 64, float, __half>::type;
+    TabT* Tab = reinterpret_cast<TabT*>(smem + kTab + qt * 32768) + r * NP;
+    const int tsw = NP == 64 ? (r & 31) : 2 * (r & 31);
+    auto tab_get = [&](int idx) -> float {
+      if constexpr (NP == 64) return Tab[idx ^ tsw];
+      else return __half2float(Tab[idx ^ tsw]);
+    };
     const float inv_sqrt_d = (float)(1.0 / p.scale);
     const float LOG2E = 1.4426950408889634f;
     const float scale2 = inv_sqrt_d * LOG2E;
@@ -735,23 +754,27 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
     {
       uint32_t v[32];
 #pragma unroll
-      for (int hb = 0; hb < 2; ++hb) {
+      for (int hb = 0; hb < NP / 32; ++hb) {
         CS_TMEM_LD32(sc + 32 * hb, v);
         tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 32; ++c) Tab[(32 * hb + c) ^ tsw] = __uint_as_float(v[c]) * LOG2E;
+        for (int c = 0; c < 32; ++c) {
+          const float tv = __uint_as_float(v[c]) * LOG2E;
+          if constexpr (NP == 64) Tab[(32 * hb + c) ^ tsw] = tv;
+          else Tab[(32 * hb + c) ^ tsw] = __float2half_rn(tv);
+        }
       }
     }
     tc_fence_before();
     mbar_arrive(mb + kBarTab + 8 * qt);  // the S columns are free for QK
-    const float tsat2 = Tab[(p.npos - 1) ^ tsw];  // saturated bias (log2 domain)
+    const float tsat2 = tab_get(p.npos - 1);  // saturated bias (log2 domain)
     // interpolated bias at position pos in [0, npos - 1] (position.py:339-344)
     auto bias_at = [&](float pos) {
       int lo;
       const float fl = floor_pos(pos, lo);
       const int hi = lo + 1 < p.npos ? lo + 1 : p.npos - 1;
-      const float t0 = Tab[lo ^ tsw];
-      return fmaf(pos - fl, Tab[hi ^ tsw] - t0, t0);
+      const float t0 = tab_get(lo);
+      return fmaf(pos - fl, tab_get(hi) - t0, t0);
     };
 
     float carry = 0.f;       // running count entering the newer edge of the tile
@@ -1352,7 +1375,8 @@ int configure(K kern, bool& done) {
 }
 
 bool same_prefill_shape(const cs_attn_params* a, const cs_attn_params* b) {
-  return a->hq == b->hq && a->hkv == b->hkv && a->in_dtype == b->in_dtype;
+  return a->hq == b->hq && a->hkv == b->hkv && a->in_dtype == b->in_dtype &&
+         (a->npos > 64) == (b->npos > 64);
 }
 
 }  // namespace
@@ -1368,7 +1392,7 @@ extern "C" int cs_cope_attn_prefill(const cs_attn_params* p, void* stream) {
   Args a;
   make_args(p, a);
   const int blocks = a.pairs_per_head * p->hkv;
-  static bool configured[2] = {false, false};
+  static bool configured[4] = {false, false, false, false};
   auto launch = [&](auto kern, int which) -> int {
     const int c = configure(kern, configured[which]);
     if (c != CS_OK) return c;
@@ -1376,8 +1400,12 @@ extern "C" int cs_cope_attn_prefill(const cs_attn_params* p, void* stream) {
     CS_LAUNCH_CHECK();
     return CS_OK;
   };
-  if (p->in_dtype == CS_BF16) return launch(cope_prefill_sm100<__nv_bfloat16>, 1);
-  return launch(cope_prefill_sm100<__half>, 0);
+  if (p->npos > 64) {
+    if (p->in_dtype == CS_BF16) return launch(cope_prefill_sm100<__nv_bfloat16, 128>, 3);
+    return launch(cope_prefill_sm100<__half, 128>, 2);
+  }
+  if (p->in_dtype == CS_BF16) return launch(cope_prefill_sm100<__nv_bfloat16, 64>, 1);
+  return launch(cope_prefill_sm100<__half, 64>, 0);
 }
 
 extern "C" int cs_cope_attn_prefill_batch(const cs_attn_params* params, int32_t count,
@@ -1389,7 +1417,7 @@ extern "C" int cs_cope_attn_prefill_batch(const cs_attn_params* params, int32_t 
     if (!prefill_supported(&params[k]) || !same_prefill_shape(&params[0], &params[k]))
       return CS_ERR_UNSUPPORTED;
   }
-  static bool configured[2] = {false, false};
+  static bool configured[4] = {false, false, false, false};
   for (int first = 0; first < count; first += kMaxPrefillBatch) {
     const int n = count - first < kMaxPrefillBatch ? count - first : kMaxPrefillBatch;
     BatchArgs b;  // the launch copies it into the kernel's parameter space
@@ -1412,9 +1440,12 @@ extern "C" int cs_cope_attn_prefill_batch(const cs_attn_params* params, int32_t 
       CS_LAUNCH_CHECK();
       return CS_OK;
     };
-    const int rc = params[first].in_dtype == CS_BF16
-                       ? launch(cope_prefill_sm100_batch<__nv_bfloat16>, 1)
-                       : launch(cope_prefill_sm100_batch<__half>, 0);
+    const bool wide = params[first].npos > 64;
+    const bool bf = params[first].in_dtype == CS_BF16;
+    const int rc = wide ? (bf ? launch(cope_prefill_sm100_batch<__nv_bfloat16, 128>, 3)
+                              : launch(cope_prefill_sm100_batch<__half, 128>, 2))
+                        : (bf ? launch(cope_prefill_sm100_batch<__nv_bfloat16, 64>, 1)
+                              : launch(cope_prefill_sm100_batch<__half, 64>, 0));
     if (rc != CS_OK) return rc;
   }
   return CS_OK;

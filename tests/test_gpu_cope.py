@@ -222,18 +222,31 @@ def test_paged_attention_reads_through_slots(cuda):
 @pytest.mark.parametrize("hq,hkv", [(32, 8), (8, 1)])
 def test_tensor_core_prefill_matches_generic_and_oracle(cuda, assoc, chunk, paged, hq, hkv):
     """cs_cope_attn_prefill (tcgen05) vs cs_cope_attn and the oracle."""
+    _tensor_core_case(cuda, assoc, chunk, paged, hq, hkv, 64)
+
+
+@pytest.mark.parametrize("npos", [96, 128, 101])
+@pytest.mark.parametrize("hq,hkv", [(32, 8), (8, 1)])
+def test_tensor_core_prefill_wide_position_tables(cuda, npos, hq, hkv):
+    """npos 65-128 (the Llama-70B TP8 slice has 128): the q.E table of a row
+    is kept in half precision; 101 (not a multiple of 4) takes the element-wise
+    E staging."""
+    _tensor_core_case(cuda, True, True, True, hq, hkv, npos)
+
+
+def _tensor_core_case(cuda, assoc, chunk, paged, hq, hkv, npos):
     import ctypes
 
     from cacheslide_b200 import _native as N
     from cacheslide_b200.position import _Holder, _base_params
 
     nq, nk, d, bs = 300, 2000, 128, 16
-    g = torch.Generator().manual_seed(hq * 7 + assoc + 2 * chunk + 4 * paged)
+    g = torch.Generator().manual_seed(hq * 7 + assoc + 2 * chunk + 4 * paged + npos)
     q = (torch.randn(nq, hq, d, generator=g) / d ** 0.5).to(torch.bfloat16).to(cuda)
     k = (torch.randn(nk, hkv, d, generator=g) / d ** 0.5).to(torch.bfloat16).to(cuda)
     v = torch.randn(nk, hkv, d, generator=g).to(torch.bfloat16).to(cuda)
     rows = torch.sort(torch.randperm(nk, generator=g)[:nq]).values.to(cuda)
-    E = torch.randn(d, 64, generator=g) * 0.02
+    E = torch.randn(d, npos, generator=g) * 0.02
     cope = _cope(E.numpy(), cuda)
     holder = _Holder(cope, cope.position_embeddings.detach())
     fixed = torch.rand(nk, generator=g) < 0.7
