@@ -52,6 +52,9 @@ def parse():
     ap.add_argument("--batched-attention", action="store_true",
                     help="with --per-request-streams: one attention launch for all requests "
                          "after their WCA / SLIDE chains")
+    ap.add_argument("--c5", action="store_true",
+                    help="also run the C5 tensor-parallel slice at one GPU (it runs by "
+                         "default whenever there are several ranks)")
     ap.add_argument("--per-request-streams", action="store_true",
                     help="one launch per request and stage, each request on its own stream "
                          "(default: every stage of the step as one launch for all requests, "
@@ -315,6 +318,65 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------ C5 slice
+def c5_slice(args, dev, rank: int, world: int) -> dict:
+    """The C5 layout (Llama-3-70B, 8 KV / 64 query heads split over the
+    ranks, 8 requests x 64K tokens in 32 chunks of 2K, WCA 10 %, npos 128):
+    one reuse-prefill layer with its collectives -- the WCA row-sum
+    all-reduces and the o_proj all-reduce of [active rows, 8192] bf16 --
+    timed per stage on the device, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from cacheslide_b200.tp_step import ShardedReuseStep, TPWorkloadConfig
+
+    cfg = TPWorkloadConfig()
+    step = ShardedReuseStep(cfg, dev, None, rank, world)
+    stream = torch.cuda.current_stream(dev)
+    steps = max(1, min(args.steps, 5))
+    for _ in range(2):
+        step.run(stream)
+    torch.cuda.synchronize(dev)
+    marks = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    for i in range(steps):
+        step.run(stream, marks[i])
+    torch.cuda.synchronize(dev)
+    step.check_status()
+    names = ["slide_scatter", "wca_sharded", "attention", "o_proj_gemm", "o_proj_all_reduce"]
+    per = [[m[j].elapsed_time(m[j + 1]) for j in range(5)] + [m[0].elapsed_time(m[5])]
+           for m in marks]
+    vals = torch.tensor([statistics.mean(x[j] for x in per) for j in range(6)],
+                        dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    ms = vals.tolist()
+    flops = step.attention_flops()
+    ar_bytes = step.proj.numel() * step.proj.element_size()
+    out = {
+        "workload": "c5-llama70b-tp: 8 requests x 64K (32 x 2K chunks), Hq/Hkv 64/8 split over "
+                    f"{world} rank(s) ({step.hq}/{step.hkv} per GPU), D=128, npos=128, WCA 10%",
+        "ms_per_step": ms[5],
+        "value": cfg.requests * cfg.seq / (ms[5] / 1e3),
+        "unit": "tok/s (per TP group)",
+        "stage_ms": dict(zip(names, ms[:5])),
+        "collective_share": (ms[4] + 0.0) / ms[5],
+        "attention_tflops_per_gpu": flops / (ms[2] / 1e3) / 1e12,
+        "o_proj_all_reduce": {"bytes": ar_bytes, "ms": ms[4],
+                              "bus_gbs": (2 * (world - 1) / world * ar_bytes / (ms[4] / 1e3) / 1e9
+                                          if world > 1 else None)},
+        "active_rows": sum(r.a for r in step.requests),
+        "steps": steps,
+        "note": "WCA stage includes its row-sum all-reduces and status agreements (host "
+                "synchronising, as ShardedWCAState is); max over ranks per stage",
+    }
+    del step
+    torch.cuda.empty_cache()
+    return out
+
+
 # ------------------------------------------------------------ our arm
 def main():
     args = parse()
@@ -506,6 +568,8 @@ def main():
     e2e_value = tokens * args.steps / (e2e_ms / 1e3)
     decode_value = args.requests * world / (dec_ms / 1e3)
 
+    c5 = c5_slice(args, dev, rank, world) if (world > 1 or args.c5) else None
+
     if rank == 0:
         pk, pk_kind = peaks()
         flops = attention_flops(work)  # per attention pass over this rank's requests
@@ -557,6 +621,8 @@ def main():
             "hot_bytes": hot_bytes(work),
             "hbm_kernels": hbm_report(work, hbm_ms, dec_ms, float(pk.get("hbm_gbs", 6650.0))),
         }
+        if c5 is not None:
+            line["c5_tp"] = c5
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

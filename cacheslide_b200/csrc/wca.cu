@@ -78,101 +78,189 @@ struct SelectSmem {
 };
 
 // Select the `slots` largest keys among available tokens, ties to the lower
-// index (the order of a stable descending argsort, wca.py:282-285).  Must be
-// called by every thread of one block of kSelectThreads threads.  `avail`
-// is a functor (int64 i) -> bool evaluated against the current state.
+// index (the order of a stable descending argsort, wca.py:282-285), for n
+// beyond what shared memory stages.  Must be called by every thread of one
+// block of kSelectThreads threads.  `avail` is a functor (int64 i) -> bool
+// evaluated against the current state.  The order codes stay in global
+// memory (L2): one pass counts the available keys and finds the first byte
+// where their codes differ; MSB-first 8-bit radix passes from that byte
+// (per-warp histogram copies) find the k-th code and stop once its bin is
+// taken whole; an ordered compaction stages the picks (code, index) in
+// shared memory, and a bitonic sort there puts them in rank order.
 template <typename Avail>
 __device__ int64_t block_select_topk(const double* __restrict__ keys, Avail avail, int64_t n,
                                      int64_t slots, uint8_t* __restrict__ selected,
                                      int64_t* __restrict__ chosen_out, SelectSmem& sm,
                                      double* stage_key, int* stage_idx, int32_t* status) {
-  const int tid = threadIdx.x;
-  // how many are available at all
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const unsigned full = 0xffffffffu;
+  __shared__ int hist4[4][256];
+  __shared__ uint64_t wlo[32], whi[32];
+  // how many are available, and the range of their codes
   int local = 0;
-  for (int64_t i = tid; i < n; i += blockDim.x) local += avail(i) ? 1 : 0;
-  int64_t total = block_sum(local, sm.warp_tot);
-  int64_t want = slots < total ? slots : total;
+  uint64_t lo = ~0ull, hi = 0ull;
+  for (int64_t i = tid; i < n; i += blockDim.x) {
+    if (!avail(i)) continue;
+    ++local;
+    const uint64_t c = order_code(keys[i]);
+    lo = c < lo ? c : lo;
+    hi = c > hi ? c : hi;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const uint64_t l2 = __shfl_xor_sync(full, lo, o), h2 = __shfl_xor_sync(full, hi, o);
+    lo = l2 < lo ? l2 : lo;
+    hi = h2 > hi ? h2 : hi;
+  }
+  if (lane == 0) {
+    wlo[warp] = lo;
+    whi[warp] = hi;
+  }
+  const int64_t total = block_sum(local, sm.warp_tot);  // also orders wlo / whi
+  const int64_t want = slots < total ? slots : total;
   if (want <= 0) return 0;
-  if (tid == 0) {
-    sm.prefix = 0;
-    sm.mask = 0;
-    sm.remaining = (int)want;
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    lo = lane < nw ? wlo[lane] : ~0ull;
+    hi = lane < nw ? whi[lane] : 0ull;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const uint64_t l2 = __shfl_xor_sync(full, lo, o), h2 = __shfl_xor_sync(full, hi, o);
+      lo = l2 < lo ? l2 : lo;
+      hi = h2 > hi ? h2 : hi;
+    }
+    if (lane == 0) {
+      sm.mask = lo ^ hi;
+      sm.prefix = hi;
+    }
   }
   __syncthreads();
-  // MSB-first radix select over 8-bit digits of the order code
-  for (int shift = 56; shift >= 0; shift -= 8) {
-    for (int b = tid; b < 256; b += blockDim.x) sm.hist[b] = 0;
+  const uint64_t diff = sm.mask;
+  int top = 56;  // first byte (from the top) where the available codes differ
+  while (top > 0 && ((diff >> top) & 255ull) == 0ull) top -= 8;
+  uint64_t mask = top < 56 ? (~0ull << (top + 8)) : 0ull;
+  uint64_t prefix = sm.prefix & mask;
+  int remaining = (int)want;
+  int* mine = hist4[warp & 3];
+  __syncthreads();
+  for (int shift = top; shift >= 0; shift -= 8) {
+    for (int b = tid; b < 4 * 256; b += blockDim.x) hist4[b >> 8][b & 255] = 0;
     __syncthreads();
-    const uint64_t prefix = sm.prefix, mask = sm.mask;
     for (int64_t i = tid; i < n; i += blockDim.x) {
       if (!avail(i)) continue;
-      uint64_t c = order_code(keys[i]);
-      if ((c & mask) == prefix) atomicAdd(&sm.hist[(c >> shift) & 255], 1);
+      const uint64_t c = order_code(keys[i]);
+      if ((c & mask) == prefix) atomicAdd(&mine[(c >> shift) & 255], 1);
     }
     __syncthreads();
-    if (tid == 0) {
-      int need = sm.remaining, above = 0, bin = 0;
-      for (int b = 255; b >= 0; --b) {
-        if (above + sm.hist[b] >= need) {
-          bin = b;
-          break;
-        }
-        above += sm.hist[b];
+    if (warp == 0) {
+      // lane l owns bins 255-8l .. 248-8l (descending)
+      int cnt[8], sum = 0;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int b = 255 - 8 * lane - q;
+        cnt[q] = hist4[0][b] + hist4[1][b] + hist4[2][b] + hist4[3][b];
+        sum += cnt[q];
       }
-      sm.remaining = need - above;  // how many equal-to-threshold keys to take
-      sm.prefix = prefix | ((uint64_t)bin << shift);
-      sm.mask = mask | (255ull << shift);
+      int inc = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(full, inc, o);
+        if (lane >= o) inc += t;
+      }
+      const unsigned hit = __ballot_sync(full, inc >= remaining);
+      const int owner = __ffs(hit) - 1;
+      if (lane == owner) {
+        int above = inc - sum, bsel = 0, inbin = 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          if (above + cnt[q] >= remaining) {
+            bsel = 255 - 8 * lane - q;
+            inbin = cnt[q];
+            break;
+          }
+          above += cnt[q];
+        }
+        sm.prefix = prefix | ((uint64_t)bsel << shift);
+        sm.remaining = remaining - above;
+        sm.whole_bin = remaining - above == inbin;
+      }
     }
     __syncthreads();
+    prefix = sm.prefix;
+    remaining = sm.remaining;
+    mask |= 255ull << shift;
+    const bool whole = sm.whole_bin != 0;
+    __syncthreads();
+    if (whole) break;  // every code with these leading bytes is a pick
   }
-  const uint64_t thr = sm.prefix;
-  const int take_eq = sm.remaining;
-  // mark picks: code > thr, or code == thr among the first take_eq by index
+  // ordered compaction: code above the k-th's leading bytes, or equal to them
+  // among the first `remaining` by index
   if (tid == 0) {
     sm.chosen_count = 0;
     sm.eq_taken = 0;
   }
   __syncthreads();
   const bool stage = chosen_out != nullptr && want <= kSelectMaxChosen;
+  uint64_t* scode = reinterpret_cast<uint64_t*>(stage_key);
   for (int64_t base = 0; base < n; base += blockDim.x) {
-    int64_t i = base + tid;
-    bool av = i < n && avail(i);
-    uint64_t c = av ? order_code(keys[i]) : 0;
-    int eq = (av && c == thr) ? 1 : 0;
-    int eq_rank = block_inclusive_scan(eq, sm.warp_tot) - eq + sm.eq_taken;
-    bool pick = av && (c > thr || (eq && eq_rank < take_eq));
-    int pk = pick ? 1 : 0;
-    int slot = block_inclusive_scan(pk, sm.warp_tot) - pk + sm.chosen_count;
+    const int64_t i = base + tid;
+    const bool av = i < n && avail(i);
+    const uint64_t c = av ? order_code(keys[i]) : 0ull;
+    const int gt = (av && (c & mask) > prefix) ? 1 : 0;
+    const int eq = (av && (c & mask) == prefix) ? 1 : 0;
+    const int inc = block_inclusive_scan(gt | (eq << 16), sm.warp_tot);
+    const int gt_before = (inc & 0xFFFF) - gt + sm.chosen_count;
+    const int eq_before = (inc >> 16) - eq + sm.eq_taken;
+    const bool pick = gt || (eq && eq_before < remaining);
     if (pick) {
       selected[i] = 1;
       if (stage) {
-        stage_key[slot] = keys[i];
+        const int slot = gt_before + (eq_before < remaining ? eq_before : remaining);
+        scode[slot] = c;
         stage_idx[slot] = (int)i;
       }
     }
     __syncthreads();
     if (tid == blockDim.x - 1) {
-      sm.eq_taken = eq_rank + eq;
-      sm.chosen_count = slot + pk;
+      sm.chosen_count = gt_before + gt;
+      sm.eq_taken = eq_before + eq;
     }
     __syncthreads();
   }
-  const int k = sm.chosen_count;
+  const int k = (int)want;
   if (chosen_out != nullptr) {
     if (!stage) {
       if (tid == 0) report(status, CS_ST_SLOT_RANGE);
       return k;
     }
-    // rank each pick by (key desc, index asc) and place it
-    for (int a = tid; a < k; a += blockDim.x) {
-      double ka = stage_key[a];
-      int ia = stage_idx[a], rank = 0;
-      for (int b = 0; b < k; ++b) {
-        double kb = stage_key[b];
-        rank += (kb > ka || (kb == ka && stage_idx[b] < ia)) ? 1 : 0;
-      }
-      chosen_out[rank] = ia;
+    // bitonic sort of the picks by (code descending, index ascending) over
+    // the next power of two, padding after every pick
+    int m = 1;
+    while (m < k) m <<= 1;
+    for (int a = k + tid; a < m; a += blockDim.x) {
+      scode[a] = 0ull;
+      stage_idx[a] = 0x7FFFFFFF;
     }
+    __syncthreads();
+    for (int w = 2; w <= m; w <<= 1) {
+      for (int j = w >> 1; j > 0; j >>= 1) {
+        for (int t = tid; t < (m >> 1); t += blockDim.x) {
+          const int lo2 = 2 * t - (t & (j - 1)), hi2 = lo2 + j;
+          const uint64_t cl = scode[lo2], ch = scode[hi2];
+          const int il = stage_idx[lo2], ih = stage_idx[hi2];
+          const bool hi_first = ch > cl || (ch == cl && ih < il);
+          const bool lo_first = cl > ch || (cl == ch && il < ih);
+          if ((lo2 & w) == 0 ? hi_first : lo_first) {
+            scode[lo2] = ch;
+            scode[hi2] = cl;
+            stage_idx[lo2] = ih;
+            stage_idx[hi2] = il;
+          }
+        }
+        __syncthreads();
+      }
+    }
+    for (int a = tid; a < k; a += blockDim.x) chosen_out[a] = stage_idx[a];
   }
   __syncthreads();
   return k;
@@ -763,7 +851,7 @@ __global__ void cosine_kernel(Rows<T> a, Rows<T> b, const int64_t* __restrict__ 
 // (f - c)^2, nrm = sum of c^2, cos = sum over its heads of the head cosine /
 // heads_total.  Summed over the ranks these are the squared deviation, the
 // norm and the head-mean cosine of all heads (wca.py:55-112).
-template <typename T, int G8>
+template <typename T, int G8, int IT>
 __global__ void row_sums_kernel(Rows<T> c, const int64_t* __restrict__ crows, Rows<T> f, int64_t n,
                                 int64_t heads, int64_t dim, int64_t heads_total, double* dev_out,
                                 double* nrm_out, double* cos_out, int32_t* status) {
@@ -773,12 +861,8 @@ __global__ void row_sums_kernel(Rows<T> c, const int64_t* __restrict__ crows, Ro
     const int64_t crow = crows ? crows[r] : r;
     double dev = 0.0, nrm = 0.0, cs = 0.0;
     bool in_ok = true;
-    if (dev_out || nrm_out) {
-      if constexpr (G8 > 0)
-        in_ok = row_dev_nrm_vec<T, G8>(c, crow, f, r, heads, dev, nrm);
-      else
-        in_ok = row_dev_nrm(c, crow, f, r, heads, dim, dev, nrm);
-    }
+    if (dev_out || nrm_out)  // the summation of deviation_kernel / update_kernel
+      in_ok = row_dev<T, G8, IT>(c, crow, f, r, heads, dim, dev, nrm);
     if (cos_out) {
       if constexpr (G8 > 0)
         cs = row_cosine_vec<T, G8>(f, r, c, crow, heads);
@@ -1452,8 +1536,8 @@ extern "C" int cs_wca_row_sums(const void* cached, int64_t c_stride_row, int64_t
   CS_DISPATCH_FLOAT(dtype, T, {
     const int g8 = vec_groups<T>(dim, {cached, fresh},
                                  {c_stride_row, c_stride_head, f_stride_row, f_stride_head});
-    with_g8<T>(g8, [&](auto G) {
-      row_sums_kernel<T, decltype(G)::value>
+    with_vec<T>(g8, row_iters(g8, heads), [&](auto G, auto I) {
+      row_sums_kernel<T, decltype(G)::value, decltype(I)::value>
           <<<row_grid(n, threads / 32), threads, 0, as_stream(stream)>>>(
               rows_of<T>(cached, c_stride_row, c_stride_head), cached_rows,
               rows_of<T>(fresh, f_stride_row, f_stride_head), n, heads, dim, heads_total,

@@ -55,13 +55,21 @@ def exchange_row_sums(partial: Tensor, group=None) -> Tensor:
     afterwards every rank holds the sums over all heads (wca.py:55-112)."""
     if partial.dtype != torch.float64 or partial.ndim != 2:
         raise ValueError("row sums must be a float64 [k, n] tensor")
+    if _single(group):  # one process holds every head: its sums are complete
+        return partial
     dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=group)
     return partial
+
+
+def _single(group) -> bool:
+    return group is None and not (dist.is_available() and dist.is_initialized())
 
 
 def agree_status(bits: int, device, group=None) -> int:
     """The union (bitwise max) of every rank's status bits, so that every rank
     raises the same error or none does before anything is committed."""
+    if _single(group):
+        return int(bits)
     flag = torch.tensor([int(bits)], dtype=torch.int32, device=device)
     dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=group)
     return int(flag.item())
