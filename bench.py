@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--batched-attention", action="store_true",
                     help="with --per-request-streams: one attention launch for all requests "
                          "after their WCA / SLIDE chains")
+    ap.add_argument("--no-c4", action="store_true",
+                    help="skip the multi-session chat slice (run at one GPU by default)")
     ap.add_argument("--c5", action="store_true",
                     help="also run the C5 tensor-parallel slice at one GPU (it runs by "
                          "default whenever there are several ranks)")
@@ -377,6 +379,58 @@ def c5_slice(args, dev, rank: int, world: int) -> dict:
     return out
 
 
+# ------------------------------------------------------------ C4 slice
+def c4_slice(args, dev) -> dict:
+    """The multi-session chat slice (C4): 32 sessions at turn 8 of
+    conversations adding 256-1024 tokens a turn plus 128 decoded tokens;
+    a turn = WCA + SLIDE relocation of the selected history rows + blend +
+    attention of the active rows, then 128 batched decode steps."""
+    import torch
+
+    from cacheslide_b200.chat import ChatConfig, ChatTurnStep
+
+    cfg = ChatConfig()
+    step = ChatTurnStep(cfg, dev)
+    stream = torch.cuda.current_stream(dev)
+    s = stream.cuda_stream
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(2):
+        step.prefill(s)
+        step.decode(s)
+    turns = max(1, min(args.steps, 5))
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(turns)]
+    torch.cuda.synchronize(dev)
+    for i in range(turns):
+        flush.fill_(i & 0xFF)
+        ev[i][0].record(stream)
+        step.prefill(s)
+        ev[i][1].record(stream)
+        step.decode(s)
+        ev[i][2].record(stream)
+    torch.cuda.synchronize(dev)
+    step.check_status()
+    pre = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+    dec = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+    reloc_rows = sum(x.reloc_src.numel() for x in step.sessions)
+    out = {
+        "workload": "c4-multi-session-chat: 32 sessions at turn 8 (+256-1024 tokens a turn, "
+                    "128 decoded), Hq=32, Hkv=8, D=128, npos=64, WCA 15%, SLIDE relocation of "
+                    "the selected history rows every turn",
+        "prompt_tokens": step.prompt_tokens(),
+        "new_tokens": step.new_tokens(),
+        "relocated_rows": reloc_rows,
+        "prefill_ms": pre,
+        "prefill_tok_s": step.prompt_tokens() / (pre / 1e3),
+        "decode_ms_per_token": dec / cfg.decode_tokens,
+        "decode_tok_s": cfg.sessions * cfg.decode_tokens / (dec / 1e3),
+        "turn_ms": pre + dec,
+        "turns_timed": turns,
+    }
+    del step
+    torch.cuda.empty_cache()
+    return out
+
+
 # ------------------------------------------------------------ our arm
 def main():
     args = parse()
@@ -569,6 +623,7 @@ def main():
     decode_value = args.requests * world / (dec_ms / 1e3)
 
     c5 = c5_slice(args, dev, rank, world) if (world > 1 or args.c5) else None
+    c4 = c4_slice(args, dev) if (world == 1 and not args.no_c4) else None
 
     if rank == 0:
         pk, pk_kind = peaks()
@@ -623,6 +678,8 @@ def main():
         }
         if c5 is not None:
             line["c5_tp"] = c5
+        if c4 is not None:
+            line["c4_chat"] = c4
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

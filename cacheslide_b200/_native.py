@@ -128,10 +128,23 @@ class CommitItem(ctypes.Structure):
     ]
 
 
+class QKVParams(ctypes.Structure):
+    """cs_qkv_params: the selective-layer QKV projection (cs_qkv_gather_lora)."""
+    _fields_ = [
+        ("src0", _p), ("src0_stride", _i64), ("src0_rows", _i64),
+        ("src1", _p), ("src1_stride", _i64), ("src1_rows", _i64),
+        ("row_src", _p), ("row_idx", _p), ("a", _i64), ("hidden", _i64), ("n_out", _i64),
+        ("w", _p), ("lora_a", _p), ("lora_b", _p), ("rank", _i32),
+        ("out", _p), ("out_stride", _i64), ("dtype", _i32), ("status", _p),
+    ]
+
+
 _SIGNATURES = {
     "cs_slide_gather": [ctypes.POINTER(PagedKV), _p, _i64, _p, _p, _i64, _i64, _p, _p],
     "cs_slide_scatter": [ctypes.POINTER(PagedKV), _p, _p, _i64, _p, _p, _i64, _i64, _p, _p],
     "cs_slide_relocate": [ctypes.POINTER(PagedKV), _p, _p, _i64, _p, _p],
+    "cs_slide_pack_pages": [ctypes.POINTER(PagedKV), _p, _i64, _p, _p, _p],
+    "cs_slide_unpack_pages": [ctypes.POINTER(PagedKV), _p, _i64, _p, _p, _p],
     "cs_slide_scatter_batch": [ctypes.POINTER(PagedKV), ctypes.POINTER(ScatterItem), _i32, _p],
     "cs_wca_initialize_batch": [ctypes.POINTER(InitializeItem), _i32, _i64, _i64, _i32, _f64,
                                 _i32, _p],
@@ -153,6 +166,7 @@ _SIGNATURES = {
                       _p, _p],
     "cs_wca_commit": [_p, _i64, _p, _p, _f64, _i32, _i64, _i64, _p, _p, _p, _p, _p, _p, _p,
                       _p, _p, _p],
+    "cs_qkv_gather_lora": [ctypes.POINTER(QKVParams), _p],
     "cs_cope_attn": [ctypes.POINTER(AttnParams), _p],
     "cs_cope_attn_prefill": [ctypes.POINTER(AttnParams), _p],
     "cs_cope_attn_prefill_batch": [ctypes.POINTER(AttnParams), _i32, _p],

@@ -97,9 +97,6 @@ constexpr uint32_t kSmemBytes = kMeta + kMetaBytes;  // 229,808 B (limit 232,448
 // TMEM columns: S of each tile (P packed over its first 64 columns), O of
 // each tile; T = Q E lands in the first NP S columns of its tile at start
 constexpr uint32_t kColS = 0, kColO = 256;  // + 128 * tile
-__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
-}
 // named barrier 1: the 128 producer threads
 // tile::gather4: rows r0..r3 of a 2-D tensor map, 64 elements from column x,
 // into 4 consecutive 128-byte rows at dst (the map's 128-byte swizzle applies)

@@ -300,6 +300,97 @@ __global__ void __launch_bounds__(256) scatter_rows_batch_kernel(
   }
 }
 
+// Page images for spill / reload: page q of the list is the block_size
+// consecutive slots pages[q] * bs .. + bs - 1 (a native block, or sidecar
+// rows), laid out as one native block [kv_head][offset][2D] in `img` (the
+// record format of the cache itself).  One warp per slot row; pack copies
+// records into the image, unpack writes them back.
+template <int UPL, bool kPack>
+__global__ void __launch_bounds__(256) page_image_kernel(
+    PagedView pv, const int64_t* __restrict__ pages, int64_t count, char* img, int uh_shift,
+    int32_t* status) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int uh_mask = (1 << uh_shift) - 1;
+  const int64_t rows = count * pv.bs;
+  const int64_t half = pv.head_dim * pv.esize;                 // bytes of a K or V half
+  const int64_t img_head = pv.bs * 2 * half, img_page = pv.kv_heads * img_head;
+  for (int64_t g = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); g < rows;
+       g += warps) {
+    const int64_t q = g / pv.bs, o = g - q * pv.bs;
+    const int64_t first = pages[q] * pv.bs, s = first + o;
+    if (pages[q] < 0 || !pv.valid(first)) {  // the page is not in the arena
+      if (lane == 0 && o == 0) report(status, CS_ST_SLOT_RANGE);
+      continue;
+    }
+    char* base = img + q * img_page + o * 2 * half;
+    if (!pv.valid(s)) {  // past the end of a partial sidecar page: zeros in the image
+      if constexpr (kPack) {
+        for (int64_t h = 0; h < pv.kv_heads; ++h)
+          for (int64_t b = lane * 16; b < 2 * half; b += 32 * 16)
+            *reinterpret_cast<uint4*>(base + h * img_head + b) = make_uint4(0, 0, 0, 0);
+      }
+      continue;
+    }
+    char *rk, *rv;
+    int64_t hs;
+    pv.record(s, rk, rv, hs);
+    uint4 kx[UPL], vx[UPL];
+#pragma unroll
+    for (int k = 0; k < UPL; ++k) {
+      const int u = lane + 32 * k;
+      const int64_t h = u >> uh_shift, off = (int64_t)(u & uh_mask) * 16;
+      if constexpr (kPack) {
+        kx[k] = *reinterpret_cast<const uint4*>(rk + h * hs + off);
+        vx[k] = *reinterpret_cast<const uint4*>(rv + h * hs + off);
+      } else {
+        kx[k] = *reinterpret_cast<const uint4*>(base + h * img_head + off);
+        vx[k] = *reinterpret_cast<const uint4*>(base + h * img_head + half + off);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < UPL; ++k) {
+      const int u = lane + 32 * k;
+      const int64_t h = u >> uh_shift, off = (int64_t)(u & uh_mask) * 16;
+      if constexpr (kPack) {
+        *reinterpret_cast<uint4*>(base + h * img_head + off) = kx[k];
+        *reinterpret_cast<uint4*>(base + h * img_head + half + off) = vx[k];
+      } else {
+        *reinterpret_cast<uint4*>(rk + h * hs + off) = kx[k];
+        *reinterpret_cast<uint4*>(rv + h * hs + off) = vx[k];
+      }
+    }
+  }
+}
+
+// the same page images for any view: one thread per element
+template <typename V, bool kPack>
+__global__ void page_image_elem_kernel(PagedView pv, const int64_t* __restrict__ pages,
+                                       int64_t count, char* img, int32_t* status) {
+  const int64_t d2 = 2 * pv.head_dim;
+  const int64_t total = count * pv.kv_heads * pv.bs * d2;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    // image element t = ((q * kv_heads + h) * bs + o) * 2D + e
+    const int64_t e = t % d2, rest = t / d2;
+    const int64_t o = rest % pv.bs, qh = rest / pv.bs;
+    const int64_t h = qh % pv.kv_heads, q = qh / pv.kv_heads;
+    const int64_t first = pages[q] * pv.bs, s = first + o;
+    V* dst = reinterpret_cast<V*>(img) + t;
+    if (pages[q] < 0 || !pv.valid(first)) {
+      if (e == 0 && o == 0 && h == 0) report(status, CS_ST_SLOT_RANGE);
+      continue;
+    }
+    if (!pv.valid(s)) {
+      if constexpr (kPack) *dst = V(0);
+      continue;
+    }
+    V* rec = reinterpret_cast<V*>(pv.addr(s, h, e));
+    if constexpr (kPack) *dst = *rec;
+    else *rec = *dst;
+  }
+}
+
 // warps for n rows: one row per warp up to 16 CTAs of 8 warps per SM
 int row_grid_for(int64_t n) {
   int64_t blocks = (n + 7) / 8;
@@ -492,4 +583,54 @@ extern "C" int cs_slide_scatter_batch(const cs_paged_kv* kv, const cs_slide_scat
     CS_LAUNCH_CHECK();
   }
   return CS_OK;
+}
+
+namespace {
+int page_images(const cs_paged_kv* kv, const int64_t* pages, int64_t count, void* image,
+                int32_t* status, void* stream, bool pack) {
+  CS_HOST_CHECK(check_view(kv) && count >= 0);
+  if (count == 0) return CS_OK;
+  CS_HOST_CHECK(pages && image);
+  PagedView pv = PagedView::make(*kv);
+  RowGeom rg{};
+  auto s = as_stream(stream);
+  if (!pv.vec16() || !row_geom(pv, rg) || (reinterpret_cast<uintptr_t>(image) & 15)) {
+    const int64_t units = count * pv.kv_heads * pv.bs * 2 * pv.head_dim;
+    const int g = grid_for(units, 256);
+    char* img = static_cast<char*>(image);
+    switch (pv.esize) {
+      case 2: pack ? page_image_elem_kernel<uint16_t, true><<<g, 256, 0, s>>>(pv, pages, count, img, status)
+                   : page_image_elem_kernel<uint16_t, false><<<g, 256, 0, s>>>(pv, pages, count, img, status); break;
+      case 4: pack ? page_image_elem_kernel<uint32_t, true><<<g, 256, 0, s>>>(pv, pages, count, img, status)
+                   : page_image_elem_kernel<uint32_t, false><<<g, 256, 0, s>>>(pv, pages, count, img, status); break;
+      default: pack ? page_image_elem_kernel<uint64_t, true><<<g, 256, 0, s>>>(pv, pages, count, img, status)
+                    : page_image_elem_kernel<uint64_t, false><<<g, 256, 0, s>>>(pv, pages, count, img, status); break;
+    }
+    CS_LAUNCH_CHECK();
+    return CS_OK;
+  }
+  const int64_t rows = count * pv.bs;
+  auto go = [&](auto kern) {
+    kern<<<row_grid_for(rows), 256, 0, s>>>(pv, pages, count, static_cast<char*>(image),
+                                            rg.uh_shift, status);
+  };
+  switch (rg.upl) {
+    case 1: pack ? go(page_image_kernel<1, true>) : go(page_image_kernel<1, false>); break;
+    case 2: pack ? go(page_image_kernel<2, true>) : go(page_image_kernel<2, false>); break;
+    case 4: pack ? go(page_image_kernel<4, true>) : go(page_image_kernel<4, false>); break;
+    default: pack ? go(page_image_kernel<8, true>) : go(page_image_kernel<8, false>); break;
+  }
+  CS_LAUNCH_CHECK();
+  return CS_OK;
+}
+}  // namespace
+
+extern "C" int cs_slide_pack_pages(const cs_paged_kv* kv, const int64_t* pages, int64_t count,
+                                   void* image, int32_t* status, void* stream) {
+  return page_images(kv, pages, count, image, status, stream, true);
+}
+
+extern "C" int cs_slide_unpack_pages(const cs_paged_kv* kv, const int64_t* pages, int64_t count,
+                                     const void* image, int32_t* status, void* stream) {
+  return page_images(kv, pages, count, const_cast<void*>(image), status, stream, false);
 }

@@ -175,6 +175,11 @@ __device__ __forceinline__ void cp_async16_hint(uint32_t dst, const void* src, b
                "l"(src), "r"(valid ? 16 : 0), "l"(policy)
                : "memory");
 }
+// an arrival on `bar` once every earlier cp.async of this thread has landed
+// (the barrier's count includes these arrivals)
+__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() {
   asm volatile("cp.async.commit_group;" ::: "memory");
 }

@@ -30,6 +30,7 @@ import queue
 import threading
 from collections.abc import Iterable, Sequence
 from concurrent.futures import Future
+from dataclasses import dataclass
 
 import torch
 
@@ -117,6 +118,17 @@ class _Waiter:
                 done.set_exception(error)
             else:
                 done.set_result(None)
+
+
+@dataclass
+class PageSpill:
+    """Pages written back by ``NativePagedKV.spill``: page ids in spill order,
+    their images ``[pages, kv_heads, block_size, 2 * head_dim]`` in pinned
+    host memory, and a Future that completes when the copy has landed."""
+
+    pages: tuple[int, ...]
+    images: torch.Tensor
+    future: Future
 
 
 class NativePagedKV:
@@ -518,6 +530,66 @@ class NativePagedKV:
         ranked = sorted(eligible,
                         key=lambda p: (p["dirty"], -p["selected_count"], p["page_id"]))
         return tuple(p["page_id"] for p in ranked)
+
+    def spill(self, pages: Sequence[int] | None = None) -> PageSpill:
+        """Write back pages: their images (one native block each, the
+        records of its ``block_size`` slots; ``cs_slide_pack_pages``) copied
+        into pinned host memory.  ``pages`` defaults to ``spill_order()`` (the
+        reference only advises that order, paged.py:530-559).  The pages'
+        slots stay pinned until the host copy has landed, so no relocation or
+        write lands in them meanwhile; the returned ``PageSpill`` carries the
+        page ids, the host images and a Future of the copy."""
+        with self._lock:
+            ids = list(self.spill_order() if pages is None else pages)
+            if any(type(p) is not int or p < 0 for p in ids) or len(set(ids)) != len(ids):
+                raise ValueError("pages must be distinct nonnegative page ids")
+            bs = self.block_size
+            slots = [p * bs + o for p in ids for o in range(bs)]
+            mapped = set(self.slot_map.snapshot().values())
+            guard = self.slot_map.pin_slots([x for x in slots if x in mapped])
+            guard.__enter__()
+            try:
+                device = self.cache.device
+                shape = (len(ids), self.kv_heads, bs, 2 * self.head_dim)
+                image = self.cache.new_empty(shape)
+                host = torch.empty(shape, dtype=self.cache.dtype, pin_memory=True)
+                launch = _Launch(device)
+                if ids:
+                    page_t = torch.tensor(ids, dtype=torch.int64).to(device, non_blocking=True)
+                    view = self.device_view()
+                    N.check(N.load().cs_slide_pack_pages(
+                        ctypes.byref(view), page_t.data_ptr(), len(ids), image.data_ptr(),
+                        launch.status_ptr, N.stream_of(device)), "cs_slide_pack_pages")
+                    host.copy_(image, non_blocking=True)
+                future = _Waiter.submit(launch.enqueue_done())
+            except BaseException:
+                guard.__exit__(None, None, None)
+                raise
+            # the pins end when the copy has landed (or failed)
+            future.add_done_callback(lambda _f: guard.__exit__(None, None, None))
+            return PageSpill(tuple(ids), host, future)
+
+    def reload(self, spilled: PageSpill) -> None:
+        """Write a spill's page images back into the same pages
+        (``cs_slide_unpack_pages``), with the slots' write guards held until
+        the device writes complete."""
+        with self._lock:
+            spilled.future.result()
+            ids = list(spilled.pages)
+            bs = self.block_size
+            slots = [p * bs + o for p in ids for o in range(bs)]
+            mapped = set(self.slot_map.snapshot().values())
+            with self.slot_map.write_guard([x for x in slots if x in mapped]):
+                device = self.cache.device
+                launch = _Launch(device)
+                if ids:
+                    image = spilled.images.to(device, non_blocking=True)
+                    page_t = torch.tensor(ids, dtype=torch.int64).to(device, non_blocking=True)
+                    view = self.device_view()
+                    N.check(N.load().cs_slide_unpack_pages(
+                        ctypes.byref(view), page_t.data_ptr(), len(ids), image.data_ptr(),
+                        launch.status_ptr, N.stream_of(device)), "cs_slide_unpack_pages")
+                launch.enqueue_done().wait()
 
     def stats(self) -> dict[str, int]:
         with self._lock:

@@ -129,6 +129,23 @@ typedef struct {
 CS_API int cs_slide_scatter_batch(const cs_paged_kv* kv, const cs_slide_scatter_item* items,
                                   int32_t count, void* stream);
 
+/*
+ * Page images for the dirty-page writeback that NativePagedKV.spill_order
+ * only advises (paged.py:530-559, slide.py:119-156): page q of `pages` is the
+ * block_size consecutive slots pages[q] * block_size .. + block_size - 1 (a
+ * native block, or sidecar rows past the native pool), and its image is one
+ * native block [kv_head][block_size][2*head_dim] (K then V per record) at
+ * `image` + q * kv_heads * block_size * 2*head_dim elements.  Pack copies
+ * the pages' records into the images (for a host copy), unpack writes
+ * images back into the same slots (a reload).  Any view strides; slots
+ * past the end of a partial sidecar page read as zeros; a page outside the
+ * arena sets CS_ST_SLOT_RANGE and is skipped.
+ */
+CS_API int cs_slide_pack_pages(const cs_paged_kv* kv, const int64_t* pages, int64_t count,
+                               void* image, int32_t* status, void* stream);
+CS_API int cs_slide_unpack_pages(const cs_paged_kv* kv, const int64_t* pages, int64_t count,
+                                 const void* image, int32_t* status, void* stream);
+
 /* ------------------------------------------------------------------ WCA */
 /*
  * Per-token squared deviation and adaptation weight in float64
@@ -325,6 +342,41 @@ typedef struct {
 /* one thread block per request; threshold and distance_mode are shared */
 CS_API int cs_wca_commit_batch(const cs_wca_commit_item* items, int32_t count, double threshold,
                                int32_t distance_mode, void* stream);
+
+/* ------------------------------------------------- selective layer loop */
+/*
+ * The QKV projection of a layer's active rows (runtime.py:409-460 with the
+ * adapter deltas of artifacts.py:189-193), on the tensor cores:
+ *   out[r] = x_r W^T + round16(x_r A^T) B^T,
+ *   x_r = (row_src[r] == 0 ? src0 : src1)[row_idx[r]]
+ * src0 holds the previous layer's output rows (continuing rows), src1 the
+ * layer's input snapshot (rows newly selected, restored); the gather is the
+ * GEMM's A-operand load.  W [n_out, hidden], A [rank, hidden], B [n_out,
+ * rank], row-major 16-bit (bf16 or fp16, one dtype for all); out [a, n_out]
+ * in active-row order, float32 accumulation.  hidden % 64 == 0, n_out % 256
+ * == 0, rank in {0, 8, ..., 32}, 16-byte aligned rows
+ * (CS_ERR_UNSUPPORTED otherwise).  A row index outside its source sets
+ * CS_ST_SLOT_RANGE and computes a zero row.
+ */
+typedef struct {
+  const void* src0;
+  int64_t src0_stride, src0_rows; /* stride in elements */
+  const void* src1;
+  int64_t src1_stride, src1_rows;
+  const int32_t* row_src; /* [a] 0 or 1 */
+  const int64_t* row_idx; /* [a] */
+  int64_t a, hidden, n_out;
+  const void* w;
+  const void* lora_a; /* or NULL when rank == 0 */
+  const void* lora_b;
+  int32_t rank;
+  void* out;
+  int64_t out_stride;
+  int32_t dtype;
+  int32_t* status;
+} cs_qkv_params;
+
+CS_API int cs_qkv_gather_lora(const cs_qkv_params* p, void* stream);
 
 /* ------------------------------------------------------------ attention */
 typedef enum {

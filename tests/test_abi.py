@@ -60,7 +60,8 @@ def test_struct_sizes_equal_the_c_compilers(tmp_path):
         pytest.skip("no C compiler")
     pairs = {"cs_paged_kv": N.PagedKV, "cs_attn_params": N.AttnParams,
              "cs_slide_scatter_item": N.ScatterItem, "cs_wca_initialize_item": N.InitializeItem,
-             "cs_wca_update_item": N.UpdateItem, "cs_wca_commit_item": N.CommitItem}
+             "cs_wca_update_item": N.UpdateItem, "cs_wca_commit_item": N.CommitItem,
+             "cs_qkv_params": N.QKVParams}
     src = tmp_path / "sizes.c"
     src.write_text('#include <stdio.h>\n#include "cacheslide_b200.h"\nint main(void) {\n'
                    + "".join(f'  printf("{k} %zu\\n", sizeof({k}));\n' for k in pairs)
