@@ -314,20 +314,20 @@ static_assert(sizeof(BatchArgs) <= 32000, "batched prefill arguments exceed the 
 
 // one CTA: query-tile pair `pair` of KV head g of request a; NP = 64 or 128
 // bounds npos (the q.E table's width)
-template <typename T, int NP>
+template <typename T, int NP, bool TBL>
 __device__ __forceinline__ void prefill_cta(const Args& a, int g, int pair);
 
-template <typename T, int NP>
+template <typename T, int NP, bool TBL>
 __global__ void __launch_bounds__(kThreads, 1) cope_prefill_sm100(const __grid_constant__ Args a) {
   // the heaviest (latest) pairs of all KV heads are launched first, so the
   // light ones fill the tail of the grid
-  prefill_cta<T, NP>(a, blockIdx.x % a.p.hkv, a.pairs_per_head - 1 - blockIdx.x / a.p.hkv);
+  prefill_cta<T, NP, TBL>(a, blockIdx.x % a.p.hkv, a.pairs_per_head - 1 - blockIdx.x / a.p.hkv);
 }
 
 // all requests of a step in one grid, heaviest pairs of every request first
 // (pair rank j from the top, then request, then KV head); a request with
 // fewer pairs leaves its CTAs of the lowest ranks empty
-template <typename T, int NP>
+template <typename T, int NP, bool TBL>
 __global__ void __launch_bounds__(kThreads, 1)
     cope_prefill_sm100_batch(const __grid_constant__ BatchArgs b) {
   const int per_rank = b.count * b.hkv;
@@ -335,10 +335,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const Args& a = b.r[ri];
   const int pair = a.pairs_per_head - 1 - j;
   if (pair < 0) return;
-  prefill_cta<T, NP>(a, blockIdx.x % b.hkv, pair);
+  prefill_cta<T, NP, TBL>(a, blockIdx.x % b.hkv, pair);
 }
 
-template <typename T, int NP>
+// TBL: the canonical-table mode (CanonicalPositionPolicy, attention.py:
+// 32-57): a row with a table row (q_row >= 0) takes, at every key with a
+// table column (k_ord >= 0), the table's position instead of its count, and
+// with `strict` checks the combined path (validate_contextual_path,
+// position.py:28-114); such rows always take the contextual path.
+template <typename T, int NP, bool TBL>
 __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const int pair) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
@@ -725,6 +730,18 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
     const float* offrow =
         (row_ok && chunked) ? p.chunk_off + (int64_t)h * p.co_stride_h + i * p.co_stride_q
                             : nullptr;
+    // canonical-table mode: this row's table row (float32 positions) or -1
+    const int32_t qrow = (TBL && row_ok) ? p.q_row[i] : -1;
+    const float* tabrow =
+        qrow >= 0 ? static_cast<const float*>(p.table) + (int64_t)h * p.tb_stride_h +
+                        (int64_t)qrow * p.tb_stride_r
+                  : nullptr;
+    const bool warp_tbl = TBL && __any_sync(0xffffffffu, qrow >= 0);
+    const bool strict = TBL && p.strict != 0;
+    const float atol = (float)p.atol;
+    float prevp = 0.f;  // strict: the position of the next newer causal key
+    bool prevv = false;
+    int32_t sbits = 0;
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
     const uint32_t sc = tmem + lane_base + kColS + 128 * qt;  // this row's S columns
     const uint32_t oc = tmem + lane_base + kColO + 128 * qt;  // this row's O columns
@@ -832,7 +849,8 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
       const bool anyb = chunked && ok && (bndm[0] | bndm[1] | bndm[2] | bndm[3]) != 0u;
       // the row is saturated for this tile when its count is already >= npos-1
       // and no live chunk boundary of the tile restarts it below that value
-      bool sat = carry >= top;
+      // (a table row never is: its positions come from the table)
+      bool sat = carry >= top && qrow < 0;
       if (anyb && sat) {
 #pragma unroll 1
         for (int cc = 0; cc < 4 && sat; ++cc) {
@@ -1012,7 +1030,7 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
           // and every row either reaches it with a count >= npos - 1 or has
           // no causal key in it: one bias (tsat2) for every visible column,
           // and the gates change no position
-          if (__all_sync(0xffffffffu, bdc == 0u && (lim <= 0 || Rc >= top))) {
+          if (!warp_tbl && __all_sync(0xffffffffu, bdc == 0u && (lim <= 0 || Rc >= top))) {
 #pragma unroll
             for (int c = 0; c < 32; c += 2) {
               const float x0 =
@@ -1051,6 +1069,43 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
               }
               Rc = c < lim ? base + __uint_as_float(v[c]) : Rc;
               v[c] = __float_as_uint(Rc);
+            }
+          }
+          if constexpr (TBL) {
+            if (qrow >= 0) {
+              // table positions at keys with a table column, then (strict)
+              // the path checks of validate_contextual_path on the causal
+              // keys, newest first so each pair is (key, next newer key)
+              const int64_t j0 = key0 + cc * 32;
+#pragma unroll
+              for (int c = 31; c >= 0; --c) {
+                if (c >= lim) continue;
+                float pos = fminf(__uint_as_float(v[c]), top);
+                const int32_t ko = __ldg(p.k_ord + j0 + c);
+                if (ko >= 0) {
+                  float t = __ldg(tabrow + (int64_t)ko * p.tb_stride_c);
+                  if (!(t >= 0.f && t <= top)) {
+                    sbits |= CS_ST_POS_RANGE;
+                    t = t >= 0.f ? fminf(t, top) : 0.f;
+                  }
+                  pos = t;
+                }
+                if (strict) {
+                  const float rnd = 1.1920928955078125e-07f * fabsf(pos);
+                  if (pos < -(atol + rnd)) sbits |= CS_ST_PATH_NEG;
+                  const float avail = (float)(qp - (j0 + c)) + 1.f;
+                  if (pos > avail + atol + rnd) sbits |= CS_ST_PATH_AVAIL;
+                  if (prevv) {
+                    const float diff = pos - prevp;
+                    const float ptol = atol + rnd + 1.1920928955078125e-07f * fabsf(prevp);
+                    if (diff < -ptol) sbits |= CS_ST_PATH_INCR;
+                    if (diff > 1.f + ptol) sbits |= CS_ST_PATH_GAP;
+                  }
+                  prevp = pos;
+                  prevv = true;
+                }
+                v[c] = __float_as_uint(pos);
+              }
             }
           }
 #pragma unroll
@@ -1136,7 +1191,7 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
                                              ((ntile - 1) >> 1) & 1, abort));
       tc_fence_after();
     }
-    int32_t bits = 0;
+    int32_t bits = sbits;  // table-mode range / strict path bits
     const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
     char* orow = row_ok ? static_cast<char*>(p.out) + (i * p.o_stride_tok +
                                                        (int64_t)h * p.o_stride_head) *
@@ -1200,9 +1255,13 @@ bool prefill_supported(const cs_attn_params* p) {
   if (p->npos > kMaxNpos) return false;
   const int G = p->hq / p->hkv;
   if (G < 1 || G > 128 || 128 % G) return false;
-  if (p->pos_mode != CS_POS_CONTEXTUAL && p->pos_mode != CS_POS_CHUNK) return false;
-  if (p->gate_mask || p->vis_mask || p->out_positions || p->positions_only || p->strict)
+  if (p->pos_mode != CS_POS_CONTEXTUAL && p->pos_mode != CS_POS_CHUNK &&
+      p->pos_mode != CS_POS_TABLE)
     return false;
+  if (p->pos_mode == CS_POS_TABLE && (!p->table || !p->q_row || !p->k_ord)) return false;
+  // strict: checked for table rows; a contextual path is valid by construction
+  if (p->strict && p->pos_mode == CS_POS_CHUNK) return false;
+  if (p->gate_mask || p->vis_mask || p->out_positions || p->positions_only) return false;
   if (p->kpos != nullptr) return false;
   const int es = 2;
   auto al = [](int64_t x) { return (x % 16) == 0; };
@@ -1373,7 +1432,8 @@ int configure(K kern, bool& done) {
 
 bool same_prefill_shape(const cs_attn_params* a, const cs_attn_params* b) {
   return a->hq == b->hq && a->hkv == b->hkv && a->in_dtype == b->in_dtype &&
-         (a->npos > 64) == (b->npos > 64);
+         (a->npos > 64) == (b->npos > 64) &&
+         (a->pos_mode == CS_POS_TABLE) == (b->pos_mode == CS_POS_TABLE);
 }
 
 }  // namespace
@@ -1389,7 +1449,7 @@ extern "C" int cs_cope_attn_prefill(const cs_attn_params* p, void* stream) {
   Args a;
   make_args(p, a);
   const int blocks = a.pairs_per_head * p->hkv;
-  static bool configured[4] = {false, false, false, false};
+  static bool configured[8] = {false, false, false, false, false, false, false, false};
   auto launch = [&](auto kern, int which) -> int {
     const int c = configure(kern, configured[which]);
     if (c != CS_OK) return c;
@@ -1397,12 +1457,19 @@ extern "C" int cs_cope_attn_prefill(const cs_attn_params* p, void* stream) {
     CS_LAUNCH_CHECK();
     return CS_OK;
   };
-  if (p->npos > 64) {
-    if (p->in_dtype == CS_BF16) return launch(cope_prefill_sm100<__nv_bfloat16, 128>, 3);
-    return launch(cope_prefill_sm100<__half, 128>, 2);
+  const bool bf = p->in_dtype == CS_BF16, wide = p->npos > 64;
+  if (p->pos_mode == CS_POS_TABLE) {
+    if (wide)
+      return bf ? launch(cope_prefill_sm100<__nv_bfloat16, 128, true>, 7)
+                : launch(cope_prefill_sm100<__half, 128, true>, 6);
+    return bf ? launch(cope_prefill_sm100<__nv_bfloat16, 64, true>, 5)
+              : launch(cope_prefill_sm100<__half, 64, true>, 4);
   }
-  if (p->in_dtype == CS_BF16) return launch(cope_prefill_sm100<__nv_bfloat16, 64>, 1);
-  return launch(cope_prefill_sm100<__half, 64>, 0);
+  if (wide)
+    return bf ? launch(cope_prefill_sm100<__nv_bfloat16, 128, false>, 3)
+              : launch(cope_prefill_sm100<__half, 128, false>, 2);
+  return bf ? launch(cope_prefill_sm100<__nv_bfloat16, 64, false>, 1)
+            : launch(cope_prefill_sm100<__half, 64, false>, 0);
 }
 
 extern "C" int cs_cope_attn_prefill_batch(const cs_attn_params* params, int32_t count,
@@ -1414,7 +1481,7 @@ extern "C" int cs_cope_attn_prefill_batch(const cs_attn_params* params, int32_t 
     if (!prefill_supported(&params[k]) || !same_prefill_shape(&params[0], &params[k]))
       return CS_ERR_UNSUPPORTED;
   }
-  static bool configured[4] = {false, false, false, false};
+  static bool configured[8] = {false, false, false, false, false, false, false, false};
   for (int first = 0; first < count; first += kMaxPrefillBatch) {
     const int n = count - first < kMaxPrefillBatch ? count - first : kMaxPrefillBatch;
     BatchArgs b;  // the launch copies it into the kernel's parameter space
@@ -1439,10 +1506,18 @@ extern "C" int cs_cope_attn_prefill_batch(const cs_attn_params* params, int32_t 
     };
     const bool wide = params[first].npos > 64;
     const bool bf = params[first].in_dtype == CS_BF16;
-    const int rc = wide ? (bf ? launch(cope_prefill_sm100_batch<__nv_bfloat16, 128>, 3)
-                              : launch(cope_prefill_sm100_batch<__half, 128>, 2))
-                        : (bf ? launch(cope_prefill_sm100_batch<__nv_bfloat16, 64>, 1)
-                              : launch(cope_prefill_sm100_batch<__half, 64>, 0));
+    const bool tbl = params[first].pos_mode == CS_POS_TABLE;
+    int rc;
+    if (tbl)
+      rc = wide ? (bf ? launch(cope_prefill_sm100_batch<__nv_bfloat16, 128, true>, 7)
+                      : launch(cope_prefill_sm100_batch<__half, 128, true>, 6))
+                : (bf ? launch(cope_prefill_sm100_batch<__nv_bfloat16, 64, true>, 5)
+                      : launch(cope_prefill_sm100_batch<__half, 64, true>, 4));
+    else
+      rc = wide ? (bf ? launch(cope_prefill_sm100_batch<__nv_bfloat16, 128, false>, 3)
+                      : launch(cope_prefill_sm100_batch<__half, 128, false>, 2))
+                : (bf ? launch(cope_prefill_sm100_batch<__nv_bfloat16, 64, false>, 1)
+                      : launch(cope_prefill_sm100_batch<__half, 64, false>, 0));
     if (rc != CS_OK) return rc;
   }
   return CS_OK;

@@ -683,7 +683,7 @@ def cope_attention(
         elif isinstance(positions_transform, ChunkResetPositions):
             keep.extend(_bind_chunk_reset(p, positions_transform, qpos, kpos, hq, device))
         fast = (
-            p.pos_mode in (N.POS_CONTEXTUAL, N.POS_CHUNK)
+            p.pos_mode in (N.POS_CONTEXTUAL, N.POS_CHUNK, N.POS_TABLE)
             and attention_mask is None
             and visibility_mask is None
             and trace is None

@@ -811,3 +811,67 @@ def test_batched_prefill_equals_per_request_launches(cuda):
         N.check(lib.cs_cope_attn_prefill(ctypes.byref(p), N.stream_of(cuda)), "single")
         torch.cuda.synchronize(cuda)
         assert torch.equal(single.view(torch.int16), out_b.view(torch.int16))
+
+
+@pytest.mark.parametrize("case", ["mixed", "strict_valid", "strict_invalid"])
+@pytest.mark.parametrize("hq,hkv", [(32, 8), (8, 1)])
+def test_tensor_core_table_mode_matches_generic(cuda, case, hq, hkv):
+    """Canonical-table mode (CanonicalPositionPolicy, attention.py:32-57) on
+    the tensor-core prefill vs the CUDA-core kernel: same outputs and the same
+    status bits; strict mode on a table taken from the prompt's own contextual
+    positions (a valid path) and on a perturbed table (an invalid one)."""
+    import ctypes
+
+    from cacheslide_b200 import _native as N
+    from cacheslide_b200.position import _Holder, _base_params
+
+    nq, nk, d, npos = 200, 1500, 128, 64
+    g = torch.Generator().manual_seed(hq + len(case))
+    q = (torch.randn(nq, hq, d, generator=g) / d ** 0.5).to(torch.bfloat16)
+    k = (torch.randn(nk, hkv, d, generator=g) / d ** 0.5).to(torch.bfloat16)
+    v = torch.randn(nk, hkv, d, generator=g).to(torch.bfloat16)
+    rows = torch.sort(torch.randperm(nk, generator=g)[:nq]).values
+    E = torch.randn(d, npos, generator=g) * 0.02
+    fixed = torch.sort(torch.randperm(nk, generator=g)[: int(0.7 * nk)]).values
+    ordinal = torch.full((nk,), -1, dtype=torch.int32)
+    ordinal[fixed] = torch.arange(fixed.numel(), dtype=torch.int32)
+    q_row = torch.full((nq,), -1, dtype=torch.int32)
+    frows = torch.nonzero(ordinal[rows] >= 0).flatten()
+    q_row[frows] = torch.arange(frows.numel(), dtype=torch.int32)
+    if case == "mixed":
+        table = torch.rand(hq, frows.numel(), fixed.numel(), generator=g) * (npos - 1)
+    else:  # the prompt's own (clamped) contextual positions on fixed x fixed
+        logits = ocope.qk_logits(q.float().numpy(), k.float().numpy())
+        allowed = ocope.causal_mask(rows.numpy(), np.arange(nk))[None].repeat(hq, 0)
+        pos = ocope.contextual_positions(logits, allowed, npos)
+        table = torch.from_numpy(pos[:, frows.numpy()][:, :, fixed.numpy()].copy())
+        if case == "strict_invalid":
+            table[:, :, fixed.numel() // 2] += 9.0  # a jump of 9 in one fixed column
+            table.clamp_(0, npos - 1)
+    dev = lambda t: t.to(cuda)  # noqa: E731
+    q, k, v, rows = dev(q), dev(k), dev(v), dev(rows)
+    table, q_row_d, k_ord_d = dev(table.float().contiguous()), dev(q_row), dev(ordinal)
+    cope = _cope(E.numpy(), cuda)
+    holder = _Holder(cope, cope.position_embeddings.detach())
+    lib = N.load()
+    outs, bits = [], []
+    for fast in (True, False):
+        out = torch.empty(nq, hq, d, dtype=torch.bfloat16, device=cuda)
+        p = _base_params(q, k, v, holder, rows, None, nk, hkv, d)
+        p.out = out.data_ptr()
+        p.o_stride_tok, p.o_stride_head = out.stride(0), out.stride(1)
+        p.pos_mode = N.POS_TABLE
+        p.table = table.data_ptr()
+        p.tb_stride_h, p.tb_stride_r, p.tb_stride_c = table.stride()
+        p.q_row, p.k_ord = q_row_d.data_ptr(), k_ord_d.data_ptr()
+        p.strict = 0 if case == "mixed" else 1
+        st = N.Status(cuda)
+        p.status = st.ptr
+        fn = lib.cs_cope_attn_prefill if fast else lib.cs_cope_attn
+        N.check(fn(ctypes.byref(p), N.stream_of(cuda)), "prefill" if fast else "generic")
+        bits.append(st.read())
+        outs.append(out.float().cpu().numpy())
+    assert bits[0] == bits[1]
+    path_bits = N.ST_PATH_NEG | N.ST_PATH_AVAIL | N.ST_PATH_INCR | N.ST_PATH_GAP
+    assert bool(bits[0] & path_bits) == (case == "strict_invalid")
+    np.testing.assert_allclose(outs[0], outs[1], **BF16)
