@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--batched-attention", action="store_true",
                     help="with --per-request-streams: one attention launch for all requests "
                          "after their WCA / SLIDE chains")
+    ap.add_argument("--no-c3", action="store_true",
+                    help="skip the RAG slice with shared chunks (run at one GPU by default)")
     ap.add_argument("--no-c4", action="store_true",
                     help="skip the multi-session chat slice (run at one GPU by default)")
     ap.add_argument("--c5", action="store_true",
@@ -379,18 +381,12 @@ def c5_slice(args, dev, rank: int, world: int) -> dict:
     return out
 
 
-# ------------------------------------------------------------ C4 slice
-def c4_slice(args, dev) -> dict:
-    """The multi-session chat slice (C4): 32 sessions at turn 8 of
-    conversations adding 256-1024 tokens a turn plus 128 decoded tokens;
-    a turn = WCA + SLIDE relocation of the selected history rows + blend +
-    attention of the active rows, then 128 batched decode steps."""
+# ------------------------------------------------------------ C3 / C4 slices
+def _turns(step, args, dev, decode_tokens: int) -> tuple[float, float, int]:
+    """Mean device ms of the prefill and of the decode of a turn step (after
+    two warm-up turns, L2 flushed before each), and the turns timed."""
     import torch
 
-    from cacheslide_b200.chat import ChatConfig, ChatTurnStep
-
-    cfg = ChatConfig()
-    step = ChatTurnStep(cfg, dev)
     stream = torch.cuda.current_stream(dev)
     s = stream.cuda_stream
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
@@ -411,6 +407,50 @@ def c4_slice(args, dev) -> dict:
     step.check_status()
     pre = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
     dec = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+    return pre, dec, turns
+
+
+def c3_slice(args, dev) -> dict:
+    """The RAG slice (C3 shapes: Mistral-7B heads, 64 requests x 10 chunks of
+    512 drawn Zipf(1.1) from a pool of 40 shared chunks + a 64-token
+    question, WCA 15 %, 32 decode tokens)."""
+    import torch
+
+    from cacheslide_b200.rag import RagConfig, RagStep
+
+    cfg = RagConfig()
+    step = RagStep(cfg, dev)
+    pre, dec, turns = _turns(step, args, dev, cfg.decode_tokens)
+    out = {
+        "workload": "c3-rag: 64 requests x 10 chunks of 512 (Zipf 1.1 over a pool of 40 "
+                    "chunks resident once) + 64-token question, Hq=32, Hkv=8, D=128, npos=64, "
+                    "WCA 15%, copy-on-write relocation of the selected chunk rows, 32 decoded",
+        "prompt_tokens": step.prompt_tokens(),
+        "shared_chunk_reads": step.shared_fraction(),
+        "relocated_rows": sum(x.reloc_src.numel() for x in step.sessions),
+        "prefill_ms": pre,
+        "prefill_tok_s": step.prompt_tokens() / (pre / 1e3),
+        "decode_ms_per_token": dec / cfg.decode_tokens,
+        "decode_tok_s": cfg.requests * cfg.decode_tokens / (dec / 1e3),
+        "batches_timed": turns,
+    }
+    del step
+    torch.cuda.empty_cache()
+    return out
+
+
+def c4_slice(args, dev) -> dict:
+    """The multi-session chat slice (C4): 32 sessions at turn 8 of
+    conversations adding 256-1024 tokens a turn plus 128 decoded tokens;
+    a turn = WCA + SLIDE relocation of the selected history rows + blend +
+    attention of the active rows, then 128 batched decode steps."""
+    import torch
+
+    from cacheslide_b200.chat import ChatConfig, ChatTurnStep
+
+    cfg = ChatConfig()
+    step = ChatTurnStep(cfg, dev)
+    pre, dec, turns = _turns(step, args, dev, cfg.decode_tokens)
     reloc_rows = sum(x.reloc_src.numel() for x in step.sessions)
     out = {
         "workload": "c4-multi-session-chat: 32 sessions at turn 8 (+256-1024 tokens a turn, "
@@ -624,6 +664,7 @@ def main():
 
     c5 = c5_slice(args, dev, rank, world) if (world > 1 or args.c5) else None
     c4 = c4_slice(args, dev) if (world == 1 and not args.no_c4) else None
+    c3 = c3_slice(args, dev) if (world == 1 and not args.no_c3) else None
 
     if rank == 0:
         pk, pk_kind = peaks()
@@ -680,6 +721,8 @@ def main():
             line["c5_tp"] = c5
         if c4 is not None:
             line["c4_chat"] = c4
+        if c3 is not None:
+            line["c3_rag"] = c3
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

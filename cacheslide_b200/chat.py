@@ -58,53 +58,34 @@ class _Session:
     """Device tensors of one session."""
 
 
-class ChatTurnStep:
-    """One chat turn for every session (see the module)."""
+class _TurnStep:
+    """The launches of a reuse turn over sessions whose reused rows are
+    resident in paged slots (``slots_all[:n]``, possibly shared between
+    sessions with identical records) and whose dynamic rows and decoded
+    tokens have slots of their own: WCA, copy-on-write relocation of the
+    selected reused rows into the session's ``private_blocks``, blend,
+    attention, decode (see the module)."""
 
-    def __init__(self, cfg: ChatConfig, device: torch.device):
+    def __init__(self, cfg, device: torch.device, cache: torch.Tensor, sessions: list,
+                 g: torch.Generator):
         self.cfg, self.device = cfg, device
         self.lib = N.load()
         hq, hkv, d, bs = cfg.q_heads, cfg.kv_heads, cfg.head_dim, cfg.block
         dt = cfg.dtype
-        lay = torch.Generator().manual_seed(cfg.seed)
-        g = torch.Generator(device=device).manual_seed(cfg.seed + 1)
 
         def randn(*shape, scale=1.0):
             return (torch.randn(*shape, generator=g, device=device) * scale).to(dt)
 
-        # session layouts: turn lengths, history, blocks (canonical + private)
-        specs = []
-        total_blocks = 0
-        for _ in range(cfg.sessions):
-            lens = torch.randint(cfg.min_tokens, cfg.max_tokens + 1, (cfg.turn,),
-                                 generator=lay).tolist()
-            turns = [x + cfg.decode_tokens for x in lens[:-1]] + [lens[-1]]
-            n = sum(turns)
-            hist = n - turns[-1]
-            canon_blocks = (n + cfg.decode_tokens + bs - 1) // bs
-            priv_blocks = (math.ceil(cfg.fraction * hist) + bs) // bs + 1
-            specs.append((turns, n, hist, canon_blocks, priv_blocks))
-            total_blocks += canon_blocks + priv_blocks
-        pool = torch.randperm(total_blocks, generator=lay).to(device)
-        self.cache = torch.zeros(total_blocks, hkv, bs, 2 * d, dtype=dt, device=device)
+        self.cache = cache
         self.kv = N.paged_view(self.cache)
         self.E = (torch.randn(d, cfg.npos, generator=g, device=device) * 0.02).contiguous()
-        self.status = torch.zeros(cfg.sessions, dtype=torch.int32, device=device)
-        self.sessions = []
-        cursor = 0
-        for b, (turns, n, hist, cb, pb) in enumerate(specs):
-            s = _Session()
-            s.n, s.hist, s.new = n, hist, turns[-1]
-            blocks = pool[cursor:cursor + cb]
-            s.private_blocks = pool[cursor + cb:cursor + cb + pb]
-            cursor += cb + pb
-            tok = torch.arange(n + cfg.decode_tokens, device=device)
-            s.slots_all = (blocks[tok // bs] * bs + tok % bs).contiguous()
+        self.status = torch.zeros(len(sessions), dtype=torch.int32, device=device)
+        self.sessions = sessions
+        for b, s in enumerate(sessions):
+            n = s.n
+            s.hist = int(s.reused.sum())
             s.canon = s.slots_all[:n].contiguous()
-            s.reused = (tok[:n] < hist).contiguous()
             s.mandatory = ~s.reused
-            s.cached_k = randn(n, hkv, d, scale=1 / math.sqrt(d))
-            s.cached_v = randn(n, hkv, d)
             s.calib_k = (s.cached_k.float() + 0.05 * torch.randn(
                 n, hkv, d, generator=g, device=device)).to(dt)
             s.calib_k[s.mandatory] = s.cached_k[s.mandatory]
@@ -125,7 +106,6 @@ class ChatTurnStep:
             s.counts2 = torch.zeros(2, dtype=torch.int64, device=device)
             s.promoted = torch.empty(n, dtype=torch.int64, device=device)
             s.removed_list = torch.empty(n, dtype=torch.int64, device=device)
-            self.sessions.append(s)
         # the resident history: every prompt record in its canonical slot
         for s in self.sessions:
             N.check(self.lib.cs_slide_scatter(
@@ -171,14 +151,14 @@ class ChatTurnStep:
             s.params = self._attn_params(s)
             s.dec_out = torch.empty(cfg.decode_tokens, hq, d, dtype=dt, device=device)
         self._update_items()
-        self.attn_params = (N.AttnParams * cfg.sessions)(*[s.params for s in self.sessions])
+        self.attn_params = (N.AttnParams * len(self.sessions))(*[s.params for s in self.sessions])
         # decode: one params array per step (the context grows by one key)
         self.dec_params = []
         for t in range(cfg.decode_tokens):
-            arr = (N.AttnParams * cfg.sessions)(*[self._decode_params(s, t)
+            arr = (N.AttnParams * len(self.sessions))(*[self._decode_params(s, t)
                                                   for s in self.sessions])
             self.dec_params.append(arr)
-        size = max(self.lib.cs_cope_attn_decode_batch_workspace(p, cfg.sessions)
+        size = max(self.lib.cs_cope_attn_decode_batch_workspace(p, len(self.sessions))
                    for p in (self.dec_params[0], self.dec_params[-1]))
         self.dec_ws = torch.empty(max(size, 1), dtype=torch.uint8, device=device)
         self.dec_rows = torch.stack([s.slots_all[s.n:] for s in self.sessions], 1).contiguous()
@@ -190,7 +170,7 @@ class ChatTurnStep:
     def _items(self) -> None:
         c = self.cfg
         p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
-        self.init_items = (N.InitializeItem * c.sessions)(*[N.InitializeItem(
+        self.init_items = (N.InitializeItem * len(self.sessions))(*[N.InitializeItem(
             p(s.cached_k), s.cached_k.stride(0), s.cached_k.stride(1), p(s.calib_k),
             s.calib_k.stride(0), s.calib_k.stride(1), s.n, p(s.reused), p(s.dev), p(s.alpha),
             p(s.candidate), p(s.selected), p(s.removed), p(s.counts), s.status_ptr)
@@ -198,19 +178,19 @@ class ChatTurnStep:
 
     def _select_items(self) -> None:
         p = lambda t: t.data_ptr()  # noqa: E731
-        self.select_items = (N.CommitItem * self.cfg.sessions)(*[N.CommitItem(
+        self.select_items = (N.CommitItem * len(self.sessions))(*[N.CommitItem(
             None, 0, None, None, s.n, s.budget, p(s.dev), p(s.alpha), p(s.candidate),
             p(s.selected), p(s.removed), None, p(s.promoted), p(s.counts2), s.status_ptr)
             for s in self.sessions])
 
     def _update_items(self) -> None:
         p = lambda t: t.data_ptr()  # noqa: E731
-        self.update_items = (N.UpdateItem * self.cfg.sessions)(*[N.UpdateItem(
+        self.update_items = (N.UpdateItem * len(self.sessions))(*[N.UpdateItem(
             p(s.cached_k), p(s.cached_v), s.cached_k.stride(0), s.cached_k.stride(1), p(s.fk),
             p(s.fv), s.fk.stride(0), s.fk.stride(1), p(s.active), s.a, p(s.alpha),
             p(s.mandatory), None, None, p(s.next_alpha), p(s.used_alpha), p(s.cos),
             p(s.active_slots), s.status_ptr) for s in self.sessions])
-        self.commit_items = (N.CommitItem * self.cfg.sessions)(*[N.CommitItem(
+        self.commit_items = (N.CommitItem * len(self.sessions))(*[N.CommitItem(
             p(s.active), s.a, p(s.next_alpha), p(s.cos), s.n, s.budget, p(s.dev), p(s.alpha),
             p(s.candidate), p(s.selected), p(s.removed), p(s.removed_list), p(s.promoted),
             p(s.counts2), s.status_ptr) for s in self.sessions])
@@ -265,11 +245,11 @@ class ChatTurnStep:
     def initialize_all(self, stream) -> None:
         c = self.cfg
         N.check(self.lib.cs_wca_initialize_batch(
-            self.init_items, c.sessions, c.kv_heads, c.head_dim, N.DTYPES[c.dtype], 1e-8, 0,
+            self.init_items, len(self.sessions), c.kv_heads, c.head_dim, N.DTYPES[c.dtype], 1e-8, 0,
             stream), "cs_wca_initialize_batch")
 
     def select_all(self, stream) -> None:
-        N.check(self.lib.cs_wca_commit_batch(self.select_items, self.cfg.sessions, 0.12, 0,
+        N.check(self.lib.cs_wca_commit_batch(self.select_items, len(self.sessions), 0.12, 0,
                                              stream), "cs_wca_commit_batch")
 
     def relocate_all(self, stream) -> None:
@@ -282,13 +262,13 @@ class ChatTurnStep:
     def update_all(self, stream) -> None:
         c = self.cfg
         N.check(self.lib.cs_wca_update_batch(
-            self.update_items, c.sessions, c.kv_heads, c.head_dim, N.DTYPES[c.dtype], 0, 1e-8,
+            self.update_items, len(self.sessions), c.kv_heads, c.head_dim, N.DTYPES[c.dtype], 0, 1e-8,
             0, ctypes.byref(self.kv), stream), "cs_wca_update_batch")
-        N.check(self.lib.cs_wca_commit_batch(self.commit_items, c.sessions, 0.12, 0, stream),
+        N.check(self.lib.cs_wca_commit_batch(self.commit_items, len(self.sessions), 0.12, 0, stream),
                 "cs_wca_commit_batch")
 
     def attention_all(self, stream) -> None:
-        N.check(self.lib.cs_cope_attn_prefill_batch(self.attn_params, self.cfg.sessions,
+        N.check(self.lib.cs_cope_attn_prefill_batch(self.attn_params, len(self.sessions),
                                                     stream), "cs_cope_attn_prefill_batch")
 
     def prefill(self, stream) -> None:
@@ -305,11 +285,11 @@ class ChatTurnStep:
         rows = self.dec_rows
         for t in range(c.decode_tokens if steps is None else steps):
             N.check(self.lib.cs_slide_scatter(
-                ctypes.byref(self.kv), rows[t].data_ptr(), None, c.sessions,
+                ctypes.byref(self.kv), rows[t].data_ptr(), None, len(self.sessions),
                 self.dec_k[t].data_ptr(), self.dec_v[t].data_ptr(), self.dec_k.stride(1),
                 self.dec_k.stride(2), self.sessions[0].status_ptr, stream), "cs_slide_scatter")
             N.check(self.lib.cs_cope_attn_decode_batch(
-                self.dec_params[t], c.sessions, self.dec_ws.data_ptr(), stream),
+                self.dec_params[t], len(self.sessions), self.dec_ws.data_ptr(), stream),
                 "cs_cope_attn_decode_batch")
 
     def check_status(self) -> None:
@@ -324,3 +304,47 @@ class ChatTurnStep:
 
     def new_tokens(self) -> int:
         return sum(s.new for s in self.sessions)
+
+
+class ChatTurnStep(_TurnStep):
+    """One chat turn for every session (see the module)."""
+
+    def __init__(self, cfg: ChatConfig, device: torch.device):
+        hq, hkv, d, bs = cfg.q_heads, cfg.kv_heads, cfg.head_dim, cfg.block
+        dt = cfg.dtype
+        lay = torch.Generator().manual_seed(cfg.seed)
+        g = torch.Generator(device=device).manual_seed(cfg.seed + 1)
+
+        def randn(*shape, scale=1.0):
+            return (torch.randn(*shape, generator=g, device=device) * scale).to(dt)
+
+        # session layouts: turn lengths, history, blocks (canonical + private)
+        specs = []
+        total_blocks = 0
+        for _ in range(cfg.sessions):
+            lens = torch.randint(cfg.min_tokens, cfg.max_tokens + 1, (cfg.turn,),
+                                 generator=lay).tolist()
+            turns = [x + cfg.decode_tokens for x in lens[:-1]] + [lens[-1]]
+            n = sum(turns)
+            hist = n - turns[-1]
+            canon_blocks = (n + cfg.decode_tokens + bs - 1) // bs
+            priv_blocks = (math.ceil(cfg.fraction * hist) + bs) // bs + 1
+            specs.append((turns, n, hist, canon_blocks, priv_blocks))
+            total_blocks += canon_blocks + priv_blocks
+        pool = torch.randperm(total_blocks, generator=lay).to(device)
+        cache = torch.zeros(total_blocks, hkv, bs, 2 * d, dtype=dt, device=device)
+        sessions = []
+        cursor = 0
+        for turns, n, hist, cb, pb in specs:
+            s = _Session()
+            s.n, s.new = n, turns[-1]
+            blocks = pool[cursor:cursor + cb]
+            s.private_blocks = pool[cursor + cb:cursor + cb + pb]
+            cursor += cb + pb
+            tok = torch.arange(n + cfg.decode_tokens, device=device)
+            s.slots_all = (blocks[tok // bs] * bs + tok % bs).contiguous()
+            s.reused = (tok[:n] < hist).contiguous()
+            s.cached_k = randn(n, hkv, d, scale=1 / math.sqrt(d))
+            s.cached_v = randn(n, hkv, d)
+            sessions.append(s)
+        super().__init__(cfg, device, cache, sessions, g)
