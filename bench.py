@@ -381,6 +381,55 @@ def c5_slice(args, dev, rank: int, world: int) -> dict:
     return out
 
 
+# ------------------------------------------------------ selective QKV layer
+def qkv_layer(args, work, dev) -> dict:
+    """The selective layer loop's QKV projection for the step's active rows
+    (the 8 requests' ~1051 rows each, Mistral-7B projection 4096 -> 6144 with
+    a rank-16 LoRA delta): rows gathered from the previous layer's output (a
+    third of them) or the layer snapshot, one tensor-core launch; TFLOP/s
+    against the measured bf16 peak."""
+    import torch
+
+    from cacheslide_b200.layer import SelectiveQKV
+
+    g = torch.Generator(device=dev).manual_seed(11)
+    hidden, n_out, rank = 4096, 6144, 16
+    rows = sum(r.a for r in work.requests)
+    n = rows * 3  # a prompt frame of which the active rows are a third
+    active = torch.sort(torch.randperm(n, generator=g, device=dev)[:rows]).values
+    previous = active[torch.randperm(rows, generator=g, device=dev)[: rows // 3]].sort().values
+    fixed = torch.arange(n, device=dev)
+    bf = torch.bfloat16
+    prev_h = torch.randn(previous.numel(), hidden, generator=g, device=dev).to(bf)
+    snap_h = torch.randn(n, hidden, generator=g, device=dev).to(bf)
+    w = (torch.randn(n_out, hidden, generator=g, device=dev) / 64).to(bf)
+    la = (torch.randn(rank, hidden, generator=g, device=dev) / 64).to(bf)
+    lb = (torch.randn(n_out, rank, generator=g, device=dev) / 4).to(bf)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    layer = SelectiveQKV(prev_h, previous, snap_h, fixed, active, n, w, la, lb)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(3):
+        layer.run(stream.cuda_stream)
+    layer.check()
+    steps = max(1, min(args.steps, 10))
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    for i in range(steps):
+        flush.fill_(i & 0xFF)
+        ev[i][0].record(stream)
+        layer.run(stream.cuda_stream)
+        ev[i][1].record(stream)
+    torch.cuda.synchronize(dev)
+    layer.check()
+    ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    flops = 2.0 * rows * hidden * (n_out + rank) + 2.0 * rows * rank * n_out
+    pk, kind = peaks()
+    tf = flops / (ms / 1e3) / 1e12
+    return {"rows": rows, "shape": f"{hidden} -> {n_out}, LoRA rank {rank}", "ms": ms,
+            "tflops": tf, "frac": tf / float(pk.get("bf16_tflops", 1590.0)),
+            "peak_kind": kind, "launches_timed": steps}
+
+
 # ------------------------------------------------------------ C3 / C4 slices
 def _turns(step, args, dev, decode_tokens: int) -> tuple[float, float, int]:
     """Mean device ms of the prefill and of the decode of a turn step (after
@@ -662,6 +711,7 @@ def main():
     e2e_value = tokens * args.steps / (e2e_ms / 1e3)
     decode_value = args.requests * world / (dec_ms / 1e3)
 
+    qkv = qkv_layer(args, work, dev) if rank == 0 else None
     c5 = c5_slice(args, dev, rank, world) if (world > 1 or args.c5) else None
     c4 = c4_slice(args, dev) if (world == 1 and not args.no_c4) else None
     c3 = c3_slice(args, dev) if (world == 1 and not args.no_c3) else None
@@ -717,6 +767,8 @@ def main():
             "hot_bytes": hot_bytes(work),
             "hbm_kernels": hbm_report(work, hbm_ms, dec_ms, float(pk.get("hbm_gbs", 6650.0))),
         }
+        if qkv is not None:
+            line["selective_qkv"] = qkv
         if c5 is not None:
             line["c5_tp"] = c5
         if c4 is not None:

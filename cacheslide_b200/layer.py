@@ -40,6 +40,61 @@ def row_sources(previous: Tensor, active: Tensor, fixed: Tensor, n: int) -> tupl
     return src.contiguous(), idx.contiguous()
 
 
+class SelectiveQKV:
+    """One layer's prepared launch of ``cs_qkv_gather_lora`` (the arguments of
+    ``selective_qkv``, checked and resolved once); ``run(stream)`` enqueues it
+    without host synchronisation, ``check()`` reads its status."""
+
+    def __init__(self, previous_hidden: Tensor, previous: Tensor, snapshot_hidden: Tensor,
+                 fixed: Tensor, active: Tensor, n: int, weight: Tensor,
+                 lora_a: Tensor | None = None, lora_b: Tensor | None = None):
+        device = N.require_cuda(weight)
+        dt = weight.dtype
+        for t in (previous_hidden, snapshot_hidden):
+            if t.dtype != dt or t.ndim != 2 or t.shape[1] != weight.shape[1] or \
+                    t.stride(1) != 1:
+                raise ValueError("hidden rows must be [rows, hidden] with the weight's dtype")
+        rank = 0
+        if lora_a is not None or lora_b is not None:
+            if lora_a is None or lora_b is None:
+                raise ValueError("LoRA needs both factors")
+            rank = lora_a.shape[0]
+            if lora_a.shape[1] != weight.shape[1] or lora_b.shape != (weight.shape[0], rank):
+                raise ValueError("LoRA factors must be [rank, hidden] and [n_out, rank]")
+            lora_a, lora_b = lora_a.contiguous(), lora_b.contiguous()
+        weight = weight.contiguous()
+        src, idx = row_sources(previous, active, fixed, n)
+        a = active.numel()
+        self.device = device
+        self.out = torch.empty(a, weight.shape[0], dtype=dt, device=device)
+        self.status = N.Status(device)
+        self._keep = (previous_hidden, snapshot_hidden, weight, lora_a, lora_b, src, idx)
+        p = N.QKVParams()
+        p.src0, p.src0_stride, p.src0_rows = (previous_hidden.data_ptr(),
+                                              previous_hidden.stride(0), previous_hidden.shape[0])
+        p.src1, p.src1_stride, p.src1_rows = (snapshot_hidden.data_ptr(),
+                                              snapshot_hidden.stride(0), snapshot_hidden.shape[0])
+        p.row_src, p.row_idx, p.a = src.data_ptr(), idx.data_ptr(), a
+        p.hidden, p.n_out = weight.shape[1], weight.shape[0]
+        p.w = weight.data_ptr()
+        p.lora_a = N.ptr(lora_a)
+        p.lora_b = N.ptr(lora_b)
+        p.rank = rank
+        p.out, p.out_stride = self.out.data_ptr(), self.out.stride(0)
+        p.dtype = N.DTYPES[dt]
+        p.status = self.status.ptr
+        self.params = p
+
+    def run(self, stream: int | None = None) -> Tensor:
+        s = N.stream_of(self.device) if stream is None else stream
+        N.check(N.load().cs_qkv_gather_lora(ctypes.byref(self.params), s), "cs_qkv_gather_lora")
+        return self.out
+
+    def check(self) -> None:
+        if self.status.read():
+            raise ValueError("selective QKV: a row index outside its source, or a timeout")
+
+
 def selective_qkv(previous_hidden: Tensor, previous: Tensor, snapshot_hidden: Tensor,
                   fixed: Tensor, active: Tensor, n: int, weight: Tensor,
                   lora_a: Tensor | None = None, lora_b: Tensor | None = None) -> Tensor:
@@ -49,40 +104,8 @@ def selective_qkv(previous_hidden: Tensor, previous: Tensor, snapshot_hidden: Te
     ``fixed`` tokens; ``weight`` is ``[n_out, hidden]``, ``lora_a``
     ``[rank, hidden]``, ``lora_b`` ``[n_out, rank]``.  Returns ``[active,
     n_out]`` in the input dtype (bf16 or fp16)."""
-    device = N.require_cuda(weight)
-    dt = weight.dtype
-    for t in (previous_hidden, snapshot_hidden):
-        if t.dtype != dt or t.ndim != 2 or t.shape[1] != weight.shape[1] or t.stride(1) != 1:
-            raise ValueError("hidden rows must be [rows, hidden] with the weight's dtype")
-    rank = 0
-    if lora_a is not None or lora_b is not None:
-        if lora_a is None or lora_b is None:
-            raise ValueError("LoRA needs both factors")
-        rank = lora_a.shape[0]
-        if lora_a.shape[1] != weight.shape[1] or lora_b.shape != (weight.shape[0], rank):
-            raise ValueError("LoRA factors must be [rank, hidden] and [n_out, rank]")
-        lora_a, lora_b = lora_a.contiguous(), lora_b.contiguous()
-    weight = weight.contiguous()
-    src, idx = row_sources(previous, active, fixed, n)
-    a = active.numel()
-    out = torch.empty(a, weight.shape[0], dtype=dt, device=device)
-    status = N.Status(device)
-    p = N.QKVParams()
-    p.src0, p.src0_stride, p.src0_rows = (previous_hidden.data_ptr(), previous_hidden.stride(0),
-                                          previous_hidden.shape[0])
-    p.src1, p.src1_stride, p.src1_rows = (snapshot_hidden.data_ptr(), snapshot_hidden.stride(0),
-                                          snapshot_hidden.shape[0])
-    p.row_src, p.row_idx, p.a = src.data_ptr(), idx.data_ptr(), a
-    p.hidden, p.n_out = weight.shape[1], weight.shape[0]
-    p.w = weight.data_ptr()
-    p.lora_a = N.ptr(lora_a)
-    p.lora_b = N.ptr(lora_b)
-    p.rank = rank
-    p.out, p.out_stride = out.data_ptr(), out.stride(0)
-    p.dtype = N.DTYPES[dt]
-    p.status = status.ptr
-    N.check(N.load().cs_qkv_gather_lora(ctypes.byref(p), N.stream_of(device)),
-            "cs_qkv_gather_lora")
-    if status.read():
-        raise ValueError("selective QKV: a row index outside its source, or a timeout")
+    step = SelectiveQKV(previous_hidden, previous, snapshot_hidden, fixed, active, n, weight,
+                        lora_a, lora_b)
+    out = step.run()
+    step.check()
     return out
