@@ -108,20 +108,6 @@ __device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* map
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(bar)
       : "memory");
 }
-// 2-D tile load: rows y..y+15, 64 elements from column x, into 16 consecutive
-// 128-byte rows at dst
-__device__ __forceinline__ void tma_tile2d(uint32_t dst, const CUtensorMap* map, int x, int y,
-                                           uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
-      : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes)
-               : "memory");
-}
 // barrier that also ANDs a flag over its participants: every participant
 // leaves with the same answer, so exits from loops stay collective and no
 // partner is left waiting at a later barrier

@@ -4,6 +4,8 @@
 // 128-byte swizzled K-major tile layout, and the hardware 2^x and reciprocal.
 #pragma once
 
+#include <cuda.h>
+
 #include <cstdint>
 
 namespace cs {
@@ -231,4 +233,19 @@ __device__ __forceinline__ void mbar_init_fence() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
+// ---------------------------------------------------------------------- TMA
+// 2-D tile load: the tensor map's box (rows from y, elements from column x)
+// into consecutive rows at dst, completing on the mbarrier at bar
+__device__ __forceinline__ void tma_tile2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                           uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
 }  // namespace cs
