@@ -91,8 +91,24 @@ constexpr uint32_t kFixMask = 176;  // [4 slots][4 words] key is fixed
 constexpr uint32_t kBndMask = 240;  // [4 slots][4 words] key is the last of its chunk
 constexpr uint32_t kBndKc = 304;    // [4 slots][4 chunks] int: chunk id of the newest boundary
 constexpr uint32_t kRedN = 368;     // [8] int64: per-warp key needs of the CTA's rows
-constexpr uint32_t kMetaBytes = kRedN + 64;
-constexpr uint32_t kSmemBytes = kMeta + kMetaBytes;  // 229,808 B (limit 232,448)
+// Key tiles a CTA can skip.  When every row of the CTA is a selected row of
+// the association policy (it sees only non-fixed keys and itself), a key tile
+// is needed only if it holds a key some row sees, or a gate that feeds the
+// count of such a key; the others are neither loaded nor computed.
+constexpr uint32_t kAllSel = 432;   // [8] int: per warp, every valid query row is selected
+constexpr int kMaxMapTiles = 512;   // tile map bound (64K keys); more keys: no skipping
+constexpr int kMapWords = kMaxMapTiles / 32;
+constexpr uint32_t kNeed = 464;     // [16] words: key tile t is needed (bit t)
+constexpr uint32_t kNfTile = 528;   // [16] words: key tile t holds a non-fixed key
+constexpr uint32_t kChunkFl = 592;  // [0] chunk ids unusable (out of range / decreasing),
+                                    // [1..2] 64-bit mask: chunk holds a non-fixed key
+constexpr int kMaxMapChunks = 64;
+constexpr uint32_t kChunkS = 608;   // [64] int: first key of chunk c
+constexpr uint32_t kChunkE = 864;   // [64] int: last key of chunk c
+constexpr uint32_t kSlotTile = 1120; // [4 slots] int: key tile of the slot's step
+constexpr uint32_t kChunkF = 1136;  // [64] int: first non-fixed key of chunk c
+constexpr uint32_t kMetaBytes = kChunkF + 4 * kMaxMapChunks;
+constexpr uint32_t kSmemBytes = kMeta + kMetaBytes;  // 230,768 B (limit 232,448)
 
 // TMEM columns: S of each tile (P packed over its first 64 columns), O of
 // each tile; T = Q E lands in the first NP S columns of its tile at start
@@ -368,16 +384,32 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
   }
   if (warp < 8) {  // keys needed by the furthest row of the two tiles: one row per thread
     int64_t n = 0;
+    bool sel = true;
     if (tid < 2 * R && i0 + tid < p.nq) {
       const int64_t qp = p.qpos[i0 + tid];
       n = qp + 1 < p.nk ? qp + 1 : p.nk;
+      sel = p.q_selected != nullptr && p.q_selected[i0 + tid] != 0;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const int64_t m = __shfl_xor_sync(0xffffffffu, n, o);
       n = m > n ? m : n;
     }
-    if (lane == 0) reinterpret_cast<int64_t*>(meta + kRedN)[warp] = n;
+    sel = __all_sync(0xffffffffu, sel);
+    if (lane == 0) {
+      reinterpret_cast<int64_t*>(meta + kRedN)[warp] = n;
+      reinterpret_cast<int*>(meta + kAllSel)[warp] = sel ? 1 : 0;
+    }
+  } else if (warp == 12) {  // empty tile and chunk maps (filled after the first barrier)
+    uint32_t* w = reinterpret_cast<uint32_t*>(meta + kNeed);
+    w[lane] = 0u;  // kNeed and kNfTile: 32 consecutive words
+    if (lane < 4) reinterpret_cast<uint32_t*>(meta + kChunkFl)[lane] = 0u;
+    int* cs = reinterpret_cast<int*>(meta + kChunkS);
+    int* ce = reinterpret_cast<int*>(meta + kChunkE);
+    int* cf = reinterpret_cast<int*>(meta + kChunkF);
+    cs[lane] = cs[32 + lane] = 0x7fffffff;
+    cf[lane] = cf[32 + lane] = 0x7fffffff;
+    ce[lane] = ce[32 + lane] = -1;
   }
   // the Q tiles and the E table need nothing from the set-up above: their
   // copies start before the first barrier (the arrivals on kBarQ come after
@@ -429,6 +461,107 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
     nneed = n > nneed ? n : nneed;
   }
   const int ntile = (int)((nneed + kTileN - 1) / kTileN);
+  // ---------------------------------------------------------- key tile map
+  // Only when every query row of the CTA is a selected row (association
+  // policy, attention.py:61-72): such a row sees the non-fixed keys and its
+  // own key.  The count of a seen key j (position.py:295-307) sums the gates
+  // of keys j .. qp; in the chunk-reset mode it restarts at the end of the
+  // first chunk at or after j's that carries an offset for the row.  A key
+  // tile is needed when it holds a seen key or such a gate; the others are
+  // hidden from every row and change no count a row uses.  (Strict path
+  // validation checks every causal key, so it keeps every tile.)
+  bool use_map = false;
+  {
+    bool allsel = p.q_selected != nullptr && p.k_fixed != nullptr && !(TBL && p.strict != 0);
+    for (int w = 0; w < 8; ++w) allsel = allsel && reinterpret_cast<const volatile int*>(meta + kAllSel)[w] != 0;
+    use_map = allsel && ntile > 0 && ntile <= kMaxMapTiles;
+  }
+  if (use_map) {
+    uint32_t* need = reinterpret_cast<uint32_t*>(meta + kNeed);
+    uint32_t* nft = reinterpret_cast<uint32_t*>(meta + kNfTile);
+    uint32_t* cfl = reinterpret_cast<uint32_t*>(meta + kChunkFl);
+    int* cs = reinterpret_cast<int*>(meta + kChunkS);
+    int* ce = reinterpret_cast<int*>(meta + kChunkE);
+    int* cf = reinterpret_cast<int*>(meta + kChunkF);
+    const bool chunked = p.pos_mode == CS_POS_CHUNK;
+    // keys 0 .. nneed-1: tiles and chunks holding a non-fixed key, chunk ranges
+#pragma unroll 1
+    for (int64_t j = tid; j < nneed; j += kThreads) {
+      const bool nf = p.k_fixed[j] == 0;
+      if (nf) atomicOr(&nft[(int)(j >> 12)], 1u << (int)((j >> 7) & 31));
+      if (chunked) {
+        const int kc = p.key_chunk[j];
+        if (kc < 0 || kc >= kMaxMapChunks) {
+          cfl[0] = 1u;
+          continue;
+        }
+        const int kp = j > 0 ? p.key_chunk[j - 1] : -1;
+        const int kn = j + 1 < nneed ? p.key_chunk[j + 1] : -1;
+        if (kp > kc) cfl[0] = 1u;
+        if (kp != kc) cs[kc] = (int)j;
+        if (kn != kc) ce[kc] = (int)j;
+        if (nf) {
+          atomicOr(&cfl[1 + (kc >> 5)], 1u << (kc & 31));
+          atomicMin(&cf[kc], (int)j);
+        }
+      }
+    }
+    __syncthreads();
+    if (warp < 8) {  // one S row per thread, as in the softmax role below
+      const int r = (warp & 3) * 32 + lane;
+      const int64_t i = i0 + (warp >> 2) * R + r / G;
+      const int h = g * G + r % G;
+      if (i < p.nq) {
+        const int64_t qp = p.qpos[i];
+        const int64_t nl = qp + 1 < p.nk ? qp + 1 : p.nk;
+        auto mark = [&](int t0, int t1) {  // tiles t0 .. t1
+          for (int w = t0 >> 5; w <= (t1 >> 5); ++w) {
+            const int lo = w * 32 > t0 ? 0 : t0 - w * 32;
+            const int hi = w * 32 + 31 < t1 ? 31 : t1 - w * 32;
+            const uint32_t bits = (hi == 31 ? ~0u : ((2u << hi) - 1u)) & ~((1u << lo) - 1u);
+            atomicOr(&need[w], bits);
+          }
+        };
+        if (nl > 0) {
+          const int tq = (int)((nl - 1) >> 7);
+          mark(tq, tq);  // the row's own key
+          if (chunked && cfl[0] == 0u) {
+            const int qc = p.key_chunk[nl - 1];
+            const float* off = p.chunk_off + (int64_t)h * p.co_stride_h + i * p.co_stride_q;
+            const uint64_t nfc = (uint64_t)cfl[1] | ((uint64_t)cfl[2] << 32);
+            bool live = false;
+            for (int c = 0; c <= qc && c < kMaxMapChunks; ++c) {
+              if (ce[c] < 0) continue;  // no key of chunk c below nneed
+              if (cs[c] >= nl) break;
+              // a gate chain coming up from an older chunk needs all of chunk
+              // c; one that starts here needs it from its first seen key on
+              const bool from_first = !live && ((nfc >> c) & 1ull) && cf[c] < nl;
+              if (live || from_first) {
+                const int64_t e = ce[c] < nl - 1 ? ce[c] : nl - 1;
+                mark((live ? cs[c] : cf[c]) >> 7, (int)(e >> 7));
+                live = true;
+              }
+              if (c < qc && off[c] >= 0.f) live = false;
+            }
+          } else {
+            int first = -1;
+            for (int w = 0; w < kMapWords && first < 0; ++w)
+              if (nft[w]) first = w * 32 + __ffs(nft[w]) - 1;
+            if (first >= 0 && first < tq) mark(first, tq);
+          }
+        }
+      }
+    }
+    __syncthreads();
+  }
+  // steps: the needed key tiles, newest first
+  const uint32_t* needmap = reinterpret_cast<const uint32_t*>(meta + kNeed);
+  int nlist = ntile;
+  if (use_map) {
+    nlist = 0;
+    for (int w = 0; w < kMapWords; ++w) nlist += __popc(needmap[w]);
+  }
+
 
   if (warp >= 8 && warp < 12) {
     // ================================================================ producer
@@ -449,8 +582,20 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
     int kcj = -1;
     bool slot_bad = false;  // a key some row sees has no valid slot (read as zeros)
     const int64_t nmax = nneed;
-    auto load_key = [&](int it2) {
-      const int64_t j = (int64_t)(ntile - 1 - it2) * kTileN + pt;
+    // key tile of the step load_key prepares (newest first, needed tiles only)
+    int ktile = ntile;
+    auto load_key = [&]() {
+      if (use_map) {
+        int w = (ktile - 1) >> 5;
+        const int b = (ktile - 1) & 31;
+        uint32_t m = needmap[w] & (b == 31 ? ~0u : ((2u << b) - 1u));
+        while (m == 0u && w > 0) m = needmap[--w];
+        ktile = w * 32 + 31 - __clz(m);  // nlist bounds the steps: a bit is left
+      } else {
+        --ktile;
+      }
+      const int64_t j = (int64_t)ktile * kTileN + pt;
+
       const bool in = j < p.nk;
       // keys past the end: zero rows by cp.async; the TMA path repeats the
       // last key's row (finite data, and its P column is zero)
@@ -470,12 +615,13 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
     // publish the key metadata of tile it2 (slot it2 % 4) and start its K copy
     auto issue_k = [&](int it2, VSrc& vs) {
       const int slot = it2 & 3;
-      const int64_t key0 = (int64_t)(ntile - 1 - it2) * kTileN;
+      const int64_t key0 = (int64_t)ktile * kTileN;
       {
         const unsigned fm = __ballot_sync(kAll, fixed);
         const unsigned bm = __ballot_sync(kAll, bnd);
         // chunk id of the newest boundary of these 32 keys (-1: none)
         const int kc_top = __shfl_sync(kAll, kcj, bm ? 31 - __clz(bm) : 0);
+        if (pt == 0) reinterpret_cast<int*>(meta + kSlotTile)[slot] = (int)(key0 / kTileN);
         if (lane == 0) {
           reinterpret_cast<unsigned*>(meta + kFixMask)[slot * 4 + (warp - 8)] = fm;
           reinterpret_cast<unsigned*>(meta + kBndMask)[slot * 4 + (warp - 8)] = bm;
@@ -592,13 +738,13 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
     // are done; the PV barriers are per tile and V stage, so their next
     // phase needs the V copy issued here and cannot be missed.
     VSrc vs{};
-    if (ntile > 0) {
-      load_key(0);
+    if (nlist > 0) {
+      load_key();
       issue_k(0, vs);
       issue_v(0, vs);
-      if (ntile > 1) load_key(1);
+      if (nlist > 1) load_key();
     }
-    for (int it = 0; it + 1 < ntile; ++it) {
+    for (int it = 0; it + 1 < nlist; ++it) {
       bool ok = mbar_wait(mb + kBarS, it & 1, abort) && mbar_wait(mb + kBarS + 8, it & 1, abort);
       if (!named_and(1, 128, ok)) break;
       issue_k(it + 1, vs);
@@ -607,10 +753,19 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
                       mbar_wait(mb + kBarPV + 16 + pst, pph, abort));
       if (!named_and(1, 128, ok)) break;
       issue_v(it + 1, vs);
-      if (it + 2 < ntile) load_key(it + 2);
+      if (it + 2 < nlist) load_key();
+    }
+    if (use_map && p.kv_slots) {  // skipped tiles: their keys' slots are checked all the same
+#pragma unroll 1
+      for (int t = 0; t < ntile; ++t) {
+        if ((needmap[t >> 5] >> (t & 31)) & 1u) continue;
+        const int64_t j = (int64_t)t * kTileN + pt;
+        int32_t r1, r2;
+        if (j < nmax && key_src<T>(a, j, g, r1, r2) == 0) slot_bad = true;
+      }
     }
     if (slot_bad) report(p.status, CS_ST_SLOT_RANGE);
-    cp_async_wait_all();
+
   } else if (warp == 12) {
     // ================================================================== MMA
     if (lane == 0) {
@@ -640,7 +795,7 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
         }
         tc_commit(mb + kBarS + 8 * qt);
       };
-      if (ok && ntile > 0) {
+      if (ok && nlist > 0) {
         ok = mbar_wait(mb + kBarK, 0, abort);
         for (int qt = 0; ok && qt < 2; ++qt) {
           // the tile's S columns hold T until its softmax has read the table
@@ -651,7 +806,7 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
         }
       }
       int lastpv[2] = {-1, -1};  // last key tile whose PV was issued, per tile
-      for (int it = 0; ok && it < ntile; ++it) {
+      for (int it = 0; ok && it < nlist; ++it) {
         const int st = it & 1;
         for (int qt = 0; ok && qt < 2; ++qt) {
           if (!(ok = mbar_wait(mb + kBarP + 8 * qt, it & 1, abort))) break;
@@ -668,7 +823,7 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
           }
           tc_commit(mb + kBarPV + 16 * qt + 8 * st);
           lastpv[qt] = it;
-          if (it + 1 < ntile) {
+          if (it + 1 < nlist) {
             // S(it+1) of this tile overwrites the TMEM columns where P(it)
             // lives: PV(it) must be done
             if (!(ok = mbar_wait(mb + kBarPV + 16 * qt + 8 * st, (it >> 1) & 1, abort))) break;
@@ -798,15 +953,16 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
       }
       tmem_wait_st();
     };
-    for (int it = 0; ok && it < ntile; ++it) {
+    for (int it = 0; ok && it < nlist; ++it) {
       const int slot = it & 3;
-      const int kt = ntile - 1 - it;
-      const int64_t key0 = (int64_t)kt * kTileN;
-      // key metadata of slot it % 4: the producer publishes it ahead of S(it),
-      // and the slot is not reused before P(it) of both tiles.  Masks, chunk
-      // restarts and the fast / contextual decision are settled while QK(it)
-      // may still be running, so their latency hides behind it.
+      // key metadata of slot it % 4 (the step's key tile among them): the
+      // producer publishes it ahead of S(it), and the slot is not reused
+      // before P(it) of both tiles.  Masks, chunk restarts and the fast /
+      // contextual decision are settled while QK(it) may still be running,
+      // so their latency hides behind it.
       ok = mbar_wait(mb + kBarMeta + 8 * slot, (it >> 2) & 1, abort);
+      const int kt = ok ? reinterpret_cast<const volatile int*>(meta + kSlotTile)[slot] : 0;
+      const int64_t key0 = (int64_t)kt * kTileN;
       const unsigned* fixm = reinterpret_cast<const unsigned*>(meta + kFixMask) + slot * 4;
       const unsigned* bndm = reinterpret_cast<const unsigned*>(meta + kBndMask) + slot * 4;
       const int* bndkc = reinterpret_cast<const int*>(meta + kBndKc) + slot * 4;
@@ -1172,9 +1328,9 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
       mbar_arrive(mb + kBarP + 8 * qt);
     }
     // epilogue: O / l
-    if (ok && ntile > 0) {
-      ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarPV + 16 * qt + 8 * ((ntile - 1) & 1),
-                                             ((ntile - 1) >> 1) & 1, abort));
+    if (ok && nlist > 0) {
+      ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarPV + 16 * qt + 8 * ((nlist - 1) & 1),
+                                             ((nlist - 1) >> 1) & 1, abort));
       tc_fence_after();
     }
     int32_t bits = sbits;  // table-mode range / strict path bits
@@ -1187,7 +1343,7 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
     for (int cc = 0; cc < 4; ++cc) {
       const int col0 = cc * 32;
       uint32_t v[32];
-      if (ntile > 0 && ok) {
+      if (nlist > 0 && ok) {
         CS_TMEM_LD32(oc + col0, v);
         tmem_wait_ld();
       } else {

@@ -705,12 +705,12 @@ def test_future_keys_do_not_change_earlier_rows(cuda):
 @pytest.mark.parametrize("restart_low", [False, True])
 def test_tensor_core_prefill_skips_inert_tiles_exactly(cuda, restart_low):
     """Rows that are all selected (association policy) over a long context of
-    mostly fixed keys: once every row's count is saturated, the tensor-core
-    kernel skips the key tiles that hold only fixed keys, no chunk boundary
-    and none of the rows' own positions.  The result must equal the
-    kernel-without-skipping (the generic kernel) and the oracle; with
-    `restart_low` a chunk boundary restarts the counts low after saturation,
-    so the tiles below it are live again for the gates."""
+    mostly fixed keys: the tensor-core kernel takes only the key tiles that
+    hold a key some row sees (a non-fixed key or the row's own) or a gate
+    that feeds the count of such a key -- the chain from a seen key up to the
+    end of the first chunk that restarts the row's count.  The result must
+    equal the generic kernel (every tile) and the oracle; with `restart_low`
+    a chunk boundary restarts the counts low, so the gates below it matter."""
     import ctypes
 
     from cacheslide_b200 import _native as N
