@@ -471,6 +471,10 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
   // hidden from every row and change no count a row uses.  (Strict path
   // validation checks every causal key, so it keeps every tile.)
   bool use_map = false;
+  // per S row (softmax threads): the newest key whose gate feeds the count of
+  // a key the row sees other than its own; above it (the row's own key
+  // aside) no gate matters to the row (set for rows of a tile-map CTA)
+  int64_t chain_hi = INT64_MAX;
   {
     bool allsel = p.q_selected != nullptr && p.k_fixed != nullptr && !(TBL && p.strict != 0);
     for (int w = 0; w < 8; ++w) allsel = allsel && reinterpret_cast<const volatile int*>(meta + kAllSel)[w] != 0;
@@ -530,6 +534,7 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
             const float* off = p.chunk_off + (int64_t)h * p.co_stride_h + i * p.co_stride_q;
             const uint64_t nfc = (uint64_t)cfl[1] | ((uint64_t)cfl[2] << 32);
             bool live = false;
+            int64_t hi = -1;
             for (int c = 0; c <= qc && c < kMaxMapChunks; ++c) {
               if (ce[c] < 0) continue;  // no key of chunk c below nneed
               if (cs[c] >= nl) break;
@@ -540,9 +545,11 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
                 const int64_t e = ce[c] < nl - 1 ? ce[c] : nl - 1;
                 mark((live ? cs[c] : cf[c]) >> 7, (int)(e >> 7));
                 live = true;
+                hi = e > hi ? e : hi;
               }
               if (c < qc && off[c] >= 0.f) live = false;
             }
+            chain_hi = hi;
           } else {
             int first = -1;
             for (int w = 0; w < kMapWords && first < 0; ++w)
@@ -1132,6 +1139,10 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
         continue;
       }
       float tmax = -INFINITY;
+      // contextual chunks that took the own-key-only path (bit cc) and their
+      // one score per row
+      unsigned somask = 0u;
+      float xs0 = -INFINITY, xs1 = -INFINITY, xs2 = -INFINITY, xs3 = -INFINITY;
       if (fast) {
         // saturated, the row's first visible tile: every visible score is
         // S * scale2 + tsat2, a monotone map of the raw S, so the tile max
@@ -1187,6 +1198,34 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
             CS_TMEM_ST32(sc + 32 * cc, s);
             if (lim > 0) Rc = fmaxf(Rc, top);
             continue;
+          }
+          // every column a row sees in the chunk is its own key, and the chunk
+          // lies above every gate chain of the row's other seen keys: the own
+          // key's count is its gate (it is the newest causal key, so the
+          // count entering it is Rc) and no other gate of the chunk matters.
+          // One gate and one interpolation a row; the P pass takes the one
+          // score from xs (the scores are not stored back).
+          {
+            const int64_t selfc = qp - (key0 + cc * 32);
+            const unsigned selfbit = (selfc >= 0 && selfc < 32) ? (1u << (int)selfc) : 0u;
+            if (!warp_tbl &&
+                __all_sync(0xffffffffu, key0 + cc * 32 > chain_hi && (~hm & ~selfbit) == 0u)) {
+              float zs = 0.f;
+#pragma unroll
+              for (int c = 0; c < 32; ++c) zs = (selfbit >> c) & 1u ? __uint_as_float(s[c]) : zs;
+              float xs = -INFINITY;
+              if ((~hm & selfbit) != 0u) {
+                Rc = Rc + fmaf(0.5f, tanh_approx(zs * half_scale), 0.5f);
+                xs = fmaf(zs, scale2, bias_at(fminf(Rc, top)));
+              }
+              t0 = fmaxf(t0, xs);
+              xs0 = cc == 0 ? xs : xs0;
+              xs1 = cc == 1 ? xs : xs1;
+              xs2 = cc == 2 ? xs : xs2;
+              xs3 = cc == 3 ? xs : xs3;
+              somask |= 1u << cc;
+              continue;
+            }
           }
 #pragma unroll
           for (int c = 0; c < 32; ++c)  // gate = sigmoid(z) = (1 + tanh(z / 2)) / 2: one MUFU op
@@ -1297,9 +1336,15 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
       for (int cc = 0; cc < 4; ++cc) {
         const unsigned hm = hide_of(cc);
         uint32_t v[32];
-        if (fast && __all_sync(0xffffffffu, hm == ~0u)) {
+        if ((fast || !((somask >> cc) & 1u)) && __all_sync(0xffffffffu, hm == ~0u)) {
 #pragma unroll
           for (int c = 0; c < 32; ++c) v[c] = 0u;
+        } else if ((somask >> cc) & 1u) {  // own key only: one exponential a row
+          const int64_t selfc = qp - (key0 + cc * 32);
+          const float xs = cc == 0 ? xs0 : cc == 1 ? xs1 : cc == 2 ? xs2 : xs3;
+          const float es = ex2(xs - mcur);
+#pragma unroll
+          for (int c = 0; c < 32; ++c) v[c] = __float_as_uint(selfc == c ? es : 0.f);
         } else {
           CS_TMEM_LD32(sc + 32 * cc, v);
           tmem_wait_ld();
