@@ -79,14 +79,22 @@ def peaks():
 # DRAM bytes of one batched prefill launch of the C2 step (8 requests), from
 # an ncu capture of that launch (dram__bytes_read.sum + dram__bytes_write.sum);
 # None until captured for the current kernel
-PREFILL_DRAM_BYTES_PER_LAUNCH = None
+# dram__bytes_read.sum + dram__bytes_write.sum of one batched C2 attention
+# launch, from the ncu --set full capture summarised in
+# profiles/cope_prefill_sm100_batch_c2_step.md (363.96 MB + 55.18 MB)
+PREFILL_DRAM_BYTES_PER_LAUNCH = 419138048
 
 
-def attention_flops(work) -> float:
+def attention_flops(work, visible_only: bool = False) -> float:
     """Algorithmic FLOPs of the attention launches of one step.
 
-    QK over every causal cell (the gates count all causal keys), PV over every
-    visible cell (association policy), plus the q.E table.
+    QK over every causal cell, PV over every visible cell (association
+    policy), plus the q.E table.  Counting QK over every causal cell follows
+    the reference's computation, whose gates count all causal keys.  The
+    kernel skips the key tiles whose cells no row of a CTA sees and whose
+    gates feed no seen key's count, so it issues less than this.  With
+    `visible_only`, QK and PV count the visible cells only: the lower bound
+    that any implementation must compute.
     """
     c = work.cfg
     total = 0.0
@@ -97,7 +105,8 @@ def attention_flops(work) -> float:
         fixed = r.reused.cpu().numpy()
         dyn_prefix = np.cumsum(~fixed)  # dynamic keys with position <= p
         visible = np.where(sel, dyn_prefix[qpos] + 1, causal)
-        total += 2 * c.head_dim * c.q_heads * (causal.sum() + visible.sum())
+        qk_cells = visible.sum() if visible_only else causal.sum()
+        total += 2 * c.head_dim * c.q_heads * (qk_cells + visible.sum())
         total += 2 * len(qpos) * c.q_heads * c.npos * c.head_dim
     return total
 
@@ -719,6 +728,7 @@ def main():
     if rank == 0:
         pk, pk_kind = peaks()
         flops = attention_flops(work)  # per attention pass over this rank's requests
+        flops_vis = attention_flops(work, visible_only=True)
         achieved = flops / (att_ms / 1e3) / 1e12
         peak = float(pk.get("bf16_tflops", 1590.0))
         cpu = None
@@ -754,11 +764,14 @@ def main():
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "peak_kind": pk_kind,
                          "flops_per_launch": flops,
+                         "visible_cell_flops_per_launch": flops_vis,
+                         "visible_cell_tflops": flops_vis / (att_ms * 1e-3) / 1e12,
                          "ms_per_launch": att_ms,
                          "launches_timed": args.steps,
                          "traffic": PREFILL_DRAM_BYTES_PER_LAUNCH,
                          "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum of one "
-                                         "C2 request launch (ncu --set full capture)"},
+                                         "batched C2 attention launch (8 requests; ncu --set full "
+                                         "capture)"},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world},

@@ -488,27 +488,72 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
     int* ce = reinterpret_cast<int*>(meta + kChunkE);
     int* cf = reinterpret_cast<int*>(meta + kChunkF);
     const bool chunked = p.pos_mode == CS_POS_CHUNK;
-    // keys 0 .. nneed-1: tiles and chunks holding a non-fixed key, chunk ranges
+    // keys 0 .. nneed-1: tiles and chunks holding a non-fixed key, chunk
+    // ranges.  A thread takes 16 consecutive keys a pass (one 16-byte load of
+    // the fixed flags, four of the chunk ids when aligned), so the loads of
+    // its keys are in flight together
+    const bool vfix = (reinterpret_cast<uintptr_t>(p.k_fixed) & 15) == 0;
+    const bool vkc = chunked && (reinterpret_cast<uintptr_t>(p.key_chunk) & 15) == 0;
 #pragma unroll 1
-    for (int64_t j = tid; j < nneed; j += kThreads) {
-      const bool nf = p.k_fixed[j] == 0;
-      if (nf) atomicOr(&nft[(int)(j >> 12)], 1u << (int)((j >> 7) & 31));
+    for (int64_t j0 = (int64_t)tid * 16; j0 < nneed; j0 += (int64_t)kThreads * 16) {
+      const bool whole = j0 + 16 <= nneed;
+      uint32_t fw[4];  // fixed flags, 4 keys a word
+      int kc[16];
+      if (whole && vfix) {
+        const uint4 f4 = __ldg(reinterpret_cast<const uint4*>(p.k_fixed + j0));
+        fw[0] = f4.x, fw[1] = f4.y, fw[2] = f4.z, fw[3] = f4.w;
+      } else {
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          uint32_t x = 0u;
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            const int64_t j = j0 + 4 * w + b;
+            x |= (uint32_t)(j < nneed ? p.k_fixed[j] : 1) << (8 * b);
+          }
+          fw[w] = x;
+        }
+      }
+      int kprev = -1, knext = -1;
       if (chunked) {
-        const int kc = p.key_chunk[j];
-        if (kc < 0 || kc >= kMaxMapChunks) {
+        if (whole && vkc) {
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            const int4 c4 = __ldg(reinterpret_cast<const int4*>(p.key_chunk + j0) + w);
+            kc[4 * w] = c4.x, kc[4 * w + 1] = c4.y, kc[4 * w + 2] = c4.z, kc[4 * w + 3] = c4.w;
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < 16; ++k) kc[k] = j0 + k < nneed ? p.key_chunk[j0 + k] : -1;
+        }
+        kprev = j0 > 0 ? p.key_chunk[j0 - 1] : -1;
+        knext = j0 + 16 < nneed ? p.key_chunk[j0 + 16] : -1;
+      }
+      bool anynf = false;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const int64_t j = j0 + k;
+        if (j >= nneed) break;
+        const bool nf = ((fw[k >> 2] >> (8 * (k & 3))) & 0xffu) == 0u;
+        anynf |= nf;
+        if (!chunked) continue;
+        const int c = kc[k];
+        if (c < 0 || c >= kMaxMapChunks) {
           cfl[0] = 1u;
           continue;
         }
-        const int kp = j > 0 ? p.key_chunk[j - 1] : -1;
-        const int kn = j + 1 < nneed ? p.key_chunk[j + 1] : -1;
-        if (kp > kc) cfl[0] = 1u;
-        if (kp != kc) cs[kc] = (int)j;
-        if (kn != kc) ce[kc] = (int)j;
+        const int kp = k > 0 ? kc[k - 1] : kprev;
+        const int kn = k < 15 ? (j + 1 < nneed ? kc[k + 1] : -1) : knext;
+        if (kp > c) cfl[0] = 1u;
+        if (kp != c) cs[c] = (int)j;
+        if (kn != c) ce[c] = (int)j;
         if (nf) {
-          atomicOr(&cfl[1 + (kc >> 5)], 1u << (kc & 31));
-          atomicMin(&cf[kc], (int)j);
+          atomicOr(&cfl[1 + (c >> 5)], 1u << (c & 31));
+          atomicMin(&cf[c], (int)j);
         }
       }
+      // the 16 keys lie in one key tile
+      if (anynf) atomicOr(&nft[(int)(j0 >> 12)], 1u << (int)((j0 >> 7) & 31));
     }
     __syncthreads();
     if (warp < 8) {  // one S row per thread, as in the softmax role below
@@ -533,21 +578,33 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
             const int qc = p.key_chunk[nl - 1];
             const float* off = p.chunk_off + (int64_t)h * p.co_stride_h + i * p.co_stride_q;
             const uint64_t nfc = (uint64_t)cfl[1] | ((uint64_t)cfl[2] << 32);
-            bool live = false;
+            bool live = false, stop = false;
             int64_t hi = -1;
-            for (int c = 0; c <= qc && c < kMaxMapChunks; ++c) {
-              if (ce[c] < 0) continue;  // no key of chunk c below nneed
-              if (cs[c] >= nl) break;
-              // a gate chain coming up from an older chunk needs all of chunk
-              // c; one that starts here needs it from its first seen key on
-              const bool from_first = !live && ((nfc >> c) & 1ull) && cf[c] < nl;
-              if (live || from_first) {
-                const int64_t e = ce[c] < nl - 1 ? ce[c] : nl - 1;
-                mark((live ? cs[c] : cf[c]) >> 7, (int)(e >> 7));
-                live = true;
-                hi = e > hi ? e : hi;
+            // the row's offsets eight chunks at a time (loads in flight together)
+            for (int c8 = 0; !stop && c8 <= qc && c8 < kMaxMapChunks; c8 += 8) {
+              float o8[8];
+#pragma unroll
+              for (int k = 0; k < 8; ++k) o8[k] = c8 + k < qc ? off[c8 + k] : -1.f;
+#pragma unroll
+              for (int k = 0; k < 8; ++k) {
+                const int c = c8 + k;
+                if (c > qc || c >= kMaxMapChunks) break;
+                if (ce[c] < 0) continue;  // no key of chunk c below nneed
+                if (cs[c] >= nl) {
+                  stop = true;
+                  break;
+                }
+                // a gate chain coming up from an older chunk needs all of chunk
+                // c; one that starts here needs it from its first seen key on
+                const bool from_first = !live && ((nfc >> c) & 1ull) && cf[c] < nl;
+                if (live || from_first) {
+                  const int64_t e = ce[c] < nl - 1 ? ce[c] : nl - 1;
+                  mark((live ? cs[c] : cf[c]) >> 7, (int)(e >> 7));
+                  live = true;
+                  hi = e > hi ? e : hi;
+                }
+                if (c < qc && o8[k] >= 0.f) live = false;
               }
-              if (c < qc && off[c] >= 0.f) live = false;
             }
             chain_hi = hi;
           } else {
