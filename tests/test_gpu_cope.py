@@ -702,28 +702,37 @@ def test_future_keys_do_not_change_earlier_rows(cuda):
     torch.testing.assert_close(changed[:2], original[:2])
 
 
-@pytest.mark.parametrize("restart_low", [False, True])
-def test_tensor_core_prefill_skips_inert_tiles_exactly(cuda, restart_low):
+@pytest.mark.parametrize("mode", ["high", "low", "carry", "plain"])
+@pytest.mark.parametrize("hq,hkv", [(32, 8), (8, 1)])
+def test_tensor_core_prefill_skips_inert_tiles_exactly(cuda, mode, hq, hkv):
     """Rows that are all selected (association policy) over a long context of
     mostly fixed keys: the tensor-core kernel takes only the key tiles that
     hold a key some row sees (a non-fixed key or the row's own) or a gate
     that feeds the count of such a key -- the chain from a seen key up to the
-    end of the first chunk that restarts the row's count.  The result must
-    equal the generic kernel (every tile) and the oracle; with `restart_low`
-    a chunk boundary restarts the counts low, so the gates below it matter."""
+    end of the first chunk that restarts the row's count, or up to the row
+    itself without restarts.  The result must equal the generic kernel
+    (every tile) and the oracle.  Modes: `high` -- every older chunk
+    restarts far above npos - 1; `low` -- one chunk restarts low, so the
+    gates below its boundary matter; `carry` -- one chunk carries the
+    running count instead (offset -1), so a chain crosses its boundary, and
+    some rows see keys of their own chunk; `plain` -- contextual positions
+    without restarts (every gate from the oldest seen key up is live)."""
     import ctypes
 
     from cacheslide_b200 import _native as N
     from cacheslide_b200.position import _Holder, _base_params
 
-    nq, nk, d, hq, hkv = 64, 4096, 128, 32, 8
-    g = torch.Generator().manual_seed(11 + restart_low)
+    nq, nk, d = 64, 4096, 128
+    seed = 11 + ["high", "low", "carry", "plain"].index(mode) + 7 * hkv
+    g = torch.Generator().manual_seed(seed)
     q = (torch.randn(nq, hq, d, generator=g) / d ** 0.5).to(torch.bfloat16).to(cuda)
     k = (torch.randn(nk, hkv, d, generator=g) / d ** 0.5).to(torch.bfloat16).to(cuda)
     v = torch.randn(nk, hkv, d, generator=g).to(torch.bfloat16).to(cuda)
     fixed = torch.ones(nk, dtype=torch.bool)
     fixed[600:610] = False       # a few visible keys far below the rows
     fixed[1800:1830] = False
+    if mode in ("carry", "plain"):
+        fixed[3300:3306] = False  # seen keys inside the rows' own chunk
     rows = torch.sort(torch.randperm(900, generator=g)[:nq] + 3100).values
     selected = rows.clone()      # every row is a selected (fixed) token
     q_sel = torch.ones(nq, dtype=torch.uint8, device=cuda)
@@ -733,12 +742,15 @@ def test_tensor_core_prefill_skips_inert_tiles_exactly(cuda, restart_low):
     key_chunk = (torch.arange(nk) // 1024).to(torch.int32)
     nch = 4
     offsets = torch.full((hq, nk, nch), 200.0)  # restarts far above npos - 1
-    if restart_low:
+    if mode == "low":
         offsets[:, :, 1] = 3.0                  # boundary after key 2047: low restart
+    if mode == "carry":
+        offsets[:, :, 1] = -1.0                 # chunk 1 carries the running count
     off_rows = offsets[:, rows].contiguous().to(cuda)
     rows_d = rows.to(cuda)
     k_fix = fixed.to(torch.uint8).to(cuda)
     kc_dev = key_chunk.to(cuda)
+    chunked = mode != "plain"
     lib = N.load()
     outs = []
     for fast in (True, False):
@@ -747,10 +759,11 @@ def test_tensor_core_prefill_skips_inert_tiles_exactly(cuda, restart_low):
         p.out = out.data_ptr()
         p.o_stride_tok, p.o_stride_head = out.stride(0), out.stride(1)
         p.q_selected, p.k_fixed = q_sel.data_ptr(), k_fix.data_ptr()
-        p.pos_mode = N.POS_CHUNK
-        p.key_chunk, p.chunk_off = kc_dev.data_ptr(), off_rows.data_ptr()
-        p.co_stride_h, p.co_stride_q = off_rows.stride(0), off_rows.stride(1)
-        p.nchunks = nch
+        if chunked:
+            p.pos_mode = N.POS_CHUNK
+            p.key_chunk, p.chunk_off = kc_dev.data_ptr(), off_rows.data_ptr()
+            p.co_stride_h, p.co_stride_q = off_rows.stride(0), off_rows.stride(1)
+            p.nchunks = nch
         st = N.Status(cuda)
         p.status = st.ptr
         fn = lib.cs_cope_attn_prefill if fast else lib.cs_cope_attn
@@ -759,12 +772,15 @@ def test_tensor_core_prefill_skips_inert_tiles_exactly(cuda, restart_low):
         assert st.read() == 0
         outs.append(out.float().cpu().numpy())
     np.testing.assert_allclose(outs[0], outs[1], **BF16)
+    kw = {}
+    if chunked:
+        kw["chunk_reset"] = (key_chunk.numpy(), off_rows.cpu().numpy())
     want = ocope.cope_attention(
         q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(), E.numpy(),
         rows.numpy(),
         visibility_fn=lambda a, b: ocope.association_mask(
             a, b, np.nonzero(fixed.numpy())[0], selected.numpy()),
-        chunk_reset=(key_chunk.numpy(), off_rows.cpu().numpy()))
+        **kw)
     np.testing.assert_allclose(outs[0], want, **BF16)
 
 
