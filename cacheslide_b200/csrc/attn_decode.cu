@@ -1204,8 +1204,12 @@ void fill_request(DecodeReq& q, const cs_attn_params* p, float* zs, float* ws, c
 }
 
 // Raises the dynamic shared memory limit of `kern` on the current device,
-// once per device.
-template <typename K>
+// once per device and kernel.  The cache is keyed by the kernel's template
+// arguments (Tag), not by the function pointer type: every instantiation of
+// a kernel template shares that type.
+template <typename T, int G>
+struct OnepassTag {};
+template <typename Tag, typename K>
 bool smem_configured(K kern, int bytes) {
   static std::atomic<uint64_t> done{0};  // bit d: device d configured
   int dev = 0;
@@ -1288,7 +1292,7 @@ int launch_batch(const cs_attn_params* ps, int count, char* workspace, cudaStrea
       using T = decltype(tag);
       constexpr int G = decltype(gtag)::value;
       auto kern = decode_onepass_tc<T, G>;
-      if (!smem_configured(kern, (int)kOnepassSmem)) {
+      if (!smem_configured<OnepassTag<T, G>>(kern, (int)kOnepassSmem)) {
         rc = CS_ERR_CUDA;
         return;
       }
