@@ -86,6 +86,7 @@ class AttnParams(ctypes.Structure):
         ("in_dtype", _i32), ("out_dtype", _i32),
         ("status", _p),
         ("launch_flags", _i32),
+        ("nq_dev", _p),
     ]
 
 
@@ -159,6 +160,7 @@ _SIGNATURES = {
                         _p, _p, _p, _p],
     "cs_wca_weights": [_p, _p, _i64, _f64, _i32, _p, _p, _p, _p, _p, _p],
     "cs_wca_select_topk": [_p, _p, _i64, _i64, _p, _p, _p, _p, _p],
+    "cs_wca_active_rows": [_p, _p, _i64, _i64, _p, _p, _p, _p, _p],
     "cs_wca_initialize": [_p, _i64, _i64, _p, _i64, _i64, _i64, _i64, _i64, _i32, _p, _f64,
                           _i32, _p, _p, _p, _p, _p, _p, _p, _p],
     "cs_wca_update": [_p, _p, _i64, _i64, _p, _p, _i64, _i64, _p, _i64, _i64, _i64, _i32, _p,

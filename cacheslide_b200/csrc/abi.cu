@@ -8,4 +8,4 @@ extern "C" const char* cs_build_info(void) {
       __CUDACC_VER_MINOR__);
 }
 
-extern "C" int32_t cs_abi_version(void) { return 2; }
+extern "C" int32_t cs_abi_version(void) { return 3; }

@@ -1109,6 +1109,7 @@ bool fast_decode_ok(const cs_attn_params* p) {
 }
 
 bool decode_supported(const cs_attn_params* p) {
+  if (p->nq_dev != nullptr) return false;  // a device row count is a prefill option
   if (p->in_dtype != CS_BF16 && p->in_dtype != CS_F16) return false;
   if (p->out_dtype != CS_BF16 && p->out_dtype != CS_F16 && p->out_dtype != CS_F32) return false;
   if (p->pos_mode != CS_POS_CONTEXTUAL) return false;

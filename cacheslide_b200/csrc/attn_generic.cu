@@ -443,6 +443,7 @@ int validate_attn_params(const cs_attn_params* p) {
 using namespace cs;
 
 extern "C" int cs_cope_attn(const cs_attn_params* p, void* stream) {
+  if (p != nullptr && p->nq_dev != nullptr) return CS_ERR_UNSUPPORTED;  // prefill only
   int rc = validate_attn_params(p);
   if (rc != CS_OK) return rc;
   if (p->nq == 0) return CS_OK;

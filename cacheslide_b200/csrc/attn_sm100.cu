@@ -364,6 +364,15 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
   const int G = a.G, R = a.R;
   const int64_t i0 = (int64_t)pair * 2 * R;
   const float top = (float)(p.npos - 1);
+  // live query rows: nq, or a count in device memory (at most nq); a CTA
+  // whose rows all lie past it leaves at once (every thread reads the same
+  // value, so the exit is uniform and comes before any barrier or TMEM use)
+  int64_t nq = p.nq;
+  if (p.nq_dev != nullptr) {
+    const int64_t c = __ldg(p.nq_dev);
+    nq = c < 0 ? 0 : (c < nq ? c : nq);
+  }
+  if (i0 >= nq) return;
 
   if (tid == 0) {
     mbar_init(mb + kBarQ, 384);  // Q copies (producer) + E split (producer and softmax)
@@ -385,7 +394,7 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
   if (warp < 8) {  // keys needed by the furthest row of the two tiles: one row per thread
     int64_t n = 0;
     bool sel = true;
-    if (tid < 2 * R && i0 + tid < p.nq) {
+    if (tid < 2 * R && i0 + tid < nq) {
       const int64_t qp = p.qpos[i0 + tid];
       n = qp + 1 < p.nk ? qp + 1 : p.nk;
       sel = p.q_selected != nullptr && p.q_selected[i0 + tid] != 0;
@@ -427,7 +436,7 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
     for (int qt = 0; qt < 2; ++qt) {
       const int64_t i = i0 + qt * R + pt / G;
       const int h = g * G + pt % G;
-      qrow[qt] = i < p.nq ? static_cast<const char*>(p.q) +
+      qrow[qt] = i < nq ? static_cast<const char*>(p.q) +
                                 (i * p.q_stride_tok + (int64_t)h * p.q_stride_head) *
                                     (int64_t)sizeof(T)
                           : nullptr;
@@ -560,7 +569,7 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
       const int r = (warp & 3) * 32 + lane;
       const int64_t i = i0 + (warp >> 2) * R + r / G;
       const int h = g * G + r % G;
-      if (i < p.nq) {
+      if (i < nq) {
         const int64_t qp = p.qpos[i];
         const int64_t nl = qp + 1 < p.nk ? qp + 1 : p.nk;
         auto mark = [&](int t0, int t1) {  // tiles t0 .. t1
@@ -926,7 +935,7 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
     const int r = q4 * 32 + lane;  // TMEM lane == tile row
     const int64_t i = i0 + qt * R + r / G;
     const int h = g * G + r % G;
-    const bool row_ok = i < p.nq;
+    const bool row_ok = i < nq;
     const int64_t qp = row_ok ? p.qpos[i] : -1;
     const int64_t nlim = row_ok ? (qp + 1 < p.nk ? qp + 1 : p.nk) : 0;
     const bool qsel = row_ok && p.q_selected != nullptr && p.q_selected[i] != 0;

@@ -1783,3 +1783,79 @@ extern "C" int cs_wca_commit_batch(const cs_wca_commit_item* items, int32_t coun
   }
   return CS_OK;
 }
+
+// ------------------------------------------------------------ active rows
+// The layer's active rows (WCAState.active_indices, wca.py:194-196:
+// nonzero(selected | mandatory), ascending) and, per active row, the
+// association flag of runtime.py:448-454 (selected and not mandatory), written
+// on the device with the count, so that the next launches of the layer need
+// no host read.  One block: a pass takes 1024 rows, a block-wide exclusive
+// scan of the active flags gives each row its output index.
+namespace cs {
+namespace {
+constexpr int kActThreads = 1024;
+__global__ void __launch_bounds__(kActThreads)
+    active_rows_kernel(const uint8_t* __restrict__ selected, const uint8_t* __restrict__ mandatory,
+                       int64_t n, int64_t capacity, int64_t* __restrict__ rows_out,
+                       uint8_t* __restrict__ sel_out, int64_t* __restrict__ count_out,
+                       int32_t* status) {
+  __shared__ int wcount[kActThreads / 32];
+  __shared__ int woff[kActThreads / 32];
+  __shared__ int64_t base;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) base = 0;
+  __syncthreads();
+  for (int64_t j0 = 0; j0 < n; j0 += kActThreads) {
+    const int64_t j = j0 + tid;
+    const bool sel = j < n && selected[j] != 0;
+    const bool man = j < n && mandatory[j] != 0;
+    const bool act = sel || man;
+    const unsigned bal = __ballot_sync(0xffffffffu, act);
+    if (lane == 0) wcount[warp] = __popc(bal);
+    __syncthreads();
+    if (warp == 0) {  // exclusive scan of the 32 warp counts
+      const int c = wcount[lane];
+      int x = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+      }
+      woff[lane] = x - c;
+    }
+    __syncthreads();
+    const int64_t pos = base + woff[warp] + __popc(bal & ((1u << lane) - 1u));
+    if (act && pos < capacity) {
+      rows_out[pos] = j;
+      sel_out[pos] = (sel && !man) ? 1 : 0;
+    }
+    __syncthreads();
+    if (tid == kActThreads - 1) base += woff[warp] + __popc(bal);
+    __syncthreads();
+  }
+  const int64_t total = base;
+  const int64_t cnt = total < capacity ? total : capacity;
+  for (int64_t q = cnt + tid; q < capacity; q += kActThreads) {  // rows past the count
+    rows_out[q] = -1;
+    sel_out[q] = 0;
+  }
+  if (tid == 0) {
+    *count_out = cnt;
+    if (total > capacity) report(status, CS_ST_SLOT_RANGE);
+  }
+}
+}  // namespace
+}  // namespace cs
+
+extern "C" int cs_wca_active_rows(const uint8_t* selected, const uint8_t* mandatory, int64_t n,
+                                  int64_t capacity, int64_t* rows_out, uint8_t* sel_out,
+                                  int64_t* count_out, int32_t* status, void* stream) {
+  if (n < 0 || capacity < 0 || count_out == nullptr) return CS_ERR_INVALID;
+  if (n > 0 && (selected == nullptr || mandatory == nullptr)) return CS_ERR_INVALID;
+  if (capacity > 0 && (rows_out == nullptr || sel_out == nullptr)) return CS_ERR_INVALID;
+  cs::active_rows_kernel<<<1, cs::kActThreads, 0, cs::as_stream(stream)>>>(selected, mandatory, n, capacity,
+                                                                rows_out, sel_out, count_out,
+                                                                status);
+  CS_LAUNCH_CHECK();
+  return CS_OK;
+}

@@ -240,6 +240,28 @@ class WCAState:
         """Sorted global token indices to compute at the next layer."""
         return (self.selected_mask | self.mandatory_mask).nonzero().flatten()
 
+    def active_rows_device(self, capacity: int, status: Tensor | None = None):
+        """The next layer's active rows without a host read.
+
+        Returns device tensors ``rows`` (int64 ``[capacity]``: ``active_indices``
+        then -1), ``association`` (uint8 ``[capacity]``: the row is selected and
+        not mandatory, runtime.py:448-454) and ``count`` (int64 ``[1]``), all
+        written by one kernel on the current stream.  Pass ``count`` as
+        ``AttnParams.nq_dev`` to run the next prefill on these rows.  Rows past
+        ``capacity`` are dropped and set CS_ST_SLOT_RANGE in ``status``.
+        """
+        dev = self.selected_mask.device
+        n = self.selected_mask.numel()
+        rows = torch.empty(max(capacity, 1), dtype=torch.int64, device=dev)[:capacity]
+        assoc = torch.empty(max(capacity, 1), dtype=torch.uint8, device=dev)[:capacity]
+        count = torch.empty(1, dtype=torch.int64, device=dev)
+        st = status.data_ptr() if status is not None else None
+        N.check(N.load().cs_wca_active_rows(
+            self.selected_mask.data_ptr(), self.mandatory_mask.data_ptr(), n, capacity,
+            rows.data_ptr(), assoc.data_ptr(), count.data_ptr(), st, N.stream_of(dev)),
+            "cs_wca_active_rows")
+        return rows, assoc, count
+
     @property
     def selected_indices(self) -> Tensor:
         return self.selected_mask.nonzero().flatten()

@@ -343,6 +343,20 @@ typedef struct {
 CS_API int cs_wca_commit_batch(const cs_wca_commit_item* items, int32_t count, double threshold,
                                int32_t distance_mode, void* stream);
 
+/*
+ * The layer's active rows on the device (WCAState.active_indices,
+ * wca.py:194-196, and the association rows of runtime.py:448-454): rows_out
+ * = the ascending indices r < n with selected[r] or mandatory[r]; sel_out[k]
+ * = 1 when row rows_out[k] is selected and not mandatory; *count_out = their
+ * number, all written by one kernel on `stream`.  Entries from the count up
+ * to `capacity` are -1 / 0; rows beyond `capacity` are dropped and set
+ * CS_ST_SLOT_RANGE.  With cs_attn_params.nq_dev = count_out the prefill of
+ * the next layer runs on these rows without a host read.
+ */
+CS_API int cs_wca_active_rows(const uint8_t* selected, const uint8_t* mandatory, int64_t n,
+                              int64_t capacity, int64_t* rows_out, uint8_t* sel_out,
+                              int64_t* count_out, int32_t* status, void* stream);
+
 /* ------------------------------------------------- selective layer loop */
 /*
  * The QKV projection of a layer's active rows (runtime.py:409-460 with the
@@ -456,6 +470,13 @@ typedef struct {
      library's cs_slide_scatter qualifies (it writes only K/V records, which
      the decode reads after waiting for it).  0 = plain stream order. */
   int32_t launch_flags;
+  /* cs_cope_attn_prefill(_batch) only (the other entry points return
+     CS_ERR_UNSUPPORTED when it is set): the number of live query rows is
+     *nq_dev, read by the kernel from device memory and clamped to [0, nq], so
+     that a count the device produced (cs_wca_active_rows) needs no host read;
+     nq is then the capacity the grid is sized for.  Rows at or past the count
+     are not computed and their output rows are not written. */
+  const int64_t* nq_dev;
 } cs_attn_params;
 
 #define CS_LAUNCH_OVERLAP_PREV 1

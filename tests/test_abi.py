@@ -37,7 +37,7 @@ def test_library_exports_every_declared_symbol():
 def test_binding_covers_every_declared_symbol():
     assert declared() <= set(N.EXPORTED)
     lib = N.load()
-    assert lib.cs_abi_version() == 2
+    assert lib.cs_abi_version() == 3
     assert b"sm_100a" in lib.cs_build_info()
 
 

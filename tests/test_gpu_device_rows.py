@@ -1,0 +1,147 @@
+"""Active rows on the device and a prefill sized by a device row count.
+
+The next layer's active rows (WCAState.active_indices, wca.py:194-196) and
+their association flags (runtime.py:448-454) are produced by
+`cs_wca_active_rows` on the device; the tensor-core prefill reads the row
+count through `AttnParams.nq_dev`, so the layer's attention runs on the
+rows the commit chose without a host read in between.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture
+def cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    return torch.device("cuda:0")
+
+
+@pytest.mark.parametrize("n,extra", [(5000, 17), (4096, 0), (1, 3), (3000, -40)])
+def test_active_rows_match_nonzero(cuda, n, extra):
+    """rows = nonzero(selected | mandatory) ascending, association = selected
+    and not mandatory, -1 / 0 padding to the capacity; a capacity below the
+    count keeps the first rows and sets CS_ST_SLOT_RANGE."""
+    from cacheslide_b200 import _native as N
+
+    g = torch.Generator().manual_seed(n)
+    selected = torch.rand(n, generator=g) < 0.15
+    mandatory = torch.zeros(n, dtype=torch.bool)
+    mandatory[n // 3: n // 3 + n // 8] = True
+    mandatory[n - 1] = True
+    selected[n // 3: n // 3 + 10] = True  # some rows both selected and mandatory
+    want = torch.nonzero(selected | mandatory).flatten()
+    cap = max(len(want) + extra, 0)
+    rows = torch.full((max(cap, 1),), 7, dtype=torch.int64, device=cuda)
+    assoc = torch.full((max(cap, 1),), 9, dtype=torch.uint8, device=cuda)
+    count = torch.full((1,), -5, dtype=torch.int64, device=cuda)
+    st = N.Status(cuda)
+    lib = N.load()
+    sel_d, man_d = selected.to(cuda), mandatory.to(cuda)  # held until the kernel has run
+    N.check(lib.cs_wca_active_rows(
+        sel_d.data_ptr(), man_d.data_ptr(), n, cap, rows.data_ptr(),
+        assoc.data_ptr(), count.data_ptr(), st.ptr, N.stream_of(cuda)), "active_rows")
+    torch.cuda.synchronize(cuda)
+    got_n = int(count.item())
+    assert got_n == min(len(want), cap)
+    assert torch.equal(rows[:got_n].cpu(), want[:got_n])
+    want_assoc = (selected & ~mandatory)[want[:got_n]].to(torch.uint8)
+    assert torch.equal(assoc[:got_n].cpu(), want_assoc)
+    assert bool((rows[got_n:cap] == -1).all()) and bool((assoc[got_n:cap] == 0).all())
+    assert st.read() == (N.ST_SLOT_RANGE if len(want) > cap else 0)
+
+
+def test_prefill_rows_from_device_count(cuda):
+    """The reuse step's attention over the rows a device-side compaction of
+    its commit's masks chose, with the count read by the kernel (nq_dev) and
+    the grid sized by a capacity: the same outputs, bit for bit, as the same
+    launch given the count on the host; the rows past the count are left as
+    they were."""
+    from cacheslide_b200 import _native as N
+    from cacheslide_b200 import reuse
+
+    cfg = reuse.WorkloadConfig(requests=1, q_heads=8, kv_heads=2, seq=1024, chunks=4, npos=64,
+                               fraction=0.15, seed=3)
+    work = reuse.SyntheticWorkload(cfg, cuda)
+    step = reuse.ReuseStep(work)
+    step.run()
+    torch.cuda.synchronize(cuda)
+    step.check_status()
+    r = work.requests[0]
+    cap = r.a + 64
+    lib = N.load()
+    rows = torch.empty(cap, dtype=torch.int64, device=cuda)
+    assoc = torch.empty(cap, dtype=torch.uint8, device=cuda)
+    count = torch.empty(1, dtype=torch.int64, device=cuda)
+    st = N.Status(cuda)
+    s = N.stream_of(cuda)
+    N.check(lib.cs_wca_active_rows(r.selected.data_ptr(), r.mandatory.data_ptr(), cfg.seq, cap,
+                                   rows.data_ptr(), assoc.data_ptr(), count.data_ptr(), st.ptr,
+                                   s), "active_rows")
+    # the layer's inputs for those rows, gathered on the device (no host read)
+    idx = rows.clamp_min(0)
+    q = r.q_all.index_select(0, idx).contiguous()
+    co = r.offsets.index_select(1, idx).contiguous()
+    outs = []
+    for device_count in (True, False):
+        out = torch.full((cap, cfg.q_heads, cfg.head_dim), 3.0, dtype=cfg.dtype, device=cuda)
+        p = step._attn_params(r)
+        p.q = q.data_ptr()
+        p.q_stride_tok, p.q_stride_head = q.stride(0), q.stride(1)
+        p.qpos = rows.data_ptr()
+        p.q_selected = assoc.data_ptr()
+        p.chunk_off = co.data_ptr()
+        p.co_stride_h, p.co_stride_q = co.stride(0), co.stride(1)
+        p.out = out.data_ptr()
+        p.o_stride_tok, p.o_stride_head = out.stride(0), out.stride(1)
+        p.status = st.ptr
+        if device_count:
+            p.nq = cap
+            p.nq_dev = count.data_ptr()
+        else:
+            torch.cuda.synchronize(cuda)
+            p.nq = int(count.item())
+        N.check(lib.cs_cope_attn_prefill(ctypes.byref(p), s), "prefill")
+        torch.cuda.synchronize(cuda)
+        assert st.read() == 0
+        outs.append(out.cpu())
+    nlive = int(count.item())
+    assert nlive == int((r.selected | r.mandatory).sum().item())
+    assert torch.equal(outs[0][:nlive], outs[1][:nlive])
+    assert bool((outs[0][nlive:] == 3.0).all())
+    # the other attention entry points refuse a device row count
+    p = step._attn_params(r)
+    p.nq_dev = count.data_ptr()
+    assert lib.cs_cope_attn(ctypes.byref(p), s) == N.CS_ERR_UNSUPPORTED
+
+
+def test_wca_state_active_rows_device(cuda):
+    """WCAState.active_rows_device equals active_indices after a commit."""
+    from cacheslide_b200 import wca as W
+
+    g = torch.Generator().manual_seed(5)
+    n, hkv, d = 2000, 2, 64
+    cached = (torch.randn(n, hkv, d, generator=g) / 8).to(torch.bfloat16).to(cuda)
+    fresh = (cached.float().cpu() + 0.05 * torch.randn(n, hkv, d, generator=g)).to(
+        torch.bfloat16).to(cuda)
+    reused = torch.ones(n, dtype=torch.bool)
+    reused[500:700] = False
+    mandatory = ~reused
+    mandatory[n - 1] = True
+    st = W.WCAState.initialize(cached, fresh, reused.to(cuda), mandatory.to(cuda))
+    rows, assoc, count = st.active_rows_device(n)
+    torch.cuda.synchronize(cuda)
+    want = st.active_indices
+    k = int(count.item())
+    assert k == want.numel()
+    assert torch.equal(rows[:k], want)
+    want_assoc = (st.selected_mask & ~st.mandatory_mask)[want].to(torch.uint8)
+    assert torch.equal(assoc[:k], want_assoc)
