@@ -115,7 +115,7 @@ class UpdateItem(ctypes.Structure):
         ("fresh_k", _p), ("fresh_v", _p), ("f_stride_row", _i64), ("f_stride_head", _i64),
         ("indices", _p), ("a", _i64), ("alpha", _p), ("mandatory", _p),
         ("fused_k", _p), ("fused_v", _p), ("next_alpha_out", _p), ("used_alpha_out", _p),
-        ("cos_out", _p), ("slots", _p), ("status", _p),
+        ("cos_out", _p), ("slots", _p), ("status", _p), ("a_dev", _p),
     ]
 
 
@@ -125,7 +125,7 @@ class CommitItem(ctypes.Structure):
         ("indices", _p), ("a", _i64), ("next_alpha", _p), ("cos", _p), ("n", _i64),
         ("budget", _i64), ("initial_dev", _p), ("alpha", _p), ("candidate", _p),
         ("selected", _p), ("removed", _p), ("removed_out", _p), ("promoted_out", _p),
-        ("counts_out", _p), ("status", _p),
+        ("counts_out", _p), ("status", _p), ("a_dev", _p),
     ]
 
 

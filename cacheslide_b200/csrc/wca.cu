@@ -1291,6 +1291,7 @@ struct UpdItem {
   double* cos;
   const int64_t* slots;
   int32_t* status;
+  const int64_t* a_dev;  // or NULL: rows r >= *a_dev are skipped
 };
 
 template <typename T>
@@ -1312,6 +1313,7 @@ __global__ void __launch_bounds__(kUpdThreads, IT > 0 ? 3 : 1)
     const int i = batch_item(b.start, b.count, g);
     const UpdItem<T>& q = b.it[i];
     const int64_t r = g - b.start[i];
+    if (q.a_dev != nullptr && r >= __ldg(q.a_dev)) continue;  // past the device row count
     update_row<T, G8, IT>(q.ck, q.cv, q.fk, q.fv, q.indices[r], r, heads, dim, q.alpha,
                           q.mandatory, same_layer, eps, clamp, q.fused_k, q.fused_v,
                           q.next_alpha, q.used, q.cos, pv, use_paged,
@@ -1328,7 +1330,12 @@ struct CommitBatch {
 __global__ void __launch_bounds__(kSelectThreads)
     commit_batch_kernel(const __grid_constant__ CommitBatch b, double thr, int distance_mode) {
   const cs_wca_commit_item& q = b.it[blockIdx.x];
-  commit_block(q.indices, q.a, q.next_alpha, q.cos, thr, distance_mode, q.n, q.budget,
+  int64_t a = q.a;
+  if (q.a_dev != nullptr) {  // a row count in device memory, at most a
+    const int64_t c = __ldg(q.a_dev);
+    a = c < 0 ? 0 : (c < a ? c : a);
+  }
+  commit_block(q.indices, a, q.next_alpha, q.cos, thr, distance_mode, q.n, q.budget,
                q.initial_dev, q.alpha, q.candidate, q.selected, q.removed, q.removed_out,
                q.promoted_out, q.counts_out, q.status);
 }
@@ -1735,7 +1742,7 @@ extern "C" int cs_wca_update_batch(const cs_wca_update_item* items, int32_t coun
                              rows_of<T>(q.fresh_v, q.f_stride_row, q.f_stride_head),
                              q.indices, q.alpha, q.mandatory, static_cast<T*>(q.fused_k),
                              static_cast<T*>(q.fused_v), q.next_alpha_out, q.used_alpha_out,
-                             q.cos_out, q.slots, q.status};
+                             q.cos_out, q.slots, q.status, q.a_dev};
         b.start[j + 1] = b.start[j] + q.a;
         if (q.a == 0) continue;
         int gj = vec_groups<T>(dim, {q.cached_k, q.cached_v, q.fresh_k, q.fresh_v, q.fused_k,

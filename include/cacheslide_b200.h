@@ -315,6 +315,11 @@ typedef struct {
   double* cos_out; /* or NULL */
   const int64_t* slots; /* paged destination rows when kv != NULL */
   int32_t* status;
+  /* or NULL: the number of rows is *a_dev, read on the device and clamped to
+     [0, a] (a is then the capacity); rows past it are skipped.  With the
+     count of cs_wca_active_rows a layer runs on the rows the previous
+     layer's commit chose without a host read. */
+  const int64_t* a_dev;
 } cs_wca_update_item;
 
 /* all items share heads, dim, dtype, the update options and the paged pool */
@@ -337,6 +342,7 @@ typedef struct {
   int64_t* promoted_out; /* or NULL */
   int64_t* counts_out;
   int32_t* status;
+  const int64_t* a_dev; /* or NULL: as cs_wca_update_item.a_dev, for indices */
 } cs_wca_commit_item;
 
 /* one thread block per request; threshold and distance_mode are shared */

@@ -145,3 +145,109 @@ def test_wca_state_active_rows_device(cuda):
     assert torch.equal(rows[:k], want)
     want_assoc = (st.selected_mask & ~st.mandatory_mask)[want].to(torch.uint8)
     assert torch.equal(assoc[:k], want_assoc)
+
+
+def test_layer_chained_on_device_rows(cuda):
+    """Layer 2 of a reuse step run from the rows layer 1's commit chose, with
+    no host read: the active rows on the device, the WCA update (blend and
+    paged scatter) and commit with the device row count (a_dev), and the
+    attention with nq_dev, every launch sized by a capacity.  Against the
+    same layer given the count on the host, from the same saved state: the
+    paged cache bytes, weights, masks, removal and promotion lists, cosines
+    and attention outputs are equal bit for bit."""
+    from cacheslide_b200 import _native as N
+    from cacheslide_b200 import reuse
+
+    cfg = reuse.WorkloadConfig(requests=1, q_heads=8, kv_heads=2, seq=1024, chunks=4, npos=64,
+                               fraction=0.15, seed=9)
+    work = reuse.SyntheticWorkload(cfg, cuda)
+    step = reuse.ReuseStep(work, batched=True)
+    step.run()  # layer 1: its commit decides layer 2's rows
+    torch.cuda.synchronize(cuda)
+    step.check_status()
+    r = work.requests[0]
+    n, hkv, d, hq = cfg.seq, cfg.kv_heads, cfg.head_dim, cfg.q_heads
+    g = torch.Generator().manual_seed(21)
+    fresh_k2 = (r.cached_k.float().cpu() + 0.05 * torch.randn(n, hkv, d, generator=g)).to(
+        cfg.dtype).to(cuda)
+    fresh_v2 = (r.cached_v.float().cpu() + 0.05 * torch.randn(n, hkv, d, generator=g)).to(
+        cfg.dtype).to(cuda)
+    q2 = (torch.randn(n, hq, d, generator=g) / d ** 0.5).to(cfg.dtype).to(cuda)
+    lib = N.load()
+    s = N.stream_of(cuda)
+    cap = r.a + 128
+    state = [r.alpha, r.candidate, r.selected, r.removed]
+    saved = [t.clone() for t in state] + [work.cache.clone()]
+
+    def layer2(device: bool):
+        st = N.Status(cuda)
+        rows = torch.empty(cap, dtype=torch.int64, device=cuda)
+        assoc = torch.empty(cap, dtype=torch.uint8, device=cuda)
+        count = torch.empty(1, dtype=torch.int64, device=cuda)
+        N.check(lib.cs_wca_active_rows(r.selected.data_ptr(), r.mandatory.data_ptr(), n, cap,
+                                       rows.data_ptr(), assoc.data_ptr(), count.data_ptr(),
+                                       st.ptr, s), "active_rows")
+        if device:
+            a, a_dev = cap, count.data_ptr()
+        else:
+            torch.cuda.synchronize(cuda)
+            a, a_dev = int(count.item()), None
+        idx = rows[:a].clamp_min(0)
+        fk, fv = fresh_k2.index_select(0, idx), fresh_v2.index_select(0, idx)
+        slots = r.slots.index_select(0, idx)
+        nxt = torch.empty(a, dtype=torch.float64, device=cuda)
+        used = torch.empty_like(nxt)
+        cos = torch.empty_like(nxt)
+        upd = (N.UpdateItem * 1)(N.UpdateItem(
+            r.cached_k.data_ptr(), r.cached_v.data_ptr(), r.cached_k.stride(0),
+            r.cached_k.stride(1), fk.data_ptr(), fv.data_ptr(), fk.stride(0), fk.stride(1),
+            rows.data_ptr(), a, r.alpha.data_ptr(), r.mandatory.data_ptr(), None, None,
+            nxt.data_ptr(), used.data_ptr(), cos.data_ptr(), slots.data_ptr(), st.ptr, a_dev))
+        N.check(lib.cs_wca_update_batch(upd, 1, hkv, d, N.DTYPES[cfg.dtype], 0, 1e-8, 0,
+                                        ctypes.byref(step.kv), s), "update")
+        q = q2.index_select(0, idx)
+        co = r.offsets.index_select(1, idx).contiguous()
+        out = torch.full((a, hq, d), 3.0, dtype=cfg.dtype, device=cuda)
+        p = step._attn_params(r)
+        p.q = q.data_ptr()
+        p.q_stride_tok, p.q_stride_head = q.stride(0), q.stride(1)
+        p.nq = a
+        p.nq_dev = a_dev
+        p.qpos = rows.data_ptr()
+        p.q_selected = assoc.data_ptr()
+        p.chunk_off = co.data_ptr()
+        p.co_stride_h, p.co_stride_q = co.stride(0), co.stride(1)
+        p.out = out.data_ptr()
+        p.o_stride_tok, p.o_stride_head = out.stride(0), out.stride(1)
+        p.status = st.ptr
+        N.check(lib.cs_cope_attn_prefill(ctypes.byref(p), s), "prefill")
+        removed_list = torch.full((n,), -7, dtype=torch.int64, device=cuda)
+        promoted = torch.full((n,), -7, dtype=torch.int64, device=cuda)
+        counts = torch.zeros(2, dtype=torch.int64, device=cuda)
+        com = (N.CommitItem * 1)(N.CommitItem(
+            rows.data_ptr(), a, nxt.data_ptr(), cos.data_ptr(), n, r.budget, r.dev.data_ptr(),
+            r.alpha.data_ptr(), r.candidate.data_ptr(), r.selected.data_ptr(),
+            r.removed.data_ptr(), removed_list.data_ptr(), promoted.data_ptr(),
+            counts.data_ptr(), st.ptr, a_dev))
+        N.check(lib.cs_wca_commit_batch(com, 1, 0.12, 0, s), "commit")
+        torch.cuda.synchronize(cuda)
+        assert st.read() == 0
+        k = int(count.item())
+        nr, npr = counts.tolist()
+        return {"count": k, "out": out[:k].cpu(), "next": nxt[:k].cpu(), "cos": cos[:k].cpu(),
+                "alpha": r.alpha.cpu(), "candidate": r.candidate.cpu(),
+                "selected": r.selected.cpu(), "removed": r.removed.cpu(),
+                "removed_list": removed_list[:nr].cpu(), "promoted": promoted[:npr].cpu(),
+                "counts": (nr, npr), "cache": work.cache.cpu(),
+                "untouched": bool((out[k:] == 3.0).all()) if device else True}
+
+    got = layer2(True)
+    for t, v in zip(state + [work.cache], saved):
+        t.copy_(v)
+    want = layer2(False)
+    assert got["count"] == want["count"] and got["count"] > 0
+    assert got["untouched"]
+    for key in ("out", "next", "cos", "alpha", "candidate", "selected", "removed",
+                "removed_list", "promoted", "cache"):
+        assert torch.equal(got[key], want[key]), key
+    assert got["counts"] == want["counts"]
