@@ -136,7 +136,7 @@ class QKVParams(ctypes.Structure):
         ("src1", _p), ("src1_stride", _i64), ("src1_rows", _i64),
         ("row_src", _p), ("row_idx", _p), ("a", _i64), ("hidden", _i64), ("n_out", _i64),
         ("w", _p), ("lora_a", _p), ("lora_b", _p), ("rank", _i32),
-        ("out", _p), ("out_stride", _i64), ("dtype", _i32), ("status", _p),
+        ("out", _p), ("out_stride", _i64), ("dtype", _i32), ("status", _p), ("a_dev", _p),
     ]
 
 

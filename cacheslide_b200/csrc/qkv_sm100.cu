@@ -72,6 +72,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort = reinterpret_cast<volatile int*>(meta + kAbortFlag);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t m0 = (int64_t)blockIdx.x * kBM, n0 = (int64_t)blockIdx.y * kBN;
+  // rows: a, or a count in device memory (at most a); a CTA whose rows all
+  // lie past it leaves before any barrier or TMEM use (a uniform exit)
+  int64_t arows = p.a;
+  if (p.a_dev != nullptr) {
+    const int64_t c = __ldg(p.a_dev);
+    arows = c < 0 ? 0 : (c < arows ? c : arows);
+  }
+  if (m0 >= arows) return;
   const int nk = (int)(p.hidden / kBK);
   const int TR = p.rank > 16 ? 32 : 16;  // LoRA columns of T (padded)
   const bool lora = p.rank > 0;
@@ -97,7 +105,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = tid;  // the A row this thread copies
     const int64_t row = m0 + r;
     const char* arow = nullptr;
-    if (row < p.a) {
+    if (row < arows) {
       const int src = p.row_src[row];
       const int64_t idx = p.row_idx[row];
       const bool ok = src == 0 ? (idx >= 0 && idx < p.src0_rows) : (idx >= 0 && idx < p.src1_rows);
@@ -191,7 +199,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t v[32];
         CS_TMEM_LD32(tmem + lane_base + 32 * cc, v);
         tmem_wait_ld();
-        if (orow < p.a) {
+        if (orow < arows) {
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint32_t w4[4];

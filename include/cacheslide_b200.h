@@ -394,6 +394,10 @@ typedef struct {
   int64_t out_stride;
   int32_t dtype;
   int32_t* status;
+  /* or NULL: the number of rows is *a_dev, read on the device and clamped to
+     [0, a] (a is then the capacity the grid is sized for); rows past it are
+     not computed and their output rows are not written */
+  const int64_t* a_dev;
 } cs_qkv_params;
 
 CS_API int cs_qkv_gather_lora(const cs_qkv_params* p, void* stream);

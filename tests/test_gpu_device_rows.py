@@ -251,3 +251,58 @@ def test_layer_chained_on_device_rows(cuda):
                 "removed_list", "promoted", "cache"):
         assert torch.equal(got[key], want[key]), key
     assert got["counts"] == want["counts"]
+
+
+def test_qkv_rows_from_device_count(cuda):
+    """The selective QKV GEMM (cs_qkv_gather_lora) over rows listed on the
+    device, with the row count read from device memory (a_dev) and the grid
+    sized by a capacity: bit for bit the launch given the count on the host;
+    the output rows past the count are not written."""
+    from cacheslide_b200 import _native as N
+
+    g = torch.Generator().manual_seed(4)
+    n, hidden, n_out, rank = 1500, 512, 512, 16
+    dt = torch.bfloat16
+    src = (torch.randn(n, hidden, generator=g)).to(dt).to(cuda)
+    w = (torch.randn(n_out, hidden, generator=g) / hidden ** 0.5).to(dt).to(cuda)
+    la = (torch.randn(rank, hidden, generator=g) / hidden ** 0.5).to(dt).to(cuda)
+    lb = (torch.randn(n_out, rank, generator=g) * 0.5).to(dt).to(cuda)
+    selected = (torch.rand(n, generator=g) < 0.2).to(cuda)
+    mandatory = torch.zeros(n, dtype=torch.bool, device=cuda)
+    mandatory[600:700] = True
+    cap = 700
+    lib = N.load()
+    s = N.stream_of(cuda)
+    st = N.Status(cuda)
+    rows = torch.empty(cap, dtype=torch.int64, device=cuda)
+    assoc = torch.empty(cap, dtype=torch.uint8, device=cuda)
+    count = torch.empty(1, dtype=torch.int64, device=cuda)
+    N.check(lib.cs_wca_active_rows(selected.data_ptr(), mandatory.data_ptr(), n, cap,
+                                   rows.data_ptr(), assoc.data_ptr(), count.data_ptr(), st.ptr, s),
+            "active_rows")
+    row_src = torch.zeros(cap, dtype=torch.int32, device=cuda)
+    outs = []
+    for device_count in (True, False):
+        out = torch.full((cap, n_out), 5.0, dtype=dt, device=cuda)
+        p = N.QKVParams()
+        p.src0, p.src0_stride, p.src0_rows = src.data_ptr(), src.stride(0), n
+        p.src1, p.src1_stride, p.src1_rows = src.data_ptr(), src.stride(0), n
+        p.row_src, p.row_idx = row_src.data_ptr(), rows.data_ptr()
+        p.hidden, p.n_out = hidden, n_out
+        p.w, p.lora_a, p.lora_b, p.rank = w.data_ptr(), la.data_ptr(), lb.data_ptr(), rank
+        p.out, p.out_stride = out.data_ptr(), out.stride(0)
+        p.dtype = N.DTYPES[dt]
+        p.status = st.ptr
+        if device_count:
+            p.a, p.a_dev = cap, count.data_ptr()
+        else:
+            torch.cuda.synchronize(cuda)
+            p.a = int(count.item())
+        N.check(lib.cs_qkv_gather_lora(ctypes.byref(p), s), "qkv")
+        torch.cuda.synchronize(cuda)
+        assert st.read() == 0
+        outs.append(out.cpu())
+    k = int(count.item())
+    assert 0 < k < cap
+    assert torch.equal(outs[0][:k], outs[1][:k])
+    assert bool((outs[0][k:] == 5.0).all())
