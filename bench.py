@@ -497,6 +497,48 @@ def c3_slice(args, dev) -> dict:
     return out
 
 
+def chained_slice(args, dev, layers: int = 8) -> dict:
+    """Layers 2..L of one C2-shaped request, each on the rows the previous
+    layer's WCA commit chose, with the row count left on the device (no host
+    read between layers), against the same layers with the count read back
+    to the host before each, the reference runtime's order (runtime.py:410)."""
+    import torch
+
+    from cacheslide_b200.chain import ChainedLayers
+    from cacheslide_b200.reuse import ReuseStep, SyntheticWorkload, WorkloadConfig
+
+    cfg = WorkloadConfig(requests=1, seq=args.seq, seed=77)
+    work = SyntheticWorkload(cfg, dev)
+    step = ReuseStep(work, batched=True)
+    step.run()  # layer 1
+    chain = ChainedLayers(step, layers=layers)
+    out = {"workload": f"c2-shaped request, layers 2-{layers} on the previous commit's rows "
+                       f"(WCA update + CCPE attention + commit per layer, 15%)",
+           "layers_timed": layers - 1}
+    for device in (True, False):
+        times = []
+        for rep in range(4):
+            torch.cuda.synchronize(dev)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            t0 = time.perf_counter()
+            e0.record()
+            chain.run(device=device)
+            e1.record()
+            torch.cuda.synchronize(dev)
+            wall = (time.perf_counter() - t0) * 1e3
+            if rep > 0:  # the first pass is a warm-up
+                times.append((e0.elapsed_time(e1), wall))
+        step.check_status()
+        key = "device_count" if device else "host_count"
+        out[key] = {"ms_per_layer": sum(t[0] for t in times) / len(times) / (layers - 1),
+                    "wall_ms_per_layer": sum(t[1] for t in times) / len(times) / (layers - 1),
+                    "host_reads_per_layer": 0 if device else 1}
+    del chain, step, work
+    torch.cuda.empty_cache()
+    return out
+
+
 def c4_slice(args, dev) -> dict:
     """The multi-session chat slice (C4): 32 sessions at turn 8 of
     conversations adding 256-1024 tokens a turn plus 128 decoded tokens;
@@ -724,6 +766,7 @@ def main():
     c5 = c5_slice(args, dev, rank, world) if (world > 1 or args.c5) else None
     c4 = c4_slice(args, dev) if (world == 1 and not args.no_c4) else None
     c3 = c3_slice(args, dev) if (world == 1 and not args.no_c3) else None
+    chained = chained_slice(args, dev) if (world == 1 and not args.no_c3) else None
 
     if rank == 0:
         pk, pk_kind = peaks()
@@ -788,6 +831,8 @@ def main():
             line["c4_chat"] = c4
         if c3 is not None:
             line["c3_rag"] = c3
+        if chained is not None:
+            line["chained_layers"] = chained
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

@@ -306,3 +306,40 @@ def test_qkv_rows_from_device_count(cuda):
     assert 0 < k < cap
     assert torch.equal(outs[0][:k], outs[1][:k])
     assert bool((outs[0][k:] == 5.0).all())
+
+
+def test_chained_layers_match_host_count_layers(cuda):
+    """chain.ChainedLayers: layers 2-4 of a request, each on the rows the
+    previous layer's commit chose, with no host read between layers, equal
+    bit for bit to the same layers with the count read back to the host
+    before each (the reference runtime's order, runtime.py:410): the final
+    WCA state, the last layer's attention rows and the paged cache."""
+    from cacheslide_b200 import reuse
+    from cacheslide_b200.chain import ChainedLayers
+
+    cfg = reuse.WorkloadConfig(requests=1, q_heads=8, kv_heads=2, seq=1024, chunks=4, npos=64,
+                               fraction=0.15, seed=12)
+    work = reuse.SyntheticWorkload(cfg, cuda)
+    step = reuse.ReuseStep(work, batched=True)
+    step.run()
+    torch.cuda.synchronize(cuda)
+    step.check_status()
+    r = work.requests[0]
+    chain = ChainedLayers(step, layers=4)
+    state = [r.alpha, r.candidate, r.selected, r.removed, work.cache]
+    saved = [t.clone() for t in state]
+    results = []
+    for device in (True, False):
+        for t, v in zip(state, saved):
+            t.copy_(v)
+        chain.run(device=device)
+        torch.cuda.synchronize(cuda)
+        step.check_status()
+        k = int(chain.count.item())
+        results.append({"k": k, "out": chain.out[:k].cpu(), "alpha": r.alpha.cpu(),
+                        "candidate": r.candidate.cpu(), "selected": r.selected.cpu(),
+                        "removed": r.removed.cpu(), "cache": work.cache.cpu()})
+    got, want = results
+    assert got["k"] == want["k"] > 0
+    for key in ("out", "alpha", "candidate", "selected", "removed", "cache"):
+        assert torch.equal(got[key], want[key]), key
