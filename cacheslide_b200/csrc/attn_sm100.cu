@@ -1355,19 +1355,37 @@ __device__ __forceinline__ void prefill_cta(const Args& a, const int g, const in
               }
             }
           }
+          // interpolated bias and score, eight columns at a time: the
+          // positions first, then all sixteen table reads, then the
+          // arithmetic, so the shared-memory loads are in flight together
+          // (each column's arithmetic is that of bias_at)
 #pragma unroll
-          for (int c = 0; c < 32; c += 2) {
-            const float x0 = (hm >> c) & 1u ? -INFINITY
-                                            : fmaf(__uint_as_float(s[c]), scale2,
-                                                   bias_at(fminf(__uint_as_float(v[c]), top)));
-            const float x1 = (hm >> (c + 1)) & 1u
-                                 ? -INFINITY
-                                 : fmaf(__uint_as_float(s[c + 1]), scale2,
-                                        bias_at(fminf(__uint_as_float(v[c + 1]), top)));
-            s[c] = __float_as_uint(x0);
-            s[c + 1] = __float_as_uint(x1);
-            t0 = fmaxf(t0, x0);
-            t1 = fmaxf(t1, x1);
+          for (int c0 = 0; c0 < 32; c0 += 8) {
+            float fr[8];
+            int lo[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const float pos = fminf(__uint_as_float(v[c0 + u]), top);
+              const float fl = floor_pos(pos, lo[u]);
+              fr[u] = pos - fl;
+            }
+            float tl[8], th[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              tl[u] = tab_get(lo[u]);
+              th[u] = tab_get(lo[u] + 1 < p.npos ? lo[u] + 1 : p.npos - 1);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const int c = c0 + u;
+              const float x = (hm >> c) & 1u
+                                  ? -INFINITY
+                                  : fmaf(__uint_as_float(s[c]), scale2,
+                                         fmaf(fr[u], th[u] - tl[u], tl[u]));
+              s[c] = __float_as_uint(x);
+              if (u & 1) t1 = fmaxf(t1, x);
+              else t0 = fmaxf(t0, x);
+            }
           }
           CS_TMEM_ST32(sc + 32 * cc, s);
         }
