@@ -81,8 +81,8 @@ def peaks():
 # None until captured for the current kernel
 # dram__bytes_read.sum + dram__bytes_write.sum of one batched C2 attention
 # launch, from the ncu --set full capture summarised in
-# profiles/cope_prefill_sm100_batch_c2_step.md (363.96 MB + 55.18 MB)
-PREFILL_DRAM_BYTES_PER_LAUNCH = 419138048
+# profiles/cope_prefill_sm100_batch_c2_step.md (362.21 MB + 50.31 MB)
+PREFILL_DRAM_BYTES_PER_LAUNCH = 412519168
 
 
 def attention_flops(work, visible_only: bool = False) -> float:
