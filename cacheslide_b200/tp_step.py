@@ -15,7 +15,8 @@ rank's batch (the same requests on every rank, each rank its own heads):
 4. ``o_proj``: the rank's attention rows times its row block of the output
    projection (``[active rows, 8192]``, cuBLAS through torch), then one NCCL
    all-reduce (sum) of ``[all requests' active rows, 8192]`` bf16 -- the
-   collective that follows attention in the model.
+   collective that follows attention in a tensor-parallel Llama-3-70B-shaped
+   model (8 KV heads split over the ranks).
 
 The token layout (chunks, which chunk is recomputed, reused / mandatory
 masks, paged blocks) is the same on every rank; the head data are seeded per
