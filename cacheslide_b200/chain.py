@@ -63,10 +63,15 @@ class ChainedLayers:
         self.counts = torch.zeros(2, dtype=torch.int64, device=dev)
         self.lib = N.load()
 
-    def layer(self, layer: int, device: bool = True, stream: int | None = None) -> None:
-        """Layer ``layer`` (1-based, >= 2) on the rows the previous commit chose."""
+    def layer(self, layer: int, device: bool = True) -> None:
+        """Layer ``layer`` (1-based, >= 2) on the rows the previous commit chose.
+
+        Everything runs on torch's current stream: the row gathers are torch
+        ops, and their buffers are released to torch's allocator after the
+        layer's launches are queued, which is safe only in one stream order.
+        """
         cfg, r, lib, step = self.work.cfg, self.r, self.lib, self.step
-        s = N.stream_of(self.work.device) if stream is None else stream
+        s = N.stream_of(self.work.device)
         n, cap = cfg.seq, self.cap
         st = r.status_ptr
         N.check(lib.cs_wca_active_rows(r.selected.data_ptr(), r.mandatory.data_ptr(), n, cap,
@@ -111,10 +116,12 @@ class ChainedLayers:
             r.removed.data_ptr(), self.removed_list.data_ptr(), self.promoted.data_ptr(),
             self.counts.data_ptr(), st, a_dev))
         N.check(lib.cs_wca_commit_batch(com, 1, 0.12, 0, s), "commit")
-        # keep the gathered inputs alive until the launches that read them ran
+        # the gathered inputs stay referenced until the next layer's are made;
+        # freed then, their memory is reused only by work queued after these
+        # launches on the same stream
         self._keep = (fk, fv, slots, q, co, upd, com)
 
-    def run(self, device: bool = True, stream: int | None = None) -> None:
-        """Layers 2..L back to back on one stream."""
+    def run(self, device: bool = True) -> None:
+        """Layers 2..L back to back on torch's current stream."""
         for layer in range(2, self.layers + 1):
-            self.layer(layer, device, stream)
+            self.layer(layer, device)
